@@ -1,0 +1,331 @@
+"""GRPO / DAPO / GSPO training loop.
+
+Reference: ``nemo_rl/algorithms/grpo.py`` - ``GRPOConfig`` ``:356``, ``GRPOSaveState``
+``:439``, ``MasterConfig`` ``:542``, ``setup`` ``:667``, ``dynamic_sampling`` ``:2168``,
+``scale_rewards`` ``:2312``, ``refit_policy_generation`` ``:3150``, ``_grpo_train_impl``
+``:3574`` (step stages in section 3.2 of the survey), ``validate`` ``:4897``.
+
+SPMD design: every rank runs this loop.  Each data-parallel rank draws its own
+``num_prompts_per_step / dp`` prompts and generates ALL samples of those prompts,
+so prompt groups never straddle ranks: rewards, baselines and advantages are
+computed locally, and only scalars (valid-token counts, metrics, loss) cross
+ranks.  Tensor-parallel peers draw identical prompts and sample identical
+tokens (same seed; logits are all-gathered before sampling).
+"""
+
+from __future__ import annotations
+
+import copy
+import math
+import os
+import time
+from typing import Any, Optional
+
+import torch
+import torch.distributed as dist
+
+from rl_b200.algorithms.advantage_estimator import make_advantage_estimator
+from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+from rl_b200.algorithms.utils import calculate_baseline_and_std_per_prompt, set_seed
+from rl_b200.data.llm_message_utils import add_loss_mask_to_message_log, batched_message_log_to_flat_message
+from rl_b200.distributed.batched_data_dict import BatchedDataDict
+from rl_b200.experience.rollouts import run_multi_turn_rollout
+from rl_b200.utils.timer import Timer, max_over_ranks
+
+__all__ = ["DEFAULT_GRPO_CONFIG", "GRPOSaveState", "grpo_train", "build_train_data", "dynamic_sampling",
+           "scale_rewards", "apply_reward_shaping", "validate", "refit_policy_generation"]
+
+DEFAULT_GRPO_CONFIG: dict[str, Any] = {
+    "num_prompts_per_step": 8,
+    "num_generations_per_prompt": 4,
+    "max_rollout_turns": 1,
+    "max_num_epochs": 1,
+    "max_num_steps": 1000000,
+    "normalize_rewards": True,
+    "use_leave_one_out_baseline": True,
+    "val_period": 0,
+    "val_at_start": False,
+    "val_at_end": False,
+    "max_val_samples": 256,
+    "val_batch_size": 256,
+    "val_num_generations_per_prompt": 1,
+    "stop_at_validation_metric": None,
+    "stop_at_validation_threshold": None,
+    "seed": 42,
+    "overlong_filtering": False,
+    "advantage_clip_low": None,
+    "advantage_clip_high": None,
+    "use_dynamic_sampling": False,
+    "dynamic_sampling_max_gen_batches": 10,
+    "batch_multiplier": 1,
+    "reward_shaping": {"enabled": False},
+    "reward_scaling": {"enabled": False},
+    "adv_estimator": {"name": "grpo"},
+    "seq_logprob_error_threshold": None,
+    "async_grpo": {"enabled": False, "max_trajectory_age_steps": 1},
+}
+
+
+class GRPOSaveState(dict):
+    """Resumable loop state (reference ``GRPOSaveState`` ``grpo.py:439``)."""
+
+    @classmethod
+    def default(cls) -> "GRPOSaveState":
+        return cls(current_step=0, current_epoch=0, total_steps=0, consumed_samples=0, total_valid_tokens=0,
+                   val_reward=None)
+
+
+def refit_policy_generation(policy) -> float:
+    """Push trained weights to the rollout engine.  Colocated on one device with
+    the same layout, the optimizer already wrote the bf16 weights the engine
+    reads, so this only validates / re-quantises (fp8 rollout)."""
+    return policy.refit()
+
+
+def apply_reward_shaping(rewards: torch.Tensor, gen_lengths: torch.Tensor, cfg: dict) -> torch.Tensor:
+    """DAPO overlong reward shaping: linear penalty over the last
+    ``overlong_buffer_length`` tokens before ``max_response_length``."""
+    if not cfg or not cfg.get("enabled", False):
+        return rewards
+    buf = float(cfg.get("overlong_buffer_length", 128))
+    pen = float(cfg.get("overlong_buffer_penalty", 1.0))
+    max_len = float(cfg.get("max_response_length", 1e9))
+    expected = max_len - buf
+    over = (gen_lengths.float() - expected).clamp_min(0)
+    return rewards - (over / max(buf, 1.0)).clamp_max(1.0) * pen
+
+
+def scale_rewards(rewards: torch.Tensor, cfg: dict) -> torch.Tensor:
+    """Linear map ``[source_min, source_max] -> [target_min, target_max]`` (clamped)."""
+    if not cfg or not cfg.get("enabled", False):
+        return rewards
+    smin, smax = float(cfg.get("source_min", 0.0)), float(cfg.get("source_max", 1.0))
+    tmin, tmax = float(cfg.get("target_min", 0.0)), float(cfg.get("target_max", 1.0))
+    r = rewards.clamp(smin, smax)
+    return tmin + (r - smin) * (tmax - tmin) / max(smax - smin, 1e-12)
+
+
+def dynamic_sampling(rewards: torch.Tensor, group_ids: torch.Tensor) -> torch.Tensor:
+    """DAPO dynamic sampling: keep only rows of groups whose rewards are not all
+    equal (a constant group has zero advantage everywhere). Returns a row mask."""
+    _, std, trivial = calculate_baseline_and_std_per_prompt(group_ids, rewards, torch.ones_like(rewards),
+                                                            leave_one_out_baseline=False)
+    return ~trivial
+
+
+def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, loss_cfg: dict,
+                     group_ids: torch.Tensor) -> tuple[BatchedDataDict, dict]:
+    """Flatten message logs and compute per-token advantages."""
+    logs = rollout_batch["message_log"]
+    add_loss_mask_to_message_log(logs, roles_to_train_on=("assistant",))
+    flat, lengths = batched_message_log_to_flat_message(logs)
+    token_mask = flat["token_loss_mask"].float()
+    rewards = rollout_batch["total_reward"].float()
+    gen_len = token_mask.sum(-1)
+    rewards = apply_reward_shaping(rewards, gen_len, cfg.get("reward_shaping", {}))
+    rewards = scale_rewards(rewards, cfg.get("reward_scaling", {}))
+    sample_mask = rollout_batch["loss_multiplier"].float().clone()
+    if cfg.get("overlong_filtering", False):
+        sample_mask = sample_mask * (~rollout_batch["truncated"]).float()
+    adv = advantages_fn.compute_advantage(group_ids.view(-1, 1), rewards, token_mask,
+                                          repeated_batch=rollout_batch, valid_mask=None)
+    if isinstance(adv, tuple):
+        adv = adv[0]
+    adv = adv.clone()
+    lo, hi = cfg.get("advantage_clip_low"), cfg.get("advantage_clip_high")
+    if lo is not None or hi is not None:
+        adv = adv.clamp(min=lo, max=hi)
+    gen_lp = flat.get("generation_logprobs", torch.zeros_like(token_mask)).float()
+    data = BatchedDataDict({
+        "input_ids": flat["token_ids"],
+        "input_lengths": lengths,
+        "advantages": adv * token_mask,
+        "generation_logprobs": gen_lp,
+        "token_mask": token_mask,
+        "sample_mask": sample_mask,
+    })
+    stats = {"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std()) if len(rewards) > 1 else 0.0,
+             "advantage_abs_mean": float((adv.abs() * token_mask).sum() / token_mask.sum().clamp_min(1))}
+    return data, stats
+
+
+def _dp_sum(x: float, ps) -> float:
+    if ps.dp_size <= 1:
+        return x
+    dev = ps.device if ps.device.type == "cuda" else torch.device("cpu")
+    t = torch.tensor([x], dtype=torch.float64, device=dev)
+    dist.all_reduce(t, group=ps.dp_group)
+    return float(t.item())
+
+
+def validate(policy, val_dataloader, val_task_to_env: dict, master_config: dict, step: int,
+             tokenizer=None) -> dict:
+    """Greedy (or val-temperature) rollouts over the validation set: mean reward
+    ("accuracy") and pass@k over ``val_num_generations_per_prompt`` samples."""
+    if val_dataloader is None:
+        return {}
+    cfg = {**DEFAULT_GRPO_CONFIG, **master_config.get("grpo", {})}
+    k = int(cfg.get("val_num_generations_per_prompt", 1))
+    max_seq = int(master_config["policy"]["max_total_sequence_length"])
+    rewards_all, passk = [], []
+    seen = 0
+    policy.prepare_for_generation()
+    for batch in val_dataloader:
+        rep = batch.repeat_interleave(k)
+        rollout, _ = run_multi_turn_rollout(policy, rep, tokenizer, val_task_to_env, max_seq,
+                                            cfg.get("max_rollout_turns", 1), greedy=(k == 1))
+        r = rollout["total_reward"]
+        rewards_all.append(r)
+        passk.append((r.view(-1, k) > 0).any(-1).float())
+        seen += len(batch["message_log"])
+        if seen >= cfg.get("max_val_samples", 256):
+            break
+    policy.finish_generation()
+    if not rewards_all:
+        return {}
+    r = torch.cat(rewards_all)
+    p = torch.cat(passk)
+    return {"accuracy": float(r.mean()), "pass_k": float(p.mean()), "num_samples": int(r.numel())}
+
+
+def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_fn=None, logger=None,
+               checkpointer=None, save_state: Optional[GRPOSaveState] = None, val_dataloader=None,
+               val_task_to_env: Optional[dict] = None, tokenizer=None, max_steps: Optional[int] = None,
+               step_callback=None) -> GRPOSaveState:
+    """Run GRPO steps; returns the final save state.  ``step_callback(step, metrics)``
+    is called after every step (benchmarks hook timing there)."""
+    ps = policy.ps
+    cfg = {**DEFAULT_GRPO_CONFIG, **master_config.get("grpo", {})}
+    loss_cfg = master_config.get("loss_fn", {})
+    loss_fn = loss_fn or ClippedPGLossFn(loss_cfg)
+    adv_cfg = dict(cfg.get("adv_estimator", {}) or {})
+    adv_cfg.setdefault("normalize_rewards", cfg["normalize_rewards"])
+    adv_cfg.setdefault("use_leave_one_out_baseline", cfg["use_leave_one_out_baseline"])
+    estimator = make_advantage_estimator(adv_cfg, loss_cfg)
+    G = int(cfg["num_generations_per_prompt"])
+    max_seq = int(master_config["policy"]["max_total_sequence_length"])
+    train_gbs = int(master_config["policy"].get("train_global_batch_size", cfg["num_prompts_per_step"] * G))
+    local_gbs = max(1, train_gbs // max(1, ps.dp_size))
+    kl_on = float(loss_cfg.get("reference_policy_kl_penalty", 0.0) or 0.0) != 0.0
+    state = save_state or GRPOSaveState.default()
+    max_steps = max_steps if max_steps is not None else int(cfg["max_num_steps"])
+    set_seed(int(cfg["seed"]) + ps.dp_rank)
+    timer = Timer()
+    step = int(state["current_step"])
+    if cfg.get("val_at_start") and step == 0 and val_dataloader is not None:
+        vm = validate(policy, val_dataloader, val_task_to_env or task_to_env, master_config, step, tokenizer)
+        if logger:
+            logger.log_metrics(vm, step, prefix="validation")
+    done = False
+    for epoch in range(int(state["current_epoch"]), int(cfg["max_num_epochs"])):
+        for batch in dataloader:
+            if step >= max_steps:
+                done = True
+                break
+            timer.reset()
+            t_step = time.perf_counter()
+            with timer.time("total_step_time"):
+                # ---- rollouts (with DAPO dynamic sampling) ----
+                kept_batches = []
+                gen_batches = 0
+                rollout_metrics: dict = {}
+                with timer.time("generation"):
+                    cur = batch
+                    while True:
+                        rep = cur.repeat_interleave(G)
+                        n_prompts = len(cur["message_log"])
+                        base = (step * 1000 + gen_batches) * 1_000_000 + ps.dp_rank * n_prompts
+                        rep["group_id"] = torch.arange(base, base + n_prompts).repeat_interleave(G)
+                        policy.prepare_for_generation(len(rep["message_log"]))
+                        rollout, rollout_metrics = run_multi_turn_rollout(
+                            policy, rep, tokenizer, task_to_env, max_seq, int(cfg["max_rollout_turns"]))
+                        gen_batches += 1
+                        if not cfg.get("use_dynamic_sampling", False):
+                            kept_batches.append(rollout)
+                            break
+                        keep = dynamic_sampling(rollout["total_reward"], rollout["group_id"])
+                        rows = torch.nonzero(keep).flatten().tolist()
+                        if rows:
+                            kept_batches.append(rollout.select_indices(rows))
+                        n_kept = sum(len(b["message_log"]) for b in kept_batches)
+                        target = n_prompts * G
+                        if n_kept >= target or gen_batches >= int(cfg["dynamic_sampling_max_gen_batches"]):
+                            break
+                        cur = batch
+                    policy.finish_generation()
+                rollout = BatchedDataDict.from_batches(kept_batches) if len(kept_batches) > 1 else kept_batches[0]
+                if cfg.get("use_dynamic_sampling", False):
+                    target = len(batch["message_log"]) * G
+                    if len(rollout["message_log"]) > target:
+                        rollout = rollout.slice(0, target)
+                # ---- advantages ----
+                with timer.time("data_processing"):
+                    train_data, adv_stats = build_train_data(rollout, estimator, cfg, loss_cfg, rollout["group_id"])
+                # ---- logprobs ----
+                with timer.time("policy_and_reference_logprobs"):
+                    policy.prepare_for_lp_inference()
+                    train_data["prev_logprobs"] = policy.get_logprobs(train_data)["logprobs"]
+                    if kl_on:
+                        train_data["reference_policy_logprobs"] = \
+                            policy.get_reference_policy_logprobs(train_data)["reference_logprobs"]
+                # ---- train ----
+                with timer.time("policy_training"):
+                    policy.prepare_for_training()
+                    n_rows = train_data.size
+                    gbs = min(local_gbs, n_rows)
+                    train_results = policy.train(train_data, loss_fn, gbs=gbs)
+                # ---- refit ----
+                with timer.time("weight_sync"):
+                    refit_policy_generation(policy)
+            step_time = time.perf_counter() - t_step
+            # ---- metrics ----
+            tok = float(train_data["input_lengths"].sum())
+            gen_tok = float(train_data["token_mask"].sum())
+            tok_all = _dp_sum(tok, ps) if ps.dp_size > 1 else tok
+            gen_all = _dp_sum(gen_tok, ps) if ps.dp_size > 1 else gen_tok
+            step_time_max = max_over_ranks(step_time)
+            world = max(1, ps.world_size)
+            metrics = dict(train_results)
+            metrics.update(adv_stats)
+            metrics.update({k: v for k, v in rollout_metrics.items() if isinstance(v, (int, float))})
+            metrics.update({
+                "total_tokens": tok_all,
+                "generated_tokens": gen_all,
+                "tokens_per_sec": tok_all / step_time_max,
+                "tokens_per_sec_per_gpu": tok_all / step_time_max / world,
+                "step_time_s": step_time_max,
+            })
+            timing = {k: v for k, v in timer.get_timing_metrics().items()}
+            step += 1
+            state["current_step"] = step
+            state["total_steps"] = int(state.get("total_steps", 0)) + 1
+            state["consumed_samples"] = int(state.get("consumed_samples", 0)) + len(batch["message_log"]) * ps.dp_size
+            state["total_valid_tokens"] = int(state.get("total_valid_tokens", 0)) + int(gen_all)
+            if logger:
+                logger.log_metrics(metrics, step, prefix="train")
+                logger.log_metrics(timing, step, prefix="timing/train")
+            if step_callback is not None:
+                step_callback(step, {**metrics, **{"timing/" + k: v for k, v in timing.items()}})
+            # ---- validation / checkpoint ----
+            val_period = int(cfg.get("val_period") or 0)
+            if val_dataloader is not None and val_period > 0 and step % val_period == 0:
+                vm = validate(policy, val_dataloader, val_task_to_env or task_to_env, master_config, step, tokenizer)
+                state["val_reward"] = vm.get("accuracy")
+                if logger:
+                    logger.log_metrics(vm, step, prefix="validation")
+                thr = cfg.get("stop_at_validation_threshold")
+                key = cfg.get("stop_at_validation_metric")
+                if key and thr is not None and vm.get(key, -math.inf) >= float(thr):
+                    done = True
+            if checkpointer is not None and checkpointer.should_save(step):
+                checkpointer.save(policy, state, dataloader, metrics, step)
+            if done:
+                break
+        if done or step >= max_steps:
+            break
+        state["current_epoch"] = epoch + 1
+    if cfg.get("val_at_end") and val_dataloader is not None:
+        vm = validate(policy, val_dataloader, val_task_to_env or task_to_env, master_config, step, tokenizer)
+        if logger:
+            logger.log_metrics(vm, step, prefix="validation")
+    return state

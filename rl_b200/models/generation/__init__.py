@@ -1,0 +1,1 @@
+"""rl_b200 subpackage."""

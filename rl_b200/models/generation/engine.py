@@ -1,0 +1,344 @@
+"""In-house rollout engine (replaces vLLM / MCore inference in the reference).
+
+Reference behaviour: ``VllmGenerationWorkerImpl.generate``
+(``nemo_rl/models/generation/vllm/vllm_worker.py:1120``), the MCore dynamic engine
+(``nemo_rl/models/generation/megatron/megatron_worker.py:1396``, paged KV with
+``block_size_tokens: 256``), sleep / wake of KV memory for colocation
+(``vllm_worker.py:1635,1663``) and CUDA-graph decode (``enforce_eager: False``).
+
+Design (B200-first)
+-------------------
+* Weights are the trainer's own bf16 parameters (colocated by construction),
+  so a refit after an optimizer step costs nothing here; an fp8 rollout copy
+  is re-quantised by the refit kernel when requested.
+* Paged KV cache in one allocation ``[L, 2, blocks, block, nkv, hd]``; blocks
+  are handed out per sequence up front for ``prompt + max_new_tokens``.
+* Prefill runs all prompts packed (THD) through the varlen attention kernel
+  and writes K/V to the cache.
+* Decode runs ENTIRELY on the device: one CUDA graph per batch bucket does
+  slot computation, the model step, LM head, sampling, the output write and
+  stop-token / length bookkeeping.  The host only replays the graph and reads
+  a single "all done" flag every ``sync_every`` steps.  Finished rows are
+  compacted into a smaller bucket when the active set halves.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from rl_b200.distributed.batched_data_dict import BatchedDataDict
+from rl_b200.models.transformer import KVCache, TransformerLM
+from rl_b200.ops.sampling import sample_tokens
+
+__all__ = ["RolloutEngine"]
+
+
+def _buckets(max_bs: int) -> list[int]:
+    out, b = [], 1
+    while b < max_bs:
+        out.append(b)
+        b *= 2
+    out.append(max_bs)
+    return sorted(set(out))
+
+
+class _DecodeState:
+    """Static device buffers for one batch bucket (graph inputs / outputs)."""
+
+    def __init__(self, B: int, max_blocks: int, max_new: int, device):
+        i32, i64 = torch.int32, torch.int64
+        self.B = B
+        self.tokens = torch.zeros(B, dtype=i64, device=device)
+        self.positions = torch.zeros(B, dtype=i32, device=device)
+        self.seq_lens = torch.zeros(B, dtype=i32, device=device)
+        self.slot = torch.zeros(B, dtype=i64, device=device)
+        self.block_tables = torch.zeros(B, max_blocks, dtype=i32, device=device)
+        self.done = torch.ones(B, dtype=torch.bool, device=device)
+        self.gen_len = torch.zeros(B, dtype=i32, device=device)
+        self.max_new = torch.zeros(B, dtype=i32, device=device)
+        self.step = torch.zeros(1, dtype=i64, device=device)
+        self.rng_offset = torch.zeros(1, dtype=i64, device=device)
+        self.out_tokens = torch.zeros(B, max_new + 1, dtype=i64, device=device)
+        self.out_logprobs = torch.zeros(B, max_new + 1, dtype=torch.float32, device=device)
+        self.next_tokens = torch.zeros(B, dtype=i64, device=device)
+        self.next_logprobs = torch.zeros(B, dtype=torch.float32, device=device)
+        self.graph: Optional[torch.cuda.CUDAGraph] = None
+
+
+class RolloutEngine:
+    def __init__(self, model: TransformerLM, gen_cfg: dict, max_num_seqs: int = 256, max_model_len: int = 2048,
+                 block_size: int = 256, kv_dtype: Optional[torch.dtype] = None, use_cuda_graphs: bool = True,
+                 seed: int = 0, sync_every: int = 32):
+        self.model = model
+        self.cfg = dict(gen_cfg)
+        self.device = model.device
+        self.max_num_seqs = max_num_seqs
+        self.max_model_len = max_model_len
+        self.block_size = block_size
+        self.kv_dtype = kv_dtype or model.dtype
+        self.use_cuda_graphs = use_cuda_graphs and self.device.type == "cuda"
+        self.seed = seed
+        self.sync_every = sync_every
+        self.kv: Optional[KVCache] = None
+        self.max_blocks_per_seq = math.ceil(max_model_len / block_size)
+        self._states: dict[int, _DecodeState] = {}
+        self._graph_pool = None
+        self.calls = 0
+        self.stats: dict = {}
+
+    # ------------------------------------------------------------ lifecycle
+    def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
+        """Allocate (wake) the KV cache."""
+        if self.kv is None:
+            n = num_seqs or self.max_num_seqs
+            blocks = n * self.max_blocks_per_seq + 1
+            self.kv = KVCache(self.model.cfg.num_layers, blocks, self.block_size, self.model.nkv, self.model.hd,
+                              self.kv_dtype, self.device)
+            self._kv_capacity_seqs = n
+        return True
+
+    def finish_generation(self) -> bool:
+        """Free (sleep) the KV cache and decode graphs so training gets the memory back."""
+        self.kv = None
+        for st in self._states.values():
+            st.graph = None
+        self._states.clear()
+        self._graph_pool = None
+        if self.device.type == "cuda":
+            torch.cuda.empty_cache()
+        return True
+
+    def invalidate_kv_cache(self) -> bool:
+        return True  # no prefix caching across refits: nothing to invalidate
+
+    def update_weights_from_training(self) -> None:
+        """Colocated refit: the engine reads the trainer's parameters directly."""
+        return None
+
+    # ------------------------------------------------------------ generation
+    @torch.no_grad()
+    def generate(self, data: BatchedDataDict, greedy: bool = False, max_new_tokens: Optional[int] = None
+                 ) -> BatchedDataDict:
+        input_ids: torch.Tensor = data["input_ids"]
+        lengths: torch.Tensor = data["input_lengths"].to(torch.int64)
+        B, S = input_ids.shape
+        cfg = self.cfg
+        max_new = int(max_new_tokens if max_new_tokens is not None else cfg.get("max_new_tokens", 16))
+        max_new = max(0, min(max_new, self.max_model_len - int(lengths.max())))
+        pad_id = int(cfg.get("pad_token_id", 0))
+        temperature = 0.0 if greedy else float(cfg.get("temperature", 1.0))
+        top_k = cfg.get("top_k")
+        top_p = float(cfg.get("top_p", 1.0) or 1.0)
+        stop_ids = list(cfg.get("stop_token_ids") or [])
+        out_ids = torch.full((B, S + max_new), pad_id, dtype=torch.int64)
+        out_lp = torch.zeros((B, S + max_new), dtype=torch.float32)
+        out_ids[:, :S] = input_ids.cpu()
+        gen_lens = torch.zeros(B, dtype=torch.int64)
+        self.calls += 1
+        if max_new == 0 or B == 0:
+            return self._pack_outputs(out_ids, out_lp, lengths, gen_lens, pad_id, max_new)
+
+        self.prepare_for_generation(max(B, getattr(self, "_kv_capacity_seqs", 0)))
+        if B > self._kv_capacity_seqs:
+            self.finish_generation()
+            self.prepare_for_generation(B)
+        dev = self.device
+        bs = self.block_size
+        nblk = self.max_blocks_per_seq
+        block_tables = (torch.arange(B * nblk, dtype=torch.int32).view(B, nblk) + 1).to(dev)  # block 0 = scratch
+
+        # ---- prefill (packed prompts) ----
+        lens_l = lengths.tolist()
+        flat = torch.cat([input_ids[b, : lens_l[b]].cpu() for b in range(B)]).to(dev)
+        positions = torch.cat([torch.arange(L, dtype=torch.int32) for L in lens_l]).to(dev)
+        cu = torch.zeros(B + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(lengths, 0)
+        cu_d = cu.to(dev)
+        seq_idx = torch.repeat_interleave(torch.arange(B), lengths).to(dev)
+        slot = (block_tables[seq_idx, (positions // bs).long()].long() * bs + (positions % bs).long())
+        last_idx = (cu[1:] - 1).to(dev).long()
+        h = self.model.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.kv, slot, last_idx)
+        logits = self.model.logits_infer(h)
+        gen = None
+        if dev.type == "cpu":
+            gen = torch.Generator().manual_seed(self.seed * 7919 + self.calls)
+        tok0, lp0 = sample_tokens(logits, temperature if temperature > 0 else 1.0,
+                                  1 if temperature == 0 else top_k, top_p, seed=self.seed + self.calls * 1000003,
+                                  offset=0, generator=gen)
+        if temperature == 0:
+            lp0 = torch.zeros_like(lp0)
+
+        # ---- decode ----
+        tokens_all, lps_all, glen = self._decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
+                                                      temperature, top_k, top_p, stop_ids, gen)
+        glen_c = glen.cpu().to(torch.int64)
+        toks_c = tokens_all.cpu()
+        lps_c = lps_all.cpu()
+        for b in range(B):
+            n = int(glen_c[b])
+            L = lens_l[b]
+            out_ids[b, L: L + n] = toks_c[b, :n]
+            out_lp[b, L: L + n] = lps_c[b, :n]
+        return self._pack_outputs(out_ids, out_lp, lengths, glen_c, pad_id, max_new)
+
+    def _pack_outputs(self, out_ids, out_lp, lengths, gen_lens, pad_id, max_new) -> BatchedDataDict:
+        unpadded = lengths.cpu() + gen_lens
+        width = int(unpadded.max()) if len(unpadded) else out_ids.shape[1]
+        width = max(width, 1)
+        return BatchedDataDict({
+            "output_ids": out_ids[:, :width].contiguous(),
+            "logprobs": out_lp[:, :width].contiguous(),
+            "generation_lengths": gen_lens.clone(),
+            "unpadded_sequence_lengths": unpadded,
+            "truncated": gen_lens >= max_new,
+        })
+
+    def _decode_loop(self, tok0, lp0, lengths, block_tables, max_new, temperature, top_k, top_p, stop_ids, gen):
+        dev = self.device
+        B = tok0.shape[0]
+        stop = torch.tensor(stop_ids if stop_ids else [-1], dtype=torch.int64, device=dev)
+        # Global outputs (original row order)
+        tokens_all = torch.zeros(B, max_new, dtype=torch.int64, device=dev)
+        lps_all = torch.zeros(B, max_new, dtype=torch.float32, device=dev)
+        tokens_all[:, 0] = tok0
+        lps_all[:, 0] = lp0
+        glen = torch.ones(B, dtype=torch.int32, device=dev)
+        done0 = torch.isin(tok0, stop) | (glen >= max_new)
+        active_rows = torch.nonzero(~done0).flatten()
+        if active_rows.numel() == 0:
+            return tokens_all, lps_all, glen
+        if self.device.type != "cuda" or not self.use_cuda_graphs:
+            return self._decode_eager(tokens_all, lps_all, glen, tok0, lengths, block_tables, max_new, temperature,
+                                      top_k, top_p, stop, gen, done0)
+        rows = active_rows
+        step_done = 1
+        while rows.numel() > 0 and step_done < max_new:
+            nb = next(b for b in _buckets(self.max_num_seqs) if b >= rows.numel()) \
+                if rows.numel() <= self.max_num_seqs else rows.numel()
+            st = self._state(nb, max_new)
+            n = rows.numel()
+            st.done.fill_(True)
+            st.done[:n] = False
+            st.tokens.zero_()
+            st.tokens[:n] = tokens_all[rows, step_done - 1]
+            st.positions.zero_()
+            st.positions[:n] = (lengths[rows] + step_done - 1).to(torch.int32)
+            st.block_tables.zero_()
+            st.block_tables[:n] = block_tables[rows]
+            st.gen_len.zero_()
+            st.gen_len[:n] = glen[rows]
+            st.max_new.fill_(max_new)
+            st.step.fill_(0)
+            st.rng_offset.fill_(step_done + 1)
+            st.out_tokens.zero_()
+            st.out_logprobs.zero_()
+            if st.graph is None:
+                self._capture(st, temperature, top_k, top_p, stop)
+            k = 0
+            while True:
+                st.graph.replay()
+                k += 1
+                step_done_k = step_done + k
+                if step_done_k >= max_new:
+                    break
+                if k % self.sync_every == 0:
+                    remaining = int((~st.done[:n]).sum().item())
+                    if remaining == 0:
+                        break
+                    if remaining <= n // 2 and nb > 1:
+                        break  # compact into a smaller bucket
+            # copy back this segment
+            seg_tok = st.out_tokens[:n, :k]
+            seg_lp = st.out_logprobs[:n, :k]
+            cols = torch.arange(step_done, step_done + k, device=dev).clamp_max(max_new - 1)
+            tokens_all[rows.unsqueeze(1), cols.unsqueeze(0)] = seg_tok
+            lps_all[rows.unsqueeze(1), cols.unsqueeze(0)] = seg_lp
+            glen[rows] = st.gen_len[:n]
+            still = ~st.done[:n]
+            step_done += k
+            rows = rows[still]
+        return tokens_all, lps_all, glen
+
+    def _state(self, nb: int, max_new: int) -> _DecodeState:
+        st = self._states.get(nb)
+        if st is None or st.out_tokens.shape[1] < max_new + 1:
+            st = _DecodeState(nb, self.max_blocks_per_seq, max_new, self.device)
+            self._states[nb] = st
+        return st
+
+    def _step_body(self, st: _DecodeState, temperature, top_k, top_p, stop):
+        """One decode step over the bucket (graph-capturable: no host syncs)."""
+        bs = self.block_size
+        blk = st.block_tables.gather(1, (st.positions // bs).long().unsqueeze(1)).squeeze(1)
+        st.slot.copy_(blk.long() * bs + (st.positions % bs).long())
+        st.seq_lens.copy_(st.positions + 1)
+        h = self.model.forward_decode(st.tokens, st.positions, self.kv, st.block_tables, st.seq_lens, st.slot,
+                                      self.max_model_len)
+        logits = self.model.logits_infer(h)
+        from rl_b200.ops.sampling import sample_tokens_graphable
+
+        sample_tokens_graphable(logits, temperature if temperature > 0 else 1.0,
+                                1 if temperature == 0 else top_k, top_p, self.seed + self.calls * 1000003,
+                                st.rng_offset, st.next_tokens, st.next_logprobs)
+        if temperature == 0:
+            st.next_logprobs.zero_()
+        active = ~st.done
+        st.out_tokens.scatter_(1, st.step.expand(st.B).unsqueeze(1), st.next_tokens.unsqueeze(1))
+        st.out_logprobs.scatter_(1, st.step.expand(st.B).unsqueeze(1), st.next_logprobs.unsqueeze(1))
+        st.gen_len.add_(active.to(torch.int32))
+        newly = torch.isin(st.next_tokens, stop) | (st.gen_len >= st.max_new)
+        st.done.logical_or_(newly)
+        st.tokens.copy_(st.next_tokens)
+        st.positions.add_(1)
+        st.step.add_(1)
+        st.rng_offset.add_(1)
+
+    def _capture(self, st: _DecodeState, temperature, top_k, top_p, stop):
+        # warm up on a side stream (allocations for the graph pool), then capture
+        saved = [t.clone() for t in (st.tokens, st.positions, st.done, st.gen_len, st.step, st.rng_offset,
+                                      st.out_tokens, st.out_logprobs)]
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            self._step_body(st, temperature, top_k, top_p, stop)
+        torch.cuda.current_stream().wait_stream(s)
+        for t, v in zip((st.tokens, st.positions, st.done, st.gen_len, st.step, st.rng_offset, st.out_tokens,
+                         st.out_logprobs), saved):
+            t.copy_(v)
+        if self._graph_pool is None:
+            self._graph_pool = torch.cuda.graph_pool_handle()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, pool=self._graph_pool):
+            self._step_body(st, temperature, top_k, top_p, stop)
+        st.graph = g
+
+    def _decode_eager(self, tokens_all, lps_all, glen, tok0, lengths, block_tables, max_new, temperature, top_k,
+                      top_p, stop, gen, done):
+        dev = self.device
+        bs = self.block_size
+        tokens = tok0.clone()
+        positions = lengths.to(torch.int32).clone()
+        for step in range(1, max_new):
+            if bool(done.all()):
+                break
+            blk = block_tables.gather(1, (positions // bs).long().unsqueeze(1)).squeeze(1)
+            slot = blk.long() * bs + (positions % bs).long()
+            h = self.model.forward_decode(tokens, positions, self.kv, block_tables, positions + 1, slot,
+                                          self.max_model_len)
+            logits = self.model.logits_infer(h)
+            nt, nlp = sample_tokens(logits, temperature if temperature > 0 else 1.0,
+                                    1 if temperature == 0 else top_k, top_p,
+                                    seed=self.seed + self.calls * 1000003, offset=step + 1, generator=gen)
+            if temperature == 0:
+                nlp = torch.zeros_like(nlp)
+            active = ~done
+            tokens_all[:, step] = torch.where(active, nt, tokens_all[:, step])
+            lps_all[:, step] = torch.where(active, nlp, lps_all[:, step])
+            glen += active.to(torch.int32)
+            done = done | torch.isin(nt, stop) | (glen >= max_new)
+            tokens = nt
+            positions = positions + 1
+        return tokens_all, lps_all, glen

@@ -1,0 +1,320 @@
+"""Per-GPU policy worker: trainer + rollout engine + reference policy on one device.
+
+Implements the policy-worker surface of the reference
+(``MegatronPolicyWorkerImpl`` ``nemo_rl/models/policy/workers/megatron_policy_worker.py:693``:
+``train`` ``:1382``, ``get_logprobs`` ``:2643``, ``use_reference_model`` ``:3128``,
+``offload_before_refit`` ``:4853``, ``save_checkpoint`` ``:5017``) for the SPMD
+design of this framework: every rank runs one worker; data arrive already
+sharded by data-parallel rank, and tensor-parallel peers see identical data.
+
+Training step (per global batch):
+  pack rows into token-budgeted micro-batches (sequence packing) ->
+  packed forward (THD) -> fused LM-head+logprob -> loss on padded [B, S-1]
+  views -> backward into fp32 main-grad buffers -> distributed AdamW step.
+"""
+
+from __future__ import annotations
+
+import contextlib
+import math
+import time
+from typing import Any, Optional
+
+import torch
+import torch.distributed as dist
+
+from rl_b200.data.packing import get_packer
+from rl_b200.distributed.batched_data_dict import BatchedDataDict
+from rl_b200.models.config import ModelConfig, get_model_config
+from rl_b200.models.generation.engine import RolloutEngine
+from rl_b200.models.transformer import TransformerLM
+from rl_b200.ops.fused_linear_logprob import linear_logprobs
+from rl_b200.parallel.dist_optimizer import FlatAdamW
+from rl_b200.parallel.state import ParallelState, get_parallel_state
+from rl_b200.utils.timer import Timer
+
+__all__ = ["PolicyWorker", "pack_rows"]
+
+
+def _dtype(precision: str) -> torch.dtype:
+    return {"bfloat16": torch.bfloat16, "bf16": torch.bfloat16, "float32": torch.float32, "fp32": torch.float32,
+            "float16": torch.float16}.get(str(precision), torch.bfloat16)
+
+
+def pack_rows(input_ids: torch.Tensor, lengths: list[int], rows: list[int], pad_to_multiple: int = 1):
+    """Concatenate the unpadded rows into one packed sequence batch.
+
+    Returns (flat_ids [T], positions [T] int32, cu_seqlens [n+1] int32, max_len,
+    T_real).  When ``pad_to_multiple`` > 1 a dummy tail sequence pads T up to the
+    multiple (needed for sequence parallelism)."""
+    pieces, pos, cu = [], [], [0]
+    for r in rows:
+        L = int(lengths[r])
+        pieces.append(input_ids[r, :L])
+        pos.append(torch.arange(L, dtype=torch.int32))
+        cu.append(cu[-1] + L)
+    T = cu[-1]
+    pad = (-T) % pad_to_multiple
+    if pad:
+        pieces.append(torch.zeros(pad, dtype=input_ids.dtype))
+        pos.append(torch.arange(pad, dtype=torch.int32))
+        cu.append(cu[-1] + pad)
+    flat = torch.cat(pieces) if pieces else torch.zeros(0, dtype=input_ids.dtype)
+    max_len = max((cu[i + 1] - cu[i]) for i in range(len(cu) - 1)) if len(cu) > 1 else 0
+    return flat, torch.cat(pos), torch.tensor(cu, dtype=torch.int32), max_len, T
+
+
+class PolicyWorker:
+    def __init__(self, policy_cfg: dict, model_cfg: Optional[ModelConfig] = None,
+                 pstate: Optional[ParallelState] = None, seed: int = 0, init_reference_model: bool = True,
+                 loss_cfg: Optional[dict] = None):
+        self.cfg = policy_cfg
+        self.ps = pstate or get_parallel_state()
+        self.device = self.ps.device
+        self.model_cfg = model_cfg or get_model_config(policy_cfg.get("model_name", "tiny-llama"))
+        self.dtype = _dtype(policy_cfg.get("precision", "bfloat16"))
+        if self.device.type == "cpu" and self.dtype != torch.float32:
+            self.dtype = torch.float32
+        mc = policy_cfg.get("megatron_cfg", {}) or {}
+        self.sequence_parallel = bool(mc.get("sequence_parallel", False)) and self.ps.tp_size > 1
+        act_ckpt = bool(mc.get("activation_checkpointing", policy_cfg.get("activation_checkpointing", False)))
+        self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
+                                   sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt)
+        opt = policy_cfg.get("optimizer", {}) or {}
+        kw = dict(opt.get("kwargs", {}) or {})
+        mopt = mc.get("optimizer", {}) or {}
+        lr = float(kw.get("lr", mopt.get("lr", 1e-5)))
+        betas = kw.get("betas", [mopt.get("adam_beta1", 0.9), mopt.get("adam_beta2", 0.999)])
+        eps = float(kw.get("eps", mopt.get("adam_eps", 1e-8)))
+        wd = float(kw.get("weight_decay", mopt.get("weight_decay", 0.0)))
+        sched = policy_cfg.get("scheduler") if policy_cfg.get("scheduler") is not None else mc.get("scheduler")
+        grad_group = self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group
+        self.optimizer = FlatAdamW(self.model, lr=lr, betas=tuple(float(b) for b in betas), eps=eps, weight_decay=wd,
+                                   max_grad_norm=policy_cfg.get("max_grad_norm", 1.0), scheduler_cfg=sched,
+                                   min_lr=float(mopt.get("min_lr", 0.0)), dp_group=grad_group,
+                                   tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel)
+        gen_cfg = dict(policy_cfg.get("generation", {}) or {})
+        mgc = gen_cfg.get("mcore_generation_config", {}) or {}
+        self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
+        self.engine = RolloutEngine(
+            self.model, gen_cfg, max_num_seqs=int(gen_cfg.get("max_num_seqs", 256)),
+            max_model_len=self.max_seq_len, block_size=int(mgc.get("block_size_tokens", 256)),
+            use_cuda_graphs=bool(gen_cfg.get("use_cuda_graphs", True)),
+            seed=seed * 7 + self.ps.dp_rank * 100003,
+        )
+        self.ref_flat: Optional[torch.Tensor] = None
+        if init_reference_model:
+            self.ref_flat = self.model.flat_param.detach().clone()
+        sp = policy_cfg.get("sequence_packing", {}) or {}
+        self.train_mb_tokens = int(sp.get("train_mb_tokens", self.max_seq_len * int(policy_cfg.get("train_micro_batch_size", 4))))
+        self.logprob_mb_tokens = int(sp.get("logprob_mb_tokens", self.train_mb_tokens))
+        self.packing_algorithm = sp.get("algorithm", "modified_first_fit_decreasing")
+        self.logprob_chunk = int(policy_cfg.get("logprob_chunk_size") or 4096)
+        self.timer = Timer()
+
+    # ------------------------------------------------------------- helpers
+    def _plan(self, lengths: list[int], rows: list[int], budget: int) -> list[list[int]]:
+        budget = max(budget, max(lengths[r] for r in rows))
+        packer = get_packer(self.packing_algorithm, bin_capacity=budget)
+        bins = packer.pack([max(1, lengths[r]) for r in rows])
+        return [[rows[i] for i in b] for b in bins]
+
+    def _forward_mb(self, input_ids: torch.Tensor, lengths: list[int], rows: list[int], temperature: float):
+        """Packed forward of ``rows``; returns per-token next-token (logprob, entropy)
+        ``[T]`` aligned so that entry j scores token j+1, plus the packing metadata."""
+        tp = self.ps.tp_size if self.sequence_parallel else 1
+        flat, pos, cu, max_len, T_real = pack_rows(input_ids, lengths, rows, pad_to_multiple=tp)
+        dev = self.device
+        flat_d, pos_d, cu_d = flat.to(dev, non_blocking=True), pos.to(dev, non_blocking=True), cu.to(dev)
+        targets = torch.empty_like(flat_d)
+        targets[:-1] = flat_d[1:]
+        targets[-1:] = 0
+        hidden = self.model(flat_d, pos_d, cu_d, max_len)
+        h = self.model.lm_input(hidden)
+        lp, ent = linear_logprobs(h, self.model.lm_head_weight(), targets, self.model.vocab_start, temperature,
+                                  self.ps.tp_group if self.ps.tp_size > 1 else None, self.logprob_chunk)
+        return lp, ent, cu
+
+    @staticmethod
+    def _to_padded(lp: torch.Tensor, cu: torch.Tensor, n_rows: int, width: int) -> torch.Tensor:
+        """Packed next-token scores -> ``[n, width-1]`` where column i scores token i+1."""
+        cu_l = cu.tolist()
+        src, dst = [], []
+        for b in range(n_rows):
+            s, e = cu_l[b], cu_l[b + 1]
+            L = e - s
+            if L > 1:
+                src.append(torch.arange(s, e - 1))
+                dst.append(torch.arange(L - 1) + b * (width - 1))
+        out = lp.new_zeros(n_rows * (width - 1))
+        if src:
+            si = torch.cat(src).to(lp.device)
+            di = torch.cat(dst).to(lp.device)
+            out = out.index_copy(0, di, lp.index_select(0, si))
+        return out.view(n_rows, width - 1)
+
+    def _lengths(self, data: BatchedDataDict) -> list[int]:
+        key = "input_lengths" if "input_lengths" in data else "unpadded_sequence_lengths"
+        return [int(x) for x in data[key].tolist()]
+
+    # --------------------------------------------------------- logprobs
+    @torch.no_grad()
+    def get_logprobs(self, data: BatchedDataDict, temperature: Optional[float] = None) -> BatchedDataDict:
+        """Logprob of token i at index i (index 0 = 0), ``[B, S]`` fp32 on CPU."""
+        temperature = float(temperature if temperature is not None else
+                            (self.cfg.get("generation", {}) or {}).get("temperature", 1.0) or 1.0)
+        ids = data["input_ids"]
+        B, S = ids.shape
+        lengths = self._lengths(data)
+        out = torch.zeros(B, S, dtype=torch.float32)
+        rows_all = [r for r in range(B) if lengths[r] > 0]
+        self.model.eval()
+        for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
+            lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
+            padded = self._to_padded(lp.float(), cu, len(rows), S).cpu()
+            out[torch.tensor(rows), 1:] = padded
+        self.model.train()
+        return BatchedDataDict({"logprobs": out})
+
+    @contextlib.contextmanager
+    def use_reference_model(self):
+        """Swap the reference (initial) weights into the live parameter buffer."""
+        if self.ref_flat is None:
+            raise RuntimeError("reference model was not initialised")
+        flat = self.model.flat_param
+        n = self.ref_flat.numel()
+        saved = flat[:n].clone()
+        flat[:n].copy_(self.ref_flat)
+        try:
+            yield
+        finally:
+            flat[:n].copy_(saved)
+            del saved
+
+    @torch.no_grad()
+    def get_reference_policy_logprobs(self, data: BatchedDataDict, temperature: Optional[float] = None):
+        with self.use_reference_model():
+            lp = self.get_logprobs(data, temperature)["logprobs"]
+        return BatchedDataDict({"reference_logprobs": lp})
+
+    # ------------------------------------------------------------- train
+    def train(self, data: BatchedDataDict, loss_fn, gbs: Optional[int] = None, eval_mode: bool = False,
+              temperature: Optional[float] = None) -> dict:
+        """One or more optimizer steps over ``data`` (this rank's shard).
+
+        ``gbs`` is the LOCAL number of rows per optimizer step (global batch / dp)."""
+        temperature = float(temperature if temperature is not None else
+                            (self.cfg.get("generation", {}) or {}).get("temperature", 1.0) or 1.0)
+        ids = data["input_ids"]
+        B, S = ids.shape
+        gbs = gbs or B
+        lengths = self._lengths(data)
+        all_metrics: list[dict] = []
+        losses, grad_norms, lrs = [], [], []
+        for g0 in range(0, B, gbs):
+            rows = list(range(g0, min(B, g0 + gbs)))
+            tok_mask = data["token_mask"][rows, 1:].float()
+            smask = data["sample_mask"][rows].float()
+            local_toks = (tok_mask * smask.unsqueeze(-1)).sum()
+            local_seqs = smask.sum()
+            counts = torch.stack([local_toks, local_seqs]).to(self.device)
+            if self.ps.dp_size > 1 or self.ps.cp_size > 1:
+                dist.all_reduce(counts, group=self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group)
+            gtoks, gseqs = counts[0], counts[1]
+            mb_plan = self._plan(lengths, [r for r in rows if lengths[r] > 0], self.train_mb_tokens)
+            self.model.aux_loss_scale = 1.0 / max(1, len(mb_plan))
+            step_loss = torch.zeros((), device=self.device)
+            mb_metrics: list[dict] = []
+            for mb_rows in mb_plan:
+                lp, ent, cu = self._forward_mb(ids, lengths, mb_rows, temperature)
+                width = max(lengths[r] for r in mb_rows)
+                curr = self._to_padded(lp, cu, len(mb_rows), width)
+                mb = data.select_indices(mb_rows)
+                mb.truncate_tensors(1, width)
+                mb = BatchedDataDict({k: (v.to(self.device) if isinstance(v, torch.Tensor) else v)
+                                      for k, v in mb.items()})
+                loss, metrics = loss_fn(curr, mb, gseqs, gtoks)
+                if not eval_mode:
+                    loss.backward()
+                    self.optimizer._fold_param_grads()
+                step_loss += loss.detach()
+                mb_metrics.append(metrics)
+            if not eval_mode:
+                opt_stats = self.optimizer.step()
+                grad_norms.append(opt_stats["grad_norm"])
+                lrs.append(opt_stats["lr"])
+            else:
+                self.optimizer.zero_grad()
+            if self.ps.dp_size > 1:
+                dist.all_reduce(step_loss, group=self.ps.dp_group)
+            losses.append(float(step_loss))
+            all_metrics.extend(mb_metrics)
+        agg = aggregate_metrics(all_metrics, self.ps.dp_group if self.ps.dp_size > 1 else None)
+        agg.update({"loss": sum(losses) / max(1, len(losses)), "global_loss": losses,
+                    "grad_norm": grad_norms[-1] if grad_norms else 0.0, "lr": lrs[-1] if lrs else 0.0,
+                    "moe_aux_loss": self.model.aux_loss()})
+        return agg
+
+    # -------------------------------------------------------- generation
+    def generate(self, data: BatchedDataDict, greedy: bool = False) -> BatchedDataDict:
+        return self.engine.generate(data, greedy=greedy)
+
+    def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
+        return self.engine.prepare_for_generation(num_seqs)
+
+    def finish_generation(self) -> bool:
+        return self.engine.finish_generation()
+
+    def prepare_for_training(self) -> None:
+        self.model.train()
+
+    def prepare_for_lp_inference(self) -> None:
+        self.model.eval()
+
+    def refit(self) -> float:
+        """Make the rollout weights current.  Colocated and same layout: the
+        optimizer step already wrote the bf16 parameters the engine reads, so the
+        refit is a no-op apart from invalidating cached state."""
+        t0 = time.perf_counter()
+        self.engine.update_weights_from_training()
+        self.engine.invalidate_kv_cache()
+        return time.perf_counter() - t0
+
+    def offload_before_refit(self) -> None:
+        pass
+
+    def offload_after_refit(self) -> None:
+        pass
+
+
+_MIN_KEYS = ("_min",)
+_MAX_KEYS = ("_max",)
+
+
+def aggregate_metrics(metrics: list[dict], group=None) -> dict:
+    """Combine per-micro-batch loss metrics: globally-normalised means add up,
+    ``*_min`` / ``*_max`` take min / max; then reduce the same way over DP."""
+    out: dict[str, float] = {}
+    for m in metrics:
+        for k, v in m.items():
+            if not isinstance(v, (int, float)):
+                continue
+            if k.endswith(_MIN_KEYS):
+                out[k] = min(out.get(k, math.inf), v)
+            elif k.endswith(_MAX_KEYS):
+                out[k] = max(out.get(k, -math.inf), v)
+            else:
+                out[k] = out.get(k, 0.0) + v
+    if group is not None and dist.is_initialized() and out:
+        keys = sorted(out)
+        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
+        for kind, op in (("min", dist.ReduceOp.MIN), ("max", dist.ReduceOp.MAX), ("sum", dist.ReduceOp.SUM)):
+            ks = [k for k in keys if (kind == "min" and k.endswith("_min")) or (kind == "max" and k.endswith("_max"))
+                  or (kind == "sum" and not k.endswith(("_min", "_max")))]
+            if not ks:
+                continue
+            t = torch.tensor([out[k] for k in ks], dtype=torch.float64, device=dev)
+            dist.all_reduce(t, op=op, group=group)
+            for k, v in zip(ks, t.tolist()):
+                out[k] = v
+    return out

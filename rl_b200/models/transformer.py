@@ -1,0 +1,541 @@
+"""Decoder-only transformer (Llama / Qwen3 dense and Qwen3-MoE families) used by
+both the trainer and the in-house rollout engine.
+
+B200-first layout decisions
+---------------------------
+* All parameters of the (TP/EP-local) model live in ONE flat buffer; every
+  ``nn.Parameter`` is a view into it.  The fp32 gradient buffer (``main_grad``
+  views), the optimizer's master weights and Adam moments mirror the same
+  flat layout.  One kernel launch then updates the whole model, distributed
+  optimizer shards are plain contiguous ranges, and the colocated refit is the
+  bf16 write of that same launch.
+* Activations are packed (THD): ``[T, H]`` with ``cu_seqlens``; no padding
+  tokens are ever computed.
+* The training forward and the rollout prefill/decode paths share weights and
+  kernels (RMSNorm, RoPE, SwiGLU, attention), which keeps train/rollout
+  log-probabilities consistent (``train/gen_kl_error``).
+* Tensor parallelism: column-parallel QKV and gate/up, row-parallel O and down
+  projections, vocab-parallel embedding and LM head; optional sequence
+  parallelism (residual stream sharded over tokens between TP regions).
+* MoE: router (fp32) -> top-k (softmax, optional renormalisation) -> token
+  permutation by expert -> grouped expert GEMMs -> weighted combine; experts
+  are sharded over the expert-parallel group with an all-to-all exchange.
+
+Reference: the model is built by Megatron-Bridge / MCore in the reference
+(``nemo_rl/models/megatron/setup.py:2520``, forward ``nemo_rl/models/megatron/train.py:158``);
+the per-layer op sequence is the one in section 3.3 of the survey.
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from typing import Callable, Optional
+
+import torch
+import torch.nn as nn
+import torch.utils.checkpoint as ckpt
+
+from rl_b200.models.config import ModelConfig
+from rl_b200.ops.activation import swiglu
+from rl_b200.ops.attention import flash_attn_varlen, flash_attn_varlen_fwd, paged_decode_attention, write_kv_cache
+from rl_b200.ops.linear import linear
+from rl_b200.ops.norm import add_rms_norm, rms_norm
+from rl_b200.ops.rope import apply_rope_qkv, build_rope_cache
+from rl_b200.parallel.comm import (all_to_all_autograd, copy_to_tp, gather_from_sp, reduce_from_tp,
+                                   reduce_scatter_to_sp)
+from rl_b200.parallel.state import ParallelState, single_process_state
+
+__all__ = ["TransformerLM", "ParamSpec", "KVCache"]
+
+
+@dataclass
+class ParamSpec:
+    name: str            # HF-style name, e.g. model.layers.0.self_attn.qkv_proj.weight
+    shape: tuple
+    init: str            # "normal", "ones", "zeros"
+    tp_dim: Optional[int] = None   # dim sharded over TP (None = replicated)
+    ep_dim: Optional[int] = None   # dim sharded over EP (experts)
+    offset: int = 0
+    numel: int = 0
+    no_weight_decay: bool = False
+
+
+class KVCache:
+    """Paged KV cache: per layer ``[num_blocks, block_size, nkv_local, hd]`` for K and V."""
+
+    def __init__(self, num_layers: int, num_blocks: int, block_size: int, nkv: int, hd: int, dtype, device):
+        self.block_size = block_size
+        self.num_blocks = num_blocks
+        self.dtype = dtype
+        shape = (num_layers, 2, num_blocks, block_size, nkv, hd)
+        self.storage = torch.zeros(shape, dtype=dtype, device=device)
+        self.k_scale = 1.0
+        self.v_scale = 1.0
+
+    def layer(self, i: int):
+        return self.storage[i, 0], self.storage[i, 1]
+
+    def nbytes(self) -> int:
+        return self.storage.numel() * self.storage.element_size()
+
+
+class _AuxLossScaler(torch.autograd.Function):
+    """Attach an auxiliary loss to an activation: forward is the identity, backward
+    injects ``scale * d(aux)`` so the aux loss trains without being added to the
+    main loss value (MoE load balancing)."""
+
+    @staticmethod
+    def forward(ctx, x, aux, scale):
+        ctx.save_for_backward(aux)
+        ctx.scale = scale
+        return x
+
+    @staticmethod
+    def backward(ctx, g):
+        (aux,) = ctx.saved_tensors
+        return g, torch.full_like(aux, ctx.scale), None
+
+
+class TransformerLM(nn.Module):
+    def __init__(self, cfg: ModelConfig, pstate: Optional[ParallelState] = None, device=None,
+                 dtype: torch.dtype = torch.bfloat16, seed: int = 0, sequence_parallel: bool = False,
+                 activation_checkpointing: bool = False, init_std: float = 0.02):
+        super().__init__()
+        self.cfg = cfg
+        self.ps = pstate or single_process_state(torch.device(device) if device else None)
+        self.device = torch.device(device) if device is not None else self.ps.device
+        self.dtype = dtype
+        self.sequence_parallel = sequence_parallel and self.ps.tp_size > 1
+        self.activation_checkpointing = activation_checkpointing
+        tp, ep = self.ps.tp_size, self.ps.ep_size
+        if cfg.num_heads % tp or cfg.num_kv_heads % tp:
+            raise ValueError(f"heads ({cfg.num_heads}/{cfg.num_kv_heads}) must divide by tp={tp}")
+        if cfg.vocab_size % tp:
+            raise ValueError(f"vocab {cfg.vocab_size} must divide by tp={tp}")
+        self.nq = cfg.num_heads // tp
+        self.nkv = cfg.num_kv_heads // tp
+        self.hd = cfg.head_dim
+        self.vocab_local = cfg.vocab_size // tp
+        self.vocab_start = self.ps.tp_rank * self.vocab_local
+        if cfg.is_moe:
+            if cfg.num_experts % ep:
+                raise ValueError(f"experts {cfg.num_experts} must divide by ep={ep}")
+            self.experts_local = cfg.num_experts // ep
+            self.expert_start = self.ps.ep_rank * self.experts_local
+        else:
+            if cfg.ffn_hidden_size % tp:
+                raise ValueError(f"ffn {cfg.ffn_hidden_size} must divide by tp={tp}")
+            self.ffn_local = cfg.ffn_hidden_size // tp
+        self.specs = self._make_specs()
+        self._allocate(seed, init_std)
+        self.rope_cache = build_rope_cache(min(cfg.max_position_embeddings, 1 << 17), cfg.head_dim,
+                                           cfg.rope_theta, cfg.rope_scaling, device=self.device)
+        self._aux_losses: list[torch.Tensor] = []
+        self.aux_loss_scale = 0.0
+        self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
+        self.router_record: Optional[dict] = None
+
+    # ------------------------------------------------------------------ params
+    def _make_specs(self) -> list[ParamSpec]:
+        c = self.cfg
+        H, hd = c.hidden_size, c.head_dim
+        s: list[ParamSpec] = [ParamSpec("model.embed_tokens.weight", (self.vocab_local, H), "normal", tp_dim=0)]
+        for i in range(c.num_layers):
+            p = f"model.layers.{i}."
+            s.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones", no_weight_decay=True))
+            s.append(ParamSpec(p + "self_attn.qkv_proj.weight", ((self.nq + 2 * self.nkv) * hd, H), "normal", tp_dim=0))
+            if c.qk_norm:
+                s.append(ParamSpec(p + "self_attn.q_norm.weight", (hd,), "ones", no_weight_decay=True))
+                s.append(ParamSpec(p + "self_attn.k_norm.weight", (hd,), "ones", no_weight_decay=True))
+            s.append(ParamSpec(p + "self_attn.o_proj.weight", (H, self.nq * hd), "normal_out", tp_dim=1))
+            s.append(ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones", no_weight_decay=True))
+            if c.is_moe:
+                F = c.moe_ffn_hidden_size
+                s.append(ParamSpec(p + "mlp.gate.weight", (c.num_experts, H), "normal"))
+                s.append(ParamSpec(p + "mlp.experts.gate_up_proj", (self.experts_local, 2 * F, H), "normal", ep_dim=0))
+                s.append(ParamSpec(p + "mlp.experts.down_proj", (self.experts_local, H, F), "normal_out", ep_dim=0))
+            else:
+                s.append(ParamSpec(p + "mlp.gate_up_proj.weight", (2 * self.ffn_local, H), "normal", tp_dim=0))
+                s.append(ParamSpec(p + "mlp.down_proj.weight", (H, self.ffn_local), "normal_out", tp_dim=1))
+        s.append(ParamSpec("model.norm.weight", (H,), "ones", no_weight_decay=True))
+        if not c.tie_word_embeddings:
+            s.append(ParamSpec("lm_head.weight", (self.vocab_local, H), "normal", tp_dim=0))
+        off = 0
+        align = 64  # keep every parameter 128-byte aligned (bf16) for vector / TMA access
+        for sp in s:
+            sp.numel = int(math.prod(sp.shape))
+            sp.offset = off
+            off += (sp.numel + align - 1) // align * align
+        self.flat_numel = off
+        return s
+
+    def _allocate(self, seed: int, std: float) -> None:
+        self.flat_param = torch.empty(self.flat_numel, dtype=self.dtype, device=self.device)
+        self.flat_param.zero_()
+        gen = torch.Generator(device="cpu")
+        out_std = std / math.sqrt(2 * self.cfg.num_layers)
+        self._params: dict[str, nn.Parameter] = {}
+        for sp in self.specs:
+            view = self.flat_param[sp.offset: sp.offset + sp.numel].view(sp.shape)
+            # Seed per (name, shard) so every TP/EP layout of one seed agrees on the
+            # full tensor: generate the FULL tensor's shard deterministically.
+            gen.manual_seed((seed * 1000003 + (hash_name(sp.name) & 0x7FFFFFFF)) & 0x7FFFFFFFFFFF)
+            if sp.init == "ones":
+                view.fill_(1.0)
+            elif sp.init == "zeros":
+                view.zero_()
+            else:
+                s = std if sp.init == "normal" else out_std
+                full_shape = list(sp.shape)
+                shard_idx, shard_dim, n_shards = 0, None, 1
+                if sp.tp_dim is not None and self.ps.tp_size > 1:
+                    shard_dim, n_shards, shard_idx = sp.tp_dim, self.ps.tp_size, self.ps.tp_rank
+                elif sp.ep_dim is not None and self.ps.ep_size > 1:
+                    shard_dim, n_shards, shard_idx = sp.ep_dim, self.ps.ep_size, self.ps.ep_rank
+                if shard_dim is not None:
+                    full_shape[shard_dim] *= n_shards
+                full = torch.randn(full_shape, generator=gen, dtype=torch.float32) * s
+                if shard_dim is not None:
+                    full = self.shard_full_tensor(sp, full, shard_idx, n_shards)
+                view.copy_(full.to(self.dtype))
+            p = nn.Parameter(view, requires_grad=True)
+            self._params[sp.name] = p
+            self.register_parameter(sp.name.replace(".", "__"), p)
+
+    def shard_full_tensor(self, sp: ParamSpec, full: torch.Tensor, idx: int, n: int) -> torch.Tensor:
+        """Slice a full (unsharded) tensor into this rank's shard, honouring the
+        fused layouts (QKV rows are [q heads | k heads | v heads]; gate/up rows are
+        [gate | up]) so that every shard holds matching heads / FFN columns."""
+        c = self.cfg
+        if sp.name.endswith("qkv_proj.weight"):
+            hd = c.head_dim
+            q, k, v = torch.split(full, [c.num_heads * hd, c.num_kv_heads * hd, c.num_kv_heads * hd], 0)
+            return torch.cat([q.chunk(n, 0)[idx], k.chunk(n, 0)[idx], v.chunk(n, 0)[idx]], 0)
+        if sp.name.endswith("gate_up_proj.weight"):
+            g, u = full.chunk(2, 0)
+            return torch.cat([g.chunk(n, 0)[idx], u.chunk(n, 0)[idx]], 0)
+        dim = sp.tp_dim if sp.tp_dim is not None else sp.ep_dim
+        return full.chunk(n, dim)[idx]
+
+    def param(self, name: str) -> nn.Parameter:
+        return self._params[name]
+
+    def named_flat_params(self):
+        for sp in self.specs:
+            yield sp, self._params[sp.name]
+
+    # ------------------------------------------------------------ embeddings
+    def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
+        w = self._params["model.embed_tokens.weight"]
+        if self.ps.tp_size == 1:
+            return w[input_ids]
+        local = input_ids - self.vocab_start
+        inside = (local >= 0) & (local < self.vocab_local)
+        x = w[local.clamp(0, self.vocab_local - 1)] * inside.unsqueeze(-1).to(w.dtype)
+        if self.sequence_parallel:
+            return reduce_scatter_to_sp(x, self.ps.tp_group)
+        return reduce_from_tp(x, self.ps.tp_group)
+
+    def lm_head_weight(self) -> torch.Tensor:
+        if self.cfg.tie_word_embeddings:
+            return self._params["model.embed_tokens.weight"]
+        return self._params["lm_head.weight"]
+
+    # -------------------------------------------------------------- attention
+    def _qkv(self, i: int, h: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+        p = f"model.layers.{i}."
+        qkv = linear(h, self._params[p + "self_attn.qkv_proj.weight"])
+        if self.cfg.qk_norm:
+            T = qkv.shape[0]
+            q, k, v = torch.split(qkv, [self.nq * self.hd, self.nkv * self.hd, self.nkv * self.hd], -1)
+            q = rms_norm(q.reshape(T * self.nq, self.hd), self._params[p + "self_attn.q_norm.weight"],
+                         self.cfg.rms_eps).view(T, -1)
+            k = rms_norm(k.reshape(T * self.nkv, self.hd), self._params[p + "self_attn.k_norm.weight"],
+                         self.cfg.rms_eps).view(T, -1)
+            qkv = torch.cat([q, k, v], -1)
+        return apply_rope_qkv(qkv, positions, self.rope_cache, self.nq, self.nkv, self.hd)
+
+    def _split_heads(self, qkv: torch.Tensor):
+        T = qkv.shape[0]
+        x = qkv.view(T, self.nq + 2 * self.nkv, self.hd)
+        return x[:, : self.nq], x[:, self.nq: self.nq + self.nkv], x[:, self.nq + self.nkv:]
+
+    def _attn_block(self, i: int, h: torch.Tensor, positions, cu_seqlens, max_seqlen) -> torch.Tensor:
+        p = f"model.layers.{i}."
+        if self.sequence_parallel:
+            h = gather_from_sp(h, self.ps.tp_group)
+        else:
+            h = copy_to_tp(h, self.ps.tp_group)
+        qkv = self._qkv(i, h, positions)
+        q, k, v = self._split_heads(qkv)
+        o = flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=True)
+        out = linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"])
+        return self._row_parallel_out(out)
+
+    def _row_parallel_out(self, out: torch.Tensor) -> torch.Tensor:
+        if self.ps.tp_size == 1:
+            return out
+        if self.sequence_parallel:
+            return reduce_scatter_to_sp(out, self.ps.tp_group)
+        return reduce_from_tp(out, self.ps.tp_group)
+
+    # -------------------------------------------------------------------- MLP
+    def _mlp_block(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        if self.cfg.is_moe:
+            return self._moe_block(i, h)
+        p = f"model.layers.{i}."
+        if self.sequence_parallel:
+            h = gather_from_sp(h, self.ps.tp_group)
+        else:
+            h = copy_to_tp(h, self.ps.tp_group)
+        gu = linear(h, self._params[p + "mlp.gate_up_proj.weight"])
+        a = swiglu(gu)
+        out = linear(a, self._params[p + "mlp.down_proj.weight"])
+        return self._row_parallel_out(out)
+
+    def route(self, i: int, h: torch.Tensor):
+        """Router: fp32 logits -> softmax -> top-k (+ renormalisation); returns
+        (topk_weights [T,k] fp32, topk_ids [T,k] int64, probs [T,E] fp32)."""
+        c = self.cfg
+        w = self._params[f"model.layers.{i}.mlp.gate.weight"]
+        rdtype = torch.float64 if c.moe_router_dtype == "fp64" else torch.float32
+        logits = torch.matmul(h.to(rdtype), w.to(rdtype).t())
+        probs = torch.softmax(logits, -1)
+        if self.router_replay is not None and i in self.router_replay:
+            ids = self.router_replay[i].to(h.device).long()
+            vals = probs.gather(-1, ids)
+        else:
+            vals, ids = torch.topk(probs, c.moe_top_k, dim=-1)
+        if self.router_record is not None:
+            self.router_record[i] = ids.detach().to(torch.int16 if c.num_experts < 32768 else torch.int32).cpu()
+        if c.moe_norm_topk_prob:
+            vals = vals / vals.sum(-1, keepdim=True)
+        return vals.to(torch.float32), ids, probs.to(torch.float32)
+
+    def _moe_block(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        c = self.cfg
+        p = f"model.layers.{i}."
+        if self.sequence_parallel:
+            h = gather_from_sp(h, self.ps.tp_group)
+        T, H = h.shape
+        k, E = c.moe_top_k, c.num_experts
+        weights, ids, probs = self.route(i, h)
+        if c.moe_aux_loss_coef > 0 and torch.is_grad_enabled():
+            # Switch-style load balance: E * sum_e f_e * P_e
+            counts = torch.zeros(E, device=h.device, dtype=torch.float32).index_add_(
+                0, ids.reshape(-1), torch.ones(T * k, device=h.device))
+            f = counts / max(1, T * k)
+            aux = E * (f.detach() * probs.mean(0)).sum() * c.moe_aux_loss_coef
+            h = _AuxLossScaler.apply(h, aux, self.aux_loss_scale if self.aux_loss_scale else 1.0)
+            self._aux_losses.append(aux.detach())
+        flat_ids = ids.reshape(-1)
+        order = torch.argsort(flat_ids, stable=True)
+        token_of = order // k
+        xs = h[token_of]                                             # [T*k, H] permuted by expert
+        counts = torch.bincount(flat_ids, minlength=E)
+        wgu = self._params[p + "mlp.experts.gate_up_proj"]
+        wdn = self._params[p + "mlp.experts.down_proj"]
+        if self.ps.ep_size > 1:
+            ys = self._moe_ep_experts(xs, counts, wgu, wdn)
+        else:
+            ys = grouped_swiglu_mlp(xs, counts, wgu, wdn)
+        # combine: out[t] += w[t, j] * y
+        wflat = weights.reshape(-1)[order].to(ys.dtype).unsqueeze(-1)
+        out = torch.zeros(T, H, dtype=ys.dtype, device=h.device).index_add_(0, token_of, ys * wflat)
+        if self.sequence_parallel:
+            out = reduce_scatter_to_sp(out, self.ps.tp_group)
+        return out
+
+    def _moe_ep_experts(self, xs, counts, wgu, wdn):
+        """Expert-parallel path: all-to-all tokens to the ranks owning their experts,
+        run the local experts, all-to-all back (NCCL baseline of the fused dispatch)."""
+        import torch.distributed as dist
+
+        ep, g = self.ps.ep_size, self.ps.ep_group
+        El = self.experts_local
+        send_per_rank = counts.view(ep, El).sum(-1)
+        all_counts = torch.empty(ep * ep * El, dtype=counts.dtype, device=counts.device)
+        dist.all_gather_into_tensor(all_counts, counts.contiguous(), group=g)
+        all_counts = all_counts.view(ep, ep, El)          # [src_rank, dst_rank, local_expert]
+        me = self.ps.ep_rank
+        recv = all_counts[:, me, :]                       # [src, El]
+        send_splits = send_per_rank.tolist()
+        recv_splits = recv.sum(-1).tolist()
+        xr = all_to_all_autograd(xs, send_splits, recv_splits, g)
+        # received rows are grouped by source, then by local expert: regroup by expert
+        src_off = torch.cumsum(torch.cat([recv.new_zeros(1), recv.sum(-1)]), 0)
+        idx = []
+        for e in range(El):
+            for s in range(ep):
+                start = int(src_off[s]) + int(recv[s, :e].sum())
+                idx.append(torch.arange(start, start + int(recv[s, e]), device=xs.device))
+        perm = torch.cat(idx) if idx else torch.zeros(0, dtype=torch.long, device=xs.device)
+        y = grouped_swiglu_mlp(xr[perm], recv.sum(0), wgu, wdn)
+        inv = torch.empty_like(perm)
+        inv[perm] = torch.arange(perm.numel(), device=perm.device)
+        return all_to_all_autograd(y[inv], recv_splits, send_splits, g)
+
+    # ------------------------------------------------------------ full model
+    def _layer(self, i: int, x: torch.Tensor, resid: Optional[torch.Tensor], positions, cu_seqlens, max_seqlen):
+        p = f"model.layers.{i}."
+        eps = self.cfg.rms_eps
+        if resid is None:
+            h = rms_norm(x, self._params[p + "input_layernorm.weight"], eps)
+            s = x
+        else:
+            h, s = add_rms_norm(x, resid, self._params[p + "input_layernorm.weight"], eps)
+        a = self._attn_block(i, h, positions, cu_seqlens, max_seqlen)
+        h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
+        m = self._mlp_block(i, h2)
+        return s2, m
+
+    def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, cu_seqlens: torch.Tensor,
+                max_seqlen: int) -> torch.Tensor:
+        """Packed forward: ``input_ids [T]`` -> final-norm hidden ``[T(/tp if SP), H]``."""
+        self._aux_losses = []
+        x = self.embed(input_ids)
+        if self.sequence_parallel:
+            # positions/cu_seqlens describe the full sequence; layers gather before attention.
+            pass
+        resid = None
+        for i in range(self.cfg.num_layers):
+            if self.activation_checkpointing and torch.is_grad_enabled():
+                if resid is None:
+                    x, resid = ckpt.checkpoint(self._layer, i, x, None, positions, cu_seqlens, max_seqlen,
+                                               use_reentrant=False)
+                else:
+                    x, resid = ckpt.checkpoint(self._layer, i, x, resid, positions, cu_seqlens, max_seqlen,
+                                               use_reentrant=False)
+            else:
+                x, resid = self._layer(i, x, resid, positions, cu_seqlens, max_seqlen)
+        h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], self.cfg.rms_eps)
+        return h
+
+    def lm_input(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Hidden states entering the vocab-parallel LM head (gathered from SP,
+        gradient all-reduced over TP)."""
+        if self.sequence_parallel:
+            return gather_from_sp(hidden, self.ps.tp_group)
+        return copy_to_tp(hidden, self.ps.tp_group)
+
+    def logits(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Vocab-local logits ``[T, V/tp]`` (hidden gathered from SP if needed)."""
+        return linear(self.lm_input(hidden), self.lm_head_weight())
+
+    def aux_loss(self) -> float:
+        return float(sum(a.item() for a in self._aux_losses)) if self._aux_losses else 0.0
+
+    # ------------------------------------------------------ rollout (no grad)
+    @torch.no_grad()
+    def forward_prefill(self, input_ids, positions, cu_seqlens, max_seqlen, kv: KVCache, slot_mapping,
+                        last_token_index: torch.Tensor) -> torch.Tensor:
+        """Prompt prefill: runs the packed prompts, writes K/V into the paged cache,
+        returns the final hidden state of each sequence's last token ``[B, H]``."""
+        x = self.embed_full(input_ids)
+        resid = None
+        eps = self.cfg.rms_eps
+        for i in range(self.cfg.num_layers):
+            p = f"model.layers.{i}."
+            if resid is None:
+                h = rms_norm(x, self._params[p + "input_layernorm.weight"], eps)
+                s = x
+            else:
+                h, s = add_rms_norm(x, resid, self._params[p + "input_layernorm.weight"], eps)
+            qkv = self._qkv(i, h, positions)
+            q, k, v = self._split_heads(qkv)
+            kc, vc = kv.layer(i)
+            write_kv_cache(k, v, kc, vc, slot_mapping)
+            o, _ = flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen, causal=True)
+            a = self._tp_sum(linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"]))
+            h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
+            m = self._mlp_infer(i, h2)
+            x, resid = s2, m
+        h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], eps)
+        return h[last_token_index]
+
+    @torch.no_grad()
+    def forward_decode(self, tokens, positions, kv: KVCache, block_tables, seq_lens, slot_mapping,
+                       max_seq_len: int = 0) -> torch.Tensor:
+        """One decode step for ``B`` sequences: ``tokens [B]`` -> hidden ``[B, H]``."""
+        x = self.embed_full(tokens)
+        resid = None
+        eps = self.cfg.rms_eps
+        for i in range(self.cfg.num_layers):
+            p = f"model.layers.{i}."
+            if resid is None:
+                h = rms_norm(x, self._params[p + "input_layernorm.weight"], eps)
+                s = x
+            else:
+                h, s = add_rms_norm(x, resid, self._params[p + "input_layernorm.weight"], eps)
+            qkv = self._qkv(i, h, positions)
+            q, k, v = self._split_heads(qkv)
+            kc, vc = kv.layer(i)
+            write_kv_cache(k, v, kc, vc, slot_mapping)
+            o = paged_decode_attention(q, kc, vc, block_tables, seq_lens, max_seq_len=max_seq_len,
+                                       k_scale=kv.k_scale, v_scale=kv.v_scale)
+            a = self._tp_sum(linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"]))
+            h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
+            m = self._mlp_infer(i, h2)
+            x, resid = s2, m
+        h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], eps)
+        return h
+
+    def embed_full(self, ids: torch.Tensor) -> torch.Tensor:
+        """Embedding with a TP all-reduce but never sequence-sharded (rollout path)."""
+        w = self._params["model.embed_tokens.weight"]
+        if self.ps.tp_size == 1:
+            return w[ids]
+        local = ids - self.vocab_start
+        inside = (local >= 0) & (local < self.vocab_local)
+        x = w[local.clamp(0, self.vocab_local - 1)] * inside.unsqueeze(-1).to(w.dtype)
+        return self._tp_sum(x)
+
+    def _tp_sum(self, x: torch.Tensor) -> torch.Tensor:
+        if self.ps.tp_size > 1:
+            import torch.distributed as dist
+
+            dist.all_reduce(x, group=self.ps.tp_group)
+        return x
+
+    def _mlp_infer(self, i: int, h: torch.Tensor) -> torch.Tensor:
+        p = f"model.layers.{i}."
+        if self.cfg.is_moe:
+            sp = self.sequence_parallel
+            self.sequence_parallel = False
+            try:
+                return self._moe_block(i, h)
+            finally:
+                self.sequence_parallel = sp
+        gu = linear(h, self._params[p + "mlp.gate_up_proj.weight"])
+        return self._tp_sum(linear(swiglu(gu), self._params[p + "mlp.down_proj.weight"]))
+
+    def logits_infer(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Full-vocab logits for sampling ``[B, V]`` (TP shards all-gathered)."""
+        local = linear(hidden, self.lm_head_weight())
+        if self.ps.tp_size == 1:
+            return local
+        import torch.distributed as dist
+
+        parts = [torch.empty_like(local) for _ in range(self.ps.tp_size)]
+        dist.all_gather(parts, local.contiguous(), group=self.ps.tp_group)
+        return torch.cat(parts, -1)
+
+
+def hash_name(name: str) -> int:
+    """Stable (process-independent) string hash for per-parameter init seeds."""
+    h = 1469598103934665603
+    for ch in name.encode():
+        h ^= ch
+        h = (h * 1099511628211) & 0xFFFFFFFFFFFFFFFF
+    return h
+
+
+def grouped_swiglu_mlp(xs: torch.Tensor, counts: torch.Tensor, wgu: torch.Tensor, wdn: torch.Tensor) -> torch.Tensor:
+    """Expert FFNs over rows grouped by expert: ``xs [N, H]`` (rows of expert e are
+    contiguous, ``counts[e]`` of them), ``wgu [E, 2F, H]``, ``wdn [E, H, F]``."""
+    from rl_b200.ops.grouped_gemm import grouped_mm_nt
+
+    gu = grouped_mm_nt(xs, wgu, counts)
+    a = swiglu(gu)
+    return grouped_mm_nt(a, wdn, counts)

@@ -1,0 +1,50 @@
+"""Loader for the in-tree native extension ``rl_b200._C`` (sm_100a kernels).
+
+CPU tensors always take the PyTorch reference path (the fp32 oracle used by
+tests and by the CPU plumbing run).  CUDA tensors MUST take the native path: if
+the extension is missing on a GPU box the op raises instead of silently
+falling back, so a run never reports numbers from a fallback by accident.
+"""
+
+from __future__ import annotations
+
+from typing import Any, Optional
+
+import torch
+
+_EXT: Optional[Any] = None
+_ERR: Optional[BaseException] = None
+
+
+def _load():
+    global _EXT, _ERR
+    if _EXT is not None or _ERR is not None:
+        return
+    try:
+        from rl_b200 import _C  # type: ignore
+
+        _EXT = _C
+    except BaseException as e:  # noqa: BLE001 - record and re-raise at use
+        _ERR = e
+
+
+def has_ext() -> bool:
+    _load()
+    return _EXT is not None
+
+
+def ext():
+    """Return the native module, raising a clear error when it is unavailable."""
+    _load()
+    if _EXT is None:
+        raise RuntimeError(
+            "rl_b200 native extension (rl_b200/_C*.so) is not built or failed to load: "
+            f"{_ERR!r}. Build it with `python setup.py build_ext --inplace` "
+            "(or __graft_entry__.build())."
+        )
+    return _EXT
+
+
+def use_native(*tensors: torch.Tensor) -> bool:
+    """True when the op must run on the native CUDA path."""
+    return any(isinstance(t, torch.Tensor) and t.is_cuda for t in tensors)

@@ -1,0 +1,144 @@
+"""Attention ops: packed variable-length causal GQA attention (training and
+prefill), paged-KV decode attention and KV-cache writes (rollout).
+
+Reference counterparts: training attention is TE ``DotProductAttention`` over
+packed THD sequences (native component N5, ``nemo_rl/models/megatron/data.py:1673``
+builds the ``cu_seqlens``); rollout attention is vLLM / MCore paged attention
+with ``block_size_tokens: 256`` (N15, ``examples/configs/grpo_math_1B.yaml:345``).
+
+Layouts
+-------
+* packed: ``q [T, nq, hd]``, ``k, v [T, nkv, hd]`` (may be strided views of the
+  QKV projection), ``cu_seqlens [B+1] int32``; output ``[T, nq, hd]`` and the
+  per-row log-sum-exp ``lse [nq, T] fp32`` kept for the backward pass.
+* paged cache: ``k_cache, v_cache [num_blocks, block_size, nkv, hd]``,
+  ``block_tables [B, max_blocks] int32``, ``seq_lens [B] int32``;
+  ``slot_mapping [T] int64`` = block * block_size + offset for writes.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from rl_b200.ops._ext import ext, use_native
+
+__all__ = [
+    "flash_attn_varlen",
+    "flash_attn_varlen_ref",
+    "paged_decode_attention",
+    "paged_decode_attention_ref",
+    "write_kv_cache",
+    "write_kv_cache_ref",
+]
+
+
+def flash_attn_varlen_ref(q, k, v, cu_seqlens, scale: Optional[float] = None, causal: bool = True):
+    """fp32 oracle: loop over packed sequences, explicit softmax."""
+    T, nq, hd = q.shape
+    nkv = k.shape[1]
+    g = nq // nkv
+    scale = scale if scale is not None else 1.0 / math.sqrt(hd)
+    out = torch.empty(T, nq, hd, dtype=torch.float32, device=q.device)
+    lse = torch.empty(nq, T, dtype=torch.float32, device=q.device)
+    cu = cu_seqlens.tolist()
+    for b in range(len(cu) - 1):
+        s, e = cu[b], cu[b + 1]
+        if e <= s:
+            continue
+        qb = q[s:e].float().transpose(0, 1)                                  # [nq, L, hd]
+        kb = k[s:e].float().transpose(0, 1).repeat_interleave(g, dim=0)      # [nq, L, hd]
+        vb = v[s:e].float().transpose(0, 1).repeat_interleave(g, dim=0)
+        sc = torch.matmul(qb, kb.transpose(-1, -2)) * scale
+        if causal:
+            L = e - s
+            m = torch.ones(L, L, dtype=torch.bool, device=q.device).triu(1)
+            sc = sc.masked_fill(m, float("-inf"))
+        lse[:, s:e] = torch.logsumexp(sc, -1)
+        out[s:e] = torch.matmul(torch.softmax(sc, -1), vb).transpose(0, 1)
+    return out.to(q.dtype), lse
+
+
+class _FlashAttnVarlen(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, cu_seqlens, max_seqlen, scale, causal):
+        o, lse = ext().flash_attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+        ctx.save_for_backward(q, k, v, o, lse, cu_seqlens)
+        ctx.meta = (int(max_seqlen), float(scale), bool(causal))
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, cu = ctx.saved_tensors
+        max_seqlen, scale, causal = ctx.meta
+        dq, dk, dv = ext().flash_attn_bwd(do.contiguous(), q, k, v, o, lse, cu, max_seqlen, scale, causal)
+        return dq, dk, dv, None, None, None, None
+
+
+def flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[float] = None, causal: bool = True):
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if use_native(q):
+        return _FlashAttnVarlen.apply(q, k, v, cu_seqlens, max_seqlen, scale, causal)
+    return flash_attn_varlen_ref(q, k, v, cu_seqlens, scale, causal)[0]
+
+
+def flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[float] = None,
+                          causal: bool = True):
+    """Forward only (prefill): returns (out, lse)."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if use_native(q):
+        return ext().flash_attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+    return flash_attn_varlen_ref(q, k, v, cu_seqlens, scale, causal)
+
+
+def write_kv_cache_ref(k, v, k_cache, v_cache, slot_mapping):
+    nb, bs = k_cache.shape[:2]
+    kc = k_cache.view(nb * bs, *k_cache.shape[2:])
+    vc = v_cache.view(nb * bs, *v_cache.shape[2:])
+    kc[slot_mapping.long()] = k.to(kc.dtype)
+    vc[slot_mapping.long()] = v.to(vc.dtype)
+
+
+def write_kv_cache(k, v, k_cache, v_cache, slot_mapping):
+    """Scatter ``k, v [T, nkv, hd]`` into the paged cache at ``slot_mapping``."""
+    if use_native(k):
+        ext().write_kv_cache(k, v, k_cache, v_cache, slot_mapping)
+    else:
+        write_kv_cache_ref(k, v, k_cache, v_cache, slot_mapping)
+
+
+def paged_decode_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, scale: Optional[float] = None):
+    B, nq, hd = q.shape
+    nkv = k_cache.shape[2]
+    bs = k_cache.shape[1]
+    g = nq // nkv
+    scale = scale if scale is not None else 1.0 / math.sqrt(hd)
+    out = torch.empty(B, nq, hd, dtype=torch.float32, device=q.device)
+    for b in range(B):
+        L = int(seq_lens[b])
+        nblk = (L + bs - 1) // bs
+        blocks = block_tables[b, :nblk].long()
+        kb = k_cache[blocks].reshape(-1, nkv, hd)[:L].float()   # [L, nkv, hd]
+        vb = v_cache[blocks].reshape(-1, nkv, hd)[:L].float()
+        kb = kb.repeat_interleave(g, dim=1).transpose(0, 1)      # [nq, L, hd]
+        vb = vb.repeat_interleave(g, dim=1).transpose(0, 1)
+        sc = torch.einsum("hd,hld->hl", q[b].float(), kb) * scale
+        out[b] = torch.einsum("hl,hld->hd", torch.softmax(sc, -1), vb)
+    return out.to(q.dtype)
+
+
+def paged_decode_attention(q, k_cache, v_cache, block_tables, seq_lens, scale: Optional[float] = None,
+                           max_seq_len: int = 0, k_scale: float = 1.0, v_scale: float = 1.0):
+    """One query token per sequence against its paged KV history (``seq_lens``
+    includes the token just written).  fp8 caches are dequantised with the
+    per-tensor ``k_scale`` / ``v_scale``."""
+    scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
+    if use_native(q):
+        return ext().paged_decode_attn(q, k_cache, v_cache, block_tables, seq_lens, float(scale),
+                                       int(max_seq_len), float(k_scale), float(v_scale))
+    if k_cache.dtype != q.dtype:
+        k_cache = k_cache.to(torch.float32) * k_scale
+        v_cache = v_cache.to(torch.float32) * v_scale
+    return paged_decode_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, scale)

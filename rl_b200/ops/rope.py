@@ -1,0 +1,91 @@
+"""Rotary position embedding (native component N8; reference enables TE's fused RoPE
+with ``apply_rope_fusion: True``, ``examples/configs/grpo_math_1B.yaml:181``).
+
+``apply_rope_qkv`` takes the packed QKV projection ``[T, (nq + 2*nkv) * hd]`` and
+returns a tensor of the same shape with the q and k heads rotated (half-split
+"rotate_half" convention used by Llama / Qwen HF checkpoints) and v copied, so
+the attention kernels read q, k and v from one buffer with strides.
+
+The cos/sin table is built once per model in fp32 from ``inv_freq`` (with the
+Llama-3.1 frequency scaling when requested) and indexed by position on device.
+"""
+
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+from rl_b200.ops._ext import ext, use_native
+
+__all__ = ["rope_inv_freq", "build_rope_cache", "apply_rope_qkv", "apply_rope_qkv_ref", "rotate_half"]
+
+
+def rope_inv_freq(head_dim: int, theta: float, scaling: Optional[dict] = None) -> torch.Tensor:
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    if scaling and scaling.get("rope_type", scaling.get("type")) == "llama3":
+        factor = float(scaling["factor"])
+        lo = float(scaling.get("low_freq_factor", 1.0))
+        hi = float(scaling.get("high_freq_factor", 4.0))
+        old_ctx = float(scaling.get("original_max_position_embeddings", 8192))
+        lo_wl, hi_wl = old_ctx / lo, old_ctx / hi
+        wl = 2 * math.pi / inv
+        scaled = torch.where(wl > lo_wl, inv / factor, inv)
+        smooth = (old_ctx / wl - lo) / (hi - lo)
+        mid = (1 - smooth) * scaled / factor + smooth * scaled
+        is_mid = (wl <= lo_wl) & (wl >= hi_wl)
+        inv = torch.where(is_mid, mid, scaled)
+    return inv.to(torch.float32)
+
+
+def build_rope_cache(max_pos: int, head_dim: int, theta: float, scaling: Optional[dict] = None,
+                     device=None) -> torch.Tensor:
+    """``[max_pos, head_dim]`` fp32 table: first half cos, second half sin."""
+    inv = rope_inv_freq(head_dim, theta, scaling)
+    t = torch.arange(max_pos, dtype=torch.float32)
+    ang = torch.outer(t, inv)
+    return torch.cat([ang.cos(), ang.sin()], dim=-1).to(device)
+
+
+def rotate_half(x: torch.Tensor) -> torch.Tensor:
+    h = x.shape[-1] // 2
+    return torch.cat([-x[..., h:], x[..., :h]], dim=-1)
+
+
+def apply_rope_qkv_ref(qkv: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor, nq: int, nkv: int,
+                       hd: int, inverse: bool = False) -> torch.Tensor:
+    T = qkv.shape[0]
+    x = qkv.float().view(T, nq + 2 * nkv, hd)
+    cs = cache[positions.long()]
+    cos = torch.cat([cs[:, : hd // 2]] * 2, -1).unsqueeze(1)
+    sin = torch.cat([cs[:, hd // 2:]] * 2, -1).unsqueeze(1)
+    if inverse:
+        sin = -sin
+    qk = x[:, : nq + nkv]
+    qk = qk * cos + rotate_half(qk) * sin
+    out = torch.cat([qk, x[:, nq + nkv:]], dim=1)
+    return out.reshape(qkv.shape).to(qkv.dtype)
+
+
+class _RopeQKV(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, qkv, positions, cache, nq, nkv, hd):
+        out = ext().rope_qkv(qkv.contiguous(), positions, cache, nq, nkv, hd, False)
+        ctx.save_for_backward(positions, cache)
+        ctx.dims = (nq, nkv, hd)
+        return out
+
+    @staticmethod
+    def backward(ctx, dout):
+        positions, cache = ctx.saved_tensors
+        nq, nkv, hd = ctx.dims
+        dqkv = ext().rope_qkv(dout.contiguous(), positions, cache, nq, nkv, hd, True)
+        return dqkv, None, None, None, None, None
+
+
+def apply_rope_qkv(qkv: torch.Tensor, positions: torch.Tensor, cache: torch.Tensor, nq: int, nkv: int,
+                   hd: int) -> torch.Tensor:
+    if use_native(qkv):
+        return _RopeQKV.apply(qkv, positions, cache, nq, nkv, hd)
+    return apply_rope_qkv_ref(qkv, positions, cache, nq, nkv, hd)

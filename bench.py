@@ -1,0 +1,278 @@
+#!/usr/bin/env python
+"""GRPO step benchmark on the Llama-3.1-8B shape (the reference's headline GRPO metric).
+
+Config: Llama-3.1-8B architecture (32 layers, hidden 4096,
+32 / 8 heads, head dim 128, SwiGLU 14336, vocab 128256, RoPE theta 5e5), random
+init, bf16, colocated rollout + train with the full refit every step; 8 samples
+per prompt, prompt lengths uniform in [128, 512] with tokens uniform over the
+vocabulary, max 1024 new tokens, deterministic seeded-hash reward.  Weak scaling:
+8 prompts (64 samples) per GPU; TP=2 when N >= 2 (TP2 x DP(N/2)), TP=1 on one GPU.
+
+Timing: W untimed warm-up GRPO steps, then K timed steps bracketed by a barrier
+and a device synchronize; device time from CUDA events on the launching stream,
+max over ranks.  ``value`` is the whole-job rollout+train tokens/s (prompt +
+generated tokens of all samples / step time).  ``e2e`` is the same metric by
+host wall clock through the public API (``grpo_train``), including the pinned
+host->device copy of every step's prompts and the device->host read of the loss.
+
+``--impl reference`` runs the unmodified reference from ``baseline/_ref`` when it
+is importable, otherwise prints its ``unavailable`` line.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+# one big model state + a KV cache that is freed and re-created every step: let the
+# caching allocator grow segments instead of fragmenting HBM
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
+
+METRIC = "GRPO step time & rollout+train tokens/s (8×B200, max over ranks) at 8B"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=3)
+    p.add_argument("--warmup", type=int, default=3)
+    p.add_argument("--impl", default="native", choices=["native", "reference"])
+    p.add_argument("--model", default="llama3.1-8b")
+    p.add_argument("--prompts-per-gpu", type=int, default=8)
+    p.add_argument("--generations", type=int, default=8)
+    p.add_argument("--min-prompt", type=int, default=128)
+    p.add_argument("--max-prompt", type=int, default=512)
+    p.add_argument("--max-new", type=int, default=1024)
+    p.add_argument("--tp", type=int, default=0, help="0 = 2 when gpus >= 2 else 1")
+    p.add_argument("--mb-tokens", type=int, default=16384)
+    p.add_argument("--kl", type=float, default=0.01)
+    p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for scoring)")
+    return p.parse_args()
+
+
+def reference_arm(args) -> None:
+    why = None
+    ref = os.path.join(ROOT, "baseline", "_ref")
+    try:
+        sys.path.insert(0, ref)
+        import nemo_rl  # noqa: F401
+
+        try:
+            import nemo_rl.algorithms.grpo  # noqa: F401
+        except Exception as e:  # noqa: BLE001
+            why = (f"reference GRPO not importable from baseline/_ref ({type(e).__name__}: {e}); its install "
+                   "carries only the top-level nemo_rl package and its GRPO path needs ray + Megatron-Core/"
+                   "Automodel, none of which are in this image or the offline wheelhouse")
+    except Exception as e:  # noqa: BLE001
+        why = f"reference not installed under baseline/_ref ({type(e).__name__}: {e})"
+    if why is None:
+        why = "reference imported but its Ray-based driver cannot start without the ray package"
+    if int(os.environ.get("RANK", "0")) == 0:
+        print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
+
+
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpus: list[int]):
+        self.gpus = gpus
+        self.rows: list[list[str]] = []
+        self.proc = None
+        self.thread = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", ",".join(str(g) for g in self.gpus)],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+            return
+
+        def reader():
+            for line in self.proc.stdout:
+                self.rows.append([x.strip() for x in line.split(",")])
+
+        self.thread = threading.Thread(target=reader, daemon=True)
+        self.thread.start()
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        if self.thread:
+            self.thread.join(timeout=2)
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in self.rows:
+            if len(r) < 9:
+                continue
+            try:
+                sm.append(float(r[1]))
+                mx.append(float(r[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, r[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        reference_arm(args)
+        return
+    import torch
+    import torch.distributed as dist
+
+    from rl_b200.algorithms.grpo import GRPOSaveState, grpo_train
+    from rl_b200.data.datasets import StatefulDataLoader, SyntheticPromptDataset
+    from rl_b200.environments.synthetic import HashRewardEnvironment
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.state import init_distributed
+    from rl_b200.utils.timer import max_over_ranks
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    tp = args.tp or (2 if args.gpus >= 2 else 1)
+    ps = init_distributed(tp=tp, timeout_s=900)
+    dev = ps.device
+    if not _ext.has_ext():
+        raise SystemExit(f"native extension not loaded: {_ext._ERR!r}")
+    mcfg = get_model_config(args.model)
+    if args.layers:
+        mcfg = mcfg.replace(num_layers=args.layers)
+    max_len = args.max_prompt + args.max_new
+    prompts_global = args.prompts_per_gpu * args.gpus
+    G = args.generations
+    pcfg = {
+        "model_name": args.model, "max_total_sequence_length": max_len, "precision": "bfloat16",
+        "train_global_batch_size": prompts_global * G, "train_micro_batch_size": 8,
+        "logprob_chunk_size": 4096, "max_grad_norm": 1.0,
+        "optimizer": {"name": "torch.optim.AdamW",
+                      "kwargs": {"lr": 3e-7, "weight_decay": 0.01, "betas": [0.9, 0.999], "eps": 1e-8}},
+        "megatron_cfg": {"activation_checkpointing": True, "sequence_parallel": False},
+        "generation": {"temperature": 1.0, "top_p": 1.0, "top_k": None, "max_new_tokens": args.max_new,
+                       "max_num_seqs": 512, "mcore_generation_config": {"block_size_tokens": 256}},
+        "sequence_packing": {"train_mb_tokens": args.mb_tokens, "logprob_mb_tokens": args.mb_tokens * 2},
+    }
+    cfg = {
+        "grpo": {"num_prompts_per_step": prompts_global, "num_generations_per_prompt": G,
+                 "max_num_steps": args.warmup + args.steps, "seed": 42},
+        "loss_fn": {"reference_policy_kl_penalty": args.kl, "ratio_clip_min": 0.2, "ratio_clip_max": 0.2},
+        "policy": pcfg,
+    }
+    torch.manual_seed(0)
+    worker = PolicyWorker(pcfg, model_cfg=mcfg, pstate=ps, seed=1234)
+    n_prompts = prompts_global * (args.warmup + args.steps + 1)
+    ds = SyntheticPromptDataset(n_prompts, args.min_prompt, args.max_prompt, mcfg.vocab_size, seed=7)
+    dl = StatefulDataLoader(ds, prompts_global, shuffle=False, shard_rank=ps.dp_rank, num_shards=ps.dp_size)
+    env = {"synthetic": HashRewardEnvironment({"seed": 0})}
+
+    step_log: list[dict] = []
+
+    def cb(step, m):
+        step_log.append({k: v for k, v in m.items() if isinstance(v, (int, float))})
+
+    state = GRPOSaveState.default()
+    # ---------------- warm-up (untimed) ----------------
+    state = grpo_train(worker, iter_epochs(dl), env, cfg, save_state=state, max_steps=args.warmup, step_callback=cb)
+    # ---------------- timed region ----------------
+    clocks = ClockSampler([int(x) for x in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if x.strip()]
+                          or list(range(args.gpus))) if ps.rank == 0 else None
+    if clocks:
+        clocks.start()
+    if dist.is_initialized():
+        dist.barrier()
+    torch.cuda.synchronize()
+    launches0 = _ext.launch_count()
+    ev0 = torch.cuda.Event(enable_timing=True)
+    ev1 = torch.cuda.Event(enable_timing=True)
+    t0 = time.perf_counter()
+    ev0.record()
+    n_before = len(step_log)
+    state = grpo_train(worker, iter_epochs(dl), env, cfg, save_state=state, max_steps=args.warmup + args.steps,
+                       step_callback=cb)
+    ev1.record()
+    torch.cuda.synchronize()
+    wall = time.perf_counter() - t0
+    if dist.is_initialized():
+        dist.barrier()
+    launches = _ext.launch_count() - launches0
+    dev_s = ev0.elapsed_time(ev1) / 1e3
+    dev_s = max_over_ranks(dev_s)
+    wall = max_over_ranks(wall)
+    clk = clocks.stop() if clocks else None
+    timed = step_log[n_before:]
+    tokens = sum(s["total_tokens"] for s in timed)
+    gen_tokens = sum(s["generated_tokens"] for s in timed)
+    prompt_bytes = (tokens - gen_tokens) / max(1, ps.dp_size) * 8 / max(1, len(timed))  # int64 prompt ids per rank
+    if ps.rank == 0:
+        value = tokens / dev_s
+        line = {
+            "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_s / args.steps * 1e3, 2),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic prompts (uniform token ids, lengths U[128,512]), random-init weights, "
+                    "seeded-hash reward",
+            "config": {"model": "Llama-3.1-8B-shape" + ("" if not args.layers else f" ({args.layers} layers: INVALID)"),
+                       "global_batch": prompts_global * G, "seq_len": max_len,
+                       "parallelism": f"tp{tp}dp{ps.dp_size}", "prompts_per_step": prompts_global,
+                       "generations_per_prompt": G, "max_new_tokens": args.max_new, "kl_penalty": args.kl,
+                       "l2": "working set (16 GB bf16 weights + KV cache) far above the 126 MB L2; no flush needed",
+                       "mean_gen_tokens": gen_tokens / max(1, len(timed)) / (prompts_global * G)},
+            "e2e": {"value": round(tokens / wall, 2), "unit": "tokens/s",
+                    "h2d_bytes_per_step": int(prompt_bytes), "d2h_bytes_per_step": 4 * len(timed) // max(1, len(timed))},
+            "gpu_launches": int(launches),
+            "clocks": clk,
+            "step_breakdown_s": {k: round(sum(s.get(k, 0.0) for s in timed) / max(1, len(timed)), 3)
+                                 for k in ("timing/generation", "timing/policy_and_reference_logprobs",
+                                           "timing/policy_training", "timing/weight_sync", "timing/data_processing")},
+            "gen_kl_error": timed[-1].get("gen_kl_error") if timed else None,
+        }
+        print(json.dumps(line), flush=True)
+    if dist.is_initialized():
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def iter_epochs(dl):
+    """Endless iterator over a StatefulDataLoader (keeps its position)."""
+
+    class _It:
+        def __iter__(self):
+            while True:
+                yielded = False
+                for b in dl:
+                    yielded = True
+                    yield b
+                if not yielded:
+                    return
+
+    return _It()
+
+
+if __name__ == "__main__":
+    main()

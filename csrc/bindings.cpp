@@ -1,0 +1,70 @@
+// Python bindings of the rl_b200 native extension (module rl_b200._C).
+#include <torch/extension.h>
+
+#include <vector>
+
+// norm.cu
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps);
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor delta, at::Tensor w, double eps);
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd);
+std::vector<at::Tensor> rmsnorm_bwd_add(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                                        c10::optional<at::Tensor> ds);
+// elementwise.cu
+at::Tensor rope_qkv(at::Tensor qkv, at::Tensor positions, at::Tensor cache, int64_t nq, int64_t nkv, int64_t hd,
+                    bool inverse);
+at::Tensor swiglu_fwd(at::Tensor gu);
+at::Tensor swiglu_bwd(at::Tensor dout, at::Tensor gu);
+void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slots);
+// logprob.cu
+std::vector<at::Tensor> logprob_partials(at::Tensor logits, at::Tensor targets, double temperature);
+void logprob_bwd(at::Tensor dlp, at::Tensor logits, at::Tensor targets, at::Tensor lse, double temperature,
+                 at::Tensor out);
+// sampling.cu
+void sample(at::Tensor logits, double temperature, int64_t top_k, double top_p, int64_t seed, at::Tensor offset,
+            at::Tensor out_tok, at::Tensor out_lp);
+// optim.cu
+void adamw_step(at::Tensor master, at::Tensor grad, at::Tensor exp_avg, at::Tensor exp_avg_sq,
+                c10::optional<at::Tensor> param_out, double lr, double beta1, double beta2, double eps,
+                double weight_decay, int64_t step, double grad_scale);
+at::Tensor sum_sq(at::Tensor x);
+// quant.cu
+std::vector<at::Tensor> quant_fp8_block(at::Tensor w, int64_t blk, bool pow2, c10::optional<at::Tensor> out,
+                                        c10::optional<at::Tensor> out_scale);
+std::vector<at::Tensor> quant_fp8_group(at::Tensor x, int64_t group, bool pow2);
+// attention.cu
+std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu_seqlens,
+                                       int64_t max_seqlen, double scale, bool causal);
+std::vector<at::Tensor> flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
+                                       at::Tensor lse, at::Tensor cu_seqlens, int64_t max_seqlen, double scale,
+                                       bool causal);
+at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,
+                             at::Tensor seq_lens, double scale, int64_t max_seq_len, double k_scale, double v_scale);
+// gemm_tcgen05.cu
+at::Tensor gemm_nt(at::Tensor a, at::Tensor b);
+int64_t gemm_error_flag(bool reset);
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "rl_b200 sm_100a kernels";
+  m.def("rmsnorm_fwd", &rmsnorm_fwd);
+  m.def("add_rmsnorm_fwd", &add_rmsnorm_fwd);
+  m.def("rmsnorm_bwd", &rmsnorm_bwd);
+  m.def("rmsnorm_bwd_add", &rmsnorm_bwd_add, py::arg("dy"), py::arg("x"), py::arg("w"), py::arg("rstd"),
+        py::arg("ds") = py::none());
+  m.def("rope_qkv", &rope_qkv);
+  m.def("swiglu_fwd", &swiglu_fwd);
+  m.def("swiglu_bwd", &swiglu_bwd);
+  m.def("write_kv_cache", &write_kv_cache);
+  m.def("logprob_partials", &logprob_partials);
+  m.def("logprob_bwd", &logprob_bwd);
+  m.def("sample", &sample);
+  m.def("adamw_step", &adamw_step);
+  m.def("sum_sq", &sum_sq);
+  m.def("quant_fp8_block", &quant_fp8_block, py::arg("w"), py::arg("blk"), py::arg("pow2"), py::arg("out") = py::none(),
+        py::arg("out_scale") = py::none());
+  m.def("quant_fp8_group", &quant_fp8_group);
+  m.def("flash_attn_fwd", &flash_attn_fwd);
+  m.def("flash_attn_bwd", &flash_attn_bwd);
+  m.def("paged_decode_attn", &paged_decode_attn);
+  m.def("gemm_nt", &gemm_nt);
+  m.def("gemm_error_flag", &gemm_error_flag, py::arg("reset") = false);
+}

@@ -1,0 +1,351 @@
+// Persistent bf16 GEMM on the 5th-generation tensor cores (sm_100a).
+//
+//   C[M, N] (bf16) = A[M, K] (bf16, row-major) x B[N, K]^T (bf16, row-major)
+//
+// Structure (one CTA per SM, 6 warps):
+//   warp 0      TMA producer: one elected lane issues cp.async.bulk.tensor loads
+//               of 128x64 A tiles and BNx64 B tiles (128-byte swizzle) into a
+//               STAGES-deep shared-memory ring, signalling mbarriers with the
+//               transaction byte count.  No multicast: every CTA loads its own
+//               tiles (this kernel is also the template for the peer-memory
+//               variants that run on several GPUs).
+//   warp 1      allocates 2*BN tensor-memory columns (two accumulators), then
+//               one lane issues tcgen05.mma (M=128, N=BN, K=16) per 16-wide K
+//               slice, committing each stage back to the producer and each
+//               finished tile to the epilogue.
+//   warps 2-5   epilogue: tcgen05.ld 32 lanes x 32 columns at a time from the
+//               accumulator their warp may access (TMEM lane quadrant = warp % 4),
+//               convert to bf16 and store; then release the accumulator so the
+//               MMA warp can start the tile after next.
+// Tiles are visited in a grouped raster (GROUP_M m-tiles per column sweep) for
+// L2 reuse.  Every mbarrier wait is bounded in time: on expiry the kernel sets
+// an error word (readable from the host), raises a CTA-wide abort flag so all
+// roles drain, frees its tensor memory and returns.
+#include "common.cuh"
+
+#include <cudaTypedefs.h>
+
+namespace rlb {
+namespace tc {
+
+__device__ int g_error = 0;
+
+constexpr int BM = 128;
+constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
+constexpr int GROUP_M = 8;
+constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
+
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(addr), "r"(count) : "memory");
+}
+__device__ __forceinline__ void mbar_expect_tx(uint32_t addr, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(addr), "r"(bytes) : "memory");
+}
+__device__ __forceinline__ void mbar_arrive(uint32_t addr) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(addr) : "memory");
+}
+__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(ok)
+      : "r"(addr), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait.  Returns false if the wait expired or another role aborted.
+__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, volatile int* abort_flag) {
+  const long long t0 = clock64();
+  while (!mbar_test(addr, parity)) {
+    if (*abort_flag) return false;
+    if (clock64() - t0 > kWaitCycles) {
+      atomicExch(&g_error, 1);
+      *abort_flag = 1;
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t mbar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(
+          dst),
+      "l"(tmap), "r"(mbar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
+// 128 bytes, 8-row core groups 1024 bytes apart (tile base 1024-byte aligned).
+__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;             // leading byte offset (unused for swizzled K-major)
+  d |= (uint64_t)(1024u >> 4) << 32;   // stride byte offset
+  d |= (uint64_t)1u << 46;             // descriptor version for sm_100
+  d |= (uint64_t)2u << 61;             // 128-byte swizzle
+  return d;
+}
+
+// Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                                          uint32_t accumulate) {
+  asm volatile(
+      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
+          tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
+}
+__device__ __forceinline__ void umma_commit(uint32_t mbar) {
+  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar) : "memory");
+}
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
+      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
+      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
+        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
+        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
+        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
+      : "r"(taddr));
+  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
+}
+
+__device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mt, int& nt) {
+  const int group = GROUP_M * num_n;
+  const int gid = tile / group;
+  const int first_m = gid * GROUP_M;
+  const int gsize = min(num_m - first_m, GROUP_M);
+  const int in = tile % group;
+  mt = first_m + in % gsize;
+  nt = in / gsize;
+}
+
+template <int BN, int STAGES>
+__global__ void __launch_bounds__(192, 1)
+gemm_nt_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
+               __nv_bfloat16* __restrict__ C, int M, int N, int K) {
+  constexpr int A_BYTES = BM * BK * 2;
+  constexpr int B_BYTES = BN * BK * 2;
+  constexpr uint32_t TMEM_COLS = 2 * BN;
+  constexpr uint32_t IDESC = idesc_bf16(BM, BN);
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sA = base;
+  const uint32_t sB = base + STAGES * A_BYTES;
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + STAGES * (A_BYTES + B_BYTES));
+  const uint32_t bar_full = smem_u32(bars);
+  const uint32_t bar_empty = bar_full + 8 * STAGES;
+  const uint32_t bar_tfull = bar_empty + 8 * STAGES;
+  const uint32_t bar_tempty = bar_tfull + 16;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 2 * STAGES + 4);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int num_m = (M + BM - 1) / BM, num_n = (N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (K + BK - 1) / BK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(bar_tfull + 8 * a, 1);
+      mbar_init(bar_tempty + 8 * a, 4);
+    }
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(TMEM_COLS));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      int it = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
+        int mt, nt;
+        tile_coords(tile, num_m, num_n, mt, nt);
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(bar_empty + 8 * s, ph ^ 1, abort_flag)) break;
+          mbar_expect_tx(bar_full + 8 * s, A_BYTES + B_BYTES);
+          tma_load_2d(sA + s * A_BYTES, &tmap_a, bar_full + 8 * s, kb * BK, mt * BM);
+          tma_load_2d(sB + s * B_BYTES, &tmap_b, bar_full + 8 * s, kb * BK, nt * BN);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      int it = 0, local = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t aph = (local >> 1) & 1;
+        if (!mbar_wait(bar_tempty + 8 * acc, aph ^ 1, abort_flag)) break;
+        tc_fence_after();
+        const uint32_t tmem_d = tmem_base + acc * BN;
+        bool ok = true;
+        for (int kb = 0; kb < num_kb; ++kb, ++it) {
+          const int s = it % STAGES;
+          const uint32_t ph = (it / STAGES) & 1;
+          if (!mbar_wait(bar_full + 8 * s, ph, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a0 = sA + s * A_BYTES, b0 = sB + s * B_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            umma_bf16(tmem_d, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), IDESC,
+                      (kb > 0 || k > 0) ? 1u : 0u);
+          }
+          umma_commit(bar_empty + 8 * s);
+        }
+        if (!ok) break;
+        umma_commit(bar_tfull + 8 * acc);
+      }
+    }
+    __syncwarp();
+  } else {
+    // epilogue warps 2..5
+    const int quad = warp & 3;
+    const int row_in_tile = quad * 32 + lane;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      int mt, nt;
+      tile_coords(tile, num_m, num_n, mt, nt);
+      const int acc = local & 1;
+      const uint32_t aph = (local >> 1) & 1;
+      if (!mbar_wait(bar_tfull + 8 * acc, aph, abort_flag)) break;
+      tc_fence_after();
+      const int m = mt * BM + row_in_tile;
+      const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * BN;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(trow + c * 32, r);
+        const int n0 = nt * BN + c * 32;
+        if (m < M && n0 < N) {
+          __nv_bfloat16* dst = C + (long long)m * N + n0;
+          if (n0 + 32 <= N && (N % 8) == 0) {
+            uint4 v[4];
+            uint32_t* pv = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(r[2 * j]), __uint_as_float(r[2 * j + 1]));
+              pv[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = v[j];
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < N) dst[j] = __float2bfloat16_rn(__uint_as_float(r[j]));
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(bar_tempty + 8 * acc);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "r"(TMEM_COLS));
+  }
+}
+
+}  // namespace tc
+}  // namespace rlb
+
+using namespace rlb;
+
+static PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    RLB_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "rl_b200: cuTensorMapEncodeTiled unavailable");
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
+}
+
+// 2-D row-major bf16 [rows, cols] tensor map with a (box_rows x 64) box, 128-byte swizzle.
+static CUtensorMap make_tmap_2d(const void* ptr, int64_t rows, int64_t cols, int box_rows) {
+  CUtensorMap m;
+  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
+  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
+  cuuint32_t estr[2] = {1u, 1u};
+  CUresult r = tma_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
+                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "rl_b200: cuTensorMapEncodeTiled failed (", (int)r, ")");
+  return m;
+}
+
+template <int BN, int STAGES>
+static void launch_gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int M, int N, int K) {
+  const CUtensorMap ta = make_tmap_2d(a.data_ptr(), M, K, tc::BM);
+  const CUtensorMap tb = make_tmap_2d(b.data_ptr(), N, K, BN);
+  const int smem = STAGES * (tc::BM * tc::BK * 2 + BN * tc::BK * 2) + 1024 + 256;
+  auto kern = tc::gemm_nt_kernel<BN, STAGES>;
+  RLB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+  const int tiles = ((M + tc::BM - 1) / tc::BM) * ((N + BN - 1) / BN);
+  const int grid = std::min(tiles, num_sms());
+  kern<<<grid, 192, smem, stream()>>>(ta, tb, (__nv_bfloat16*)c.data_ptr(), M, N, K);
+  RLB_CUDA_CHECK(cudaGetLastError());
+}
+
+at::Tensor gemm_nt(at::Tensor a, at::Tensor b) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "rl_b200 gemm_nt: bf16 CUDA operands expected");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && a.size(1) == b.size(1), "rl_b200 gemm_nt: a [M,K], b [N,K]");
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous(), "rl_b200 gemm_nt: operands must be contiguous");
+  const int M = a.size(0), N = b.size(0), K = a.size(1);
+  TORCH_CHECK(K % 8 == 0 && K > 0, "rl_b200 gemm_nt: K must be a positive multiple of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(a.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(b.data_ptr()) % 16 == 0,
+              "rl_b200 gemm_nt: operands must be 16-byte aligned");
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto c = at::empty({M, N}, a.options());
+  if (M == 0 || N == 0) return c;
+  if (N >= 256) launch_gemm<256, 4>(a, b, c, M, N, K);
+  else launch_gemm<128, 6>(a, b, c, M, N, K);
+  return c;
+}
+
+int64_t gemm_error_flag(bool reset) {
+  int v = 0;
+  RLB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, tc::g_error, sizeof(int)));
+  if (reset) {
+    int z = 0;
+    RLB_CUDA_CHECK(cudaMemcpyToSymbol(tc::g_error, &z, sizeof(int)));
+  }
+  return v;
+}

@@ -1,0 +1,231 @@
+// RMSNorm forward / backward and the fused residual-add + RMSNorm.
+//
+// One warp per row (rows are hidden vectors of a packed token batch).  The
+// forward makes two passes over the row (sum of squares, then normalise); the
+// second pass re-reads from L1, so DRAM sees one read of x (and delta) and
+// one write of y (and the residual sum).  bf16 rows with H % 8 == 0 use 16-byte
+// vector accesses.  The backward accumulates the weight gradient per warp in
+// shared memory and writes one fp32 partial row per CTA; a second kernel sums
+// the partials (deterministic, no atomics).
+#include "common.cuh"
+
+namespace rlb {
+
+constexpr int kNormWarps = 4;
+
+template <typename T>
+__global__ void __launch_bounds__(kNormWarps * 32)
+rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta, const T* __restrict__ w,
+                   T* __restrict__ y, T* __restrict__ s_out, float* __restrict__ rstd, int rows, int H,
+                   float eps) {
+  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+  if (row >= rows) return;
+  const T* xr = x + (size_t)row * H;
+  const T* dr = delta ? delta + (size_t)row * H : nullptr;
+  T* sr = s_out ? s_out + (size_t)row * H : nullptr;
+  float ss = 0.f;
+  const bool vec = (sizeof(T) == 2) && (H % 8 == 0);
+  if (vec) {
+    const int nv = H / 8;
+    for (int j = lane; j < nv; j += 32) {
+      float f[8];
+      unpack8(reinterpret_cast<const bf16x8*>(xr)[j], f);
+      if (dr) {
+        float g[8];
+        unpack8(reinterpret_cast<const bf16x8*>(dr)[j], g);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] += g[i];
+        bf16x8 p = pack8(f);
+        reinterpret_cast<bf16x8*>(sr)[j] = p;
+        unpack8(p, f);  // normalise the rounded sum that is stored
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += f[i] * f[i];
+    }
+  } else {
+    for (int j = lane; j < H; j += 32) {
+      float v = to_f(xr[j]);
+      if (dr) {
+        T s = from_f<T>(v + to_f(dr[j]));
+        sr[j] = s;
+        v = to_f(s);
+      }
+      ss += v * v;
+    }
+  }
+  ss = warp_sum(ss);
+  const float r = rsqrtf(ss / H + eps);
+  if (lane == 0) rstd[row] = r;
+  const T* src = dr ? sr : xr;
+  __syncwarp();
+  T* yr = y + (size_t)row * H;
+  if (vec) {
+    const int nv = H / 8;
+    for (int j = lane; j < nv; j += 32) {
+      float f[8], g[8];
+      unpack8(reinterpret_cast<const bf16x8*>(src)[j], f);
+      unpack8(reinterpret_cast<const bf16x8*>(w)[j], g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) f[i] = f[i] * r * g[i];
+      reinterpret_cast<bf16x8*>(yr)[j] = pack8(f);
+    }
+  } else {
+    for (int j = lane; j < H; j += 32) yr[j] = from_f<T>(to_f(src[j]) * r * to_f(w[j]));
+  }
+}
+
+// dx = r * dy * w - x * r^3 * sum(dy * w * x) / H   (+ ds)
+// dw_partial[cta][h] = sum over this CTA's rows of dy * x * r
+template <typename T>
+__global__ void __launch_bounds__(kNormWarps * 32)
+rmsnorm_bwd_kernel(const T* __restrict__ dy, const T* __restrict__ x, const T* __restrict__ w,
+                   const float* __restrict__ rstd, const T* __restrict__ ds, T* __restrict__ dx,
+                   float* __restrict__ dw_partial, int rows, int H) {
+  extern __shared__ float acc[];  // [kNormWarps][H]
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+  float* my = acc + (size_t)wid * H;
+  for (int j = lane; j < H; j += 32) my[j] = 0.f;
+  __syncwarp();
+  const bool vec = (sizeof(T) == 2) && (H % 8 == 0);
+  for (int row = blockIdx.x * kNormWarps + wid; row < rows; row += gridDim.x * kNormWarps) {
+    const T* dyr = dy + (size_t)row * H;
+    const T* xr = x + (size_t)row * H;
+    const float r = rstd[row];
+    float dot = 0.f;
+    if (vec) {
+      for (int j = lane; j < H / 8; j += 32) {
+        float a[8], b[8], c[8];
+        unpack8(reinterpret_cast<const bf16x8*>(dyr)[j], a);
+        unpack8(reinterpret_cast<const bf16x8*>(xr)[j], b);
+        unpack8(reinterpret_cast<const bf16x8*>(w)[j], c);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) dot += a[i] * c[i] * b[i];
+      }
+    } else {
+      for (int j = lane; j < H; j += 32) dot += to_f(dyr[j]) * to_f(w[j]) * to_f(xr[j]);
+    }
+    dot = warp_sum(dot);
+    const float c3 = dot * r * r * r / H;
+    T* dxr = dx + (size_t)row * H;
+    const T* dsr = ds ? ds + (size_t)row * H : nullptr;
+    if (vec) {
+      for (int j = lane; j < H / 8; j += 32) {
+        float a[8], b[8], c[8], o[8];
+        unpack8(reinterpret_cast<const bf16x8*>(dyr)[j], a);
+        unpack8(reinterpret_cast<const bf16x8*>(xr)[j], b);
+        unpack8(reinterpret_cast<const bf16x8*>(w)[j], c);
+        float e[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        if (dsr) unpack8(reinterpret_cast<const bf16x8*>(dsr)[j], e);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          o[i] = r * a[i] * c[i] - b[i] * c3 + e[i];
+          my[j * 8 + i] += a[i] * b[i] * r;
+        }
+        reinterpret_cast<bf16x8*>(dxr)[j] = pack8(o);
+      }
+    } else {
+      for (int j = lane; j < H; j += 32) {
+        float a = to_f(dyr[j]), b = to_f(xr[j]);
+        float o = r * a * to_f(w[j]) - b * c3 + (dsr ? to_f(dsr[j]) : 0.f);
+        dxr[j] = from_f<T>(o);
+        my[j] += a * b * r;
+      }
+    }
+  }
+  __syncthreads();
+  for (int j = threadIdx.x; j < H; j += blockDim.x) {
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < kNormWarps; ++k) s += acc[(size_t)k * H + j];
+    dw_partial[(size_t)blockIdx.x * H + j] = s;
+  }
+}
+
+__global__ void reduce_rows_kernel(const float* __restrict__ part, float* __restrict__ out, int n_rows, int H) {
+  int j = blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= H) return;
+  float s = 0.f;
+  for (int i = 0; i < n_rows; ++i) s += part[(size_t)i * H + j];
+  out[j] = s;
+}
+
+}  // namespace rlb
+
+using namespace rlb;
+
+static void check_rows(const at::Tensor& x, const at::Tensor& w) {
+  RLB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "norm input must be a contiguous 2-D CUDA tensor");
+  RLB_CHECK(w.dim() == 1 && w.size(0) == x.size(1) && w.scalar_type() == x.scalar_type(), "norm weight mismatch");
+}
+
+std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
+  check_rows(x, w);
+  const c10::cuda::CUDAGuard g(x.device());
+  const int rows = x.size(0), H = x.size(1);
+  auto y = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, rstd};
+  dim3 grid((rows + kNormWarps - 1) / kNormWarps);
+  RLB_DISPATCH_FLOAT(x.scalar_type(), "rmsnorm_fwd", [&] {
+    rmsnorm_fwd_kernel<scalar_t><<<grid, kNormWarps * 32, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), nullptr, (const scalar_t*)w.data_ptr(), (scalar_t*)y.data_ptr(), nullptr,
+        rstd.data_ptr<float>(), rows, H, (float)eps);
+  });
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {y, rstd};
+}
+
+std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor delta, at::Tensor w, double eps) {
+  check_rows(x, w);
+  RLB_CHECK(delta.sizes() == x.sizes() && delta.is_contiguous(), "delta shape mismatch");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int rows = x.size(0), H = x.size(1);
+  auto y = at::empty_like(x);
+  auto s = at::empty_like(x);
+  auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {y, s, rstd};
+  dim3 grid((rows + kNormWarps - 1) / kNormWarps);
+  RLB_DISPATCH_FLOAT(x.scalar_type(), "add_rmsnorm_fwd", [&] {
+    rmsnorm_fwd_kernel<scalar_t><<<grid, kNormWarps * 32, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), (const scalar_t*)delta.data_ptr(), (const scalar_t*)w.data_ptr(),
+        (scalar_t*)y.data_ptr(), (scalar_t*)s.data_ptr(), rstd.data_ptr<float>(), rows, H, (float)eps);
+  });
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {y, s, rstd};
+}
+
+static std::vector<at::Tensor> rmsnorm_bwd_impl(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                                                c10::optional<at::Tensor> ds) {
+  check_rows(x, w);
+  RLB_CHECK(dy.sizes() == x.sizes() && dy.is_contiguous(), "dy shape mismatch");
+  const c10::cuda::CUDAGuard g(x.device());
+  const int rows = x.size(0), H = x.size(1);
+  auto dx = at::empty_like(x);
+  auto dw = at::zeros({H}, x.options().dtype(at::kFloat));
+  if (rows == 0) return {dx, dw};
+  int ctas = std::min((rows + kNormWarps - 1) / kNormWarps, 2 * num_sms());
+  size_t smem = (size_t)kNormWarps * H * sizeof(float);
+  RLB_CHECK(smem <= 200 * 1024, "hidden size too large for rmsnorm_bwd shared accumulator");
+  auto part = at::empty({ctas, H}, x.options().dtype(at::kFloat));
+  const void* dsp = (ds.has_value() && ds->defined()) ? ds->data_ptr() : nullptr;
+  RLB_DISPATCH_FLOAT(x.scalar_type(), "rmsnorm_bwd", [&] {
+    auto kern = rmsnorm_bwd_kernel<scalar_t>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    kern<<<ctas, kNormWarps * 32, smem, stream()>>>(
+        (const scalar_t*)dy.data_ptr(), (const scalar_t*)x.data_ptr(), (const scalar_t*)w.data_ptr(),
+        rstd.data_ptr<float>(), (const scalar_t*)dsp, (scalar_t*)dx.data_ptr(), part.data_ptr<float>(), rows, H);
+  });
+  reduce_rows_kernel<<<(H + 255) / 256, 256, 0, stream()>>>(part.data_ptr<float>(), dw.data_ptr<float>(), ctas, H);
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {dx, dw};
+}
+
+std::vector<at::Tensor> rmsnorm_bwd(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd) {
+  return rmsnorm_bwd_impl(dy, x, w, rstd, c10::nullopt);
+}
+
+std::vector<at::Tensor> rmsnorm_bwd_add(at::Tensor dy, at::Tensor x, at::Tensor w, at::Tensor rstd,
+                                        c10::optional<at::Tensor> ds) {
+  return rmsnorm_bwd_impl(dy, x, w, rstd, ds);
+}

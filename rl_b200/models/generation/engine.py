@@ -31,6 +31,7 @@ import torch
 
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
 from rl_b200.models.transformer import KVCache, TransformerLM
+from rl_b200.ops._ext import add_launches, launch_count
 from rl_b200.ops.sampling import sample_tokens
 
 __all__ = ["RolloutEngine"]
@@ -66,6 +67,7 @@ class _DecodeState:
         self.next_tokens = torch.zeros(B, dtype=i64, device=device)
         self.next_logprobs = torch.zeros(B, dtype=torch.float32, device=device)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
+        self.native_launches = 0
 
 
 class RolloutEngine:
@@ -152,7 +154,10 @@ class RolloutEngine:
 
         # ---- prefill (packed prompts) ----
         lens_l = lengths.tolist()
-        flat = torch.cat([input_ids[b, : lens_l[b]].cpu() for b in range(B)]).to(dev)
+        flat = torch.cat([input_ids[b, : lens_l[b]].cpu() for b in range(B)])
+        if dev.type == "cuda":
+            flat = flat.pin_memory()  # the step's inputs cross PCIe once, from pinned memory
+        flat = flat.to(dev, non_blocking=True)
         positions = torch.cat([torch.arange(L, dtype=torch.int32) for L in lens_l]).to(dev)
         cu = torch.zeros(B + 1, dtype=torch.int32)
         cu[1:] = torch.cumsum(lengths, 0)
@@ -240,6 +245,7 @@ class RolloutEngine:
             k = 0
             while True:
                 st.graph.replay()
+                add_launches(st.native_launches)
                 k += 1
                 step_done_k = step_done + k
                 if step_done_k >= max_new:
@@ -311,8 +317,11 @@ class RolloutEngine:
         if self._graph_pool is None:
             self._graph_pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
+        c0 = launch_count()
         with torch.cuda.graph(g, pool=self._graph_pool):
             self._step_body(st, temperature, top_k, top_p, stop)
+        st.native_launches = launch_count() - c0
+        add_launches(-st.native_launches)  # captured, not executed
         st.graph = g
 
     def _decode_eager(self, tokens_all, lps_all, glen, tok0, lengths, block_tables, max_new, temperature, top_k,

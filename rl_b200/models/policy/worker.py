@@ -110,6 +110,8 @@ class PolicyWorker:
         self.logprob_mb_tokens = int(sp.get("logprob_mb_tokens", self.train_mb_tokens))
         self.packing_algorithm = sp.get("algorithm", "modified_first_fit_decreasing")
         self.logprob_chunk = int(policy_cfg.get("logprob_chunk_size") or 4096)
+        # colocated rollout needs the HBM of the fp32 gradient buffer for its KV cache
+        self.release_grad_after_train = bool(policy_cfg.get("release_grad_after_train", self.device.type == "cuda"))
         self.timer = Timer()
 
     # ------------------------------------------------------------- helpers
@@ -183,13 +185,13 @@ class PolicyWorker:
             raise RuntimeError("reference model was not initialised")
         flat = self.model.flat_param
         n = self.ref_flat.numel()
-        saved = flat[:n].clone()
         flat[:n].copy_(self.ref_flat)
         try:
             yield
         finally:
-            flat[:n].copy_(saved)
-            del saved
+            # the live bf16 weights are exactly bf16(master): restore by casting
+            # the fp32 master shard (no second copy of the model is held)
+            self.optimizer.restore_params_from_master()
 
     @torch.no_grad()
     def get_reference_policy_logprobs(self, data: BatchedDataDict, temperature: Optional[float] = None):
@@ -209,6 +211,7 @@ class PolicyWorker:
         B, S = ids.shape
         gbs = gbs or B
         lengths = self._lengths(data)
+        self.optimizer.ensure_grad_buffer()
         all_metrics: list[dict] = []
         losses, grad_norms, lrs = [], [], []
         for g0 in range(0, B, gbs):
@@ -249,6 +252,8 @@ class PolicyWorker:
                 dist.all_reduce(step_loss, group=self.ps.dp_group)
             losses.append(float(step_loss))
             all_metrics.extend(mb_metrics)
+        if self.release_grad_after_train:
+            self.optimizer.release_grad_buffer()
         agg = aggregate_metrics(all_metrics, self.ps.dp_group if self.ps.dp_size > 1 else None)
         agg.update({"loss": sum(losses) / max(1, len(losses)), "global_loss": losses,
                     "grad_norm": grad_norms[-1] if grad_norms else 0.0, "lr": lrs[-1] if lrs else 0.0,

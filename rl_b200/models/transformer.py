@@ -173,7 +173,9 @@ class TransformerLM(nn.Module):
     def _allocate(self, seed: int, std: float) -> None:
         self.flat_param = torch.empty(self.flat_numel, dtype=self.dtype, device=self.device)
         self.flat_param.zero_()
-        gen = torch.Generator(device="cpu")
+        # random init runs on the model's device (an 8B model initialises in seconds on a B200);
+        # the CPU and CUDA streams of one seed differ, every TP/EP layout of one device type agrees
+        gen = torch.Generator(device=self.device)
         out_std = std / math.sqrt(2 * self.cfg.num_layers)
         self._params: dict[str, nn.Parameter] = {}
         for sp in self.specs:
@@ -195,7 +197,7 @@ class TransformerLM(nn.Module):
                     shard_dim, n_shards, shard_idx = sp.ep_dim, self.ps.ep_size, self.ps.ep_rank
                 if shard_dim is not None:
                     full_shape[shard_dim] *= n_shards
-                full = torch.randn(full_shape, generator=gen, dtype=torch.float32) * s
+                full = torch.randn(full_shape, generator=gen, dtype=torch.float32, device=self.device) * s
                 if shard_dim is not None:
                     full = self.shard_full_tensor(sp, full, shard_idx, n_shards)
                 view.copy_(full.to(self.dtype))

@@ -4,6 +4,11 @@ CPU tensors always take the PyTorch reference path (the fp32 oracle used by
 tests and by the CPU plumbing run).  CUDA tensors MUST take the native path: if
 the extension is missing on a GPU box the op raises instead of silently
 falling back, so a run never reports numbers from a fallback by accident.
+
+Every call into the extension goes through a counting proxy: ``launch_count()``
+returns how many native kernels have been launched (each entry point adds the
+number of kernels it launches; CUDA-graph replays add the count recorded at
+capture).  Benchmarks report this as their native launch count.
 """
 
 from __future__ import annotations
@@ -14,6 +19,36 @@ import torch
 
 _EXT: Optional[Any] = None
 _ERR: Optional[BaseException] = None
+_LAUNCHES = 0
+_CAPTURE_DEPTH = 0
+
+# kernels launched per entry-point call (default 1)
+_KERNELS_PER_CALL = {
+    "rmsnorm_bwd": 2,
+    "rmsnorm_bwd_add": 2,
+    "sum_sq": 2,
+    "flash_attn_bwd": 3,
+    "paged_decode_attn": 1,  # +1 when split (counted at call time below)
+    "gemm_error_flag": 0,
+}
+
+
+class _Counting:
+    def __init__(self, mod):
+        self._mod = mod
+
+    def __getattr__(self, name):
+        fn = getattr(self._mod, name)
+        if not callable(fn):
+            return fn
+        n = _KERNELS_PER_CALL.get(name, 1)
+
+        def wrapped(*a, **k):
+            global _LAUNCHES
+            _LAUNCHES += n
+            return fn(*a, **k)
+
+        return wrapped
 
 
 def _load():
@@ -23,7 +58,7 @@ def _load():
     try:
         from rl_b200 import _C  # type: ignore
 
-        _EXT = _C
+        _EXT = _Counting(_C)
     except BaseException as e:  # noqa: BLE001 - record and re-raise at use
         _ERR = e
 
@@ -43,6 +78,16 @@ def ext():
             "(or __graft_entry__.build())."
         )
     return _EXT
+
+
+def launch_count() -> int:
+    return _LAUNCHES
+
+
+def add_launches(n: int) -> None:
+    """Account kernels launched outside a direct call (CUDA-graph replays)."""
+    global _LAUNCHES
+    _LAUNCHES += n
 
 
 def use_native(*tensors: torch.Tensor) -> bool:

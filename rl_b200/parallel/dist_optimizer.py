@@ -8,11 +8,14 @@ and ``data_parallel_sharding_strategy: optim_grads_params``
   attached to the parameters (``rl_b200.ops.linear`` adds into them);
 * ``step()``: reduce-scatter the flat gradient over the DP(xCP) group so every
   rank owns ``1/dp`` of it, compute the global grad norm (squares summed over
-  the shard, then over DP and TP groups), run ONE fused AdamW launch over the
-  shard (which also writes the bf16 parameters), and all-gather the bf16
+  the shard, then over DP and TP groups), run the fused AdamW kernel over the
+  shard (which also writes the bf16 parameters) and all-gather the bf16
   parameter shards back into the flat buffer;
 * master weights / Adam moments exist only for the local shard
-  (``12 bytes x params / dp`` per rank).
+  (``12 bytes x params / dp`` per rank); no other shard-sized state is kept
+  (weight-decay and TP-replication classes are contiguous ranges).
+* ``release_grad_buffer()`` frees the fp32 gradient buffer between training
+  phases (the colocated rollout needs that HBM for its KV cache).
 
 The reduce-scatter / all-gather here use NCCL; ``rl_b200.parallel.fused``
 provides the peer-memory kernels that fuse them with the cast/scale/Adam work.
@@ -77,6 +80,16 @@ class LRScheduler:
         return self.base_lr
 
 
+def _merge(ranges: list[tuple[int, int, bool]]) -> list[tuple[int, int, bool]]:
+    out: list[tuple[int, int, bool]] = []
+    for a, b, f in sorted(ranges):
+        if out and out[-1][2] == f and out[-1][1] == a:
+            out[-1] = (out[-1][0], b, f)
+        else:
+            out.append((a, b, f))
+    return out
+
+
 class FlatAdamW:
     def __init__(self, model, lr: float = 1e-5, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  max_grad_norm: Optional[float] = 1.0, scheduler_cfg=None, min_lr: float = 0.0,
@@ -96,50 +109,67 @@ class FlatAdamW:
         self.tp = dist.get_world_size(tp_group) if (tp_group is not None and dist.is_initialized()) else 1
         flat = model.flat_param
         n = flat.numel()
-        # pad so the flat buffer splits evenly over DP ranks in 128-element units
-        unit = 128 * self.dp
+        unit = 128 * self.dp  # shards are 128-element aligned
         self.padded = (n + unit - 1) // unit * unit
         if self.padded != n:
-            pad = torch.zeros(self.padded - n, dtype=flat.dtype, device=flat.device)
-            # re-home the flat buffer into a padded allocation (parameters keep their views)
-            big = torch.cat([flat.detach(), pad])
+            big = torch.zeros(self.padded, dtype=flat.dtype, device=flat.device)
+            big[:n].copy_(flat.detach())
             self._rehome(big)
+            del flat
         self.shard = self.padded // self.dp
         lo = self.dp_rank * self.shard
         self.lo, self.hi = lo, lo + self.shard
-        dev = flat.device
-        self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=dev)
-        self.master = model.flat_param[lo:lo + self.shard].float().clone()
+        dev = model.flat_param.device
+        self.device = dev
+        self.master = torch.empty(self.shard, dtype=torch.float32, device=dev)
+        self.master.copy_(model.flat_param[lo:lo + self.shard])
         self.exp_avg = torch.zeros(self.shard, dtype=torch.float32, device=dev)
         self.exp_avg_sq = torch.zeros(self.shard, dtype=torch.float32, device=dev)
-        self.grad_shard = self.main_grad[lo:lo + self.shard] if self.dp == 1 else \
-            torch.zeros(self.shard, dtype=torch.float32, device=dev)
-        # weight-decay mask over the shard (norm weights / biases are excluded)
-        self.wd_mask = torch.ones(self.shard, dtype=torch.float32, device=dev)
-        self.replicated_mask = torch.zeros(self.shard, dtype=torch.float32, device=dev)
+        # contiguous shard-local ranges: (start, end, weight-decayed) and (start, end, TP-replicated)
+        wd_r, rep_r = [], []
+        covered = 0
         for sp, p in model.named_flat_params():
             a, b = max(sp.offset, lo), min(sp.offset + sp.numel, lo + self.shard)
             if a < b:
-                if sp.no_weight_decay:
-                    self.wd_mask[a - lo:b - lo] = 0.0
-                if sp.tp_dim is None and sp.ep_dim is None:
-                    self.replicated_mask[a - lo:b - lo] = 1.0
-        self._attach_grads()
+                wd_r.append((a - lo, b - lo, not sp.no_weight_decay))
+                rep_r.append((a - lo, b - lo, sp.tp_dim is None and sp.ep_dim is None))
+        self.wd_ranges = _merge(wd_r)
+        self.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
+        self.main_grad: Optional[torch.Tensor] = None
+        self.grad_shard: Optional[torch.Tensor] = None
+        self.ensure_grad_buffer()
         self.step_count = 0
         self.last_grad_norm = 0.0
 
+    # -------------------------------------------------------------- buffers
     def _rehome(self, big: torch.Tensor) -> None:
         m = self.model
         m.flat_param = big
         for sp, p in m.named_flat_params():
             p.data = big[sp.offset: sp.offset + sp.numel].view(sp.shape)
 
-    def _attach_grads(self) -> None:
+    def ensure_grad_buffer(self) -> None:
+        if self.main_grad is not None:
+            return
+        self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
+        if self.dp == 1:
+            self.grad_shard = self.main_grad[self.lo:self.hi]
+        else:
+            self.grad_shard = torch.zeros(self.shard, dtype=torch.float32, device=self.device)
         for sp, p in self.model.named_flat_params():
             p.main_grad = self.main_grad[sp.offset: sp.offset + sp.numel].view(sp.shape)
 
+    def release_grad_buffer(self) -> None:
+        """Free the fp32 gradient buffers (re-created zeroed by ``ensure_grad_buffer``)."""
+        for _, p in self.model.named_flat_params():
+            p.main_grad = None
+            p.grad = None
+        self.main_grad = None
+        self.grad_shard = None
+
     def zero_grad(self) -> None:
-        self.main_grad.zero_()
+        if self.main_grad is not None:
+            self.main_grad.zero_()
         for _, p in self.model.named_flat_params():
             p.grad = None
 
@@ -151,8 +181,10 @@ class FlatAdamW:
                 p.main_grad.add_(p.grad.float())
                 p.grad = None
 
+    # ----------------------------------------------------------------- step
     @torch.no_grad()
     def step(self) -> dict:
+        self.ensure_grad_buffer()
         self._fold_param_grads()
         m = self.model
         if self.sequence_parallel and self.tp > 1:
@@ -166,9 +198,11 @@ class FlatAdamW:
             dist.reduce_scatter_tensor(self.grad_shard, self.main_grad, group=self.dp_group)
         g = self.grad_shard
         # global grad norm: TP-sharded parts summed over TP; replicated parts counted once
-        sq_rep = sum_of_squares(g * self.replicated_mask) if self.tp > 1 else None
         sq_all = sum_of_squares(g)
         if self.tp > 1:
+            sq_rep = torch.zeros((), dtype=torch.float32, device=g.device)
+            for a, b in self.rep_ranges:
+                sq_rep = sq_rep + sum_of_squares(g[a:b])
             sq_shard = sq_all - sq_rep
             dist.all_reduce(sq_shard, group=self.tp_group)
             sq = sq_shard + sq_rep
@@ -186,16 +220,11 @@ class FlatAdamW:
             return {"grad_norm": norm, "lr": self.current_lr(), "skipped": 1.0}
         self.step_count += 1
         lr = self.scheduler.lr_at(self.step_count - 1)
-        wd = self.weight_decay
         out = m.flat_param[self.lo:self.hi]
-        if wd > 0 and float(self.wd_mask.min()) < 1.0:
-            # decoupled decay only on masked-in params: apply decay separately
-            self.master.mul_(1 - lr * wd * self.wd_mask)
-            wd_eff = 0.0
-        else:
-            wd_eff = wd
-        adamw_step(self.master, g, self.exp_avg, self.exp_avg_sq, lr, self.beta1, self.beta2, self.eps, wd_eff,
-                   self.step_count, grad_scale=scale, param_out=out)
+        for a, b, decayed in self.wd_ranges:
+            adamw_step(self.master[a:b], g[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b], lr, self.beta1,
+                       self.beta2, self.eps, self.weight_decay if decayed else 0.0, self.step_count,
+                       grad_scale=scale, param_out=out[a:b])
         if self.dp > 1:
             dist.all_gather_into_tensor(m.flat_param, out.clone(), group=self.dp_group)
         self.zero_grad()
@@ -203,6 +232,14 @@ class FlatAdamW:
 
     def current_lr(self) -> float:
         return self.scheduler.lr_at(max(0, self.step_count - 1))
+
+    @torch.no_grad()
+    def restore_params_from_master(self) -> None:
+        """Rewrite the bf16 parameters from the fp32 master copy (after a weight swap)."""
+        m = self.model
+        m.flat_param[self.lo:self.hi].copy_(self.master)
+        if self.dp > 1:
+            dist.all_gather_into_tensor(m.flat_param, m.flat_param[self.lo:self.hi].clone(), group=self.dp_group)
 
     # ---------------------------------------------------------- state dict
     def state_dict(self) -> dict:
@@ -216,11 +253,7 @@ class FlatAdamW:
         self.exp_avg.copy_(sd["exp_avg"])
         self.exp_avg_sq.copy_(sd["exp_avg_sq"])
         self.step_count = int(sd["step"])
-        with torch.no_grad():
-            self.model.flat_param[self.lo:self.hi].copy_(self.master.to(self.model.flat_param.dtype))
-            if self.dp > 1:
-                dist.all_gather_into_tensor(self.model.flat_param, self.model.flat_param[self.lo:self.hi].clone(),
-                                            group=self.dp_group)
+        self.restore_params_from_master()
 
     def offload(self) -> None:
         for name in ("master", "exp_avg", "exp_avg_sq"):

@@ -1,0 +1,284 @@
+"""Numerics of every native sm_100a kernel against a plain PyTorch fp32 reference of the same op."""
+
+import math
+
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+
+from rl_b200.ops import _ext  # noqa: E402
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _need_ext(cuda_device):
+    assert _ext.has_ext(), "native extension must be built and loadable on a GPU box"
+    yield
+
+
+def rel_err(a, b):
+    a, b = a.float(), b.float()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+def test_rmsnorm_fwd_bwd(cuda_device):
+    from rl_b200.ops.norm import add_rms_norm, add_rms_norm_ref, rms_norm, rms_norm_ref
+
+    torch.manual_seed(0)
+    for H in (64, 4096, 5120, 100):
+        x = torch.randn(37, H, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+        w = (1 + 0.1 * torch.randn(H, device=cuda_device)).to(torch.bfloat16).requires_grad_(True)
+        y = rms_norm(x, w, 1e-5)
+        xr = x.detach().float().requires_grad_(True)
+        wr = w.detach().float().requires_grad_(True)
+        yr = rms_norm_ref(xr, wr, 1e-5)
+        assert rel_err(y, yr) < 1e-2
+        g = torch.randn_like(yr)
+        y.backward(g.to(torch.bfloat16))
+        yr.backward(g)
+        assert rel_err(x.grad, xr.grad) < 2e-2
+        assert rel_err(w.grad, wr.grad) < 2e-2
+    # fused residual add
+    H = 4096
+    x = torch.randn(19, H, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    d = torch.randn(19, H, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    w = torch.ones(H, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    y, s = add_rms_norm(x, d, w, 1e-5)
+    xr, dr, wr = (t.detach().float().requires_grad_(True) for t in (x, d, w))
+    yr, sr = add_rms_norm_ref(xr, dr, wr, 1e-5)
+    assert rel_err(y, yr) < 1e-2 and rel_err(s, sr) < 1e-2
+    gy, gs = torch.randn_like(yr), torch.randn_like(sr)
+    (y.float() * gy + s.float() * gs).sum().backward()
+    (yr * gy + sr * gs).sum().backward()
+    assert rel_err(x.grad, xr.grad) < 2e-2 and rel_err(d.grad, dr.grad) < 2e-2
+    assert rel_err(w.grad, wr.grad) < 2e-2
+
+
+def test_rope_and_inverse(cuda_device):
+    from rl_b200.ops.rope import apply_rope_qkv, apply_rope_qkv_ref, build_rope_cache
+
+    nq, nkv, hd, T = 8, 2, 128, 50
+    cache = build_rope_cache(4096, hd, 500000.0, {"rope_type": "llama3", "factor": 8.0, "low_freq_factor": 1.0,
+                                                  "high_freq_factor": 4.0, "original_max_position_embeddings": 8192},
+                             device=cuda_device)
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+    pos = torch.randint(0, 4000, (T,), device=cuda_device, dtype=torch.int32)
+    out = apply_rope_qkv(qkv, pos, cache, nq, nkv, hd)
+    ref = apply_rope_qkv_ref(qkv.detach().float(), pos, cache, nq, nkv, hd)
+    assert rel_err(out, ref) < 1e-2
+    g = torch.randn_like(ref)
+    out.backward(g.to(torch.bfloat16))
+    gref = apply_rope_qkv_ref(g, pos, cache, nq, nkv, hd, inverse=True)
+    assert rel_err(qkv.grad, gref) < 1e-2
+
+
+def test_swiglu(cuda_device):
+    from rl_b200.ops.activation import swiglu, swiglu_ref
+
+    for F in (14336, 172):
+        gu = torch.randn(33, 2 * F, device=cuda_device, dtype=torch.bfloat16, requires_grad=True)
+        out = swiglu(gu)
+        gr = gu.detach().float().requires_grad_(True)
+        ref = swiglu_ref(gr)
+        assert rel_err(out, ref) < 1e-2
+        g = torch.randn_like(ref)
+        out.backward(g.to(torch.bfloat16))
+        ref.backward(g)
+        assert rel_err(gu.grad, gr.grad) < 2e-2
+
+
+def test_logprob_partials_and_grad(cuda_device):
+    from rl_b200.ops.logprob import logits_entropy_ref, token_logprobs_and_entropy, token_logprobs_ref, \
+        vocab_parallel_logprobs
+
+    torch.manual_seed(1)
+    for V in (128256, 1000):
+        T = 40
+        logits = (3 * torch.randn(T, V, device=cuda_device)).to(torch.bfloat16)
+        tgt = torch.randint(0, V, (T,), device=cuda_device)
+        for temp in (1.0, 0.7):
+            lp, ent = token_logprobs_and_entropy(logits, tgt, temp)
+            assert torch.allclose(lp, token_logprobs_ref(logits, tgt, temp), atol=2e-3, rtol=1e-3)
+            assert torch.allclose(ent, logits_entropy_ref(logits, temp), atol=2e-3, rtol=1e-3)
+        # gradient (in-place backward) vs autograd of the fp32 reference
+        lg = logits.clone().requires_grad_(True)
+        lp, _ = vocab_parallel_logprobs(lg, tgt, 0, 1.0, None, inplace_backward=False)
+        g = torch.randn(T, device=cuda_device)
+        lp.backward(g)
+        lr = logits.float().requires_grad_(True)
+        token_logprobs_ref(lr, tgt, 1.0).backward(g)
+        assert rel_err(lg.grad, lr.grad) < 2e-2
+
+
+def test_fused_linear_logprobs(cuda_device):
+    from rl_b200.ops.fused_linear_logprob import linear_logprobs
+
+    torch.manual_seed(2)
+    T, H, V = 300, 256, 5000
+    h = (torch.randn(T, H, device=cuda_device) * 0.5).to(torch.bfloat16).requires_grad_(True)
+    W = (torch.randn(V, H, device=cuda_device) * 0.05).to(torch.bfloat16).requires_grad_(True)
+    tgt = torch.randint(0, V, (T,), device=cuda_device)
+    lp, ent = linear_logprobs(h, W, tgt, chunk=128)
+    hr, Wr = h.detach().float().requires_grad_(True), W.detach().float().requires_grad_(True)
+    lpr = torch.log_softmax(hr @ Wr.t(), -1).gather(-1, tgt[:, None]).squeeze(-1)
+    assert torch.allclose(lp, lpr, atol=3e-2, rtol=1e-2)
+    g = torch.randn(T, device=cuda_device)
+    lp.backward(g)
+    lpr.backward(g)
+    assert rel_err(h.grad, hr.grad) < 3e-2
+    assert rel_err(W.grad, Wr.grad) < 3e-2
+
+
+def test_sampling(cuda_device):
+    from rl_b200.ops.sampling import sample_tokens
+
+    torch.manual_seed(3)
+    B, V = 8, 50000
+    logits = torch.randn(B, V, device=cuda_device).to(torch.bfloat16)
+    # top_k = 1 is greedy
+    tok, lp = sample_tokens(logits, 1.0, top_k=1, top_p=1.0, seed=1)
+    assert torch.equal(tok, logits.float().argmax(-1))
+    assert torch.allclose(lp, torch.zeros_like(lp), atol=1e-5)
+    # logprob of the sampled token under the full distribution
+    tok, lp = sample_tokens(logits, 0.8, None, 1.0, seed=2)
+    ref = torch.log_softmax(logits.float() / 0.8, -1).gather(-1, tok[:, None]).squeeze(-1)
+    assert torch.allclose(lp, ref, atol=2e-3)
+    # empirical distribution over a small vocabulary
+    small = torch.tensor([[0.0, 1.0, 2.0, -1.0]], device=cuda_device).repeat(4096, 1)
+    toks, _ = sample_tokens(small, 1.0, None, 1.0, seed=7)
+    freq = torch.bincount(toks, minlength=4).float() / toks.numel()
+    p = torch.softmax(small[0], -1)
+    assert (freq - p).abs().max() < 0.03
+    # top-p keeps the smallest prefix reaching the mass
+    toks, lps = sample_tokens(small, 1.0, None, 0.8, seed=9)
+    assert set(toks.unique().tolist()) <= {2, 1}
+    kept = torch.softmax(torch.tensor([1.0, 2.0]), -1)
+    assert torch.allclose(lps[toks == 2].mean().exp().cpu(), kept[1], atol=1e-3)
+    # top-k = 2
+    toks, _ = sample_tokens(small, 1.0, 2, 1.0, seed=11)
+    assert set(toks.unique().tolist()) <= {1, 2}
+
+
+def test_adamw(cuda_device):
+    from rl_b200.ops.optim import adamw_step, adamw_step_ref, sum_of_squares
+
+    n = 10007
+    p = torch.randn(n, device=cuda_device)
+    g = torch.randn(n, device=cuda_device)
+    m = torch.zeros(n, device=cuda_device)
+    v = torch.zeros(n, device=cuda_device)
+    out = torch.empty(n, device=cuda_device, dtype=torch.bfloat16)
+    p2, m2, v2 = p.clone(), m.clone(), v.clone()
+    for step in (1, 2, 3):
+        adamw_step(p, g, m, v, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, 0.5, out)
+        adamw_step_ref(p2, g, m2, v2, 1e-3, 0.9, 0.999, 1e-8, 0.01, step, 0.5, None)
+    assert torch.allclose(p, p2, atol=1e-6, rtol=1e-5)
+    assert torch.allclose(out.float(), p2, atol=1e-2, rtol=1e-2)
+    assert torch.allclose(sum_of_squares(g), g.pow(2).sum(), rtol=1e-4)
+
+
+def test_fp8_quant(cuda_device):
+    from rl_b200.ops.quant import dequant_fp8_block, quant_fp8_block, quant_fp8_block_ref, quant_fp8_group, \
+        quant_fp8_group_ref
+
+    w = torch.randn(300, 520, device=cuda_device).to(torch.bfloat16)
+    for pow2 in (False, True):
+        q, s = quant_fp8_block(w, 128, pow2)
+        qr, sr = quant_fp8_block_ref(w, 128, pow2)
+        assert torch.allclose(s, sr, rtol=1e-6)
+        assert (q.float() - qr.float()).abs().max() <= 32.0  # at most one e4m3 ulp at the top of range
+        assert rel_err(dequant_fp8_block(q, s), w.float()) < 0.05
+    x = torch.randn(64, 512, device=cuda_device).to(torch.bfloat16)
+    q, s = quant_fp8_group(x, 128, False)
+    qr, sr = quant_fp8_group_ref(x, 128, False)
+    assert torch.allclose(s, sr, rtol=1e-6)
+    assert rel_err(q.float() * s.repeat_interleave(128, -1), x.float()) < 0.05
+
+
+def _varlen(cuda_device, lens, nq, nkv, hd):
+    T = sum(lens)
+    qkv = torch.randn(T, (nq + 2 * nkv) * hd, device=cuda_device, dtype=torch.bfloat16)
+    x = qkv.view(T, nq + 2 * nkv, hd)
+    q, k, v = x[:, :nq], x[:, nq:nq + nkv], x[:, nq + nkv:]
+    cu = torch.tensor([0] + list(torch.tensor(lens).cumsum(0)), device=cuda_device, dtype=torch.int32)
+    return q, k, v, cu
+
+
+@pytest.mark.parametrize("hd,nq,nkv", [(128, 8, 2), (64, 4, 4), (16, 4, 2)])
+def test_flash_attention_fwd_bwd(cuda_device, hd, nq, nkv):
+    from rl_b200.ops.attention import flash_attn_varlen, flash_attn_varlen_ref
+
+    torch.manual_seed(4)
+    lens = [1, 63, 64, 65, 200, 7]
+    q, k, v, cu = _varlen(cuda_device, lens, nq, nkv, hd)
+    q, k, v = (t.detach().requires_grad_(True) for t in (q, k, v))
+    o = flash_attn_varlen(q, k, v, cu, max(lens), causal=True)
+    qr, kr, vr = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    oref, _ = flash_attn_varlen_ref(qr, kr, vr, cu, None, True)
+    oref = oref.float()
+    # recompute ref in fp32 with autograd
+    qf, kf, vf = (t.detach().float().requires_grad_(True) for t in (q, k, v))
+    outs = []
+    for b in range(len(lens)):
+        s, e = int(cu[b]), int(cu[b + 1])
+        qb = qf[s:e].transpose(0, 1)
+        kb = kf[s:e].transpose(0, 1).repeat_interleave(nq // nkv, 0)
+        vb = vf[s:e].transpose(0, 1).repeat_interleave(nq // nkv, 0)
+        sc = (qb @ kb.transpose(-1, -2)) / math.sqrt(hd)
+        sc = sc.masked_fill(torch.ones(e - s, e - s, device=cuda_device, dtype=torch.bool).triu(1), float("-inf"))
+        outs.append((torch.softmax(sc, -1) @ vb).transpose(0, 1))
+    of = torch.cat(outs)
+    assert rel_err(o, of) < 2e-2
+    g = torch.randn_like(of)
+    o.backward(g.to(torch.bfloat16))
+    of.backward(g)
+    assert rel_err(q.grad, qf.grad) < 3e-2
+    assert rel_err(k.grad, kf.grad) < 3e-2
+    assert rel_err(v.grad, vf.grad) < 3e-2
+
+
+@pytest.mark.parametrize("G", [4, 8, 1])
+def test_paged_decode_and_cache_write(cuda_device, G):
+    from rl_b200.ops.attention import paged_decode_attention, paged_decode_attention_ref, write_kv_cache, \
+        write_kv_cache_ref
+
+    torch.manual_seed(5)
+    B, nkv, hd, bs = 5, 4, 128, 16
+    nq = nkv * G
+    lens = torch.tensor([1, 17, 100, 600, 33], dtype=torch.int32)
+    maxb = 64
+    nblocks = B * maxb + 1
+    kc = torch.zeros(nblocks, bs, nkv, hd, device=cuda_device, dtype=torch.bfloat16)
+    vc = torch.zeros_like(kc)
+    bt = (torch.randperm(nblocks - 1)[: B * maxb].view(B, maxb) + 1).to(torch.int32).to(cuda_device)
+    # fill the cache through the write kernel
+    rows, slots = [], []
+    for b in range(B):
+        for t in range(int(lens[b])):
+            slots.append(int(bt[b, t // bs]) * bs + t % bs)
+    n = len(slots)
+    kk = torch.randn(n, nkv, hd, device=cuda_device, dtype=torch.bfloat16)
+    vv = torch.randn(n, nkv, hd, device=cuda_device, dtype=torch.bfloat16)
+    sl = torch.tensor(slots, device=cuda_device)
+    write_kv_cache(kk, vv, kc, vc, sl)
+    kc2, vc2 = torch.zeros_like(kc), torch.zeros_like(vc)
+    write_kv_cache_ref(kk, vv, kc2, vc2, sl)
+    assert torch.equal(kc, kc2) and torch.equal(vc, vc2)
+    q = torch.randn(B, nq, hd, device=cuda_device, dtype=torch.bfloat16)
+    out = paged_decode_attention(q, kc, vc, bt, lens.to(cuda_device), max_seq_len=maxb * bs)
+    ref = paged_decode_attention_ref(q, kc, vc, bt, lens, None)
+    assert rel_err(out, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(256, 256, 64), (1000, 6144, 4096), (384, 4096, 14336), (77, 128, 192),
+                                   (4096, 768, 2048), (130, 96, 128)])
+def test_gemm_tcgen05(cuda_device, M, N, K):
+    ext = _ext.ext()
+    torch.manual_seed(6)
+    a = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    b = torch.randn(N, K, device=cuda_device).to(torch.bfloat16)
+    c = ext.gemm_nt(a, b)
+    torch.cuda.synchronize()
+    assert ext.gemm_error_flag(True) == 0
+    ref = a.float() @ b.float().t()
+    assert rel_err(c, ref) < 1e-2

@@ -229,3 +229,83 @@ std::vector<at::Tensor> rmsnorm_bwd_add(at::Tensor dy, at::Tensor x, at::Tensor 
                                         c10::optional<at::Tensor> ds) {
   return rmsnorm_bwd_impl(dy, x, w, rstd, ds);
 }
+
+// ---------------------------------------------------------------------------
+// Allocation-free C entry point (declared in noalloc.h, where its contract is
+// described; it has no counterpart in the reference).  It launches the same
+// backward kernels as rmsnorm_bwd above, with the per-CTA dw partials placed in
+// a static device array instead of a freshly allocated tensor.
+#include <cstdio>
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace rlb {
+static __device__ __align__(256) float g_noalloc_rmsnorm_partials[RLB_NOALLOC_MAX_CTAS * RLB_NOALLOC_MAX_HIDDEN];
+}  // namespace rlb
+
+namespace {
+constexpr int kNoallocMaxDevices = 64;
+float* g_noalloc_scratch[kNoallocMaxDevices] = {nullptr};
+std::mutex g_noalloc_mu;
+thread_local char g_noalloc_err[256] = "";
+
+int noalloc_fail(int code, const char* msg) {
+  std::snprintf(g_noalloc_err, sizeof(g_noalloc_err), "%s", msg);
+  return code;
+}
+
+bool aligned(const void* p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+}  // namespace
+
+extern "C" __attribute__((visibility("default"))) const char* rlb_noalloc_last_error(void) { return g_noalloc_err; }
+
+extern "C" __attribute__((visibility("default"))) int rlb_rmsnorm_bwd_noalloc(const void* dy, const void* x,
+                                                                            const void* w, const float* rstd,
+                                                                            void* dx, float* dw, int rows,
+                                                                            int hidden, cudaStream_t stream) {
+  if (!dy || !x || !w || !rstd || !dx || !dw) return noalloc_fail(1, "rlb_rmsnorm_bwd_noalloc: null pointer");
+  if (rows < 0 || hidden <= 0) return noalloc_fail(1, "rlb_rmsnorm_bwd_noalloc: rows must be >= 0 and hidden > 0");
+  if (hidden > RLB_NOALLOC_MAX_HIDDEN) {
+    std::snprintf(g_noalloc_err, sizeof(g_noalloc_err),
+                  "rlb_rmsnorm_bwd_noalloc: hidden=%d exceeds the static scratch maximum of %d", hidden,
+                  RLB_NOALLOC_MAX_HIDDEN);
+    return 2;
+  }
+  if (hidden % 8 == 0 && !(aligned(dy, 16) && aligned(x, 16) && aligned(w, 16) && aligned(dx, 16)))
+    return noalloc_fail(3, "rlb_rmsnorm_bwd_noalloc: dy, x, w and dx must be 16-byte aligned");
+  if (!aligned(rstd, 4) || !aligned(dw, 4)) return noalloc_fail(3, "rlb_rmsnorm_bwd_noalloc: rstd/dw misaligned");
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return noalloc_fail(4, cudaGetErrorString(e));
+  if (dev < 0 || dev >= kNoallocMaxDevices) return noalloc_fail(4, "rlb_rmsnorm_bwd_noalloc: device index too large");
+  float* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    if (g_noalloc_scratch[dev] == nullptr) {
+      void* p = nullptr;
+      e = cudaGetSymbolAddress(&p, rlb::g_noalloc_rmsnorm_partials);
+      if (e != cudaSuccess || p == nullptr) return noalloc_fail(5, cudaGetErrorString(e));
+      g_noalloc_scratch[dev] = static_cast<float*>(p);
+    }
+    scratch = g_noalloc_scratch[dev];
+  }
+  if (rows == 0) {
+    e = cudaMemsetAsync(dw, 0, sizeof(float) * hidden, stream);
+    return e == cudaSuccess ? 0 : noalloc_fail(6, cudaGetErrorString(e));
+  }
+  const int ctas = std::min((rows + kNormWarps - 1) / kNormWarps, RLB_NOALLOC_MAX_CTAS);
+  const size_t smem = (size_t)kNormWarps * hidden * sizeof(float);
+  auto kern = rmsnorm_bwd_kernel<__nv_bfloat16>;
+  if (smem > 48 * 1024) {
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    if (e != cudaSuccess) return noalloc_fail(6, cudaGetErrorString(e));
+  }
+  kern<<<ctas, kNormWarps * 32, smem, stream>>>(
+      static_cast<const __nv_bfloat16*>(dy), static_cast<const __nv_bfloat16*>(x),
+      static_cast<const __nv_bfloat16*>(w), rstd, nullptr, static_cast<__nv_bfloat16*>(dx), scratch, rows, hidden);
+  reduce_rows_kernel<<<(hidden + 255) / 256, 256, 0, stream>>>(scratch, dw, ctas, hidden);
+  e = cudaGetLastError();
+  if (e != cudaSuccess) return noalloc_fail(6, cudaGetErrorString(e));
+  return 0;
+}

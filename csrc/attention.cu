@@ -210,6 +210,174 @@ paged_decode_kernel(const bf16* __restrict__ q, long long q_stride, const C* __r
   }
 }
 
+// Tensor-core decode: each warp owns 32-token K/V tiles of one (sequence, KV
+// head), loaded with cp.async as whole 256-byte rows (coalesced) into swizzled
+// shared memory; S = Q K^T and O += P V run as m16n8k16 MMAs with the G query
+// heads of the group in rows 0..G-1 of the A operand (rows G..15 are zero).
+// The 4 warps of a CTA take tiles round-robin and merge their online-softmax
+// states at the end; split-K partials go to the combine kernel.
+template <int HD, int G>
+__global__ void __launch_bounds__(128)
+paged_decode_tc_kernel(const bf16* __restrict__ q, long long q_stride, const bf16* __restrict__ kc,
+                       const bf16* __restrict__ vc, const int* __restrict__ block_tables, int max_blocks,
+                       const int* __restrict__ seq_lens, int block_size, int nkv, float scale_log2,
+                       int tokens_per_split, float* __restrict__ part_o, float* __restrict__ part_ml,
+                       bf16* __restrict__ out) {
+  constexpr int BT = 32, CH = HD / 8, KS = HD / 16, NT = HD / 8;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  bf16* Ks = reinterpret_cast<bf16*>(smem_raw) + w * 2 * BT * HD;
+  bf16* Vs = Ks + BT * HD;
+  float* red = reinterpret_cast<float*>(reinterpret_cast<bf16*>(smem_raw) + 4 * 2 * BT * HD);  // [4][G][HD+2]
+  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int g = lane >> 2, t = lane & 3;
+  const int L = seq_lens[b];
+  const int t_begin = split * tokens_per_split;
+  const int t_end = min(L, t_begin + tokens_per_split);
+  const int nq = nkv * G;
+  const int* bt = block_tables + (long long)b * max_blocks;
+  // Q fragments (rows >= G are zero)
+  uint32_t qf[KS][4];
+  {
+    const bf16* qb = q + (long long)b * q_stride + (long long)kvh * G * HD;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      const int c0 = kk * 16 + 2 * t;
+      const bool ok = g < G;
+      const uint32_t lo0 = ok ? *reinterpret_cast<const uint32_t*>(qb + g * HD + c0) : 0u;
+      const uint32_t lo1 = ok ? *reinterpret_cast<const uint32_t*>(qb + g * HD + c0 + 8) : 0u;
+      qf[kk][0] = lo0;
+      qf[kk][1] = 0u;  // row g + 8 >= 8 > G - 1 for G <= 8
+      qf[kk][2] = lo1;
+      qf[kk][3] = 0u;
+    }
+  }
+  float oacc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+  float mrow = -INFINITY, lrow = 0.f;
+  for (int t0 = t_begin + w * BT; t0 < t_end; t0 += 4 * BT) {
+    const int nvalid = min(BT, t_end - t0);
+    // cp.async K/V rows of this tile (per-row block-table lookup)
+    for (int c = lane; c < BT * CH; c += 32) {
+      const int r = c / CH, ch = c % CH;
+      const bool ok = r < nvalid;
+      long long row = 0;
+      if (ok) {
+        const int tok = t0 + r;
+        row = ((long long)bt[tok / block_size] * block_size + (tok % block_size)) * nkv + kvh;
+      }
+      cp_async16(smem_u32(Ks + swz<CH>(r, ch) * 8), kc + row * HD + ch * 8, ok ? 16 : 0);
+      cp_async16(smem_u32(Vs + swz<CH>(r, ch) * 8), vc + row * HD + ch * 8, ok ? 16 : 0);
+    }
+    cp_async_commit();
+    cp_async_wait_all();
+    __syncwarp();
+    float s[BT / 8][4];
+#pragma unroll
+    for (int j = 0; j < BT / 8; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+#pragma unroll
+      for (int np = 0; np < BT / 16; ++np) {
+        uint32_t bfr[4];
+        ldsm_x4(bfr, smem_u32(Ks + swz<CH>(np * 16 + ((lane >> 4) << 3) + (lane & 7), 2 * kk + ((lane >> 3) & 1)) * 8));
+        mma16816(s[2 * np], qf[kk], bfr[0], bfr[1]);
+        mma16816(s[2 * np + 1], qf[kk], bfr[2], bfr[3]);
+      }
+    }
+    // online softmax over row g (rows g+8 are padding)
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < BT / 8; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = 8 * j + 2 * t + e;
+        const float v = key < nvalid ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][e] = v;
+        mx = fmaxf(mx, v);
+      }
+      s[j][2] = s[j][3] = 0.f;
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(mrow, mx);
+    const float muse = mnew == -INFINITY ? 0.f : mnew;
+    const float alpha = exp2f(mrow - muse);
+    mrow = mnew;
+    lrow *= alpha;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      oacc[j][0] *= alpha;
+      oacc[j][1] *= alpha;
+    }
+#pragma unroll
+    for (int j = 0; j < BT / 8; ++j) {
+      s[j][0] = exp2f(s[j][0] - muse);
+      s[j][1] = exp2f(s[j][1] - muse);
+      lrow += s[j][0] + s[j][1];
+    }
+#pragma unroll
+    for (int kk = 0; kk < BT / 16; ++kk) {
+      uint32_t a[4];
+      a[0] = pack_bf16(s[2 * kk][0], s[2 * kk][1]);
+      a[1] = 0u;
+      a[2] = pack_bf16(s[2 * kk + 1][0], s[2 * kk + 1][1]);
+      a[3] = 0u;
+#pragma unroll
+      for (int dp = 0; dp < NT / 2; ++dp) {
+        uint32_t bfr[4];
+        ldsm_x4_t(bfr, smem_u32(Vs + swz<CH>(kk * 16 + (lane & 15), 2 * dp + (lane >> 4)) * 8));
+        mma16816(oacc[2 * dp], a, bfr[0], bfr[1]);
+        mma16816(oacc[2 * dp + 1], a, bfr[2], bfr[3]);
+      }
+    }
+    __syncwarp();
+  }
+  lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
+  lrow += __shfl_xor_sync(0xffffffffu, lrow, 2);
+  // per-warp state -> shared memory: red[w][g][0..HD) = o, [HD] = m, [HD+1] = l
+  constexpr int RS = HD + 2;
+  if (g < G) {
+    float* rw = red + ((size_t)w * G + g) * RS;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      rw[8 * j + 2 * t] = oacc[j][0];
+      rw[8 * j + 2 * t + 1] = oacc[j][1];
+    }
+    if (t == 0) {
+      rw[HD] = mrow;
+      rw[HD + 1] = lrow;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * HD; e += blockDim.x) {
+    const int gg = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) M = fmaxf(M, red[((size_t)k * G + gg) * RS + HD]);
+    float Lsum = 0.f, O = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float* rk = red + ((size_t)k * G + gg) * RS;
+      const float f = rk[HD] == -INFINITY ? 0.f : exp2f(rk[HD] - M);
+      Lsum += rk[HD + 1] * f;
+      O += rk[d] * f;
+    }
+    const int h = kvh * G + gg;
+    if (part_o == nullptr) {
+      out[(long long)b * nq * HD + h * HD + d] = __float2bfloat16_rn(Lsum > 0.f ? O / Lsum : 0.f);
+    } else {
+      const long long pi = ((long long)(b * nq + h) * gridDim.z + split);
+      part_o[pi * HD + d] = O;
+      if (d == 0) {
+        part_ml[pi * 2] = M;
+        part_ml[pi * 2 + 1] = Lsum;
+      }
+    }
+  }
+}
+
 template <int HD>
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits,
                                       int nq, bf16* __restrict__ out) {
@@ -722,7 +890,20 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
     constexpr int GG = decltype(gtag)::value;
     using C = typename decltype(ctag)::type;
     RLB_HD_SWITCH(hd, [&] {
-      if constexpr (HD >= 32) {
+      if constexpr (HD >= 64 && std::is_same<C, bf16>::value) {
+        dim3 grid(B, nkv, splits);
+        const int smem = 4 * 2 * 32 * HD * 2 + 4 * GG * (HD + 2) * 4;
+        auto kern = paged_decode_tc_kernel<HD, GG>;
+        if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        kern<<<grid, 128, smem, stream()>>>(
+            (const bf16*)q.data_ptr(), q.stride(0), (const bf16*)k_cache.data_ptr(), (const bf16*)v_cache.data_ptr(),
+            bt.data_ptr<int>(), max_blocks, sl.data_ptr<int>(), bs, nkv, scale_log2, tps,
+            splits > 1 ? part_o.data_ptr<float>() : nullptr, splits > 1 ? part_ml.data_ptr<float>() : nullptr,
+            (bf16*)out.data_ptr());
+        if (splits > 1)
+          decode_combine_kernel<HD><<<B * nq, HD, 0, stream()>>>(part_o.data_ptr<float>(), part_ml.data_ptr<float>(),
+                                                                 splits, nq, (bf16*)out.data_ptr());
+      } else if constexpr (HD >= 32) {
         dim3 grid(B, nkv, splits);
         paged_decode_kernel<C, HD, GG><<<grid, 128, 0, stream()>>>(
             (const bf16*)q.data_ptr(), q.stride(0), (const C*)k_cache.data_ptr(), (const C*)v_cache.data_ptr(),

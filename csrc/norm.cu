@@ -75,6 +75,57 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta, const T
   }
 }
 
+// Few-row variant (decode batches): one 128-thread CTA per row so that a batch of
+// tens of rows still spreads over many SMs.  bf16 rows with H % 8 == 0 only.
+__global__ void __launch_bounds__(128)
+rmsnorm_fwd_rowcta_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
+                          const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
+                          __nv_bfloat16* __restrict__ s_out, float* __restrict__ rstd, int H, float eps) {
+  __shared__ float red[32];
+  const int row = blockIdx.x;
+  const int nv = H / 8;
+  const bf16x8* xr = reinterpret_cast<const bf16x8*>(x + (size_t)row * H);
+  const bf16x8* dr = delta ? reinterpret_cast<const bf16x8*>(delta + (size_t)row * H) : nullptr;
+  bf16x8* sr = s_out ? reinterpret_cast<bf16x8*>(s_out + (size_t)row * H) : nullptr;
+  constexpr int kMaxV = 8;  // vectors per thread kept in registers (H <= 8192)
+  float v[kMaxV][8];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < kMaxV; ++k) {
+    const int j = threadIdx.x + k * 128;
+    if (j < nv) {
+      unpack8(xr[j], v[k]);
+      if (dr) {
+        float d[8];
+        unpack8(dr[j], d);
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[k][i] += d[i];
+        bf16x8 p = pack8(v[k]);
+        sr[j] = p;
+        unpack8(p, v[k]);
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) ss += v[k][i] * v[k][i];
+    }
+  }
+  ss = block_sum(ss, red);
+  const float r = rsqrtf(ss / H + eps);
+  if (threadIdx.x == 0) rstd[row] = r;
+  bf16x8* yr = reinterpret_cast<bf16x8*>(y + (size_t)row * H);
+  const bf16x8* wv = reinterpret_cast<const bf16x8*>(w);
+#pragma unroll
+  for (int k = 0; k < kMaxV; ++k) {
+    const int j = threadIdx.x + k * 128;
+    if (j < nv) {
+      float g[8];
+      unpack8(wv[j], g);
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[k][i] = v[k][i] * r * g[i];
+      yr[j] = pack8(v[k]);
+    }
+  }
+}
+
 // dx = r * dy * w - x * r^3 * sum(dy * w * x) / H   (+ ds)
 // dw_partial[cta][h] = sum over this CTA's rows of dy * x * r
 template <typename T>
@@ -166,6 +217,13 @@ std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
   auto y = at::empty_like(x);
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   if (rows == 0) return {y, rstd};
+  if (x.scalar_type() == at::kBFloat16 && H % 8 == 0 && H <= 8192 && rows < 4 * num_sms()) {
+    rmsnorm_fwd_rowcta_kernel<<<rows, 128, 0, stream()>>>(
+        (const __nv_bfloat16*)x.data_ptr(), nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
+        nullptr, rstd.data_ptr<float>(), H, (float)eps);
+    RLB_CUDA_CHECK(cudaGetLastError());
+    return {y, rstd};
+  }
   dim3 grid((rows + kNormWarps - 1) / kNormWarps);
   RLB_DISPATCH_FLOAT(x.scalar_type(), "rmsnorm_fwd", [&] {
     rmsnorm_fwd_kernel<scalar_t><<<grid, kNormWarps * 32, 0, stream()>>>(
@@ -185,6 +243,13 @@ std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor delta, at::Tens
   auto s = at::empty_like(x);
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   if (rows == 0) return {y, s, rstd};
+  if (x.scalar_type() == at::kBFloat16 && H % 8 == 0 && H <= 8192 && rows < 4 * num_sms()) {
+    rmsnorm_fwd_rowcta_kernel<<<rows, 128, 0, stream()>>>(
+        (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)delta.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
+        (__nv_bfloat16*)y.data_ptr(), (__nv_bfloat16*)s.data_ptr(), rstd.data_ptr<float>(), H, (float)eps);
+    RLB_CUDA_CHECK(cudaGetLastError());
+    return {y, s, rstd};
+  }
   dim3 grid((rows + kNormWarps - 1) / kNormWarps);
   RLB_DISPATCH_FLOAT(x.scalar_type(), "add_rmsnorm_fwd", [&] {
     rmsnorm_fwd_kernel<scalar_t><<<grid, kNormWarps * 32, 0, stream()>>>(

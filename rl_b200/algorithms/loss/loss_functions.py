@@ -72,6 +72,12 @@ DEFAULT_CLIPPED_PG_CONFIG: dict[str, Any] = {
 }
 
 
+def _m(x):
+    """Metric value: kept on the device (detached) so that a training step reads all
+    metrics back in one transfer instead of synchronising per micro-batch."""
+    return x.detach() if isinstance(x, torch.Tensor) else float(x)
+
+
 def _finite(x: torch.Tensor) -> torch.Tensor:
     return torch.nan_to_num(x, nan=0.0, posinf=0.0, neginf=0.0)
 
@@ -151,7 +157,7 @@ class ClippedPGLossFn:
         if self.seq_err_in_loss:
             errs, _ = compute_seq_logprob_errors(curr.detach(), gen_lp, token_mask, sample_mask)
             keep = (errs <= float(self.seq_err_threshold)).to(curr.dtype)
-            metrics["num_masked_seqs_by_logprob_error"] = float((sample_mask * (1 - keep)).sum())
+            metrics["num_masked_seqs_by_logprob_error"] = _m((sample_mask * (1 - keep)).sum())
             sample_mask = sample_mask * keep
             mask = token_mask * sample_mask.unsqueeze(-1)
             prev_lp = curr.detach()
@@ -218,25 +224,25 @@ class ClippedPGLossFn:
             pos = (data["advantages"][:, 1:] > 0).to(curr.dtype) * mask
             nll = masked_mean(-curr_m, pos, global_normalization_factor=global_valid_toks)
             loss = loss + self.nll_weight * nll
-            metrics["positive_nll"] = float(nll.detach())
+            metrics["positive_nll"] = _m(nll.detach())
 
         with torch.no_grad():
             gtok = global_valid_toks
             metrics.update({
-                "loss": float(loss.detach()),
-                "actor_loss": float(actor.detach()),
-                "kl_penalty": float(kl.detach()),
-                "num_valid_samples": float(sample_mask.sum()),
+                "loss": _m(loss.detach()),
+                "actor_loss": _m(actor.detach()),
+                "kl_penalty": _m(kl.detach()),
+                "num_valid_samples": _m(sample_mask.sum()),
             })
             if self.full_metrics:
                 big = torch.full_like(ratios, float("inf"))
                 metrics.update({
-                    "probs_ratio": float(masked_mean(ratios.detach(), mask, global_normalization_factor=gtok)),
-                    "probs_ratio_clamped": float(masked_mean(ratios_c.detach(), mask, global_normalization_factor=gtok)),
-                    "probs_ratio_min": float(torch.where(mb, ratios.detach(), big).min()),
-                    "probs_ratio_max": float(torch.where(mb, ratios.detach(), -big).max()),
-                    "probs_ratio_clamped_min": float(torch.where(mb, ratios_c.detach(), big).min()),
-                    "probs_ratio_clamped_max": float(torch.where(mb, ratios_c.detach(), -big).max()),
+                    "probs_ratio": _m(masked_mean(ratios.detach(), mask, global_normalization_factor=gtok)),
+                    "probs_ratio_clamped": _m(masked_mean(ratios_c.detach(), mask, global_normalization_factor=gtok)),
+                    "probs_ratio_min": _m(torch.where(mb, ratios.detach(), big).min()),
+                    "probs_ratio_max": _m(torch.where(mb, ratios.detach(), -big).max()),
+                    "probs_ratio_clamped_min": _m(torch.where(mb, ratios_c.detach(), big).min()),
+                    "probs_ratio_clamped_max": _m(torch.where(mb, ratios_c.detach(), -big).max()),
                 })
                 metrics.update(self._diagnostics(curr_m.detach(), prev_m, gen_m, mask, gtok))
         return loss, metrics
@@ -265,11 +271,11 @@ class ClippedPGLossFn:
             keep = ((geo >= float(lo)) & (geo <= hi)).to(w.dtype)
             raw = _finite(torch.exp(prev_m - gen_m)).detach()
             w = raw * keep.unsqueeze(-1)
-            oob_frac = float(((1 - keep) * (mask.sum(-1) > 0).to(w.dtype)).sum())
+            oob_frac = _m(((1 - keep) * (mask.sum(-1) > 0).to(w.dtype)).sum())
             return w, oob_frac
         else:
             raise ValueError(f"unknown truncated_importance_sampling_type {kind!r}")
-        return w, float((oob.expand_as(mask) * mask).sum() / mask.sum().clamp_min(1))
+        return w, _m((oob.expand_as(mask) * mask).sum() / mask.sum().clamp_min(1))
 
     @staticmethod
     @torch.no_grad()
@@ -283,11 +289,11 @@ class ClippedPGLossFn:
         ent = -masked_mean(torch.exp(curr_m - gen_m) * curr_m, mask, global_normalization_factor=gtok)
         mult_err = masked_mean(torch.exp((gen_m - prev_m).abs()), mask, global_normalization_factor=gtok)
         return {
-            "gen_kl_error": float(kl_gen),
-            "policy_kl_error": float(kl_pol),
-            "js_divergence_error": float(js),
-            "approx_entropy": float(ent),
-            "token_mult_prob_error": float(mult_err),
+            "gen_kl_error": _m(kl_gen),
+            "policy_kl_error": _m(kl_pol),
+            "js_divergence_error": _m(js),
+            "approx_entropy": _m(ent),
+            "token_mult_prob_error": _m(mult_err),
         }
 
 
@@ -302,7 +308,7 @@ class NLLLossFn:
         sample_mask = data["sample_mask"].to(next_token_logprobs.dtype)
         mask = token_mask * sample_mask.unsqueeze(-1)
         loss = masked_mean(-next_token_logprobs, mask, global_normalization_factor=global_valid_toks)
-        return loss, {"loss": float(loss.detach()), "num_unmasked_tokens": float(mask.sum())}
+        return loss, {"loss": _m(loss.detach()), "num_unmasked_tokens": _m(mask.sum())}
 
 
 def _seq_logprob(lp: torch.Tensor, mask: torch.Tensor, average: bool) -> torch.Tensor:
@@ -344,11 +350,11 @@ class DPOLossFn:
             loss = loss + self.sft_loss_weight * sft
         acc = masked_mean((margin > 0).to(margin.dtype), pair_mask, global_normalization_factor=n_pairs)
         return loss, {
-            "loss": float(loss.detach()),
-            "preference_loss": float(pref.detach()),
-            "accuracy": float(acc),
-            "rewards_chosen_mean": float((self.beta * chosen).mean().detach()),
-            "rewards_rejected_mean": float((self.beta * rejected).mean().detach()),
+            "loss": _m(loss.detach()),
+            "preference_loss": _m(pref.detach()),
+            "accuracy": _m(acc),
+            "rewards_chosen_mean": _m((self.beta * chosen).mean().detach()),
+            "rewards_rejected_mean": _m((self.beta * rejected).mean().detach()),
         }
 
 
@@ -364,7 +370,7 @@ class PreferenceLossFn:
         n_pairs = global_valid_seqs / 2
         loss = masked_mean(-F.logsigmoid(chosen - rejected), pair_mask, global_normalization_factor=n_pairs)
         acc = masked_mean((chosen > rejected).to(rewards.dtype), pair_mask, global_normalization_factor=n_pairs)
-        return loss, {"loss": float(loss.detach()), "accuracy": float(acc)}
+        return loss, {"loss": _m(loss.detach()), "accuracy": _m(acc)}
 
 
 class DistillationLossFn:
@@ -403,7 +409,7 @@ class DistillationLossFn:
         else:
             tok = self.mixed_kl_weight * fwd + (1 - self.mixed_kl_weight) * rev
         loss = masked_mean(tok, mask, global_normalization_factor=global_valid_toks)
-        return loss, {"loss": float(loss.detach())}
+        return loss, {"loss": _m(loss.detach())}
 
 
 class ValueLossFn:
@@ -425,4 +431,4 @@ class ValueLossFn:
             vc = old + (values - old).clamp(-float(self.clip), float(self.clip))
             l1 = torch.maximum(l1, (vc - returns) ** 2)
         loss = 0.5 * masked_mean(l1, mask, global_normalization_factor=global_valid_toks)
-        return loss, {"value_loss": float(loss.detach())}
+        return loss, {"value_loss": _m(loss.detach())}

@@ -66,6 +66,7 @@ class _DecodeState:
         self.out_logprobs = torch.zeros(B, max_new + 1, dtype=torch.float32, device=device)
         self.next_tokens = torch.zeros(B, dtype=i64, device=device)
         self.next_logprobs = torch.zeros(B, dtype=torch.float32, device=device)
+        self.stop = torch.full((8,), -1, dtype=i64, device=device)  # stop-token ids (graph input)
         self.graph: Optional[torch.cuda.CUDAGraph] = None
         self.native_launches = 0
 
@@ -90,6 +91,9 @@ class RolloutEngine:
         self._graph_pool = None
         self.calls = 0
         self.stats: dict = {}
+        # optional callable returning a device buffer whose bytes the KV cache may
+        # occupy while generating (colocated trainer: its idle gradient arena)
+        self.kv_arena = None
 
     # ------------------------------------------------------------ lifecycle
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
@@ -97,20 +101,35 @@ class RolloutEngine:
         if self.kv is None:
             n = num_seqs or self.max_num_seqs
             blocks = n * self.max_blocks_per_seq + 1
+            arena = self.kv_arena() if self.kv_arena is not None else None
             self.kv = KVCache(self.model.cfg.num_layers, blocks, self.block_size, self.model.nkv, self.model.hd,
-                              self.kv_dtype, self.device)
+                              self.kv_dtype, self.device, arena=arena)
             self._kv_capacity_seqs = n
+            sig = (self.kv.storage.data_ptr(), tuple(self.kv.storage.shape))
+            if sig != getattr(self, "_kv_sig", None):
+                self._drop_graphs()  # captured graphs point at the old cache
+            self._kv_sig = sig
         return True
 
-    def finish_generation(self) -> bool:
-        """Free (sleep) the KV cache and decode graphs so training gets the memory back."""
-        self.kv = None
+    def _drop_graphs(self) -> None:
         for st in self._states.values():
             st.graph = None
         self._states.clear()
         self._graph_pool = None
-        if self.device.type == "cuda":
-            torch.cuda.empty_cache()
+
+    def finish_generation(self) -> bool:
+        """Release (sleep) the KV cache so training gets the memory back.
+
+        When the cache lives in a persistent arena its address is stable across
+        steps, so the captured decode graphs are kept and replayed next time;
+        otherwise they are dropped with the cache."""
+        self.kv = None
+        if self.kv_arena is None:
+            self._drop_graphs()
+            self._kv_sig = None
+        # No empty_cache(): the freed KV blocks stay mapped in the caching allocator and
+        # are reused by the trainer's gradient buffer (and vice versa) every step,
+        # instead of being unmapped and re-mapped (seconds per step for ~45 GB).
         return True
 
     def invalidate_kv_cache(self) -> bool:
@@ -171,8 +190,8 @@ class RolloutEngine:
         if dev.type == "cpu":
             gen = torch.Generator().manual_seed(self.seed * 7919 + self.calls)
         tok0, lp0 = sample_tokens(logits, temperature if temperature > 0 else 1.0,
-                                  1 if temperature == 0 else top_k, top_p, seed=self.seed + self.calls * 1000003,
-                                  offset=0, generator=gen)
+                                  1 if temperature == 0 else top_k, top_p, seed=self.seed,
+                                  offset=self.calls * (1 << 24), generator=gen)
         if temperature == 0:
             lp0 = torch.zeros_like(lp0)
 
@@ -223,8 +242,10 @@ class RolloutEngine:
         while rows.numel() > 0 and step_done < max_new:
             nb = next(b for b in _buckets(self.max_num_seqs) if b >= rows.numel()) \
                 if rows.numel() <= self.max_num_seqs else rows.numel()
-            st = self._state(nb, max_new)
+            st = self._state(nb, max_new, (temperature, top_k, top_p))
             n = rows.numel()
+            st.stop.fill_(-1)
+            st.stop[: min(len(stop_ids), st.stop.numel())] = stop[: st.stop.numel()] if stop_ids else -1
             st.done.fill_(True)
             st.done[:n] = False
             st.tokens.zero_()
@@ -237,11 +258,13 @@ class RolloutEngine:
             st.gen_len[:n] = glen[rows]
             st.max_new.fill_(max_new)
             st.step.fill_(0)
-            st.rng_offset.fill_(step_done + 1)
+            # the random stream depends on (call, step) through this device offset, so a
+            # replayed graph draws fresh noise on every generate() call and step
+            st.rng_offset.fill_(self.calls * (1 << 24) + step_done + 1)
             st.out_tokens.zero_()
             st.out_logprobs.zero_()
             if st.graph is None:
-                self._capture(st, temperature, top_k, top_p, stop)
+                self._capture(st, temperature, top_k, top_p, st.stop)
             k = 0
             while True:
                 st.graph.replay()
@@ -268,11 +291,14 @@ class RolloutEngine:
             rows = rows[still]
         return tokens_all, lps_all, glen
 
-    def _state(self, nb: int, max_new: int) -> _DecodeState:
-        st = self._states.get(nb)
+    def _state(self, nb: int, max_new: int, sampling_key: tuple = ()) -> _DecodeState:
+        """Decode buffers + graph for one batch bucket.  Sampling parameters are
+        baked into a captured graph, so they are part of the cache key."""
+        key = (nb,) + tuple(sampling_key)
+        st = self._states.get(key)
         if st is None or st.out_tokens.shape[1] < max_new + 1:
             st = _DecodeState(nb, self.max_blocks_per_seq, max_new, self.device)
-            self._states[nb] = st
+            self._states[key] = st
         return st
 
     def _step_body(self, st: _DecodeState, temperature, top_k, top_p, stop):
@@ -287,7 +313,7 @@ class RolloutEngine:
         from rl_b200.ops.sampling import sample_tokens_graphable
 
         sample_tokens_graphable(logits, temperature if temperature > 0 else 1.0,
-                                1 if temperature == 0 else top_k, top_p, self.seed + self.calls * 1000003,
+                                1 if temperature == 0 else top_k, top_p, self.seed,
                                 st.rng_offset, st.next_tokens, st.next_logprobs)
         if temperature == 0:
             st.next_logprobs.zero_()
@@ -340,7 +366,7 @@ class RolloutEngine:
             logits = self.model.logits_infer(h)
             nt, nlp = sample_tokens(logits, temperature if temperature > 0 else 1.0,
                                     1 if temperature == 0 else top_k, top_p,
-                                    seed=self.seed + self.calls * 1000003, offset=step + 1, generator=gen)
+                                    seed=self.seed, offset=self.calls * (1 << 24) + step + 1, generator=gen)
             if temperature == 0:
                 nlp = torch.zeros_like(nlp)
             active = ~done

@@ -20,6 +20,7 @@ import math
 import time
 from typing import Any, Optional
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -39,6 +40,13 @@ __all__ = ["PolicyWorker", "pack_rows"]
 def _dtype(precision: str) -> torch.dtype:
     return {"bfloat16": torch.bfloat16, "bf16": torch.bfloat16, "float32": torch.float32, "fp32": torch.float32,
             "float16": torch.float16}.get(str(precision), torch.bfloat16)
+
+
+def _to_device(t: torch.Tensor, dev: torch.device) -> torch.Tensor:
+    """Host tensor -> device via pinned memory (asynchronous on the current stream)."""
+    if dev.type != "cuda" or t.is_cuda:
+        return t.to(dev)
+    return t.pin_memory().to(dev, non_blocking=True)
 
 
 def pack_rows(input_ids: torch.Tensor, lengths: list[int], rows: list[int], pad_to_multiple: int = 1):
@@ -111,7 +119,12 @@ class PolicyWorker:
         self.packing_algorithm = sp.get("algorithm", "modified_first_fit_decreasing")
         self.logprob_chunk = int(policy_cfg.get("logprob_chunk_size") or 4096)
         # colocated rollout needs the HBM of the fp32 gradient buffer for its KV cache
-        self.release_grad_after_train = bool(policy_cfg.get("release_grad_after_train", self.device.type == "cuda"))
+        # HBM plan of the colocated worker: the fp32 gradient buffer (4 bytes/param) is
+        # persistent and doubles as the paged KV cache's storage during rollout (the
+        # two are never live together); it is re-zeroed at the start of train().
+        self.release_grad_after_train = bool(policy_cfg.get("release_grad_after_train", False))
+        if bool(policy_cfg.get("kv_cache_in_grad_arena", self.device.type == "cuda")):
+            self.engine.kv_arena = lambda: self.optimizer.main_grad
         self.timer = Timer()
 
     # ------------------------------------------------------------- helpers
@@ -127,7 +140,7 @@ class PolicyWorker:
         tp = self.ps.tp_size if self.sequence_parallel else 1
         flat, pos, cu, max_len, T_real = pack_rows(input_ids, lengths, rows, pad_to_multiple=tp)
         dev = self.device
-        flat_d, pos_d, cu_d = flat.to(dev, non_blocking=True), pos.to(dev, non_blocking=True), cu.to(dev)
+        flat_d, pos_d, cu_d = _to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev)
         targets = torch.empty_like(flat_d)
         targets[:-1] = flat_d[1:]
         targets[-1:] = 0
@@ -139,21 +152,25 @@ class PolicyWorker:
 
     @staticmethod
     def _to_padded(lp: torch.Tensor, cu: torch.Tensor, n_rows: int, width: int) -> torch.Tensor:
-        """Packed next-token scores -> ``[n, width-1]`` where column i scores token i+1."""
-        cu_l = cu.tolist()
-        src, dst = [], []
-        for b in range(n_rows):
-            s, e = cu_l[b], cu_l[b + 1]
-            L = e - s
-            if L > 1:
-                src.append(torch.arange(s, e - 1))
-                dst.append(torch.arange(L - 1) + b * (width - 1))
-        out = lp.new_zeros(n_rows * (width - 1))
-        if src:
-            si = torch.cat(src).to(lp.device)
-            di = torch.cat(dst).to(lp.device)
-            out = out.index_copy(0, di, lp.index_select(0, si))
-        return out.view(n_rows, width - 1)
+        """Packed next-token scores -> ``[n, width-1]`` where column i scores token i+1.
+
+        The scatter map is built vectorised on the host from the (host) cu_seqlens
+        and copied once; entries that score nothing (each sequence's last token,
+        the padding tail) go to a sink slot that is dropped."""
+        cu_np = cu.numpy().astype(np.int64)
+        T = int(lp.shape[0])
+        lens = np.diff(cu_np)[:n_rows]
+        seq = np.repeat(np.arange(n_rows), lens)
+        offs = np.arange(int(cu_np[n_rows])) - np.repeat(cu_np[:n_rows], lens)
+        N = n_rows * (width - 1)
+        dst = np.full(T, N, dtype=np.int64)
+        ok = offs < np.repeat(lens, lens) - 1
+        dst[: len(offs)][ok] = seq[ok] * (width - 1) + offs[ok]
+        di = torch.from_numpy(dst)
+        if lp.is_cuda:
+            di = di.pin_memory().to(lp.device, non_blocking=True)
+        out = lp.new_zeros(N + 1).index_add(0, di, lp)
+        return out[:N].view(n_rows, width - 1)
 
     def _lengths(self, data: BatchedDataDict) -> list[int]:
         key = "input_lengths" if "input_lengths" in data else "unpadded_sequence_lengths"
@@ -212,15 +229,19 @@ class PolicyWorker:
         gbs = gbs or B
         lengths = self._lengths(data)
         self.optimizer.ensure_grad_buffer()
+        if self.engine.kv_arena is not None:
+            self.engine.finish_generation()   # the arena goes back to being gradients
+            self.optimizer.zero_grad()
+        # the per-token training tensors cross PCIe once (pinned, async) and are
+        # sliced on the device; no pageable copy stalls the launch stream later
+        dev_data = {k: _to_device(v, self.device) for k, v in data.items() if isinstance(v, torch.Tensor)}
         all_metrics: list[dict] = []
         losses, grad_norms, lrs = [], [], []
         for g0 in range(0, B, gbs):
             rows = list(range(g0, min(B, g0 + gbs)))
-            tok_mask = data["token_mask"][rows, 1:].float()
-            smask = data["sample_mask"][rows].float()
-            local_toks = (tok_mask * smask.unsqueeze(-1)).sum()
-            local_seqs = smask.sum()
-            counts = torch.stack([local_toks, local_seqs]).to(self.device)
+            tok_mask = dev_data["token_mask"][g0:g0 + len(rows), 1:].float()
+            smask = dev_data["sample_mask"][g0:g0 + len(rows)].float()
+            counts = torch.stack([(tok_mask * smask.unsqueeze(-1)).sum(), smask.sum()])
             if self.ps.dp_size > 1 or self.ps.cp_size > 1:
                 dist.all_reduce(counts, group=self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group)
             gtoks, gseqs = counts[0], counts[1]
@@ -232,10 +253,10 @@ class PolicyWorker:
                 lp, ent, cu = self._forward_mb(ids, lengths, mb_rows, temperature)
                 width = max(lengths[r] for r in mb_rows)
                 curr = self._to_padded(lp, cu, len(mb_rows), width)
-                mb = data.select_indices(mb_rows)
-                mb.truncate_tensors(1, width)
-                mb = BatchedDataDict({k: (v.to(self.device) if isinstance(v, torch.Tensor) else v)
-                                      for k, v in mb.items()})
+                ridx = torch.tensor(mb_rows, dtype=torch.long).pin_memory().to(self.device, non_blocking=True) \
+                    if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
+                mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
+                                      for k, v in dev_data.items()})
                 loss, metrics = loss_fn(curr, mb, gseqs, gtoks)
                 if not eval_mode:
                     loss.backward()
@@ -298,28 +319,39 @@ _MAX_KEYS = ("_max",)
 
 def aggregate_metrics(metrics: list[dict], group=None) -> dict:
     """Combine per-micro-batch loss metrics: globally-normalised means add up,
-    ``*_min`` / ``*_max`` take min / max; then reduce the same way over DP."""
-    out: dict[str, float] = {}
+    ``*_min`` / ``*_max`` take min / max; then reduce the same way over DP.
+
+    Values may be device tensors: everything is reduced on the device and read
+    back with ONE transfer."""
+    per_key: dict[str, list] = {}
+    dev = None
     for m in metrics:
         for k, v in m.items():
-            if not isinstance(v, (int, float)):
-                continue
-            if k.endswith(_MIN_KEYS):
-                out[k] = min(out.get(k, math.inf), v)
-            elif k.endswith(_MAX_KEYS):
-                out[k] = max(out.get(k, -math.inf), v)
-            else:
-                out[k] = out.get(k, 0.0) + v
-    if group is not None and dist.is_initialized() and out:
-        keys = sorted(out)
-        dev = torch.device("cuda", torch.cuda.current_device()) if torch.cuda.is_available() else torch.device("cpu")
-        for kind, op in (("min", dist.ReduceOp.MIN), ("max", dist.ReduceOp.MAX), ("sum", dist.ReduceOp.SUM)):
-            ks = [k for k in keys if (kind == "min" and k.endswith("_min")) or (kind == "max" and k.endswith("_max"))
-                  or (kind == "sum" and not k.endswith(("_min", "_max")))]
-            if not ks:
-                continue
-            t = torch.tensor([out[k] for k in ks], dtype=torch.float64, device=dev)
+            if isinstance(v, torch.Tensor):
+                dev = dev or v.device
+                per_key.setdefault(k, []).append(v.detach().reshape(()).to(torch.float64))
+            elif isinstance(v, (int, float)):
+                per_key.setdefault(k, []).append(float(v))
+    if not per_key:
+        return {}
+    dev = dev or (torch.device("cuda", torch.cuda.current_device())
+                  if (group is not None and torch.cuda.is_available()) else torch.device("cpu"))
+    kinds = {"min": [], "max": [], "sum": []}
+    for k in sorted(per_key):
+        kinds["min" if k.endswith(_MIN_KEYS) else "max" if k.endswith(_MAX_KEYS) else "sum"].append(k)
+    out: dict[str, float] = {}
+    for kind, op in (("min", dist.ReduceOp.MIN), ("max", dist.ReduceOp.MAX), ("sum", dist.ReduceOp.SUM)):
+        ks = kinds[kind]
+        if not ks:
+            continue
+        vals = []
+        for k in ks:
+            t = torch.stack([x if isinstance(x, torch.Tensor) else torch.tensor(x, dtype=torch.float64, device=dev)
+                             for x in per_key[k]]).to(dev)
+            vals.append(t.min() if kind == "min" else t.max() if kind == "max" else t.sum())
+        t = torch.stack(vals)
+        if group is not None and dist.is_initialized():
             dist.all_reduce(t, op=op, group=group)
-            for k, v in zip(ks, t.tolist()):
-                out[k] = v
+        for k, v in zip(ks, t.tolist()):
+            out[k] = v
     return out

@@ -64,12 +64,24 @@ class ParamSpec:
 class KVCache:
     """Paged KV cache: per layer ``[num_blocks, block_size, nkv_local, hd]`` for K and V."""
 
-    def __init__(self, num_layers: int, num_blocks: int, block_size: int, nkv: int, hd: int, dtype, device):
+    def __init__(self, num_layers: int, num_blocks: int, block_size: int, nkv: int, hd: int, dtype, device,
+                 arena: Optional[torch.Tensor] = None):
         self.block_size = block_size
         self.num_blocks = num_blocks
         self.dtype = dtype
         shape = (num_layers, 2, num_blocks, block_size, nkv, hd)
-        self.storage = torch.zeros(shape, dtype=dtype, device=device)
+        # every slot is written before it is read (block 0 is a never-read sink), so
+        # the cache is not cleared: allocation is free, no 10+ GB memset per step
+        n = 1
+        for d in shape:
+            n *= d
+        elt = torch.empty((), dtype=dtype).element_size()
+        if arena is not None and arena.numel() * arena.element_size() >= n * elt:
+            # borrow the bytes of a caller-owned buffer (the trainer's fp32 gradient
+            # arena, idle while the rollout runs)
+            self.storage = arena.view(torch.uint8)[: n * elt].view(dtype).view(shape)
+        else:
+            self.storage = torch.empty(shape, dtype=dtype, device=device)
         self.k_scale = 1.0
         self.v_scale = 1.0
 
@@ -95,6 +107,36 @@ class _AuxLossScaler(torch.autograd.Function):
     def backward(ctx, g):
         (aux,) = ctx.saved_tensors
         return g, torch.full_like(aux, ctx.scale), None
+
+
+class _EmbedFn(torch.autograd.Function):
+    """Vocab-(shard-)local embedding lookup whose backward scatters straight into
+    the fp32 ``main_grad`` of the table (no dense bf16 table gradient)."""
+
+    @staticmethod
+    def forward(ctx, w, ids, vocab_start, sharded):
+        ctx.needs_mask = bool(sharded)
+        local = ids - vocab_start
+        inside = (local >= 0) & (local < w.shape[0])
+        lc = local.clamp(0, w.shape[0] - 1)
+        ctx.save_for_backward(lc, inside)
+        ctx.w = w
+        out = w[lc]
+        if ctx.needs_mask:
+            out = out * inside.unsqueeze(-1).to(w.dtype)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        lc, inside = ctx.saved_tensors
+        w = ctx.w
+        g = g * inside.unsqueeze(-1).to(g.dtype)
+        main = getattr(w, "main_grad", None)
+        if main is not None:
+            main.index_add_(0, lc, g.float())
+            return None, None, None, None
+        dw = torch.zeros(w.shape, dtype=torch.float32, device=w.device).index_add_(0, lc, g.float())
+        return dw.to(w.dtype), None, None, None
 
 
 class TransformerLM(nn.Module):
@@ -231,10 +273,8 @@ class TransformerLM(nn.Module):
     def embed(self, input_ids: torch.Tensor) -> torch.Tensor:
         w = self._params["model.embed_tokens.weight"]
         if self.ps.tp_size == 1:
-            return w[input_ids]
-        local = input_ids - self.vocab_start
-        inside = (local >= 0) & (local < self.vocab_local)
-        x = w[local.clamp(0, self.vocab_local - 1)] * inside.unsqueeze(-1).to(w.dtype)
+            return _EmbedFn.apply(w, input_ids, 0, False)
+        x = _EmbedFn.apply(w, input_ids, self.vocab_start, True)
         if self.sequence_parallel:
             return reduce_scatter_to_sp(x, self.ps.tp_group)
         return reduce_from_tp(x, self.ps.tp_group)

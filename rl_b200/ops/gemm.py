@@ -28,11 +28,27 @@ __all__ = ["mm_nt", "mm_nn", "mm_tn", "mm_tn_accumulate", "native_gemm_supported
 _NATIVE_GEMM = os.environ.get("RL_B200_NATIVE_GEMM", "1") == "1"
 
 
+_NUM_SMS = None
+
+
+def _sms() -> int:
+    global _NUM_SMS
+    if _NUM_SMS is None:
+        _NUM_SMS = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count \
+            if torch.cuda.is_available() else 148
+    return _NUM_SMS
+
+
 def native_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
-    return (
-        _NATIVE_GEMM and dtype == torch.bfloat16 and has_ext() and hasattr(ext(), "gemm_nt")
-        and K % 64 == 0 and N % 16 == 0 and M > 0
-    )
+    """The persistent tcgen05 kernel computes 128 x 256 output tiles, one CTA per
+    SM; shapes that give fewer tiles than half the SMs (decode-time GEMMs with a
+    handful of rows) leave most of the GPU idle in it, so they go to the library
+    GEMM's split-K kernels instead."""
+    if not (_NATIVE_GEMM and dtype == torch.bfloat16 and has_ext() and K % 64 == 0 and N % 16 == 0 and M > 0):
+        return False
+    bn = 256 if N >= 256 else 128
+    tiles = -(-M // 128) * -(-N // bn)
+    return tiles * 2 >= _sms()
 
 
 def mm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:

@@ -27,6 +27,16 @@ def add_rms_norm_ref(x: torch.Tensor, delta: torch.Tensor, w: torch.Tensor, eps:
     return rms_norm_ref(s, w, eps), s
 
 
+def _weight_grad(w: torch.Tensor, dw_fp32: torch.Tensor):
+    """Accumulate the fp32 weight gradient straight into ``w.main_grad`` when the
+    optimizer attached one (no bf16 ``.grad`` round trip); else return it."""
+    main = getattr(w, "main_grad", None)
+    if main is not None:
+        main.add_(dw_fp32.view_as(main))
+        return None
+    return dw_fp32.to(w.dtype)
+
+
 class _RMSNorm(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, w, eps):
@@ -41,7 +51,7 @@ class _RMSNorm(torch.autograd.Function):
     def backward(ctx, dy):
         x2, w, rstd = ctx.saved_tensors
         dx, dw = ext().rmsnorm_bwd(dy.reshape(x2.shape).contiguous(), x2, w, rstd)
-        return dx.view(ctx.shape), dw.to(w.dtype), None
+        return dx.view(ctx.shape), _weight_grad(w, dw), None
 
 
 class _AddRMSNorm(torch.autograd.Function):
@@ -65,7 +75,7 @@ class _AddRMSNorm(torch.autograd.Function):
         ds2 = None if ds is None else ds.reshape(s.shape).contiguous()
         dx, dw = ext().rmsnorm_bwd_add(dy2, s, w, rstd, ds2)
         dx = dx.view(ctx.shape)
-        return dx, dx, dw.to(w.dtype), None
+        return dx, dx, _weight_grad(w, dw), None
 
 
 def rms_norm(x: torch.Tensor, w: torch.Tensor, eps: float = 1e-5) -> torch.Tensor:

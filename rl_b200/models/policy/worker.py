@@ -100,7 +100,8 @@ class PolicyWorker:
         self.optimizer = FlatAdamW(self.model, lr=lr, betas=tuple(float(b) for b in betas), eps=eps, weight_decay=wd,
                                    max_grad_norm=policy_cfg.get("max_grad_norm", 1.0), scheduler_cfg=sched,
                                    min_lr=float(mopt.get("min_lr", 0.0)), dp_group=grad_group,
-                                   tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel)
+                                   tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel,
+                                   edp_group=self.ps.edp_group, ep_group=self.ps.ep_group)
         gen_cfg = dict(policy_cfg.get("generation", {}) or {})
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
@@ -129,10 +130,29 @@ class PolicyWorker:
 
     # ------------------------------------------------------------- helpers
     def _plan(self, lengths: list[int], rows: list[int], budget: int) -> list[list[int]]:
-        budget = max(budget, max(lengths[r] for r in rows))
-        packer = get_packer(self.packing_algorithm, bin_capacity=budget)
-        bins = packer.pack([max(1, lengths[r]) for r in rows])
-        return [[rows[i] for i in b] for b in bins]
+        """Sequence-packing plan (list of row lists).  Under expert parallelism the
+        ranks of an EP group exchange tokens inside every forward / backward, so
+        they must run the SAME number of micro-batches: the plan is padded to the
+        group maximum - first by splitting multi-row bins, then with dummy bins
+        (negative row ids: the first row again, run with zero loss weight)."""
+        bins: list[list[int]] = []
+        if rows:
+            budget = max(budget, max(lengths[r] for r in rows))
+            packer = get_packer(self.packing_algorithm, bin_capacity=budget)
+            bins = [[rows[i] for i in b] for b in packer.pack([max(1, lengths[r]) for r in rows])]
+        if self.ps.ep_size > 1 and self.model_cfg.is_moe:
+            n = torch.tensor([len(bins)], dtype=torch.int64,
+                             device=self.device if self.ps.backend == "nccl" else torch.device("cpu"))
+            dist.all_reduce(n, op=dist.ReduceOp.MAX, group=self.ps.ep_group)
+            target = int(n.item())
+            while len(bins) < target and any(len(b) > 1 for b in bins):
+                b = max((b for b in bins if len(b) > 1), key=lambda bb: sum(lengths[r] for r in bb))
+                bins.remove(b)
+                bins += [b[: len(b) // 2], b[len(b) // 2:]]
+            filler = rows[0] if rows else 0
+            while len(bins) < target:
+                bins.append([-1 - filler])
+        return bins
 
     def _forward_mb(self, input_ids: torch.Tensor, lengths: list[int], rows: list[int], temperature: float):
         """Packed forward of ``rows``; returns per-token next-token (logprob, entropy)
@@ -189,7 +209,11 @@ class PolicyWorker:
         rows_all = [r for r in range(B) if lengths[r] > 0]
         self.model.eval()
         for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
+            dummy = rows[0] < 0
+            rows = [-1 - rows[0]] if dummy else rows
             lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
+            if dummy:
+                continue  # padding pass that only keeps the EP group's collectives paired
             padded = self._to_padded(lp.float(), cu, len(rows), S).cpu()
             out[torch.tensor(rows), 1:] = padded
         self.model.train()
@@ -250,6 +274,9 @@ class PolicyWorker:
             step_loss = torch.zeros((), device=self.device)
             mb_metrics: list[dict] = []
             for mb_rows in mb_plan:
+                dummy = mb_rows[0] < 0
+                if dummy:
+                    mb_rows = [-1 - mb_rows[0]]
                 lp, ent, cu = self._forward_mb(ids, lengths, mb_rows, temperature)
                 width = max(lengths[r] for r in mb_rows)
                 curr = self._to_padded(lp, cu, len(mb_rows), width)
@@ -258,6 +285,10 @@ class PolicyWorker:
                 mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
                                       for k, v in dev_data.items()})
                 loss, metrics = loss_fn(curr, mb, gseqs, gtoks)
+                if dummy:
+                    # zero-weight pass: keeps the EP group's all-to-alls paired, adds nothing
+                    loss = loss * 0.0
+                    metrics = {}
                 if not eval_mode:
                     loss.backward()
                     self.optimizer._fold_param_grads()

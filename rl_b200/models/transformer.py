@@ -203,13 +203,22 @@ class TransformerLM(nn.Module):
         s.append(ParamSpec("model.norm.weight", (H,), "ones", no_weight_decay=True))
         if not c.tie_word_embeddings:
             s.append(ParamSpec("lm_head.weight", (self.vocab_local, H), "normal", tp_dim=0))
+        # Flat layout: every dense (non-expert) parameter first, then every expert
+        # parameter, so that the two gradient-reduction domains (data parallel vs
+        # expert data parallel) are two contiguous segments of one buffer.
+        s = [sp for sp in s if sp.ep_dim is None] + [sp for sp in s if sp.ep_dim is not None]
         off = 0
         align = 64  # keep every parameter 128-byte aligned (bf16) for vector / TMA access
+        self.expert_offset = None
         for sp in s:
+            if sp.ep_dim is not None and self.expert_offset is None:
+                self.expert_offset = off
             sp.numel = int(math.prod(sp.shape))
             sp.offset = off
             off += (sp.numel + align - 1) // align * align
         self.flat_numel = off
+        if self.expert_offset is None:
+            self.expert_offset = off
         return s
 
     def _allocate(self, seed: int, std: float) -> None:

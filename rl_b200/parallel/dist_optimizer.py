@@ -6,16 +6,17 @@ and ``data_parallel_sharding_strategy: optim_grads_params``
 
 * gradients accumulate (fp32) in one flat ``main_grad`` buffer whose views are
   attached to the parameters (``rl_b200.ops.linear`` adds into them);
-* ``step()``: reduce-scatter the flat gradient over the DP(xCP) group so every
-  rank owns ``1/dp`` of it, compute the global grad norm (squares summed over
-  the shard, then over DP and TP groups), run the fused AdamW kernel over the
-  shard (which also writes the bf16 parameters) and all-gather the bf16
-  parameter shards back into the flat buffer;
-* master weights / Adam moments exist only for the local shard
-  (``12 bytes x params / dp`` per rank); no other shard-sized state is kept
+* the flat buffer has up to two contiguous SEGMENTS - dense parameters, reduced
+  over the data-parallel (x context-parallel) group, and MoE expert parameters,
+  reduced over the expert-data-parallel group (ranks that hold the same experts);
+* ``step()``: per segment, reduce-scatter the gradient so each rank owns
+  ``1/group`` of it, compute the global grad norm (shard squares summed over the
+  reduction group, TP-replicated parts counted once, expert parts summed over the
+  EP group), run the fused AdamW kernel over the shard (which also writes the
+  bf16 parameters) and all-gather the bf16 shards back into the flat buffer;
+* master weights / Adam moments exist only for the local shards
+  (``12 bytes x params / group`` per rank); no other shard-sized state is kept
   (weight-decay and TP-replication classes are contiguous ranges).
-* ``release_grad_buffer()`` frees the fp32 gradient buffer between training
-  phases (the colocated rollout needs that HBM for its KV cache).
 
 The reduce-scatter / all-gather here use NCCL; ``rl_b200.parallel.fused``
 provides the peer-memory kernels that fuse them with the cast/scale/Adam work.
@@ -90,10 +91,30 @@ def _merge(ranges: list[tuple[int, int, bool]]) -> list[tuple[int, int, bool]]:
     return out
 
 
+def _ws(group) -> int:
+    return dist.get_world_size(group) if (group is not None and dist.is_initialized()) else 1
+
+
+class _Segment:
+    """A contiguous range of the flat buffer with one gradient-reduction group."""
+
+    def __init__(self, lo: int, hi: int, group, norm_sum_group, expert: bool):
+        self.lo, self.hi = lo, hi            # global offsets in the flat buffer (padded)
+        self.group = group
+        self.n = _ws(group)
+        self.rank = dist.get_rank(group) if self.n > 1 else 0
+        self.norm_sum_group = norm_sum_group  # extra group the shard norm^2 is summed over
+        self.expert = expert
+        size = hi - lo
+        self.shard = size // self.n
+        self.s_lo = lo + self.rank * self.shard  # this rank's shard (global offsets)
+        self.s_hi = self.s_lo + self.shard
+
+
 class FlatAdamW:
     def __init__(self, model, lr: float = 1e-5, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  max_grad_norm: Optional[float] = 1.0, scheduler_cfg=None, min_lr: float = 0.0,
-                 dp_group=None, tp_group=None, sequence_parallel: bool = False):
+                 dp_group=None, tp_group=None, sequence_parallel: bool = False, edp_group=None, ep_group=None):
         self.model = model
         self.lr = lr
         self.beta1, self.beta2 = betas
@@ -104,58 +125,73 @@ class FlatAdamW:
         self.dp_group = dp_group
         self.tp_group = tp_group
         self.sequence_parallel = sequence_parallel
-        self.dp = dist.get_world_size(dp_group) if (dp_group is not None and dist.is_initialized()) else 1
-        self.dp_rank = dist.get_rank(dp_group) if self.dp > 1 else 0
-        self.tp = dist.get_world_size(tp_group) if (tp_group is not None and dist.is_initialized()) else 1
-        flat = model.flat_param
-        n = flat.numel()
-        unit = 128 * self.dp  # shards are 128-element aligned
-        self.padded = (n + unit - 1) // unit * unit
-        if self.padded != n:
-            big = torch.zeros(self.padded, dtype=flat.dtype, device=flat.device)
-            big[:n].copy_(flat.detach())
-            self._rehome(big)
-            del flat
-        self.shard = self.padded // self.dp
-        lo = self.dp_rank * self.shard
-        self.lo, self.hi = lo, lo + self.shard
+        self.tp = _ws(tp_group)
+        self.dp = _ws(dp_group)
+        dense_n = int(getattr(model, "expert_offset", model.flat_numel))
+        expert_n = int(model.flat_numel) - dense_n
+        u_d = 128 * max(1, _ws(dp_group))
+        dense_pad = (dense_n + u_d - 1) // u_d * u_d
+        segs = [_Segment(0, dense_pad, dp_group, None, False)]
+        total = dense_pad
+        if expert_n > 0:
+            g = edp_group if edp_group is not None else dp_group
+            u_e = 128 * max(1, _ws(g))
+            exp_pad = (expert_n + u_e - 1) // u_e * u_e
+            segs.append(_Segment(dense_pad, dense_pad + exp_pad, g, ep_group, True))
+            total = dense_pad + exp_pad
+        self.segments = segs
+        self.padded = total
+        self._relayout(dense_pad - dense_n)
         dev = model.flat_param.device
         self.device = dev
-        self.master = torch.empty(self.shard, dtype=torch.float32, device=dev)
-        self.master.copy_(model.flat_param[lo:lo + self.shard])
-        self.exp_avg = torch.zeros(self.shard, dtype=torch.float32, device=dev)
-        self.exp_avg_sq = torch.zeros(self.shard, dtype=torch.float32, device=dev)
-        # contiguous shard-local ranges: (start, end, weight-decayed) and (start, end, TP-replicated)
-        wd_r, rep_r = [], []
-        covered = 0
-        for sp, p in model.named_flat_params():
-            a, b = max(sp.offset, lo), min(sp.offset + sp.numel, lo + self.shard)
-            if a < b:
-                wd_r.append((a - lo, b - lo, not sp.no_weight_decay))
-                rep_r.append((a - lo, b - lo, sp.tp_dim is None and sp.ep_dim is None))
-        self.wd_ranges = _merge(wd_r)
-        self.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
+        for seg in self.segments:
+            seg.master = torch.empty(seg.shard, dtype=torch.float32, device=dev)
+            seg.master.copy_(model.flat_param[seg.s_lo:seg.s_hi])
+            seg.exp_avg = torch.zeros(seg.shard, dtype=torch.float32, device=dev)
+            seg.exp_avg_sq = torch.zeros(seg.shard, dtype=torch.float32, device=dev)
+            wd_r, rep_r = [], []
+            for sp, p in model.named_flat_params():
+                a, b = max(sp.offset, seg.s_lo), min(sp.offset + sp.numel, seg.s_hi)
+                if a < b:
+                    wd_r.append((a - seg.s_lo, b - seg.s_lo, not sp.no_weight_decay))
+                    rep_r.append((a - seg.s_lo, b - seg.s_lo, sp.tp_dim is None and sp.ep_dim is None))
+            seg.wd_ranges = _merge(wd_r)
+            seg.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
         self.main_grad: Optional[torch.Tensor] = None
-        self.grad_shard: Optional[torch.Tensor] = None
         self.ensure_grad_buffer()
         self.step_count = 0
         self.last_grad_norm = 0.0
 
-    # -------------------------------------------------------------- buffers
-    def _rehome(self, big: torch.Tensor) -> None:
+    # ------------------------------------------------------- flat re-layout
+    def _relayout(self, expert_shift: int) -> None:
+        """Move the flat buffer into a ``self.padded`` allocation, shifting expert
+        parameters behind the padded dense segment; parameters are rebound."""
         m = self.model
+        old = m.flat_param
+        if self.padded == old.numel() and expert_shift == 0:
+            return
+        big = torch.zeros(self.padded, dtype=old.dtype, device=old.device)
+        for sp, p in m.named_flat_params():
+            new_off = sp.offset + (expert_shift if sp.ep_dim is not None else 0)
+            big[new_off:new_off + sp.numel].copy_(old[sp.offset:sp.offset + sp.numel])
+            sp.offset = new_off
         m.flat_param = big
         for sp, p in m.named_flat_params():
             p.data = big[sp.offset: sp.offset + sp.numel].view(sp.shape)
+        if hasattr(m, "expert_offset"):
+            m.expert_offset = self.segments[-1].lo if self.segments[-1].expert else self.padded
+        del old
 
+    # -------------------------------------------------------------- buffers
     def ensure_grad_buffer(self) -> None:
         if self.main_grad is not None:
             return
         self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
-        if self.dp == 1:
-            self.grad_shard = self.main_grad[self.lo:self.hi]
-        else:
-            self.grad_shard = torch.zeros(self.shard, dtype=torch.float32, device=self.device)
+        for seg in self.segments:
+            if seg.n == 1:
+                seg.grad_shard = self.main_grad[seg.s_lo:seg.s_hi]
+            else:
+                seg.grad_shard = torch.zeros(seg.shard, dtype=torch.float32, device=self.device)
         for sp, p in self.model.named_flat_params():
             p.main_grad = self.main_grad[sp.offset: sp.offset + sp.numel].view(sp.shape)
 
@@ -165,7 +201,8 @@ class FlatAdamW:
             p.main_grad = None
             p.grad = None
         self.main_grad = None
-        self.grad_shard = None
+        for seg in self.segments:
+            seg.grad_shard = None
 
     def zero_grad(self) -> None:
         if self.main_grad is not None:
@@ -174,8 +211,8 @@ class FlatAdamW:
             p.grad = None
 
     def _fold_param_grads(self) -> None:
-        """Parameters whose gradient autograd produced in ``.grad`` (embedding
-        lookups, norms, routers) are folded into the flat fp32 buffer."""
+        """Parameters whose gradient autograd produced in ``.grad`` (routers,
+        parameters outside the fused ops) are folded into the flat fp32 buffer."""
         for _, p in self.model.named_flat_params():
             if p.grad is not None:
                 p.main_grad.add_(p.grad.float())
@@ -192,25 +229,29 @@ class FlatAdamW:
             for sp, p in m.named_flat_params():
                 if sp.tp_dim is None and sp.ep_dim is None:
                     dist.all_reduce(p.main_grad, group=self.tp_group)
-        if self.dp > 1:
-            # losses are normalised by GLOBAL token / sequence counts, so the
-            # per-rank gradients are partial sums: reduce with SUM, not mean.
-            dist.reduce_scatter_tensor(self.grad_shard, self.main_grad, group=self.dp_group)
-        g = self.grad_shard
-        # global grad norm: TP-sharded parts summed over TP; replicated parts counted once
-        sq_all = sum_of_squares(g)
-        if self.tp > 1:
-            sq_rep = torch.zeros((), dtype=torch.float32, device=g.device)
-            for a, b in self.rep_ranges:
-                sq_rep = sq_rep + sum_of_squares(g[a:b])
-            sq_shard = sq_all - sq_rep
-            dist.all_reduce(sq_shard, group=self.tp_group)
-            sq = sq_shard + sq_rep
-        else:
-            sq = sq_all
-        if self.dp > 1:
-            dist.all_reduce(sq, group=self.dp_group)
-        norm = float(sq.sqrt())
+        sq_total = torch.zeros((), dtype=torch.float32, device=self.device)
+        for seg in self.segments:
+            if seg.n > 1:
+                # losses are normalised by GLOBAL token / sequence counts, so the
+                # per-rank gradients are partial sums: reduce with SUM, not mean.
+                dist.reduce_scatter_tensor(seg.grad_shard, self.main_grad[seg.lo:seg.hi], group=seg.group)
+            g = seg.grad_shard
+            sq_all = sum_of_squares(g)
+            if self.tp > 1:
+                sq_rep = torch.zeros((), dtype=torch.float32, device=g.device)
+                for a, b in seg.rep_ranges:
+                    sq_rep = sq_rep + sum_of_squares(g[a:b])
+                sq_sh = sq_all - sq_rep
+                dist.all_reduce(sq_sh, group=self.tp_group)
+                sq = sq_sh + sq_rep
+            else:
+                sq = sq_all
+            if seg.n > 1:
+                dist.all_reduce(sq, group=seg.group)
+            if seg.norm_sum_group is not None and _ws(seg.norm_sum_group) > 1:
+                dist.all_reduce(sq, group=seg.norm_sum_group)
+            sq_total = sq_total + sq
+        norm = float(sq_total.sqrt())
         self.last_grad_norm = norm
         scale = 1.0
         if self.max_grad_norm and self.max_grad_norm > 0 and norm > self.max_grad_norm:
@@ -220,13 +261,15 @@ class FlatAdamW:
             return {"grad_norm": norm, "lr": self.current_lr(), "skipped": 1.0}
         self.step_count += 1
         lr = self.scheduler.lr_at(self.step_count - 1)
-        out = m.flat_param[self.lo:self.hi]
-        for a, b, decayed in self.wd_ranges:
-            adamw_step(self.master[a:b], g[a:b], self.exp_avg[a:b], self.exp_avg_sq[a:b], lr, self.beta1,
-                       self.beta2, self.eps, self.weight_decay if decayed else 0.0, self.step_count,
-                       grad_scale=scale, param_out=out[a:b])
-        if self.dp > 1:
-            dist.all_gather_into_tensor(m.flat_param, out.clone(), group=self.dp_group)
+        for seg in self.segments:
+            out = m.flat_param[seg.s_lo:seg.s_hi]
+            g = seg.grad_shard
+            for a, b, decayed in seg.wd_ranges:
+                adamw_step(seg.master[a:b], g[a:b], seg.exp_avg[a:b], seg.exp_avg_sq[a:b], lr, self.beta1,
+                           self.beta2, self.eps, self.weight_decay if decayed else 0.0, self.step_count,
+                           grad_scale=scale, param_out=out[a:b])
+            if seg.n > 1:
+                dist.all_gather_into_tensor(m.flat_param[seg.lo:seg.hi], out.clone(), group=seg.group)
         self.zero_grad()
         return {"grad_norm": norm, "lr": lr}
 
@@ -235,34 +278,42 @@ class FlatAdamW:
 
     @torch.no_grad()
     def restore_params_from_master(self) -> None:
-        """Rewrite the bf16 parameters from the fp32 master copy (after a weight swap)."""
+        """Rewrite the bf16 parameters from the fp32 master shards (after a weight swap)."""
         m = self.model
-        m.flat_param[self.lo:self.hi].copy_(self.master)
-        if self.dp > 1:
-            dist.all_gather_into_tensor(m.flat_param, m.flat_param[self.lo:self.hi].clone(), group=self.dp_group)
+        for seg in self.segments:
+            m.flat_param[seg.s_lo:seg.s_hi].copy_(seg.master)
+            if seg.n > 1:
+                dist.all_gather_into_tensor(m.flat_param[seg.lo:seg.hi], m.flat_param[seg.s_lo:seg.s_hi].clone(),
+                                            group=seg.group)
 
     # ---------------------------------------------------------- state dict
     def state_dict(self) -> dict:
-        return {"master": self.master.cpu(), "exp_avg": self.exp_avg.cpu(), "exp_avg_sq": self.exp_avg_sq.cpu(),
-                "step": self.step_count, "lo": self.lo, "hi": self.hi, "padded": self.padded}
+        return {"segments": [{"master": s.master.cpu(), "exp_avg": s.exp_avg.cpu(), "exp_avg_sq": s.exp_avg_sq.cpu(),
+                              "s_lo": s.s_lo, "s_hi": s.s_hi} for s in self.segments],
+                "step": self.step_count, "padded": self.padded}
 
     def load_state_dict(self, sd: dict) -> None:
-        if sd["lo"] != self.lo or sd["hi"] != self.hi:
-            raise ValueError("optimizer shard layout mismatch (different DP size?)")
-        self.master.copy_(sd["master"])
-        self.exp_avg.copy_(sd["exp_avg"])
-        self.exp_avg_sq.copy_(sd["exp_avg_sq"])
+        segs = sd["segments"]
+        if len(segs) != len(self.segments) or any(a["s_lo"] != b.s_lo or a["s_hi"] != b.s_hi
+                                                   for a, b in zip(segs, self.segments)):
+            raise ValueError("optimizer shard layout mismatch (different parallel layout?)")
+        for a, b in zip(segs, self.segments):
+            b.master.copy_(a["master"])
+            b.exp_avg.copy_(a["exp_avg"])
+            b.exp_avg_sq.copy_(a["exp_avg_sq"])
         self.step_count = int(sd["step"])
         self.restore_params_from_master()
 
     def offload(self) -> None:
-        for name in ("master", "exp_avg", "exp_avg_sq"):
-            t = getattr(self, name)
-            if t.is_cuda:
-                setattr(self, name, t.cpu())
+        for seg in self.segments:
+            for name in ("master", "exp_avg", "exp_avg_sq"):
+                t = getattr(seg, name)
+                if t.is_cuda:
+                    setattr(seg, name, t.cpu())
 
     def onload(self, device) -> None:
-        for name in ("master", "exp_avg", "exp_avg_sq"):
-            t = getattr(self, name)
-            if not t.is_cuda:
-                setattr(self, name, t.to(device))
+        for seg in self.segments:
+            for name in ("master", "exp_avg", "exp_avg_sq"):
+                t = getattr(seg, name)
+                if not t.is_cuda:
+                    setattr(seg, name, t.to(device))

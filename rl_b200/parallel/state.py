@@ -46,6 +46,8 @@ class ParallelState:
     dp_group: Optional[object] = None
     dp_cp_group: Optional[object] = None
     mp_group: Optional[object] = None  # TP x CP x PP (all ranks of one model replica)
+    edp_group: Optional[object] = None  # expert-data-parallel: ranks holding the same experts
+    edp_ranks: list = field(default_factory=lambda: [0])
     tp_ranks: list = field(default_factory=lambda: [0])
     dp_ranks: list = field(default_factory=lambda: [0])
     ep_ranks: list = field(default_factory=lambda: [0])
@@ -155,5 +157,15 @@ def init_distributed(tp: int = 1, cp: int = 1, ep: int = 1, pp: int = 1, backend
                 ep_groups.append(members[i:i + ep])
     make(ep_groups, "ep_group", "ep_ranks")
     st.ep_rank = st.ep_ranks.index(rank) if rank in st.ep_ranks else 0
+    # Expert-data-parallel groups: ranks holding the SAME experts (same position in
+    # their EP group) within a pipeline stage / TP rank; expert gradients are
+    # reduced over these only.
+    edp_groups = []
+    for p in range(pp):
+        for t in range(tp):
+            blocks = [g for g in ep_groups if coords[g[0]][3] == p and coords[g[0]][0] == t]
+            for e in range(ep):
+                edp_groups.append([blk[e] for blk in blocks if e < len(blk)])
+    make(edp_groups, "edp_group", "edp_ranks")
     set_parallel_state(st)
     return st

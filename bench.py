@@ -253,9 +253,27 @@ def main():
             "gen_kl_error": timed[-1].get("gen_kl_error") if timed else None,
         }
         print(json.dumps(line), flush=True)
+    shutdown(worker)
+
+
+def shutdown(worker) -> None:
+    """Tear down in an order that cannot hang: CUDA graphs that captured NCCL
+    collectives are released before the process group, and a watchdog ends the
+    process if teardown still stalls (the result line is already printed)."""
+    import gc
+    import threading
+
+    import torch
+    import torch.distributed as dist
+
+    threading.Timer(90.0, lambda: os._exit(0)).start()
+    worker.shutdown()
+    gc.collect()
+    torch.cuda.synchronize()
     if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
+    os._exit(0)
 
 
 def iter_epochs(dl):

@@ -1,0 +1,92 @@
+#!/usr/bin/env python
+"""GRPO entry point (reference: ``examples/run_grpo.py:66``).
+
+    python examples/run_grpo.py --config examples/configs/grpo_tiny_cpu.yaml [key=value ...]
+    torchrun --nproc-per-node 8 --master-addr 127.0.0.1 examples/run_grpo.py --config ...
+
+Loads the YAML (``defaults`` inheritance, ``${...}`` interpolation, Hydra-style
+overrides), initialises the process groups from the torchrun environment
+(TP / CP / EP sizes from ``policy.megatron_cfg``), builds the policy worker,
+the sharded prompt loader and the environments, and runs ``grpo_train`` with
+checkpointing and logging.  Resumes from the latest checkpoint when present.
+"""
+
+from __future__ import annotations
+
+import argparse
+import os
+import sys
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+
+
+def build_envs(env_cfg: dict) -> dict:
+    from rl_b200.environments.math_environment import MathEnvironment
+    from rl_b200.environments.synthetic import EvenTokenEnvironment, HashRewardEnvironment
+
+    envs = {}
+    for task, c in (env_cfg or {}).items():
+        kind = (c or {}).get("kind", task)
+        if kind in ("hash", "synthetic"):
+            envs[task] = HashRewardEnvironment(c)
+        elif kind == "even":
+            envs[task] = EvenTokenEnvironment(c)
+        elif kind == "math":
+            envs[task] = MathEnvironment(c)
+        else:
+            from rl_b200.environments.registry import make_environment
+
+            envs[task] = make_environment(kind, c)
+    return envs
+
+
+def main(argv=None) -> dict:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--config", default=os.path.join(ROOT, "examples", "configs", "grpo_tiny_cpu.yaml"))
+    args, overrides = ap.parse_known_args(argv)
+    from rl_b200.algorithms.grpo import GRPOSaveState, grpo_train
+    from rl_b200.data.datasets import StatefulDataLoader, SyntheticPromptDataset
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import init_distributed
+    from rl_b200.utils.checkpoint import CheckpointManager
+    from rl_b200.utils.config import load_config
+    from rl_b200.utils.logger import Logger
+
+    cfg = load_config(args.config, overrides)
+    mc = cfg["policy"].get("megatron_cfg", {}) or {}
+    ps = init_distributed(tp=int(mc.get("tensor_model_parallel_size", 1)), cp=int(mc.get("context_parallel_size", 1)),
+                          ep=int(mc.get("expert_model_parallel_size", 1)),
+                          pp=int(mc.get("pipeline_model_parallel_size", 1)))
+    mcfg = get_model_config(cfg["policy"]["model_name"])
+    policy = PolicyWorker(cfg["policy"], model_cfg=mcfg, pstate=ps, seed=int(cfg["grpo"].get("seed", 0)))
+    d = cfg.get("data", {})
+    task = next(iter(cfg.get("env", {"synthetic": {}})))
+    ds = SyntheticPromptDataset(int(d.get("num_prompts", 1024)), int(d.get("min_prompt_len", 16)),
+                                int(d.get("max_prompt_len", 64)), mcfg.vocab_size, seed=int(cfg["grpo"].get("seed", 0)),
+                                task_name=task)
+    dl = StatefulDataLoader(ds, int(cfg["grpo"]["num_prompts_per_step"]), shuffle=bool(d.get("shuffle", True)),
+                            seed=int(cfg["grpo"].get("seed", 0)), shard_rank=ps.dp_rank, num_shards=ps.dp_size)
+    envs = build_envs(cfg.get("env", {}))
+    ck = CheckpointManager(cfg.get("checkpointing", {})) if cfg.get("checkpointing", {}).get("enabled") else None
+    state = GRPOSaveState.default()
+    if ck is not None and ck.get_latest_checkpoint_path():
+        paths = ck.get_resume_paths()
+        info = ck.load_training_info(paths["root"])
+        policy.load_checkpoint(paths["policy_weights"], paths["policy_optimizer"])
+        if os.path.exists(paths["dataloader"]):
+            import torch
+
+            dl.load_state_dict(torch.load(paths["dataloader"]))
+        state.update({k: info[k] for k in state if k in info})
+    logger = Logger(cfg.get("logger", {}))
+    logger.log_hyperparams(cfg)
+    state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
+    logger.close()
+    policy.shutdown()
+    return state
+
+
+if __name__ == "__main__":
+    main()

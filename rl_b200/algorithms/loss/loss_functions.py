@@ -365,6 +365,10 @@ class PreferenceLossFn:
     loss_type = LossType.SEQUENCE_LEVEL
 
     def __call__(self, rewards: torch.Tensor, data, global_valid_seqs, global_valid_toks, **kwargs):
+        if rewards.dim() == 2:
+            # per-token values: the sequence reward is the value at its last token
+            last = (data["input_lengths"].to(rewards.device).long() - 1).clamp_min(0)
+            rewards = rewards.gather(1, last.unsqueeze(1)).squeeze(1)
         chosen, rejected = rewards[0::2], rewards[1::2]
         pair_mask = data["sample_mask"][0::2].to(rewards.dtype)
         n_pairs = global_valid_seqs / 2

@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import contextlib
 import math
+import os
 import time
 from typing import Any, Optional
 
@@ -86,8 +87,10 @@ class PolicyWorker:
         mc = policy_cfg.get("megatron_cfg", {}) or {}
         self.sequence_parallel = bool(mc.get("sequence_parallel", False)) and self.ps.tp_size > 1
         act_ckpt = bool(mc.get("activation_checkpointing", policy_cfg.get("activation_checkpointing", False)))
+        self.num_labels = int(policy_cfg.get("num_labels", 0) or 0)  # > 0: value / reward model
         self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
-                                   sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt)
+                                   sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt,
+                                   num_labels=self.num_labels)
         opt = policy_cfg.get("optimizer", {}) or {}
         kw = dict(opt.get("kwargs", {}) or {})
         mopt = mc.get("optimizer", {}) or {}
@@ -136,7 +139,16 @@ class PolicyWorker:
         group maximum - first by splitting multi-row bins, then with dummy bins
         (negative row ids: the first row again, run with zero loss weight)."""
         bins: list[list[int]] = []
-        if rows:
+        if rows and getattr(self, "_pair_rows", False):
+            # preference data: rows (2i, 2i+1) are a (chosen, rejected) pair and must
+            # share a micro-batch, in order; pack pairs as units
+            pairs = [(r, r + 1) for r in rows if r % 2 == 0 and r + 1 in set(rows)]
+            plen = [lengths[a] + lengths[b] for a, b in pairs]
+            budget = max(budget, max(plen))
+            packer = get_packer(self.packing_algorithm, bin_capacity=budget)
+            for b in packer.pack([max(1, L) for L in plen]):
+                bins.append([x for i in sorted(b) for x in pairs[i]])
+        elif rows:
             budget = max(budget, max(lengths[r] for r in rows))
             packer = get_packer(self.packing_algorithm, bin_capacity=budget)
             bins = [[rows[i] for i in b] for b in packer.pack([max(1, lengths[r]) for r in rows])]
@@ -170,6 +182,65 @@ class PolicyWorker:
                                   self.ps.tp_group if self.ps.tp_size > 1 else None, self.logprob_chunk)
         return lp, ent, cu
 
+    def _loss_input(self, loss_fn, ids, lengths, rows, width, temperature):
+        """What the loss consumes for one packed micro-batch:
+        LOGPROB -> next-token logprobs ``[n, width-1]``;
+        VALUE   -> per-token values ``[n, width]`` (value of token i at index i);
+        LOGIT   -> full next-token logits ``[n, width-1, V]`` (distillation)."""
+        kind = getattr(getattr(loss_fn, "input_type", None), "value", "logprob")
+        if kind == "logprob":
+            lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
+            return self._to_padded(lp, cu, len(rows), width)
+        tp = self.ps.tp_size if self.sequence_parallel else 1
+        flat, pos, cu, max_len, _ = pack_rows(ids, lengths, rows, pad_to_multiple=tp)
+        dev = self.device
+        hidden = self.model(_to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev), max_len)
+        if kind == "value":
+            v = self.model.values(hidden)
+            return self._to_padded_full(v, cu, len(rows), width)
+        logits = self.model.logits(hidden).float() / temperature
+        if self.ps.tp_size > 1:
+            from rl_b200.parallel.comm import gather_from_sp
+
+            logits = gather_from_sp(logits.t().contiguous(), self.ps.tp_group).t()
+        V = logits.shape[-1]
+        out = self._to_padded(logits, cu, len(rows), width)  # [n, width-1, V]
+        return out.view(len(rows), width - 1, V)
+
+    @staticmethod
+    def _to_padded_full(v: torch.Tensor, cu: torch.Tensor, n_rows: int, width: int) -> torch.Tensor:
+        """Packed per-token values -> ``[n, width]`` aligned with the input tokens."""
+        cu_np = cu.numpy().astype(np.int64)
+        lens = np.diff(cu_np)[:n_rows]
+        seq = np.repeat(np.arange(n_rows), lens)
+        offs = np.arange(int(cu_np[n_rows])) - np.repeat(cu_np[:n_rows], lens)
+        N = n_rows * width
+        dst = np.full(int(v.shape[0]), N, dtype=np.int64)
+        dst[: len(offs)] = seq * width + offs
+        di = torch.from_numpy(dst)
+        if v.is_cuda:
+            di = di.pin_memory().to(v.device, non_blocking=True)
+        out = v.new_zeros(N + 1).index_add(0, di, v)
+        return out[:N].view(n_rows, width)
+
+    @torch.no_grad()
+    def get_values(self, data: BatchedDataDict) -> BatchedDataDict:
+        """Value-head outputs ``[B, S]`` (value model / critic)."""
+        ids = data["input_ids"]
+        B, S = ids.shape
+        lengths = self._lengths(data)
+        out = torch.zeros(B, S, dtype=torch.float32)
+        rows_all = [r for r in range(B) if lengths[r] > 0]
+        self.model.eval()
+        for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
+            if rows[0] < 0:
+                continue
+            width = max(lengths[r] for r in rows)
+            v = self._loss_input(_VALUE_INPUT, ids, lengths, rows, width, 1.0).float().cpu()
+            out[torch.tensor(rows), :width] = v
+        self.model.train()
+        return BatchedDataDict({"values": out})
+
     @staticmethod
     def _to_padded(lp: torch.Tensor, cu: torch.Tensor, n_rows: int, width: int) -> torch.Tensor:
         """Packed next-token scores -> ``[n, width-1]`` where column i scores token i+1.
@@ -189,8 +260,9 @@ class PolicyWorker:
         di = torch.from_numpy(dst)
         if lp.is_cuda:
             di = di.pin_memory().to(lp.device, non_blocking=True)
-        out = lp.new_zeros(N + 1).index_add(0, di, lp)
-        return out[:N].view(n_rows, width - 1)
+        rest = tuple(lp.shape[1:])
+        out = lp.new_zeros((N + 1,) + rest).index_add(0, di, lp)
+        return out[:N].view(n_rows, width - 1, *rest)
 
     def _lengths(self, data: BatchedDataDict) -> list[int]:
         key = "input_lengths" if "input_lengths" in data else "unpadded_sequence_lengths"
@@ -242,10 +314,18 @@ class PolicyWorker:
 
     # ------------------------------------------------------------- train
     def train(self, data: BatchedDataDict, loss_fn, gbs: Optional[int] = None, eval_mode: bool = False,
-              temperature: Optional[float] = None) -> dict:
+              temperature: Optional[float] = None, pair_rows: bool = False) -> dict:
         """One or more optimizer steps over ``data`` (this rank's shard).
 
-        ``gbs`` is the LOCAL number of rows per optimizer step (global batch / dp)."""
+        ``gbs`` is the LOCAL number of rows per optimizer step (global batch / dp).
+        ``pair_rows`` keeps rows (2i, 2i+1) in one micro-batch (preference losses)."""
+        self._pair_rows = pair_rows
+        try:
+            return self._train(data, loss_fn, gbs, eval_mode, temperature)
+        finally:
+            self._pair_rows = False
+
+    def _train(self, data: BatchedDataDict, loss_fn, gbs, eval_mode, temperature) -> dict:
         temperature = float(temperature if temperature is not None else
                             (self.cfg.get("generation", {}) or {}).get("temperature", 1.0) or 1.0)
         ids = data["input_ids"]
@@ -277,9 +357,8 @@ class PolicyWorker:
                 dummy = mb_rows[0] < 0
                 if dummy:
                     mb_rows = [-1 - mb_rows[0]]
-                lp, ent, cu = self._forward_mb(ids, lengths, mb_rows, temperature)
                 width = max(lengths[r] for r in mb_rows)
-                curr = self._to_padded(lp, cu, len(mb_rows), width)
+                curr = self._loss_input(loss_fn, ids, lengths, mb_rows, width, temperature)
                 ridx = torch.tensor(mb_rows, dtype=torch.long).pin_memory().to(self.device, non_blocking=True) \
                     if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
                 mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
@@ -337,12 +416,59 @@ class PolicyWorker:
         self.engine.invalidate_kv_cache()
         return time.perf_counter() - t0
 
+    # ------------------------------------------------------- checkpoints
+    def save_checkpoint(self, weights_path: str, optimizer_path: Optional[str] = None,
+                        fmt: str = "safetensors") -> None:
+        """``safetensors``: consolidated HF checkpoint (+ per-rank optimizer shards);
+        ``torch_dist``: per-rank shard files with layout metadata."""
+        from rl_b200.models import checkpoint_io as cio
+
+        if fmt == "torch_dist":
+            cio.save_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
+            return
+        cio.save_hf_checkpoint(self.model, weights_path)
+        if optimizer_path is not None:
+            os.makedirs(optimizer_path, exist_ok=True)
+            rank = dist.get_rank() if dist.is_initialized() else 0
+            torch.save(self.optimizer.state_dict(), os.path.join(optimizer_path, f"__{rank}.pt"))
+
+    def load_checkpoint(self, weights_path: str, optimizer_path: Optional[str] = None) -> None:
+        from rl_b200.models import checkpoint_io as cio
+
+        if os.path.isdir(os.path.join(weights_path, "iter_0000000")):
+            cio.load_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
+            return
+        cio.load_hf_checkpoint(self.model, weights_path)
+        rank = dist.get_rank() if dist.is_initialized() else 0
+        opt_file = os.path.join(optimizer_path, f"__{rank}.pt") if optimizer_path else None
+        if opt_file and os.path.exists(opt_file):
+            self.optimizer.load_state_dict(torch.load(opt_file, map_location="cpu"))
+        else:
+            with torch.no_grad():
+                for seg in self.optimizer.segments:
+                    seg.master.copy_(self.model.flat_param[seg.s_lo:seg.s_hi])
+
+    def shutdown(self) -> None:
+        """Release the rollout engine's captured graphs (they may hold NCCL
+        collectives, which must be gone before the process group is destroyed)."""
+        self.engine.finish_generation()
+        self.engine._drop_graphs()
+        self.engine._kv_sig = None
+
     def offload_before_refit(self) -> None:
         pass
 
     def offload_after_refit(self) -> None:
         pass
 
+
+class _ValueInput:
+    from rl_b200.algorithms.loss.interfaces import LossInputType as _LIT
+
+    input_type = _LIT.VALUE
+
+
+_VALUE_INPUT = _ValueInput()
 
 _MIN_KEYS = ("_min",)
 _MAX_KEYS = ("_max",)

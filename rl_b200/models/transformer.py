@@ -142,8 +142,9 @@ class _EmbedFn(torch.autograd.Function):
 class TransformerLM(nn.Module):
     def __init__(self, cfg: ModelConfig, pstate: Optional[ParallelState] = None, device=None,
                  dtype: torch.dtype = torch.bfloat16, seed: int = 0, sequence_parallel: bool = False,
-                 activation_checkpointing: bool = False, init_std: float = 0.02):
+                 activation_checkpointing: bool = False, init_std: float = 0.02, num_labels: int = 0):
         super().__init__()
+        self.num_labels = int(num_labels)  # > 0: value / reward model (scalar head instead of LM head)
         self.cfg = cfg
         self.ps = pstate or single_process_state(torch.device(device) if device else None)
         self.device = torch.device(device) if device is not None else self.ps.device
@@ -201,7 +202,10 @@ class TransformerLM(nn.Module):
                 s.append(ParamSpec(p + "mlp.gate_up_proj.weight", (2 * self.ffn_local, H), "normal", tp_dim=0))
                 s.append(ParamSpec(p + "mlp.down_proj.weight", (H, self.ffn_local), "normal_out", tp_dim=1))
         s.append(ParamSpec("model.norm.weight", (H,), "ones", no_weight_decay=True))
-        if not c.tie_word_embeddings:
+        if self.num_labels > 0:
+            # value / reward head (HF ``score`` naming of *ForSequenceClassification)
+            s.append(ParamSpec("score.weight", (self.num_labels, H), "normal"))
+        elif not c.tie_word_embeddings:
             s.append(ParamSpec("lm_head.weight", (self.vocab_local, H), "normal", tp_dim=0))
         # Flat layout: every dense (non-expert) parameter first, then every expert
         # parameter, so that the two gradient-reduction domains (data parallel vs
@@ -287,6 +291,13 @@ class TransformerLM(nn.Module):
         if self.sequence_parallel:
             return reduce_scatter_to_sp(x, self.ps.tp_group)
         return reduce_from_tp(x, self.ps.tp_group)
+
+    def values(self, hidden: torch.Tensor) -> torch.Tensor:
+        """Per-token scalar values ``[T]`` (or ``[T, num_labels]``) from the value head."""
+        if self.sequence_parallel:
+            hidden = gather_from_sp(hidden, self.ps.tp_group)
+        v = linear(hidden, self._params["score.weight"]).float()
+        return v.squeeze(-1) if self.num_labels == 1 else v
 
     def lm_head_weight(self) -> torch.Tensor:
         if self.cfg.tie_word_embeddings:

@@ -1,0 +1,369 @@
+"""CPU unit tests of the framework layer (no GPU): configs, batch containers, packing,
+losses, advantage estimators, checkpoint formats, environments and training loops."""
+
+import math
+import os
+import random
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+# ------------------------------------------------------------------ config
+def test_config_inheritance_interpolation_overrides(tmp_path):
+    from rl_b200.utils.config import load_config
+
+    cfg = load_config(os.path.join(ROOT, "examples", "configs", "grpo_tiny_cpu.yaml"),
+                      ["grpo.seed=7", "+policy.new_key=3", "~logger.monitor_gpus"])
+    assert cfg["grpo"]["seed"] == 7
+    assert cfg["policy"]["new_key"] == 3
+    assert "monitor_gpus" not in cfg["logger"]
+    # ${mul:...} resolver and ${a.b} interpolation
+    assert cfg["policy"]["sequence_packing"]["train_mb_tokens"] == 32 * 4
+    assert cfg["grpo"]["reward_shaping"]["max_response_length"] == 32
+    assert cfg["grpo"]["adv_estimator"]["normalize_rewards"] is True
+    with pytest.raises(KeyError):
+        load_config(os.path.join(ROOT, "examples", "configs", "grpo_tiny_cpu.yaml"), ["grpo.not_a_key=1"])
+    for f in os.listdir(os.path.join(ROOT, "examples", "configs")):
+        load_config(os.path.join(ROOT, "examples", "configs", f))
+
+
+# ------------------------------------------------------- BatchedDataDict
+def test_batched_data_dict_shard_and_microbatch():
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+
+    B, S = 16, 10
+    d = BatchedDataDict({"x": torch.arange(B * S).view(B, S), "lens": torch.tensor([2 + i % 8 for i in range(B)]),
+                         "tags": [f"t{i}" for i in range(B)]})
+    shards = d.shard_by_batch_size(4, batch_size=8)
+    assert [s.size for s in shards] == [4, 4, 4, 4]
+    # shard 0 holds rows 0,1 of each global batch of 8
+    assert shards[0]["tags"] == ["t0", "t1", "t8", "t9"]
+    back = BatchedDataDict.from_batches(shards)
+    assert back.size == B
+    mbs = list(d.make_microbatch_iterator(5))
+    assert [m.size for m in mbs] == [5, 5, 5, 1]
+    sh = d.shard_by_batch_size(2, batch_size=16, dynamic_batching_args={
+        "max_tokens_per_microbatch": 16, "sequence_length_round": 4, "input_lengths_key": "lens"})
+    for s in sh:
+        for mb in s.make_microbatch_iterator_with_dynamic_shapes():
+            assert mb["x"].shape[1] * mb.size <= 16 or mb.size == 1
+    sp = d.shard_by_batch_size(1, sequence_packing_args={"max_tokens_per_microbatch": 20, "input_lengths_key": "lens"})
+    rows = sorted(r for mb in sp[0].micro_batch_indices for r in mb)
+    assert rows == list(range(B))
+    rep = d.repeat_interleave(2)
+    assert rep.size == 2 * B and rep["tags"][:2] == ["t0", "t0"]
+
+
+# ---------------------------------------------------------------- packing
+@pytest.mark.parametrize("alg", ["concatenative", "first_fit", "first_fit_decreasing", "first_fit_shuffle",
+                                 "modified_first_fit_decreasing", "greedy_knapsack", "balanced_greedy_knapsack"])
+def test_packers_valid(alg):
+    from rl_b200.data.packing import get_packer
+
+    rng = random.Random(0)
+    lengths = [rng.randint(1, 100) for _ in range(200)]
+    bins = get_packer(alg, bin_capacity=128).pack(lengths)
+    seen = sorted(i for b in bins for i in b)
+    assert seen == list(range(200))
+    assert all(sum(lengths[i] for i in b) <= 128 for b in bins)
+    lb = math.ceil(sum(lengths) / 128)
+    if alg in ("modified_first_fit_decreasing", "first_fit_decreasing"):
+        assert len(bins) <= math.ceil(1.25 * lb) + 1
+
+
+# ----------------------------------------------------------------- losses
+def _pg_data(B=3, S=6, seed=0):
+    g = torch.Generator().manual_seed(seed)
+    tm = torch.ones(B, S)
+    tm[:, 0] = 0
+    tm[0, 4:] = 0
+    return {"token_mask": tm, "sample_mask": torch.ones(B), "advantages": torch.randn(B, S, generator=g),
+            "prev_logprobs": -torch.rand(B, S, generator=g), "generation_logprobs": -torch.rand(B, S, generator=g),
+            "reference_policy_logprobs": -torch.rand(B, S, generator=g)}
+
+
+def test_clipped_pg_matches_formula():
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+
+    d = _pg_data()
+    curr = (-torch.rand(3, 5)).requires_grad_(True)
+    fn = ClippedPGLossFn({"ratio_clip_min": 0.2, "ratio_clip_max": 0.28, "reference_policy_kl_penalty": 0.0})
+    gtok = d["token_mask"][:, 1:].sum()
+    loss, m = fn(curr, d, torch.tensor(3.0), gtok)
+    A = d["advantages"][:, 1:]
+    r = torch.exp(curr - d["prev_logprobs"][:, 1:])
+    per = torch.maximum(-A * r, -A * r.clamp(0.8, 1.28))
+    mask = d["token_mask"][:, 1:]
+    ref = (per * mask).sum() / (gtok + 1e-8)
+    assert torch.allclose(loss, ref, atol=1e-6)
+    loss.backward()
+    assert curr.grad is not None and torch.isfinite(curr.grad).all()
+    assert 0.8 - 1e-6 <= float(m["probs_ratio_clamped_min"]) <= float(m["probs_ratio_clamped_max"]) <= 1.28 + 1e-6
+
+
+def test_kl_estimators_and_dual_clip_and_gspo():
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.algorithms.utils import calculate_kl
+
+    a, b = torch.tensor([-1.0, -2.0]), torch.tensor([-1.5, -1.0])
+    lr = b - a
+    assert torch.allclose(calculate_kl(a, b, "k1"), -lr)
+    assert torch.allclose(calculate_kl(a, b, "k2"), lr * lr / 2)
+    assert torch.allclose(calculate_kl(a, b, "k3"), torch.exp(lr) - 1 - lr)
+    d = _pg_data(seed=1)
+    curr = -torch.rand(3, 5)
+    for cfg in ({"ratio_clip_c": 3.0}, {"sequence_level_importance_ratios": True}, {"use_cispo": True},
+                {"reference_policy_kl_penalty": 0.1, "reference_policy_kl_type": "k2"},
+                {"use_importance_sampling_correction": True, "truncated_importance_sampling_type": "tis",
+                 "truncated_importance_sampling_ratio": 2.0},
+                {"use_importance_sampling_correction": True, "truncated_importance_sampling_type": "icepop",
+                 "truncated_importance_sampling_ratio": 5.0, "truncated_importance_sampling_ratio_min": 0.5},
+                {"disable_ppo_ratio": True}, {"force_on_policy_ratio": True}, {"token_level_loss": False},
+                {"positive_example_nll_weight": 0.1}):
+        loss, m = ClippedPGLossFn(cfg)(curr.clone().requires_grad_(True), d, torch.tensor(3.0),
+                                       d["token_mask"][:, 1:].sum())
+        assert torch.isfinite(loss), cfg
+
+
+def test_dpo_nll_preference_losses():
+    from rl_b200.algorithms.loss.loss_functions import DPOLossFn, NLLLossFn, PreferenceLossFn
+
+    B, S = 4, 5
+    tm = torch.ones(B, S)
+    d = {"token_mask": tm, "sample_mask": torch.ones(B), "reference_policy_logprobs": torch.zeros(B, S),
+         "input_lengths": torch.full((B,), S)}
+    lp = torch.zeros(B, S - 1, requires_grad=True)
+    loss, m = DPOLossFn({"reference_policy_kl_penalty": 0.1})(lp, d, torch.tensor(4.0), tm[:, 1:].sum())
+    assert abs(float(loss) - math.log(2)) < 1e-5
+    loss, _ = NLLLossFn()(torch.full((B, S - 1), -2.0), d, torch.tensor(4.0), tm[:, 1:].sum())
+    assert abs(float(loss) - 2.0) < 1e-6
+    r = torch.tensor([1.0, 0.0, 2.0, 3.0])
+    loss, m = PreferenceLossFn()(r, d, torch.tensor(4.0), None)
+    ref = -(torch.nn.functional.logsigmoid(torch.tensor(1.0)) + torch.nn.functional.logsigmoid(torch.tensor(-1.0))) / 2
+    assert abs(float(loss) - float(ref)) < 1e-5
+
+
+# ------------------------------------------------------ advantages
+def _loo_reference(groups, rewards, valid):
+    """Explicit per-group leave-one-out baseline / unbiased std."""
+    B = len(rewards)
+    base, std = torch.zeros(B), torch.zeros(B)
+    for i in range(B):
+        same = [j for j in range(B) if groups[j] == groups[i] and valid[j]]
+        others = [j for j in same if j != i]
+        if len(same) <= 1:
+            base[i] = rewards[i]
+            continue
+        vals = torch.tensor([rewards[j] for j in others])
+        base[i] = vals.mean()
+        std[i] = vals.std(unbiased=True) if len(vals) > 1 else 0.0
+    return base, std
+
+
+def test_grpo_advantage_leave_one_out():
+    from rl_b200.algorithms.advantage_estimator import GRPOAdvantageEstimator
+    from rl_b200.algorithms.utils import calculate_baseline_and_std_per_prompt
+
+    g = torch.Generator().manual_seed(0)
+    groups = torch.tensor([0, 0, 0, 0, 1, 1, 1, 1, 2, 2, 2, 2])
+    rewards = torch.rand(12, generator=g)
+    rewards[8:] = 0.5  # trivial group
+    valid = torch.ones(12)
+    base, std, trivial = calculate_baseline_and_std_per_prompt(groups, rewards, valid, True)
+    rb, rs = _loo_reference(groups.tolist(), rewards.tolist(), valid.tolist())
+    assert torch.allclose(base, rb, atol=1e-6)
+    assert torch.allclose(std, rs, atol=1e-5)
+    assert trivial[8:].all() and not trivial[:8].any()
+    adv = GRPOAdvantageEstimator({}).compute_advantage(groups.view(-1, 1), rewards, torch.ones(12, 3))
+    assert adv.shape == (12, 3)
+    assert torch.allclose(adv[8:], torch.zeros(4, 3))
+    assert torch.allclose(adv[:8, 0], (rewards[:8] - rb[:8]) / (rs[:8] + 1e-6), atol=1e-5)
+
+
+def test_other_advantage_estimators():
+    from rl_b200.algorithms.advantage_estimator import (GDPOAdvantageEstimator, GeneralizedAdvantageEstimator,
+                                                        OPDAdvantageEstimator, ReinforcePlusPlusAdvantageEstimator)
+
+    groups = torch.tensor([0, 0, 1, 1])
+    mask = torch.ones(4, 3)
+    batch = {"reward/a": torch.tensor([1.0, 0.0, 1.0, 1.0]), "reward/b": torch.tensor([0.0, 1.0, 0.5, 0.0])}
+    adv = GDPOAdvantageEstimator({}).compute_advantage(groups, None, mask, repeated_batch=batch)
+    assert adv.shape == (4, 3) and torch.isfinite(adv).all()
+    adv = ReinforcePlusPlusAdvantageEstimator({}).compute_advantage(groups, torch.tensor([1.0, 0.0, 0.5, 0.2]), mask)
+    assert abs(float((adv * mask).sum())) < 1e-4
+    # GAE with lambda=1, gamma=1 and zero values: advantage = terminal reward at every valid token
+    est = GeneralizedAdvantageEstimator({"gae_lambda": 1.0, "gae_gamma": 1.0, "normalize_advantages": False})
+    adv, ret = est.compute_advantage(groups, torch.tensor([1.0, 2.0, 0.0, -1.0]), mask, values=torch.zeros(4, 3))
+    assert torch.allclose(adv[:, 0], torch.tensor([1.0, 2.0, 0.0, -1.0]))
+    opd = OPDAdvantageEstimator({})
+    a = opd.compute_advantage(None, None, mask, logprobs_policy=torch.zeros(4, 3), logprobs_teacher=-torch.ones(4, 3))
+    assert torch.allclose(a, -mask)
+
+
+# ------------------------------------------------------------ checkpoints
+def test_safetensors_roundtrip_and_hf_export(tmp_path):
+    from rl_b200.models.checkpoint_io import hf_state_dict, load_hf_checkpoint, load_safetensors, save_hf_checkpoint, \
+        save_safetensors
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.transformer import TransformerLM
+
+    t = {"a": torch.randn(3, 4), "b": torch.arange(5, dtype=torch.int64), "c": torch.randn(2, 2).to(torch.bfloat16)}
+    p = str(tmp_path / "x.safetensors")
+    save_safetensors(t, p, {"format": "pt"})
+    back = load_safetensors(p)
+    for k in t:
+        assert torch.equal(back[k], t[k])
+    try:  # files written here are readable by the reference implementation of the format
+        from safetensors.torch import load_file
+
+        lib = load_file(p)
+        assert torch.equal(lib["a"], t["a"])
+    except ImportError:
+        pass
+    cfg = get_model_config("tiny-moe")
+    m = TransformerLM(cfg, device="cpu", dtype=torch.float32, seed=1)
+    sd = hf_state_dict(m, dtype=None)
+    assert "model.layers.0.self_attn.q_proj.weight" in sd
+    assert "model.layers.1.mlp.experts.7.down_proj.weight" in sd
+    save_hf_checkpoint(m, str(tmp_path / "hf"))
+    m2 = TransformerLM(cfg, device="cpu", dtype=torch.float32, seed=2)
+    load_hf_checkpoint(m2, str(tmp_path / "hf"))
+    # bf16 round trip of the saved copy
+    assert torch.allclose(m2.flat_param, m.flat_param.to(torch.bfloat16).float())
+
+
+def test_checkpoint_manager_topk_and_resume(tmp_path):
+    from rl_b200.utils.checkpoint import CheckpointManager
+
+    ck = CheckpointManager({"checkpoint_dir": str(tmp_path), "keep_top_k": 2, "metric_name": "train:loss",
+                            "higher_is_better": False, "save_period": 1})
+    for step, loss in [(1, 3.0), (2, 1.0), (3, 2.0), (4, 5.0)]:
+        tmp = ck.init_tmp_checkpoint(step, {"current_step": step, "train": {"loss": loss}}, {"a": 1})
+        ck.finalize_checkpoint(tmp)
+    assert ck.list_steps() == [2, 3, 4]  # best two by loss (2, 3) + latest (4)
+    assert ck.get_best_checkpoint_path().endswith("step_2")
+    assert ck.load_training_info(ck.get_latest_checkpoint_path())["current_step"] == 4
+    assert not any(n.startswith("tmp_") for n in os.listdir(tmp_path))
+
+
+def test_policy_checkpoint_roundtrip_both_formats(tmp_path):
+    from rl_b200.models.policy.worker import PolicyWorker
+    from tests.dist_cases import TINY, _pcfg, make_batch
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+
+    for fmt in ("safetensors", "torch_dist"):
+        w = PolicyWorker(_pcfg(False), model_cfg=TINY, seed=3)
+        w.train(make_batch(), ClippedPGLossFn({}), gbs=8)
+        w.save_checkpoint(str(tmp_path / fmt / "w"), str(tmp_path / fmt / "o"), fmt=fmt)
+        w2 = PolicyWorker(_pcfg(False), model_cfg=TINY, seed=9)
+        w2.load_checkpoint(str(tmp_path / fmt / "w"), str(tmp_path / fmt / "o"))
+        tol = 1e-2 if fmt == "safetensors" else 0.0  # safetensors export is bf16
+        assert (w2.model.flat_param - w.model.flat_param).abs().max() <= tol + 1e-7
+        assert w2.optimizer.step_count == w.optimizer.step_count
+
+
+# ----------------------------------------------------------- environments
+def test_environments():
+    from rl_b200.environments.math_environment import MathEnvironment, answers_match, extract_answer
+    from rl_b200.environments.registry import make_environment
+    from rl_b200.environments.synthetic import EvenTokenEnvironment, hash_reward
+
+    assert extract_answer("so the answer is \\boxed{\\frac{1}{2}}") == "\\frac{1}{2}"
+    assert answers_match("1/2", "0.5") and answers_match("\\frac{1}{2}", "1/2") and not answers_match("3", "4")
+    env = MathEnvironment()
+    r = env.step([[{"role": "assistant", "content": "x = \\boxed{4}"}]], [{"ground_truth": "4"}])
+    assert float(r.rewards[0]) == 1.0
+    e = EvenTokenEnvironment().step([[{"role": "assistant", "token_ids": torch.tensor([2, 4, 5, 7])}]], [None])
+    assert float(e.rewards[0]) == 0.5
+    assert hash_reward(torch.tensor([1, 2, 3])) in (0.0, 1.0)
+    code = make_environment("code", {"timeout_s": 10})
+    ok = code.step([[{"role": "assistant", "content": "```python\ndef f(x):\n    return x + 1\n```"}]],
+                   [{"tests": "assert f(1) == 2"}])
+    assert float(ok.rewards[0]) == 1.0
+    pz = make_environment("sliding_puzzle", {})
+    res = pz.step([[{"role": "assistant", "content": "right"}]], [{"board": [[1, 2], [0, 3]]}])
+    assert float(res.rewards[0]) == 1.0 and bool(res.terminateds[0])
+
+
+# ---------------------------------------------------------- training loops
+def _tiny_policy(seed=0, **kw):
+    from rl_b200.models.policy.worker import PolicyWorker
+    from tests.dist_cases import TINY
+
+    cfg = {"max_total_sequence_length": 48, "precision": "float32", "train_global_batch_size": 8,
+           "optimizer": {"kwargs": {"lr": 1e-3, "weight_decay": 0.0}},
+           "generation": {"temperature": 1.0, "max_new_tokens": 8},
+           "sequence_packing": {"train_mb_tokens": 96, "logprob_mb_tokens": 96}}
+    cfg.update(kw)
+    return PolicyWorker(cfg, model_cfg=TINY, seed=seed)
+
+
+def test_grpo_tiny_config1_runs():
+    from examples.run_grpo import main
+
+    state = main(["--config", os.path.join(ROOT, "examples", "configs", "grpo_tiny_cpu.yaml"),
+                  "logger.log_dir=/tmp/rlb_test_logs", "logger.stdout=false"])
+    assert state["current_step"] == 2
+
+
+def test_sft_loss_decreases():
+    from rl_b200.algorithms.sft import sft_train
+    from rl_b200.data.datasets import SFTDataset, StatefulDataLoader
+
+    g = random.Random(0)
+    samples = [([g.randrange(512) for _ in range(6)], [7, 8, 9, 10, 11, 12]) for _ in range(16)]
+    dl = StatefulDataLoader(SFTDataset(samples), 8, shuffle=False)
+    w = _tiny_policy()
+    losses = []
+    sft_train(w, dl, {"sft": {"max_num_epochs": 6}, "policy": {"train_global_batch_size": 8}},
+              step_callback=lambda s, m: losses.append(m["loss"]))
+    assert len(losses) == 12 and losses[-1] < losses[0]
+
+
+def test_dpo_and_rm_loops():
+    from rl_b200.algorithms.dpo import dpo_train, rm_train
+    from rl_b200.data.datasets import PreferenceDataset, StatefulDataLoader
+
+    g = random.Random(1)
+    samples = [([g.randrange(512) for _ in range(5)], [1, 2, 3], [4, 5, 6, 7]) for _ in range(8)]
+    dl = StatefulDataLoader(PreferenceDataset(samples), 4, shuffle=False, collate_fn=lambda b: b)
+    out = []
+    dpo_train(_tiny_policy(), dl, {"dpo": {"max_num_epochs": 2, "reference_policy_kl_penalty": 0.1}},
+              step_callback=lambda s, m: out.append(m))
+    assert len(out) == 4 and all(math.isfinite(m["loss"]) for m in out)
+    rm = _tiny_policy(num_labels=1)
+    out = []
+    rm_train(rm, StatefulDataLoader(PreferenceDataset(samples), 4, shuffle=False, collate_fn=lambda b: b),
+             {"rm": {"max_num_epochs": 3}}, step_callback=lambda s, m: out.append(m))
+    assert len(out) == 6 and out[-1]["loss"] < out[0]["loss"] + 1e-6
+
+
+def test_ppo_and_distillation_loops():
+    from rl_b200.algorithms.distillation import distillation_train, kd_train
+    from rl_b200.algorithms.ppo import ppo_train
+    from rl_b200.algorithms.sft import build_sft_batch
+    from rl_b200.data.datasets import SFTDataset, StatefulDataLoader, SyntheticPromptDataset
+    from rl_b200.environments.synthetic import EvenTokenEnvironment
+
+    ds = SyntheticPromptDataset(16, 6, 10, 512, seed=0)
+    env = {"synthetic": EvenTokenEnvironment()}
+    cfg = {"ppo": {"num_generations_per_prompt": 2, "max_num_steps": 2}, "loss_fn": {},
+           "policy": {"max_total_sequence_length": 48}}
+    seen = []
+    ppo_train(_tiny_policy(), _tiny_policy(seed=5, num_labels=1), StatefulDataLoader(ds, 4, shuffle=False), env, cfg,
+              step_callback=lambda s, m: seen.append(m))
+    assert len(seen) == 2 and all(math.isfinite(m["value_loss"]) for m in seen)
+    seen = []
+    distillation_train(_tiny_policy(), _tiny_policy(seed=11), StatefulDataLoader(ds, 4, shuffle=False), env,
+                       {"distillation": {"max_num_steps": 2}, "policy": {"max_total_sequence_length": 48}},
+                       step_callback=lambda s, m: seen.append(m))
+    assert len(seen) == 2
+    samples = [([1, 2, 3], [4, 5, 6]) for _ in range(4)]
+    batches = [build_sft_batch(b) for b in StatefulDataLoader(SFTDataset(samples), 4, shuffle=False)]
+    seen = []
+    kd_train(_tiny_policy(), _tiny_policy(seed=3), batches, {"distillation": {}}, k=8,
+             step_callback=lambda s, m: seen.append(m))
+    assert len(seen) == 1 and math.isfinite(seen[0]["loss"])

@@ -42,6 +42,13 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
 // gemm_tcgen05.cu
 at::Tensor gemm_nt(at::Tensor a, at::Tensor b);
 int64_t gemm_error_flag(bool reset);
+void gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> recv_ptrs,
+             std::vector<int64_t> flag_ptrs, std::vector<int64_t> ack_ptrs, int64_t me, int64_t epoch);
+// symm.cu
+std::tuple<int64_t, at::Tensor> symm_alloc(int64_t bytes);
+int64_t symm_open(at::Tensor handle);
+void symm_close(int64_t ptr);
+at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rl_b200 sm_100a kernels";
@@ -67,4 +74,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("paged_decode_attn", &paged_decode_attn);
   m.def("gemm_nt", &gemm_nt);
   m.def("gemm_error_flag", &gemm_error_flag, py::arg("reset") = false);
+  m.def("gemm_rs", &gemm_rs);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("symm_open", &symm_open);
+  m.def("symm_close", &symm_close);
+  m.def("symm_view", &symm_view);
 }

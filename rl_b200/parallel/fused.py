@@ -1,0 +1,64 @@
+"""Fused compute + collective ops over NVLink peer memory.
+
+``GemmReduceScatter``: ``out_r = (sum_ranks A_rank @ W_rank^T)[rows of rank r]`` -
+the row-parallel linear of tensor parallelism with sequence parallelism - as ONE
+tcgen05 kernel per rank (``csrc/gemm_tcgen05.cu``, epilogue ``EPI=1``): tiles
+destined to a peer are stored straight into the peer's receive buffer over
+NVLink as they finish (so the transfer overlaps the remaining MMA work), own
+tiles wait for the peers' partials and reduce them in the epilogue.  The NCCL
+baseline it replaces is ``GEMM`` then ``reduce_scatter_tensor``.
+
+The op keeps symmetric receive / flag / ack buffers sized for ``max_rows`` rows
+and an epoch counter that advances identically on every rank (all ranks of the
+group must call it in the same order).
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from rl_b200.ops._ext import ext
+from rl_b200.parallel.symm import SymmetricBuffer
+
+__all__ = ["GemmReduceScatter"]
+
+
+class GemmReduceScatter:
+    BM = 128
+
+    def __init__(self, group, max_rows: int, n_cols: int):
+        self.group = group
+        self.n = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        self.N = int(n_cols)
+        unit = self.BM * self.n
+        self.max_rows = (int(max_rows) + unit - 1) // unit * unit
+        ms = self.max_rows // self.n
+        bn = 256 if self.N >= 256 else 128
+        self.tiles_per_shard = (ms // self.BM) * ((self.N + bn - 1) // bn)
+        self.recv = SymmetricBuffer(2 * self.n * ms * self.N * 2, group)
+        self.flags = SymmetricBuffer(2 * self.n * self.tiles_per_shard * 4, group)
+        self.acks = SymmetricBuffer((2 * self.n + 2) * 4, group)  # per-parity ack words + launch counters
+        self.epoch = 0
+        self._shape_ms = None
+
+    def __call__(self, a: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        M = a.shape[0]
+        if M % (self.BM * self.n) or M > self.max_rows:
+            raise ValueError(f"rows {M} must be a multiple of {self.BM * self.n} and <= {self.max_rows}")
+        ms = M // self.n
+        if self._shape_ms is not None and self._shape_ms != ms:
+            # the per-tile flag indexing depends on the shard height: keep epochs
+            # monotone (flags / acks compare against the epoch, never reset)
+            pass
+        self._shape_ms = ms
+        out = torch.empty(ms, self.N, dtype=a.dtype, device=a.device)
+        self.epoch += 1
+        ext().gemm_rs(a.contiguous(), w.contiguous(), out, self.recv.ptrs, self.flags.ptrs, self.acks.ptrs, self.me,
+                      self.epoch)
+        return out
+
+    def close(self) -> None:
+        for b in (self.recv, self.flags, self.acks):
+            b.close()

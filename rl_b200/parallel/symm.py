@@ -1,0 +1,51 @@
+"""Symmetric device buffers across the ranks of a process group (one node).
+
+Each rank allocates the same number of bytes (raw cudaMalloc in the native
+library), the CUDA IPC handles are exchanged over the group, and every rank
+opens every peer's handle.  ``ptrs[r]`` is then a device address through which
+this rank's kernels load / store rank r's buffer over NVLink (``ptrs[me]`` is
+the local allocation).  This is the substrate of the fused compute+collective
+kernels in ``rl_b200.parallel.fused``.
+"""
+
+from __future__ import annotations
+
+import torch
+import torch.distributed as dist
+
+from rl_b200.ops._ext import ext
+
+__all__ = ["SymmetricBuffer"]
+
+
+class SymmetricBuffer:
+    def __init__(self, nbytes: int, group=None):
+        self.nbytes = int(nbytes)
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        ptr, handle = ext().symm_alloc(self.nbytes)
+        self.local_ptr = int(ptr)
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=group)
+        else:
+            handles = [bytes(handle.numpy().tobytes())]
+        self.ptrs: list[int] = []
+        for r, h in enumerate(handles):
+            if r == self.rank:
+                self.ptrs.append(self.local_ptr)
+            else:
+                self.ptrs.append(int(ext().symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8))))
+        self.device = torch.cuda.current_device()
+
+    def local_view(self, dtype: torch.dtype, numel: int, offset_bytes: int = 0) -> torch.Tensor:
+        code = {torch.bfloat16: 15, torch.float32: 6, torch.int32: 3, torch.uint8: 0}[dtype]
+        return ext().symm_view(self.local_ptr + offset_bytes, numel, code, self.device)
+
+    def close(self) -> None:
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                ext().symm_close(p)
+        ext().symm_close(self.local_ptr)
+        self.ptrs = []

@@ -1,0 +1,96 @@
+"""Kernel micro-benchmarks (CUDA-event timing, warm-up first) for the native kernels.
+
+    python -m rl_b200.bench_kernels gemm      [M N K]
+    python -m rl_b200.bench_kernels decode    [B L]
+    python -m rl_b200.bench_kernels attn      [T_per_seq n_seq]
+    python -m rl_b200.bench_kernels logprob   [T V]
+
+Each prints one line with the time and the achieved rate, and is small enough
+to be captured under ``ncu -k <kernel> -c 1`` (a few GB on the device at most).
+"""
+
+from __future__ import annotations
+
+import sys
+
+import torch
+
+
+def _time(fn, reps: int = 10, warm: int = 3) -> float:
+    for _ in range(warm):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps  # ms
+
+
+def bench_gemm(M=8192, N=8192, K=4096):
+    from rl_b200.ops._ext import ext
+
+    dev = torch.device("cuda")
+    a = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    b = torch.randn(N, K, device=dev).to(torch.bfloat16)
+    t = _time(lambda: ext().gemm_nt(a, b))
+    tl = _time(lambda: torch.matmul(a, b.t()))
+    fl = 2 * M * N * K
+    print(f"gemm_nt {M}x{N}x{K}: {t:.3f} ms {fl / t / 1e9:.1f} TFLOP/s | library {tl:.3f} ms {fl / tl / 1e9:.1f} TFLOP/s")
+
+
+def bench_decode(B=64, L=1024, nkv=8, G=4, hd=128, bs=256):
+    from rl_b200.ops.attention import paged_decode_attention
+
+    dev = torch.device("cuda")
+    per = L // bs + 1
+    kc = torch.randn(B * per + 1, bs, nkv, hd, device=dev).to(torch.bfloat16)
+    vc = torch.randn_like(kc)
+    bt = (torch.arange(B * per).view(B, per) + 1).to(torch.int32).to(dev)
+    sl = torch.full((B,), L, dtype=torch.int32, device=dev)
+    q = torch.randn(B, nkv * G, hd, device=dev).to(torch.bfloat16)
+    t = _time(lambda: paged_decode_attention(q, kc, vc, bt, sl, max_seq_len=per * bs), reps=20)
+    byts = B * L * nkv * hd * 2 * 2
+    print(f"paged_decode B={B} L={L}: {t * 1e3:.1f} us {byts / (t * 1e-3) / 1e12:.2f} TB/s")
+
+
+def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):
+    from rl_b200.ops.attention import flash_attn_varlen
+
+    dev = torch.device("cuda")
+    T = L * n
+    q = torch.randn(T, nq, hd, device=dev).to(torch.bfloat16).requires_grad_(True)
+    k = torch.randn(T, nkv, hd, device=dev).to(torch.bfloat16).requires_grad_(True)
+    v = torch.randn(T, nkv, hd, device=dev).to(torch.bfloat16).requires_grad_(True)
+    cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
+    tf = _time(lambda: flash_attn_varlen(q, k, v, cu, L))
+    o = flash_attn_varlen(q, k, v, cu, L)
+    g = torch.randn_like(o)
+    tb = _time(lambda: torch.autograd.grad(o, (q, k, v), g, retain_graph=True))
+    fl = 4 * n * L * L / 2 * hd * nq
+    print(f"flash_attn L={L} n={n}: fwd {tf:.3f} ms {fl / tf / 1e9:.1f} TFLOP/s | bwd {tb:.3f} ms "
+          f"{2.5 * fl / tb / 1e9:.1f} TFLOP/s")
+
+
+def bench_logprob(T=8192, V=128256):
+    from rl_b200.ops.logprob import token_logprobs_and_entropy
+
+    dev = torch.device("cuda")
+    x = torch.randn(T, V, device=dev).to(torch.bfloat16)
+    tg = torch.randint(0, V, (T,), device=dev)
+    t = _time(lambda: token_logprobs_and_entropy(x, tg))
+    print(f"logprob T={T} V={V}: {t:.3f} ms {T * V * 2 / (t * 1e-3) / 1e12:.2f} TB/s")
+
+
+def main(argv=None):
+    argv = list(sys.argv[1:] if argv is None else argv)
+    what = argv.pop(0) if argv else "gemm"
+    args = [int(x) for x in argv]
+    torch.manual_seed(0)
+    {"gemm": bench_gemm, "decode": bench_decode, "attn": bench_attn, "logprob": bench_logprob}[what](*args)
+
+
+if __name__ == "__main__":
+    main()

@@ -52,6 +52,8 @@ def parse():
     p.add_argument("--max-prompt", type=int, default=512)
     p.add_argument("--max-new", type=int, default=1024)
     p.add_argument("--tp", type=int, default=0, help="0 = 2 when gpus >= 2 else 1")
+    p.add_argument("--sp", type=int, default=-1,
+                   help="sequence parallelism (fused GEMM + reduce-scatter kernels) under TP; -1 = on when tp > 1")
     p.add_argument("--mb-tokens", type=int, default=16384)
     p.add_argument("--kl", type=float, default=0.01)
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for scoring)")
@@ -173,7 +175,7 @@ def main():
         "logprob_chunk_size": 4096, "max_grad_norm": 1.0,
         "optimizer": {"name": "torch.optim.AdamW",
                       "kwargs": {"lr": 3e-7, "weight_decay": 0.01, "betas": [0.9, 0.999], "eps": 1e-8}},
-        "megatron_cfg": {"activation_checkpointing": True, "sequence_parallel": False},
+        "megatron_cfg": {"activation_checkpointing": True, "sequence_parallel": (tp > 1) if args.sp < 0 else bool(args.sp)},
         "generation": {"temperature": 1.0, "top_p": 1.0, "top_k": None, "max_new_tokens": args.max_new,
                        "max_num_seqs": 512, "mcore_generation_config": {"block_size_tokens": 256}},
         "sequence_packing": {"train_mb_tokens": args.mb_tokens, "logprob_mb_tokens": args.mb_tokens * 2},

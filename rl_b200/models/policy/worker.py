@@ -166,11 +166,21 @@ class PolicyWorker:
                 bins.append([-1 - filler])
         return bins
 
+    def _pack_multiple(self) -> int:
+        """Packed-token count multiple: the TP size under sequence parallelism, and
+        128 x TP when the fused GEMM + reduce-scatter kernel takes the row-parallel
+        projections (whole 128-row tiles per rank)."""
+        if not self.sequence_parallel:
+            return 1
+        tp = self.ps.tp_size
+        if self.device.type == "cuda" and getattr(self.model, "fused_collectives", False):
+            return 128 * tp
+        return tp
+
     def _forward_mb(self, input_ids: torch.Tensor, lengths: list[int], rows: list[int], temperature: float):
         """Packed forward of ``rows``; returns per-token next-token (logprob, entropy)
         ``[T]`` aligned so that entry j scores token j+1, plus the packing metadata."""
-        tp = self.ps.tp_size if self.sequence_parallel else 1
-        flat, pos, cu, max_len, T_real = pack_rows(input_ids, lengths, rows, pad_to_multiple=tp)
+        flat, pos, cu, max_len, T_real = pack_rows(input_ids, lengths, rows, pad_to_multiple=self._pack_multiple())
         dev = self.device
         flat_d, pos_d, cu_d = _to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev)
         targets = torch.empty_like(flat_d)
@@ -191,8 +201,7 @@ class PolicyWorker:
         if kind == "logprob":
             lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
             return self._to_padded(lp, cu, len(rows), width)
-        tp = self.ps.tp_size if self.sequence_parallel else 1
-        flat, pos, cu, max_len, _ = pack_rows(ids, lengths, rows, pad_to_multiple=tp)
+        flat, pos, cu, max_len, _ = pack_rows(ids, lengths, rows, pad_to_multiple=self._pack_multiple())
         dev = self.device
         hidden = self.model(_to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev), max_len)
         if kind == "value":
@@ -454,6 +463,9 @@ class PolicyWorker:
         self.engine.finish_generation()
         self.engine._drop_graphs()
         self.engine._kv_sig = None
+        if getattr(self.model, "_fused_rs", None) is not None:
+            self.model._fused_rs.close()
+            self.model._fused_rs = None
 
     def offload_before_refit(self) -> None:
         pass

@@ -176,6 +176,9 @@ class TransformerLM(nn.Module):
                                            cfg.rope_theta, cfg.rope_scaling, device=self.device)
         self._aux_losses: list[torch.Tensor] = []
         self.aux_loss_scale = 0.0
+        # fused compute+collective kernels for TP + SP (GEMM -> reduce-scatter over NVLink)
+        self.fused_collectives = True
+        self._fused_rs = None
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
         self.router_record: Optional[dict] = None
 
@@ -332,8 +335,7 @@ class TransformerLM(nn.Module):
         qkv = self._qkv(i, h, positions)
         q, k, v = self._split_heads(qkv)
         o = flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=True)
-        out = linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"])
-        return self._row_parallel_out(out)
+        return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"])
 
     def _row_parallel_out(self, out: torch.Tensor) -> torch.Tensor:
         if self.ps.tp_size == 1:
@@ -341,6 +343,22 @@ class TransformerLM(nn.Module):
         if self.sequence_parallel:
             return reduce_scatter_to_sp(out, self.ps.tp_group)
         return reduce_from_tp(out, self.ps.tp_group)
+
+    def _row_parallel_linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        """Row-parallel projection.  With TP + SP on CUDA the GEMM and its
+        reduce-scatter run as ONE fused tcgen05 kernel writing peer tiles over
+        NVLink (``rl_b200.parallel.fused``); otherwise GEMM then the collective."""
+        tp = self.ps.tp_size
+        if (tp > 1 and self.sequence_parallel and self.fused_collectives and x.is_cuda
+                and x.dtype == torch.bfloat16 and x.shape[0] % (128 * tp) == 0 and w.shape[0] % 32 == 0):
+            from rl_b200.parallel.fused import GemmReduceScatter, row_parallel_rs
+
+            if self._fused_rs is None or self._fused_rs.max_rows < x.shape[0] or self._fused_rs.N != w.shape[0]:
+                if self._fused_rs is not None:
+                    self._fused_rs.close()
+                self._fused_rs = GemmReduceScatter(self.ps.tp_group, max(x.shape[0], 16384), w.shape[0])
+            return row_parallel_rs(x, w, self._fused_rs)
+        return self._row_parallel_out(linear(x, w))
 
     # -------------------------------------------------------------------- MLP
     def _mlp_block(self, i: int, h: torch.Tensor) -> torch.Tensor:
@@ -353,8 +371,7 @@ class TransformerLM(nn.Module):
             h = copy_to_tp(h, self.ps.tp_group)
         gu = linear(h, self._params[p + "mlp.gate_up_proj.weight"])
         a = swiglu(gu)
-        out = linear(a, self._params[p + "mlp.down_proj.weight"])
-        return self._row_parallel_out(out)
+        return self._row_parallel_linear(a, self._params[p + "mlp.down_proj.weight"])
 
     def route(self, i: int, h: torch.Tensor):
         """Router: fp32 logits -> softmax -> top-k (+ renormalisation); returns

@@ -21,7 +21,40 @@ import torch.distributed as dist
 from rl_b200.ops._ext import ext
 from rl_b200.parallel.symm import SymmetricBuffer
 
-__all__ = ["GemmReduceScatter"]
+__all__ = ["GemmReduceScatter", "row_parallel_rs"]
+
+
+class _RowParallelRS(torch.autograd.Function):
+    """y_shard = RS(x @ w^T) fused forward; backward gathers dy over TP and runs
+    the input / weight gradient GEMMs (weight gradient straight into main_grad)."""
+
+    @staticmethod
+    def forward(ctx, x, w, op):
+        ctx.save_for_backward(x, w)
+        ctx.op = op
+        return op(x, w)
+
+    @staticmethod
+    def backward(ctx, dy):
+        from rl_b200.ops import gemm as _gemm
+
+        x, w = ctx.saved_tensors
+        op = ctx.op
+        full = torch.empty((dy.shape[0] * op.n, dy.shape[1]), dtype=dy.dtype, device=dy.device)
+        dist.all_gather_into_tensor(full, dy.contiguous(), group=op.group)
+        dx = _gemm.mm_nn(full, w) if ctx.needs_input_grad[0] else None
+        dw = None
+        if ctx.needs_input_grad[1]:
+            main = getattr(w, "main_grad", None)
+            if main is not None:
+                _gemm.mm_tn_accumulate(full, x, main)
+            else:
+                dw = _gemm.mm_tn(full, x).to(w.dtype)
+        return dx, dw, None
+
+
+def row_parallel_rs(x: torch.Tensor, w: torch.Tensor, op: "GemmReduceScatter") -> torch.Tensor:
+    return _RowParallelRS.apply(x, w, op)
 
 
 class GemmReduceScatter:

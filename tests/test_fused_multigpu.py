@@ -80,3 +80,61 @@ def test_gemm_reduce_scatter_2gpu():
         assert max(o["errs"]) < 2e-2, o["errs"]
     print("gemm_rs timing (max over ranks):", outs[0]["shape"], f"fused {outs[0]['t_fused_ms']:.3f} ms",
           f"cuBLAS+NCCL {outs[0]['t_nccl_ms']:.3f} ms")
+
+
+def case_tp_sp_model(rank: int, T: int):
+    """TP=2 + SP transformer: the fused GEMM + reduce-scatter row-parallel path
+    against GEMM then NCCL reduce-scatter (forward output and weight gradients)."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(tp=2, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="tp-sp", vocab_size=1024, hidden_size=512, num_layers=2, num_heads=8, num_kv_heads=4,
+                      head_dim=64, ffn_hidden_size=1024, rope_theta=10000.0, max_position_embeddings=1024)
+    g = torch.Generator().manual_seed(7)
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=g).cuda()
+    lens = [T // 2 - 64, T // 2 + 64]
+    pos = torch.cat([torch.arange(n) for n in lens]).cuda()
+    cu = torch.tensor([0, lens[0], T], dtype=torch.int32).cuda()
+    proj = torch.randn(T // 2, cfg.hidden_size, generator=g).cuda()
+    res = {}
+    for fused in (False, True):
+        m = TransformerLM(cfg, ps, seed=5, sequence_parallel=True)
+        m.fused_collectives = fused
+        h = m(ids, pos, cu, max(lens))
+        (h.float() * proj).sum().backward()
+        torch.cuda.synchronize()
+        grads = {n: p.grad.float().clone() for n, p in m._params.items() if p.grad is not None}
+        res[fused] = (h.float().clone(), grads, m._fused_rs is not None)
+        if m._fused_rs is not None:
+            m._fused_rs.close()
+    h0, g0, _ = res[False]
+    h1, g1, used = res[True]
+    errs = {"hidden": ((h1 - h0).norm() / h0.norm()).item()}
+    for n in g0:
+        if n in g1:
+            errs[n] = ((g1[n] - g0[n]).norm() / (g0[n].norm() + 1e-12)).item()
+    flag = _ext.ext().gemm_error_flag(True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"errs": errs, "used": used, "flag": flag, "missing": sorted(set(g0) - set(g1))}
+
+
+def test_tp_sp_model_fused_rs_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_tp_sp_model, 2, 1024, timeout_s=300)
+    for o in outs:
+        assert o["used"], "fused GEMM+RS path was not taken"
+        assert o["flag"] == 0
+        assert not o["missing"], o["missing"]
+        worst = max(o["errs"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 3e-2, worst

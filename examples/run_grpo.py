@@ -82,7 +82,12 @@ def main(argv=None) -> dict:
         state.update({k: info[k] for k in state if k in info})
     logger = Logger(cfg.get("logger", {}))
     logger.log_hyperparams(cfg)
-    state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
+    if (cfg["grpo"].get("async_grpo") or {}).get("enabled", False):
+        from rl_b200.algorithms.async_grpo import async_grpo_train
+
+        state = async_grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
+    else:
+        state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
     logger.close()
     policy.shutdown()
     return state

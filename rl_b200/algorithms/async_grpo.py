@@ -1,0 +1,153 @@
+"""Asynchronous GRPO training loop.
+
+Reference: ``async_grpo_train`` (``nemo_rl/algorithms/grpo.py:5257``) with the
+replay buffer / trajectory collector of ``nemo_rl/algorithms/async_utils``.
+Config keys (``grpo.async_grpo``): ``enabled``, ``max_trajectory_age_steps``,
+``in_flight_weight_updates``, ``max_generation_failures``; the loss should
+enable ``use_importance_sampling_correction`` because trajectories may come
+from weights up to ``max_trajectory_age_steps`` updates old.
+
+One rank = one trainer + one rollout pump thread (``AsyncTrajectoryCollector``).
+The trainer takes, at weight version ``v``, the groups generated for step
+``v``; it computes advantages, the current policy's logprobs (``prev_logprobs``,
+so the clipped ratio is against the current weights, with the rollout
+logprobs kept for the importance-sampling correction), trains one step through
+the split train API and bumps the version the pump generates with.
+
+Rollout generation in the pump thread issues no collectives: tensor-parallel
+generation (collectives on the TP group from two threads) is not supported in
+async mode, so the policy must be TP=1 for generation.
+"""
+
+from __future__ import annotations
+
+import time
+from typing import Optional
+
+import torch
+
+from rl_b200.algorithms.advantage_estimator import make_advantage_estimator
+from rl_b200.algorithms.async_utils import AsyncTrajectoryCollector, ReplayBuffer, groups_to_batch, wait_for_groups
+from rl_b200.algorithms.grpo import DEFAULT_GRPO_CONFIG, GRPOSaveState, _dp_sum, build_train_data, validate
+from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+from rl_b200.algorithms.utils import set_seed
+from rl_b200.experience.rollouts import run_multi_turn_rollout
+from rl_b200.utils.timer import Timer, max_over_ranks
+
+__all__ = ["async_grpo_train"]
+
+
+def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_fn=None, logger=None,
+                     checkpointer=None, save_state: Optional[GRPOSaveState] = None, val_dataloader=None,
+                     val_task_to_env: Optional[dict] = None, tokenizer=None, max_steps: Optional[int] = None,
+                     step_callback=None, replay_buffer: Optional[ReplayBuffer] = None,
+                     wait_timeout_s: float = 3600.0) -> GRPOSaveState:
+    ps = policy.ps
+    if ps.tp_size > 1:
+        raise NotImplementedError("async GRPO generates in a side thread and needs TP=1 generation")
+    cfg = {**DEFAULT_GRPO_CONFIG, **master_config.get("grpo", {})}
+    acfg = {**DEFAULT_GRPO_CONFIG["async_grpo"], **(cfg.get("async_grpo") or {})}
+    max_age = int(acfg.get("max_trajectory_age_steps", 1))
+    loss_cfg = master_config.get("loss_fn", {})
+    loss_fn = loss_fn or ClippedPGLossFn(loss_cfg)
+    adv_cfg = dict(cfg.get("adv_estimator", {}) or {})
+    adv_cfg.setdefault("normalize_rewards", cfg["normalize_rewards"])
+    adv_cfg.setdefault("use_leave_one_out_baseline", cfg["use_leave_one_out_baseline"])
+    estimator = make_advantage_estimator(adv_cfg, loss_cfg)
+    G = int(cfg["num_generations_per_prompt"])
+    n_groups = max(1, int(cfg["num_prompts_per_step"]) // max(1, ps.dp_size))
+    max_seq = int(master_config["policy"]["max_total_sequence_length"])
+    kl_on = float(loss_cfg.get("reference_policy_kl_penalty", 0.0) or 0.0) != 0.0
+    state = save_state or GRPOSaveState.default()
+    step = int(state["current_step"])
+    max_steps = max_steps if max_steps is not None else int(cfg["max_num_steps"])
+    set_seed(int(cfg["seed"]) + ps.dp_rank)
+    buffer = replay_buffer or ReplayBuffer(max_size=n_groups * (max_age + 1) * 2)
+    engine = getattr(policy, "engine", None)
+    if engine is not None:
+        engine.capture_error_mode = "thread_local"
+        # the KV cache may not borrow the gradient arena: training runs meanwhile
+        engine.kv_arena = None
+
+    def rollout_fn(batch, target):
+        rep = batch.repeat_interleave(G)
+        n_prompts = len(batch["message_log"])
+        base = target * 1_000_000 + ps.dp_rank * n_prompts
+        rep["group_id"] = torch.arange(base, base + n_prompts).repeat_interleave(G)
+        policy.prepare_for_generation(len(rep["message_log"]))
+        return run_multi_turn_rollout(policy, rep, tokenizer, task_to_env, max_seq, int(cfg["max_rollout_turns"]))
+
+    collector = AsyncTrajectoryCollector(rollout_fn, dataloader, buffer, n_groups, G, max_age,
+                                         initial_weight_version=step,
+                                         in_flight_weight_updates=bool(acfg.get("in_flight_weight_updates", False)),
+                                         max_generation_failures=int(acfg.get("max_generation_failures", 0)))
+    collector.start()
+    timer = Timer()
+    try:
+        while step < max_steps:
+            timer.reset()
+            t_step = time.perf_counter()
+            with timer.time("total_step_time"):
+                with timer.time("exposed_generation"):
+                    try:
+                        sample = wait_for_groups(buffer, collector, n_groups, step, max_age, wait_timeout_s)
+                    except StopIteration:
+                        break
+                rollout = groups_to_batch(sample["trajectories"])
+                with timer.time("data_processing"):
+                    train_data, adv_stats = build_train_data(rollout, estimator, cfg, loss_cfg, rollout["group_id"])
+                with timer.time("policy_and_reference_logprobs"):
+                    policy.prepare_for_lp_inference()
+                    train_data["prev_logprobs"] = policy.get_logprobs(train_data)["logprobs"]
+                    if kl_on:
+                        train_data["reference_policy_logprobs"] = \
+                            policy.get_reference_policy_logprobs(train_data)["reference_logprobs"]
+                with timer.time("policy_training"):
+                    policy.prepare_for_training()
+                    st = policy.begin_train_step(train_data, loss_fn)
+                    for i in range(st.num_microbatches):
+                        policy.train_microbatch(st, i)
+                    # the update and the refit exclude rollouts that must not see a
+                    # half-written model (in-flight updates only exclude the write)
+                    with collector.weights_lock:
+                        train_results = policy.finish_train_step(st)
+                        with timer.time("weight_sync"):
+                            policy.refit()
+                step += 1
+                collector.set_weight_version(step)
+            step_time = time.perf_counter() - t_step
+            tok = float(train_data["input_lengths"].sum())
+            tok_all = _dp_sum(tok, ps) if ps.dp_size > 1 else tok
+            step_time_max = max_over_ranks(step_time)
+            metrics = dict(train_results)
+            metrics.update(adv_stats)
+            metrics.update(collector.efficiency_metrics())
+            metrics.update({"avg_trajectory_age": sample["avg_trajectory_age"], "buffer_size": buffer.size(),
+                            "total_tokens": tok_all, "tokens_per_sec": tok_all / step_time_max,
+                            "tokens_per_sec_per_gpu": tok_all / step_time_max / max(1, ps.world_size),
+                            "step_time_s": step_time_max})
+            timing = timer.get_timing_metrics()
+            state["current_step"] = step
+            state["total_steps"] = int(state.get("total_steps", 0)) + 1
+            state["consumed_samples"] = int(state.get("consumed_samples", 0)) + n_groups * ps.dp_size
+            if logger:
+                logger.log_metrics(metrics, step, prefix="train")
+                logger.log_metrics(timing, step, prefix="timing/train")
+            if step_callback is not None:
+                step_callback(step, {**metrics, **{"timing/" + k: v for k, v in timing.items()}})
+            val_period = int(cfg.get("val_period") or 0)
+            if val_dataloader is not None and val_period > 0 and step % val_period == 0:
+                with collector.weights_lock:
+                    vm = validate(policy, val_dataloader, val_task_to_env or task_to_env, master_config, step,
+                                  tokenizer)
+                if logger:
+                    logger.log_metrics(vm, step, prefix="validation")
+            if checkpointer is not None and checkpointer.should_save(step):
+                with collector.weights_lock:
+                    state["replay_buffer"] = buffer.state_dict()
+                    checkpointer.save(policy, state, dataloader, metrics, step)
+                    state.pop("replay_buffer", None)
+    finally:
+        collector.stop()
+    collector.check_health()
+    return state

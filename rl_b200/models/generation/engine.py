@@ -94,6 +94,11 @@ class RolloutEngine:
         # optional callable returning a device buffer whose bytes the KV cache may
         # occupy while generating (colocated trainer: its idle gradient arena)
         self.kv_arena = None
+        # True once the KV cache has written into the arena (the owner must reset it)
+        self.arena_dirty = False
+        # "thread_local" when another thread keeps launching work while decode
+        # graphs are captured (async GRPO's rollout thread)
+        self.capture_error_mode = "global"
 
     # ------------------------------------------------------------ lifecycle
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
@@ -104,6 +109,7 @@ class RolloutEngine:
             arena = self.kv_arena() if self.kv_arena is not None else None
             self.kv = KVCache(self.model.cfg.num_layers, blocks, self.block_size, self.model.nkv, self.model.hd,
                               self.kv_dtype, self.device, arena=arena)
+            self.arena_dirty = self.arena_dirty or (arena is not None)
             self._kv_capacity_seqs = n
             sig = (self.kv.storage.data_ptr(), tuple(self.kv.storage.shape))
             if sig != getattr(self, "_kv_sig", None):
@@ -344,7 +350,7 @@ class RolloutEngine:
             self._graph_pool = torch.cuda.graph_pool_handle()
         g = torch.cuda.CUDAGraph()
         c0 = launch_count()
-        with torch.cuda.graph(g, pool=self._graph_pool):
+        with torch.cuda.graph(g, pool=self._graph_pool, capture_error_mode=self.capture_error_mode):
             self._step_body(st, temperature, top_k, top_p, stop)
         st.native_launches = launch_count() - c0
         add_launches(-st.native_launches)  # captured, not executed

@@ -35,7 +35,21 @@ from rl_b200.parallel.dist_optimizer import FlatAdamW
 from rl_b200.parallel.state import ParallelState, get_parallel_state
 from rl_b200.utils.timer import Timer
 
-__all__ = ["PolicyWorker", "pack_rows"]
+__all__ = ["PolicyWorker", "TrainStepState", "pack_rows"]
+
+
+class TrainStepState:
+    """State of one optimizer step between ``begin_train_step`` and
+    ``finish_train_step`` (micro-batch plan, device batch, global counts)."""
+
+    def __init__(self, **kw):
+        self.__dict__.update(kw)
+        self.mb_metrics: list[dict] = []
+        self.done = 0
+
+    @property
+    def num_microbatches(self) -> int:
+        return len(self.plan)
 
 
 def _dtype(precision: str) -> torch.dtype:
@@ -335,63 +349,23 @@ class PolicyWorker:
             self._pair_rows = False
 
     def _train(self, data: BatchedDataDict, loss_fn, gbs, eval_mode, temperature) -> dict:
-        temperature = float(temperature if temperature is not None else
-                            (self.cfg.get("generation", {}) or {}).get("temperature", 1.0) or 1.0)
-        ids = data["input_ids"]
-        B, S = ids.shape
+        B = data["input_ids"].shape[0]
         gbs = gbs or B
-        lengths = self._lengths(data)
-        self.optimizer.ensure_grad_buffer()
-        if self.engine.kv_arena is not None:
-            self.engine.finish_generation()   # the arena goes back to being gradients
-            self.optimizer.zero_grad()
-        # the per-token training tensors cross PCIe once (pinned, async) and are
-        # sliced on the device; no pageable copy stalls the launch stream later
-        dev_data = {k: _to_device(v, self.device) for k, v in data.items() if isinstance(v, torch.Tensor)}
         all_metrics: list[dict] = []
         losses, grad_norms, lrs = [], [], []
+        dev_data = None
         for g0 in range(0, B, gbs):
-            rows = list(range(g0, min(B, g0 + gbs)))
-            tok_mask = dev_data["token_mask"][g0:g0 + len(rows), 1:].float()
-            smask = dev_data["sample_mask"][g0:g0 + len(rows)].float()
-            counts = torch.stack([(tok_mask * smask.unsqueeze(-1)).sum(), smask.sum()])
-            if self.ps.dp_size > 1 or self.ps.cp_size > 1:
-                dist.all_reduce(counts, group=self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group)
-            gtoks, gseqs = counts[0], counts[1]
-            mb_plan = self._plan(lengths, [r for r in rows if lengths[r] > 0], self.train_mb_tokens)
-            self.model.aux_loss_scale = 1.0 / max(1, len(mb_plan))
-            step_loss = torch.zeros((), device=self.device)
-            mb_metrics: list[dict] = []
-            for mb_rows in mb_plan:
-                dummy = mb_rows[0] < 0
-                if dummy:
-                    mb_rows = [-1 - mb_rows[0]]
-                width = max(lengths[r] for r in mb_rows)
-                curr = self._loss_input(loss_fn, ids, lengths, mb_rows, width, temperature)
-                ridx = torch.tensor(mb_rows, dtype=torch.long).pin_memory().to(self.device, non_blocking=True) \
-                    if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
-                mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
-                                      for k, v in dev_data.items()})
-                loss, metrics = loss_fn(curr, mb, gseqs, gtoks)
-                if dummy:
-                    # zero-weight pass: keeps the EP group's all-to-alls paired, adds nothing
-                    loss = loss * 0.0
-                    metrics = {}
-                if not eval_mode:
-                    loss.backward()
-                    self.optimizer._fold_param_grads()
-                step_loss += loss.detach()
-                mb_metrics.append(metrics)
+            st = self.begin_train_step(data, loss_fn, rows=range(g0, min(B, g0 + gbs)), eval_mode=eval_mode,
+                                       temperature=temperature, _dev_data=dev_data)
+            dev_data = st.dev_data
+            for i in range(st.num_microbatches):
+                self.train_microbatch(st, i)
+            res = self.finish_train_step(st, release_grad=False, aggregate=False)
+            losses.append(res["loss"])
             if not eval_mode:
-                opt_stats = self.optimizer.step()
-                grad_norms.append(opt_stats["grad_norm"])
-                lrs.append(opt_stats["lr"])
-            else:
-                self.optimizer.zero_grad()
-            if self.ps.dp_size > 1:
-                dist.all_reduce(step_loss, group=self.ps.dp_group)
-            losses.append(float(step_loss))
-            all_metrics.extend(mb_metrics)
+                grad_norms.append(res["grad_norm"])
+                lrs.append(res["lr"])
+            all_metrics.extend(st.mb_metrics)
         if self.release_grad_after_train:
             self.optimizer.release_grad_buffer()
         agg = aggregate_metrics(all_metrics, self.ps.dp_group if self.ps.dp_size > 1 else None)
@@ -399,6 +373,95 @@ class PolicyWorker:
                     "grad_norm": grad_norms[-1] if grad_norms else 0.0, "lr": lrs[-1] if lrs else 0.0,
                     "moe_aux_loss": self.model.aux_loss()})
         return agg
+
+    # ------------------------------------------- split train API (one step)
+    def begin_train_step(self, data: BatchedDataDict, loss_fn, rows=None, eval_mode: bool = False,
+                         temperature: Optional[float] = None, _dev_data=None) -> "TrainStepState":
+        """Start ONE optimizer step over ``rows`` of ``data`` (default: all rows):
+        moves the batch to the device, reduces the global valid-token / sequence
+        counts over DP(xCP) and plans the packed micro-batches.  Follow with
+        ``train_microbatch(state, i)`` for ``i < state.num_microbatches`` (the
+        caller may interleave other work between micro-batches, e.g. an async
+        rollout pump) and ``finish_train_step(state)``.
+
+        Reference: the single-controller split train API
+        (``begin_train_step`` / ``train_microbatch`` / ``finish_train_step``,
+        ``nemo_rl/algorithms/single_controller.py:1-25``)."""
+        temperature = float(temperature if temperature is not None else
+                            (self.cfg.get("generation", {}) or {}).get("temperature", 1.0) or 1.0)
+        ids = data["input_ids"]
+        B = ids.shape[0]
+        rows = list(rows) if rows is not None else list(range(B))
+        lengths = self._lengths(data)
+        self.optimizer.ensure_grad_buffer()
+        if self.engine.kv_arena is not None and self.engine.arena_dirty:
+            self.engine.finish_generation()   # the arena goes back to being gradients
+            self.engine.arena_dirty = False
+            self.optimizer.zero_grad()
+        # the per-token training tensors cross PCIe once (pinned, async) and are
+        # sliced on the device; no pageable copy stalls the launch stream later
+        dev_data = _dev_data if _dev_data is not None else \
+            {k: _to_device(v, self.device) for k, v in data.items() if isinstance(v, torch.Tensor)}
+        g0, n = rows[0], len(rows)
+        tok_mask = dev_data["token_mask"][g0:g0 + n, 1:].float()
+        smask = dev_data["sample_mask"][g0:g0 + n].float()
+        counts = torch.stack([(tok_mask * smask.unsqueeze(-1)).sum(), smask.sum()])
+        if self.ps.dp_size > 1 or self.ps.cp_size > 1:
+            dist.all_reduce(counts, group=self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group)
+        plan = self._plan(lengths, [r for r in rows if lengths[r] > 0], self.train_mb_tokens)
+        self.model.aux_loss_scale = 1.0 / max(1, len(plan))
+        return TrainStepState(ids=ids, lengths=lengths, dev_data=dev_data, loss_fn=loss_fn, plan=plan,
+                              gtoks=counts[0], gseqs=counts[1], eval_mode=eval_mode, temperature=temperature,
+                              step_loss=torch.zeros((), device=self.device))
+
+    def train_microbatch(self, st: "TrainStepState", i: int) -> dict:
+        """Forward + backward of packed micro-batch ``i`` of the step; gradients
+        accumulate into the fp32 main-grad buffer.  Returns the (device) metrics."""
+        mb_rows = st.plan[i]
+        dummy = mb_rows[0] < 0
+        if dummy:
+            mb_rows = [-1 - mb_rows[0]]
+        width = max(st.lengths[r] for r in mb_rows)
+        curr = self._loss_input(st.loss_fn, st.ids, st.lengths, mb_rows, width, st.temperature)
+        ridx = torch.tensor(mb_rows, dtype=torch.long).pin_memory().to(self.device, non_blocking=True) \
+            if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
+        mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
+                              for k, v in st.dev_data.items()})
+        loss, metrics = st.loss_fn(curr, mb, st.gseqs, st.gtoks)
+        if dummy:
+            # zero-weight pass: keeps the EP group's all-to-alls paired, adds nothing
+            loss = loss * 0.0
+            metrics = {}
+        if not st.eval_mode:
+            loss.backward()
+            self.optimizer._fold_param_grads()
+        st.step_loss += loss.detach()
+        st.mb_metrics.append(metrics)
+        st.done += 1
+        return metrics
+
+    def finish_train_step(self, st: "TrainStepState", release_grad: Optional[bool] = None,
+                          aggregate: bool = True) -> dict:
+        """Optimizer step (or gradient reset in eval mode) and the step's metrics."""
+        if st.done != st.num_microbatches:
+            raise RuntimeError(f"finish_train_step after {st.done}/{st.num_microbatches} micro-batches")
+        out: dict = {}
+        if not st.eval_mode:
+            opt_stats = self.optimizer.step()
+            out.update(grad_norm=opt_stats["grad_norm"], lr=opt_stats["lr"])
+        else:
+            self.optimizer.zero_grad()
+        if self.ps.dp_size > 1:
+            dist.all_reduce(st.step_loss, group=self.ps.dp_group)
+        out["loss"] = float(st.step_loss)
+        if release_grad if release_grad is not None else self.release_grad_after_train:
+            self.optimizer.release_grad_buffer()
+        if aggregate:
+            agg = aggregate_metrics(st.mb_metrics, self.ps.dp_group if self.ps.dp_size > 1 else None)
+            agg.update(out)
+            agg["moe_aux_loss"] = self.model.aux_loss()
+            return agg
+        return out
 
     # -------------------------------------------------------- generation
     def generate(self, data: BatchedDataDict, greedy: bool = False) -> BatchedDataDict:

@@ -49,6 +49,8 @@ std::tuple<int64_t, at::Tensor> symm_alloc(int64_t bytes);
 int64_t symm_open(at::Tensor handle);
 void symm_close(int64_t ptr);
 at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
+void refit_copy(at::Tensor tasks, at::Tensor dst);
+void refit_quant_fp8(at::Tensor tasks, at::Tensor q, at::Tensor scales, bool pow2);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rl_b200 sm_100a kernels";
@@ -79,4 +81,6 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("symm_view", &symm_view);
+  m.def("refit_copy", &refit_copy, "train->rollout reshard (bf16) reading peer shards over NVLink");
+  m.def("refit_quant_fp8", &refit_quant_fp8, "train->rollout reshard fused with 128x128 e4m3 block quantisation");
 }

@@ -102,9 +102,28 @@ class PolicyWorker:
         self.sequence_parallel = bool(mc.get("sequence_parallel", False)) and self.ps.tp_size > 1
         act_ckpt = bool(mc.get("activation_checkpointing", policy_cfg.get("activation_checkpointing", False)))
         self.num_labels = int(policy_cfg.get("num_labels", 0) or 0)  # > 0: value / reward model
+        gen_cfg = dict(policy_cfg.get("generation", {}) or {})
+        vcfg = gen_cfg.get("vllm_cfg", {}) or {}
+        # rollout tensor parallelism: the training TP size (same layout, in-place refit)
+        # or 1 (every GPU holds full rollout weights; refit reshards over NVLink)
+        self.gen_tp = int(gen_cfg.get("tensor_parallel_size") or vcfg.get("tensor_parallel_size")
+                          or self.ps.tp_size)
+        if self.gen_tp not in (1, self.ps.tp_size):
+            raise NotImplementedError(f"generation TP {self.gen_tp} must be 1 or the training TP {self.ps.tp_size}")
+        self.fp8_rollout = str(vcfg.get("precision", gen_cfg.get("precision", "bfloat16"))).lower() == "fp8"
+        resharded = self.gen_tp != self.ps.tp_size
+        self._symm = None
+        flat_alloc = None
+        if resharded and self.device.type == "cuda" and self.ps.tp_size > 1:
+            def flat_alloc(numel, dtype, _w=self):
+                from rl_b200.parallel.symm import SymmetricBuffer
+
+                elt = torch.empty((), dtype=dtype).element_size()
+                _w._symm = SymmetricBuffer(numel * elt, _w.ps.tp_group)
+                return _w._symm.local_view(dtype, numel)
         self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
                                    sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt,
-                                   num_labels=self.num_labels)
+                                   num_labels=self.num_labels, flat_alloc=flat_alloc)
         opt = policy_cfg.get("optimizer", {}) or {}
         kw = dict(opt.get("kwargs", {}) or {})
         mopt = mc.get("optimizer", {}) or {}
@@ -119,11 +138,17 @@ class PolicyWorker:
                                    min_lr=float(mopt.get("min_lr", 0.0)), dp_group=grad_group,
                                    tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel,
                                    edp_group=self.ps.edp_group, ep_group=self.ps.ep_group)
-        gen_cfg = dict(policy_cfg.get("generation", {}) or {})
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
+        self.gen_model = self.model
+        if resharded:
+            from rl_b200.parallel.state import single_process_state
+
+            self.gen_model = TransformerLM(self.model_cfg, single_process_state(self.device), device=self.device,
+                                           dtype=self.dtype, skip_init=True)
+        self.weight_sync = self._make_weight_sync(resharded)
         self.engine = RolloutEngine(
-            self.model, gen_cfg, max_num_seqs=int(gen_cfg.get("max_num_seqs", 256)),
+            self.gen_model, gen_cfg, max_num_seqs=int(gen_cfg.get("max_num_seqs", 256)),
             max_model_len=self.max_seq_len, block_size=int(mgc.get("block_size_tokens", 256)),
             use_cuda_graphs=bool(gen_cfg.get("use_cuda_graphs", True)),
             seed=seed * 7 + self.ps.dp_rank * 100003,
@@ -144,6 +169,16 @@ class PolicyWorker:
         if bool(policy_cfg.get("kv_cache_in_grad_arena", self.device.type == "cuda")):
             self.engine.kv_arena = lambda: self.optimizer.main_grad
         self.timer = Timer()
+        self.weight_sync.sync()  # the rollout copy starts from the initial weights
+
+    def _make_weight_sync(self, resharded: bool):
+        from rl_b200.weight_sync.colocated import ColocatedInPlaceSynchronizer, ColocatedReshardSynchronizer
+
+        if not resharded:
+            return ColocatedInPlaceSynchronizer()
+        return ColocatedReshardSynchronizer(self.model, self.gen_model, self.ps.tp_group, self.ps.tp_rank,
+                                            self.ps.tp_size, peer_ptrs=self._symm.ptrs if self._symm else None,
+                                            fp8=self.fp8_rollout)
 
     # ------------------------------------------------------------- helpers
     def _plan(self, lengths: list[int], rows: list[int], budget: int) -> list[list[int]]:
@@ -465,7 +500,28 @@ class PolicyWorker:
 
     # -------------------------------------------------------- generation
     def generate(self, data: BatchedDataDict, greedy: bool = False) -> BatchedDataDict:
-        return self.engine.generate(data, greedy=greedy)
+        """Roll out ``data``.  With rollout TP 1 under training TP ``t`` the TP peers
+        (which hold identical data) each generate every t-th row with their full
+        rollout copy and exchange the results, so every peer returns the whole
+        batch (identical, as the trainer requires)."""
+        t = self.ps.tp_size
+        if self.gen_tp == t or t == 1:
+            return self.engine.generate(data, greedy=greedy)
+        B = data.size
+        r = self.ps.tp_rank
+        rows = list(range(r, B, t))
+        part = self.engine.generate(data.select_indices(rows), greedy=greedy) if rows else None
+        part = BatchedDataDict({k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in part.items()}) \
+            if part is not None else None
+        parts = [None] * t
+        dist.all_gather_object(parts, part, group=self.ps.tp_group)
+        order = [i for q in range(t) for i in range(q, B, t)]
+        out = BatchedDataDict.from_batches([p for p in parts if p is not None])
+        inv = [0] * B
+        for pos, i in enumerate(order):
+            inv[i] = pos
+        out.reorder_data(inv)
+        return out
 
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
         return self.engine.prepare_for_generation(num_seqs)
@@ -482,8 +538,11 @@ class PolicyWorker:
     def refit(self) -> float:
         """Make the rollout weights current.  Colocated and same layout: the
         optimizer step already wrote the bf16 parameters the engine reads, so the
-        refit is a no-op apart from invalidating cached state."""
+        refit is a no-op apart from invalidating cached state; with a different
+        rollout layout (or fp8 rollout weights) the weight synchronizer reshards
+        the training shards from the TP peers into the rollout copy."""
         t0 = time.perf_counter()
+        self.weight_sync.sync()
         self.engine.update_weights_from_training()
         self.engine.invalidate_kv_cache()
         return time.perf_counter() - t0
@@ -509,6 +568,7 @@ class PolicyWorker:
 
         if os.path.isdir(os.path.join(weights_path, "iter_0000000")):
             cio.load_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
+            self.weight_sync.sync()
             return
         cio.load_hf_checkpoint(self.model, weights_path)
         rank = dist.get_rank() if dist.is_initialized() else 0
@@ -519,6 +579,7 @@ class PolicyWorker:
             with torch.no_grad():
                 for seg in self.optimizer.segments:
                     seg.master.copy_(self.model.flat_param[seg.s_lo:seg.s_hi])
+        self.weight_sync.sync()
 
     def shutdown(self) -> None:
         """Release the rollout engine's captured graphs (they may hold NCCL
@@ -529,6 +590,7 @@ class PolicyWorker:
         if getattr(self.model, "_fused_rs", None) is not None:
             self.model._fused_rs.close()
             self.model._fused_rs = None
+        self.weight_sync.shutdown()
 
     def offload_before_refit(self) -> None:
         pass

@@ -142,8 +142,14 @@ class _EmbedFn(torch.autograd.Function):
 class TransformerLM(nn.Module):
     def __init__(self, cfg: ModelConfig, pstate: Optional[ParallelState] = None, device=None,
                  dtype: torch.dtype = torch.bfloat16, seed: int = 0, sequence_parallel: bool = False,
-                 activation_checkpointing: bool = False, init_std: float = 0.02, num_labels: int = 0):
+                 activation_checkpointing: bool = False, init_std: float = 0.02, num_labels: int = 0,
+                 flat_alloc: Optional[Callable[[int, torch.dtype], torch.Tensor]] = None, skip_init: bool = False):
+        """``flat_alloc(numel, dtype)`` supplies the flat parameter buffer (e.g. a
+        view of symmetric memory that TP peers can read over NVLink);
+        ``skip_init`` leaves the weights unset (a rollout copy filled by refit)."""
         super().__init__()
+        self._flat_alloc = flat_alloc
+        self._skip_init = skip_init
         self.num_labels = int(num_labels)  # > 0: value / reward model (scalar head instead of LM head)
         self.cfg = cfg
         self.ps = pstate or single_process_state(torch.device(device) if device else None)
@@ -229,8 +235,18 @@ class TransformerLM(nn.Module):
         return s
 
     def _allocate(self, seed: int, std: float) -> None:
-        self.flat_param = torch.empty(self.flat_numel, dtype=self.dtype, device=self.device)
+        if self._flat_alloc is not None:
+            self.flat_param = self._flat_alloc(self.flat_numel, self.dtype)
+        else:
+            self.flat_param = torch.empty(self.flat_numel, dtype=self.dtype, device=self.device)
         self.flat_param.zero_()
+        if self._skip_init:
+            self._params = {}
+            for sp in self.specs:
+                p = nn.Parameter(self.flat_param[sp.offset: sp.offset + sp.numel].view(sp.shape), requires_grad=False)
+                self._params[sp.name] = p
+                self.register_parameter(sp.name.replace(".", "__"), p)
+            return
         # random init runs on the model's device (an 8B model initialises in seconds on a B200);
         # the CPU and CUDA streams of one seed differ, every TP/EP layout of one device type agrees
         gen = torch.Generator(device=self.device)

@@ -1,0 +1,109 @@
+"""Colocated refit transports (trainer and rollout engine share each GPU)."""
+
+from __future__ import annotations
+
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from rl_b200.weight_sync.interfaces import WeightSynchronizer
+from rl_b200.weight_sync.reshard import (apply_regions_reference, build_regions, copy_tasks, quant_layout,
+                                         quant_regions_reference, quant_tasks)
+
+__all__ = ["ColocatedInPlaceSynchronizer", "ColocatedReshardSynchronizer"]
+
+
+class ColocatedInPlaceSynchronizer(WeightSynchronizer):
+    """Same layout: the optimizer step already wrote the bf16 weights the
+    engine reads (the flat parameter buffer is shared), nothing to move."""
+    name = "inplace"
+
+    def _sync(self) -> int:
+        return 0
+
+
+class ColocatedReshardSynchronizer(WeightSynchronizer):
+    """Training TP ``t`` -> generation TP ``g`` (``g`` divides ``t``), optionally
+    quantising the linear weights to 128x128 block-scaled e4m3.
+
+    On CUDA the training flat buffers are symmetric memory (``peer_ptrs[r]`` is
+    TP rank r's buffer mapped on this GPU) and ONE native launch per output
+    kind does the whole reshard (``rl_b200._C.refit_copy`` / ``refit_quant_fp8``).
+    On CPU (gloo tests) the shards are all-gathered and the same region table is
+    applied with torch indexing."""
+    name = "reshard"
+
+    def __init__(self, train_model, gen_model, tp_group, tp_rank: int, tp_size: int,
+                 peer_ptrs: Optional[list[int]] = None, fp8: bool = False, pow2_scales: bool = False,
+                 copy_bf16: bool = True):
+        super().__init__()
+        self.train_model, self.gen_model = train_model, gen_model
+        self.group, self.rank, self.t = tp_group, tp_rank, tp_size
+        self.g = gen_model.ps.tp_size
+        self.peer_ptrs = peer_ptrs
+        self.fp8, self.pow2, self.copy_bf16 = fp8, pow2_scales, copy_bf16
+        self.regions = build_regions(train_model.specs, gen_model.specs, train_model.cfg, self.t, self.g, tp_rank)
+        self.dev = gen_model.flat_param.device
+        self.native = self.dev.type == "cuda"
+        self.q_layout, qbytes, nscales = quant_layout(gen_model.specs) if fp8 else ({}, 0, 0)
+        self.q = torch.zeros(qbytes, dtype=torch.uint8, device=self.dev) if fp8 else None
+        self.scales = torch.zeros(nscales, dtype=torch.float32, device=self.dev) if fp8 else None
+        self._tasks = self._qtasks = None
+        if self.native:
+            if peer_ptrs is None or len(peer_ptrs) != self.t:
+                raise ValueError("native reshard needs the TP peers' symmetric parameter buffers")
+            if copy_bf16:
+                self._tasks = torch.from_numpy(copy_tasks(self.regions, peer_ptrs)).to(self.dev)
+            if fp8:
+                self._qtasks = torch.from_numpy(quant_tasks(self.regions, self.q_layout, peer_ptrs)).to(self.dev)
+
+    def fp8_weight(self, name: str):
+        """(e4m3 ``[R, C]``, fp32 scales ``[ceil(R/128), ceil(C/128)]``) views of one quantised weight."""
+        qoff, soff, R, C, nb, kb = self.q_layout[name]
+        return (self.q[qoff: qoff + R * C].view(torch.float8_e4m3fn).view(R, C),
+                self.scales[soff: soff + nb * kb].view(nb, kb))
+
+    def _fence(self) -> None:
+        # every TP peer's optimizer step must be complete before its shard is read:
+        # a stream-ordered all-reduce on the TP group orders this rank's kernels
+        # after the peers' preceding work
+        if self.t > 1:
+            x = torch.zeros(1, device=self.dev)
+            dist.all_reduce(x, group=self.group)
+
+    def _sync(self) -> int:
+        nbytes = 0
+        if self.native:
+            from rl_b200.ops._ext import add_launches, ext
+
+            self._fence()
+            if self._tasks is not None:
+                ext().refit_copy(self._tasks, self.gen_model.flat_param)
+                add_launches(1)
+                nbytes += self.gen_model.flat_param.numel() * 2
+            if self._qtasks is not None:
+                ext().refit_quant_fp8(self._qtasks, self.q, self.scales, self.pow2)
+                add_launches(1)
+                nbytes += self.q.numel() + self.scales.numel() * 4
+            # peers must finish reading this rank's shard before its next optimizer
+            # step overwrites it; their next TP collective (in the next training
+            # step, after this kernel in their stream order) gives that order
+            return nbytes
+        src = self.train_model.flat_param.detach()
+        if self.t > 1:
+            shards = [torch.empty_like(src) for _ in range(self.t)]
+            dist.all_gather(shards, src.contiguous(), group=self.group)
+        else:
+            shards = [src]
+        with torch.no_grad():
+            apply_regions_reference(self.regions, shards, self.gen_model.flat_param)
+            if self.fp8:
+                quant_regions_reference(self.gen_model.flat_param, self.q_layout, self.q, self.scales,
+                                        self.gen_model.specs, self.pow2)
+        return self.gen_model.flat_param.numel() * self.gen_model.flat_param.element_size()
+
+
+def regions_bytes(regions) -> int:
+    return int(np.sum([r.rows * r.cols for r in regions])) * 2

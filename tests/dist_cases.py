@@ -51,3 +51,48 @@ def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool):
     lp_after = w.get_logprobs(full)["logprobs"]
     return {"loss": res["loss"], "grad_norm": res["grad_norm"], "lp": lp_after,
             "probs_ratio_clamped_min": res.get("probs_ratio_clamped_min")}
+
+
+def case_reshard_refit(rank: int, tp: int):
+    """Training TP=tp, rollout TP=1: the resharded rollout copy equals the
+    full-weight model of the same seed, before and after a training step, and
+    the TP peers return the same rollouts."""
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.parallel.state import init_distributed, single_process_state
+
+    torch.manual_seed(0)
+    ps = init_distributed(tp=tp, backend="gloo")
+    cfg = _pcfg(False)
+    cfg["generation"] = dict(cfg["generation"], tensor_parallel_size=1)
+    w = PolicyWorker(cfg, model_cfg=TINY, pstate=ps, seed=3)
+    full = TransformerLM(TINY, single_process_state(), dtype=torch.float32, seed=3)
+    init_err = (w.gen_model.flat_param - full.flat_param).abs().max().item()
+    batch = make_batch()
+    res = w.train(batch, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=batch.size)
+    w.refit()
+    # gather the trained shards and rebuild the full tensors independently
+    errs = []
+    for sp, p in w.model.named_flat_params():
+        gp = w.gen_model.param(sp.name)
+        if sp.tp_dim is None or tp == 1:
+            errs.append((gp - p).abs().max().item())
+            continue
+        shards = [torch.empty_like(p) for _ in range(tp)]
+        torch.distributed.all_gather(shards, p.detach().contiguous(), group=ps.tp_group)
+        if sp.name.endswith(("qkv_proj.weight", "gate_up_proj.weight")):
+            secs = 3 if "qkv" in sp.name else 2
+            if secs == 3:
+                hd, nq, nkv = TINY.head_dim, TINY.num_heads // tp, TINY.num_kv_heads // tp
+                parts = [torch.split(s, [nq * hd, nkv * hd, nkv * hd], 0) for s in shards]
+            else:
+                parts = [s.chunk(2, 0) for s in shards]
+            ref = torch.cat([torch.cat([pp[k] for pp in parts], 0) for k in range(secs)], 0)
+        else:
+            ref = torch.cat(shards, sp.tp_dim)
+        errs.append((gp - ref).abs().max().item())
+    data = BatchedDataDict({"input_ids": batch["input_ids"][:5, :8].clone(),
+                            "input_lengths": torch.full((5,), 8, dtype=torch.long)})
+    out = w.generate(data, greedy=True)
+    return {"init_err": init_err, "refit_err": max(errs), "loss": res["loss"], "out_ids": out["output_ids"],
+            "gen_lens": out["generation_lengths"]}

@@ -38,3 +38,14 @@ def test_moe_expert_parallel_matches_single(moe_single):
     outs = spawn_ranks(case_train_step, 2, 1, 2, False, True)
     for o in outs:
         _close(o, moe_single)
+
+
+def test_reshard_refit_tp2_to_rollout_tp1():
+    from tests.dist_cases import case_reshard_refit
+
+    outs = spawn_ranks(case_reshard_refit, 2, 2)
+    for o in outs:
+        assert o["init_err"] == 0.0, o["init_err"]
+        assert o["refit_err"] == 0.0, o["refit_err"]
+    assert torch.equal(outs[0]["out_ids"], outs[1]["out_ids"])
+    assert outs[0]["out_ids"].shape[0] == 5

@@ -138,3 +138,82 @@ def test_tp_sp_model_fused_rs_2gpu():
         assert not o["missing"], o["missing"]
         worst = max(o["errs"].items(), key=lambda kv: kv[1])
         assert worst[1] < 3e-2, worst
+
+
+def case_refit_reshard(rank: int):
+    """Training TP=2 -> rollout TP=1 on 2 GPUs through the native reshard kernels
+    (peer loads of the TP partner's flat parameters), bf16 copy and fused fp8
+    block quantisation, against torch references built from NCCL-gathered shards."""
+    import os
+    import time
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.ops import _ext
+    from rl_b200.ops.quant import dequant_fp8_block, quant_fp8_block_ref
+    from rl_b200.parallel.state import init_distributed
+    from rl_b200.weight_sync.reshard import apply_regions_reference
+
+    ps = init_distributed(tp=2, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="refit", vocab_size=2048, hidden_size=1024, num_layers=2, num_heads=8, num_kv_heads=4,
+                      head_dim=128, ffn_hidden_size=2048, rope_theta=10000.0, max_position_embeddings=512)
+    pcfg = {"max_total_sequence_length": 128, "precision": "bfloat16",
+            "generation": {"temperature": 1.0, "max_new_tokens": 8, "tensor_parallel_size": 1,
+                           "vllm_cfg": {"precision": "fp8"}}}
+    w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=11)
+    ws = w.weight_sync
+    launches0 = _ext.launch_count()
+    with torch.no_grad():
+        w.model.flat_param.add_(0.01 * (rank + 1))  # make the shards differ from init
+    ws.sync()
+    torch.cuda.synchronize()
+    launches = _ext.launch_count() - launches0
+    src = w.model.flat_param.detach()
+    shards = [torch.empty_like(src) for _ in range(2)]
+    dist.all_gather(shards, src)
+    ref = torch.zeros_like(w.gen_model.flat_param)
+    apply_regions_reference(ws.regions, shards, ref)
+    copy_err = (ref.float() - w.gen_model.flat_param.float()).abs().max().item()
+    q_mismatch, deq_err, scale_err = 0.0, 0.0, 0.0
+    for name in ws.q_layout:
+        q, s = ws.fp8_weight(name)
+        qr, sr = quant_fp8_block_ref(w.gen_model.param(name).detach(), 128, False)
+        scale_err = max(scale_err, ((s - sr).abs() / sr).max().item())
+        q_mismatch = max(q_mismatch, (q.view(torch.uint8) != qr.view(torch.uint8)).float().mean().item())
+        a, b = dequant_fp8_block(q, s), dequant_fp8_block(qr, sr)
+        deq_err = max(deq_err, ((a - b).abs().max() / b.abs().max()).item())
+    # timing (max over ranks)
+    for _ in range(3):
+        ws.sync()
+    dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    reps = 5
+    for _ in range(reps):
+        ws.sync()
+    e1.record()
+    torch.cuda.synchronize()
+    t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    w.shutdown()
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"copy_err": copy_err, "q_mismatch": q_mismatch, "deq_err": deq_err, "scale_err": scale_err,
+            "launches": launches, "ms": t.item(), "bytes": int(w.gen_model.flat_param.numel() * 2)}
+
+
+def test_refit_reshard_tp2_to_tp1_fp8_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_refit_reshard, 2, timeout_s=300)
+    for o in outs:
+        assert o["copy_err"] == 0.0, o
+        assert o["scale_err"] < 1e-6, o
+        assert o["q_mismatch"] < 1e-3 and o["deq_err"] < 0.07, o
+        assert o["launches"] == 2, o
+    print("refit reshard (bf16 copy + fp8 quant):", f"{outs[0]['ms']:.3f} ms for {outs[0]['bytes'] / 2**20:.1f} MiB")

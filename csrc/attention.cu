@@ -378,6 +378,191 @@ paged_decode_tc_kernel(const bf16* __restrict__ q, long long q_stride, const bf1
   }
 }
 
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N));
+}
+
+// Pipelined tensor-core decode.  Each of the W warps of a CTA streams its own
+// sequence of 16-token K/V tiles (tiles w, w+W, w+2W, ... of the CTA's token
+// range) through a private ST-stage cp.async ring, so ST-1 tiles per warp are
+// always in flight while the warp runs the MMAs of the current one; the
+// CTA's block-table entries are staged in shared memory once, so no load on
+// the critical path waits for a block-table read.  S = Q K^T and O += P V run
+// as m16n8k16 MMAs with the G query heads of the group in rows 0..G-1.  After
+// the loop the ring is reused to merge the warps' online-softmax states.
+// Requires block_size % 16 == 0 and tokens_per_split % 16 == 0.
+template <int HD, int G, int W, int ST>
+__global__ void __launch_bounds__(W * 32)
+paged_decode_pipe_kernel(const bf16* __restrict__ q, long long q_stride, const bf16* __restrict__ kc,
+                         const bf16* __restrict__ vc, const int* __restrict__ block_tables, int max_blocks,
+                         const int* __restrict__ seq_lens, int block_size, int nkv, float scale_log2,
+                         int tokens_per_split, float* __restrict__ part_o, float* __restrict__ part_ml,
+                         bf16* __restrict__ out) {
+  constexpr int BT = 16, CH = HD / 8, KS = HD / 16, NT = HD / 8, TILE = BT * HD;
+  extern __shared__ __align__(128) unsigned char smem_raw[];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  bf16* ring = reinterpret_cast<bf16*>(smem_raw) + (size_t)w * ST * 2 * TILE;
+  int* sbt = reinterpret_cast<int*>(smem_raw + (size_t)W * ST * 2 * TILE * sizeof(bf16));
+  const int b = blockIdx.x, kvh = blockIdx.y, split = blockIdx.z;
+  const int g = lane >> 2, t = lane & 3;
+  const int L = seq_lens[b];
+  const int t_begin = split * tokens_per_split;
+  const int t_end = min(L, t_begin + tokens_per_split);
+  const int nq = nkv * G;
+  const int* bt = block_tables + (long long)b * max_blocks;
+  const int blk0 = t_begin / block_size;
+  if (t_end > t_begin) {
+    const int nblk = (t_end - 1) / block_size - blk0 + 1;
+    for (int i = threadIdx.x; i < nblk; i += W * 32) sbt[i] = bt[blk0 + i];
+  }
+  uint32_t qf[KS][4];
+  {
+    const bf16* qb = q + (long long)b * q_stride + (long long)kvh * G * HD;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      const int c0 = kk * 16 + 2 * t;
+      const bool ok = g < G;
+      qf[kk][0] = ok ? *reinterpret_cast<const uint32_t*>(qb + g * HD + c0) : 0u;
+      qf[kk][1] = 0u;
+      qf[kk][2] = ok ? *reinterpret_cast<const uint32_t*>(qb + g * HD + c0 + 8) : 0u;
+      qf[kk][3] = 0u;
+    }
+  }
+  __syncthreads();
+  const int ntiles = t_end > t_begin ? (t_end - t_begin + BT - 1) / BT : 0;
+  const int n_my = ntiles > w ? (ntiles - w + W - 1) / W : 0;
+  auto issue = [&](int k) {
+    if (k < n_my) {
+      const int t0 = t_begin + (w + k * W) * BT;
+      const int nvalid = min(BT, t_end - t0);
+      const long long base = (long long)sbt[t0 / block_size - blk0] * block_size + (t0 % block_size);
+      bf16* Ks = ring + (k % ST) * 2 * TILE;
+      bf16* Vs = Ks + TILE;
+#pragma unroll
+      for (int c = lane; c < BT * CH; c += 32) {
+        const int r = c / CH, ch = c % CH;
+        const bool ok = r < nvalid;
+        const long long row = ((base + (ok ? r : 0)) * nkv + kvh) * HD + ch * 8;
+        cp_async16(smem_u32(Ks + swz<CH>(r, ch) * 8), kc + row, ok ? 16 : 0);
+        cp_async16(smem_u32(Vs + swz<CH>(r, ch) * 8), vc + row, ok ? 16 : 0);
+      }
+    }
+    cp_async_commit();
+  };
+#pragma unroll
+  for (int k = 0; k < ST - 1; ++k) issue(k);
+  float oacc[NT][4];
+#pragma unroll
+  for (int j = 0; j < NT; ++j) oacc[j][0] = oacc[j][1] = oacc[j][2] = oacc[j][3] = 0.f;
+  float mrow = -INFINITY, lrow = 0.f;
+  for (int k = 0; k < n_my; ++k) {
+    issue(k + ST - 1);
+    cp_async_wait<ST - 1>();
+    __syncwarp();
+    const int t0 = t_begin + (w + k * W) * BT;
+    const int nvalid = min(BT, t_end - t0);
+    const bf16* Ks = ring + (k % ST) * 2 * TILE;
+    const bf16* Vs = Ks + TILE;
+    float s[2][4];
+#pragma unroll
+    for (int j = 0; j < 2; ++j) s[j][0] = s[j][1] = s[j][2] = s[j][3] = 0.f;
+#pragma unroll
+    for (int kk = 0; kk < KS; ++kk) {
+      uint32_t bfr[4];
+      ldsm_x4(bfr, smem_u32(Ks + swz<CH>(((lane >> 4) << 3) + (lane & 7), 2 * kk + ((lane >> 3) & 1)) * 8));
+      mma16816(s[0], qf[kk], bfr[0], bfr[1]);
+      mma16816(s[1], qf[kk], bfr[2], bfr[3]);
+    }
+    float mx = -INFINITY;
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int key = 8 * j + 2 * t + e;
+        const float v = key < nvalid ? s[j][e] * scale_log2 : -INFINITY;
+        s[j][e] = v;
+        mx = fmaxf(mx, v);
+      }
+    }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    const float mnew = fmaxf(mrow, mx);
+    const float muse = mnew == -INFINITY ? 0.f : mnew;
+    const float alpha = exp2f(mrow - muse);
+    mrow = mnew;
+    lrow *= alpha;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      oacc[j][0] *= alpha;
+      oacc[j][1] *= alpha;
+    }
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+      s[j][0] = exp2f(s[j][0] - muse);
+      s[j][1] = exp2f(s[j][1] - muse);
+      lrow += s[j][0] + s[j][1];
+    }
+    uint32_t a[4];
+    a[0] = pack_bf16(s[0][0], s[0][1]);
+    a[1] = 0u;
+    a[2] = pack_bf16(s[1][0], s[1][1]);
+    a[3] = 0u;
+#pragma unroll
+    for (int dp = 0; dp < NT / 2; ++dp) {
+      uint32_t bfr[4];
+      ldsm_x4_t(bfr, smem_u32(Vs + swz<CH>(lane & 15, 2 * dp + (lane >> 4)) * 8));
+      mma16816(oacc[2 * dp], a, bfr[0], bfr[1]);
+      mma16816(oacc[2 * dp + 1], a, bfr[2], bfr[3]);
+    }
+    __syncwarp();
+  }
+  cp_async_wait<0>();
+  lrow += __shfl_xor_sync(0xffffffffu, lrow, 1);
+  lrow += __shfl_xor_sync(0xffffffffu, lrow, 2);
+  __syncthreads();  // every warp is done with its ring: reuse it for the merge
+  constexpr int RS = HD + 2;
+  float* red = reinterpret_cast<float*>(smem_raw);  // [W][G][HD+2]
+  if (g < G) {
+    float* rw = red + ((size_t)w * G + g) * RS;
+#pragma unroll
+    for (int j = 0; j < NT; ++j) {
+      rw[8 * j + 2 * t] = oacc[j][0];
+      rw[8 * j + 2 * t + 1] = oacc[j][1];
+    }
+    if (t == 0) {
+      rw[HD] = mrow;
+      rw[HD + 1] = lrow;
+    }
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < G * HD; e += W * 32) {
+    const int gg = e / HD, d = e % HD;
+    float M = -INFINITY;
+#pragma unroll
+    for (int k = 0; k < W; ++k) M = fmaxf(M, red[((size_t)k * G + gg) * RS + HD]);
+    float Lsum = 0.f, O = 0.f;
+#pragma unroll
+    for (int k = 0; k < W; ++k) {
+      const float* rk = red + ((size_t)k * G + gg) * RS;
+      const float f = rk[HD] == -INFINITY ? 0.f : exp2f(rk[HD] - M);
+      Lsum += rk[HD + 1] * f;
+      O += rk[d] * f;
+    }
+    const int h = kvh * G + gg;
+    if (part_o == nullptr) {
+      out[(long long)b * nq * HD + h * HD + d] = __float2bfloat16_rn(Lsum > 0.f ? O / Lsum : 0.f);
+    } else {
+      const long long pi = ((long long)(b * nq + h) * gridDim.z + split);
+      part_o[pi * HD + d] = O;
+      if (d == 0) {
+        part_ml[pi * 2] = M;
+        part_ml[pi * 2 + 1] = Lsum;
+      }
+    }
+  }
+}
+
 template <int HD>
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits,
                                       int nq, bf16* __restrict__ out) {
@@ -873,11 +1058,31 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
   if (B == 0) return out;
   const int max_blocks = bt.size(1);
   const int cap = max_seq_len > 0 ? (int)max_seq_len : max_blocks * bs;
-  // split the sequence so that the grid fills the GPU at least twice
+  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
+  // pipelined tensor-core kernel: W=4 warps x ST=3 stages x 16-token tiles,
+  // two CTAs per SM; the split count makes the grid a near-whole number of
+  // waves of those 2 x SMs slots
+  constexpr int kW = 4, kST = 3;
+  const bool pipe = !fp8 && hd >= 64 && bs % 16 == 0;
   int splits = 1;
   const int base_ctas = B * nkv;
-  const int target = 2 * num_sms();
-  if (base_ctas < target) splits = std::min((target + base_ctas - 1) / base_ctas, std::max(1, cap / 256));
+  if (pipe) {
+    const int slots = 2 * num_sms();
+    const int max_s = std::max(1, std::min(8, cap / 128));
+    double best = -1.0;
+    for (int s_ = 1; s_ <= max_s; ++s_) {
+      const double waves = (double)base_ctas * s_ / slots;
+      const double eff = waves / std::ceil(waves);
+      if (eff > best + 0.02) {
+        best = eff;
+        splits = s_;
+      }
+      if (eff >= 0.95) break;
+    }
+  } else {
+    const int target = 2 * num_sms();
+    if (base_ctas < target) splits = std::min((target + base_ctas - 1) / base_ctas, std::max(1, cap / 256));
+  }
   const int tps = ((cap + splits - 1) / splits + 127) / 128 * 128;
   splits = (cap + tps - 1) / tps;
   at::Tensor part_o, part_ml;
@@ -892,6 +1097,24 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
     RLB_HD_SWITCH(hd, [&] {
       if constexpr (HD >= 64 && std::is_same<C, bf16>::value) {
         dim3 grid(B, nkv, splits);
+        if (pipe) {
+          const int ring = kW * kST * 2 * 16 * HD * 2;
+          const int nbt = tps / bs + 2;
+          const int smem = std::max(ring + nbt * 4, kW * GG * (HD + 2) * 4 + nbt * 4);
+          TORCH_CHECK(smem <= 227 * 1024, "decode: block table of a split does not fit in shared memory");
+          auto kern = paged_decode_pipe_kernel<HD, GG, kW, kST>;
+          cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+          kern<<<grid, kW * 32, smem, stream()>>>(
+              (const bf16*)q.data_ptr(), q.stride(0), (const bf16*)k_cache.data_ptr(),
+              (const bf16*)v_cache.data_ptr(), bt.data_ptr<int>(), max_blocks, sl.data_ptr<int>(), bs, nkv,
+              scale_log2, tps, splits > 1 ? part_o.data_ptr<float>() : nullptr,
+              splits > 1 ? part_ml.data_ptr<float>() : nullptr, (bf16*)out.data_ptr());
+          RLB_CUDA_CHECK(cudaGetLastError());
+          if (splits > 1)
+            decode_combine_kernel<HD><<<B * nq, HD, 0, stream()>>>(
+                part_o.data_ptr<float>(), part_ml.data_ptr<float>(), splits, nq, (bf16*)out.data_ptr());
+          return;
+        }
         const int smem = 4 * 2 * 32 * HD * 2 + 4 * GG * (HD + 2) * 4;
         auto kern = paged_decode_tc_kernel<HD, GG>;
         if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -920,7 +1143,6 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
   };
   struct BF { using type = bf16; };
   struct F8 { using type = __nv_fp8_e4m3; };
-  const bool fp8 = k_cache.scalar_type() == at::kFloat8_e4m3fn;
   TORCH_CHECK(fp8 || k_cache.scalar_type() == at::kBFloat16, "decode: cache must be bf16 or fp8 e4m3");
   auto dispatch_c = [&](auto gtag) {
     if (fp8) launch(gtag, F8{}); else launch(gtag, BF{});

@@ -105,7 +105,6 @@ quant_kernel(const Task* __restrict__ tasks, long long ntasks, uint8_t* __restri
     amax = block_max(amax, red);
     float s = fmaxf(amax, 1e-12f) / kFp8Max;
     if (pow2) s = pow2_ceil(s);
-    const float inv = 1.f / s;
     if (threadIdx.x == 0) scales[tk.scale_off] = s;
 #pragma unroll
     for (int u = 0; u < kPer; ++u) {
@@ -120,7 +119,9 @@ quant_kernel(const Task* __restrict__ tasks, long long ntasks, uint8_t* __restri
           uint32_t packed = 0;
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
-            const float x = fminf(fmaxf(f[h * 4 + e] * inv, -kFp8Max), kFp8Max);
+            // IEEE division (not a reciprocal multiply): the same e4m3 bytes as
+            // the torch reference quantisation x / s
+            const float x = fminf(fmaxf(__fdiv_rn(f[h * 4 + e], s), -kFp8Max), kFp8Max);
             const __nv_fp8_e4m3 b(x);
             packed |= (uint32_t)(*reinterpret_cast<const uint8_t*>(&b)) << (8 * e);
           }

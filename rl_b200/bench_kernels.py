@@ -2,6 +2,7 @@
 
     python -m rl_b200.bench_kernels gemm      [M N K]
     python -m rl_b200.bench_kernels decode    [B L]
+    python -m rl_b200.bench_kernels decode_gemm [M]
     python -m rl_b200.bench_kernels attn      [T_per_seq n_seq]
     python -m rl_b200.bench_kernels logprob   [T V]
 
@@ -56,6 +57,25 @@ def bench_decode(B=64, L=1024, nkv=8, G=4, hd=128, bs=256):
     print(f"paged_decode B={B} L={L}: {t * 1e3:.1f} us {byts / (t * 1e-3) / 1e12:.2f} TB/s")
 
 
+def bench_decode_gemm(M=64):
+    """The Llama-3.1-8B linear layers at decode batch M (weight-streaming bound):
+    time and achieved weight bandwidth per projection."""
+    dev = torch.device("cuda")
+    shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "down": (4096, 14336),
+              "lm_head": (128256, 4096)}
+    tot_t, tot_b = 0.0, 0
+    for name, (N, K) in shapes.items():
+        w = torch.randn(N, K, device=dev).to(torch.bfloat16)
+        x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+        t = _time(lambda: torch.matmul(x, w.t()), reps=20)
+        byts = N * K * 2
+        mult = 32 if name != "lm_head" else 1
+        tot_t += t * mult
+        tot_b += byts * mult
+        print(f"decode gemm {name} M={M} N={N} K={K}: {t * 1e3:.1f} us {byts / (t * 1e-3) / 1e12:.2f} TB/s")
+    print(f"decode gemms per token step (32 layers + head): {tot_t:.3f} ms {tot_b / (tot_t * 1e-3) / 1e12:.2f} TB/s")
+
+
 def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):
     from rl_b200.ops.attention import flash_attn_varlen
 
@@ -89,7 +109,8 @@ def main(argv=None):
     what = argv.pop(0) if argv else "gemm"
     args = [int(x) for x in argv]
     torch.manual_seed(0)
-    {"gemm": bench_gemm, "decode": bench_decode, "attn": bench_attn, "logprob": bench_logprob}[what](*args)
+    {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
+     "logprob": bench_logprob}[what](*args)
 
 
 if __name__ == "__main__":

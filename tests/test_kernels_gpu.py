@@ -237,16 +237,17 @@ def test_flash_attention_fwd_bwd(cuda_device, hd, nq, nkv):
     assert rel_err(v.grad, vf.grad) < 3e-2
 
 
-@pytest.mark.parametrize("G", [4, 8, 1])
-def test_paged_decode_and_cache_write(cuda_device, G):
+@pytest.mark.parametrize("G,hd,bs", [(4, 128, 16), (8, 128, 16), (1, 128, 16), (4, 128, 256), (8, 64, 32),
+                                     (2, 128, 8)])
+def test_paged_decode_and_cache_write(cuda_device, G, hd, bs):
     from rl_b200.ops.attention import paged_decode_attention, paged_decode_attention_ref, write_kv_cache, \
         write_kv_cache_ref
 
     torch.manual_seed(5)
-    B, nkv, hd, bs = 5, 4, 128, 16
+    B, nkv = 5, 4
     nq = nkv * G
     lens = torch.tensor([1, 17, 100, 600, 33], dtype=torch.int32)
-    maxb = 64
+    maxb = -(-1024 // bs)
     nblocks = B * maxb + 1
     kc = torch.zeros(nblocks, bs, nkv, hd, device=cuda_device, dtype=torch.bfloat16)
     vc = torch.zeros_like(kc)

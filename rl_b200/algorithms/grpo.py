@@ -30,6 +30,8 @@ from rl_b200.algorithms.utils import calculate_baseline_and_std_per_prompt, set_
 from rl_b200.data.llm_message_utils import add_loss_mask_to_message_log, batched_message_log_to_flat_message
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
 from rl_b200.experience.rollouts import run_multi_turn_rollout
+from rl_b200.utils.flops import FLOPTracker, mfu
+from rl_b200.utils.nvtx import maybe_gpu_profile_step
 from rl_b200.utils.timer import Timer, max_over_ranks
 
 __all__ = ["DEFAULT_GRPO_CONFIG", "GRPOSaveState", "grpo_train", "build_train_data", "dynamic_sampling",
@@ -211,6 +213,8 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     max_steps = max_steps if max_steps is not None else int(cfg["max_num_steps"])
     set_seed(int(cfg["seed"]) + ps.dp_rank)
     timer = Timer()
+    model_cfg = getattr(getattr(policy, "model", None), "cfg", None)
+    flop_tracker = FLOPTracker(model_cfg) if model_cfg is not None else None
     step = int(state["current_step"])
     if cfg.get("val_at_start") and step == 0 and val_dataloader is not None:
         vm = validate(policy, val_dataloader, val_task_to_env or task_to_env, master_config, step, tokenizer)
@@ -223,6 +227,7 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 done = True
                 break
             timer.reset()
+            maybe_gpu_profile_step(step)
             t_step = time.perf_counter()
             with timer.time("total_step_time"):
                 # ---- rollouts (with DAPO dynamic sampling) ----
@@ -286,6 +291,15 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
             step_time_max = max_over_ranks(step_time)
             world = max(1, ps.world_size)
             metrics = dict(train_results)
+            if flop_tracker is not None:
+                # model FLOPs of this rank's sequences (TP peers share them), summed over DP
+                flop_tracker.reset()
+                fwd = _dp_sum(flop_tracker.track(train_data["input_lengths"].tolist()), ps)
+                n_fwd_lp = 2 if kl_on else 1
+                t_train = max_over_ranks(timer.get_elapsed("policy_training"))
+                metrics["train_mfu"] = mfu(3 * fwd, t_train, world)
+                metrics["step_mfu"] = mfu((3 + n_fwd_lp) * fwd, step_time_max, world)
+                metrics["train_tflops_per_gpu"] = 3 * fwd / max(t_train, 1e-9) / world / 1e12
             metrics.update(adv_stats)
             metrics.update({k: v for k, v in rollout_metrics.items() if isinstance(v, (int, float))})
             metrics.update({

@@ -38,9 +38,13 @@ class Timer:
 
     @contextlib.contextmanager
     def time(self, label: str):
+        """Time a block (host wall clock) and mark it as an NVTX range."""
+        from rl_b200.utils.nvtx import nvtx_range
+
         self.start(label)
         try:
-            yield
+            with nvtx_range(label):
+                yield
         finally:
             self.stop(label)
 

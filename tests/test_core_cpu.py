@@ -367,3 +367,18 @@ def test_ppo_and_distillation_loops():
     kd_train(_tiny_policy(), _tiny_policy(seed=3), batches, {"distillation": {}}, k=8,
              step_callback=lambda s, m: seen.append(m))
     assert len(seen) == 1 and math.isfinite(seen[0]["loss"])
+
+
+def test_flops_formula_and_mfu():
+    from rl_b200.models.config import get_model_config
+    from rl_b200.utils.flops import FLOPTracker, forward_flops, mfu
+
+    cfg = get_model_config("llama3.1-8b")
+    # ~2 x 8.03e9 params per token (embedding lookup excluded, LM head included) + attention
+    f = forward_flops(cfg, [1])
+    n_lin = 32 * (4096 * (4096 + 2 * 1024) + 4096 * 4096 + 3 * 4096 * 14336) + 4096 * 128256
+    assert abs(f - 2 * n_lin - 32 * 2 * 32 * 128) < 1
+    tr = FLOPTracker(cfg)
+    tr.track([1024, 512])
+    assert tr.model_train_flops() == 3 * forward_flops(cfg, [1024, 512])
+    assert abs(mfu(2250e12, 1.0, 1, device="B200") - 1.0) < 1e-9

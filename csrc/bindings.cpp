@@ -50,6 +50,8 @@ int64_t symm_open(at::Tensor handle);
 void symm_close(int64_t ptr);
 at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
 void refit_copy(at::Tensor tasks, at::Tensor dst);
+at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
+int64_t gemm_decode_error_flag(bool reset);
 void refit_quant_fp8(at::Tensor tasks, at::Tensor q, at::Tensor scales, bool pow2);
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -81,6 +83,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("symm_view", &symm_view);
+  m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
+  m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);
   m.def("refit_copy", &refit_copy, "train->rollout reshard (bf16) reading peer shards over NVLink");
   m.def("refit_quant_fp8", &refit_quant_fp8, "train->rollout reshard fused with 128x128 e4m3 block quantisation");
 }

@@ -21,106 +21,14 @@
 // L2 reuse.  Every mbarrier wait is bounded in time: on expiry the kernel sets
 // an error word (readable from the host), raises a CTA-wide abort flag so all
 // roles drain, frees its tensor memory and returns.
-#include "common.cuh"
-
-#include <cudaTypedefs.h>
+#include "tc_common.cuh"
 
 namespace rlb {
 namespace tc {
 
 __device__ int g_error = 0;
 
-constexpr int BM = 128;
-constexpr int BK = 64;  // 64 bf16 = 128 bytes = one swizzle row
 constexpr int GROUP_M = 8;
-constexpr long long kWaitCycles = 4000000000LL;  // ~2 s at 2 GHz
-
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-
-__device__ __forceinline__ void mbar_init(uint32_t addr, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;\n" ::"r"(addr), "r"(count) : "memory");
-}
-__device__ __forceinline__ void mbar_expect_tx(uint32_t addr, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;\n" ::"r"(addr), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ void mbar_arrive(uint32_t addr) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];\n" ::"r"(addr) : "memory");
-}
-__device__ __forceinline__ bool mbar_test(uint32_t addr, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok)
-      : "r"(addr), "r"(parity)
-      : "memory");
-  return ok != 0;
-}
-
-// Bounded wait.  Returns false if the wait expired or another role aborted.
-__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, volatile int* abort_flag) {
-  const long long t0 = clock64();
-  while (!mbar_test(addr, parity)) {
-    if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
-      atomicExch(&g_error, 1);
-      *abort_flag = 1;
-      return false;
-    }
-  }
-  return true;
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const void* tmap, uint32_t mbar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%3, %4}], [%2];\n" ::"r"(
-          dst),
-      "l"(tmap), "r"(mbar), "r"(x), "r"(y)
-      : "memory");
-}
-
-// Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, rows of
-// 128 bytes, 8-row core groups 1024 bytes apart (tile base 1024-byte aligned).
-__device__ __forceinline__ uint64_t desc_kmajor_sw128(uint32_t saddr) {
-  uint64_t d = 0;
-  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
-  d |= (uint64_t)1u << 16;             // leading byte offset (unused for swizzled K-major)
-  d |= (uint64_t)(1024u >> 4) << 32;   // stride byte offset
-  d |= (uint64_t)1u << 46;             // descriptor version for sm_100
-  d |= (uint64_t)2u << 61;             // 128-byte swizzle
-  return d;
-}
-
-// Instruction descriptor: bf16 x bf16 -> fp32, both operands K-major.
-__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
-  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
-                                          uint32_t accumulate) {
-  asm volatile(
-      "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}\n" ::"r"(
-          tmem_d),
-      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate));
-}
-__device__ __forceinline__ void umma_commit(uint32_t mbar) {
-  asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mbar) : "memory");
-}
-__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;\n" ::: "memory"); }
-__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;\n" ::: "memory"); }
-
-__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t* r) {
-  asm volatile(
-      "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,%17,%18,%19,"
-      "%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31}, [%32];\n"
-      : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3]), "=r"(r[4]), "=r"(r[5]), "=r"(r[6]), "=r"(r[7]), "=r"(r[8]),
-        "=r"(r[9]), "=r"(r[10]), "=r"(r[11]), "=r"(r[12]), "=r"(r[13]), "=r"(r[14]), "=r"(r[15]), "=r"(r[16]),
-        "=r"(r[17]), "=r"(r[18]), "=r"(r[19]), "=r"(r[20]), "=r"(r[21]), "=r"(r[22]), "=r"(r[23]), "=r"(r[24]),
-        "=r"(r[25]), "=r"(r[26]), "=r"(r[27]), "=r"(r[28]), "=r"(r[29]), "=r"(r[30]), "=r"(r[31])
-      : "r"(taddr));
-  asm volatile("tcgen05.wait::ld.sync.aligned;\n" ::: "memory");
-}
 
 __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int& mt, int& nt) {
   const int group = GROUP_M * num_n;
@@ -130,6 +38,11 @@ __device__ __forceinline__ void tile_coords(int tile, int num_m, int num_n, int&
   const int in = tile % group;
   mt = first_m + in % gsize;
   nt = in / gsize;
+}
+
+// Bounded wait on this file's error word.
+__device__ __forceinline__ bool mbar_wait(uint32_t addr, uint32_t parity, volatile int* abort_flag) {
+  return mbar_wait_err(addr, parity, abort_flag, &g_error, 1);
 }
 
 // ------------------------------------------------------------------------
@@ -450,32 +363,6 @@ gemm_nt_kernel_t(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
 }  // namespace rlb
 
 using namespace rlb;
-
-static PFN_cuTensorMapEncodeTiled_v12000 tma_encode_fn() {
-  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
-  if (fn == nullptr) {
-    cudaDriverEntryPointQueryResult q;
-    void* p = nullptr;
-    RLB_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q));
-    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "rl_b200: cuTensorMapEncodeTiled unavailable");
-    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
-  }
-  return fn;
-}
-
-// 2-D row-major bf16 [rows, cols] tensor map with a (box_rows x 64) box, 128-byte swizzle.
-static CUtensorMap make_tmap_2d(const void* ptr, int64_t rows, int64_t cols, int box_rows) {
-  CUtensorMap m;
-  cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
-  cuuint64_t strides[1] = {(cuuint64_t)cols * 2};
-  cuuint32_t box[2] = {64u, (cuuint32_t)box_rows};
-  cuuint32_t estr[2] = {1u, 1u};
-  CUresult r = tma_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides, box,
-                               estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  TORCH_CHECK(r == CUDA_SUCCESS, "rl_b200: cuTensorMapEncodeTiled failed (", (int)r, ")");
-  return m;
-}
 
 template <int BN, int STAGES, int EPI>
 static void launch_gemm(const at::Tensor& a, const at::Tensor& b, __nv_bfloat16* c, int M, int N, int K,

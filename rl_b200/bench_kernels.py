@@ -63,17 +63,26 @@ def bench_decode_gemm(M=64):
     dev = torch.device("cuda")
     shapes = {"qkv": (6144, 4096), "o": (4096, 4096), "gate_up": (28672, 4096), "down": (4096, 14336),
               "lm_head": (128256, 4096)}
-    tot_t, tot_b = 0.0, 0
+    from rl_b200.ops._ext import ext
+
+    tp = int(__import__("os").environ.get("RLB_BENCH_TP", "1"))
+    tot_t, tot_l, tot_b = 0.0, 0.0, 0
     for name, (N, K) in shapes.items():
+        if tp > 1:  # this rank's shard: column-parallel split N, row-parallel split K
+            N, K = (N, K // tp) if name in ("o", "down") else (N // tp, K)
         w = torch.randn(N, K, device=dev).to(torch.bfloat16)
         x = torch.randn(M, K, device=dev).to(torch.bfloat16)
-        t = _time(lambda: torch.matmul(x, w.t()), reps=20)
+        t = _time(lambda: ext().gemm_decode(x, w), reps=20)
+        tl = _time(lambda: torch.matmul(x, w.t()), reps=20)
         byts = N * K * 2
         mult = 32 if name != "lm_head" else 1
         tot_t += t * mult
+        tot_l += tl * mult
         tot_b += byts * mult
-        print(f"decode gemm {name} M={M} N={N} K={K}: {t * 1e3:.1f} us {byts / (t * 1e-3) / 1e12:.2f} TB/s")
-    print(f"decode gemms per token step (32 layers + head): {tot_t:.3f} ms {tot_b / (tot_t * 1e-3) / 1e12:.2f} TB/s")
+        print(f"decode gemm {name} M={M} N={N} K={K}: native {t * 1e3:.1f} us {byts / (t * 1e-3) / 1e12:.2f} TB/s | "
+              f"library {tl * 1e3:.1f} us {byts / (tl * 1e-3) / 1e12:.2f} TB/s")
+    print(f"decode gemms per token step (32 layers + head, tp={tp}): native {tot_t:.3f} ms "
+          f"{tot_b / (tot_t * 1e-3) / 1e12:.2f} TB/s | library {tot_l:.3f} ms {tot_b / (tot_l * 1e-3) / 1e12:.2f} TB/s")
 
 
 def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):

@@ -31,6 +31,11 @@ _KERNELS_PER_CALL = {
     "paged_decode_attn": 1,
     "sample": 2,
     "gemm_error_flag": 0,
+    "gemm_decode_error_flag": 0,
+    "symm_alloc": 0,
+    "symm_open": 0,
+    "symm_close": 0,
+    "symm_view": 0,
 }
 
 

@@ -23,7 +23,7 @@ import torch
 
 from rl_b200.ops._ext import ext, has_ext, use_native
 
-__all__ = ["mm_nt", "mm_nn", "mm_tn", "mm_tn_accumulate", "native_gemm_supported"]
+__all__ = ["mm_nt", "mm_nn", "mm_tn", "mm_tn_accumulate", "native_gemm_supported", "decode_gemm_supported"]
 
 _NATIVE_GEMM = os.environ.get("RL_B200_NATIVE_GEMM", "1") == "1"
 
@@ -51,10 +51,19 @@ def native_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
     return tiles * 2 >= _sms()
 
 
+def decode_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
+    """Few-row products (rollout decode: one token per sequence) stream the
+    weight matrix: the split-K transposed tcgen05 kernel of ``csrc/gemm_decode.cu``."""
+    return _NATIVE_GEMM and dtype == torch.bfloat16 and has_ext() and 0 < M <= 256 and N >= 128 and K % 8 == 0
+
+
 def mm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
-    if use_native(a) and native_gemm_supported(a.shape[0], b.shape[0], a.shape[1], a.dtype) \
-            and a.is_contiguous() and b.is_contiguous():
-        return ext().gemm_nt(a, b)
+    if use_native(a) and a.is_contiguous() and b.is_contiguous():
+        M, N, K = a.shape[0], b.shape[0], a.shape[1]
+        if native_gemm_supported(M, N, K, a.dtype):
+            return ext().gemm_nt(a, b)
+        if decode_gemm_supported(M, N, K, a.dtype):
+            return ext().gemm_decode(a, b)
     return torch.matmul(a, b.t())
 
 

@@ -283,3 +283,19 @@ def test_gemm_tcgen05(cuda_device, M, N, K):
     assert ext.gemm_error_flag(True) == 0
     ref = a.float() @ b.float().t()
     assert rel_err(c, ref) < 1e-2
+
+
+@pytest.mark.parametrize("M,N,K", [(1, 6144, 4096), (64, 4096, 4096), (64, 28672, 4096), (128, 4096, 14336),
+                                   (200, 1000, 128), (33, 384, 4104), (256, 3072, 4096), (7, 128256, 512)])
+def test_gemm_decode_tcgen05(cuda_device, M, N, K):
+    ext = _ext.ext()
+    torch.manual_seed(8)
+    x = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    y = ext.gemm_decode(x, w)
+    y2 = ext.gemm_decode(x, w)
+    torch.cuda.synchronize()
+    ref = x.float() @ w.float().t()
+    assert rel_err(y, ref) < 1e-2
+    assert torch.equal(y, y2)  # split-K reduction is deterministic
+    assert ext.gemm_decode_error_flag(True) == 0

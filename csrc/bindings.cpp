@@ -51,6 +51,10 @@ void symm_close(int64_t ptr);
 at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
 void refit_copy(at::Tensor tasks, at::Tensor dst);
 at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
+at::Tensor dp_reduce_shard(std::vector<int64_t> grad_ptrs, int64_t lo, int64_t len, at::Tensor out);
+void dp_adam_allgather(std::vector<int64_t> param_ptrs, int64_t lo, at::Tensor master, at::Tensor grad,
+                       at::Tensor exp_avg, at::Tensor exp_avg_sq, at::Tensor nodecay, double lr, double b1, double b2,
+                       double eps, double wd, int64_t step, double gscale);
 int64_t gemm_decode_error_flag(bool reset);
 void refit_quant_fp8(at::Tensor tasks, at::Tensor q, at::Tensor scales, bool pow2);
 
@@ -83,6 +87,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);
   m.def("symm_view", &symm_view);
+  m.def("dp_reduce_shard", &dp_reduce_shard, "DP gradient reduce-scatter over NVLink peer loads (+ norm partials)");
+  m.def("dp_adam_allgather", &dp_adam_allgather, "sharded AdamW fused with the parameter all-gather (peer stores)");
   m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
   m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);
   m.def("refit_copy", &refit_copy, "train->rollout reshard (bf16) reading peer shards over NVLink");

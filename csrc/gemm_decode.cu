@@ -178,11 +178,24 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
         if (last_flag) {
           __threadfence();
           if (n < N) {
+            // 8 batch rows at a time: 8 independent L2 loads in flight per split
 #pragma unroll 1
-            for (int b = 0; b < Mb; ++b) {
-              float v = 0.f;
-              for (int sp = 0; sp < S; ++sp) v += __ldcg(ws + ((long long)sp * Mb + b) * N + n);
-              out[(long long)b * N + n] = __float2bfloat16_rn(v);
+            for (int b0 = 0; b0 < Mb; b0 += 8) {
+              float acc[8];
+#pragma unroll
+              for (int q = 0; q < 8; ++q) acc[q] = 0.f;
+#pragma unroll 1
+              for (int sp = 0; sp < S; ++sp) {
+                float t[8];
+#pragma unroll
+                for (int q = 0; q < 8; ++q)
+                  t[q] = (b0 + q < Mb) ? __ldcg(ws + ((long long)sp * Mb + b0 + q) * N + n) : 0.f;
+#pragma unroll
+                for (int q = 0; q < 8; ++q) acc[q] += t[q];
+              }
+#pragma unroll
+              for (int q = 0; q < 8; ++q)
+                if (b0 + q < Mb) out[(long long)(b0 + q) * N + n] = __float2bfloat16_rn(acc[q]);
             }
           }
           asm volatile("bar.sync 1, 128;\n" ::: "memory");

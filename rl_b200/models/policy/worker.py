@@ -112,15 +112,14 @@ class PolicyWorker:
             raise NotImplementedError(f"generation TP {self.gen_tp} must be 1 or the training TP {self.ps.tp_size}")
         self.fp8_rollout = str(vcfg.get("precision", gen_cfg.get("precision", "bfloat16"))).lower() == "fp8"
         resharded = self.gen_tp != self.ps.tp_size
-        self._symm = None
-        flat_alloc = None
-        if resharded and self.device.type == "cuda" and self.ps.tp_size > 1:
-            def flat_alloc(numel, dtype, _w=self):
-                from rl_b200.parallel.symm import SymmetricBuffer
+        # symmetric memory (every rank of the node maps every other's parameter and
+        # gradient buffers): needed by the reshard refit and the fused DP optimizer
+        from rl_b200.parallel.symm import NodeSymmetric
 
-                elt = torch.empty((), dtype=dtype).element_size()
-                _w._symm = SymmetricBuffer(numel * elt, _w.ps.tp_group)
-                return _w._symm.local_view(dtype, numel)
+        fused_dp = bool(mc.get("fused_dp_optimizer", True)) and self.ps.dp_size > 1
+        self.symmetric = NodeSymmetric() if NodeSymmetric.supported() and (
+            (resharded and self.ps.tp_size > 1) or fused_dp) else None
+        flat_alloc = self.symmetric.flat_alloc if self.symmetric is not None else None
         self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
                                    sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt,
                                    num_labels=self.num_labels, flat_alloc=flat_alloc)
@@ -137,7 +136,8 @@ class PolicyWorker:
                                    max_grad_norm=policy_cfg.get("max_grad_norm", 1.0), scheduler_cfg=sched,
                                    min_lr=float(mopt.get("min_lr", 0.0)), dp_group=grad_group,
                                    tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel,
-                                   edp_group=self.ps.edp_group, ep_group=self.ps.ep_group)
+                                   edp_group=self.ps.edp_group, ep_group=self.ps.ep_group,
+                                   symmetric=self.symmetric if fused_dp else None)
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
         self.gen_model = self.model
@@ -176,9 +176,13 @@ class PolicyWorker:
 
         if not resharded:
             return ColocatedInPlaceSynchronizer()
+        peer_ptrs = None
+        symm = getattr(self.model.flat_param, "_symm", None)
+        if symm is not None:
+            # symmetric buffers are indexed by global rank; the reshard wants TP-group order
+            peer_ptrs = [symm.ptrs[dist.get_global_rank(self.ps.tp_group, r)] for r in range(self.ps.tp_size)]
         return ColocatedReshardSynchronizer(self.model, self.gen_model, self.ps.tp_group, self.ps.tp_rank,
-                                            self.ps.tp_size, peer_ptrs=self._symm.ptrs if self._symm else None,
-                                            fp8=self.fp8_rollout)
+                                            self.ps.tp_size, peer_ptrs=peer_ptrs, fp8=self.fp8_rollout)
 
     # ------------------------------------------------------------- helpers
     def _plan(self, lengths: list[int], rows: list[int], budget: int) -> list[list[int]]:

@@ -26,6 +26,8 @@ from rl_b200.ops._ext import ext, has_ext, use_native
 __all__ = ["mm_nt", "mm_nn", "mm_tn", "mm_tn_accumulate", "native_gemm_supported", "decode_gemm_supported"]
 
 _NATIVE_GEMM = os.environ.get("RL_B200_NATIVE_GEMM", "1") == "1"
+# the decode-shaped kernel is opt-in until it beats the library GEMM on every decode shape
+_DECODE_GEMM = os.environ.get("RL_B200_DECODE_GEMM", "0") == "1"
 
 
 _NUM_SMS = None
@@ -54,7 +56,8 @@ def native_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
 def decode_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
     """Few-row products (rollout decode: one token per sequence) stream the
     weight matrix: the split-K transposed tcgen05 kernel of ``csrc/gemm_decode.cu``."""
-    return _NATIVE_GEMM and dtype == torch.bfloat16 and has_ext() and 0 < M <= 256 and N >= 128 and K % 8 == 0
+    return (_DECODE_GEMM and dtype == torch.bfloat16 and has_ext() and 0 < M <= 256 and N >= 128
+            and K % 8 == 0)
 
 
 def mm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:

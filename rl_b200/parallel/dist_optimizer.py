@@ -30,6 +30,8 @@ from typing import Optional
 import torch
 import torch.distributed as dist
 
+from rl_b200.ops._ext import ext
+
 from rl_b200.ops.optim import adamw_step, sum_of_squares
 
 __all__ = ["FlatAdamW", "LRScheduler"]
@@ -114,8 +116,16 @@ class _Segment:
 class FlatAdamW:
     def __init__(self, model, lr: float = 1e-5, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  max_grad_norm: Optional[float] = 1.0, scheduler_cfg=None, min_lr: float = 0.0,
-                 dp_group=None, tp_group=None, sequence_parallel: bool = False, edp_group=None, ep_group=None):
+                 dp_group=None, tp_group=None, sequence_parallel: bool = False, edp_group=None, ep_group=None,
+                 symmetric=None):
+        """``symmetric``: a ``rl_b200.parallel.symm.NodeSymmetric`` allocator.  When
+        given (CUDA, every rank on one node) the fp32 gradient buffer and the bf16
+        parameter buffer are symmetric memory and the dense data-parallel segment
+        steps with the fused kernels of ``csrc/dp_optim.cu`` (reduce-scatter by
+        peer loads + norm partials, then AdamW fused with the parameter all-gather
+        by peer stores) instead of NCCL reduce-scatter / all-gather."""
         self.model = model
+        self.symmetric = symmetric
         self.lr = lr
         self.beta1, self.beta2 = betas
         self.eps = eps
@@ -157,6 +167,9 @@ class FlatAdamW:
                     rep_r.append((a - seg.s_lo, b - seg.s_lo, sp.tp_dim is None and sp.ep_dim is None))
             seg.wd_ranges = _merge(wd_r)
             seg.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
+            nd = [(a, b) for a, b, d in seg.wd_ranges if not d]
+            seg.nodecay_dev = torch.tensor(nd if nd else [[seg.shard, seg.shard]], dtype=torch.int64,
+                                           device=dev).view(-1, 2)
         self.main_grad: Optional[torch.Tensor] = None
         self.ensure_grad_buffer()
         self.step_count = 0
@@ -170,7 +183,12 @@ class FlatAdamW:
         old = m.flat_param
         if self.padded == old.numel() and expert_shift == 0:
             return
-        big = torch.zeros(self.padded, dtype=old.dtype, device=old.device)
+        alloc = getattr(m, "_flat_alloc", None)
+        if alloc is not None:
+            big = alloc(self.padded, old.dtype)
+            big.zero_()
+        else:
+            big = torch.zeros(self.padded, dtype=old.dtype, device=old.device)
         for sp, p in m.named_flat_params():
             new_off = sp.offset + (expert_shift if sp.ep_dim is not None else 0)
             big[new_off:new_off + sp.numel].copy_(old[sp.offset:sp.offset + sp.numel])
@@ -178,6 +196,9 @@ class FlatAdamW:
         m.flat_param = big
         for sp, p in m.named_flat_params():
             p.data = big[sp.offset: sp.offset + sp.numel].view(sp.shape)
+        old_symm = getattr(old, "_symm", None)
+        if old_symm is not None and self.symmetric is not None:
+            self.symmetric.release(old_symm)
         if hasattr(m, "expert_offset"):
             m.expert_offset = self.segments[-1].lo if self.segments[-1].expert else self.padded
         del old
@@ -186,7 +207,12 @@ class FlatAdamW:
     def ensure_grad_buffer(self) -> None:
         if self.main_grad is not None:
             return
-        self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
+        if self.symmetric is not None:
+            self._grad_symm = self.symmetric.alloc(self.padded * 4)
+            self.main_grad = self._grad_symm.local_view(torch.float32, self.padded)
+            self.main_grad.zero_()
+        else:
+            self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
         for seg in self.segments:
             if seg.n == 1:
                 seg.grad_shard = self.main_grad[seg.s_lo:seg.s_hi]
@@ -196,7 +222,10 @@ class FlatAdamW:
             p.main_grad = self.main_grad[sp.offset: sp.offset + sp.numel].view(sp.shape)
 
     def release_grad_buffer(self) -> None:
-        """Free the fp32 gradient buffers (re-created zeroed by ``ensure_grad_buffer``)."""
+        """Free the fp32 gradient buffers (re-created zeroed by ``ensure_grad_buffer``).
+        A symmetric gradient buffer stays (its allocation is collective)."""
+        if self.symmetric is not None:
+            return
         for _, p in self.model.named_flat_params():
             p.main_grad = None
             p.grad = None
@@ -231,12 +260,21 @@ class FlatAdamW:
                     dist.all_reduce(p.main_grad, group=self.tp_group)
         sq_total = torch.zeros((), dtype=torch.float32, device=self.device)
         for seg in self.segments:
-            if seg.n > 1:
+            fused = self._fused(seg)
+            if seg.n > 1 and fused:
+                # peers finished their backward passes (stream-ordered fence), then
+                # this rank reduces its shard straight out of their gradient buffers
+                self._fence(seg.group)
+                part = ext().dp_reduce_shard(self._peer_ptrs(self._grad_symm, seg), seg.s_lo, seg.shard,
+                                             seg.grad_shard)
+                sq_all = part.sum()
+            elif seg.n > 1:
                 # losses are normalised by GLOBAL token / sequence counts, so the
                 # per-rank gradients are partial sums: reduce with SUM, not mean.
                 dist.reduce_scatter_tensor(seg.grad_shard, self.main_grad[seg.lo:seg.hi], group=seg.group)
             g = seg.grad_shard
-            sq_all = sum_of_squares(g)
+            if not (seg.n > 1 and fused):
+                sq_all = sum_of_squares(g)
             if self.tp > 1:
                 sq_rep = torch.zeros((), dtype=torch.float32, device=g.device)
                 for a, b in seg.rep_ranges:
@@ -261,17 +299,50 @@ class FlatAdamW:
             return {"grad_norm": norm, "lr": self.current_lr(), "skipped": 1.0}
         self.step_count += 1
         lr = self.scheduler.lr_at(self.step_count - 1)
+        fenced = False
         for seg in self.segments:
             out = m.flat_param[seg.s_lo:seg.s_hi]
             g = seg.grad_shard
+            if seg.n > 1 and self._fused(seg):
+                ext().dp_adam_allgather(self._peer_ptrs(self._flat_symm(), seg, param=True), seg.s_lo, seg.master, g,
+                                        seg.exp_avg, seg.exp_avg_sq, seg.nodecay_dev, lr, self.beta1, self.beta2,
+                                        self.eps, self.weight_decay, self.step_count, scale)
+                fenced = True
+                continue
             for a, b, decayed in seg.wd_ranges:
                 adamw_step(seg.master[a:b], g[a:b], seg.exp_avg[a:b], seg.exp_avg_sq[a:b], lr, self.beta1,
                            self.beta2, self.eps, self.weight_decay if decayed else 0.0, self.step_count,
                            grad_scale=scale, param_out=out[a:b])
             if seg.n > 1:
                 dist.all_gather_into_tensor(m.flat_param[seg.lo:seg.hi], out.clone(), group=seg.group)
+        if fenced:
+            # every rank's peer stores of its updated shard must land before the
+            # parameters are read (or the gradients zeroed under a peer's loads)
+            for seg in self.segments:
+                if seg.n > 1 and self._fused(seg):
+                    self._fence(seg.group)
         self.zero_grad()
         return {"grad_norm": norm, "lr": lr}
+
+    # ------------------------------------------------------ fused DP path
+    def _fused(self, seg) -> bool:
+        return (self.symmetric is not None and not seg.expert and self.device.type == "cuda"
+                and self._flat_symm() is not None)
+
+    def _flat_symm(self):
+        return getattr(self.model.flat_param, "_symm", None)
+
+    def _fence(self, group) -> None:
+        x = torch.zeros(1, device=self.device)
+        dist.all_reduce(x, group=group)
+
+    def _peer_ptrs(self, buf, seg, param: bool = False) -> list[int]:
+        """Base addresses of every group rank's buffer (group-rank order) on this GPU."""
+        key = ("p" if param else "g", id(buf), id(seg.group))
+        cache = self.__dict__.setdefault("_ptr_cache", {})
+        if key not in cache:
+            cache[key] = [buf.ptrs[dist.get_global_rank(seg.group, r)] for r in range(seg.n)]
+        return cache[key]
 
     def current_lr(self) -> float:
         return self.scheduler.lr_at(max(0, self.step_count - 1))

@@ -15,7 +15,7 @@ import torch.distributed as dist
 
 from rl_b200.ops._ext import ext
 
-__all__ = ["SymmetricBuffer"]
+__all__ = ["SymmetricBuffer", "NodeSymmetric"]
 
 
 class SymmetricBuffer:
@@ -49,3 +49,56 @@ class SymmetricBuffer:
                 ext().symm_close(p)
         ext().symm_close(self.local_ptr)
         self.ptrs = []
+
+    def close_collective(self) -> None:
+        """Collective release: every rank unmaps its peers' buffers, all ranks
+        synchronise, then each frees its own allocation (no rank frees memory a
+        peer still maps)."""
+        for r, p in enumerate(self.ptrs):
+            if r != self.rank:
+                ext().symm_close(p)
+        torch.cuda.synchronize()
+        if self.world > 1:
+            dist.barrier(group=self.group)
+        ext().symm_close(self.local_ptr)
+        self.ptrs = []
+
+
+class NodeSymmetric:
+    """Allocator of symmetric buffers across every rank of a single-node job
+    (``group`` defaults to the world): ``ptrs`` are indexed by the group rank,
+    which for the world group is the global rank, so TP, DP and EP peers are
+    all addressable.  ``flat_alloc`` is the ``TransformerLM`` flat-buffer hook: the
+    returned tensor carries its ``SymmetricBuffer`` as ``tensor._symm``."""
+
+    def __init__(self, group=None):
+        self.group = group
+        self.buffers: list[SymmetricBuffer] = []
+
+    def alloc(self, nbytes: int) -> SymmetricBuffer:
+        b = SymmetricBuffer(nbytes, self.group)
+        self.buffers.append(b)
+        return b
+
+    def flat_alloc(self, numel: int, dtype: torch.dtype) -> torch.Tensor:
+        elt = torch.empty((), dtype=dtype).element_size()
+        b = self.alloc(numel * elt)
+        t = b.local_view(dtype, numel)
+        t._symm = b
+        return t
+
+    def release(self, buf: SymmetricBuffer) -> None:
+        if buf in self.buffers:
+            self.buffers.remove(buf)
+            buf.close_collective()
+
+    @staticmethod
+    def supported() -> bool:
+        """CUDA, initialised process group, every rank on this node."""
+        import os
+
+        if not (torch.cuda.is_available() and dist.is_initialized()):
+            return False
+        world = dist.get_world_size()
+        local = int(os.environ.get("LOCAL_WORLD_SIZE", world))
+        return world > 1 and local == world

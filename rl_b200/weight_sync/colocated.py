@@ -76,16 +76,14 @@ class ColocatedReshardSynchronizer(WeightSynchronizer):
     def _sync(self) -> int:
         nbytes = 0
         if self.native:
-            from rl_b200.ops._ext import add_launches, ext
+            from rl_b200.ops._ext import ext
 
             self._fence()
             if self._tasks is not None:
                 ext().refit_copy(self._tasks, self.gen_model.flat_param)
-                add_launches(1)
                 nbytes += self.gen_model.flat_param.numel() * 2
             if self._qtasks is not None:
                 ext().refit_quant_fp8(self._qtasks, self.q, self.scales, self.pow2)
-                add_launches(1)
                 nbytes += self.q.numel() + self.scales.numel() * 4
             # peers must finish reading this rank's shard before its next optimizer
             # step overwrites it; their next TP collective (in the next training

@@ -224,3 +224,61 @@ def test_refit_reshard_tp2_to_tp1_fp8_2gpu():
         assert o["q_mismatch"] == 0.0 and o["deq_err"] < 0.075, o
         assert o["launches"] == 2, o
     print("refit reshard (bf16 copy + fp8 quant):", f"{outs[0]['ms']:.3f} ms for {outs[0]['bytes'] / 2**20:.1f} MiB")
+
+
+def case_fused_dp_optimizer(rank: int, fused: bool):
+    """DP=2 training steps with the fused reduce-scatter / AdamW+all-gather
+    kernels (peer loads and stores) or with NCCL; returns what must agree."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.state import init_distributed
+    from tests.dist_cases import make_batch
+
+    ps = init_distributed(tp=1, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="dp", vocab_size=512, hidden_size=256, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=64, ffn_hidden_size=512, rope_theta=10000.0, max_position_embeddings=256)
+    pcfg = {"max_total_sequence_length": 32, "precision": "bfloat16", "train_global_batch_size": 8,
+            "optimizer": {"kwargs": {"lr": 1e-3, "weight_decay": 0.01}},
+            "megatron_cfg": {"fused_dp_optimizer": fused},
+            "generation": {"temperature": 1.0, "max_new_tokens": 4},
+            "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
+    w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=3)
+    used = w.optimizer._fused(w.optimizer.segments[0])
+    full = make_batch(B=8, S=24, vocab=512, seed=1)
+    shard = full.slice(rank * 4, rank * 4 + 4)
+    lf = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
+    res = [w.train(shard, lf, gbs=4) for _ in range(3)]
+    torch.cuda.synchronize()
+    flat = w.model.flat_param.float().cpu()
+    other = [torch.empty_like(w.model.flat_param) for _ in range(2)]
+    dist.all_gather(other, w.model.flat_param)
+    same = torch.equal(other[0], other[1])
+    w.shutdown()
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"used": used, "loss": [r["loss"] for r in res], "gn": [r["grad_norm"] for r in res], "flat": flat,
+            "same": same}
+
+
+def test_fused_dp_optimizer_matches_nccl_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    a = spawn_ranks(case_fused_dp_optimizer, 2, True, timeout_s=300)
+    b = spawn_ranks(case_fused_dp_optimizer, 2, False, timeout_s=300)
+    assert a[0]["used"] and not b[0]["used"]
+    for x, y in zip(a, b):
+        assert x["same"] and y["same"]  # every DP rank holds the same parameters after the all-gather
+        for la, lb in zip(x["loss"], y["loss"]):
+            assert abs(la - lb) < 1e-3 * max(1.0, abs(lb)), (x["loss"], y["loss"])
+        for ga, gb in zip(x["gn"], y["gn"]):
+            assert abs(ga - gb) < 1e-3 * max(1.0, gb), (x["gn"], y["gn"])
+        d = (x["flat"] - y["flat"]).abs().max().item()
+        assert d < 2e-2, d

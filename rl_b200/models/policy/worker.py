@@ -123,6 +123,22 @@ class PolicyWorker:
         self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
                                    sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt,
                                    num_labels=self.num_labels, flat_alloc=flat_alloc)
+        from rl_b200.models.lora import LoRAAdapters, LoRAConfig
+
+        lcfg = LoRAConfig(policy_cfg.get("lora_cfg") or mc.get("lora_cfg")
+                          or (policy_cfg.get("dtensor_cfg") or {}).get("lora_cfg"))
+        self.lora = None
+        opt_target = self.model
+        if lcfg.enabled:
+            # base weights frozen; the optimizer steps the adapters' flat buffer
+            for prm in self.model._params.values():
+                prm.requires_grad_(False)
+            self.lora = LoRAAdapters(self.model, lcfg, seed=seed)
+            self.model.lora = self.lora
+            opt_target = self.lora
+            fused_dp = False
+            if lcfg.restore_from:
+                self.lora.load_peft(lcfg.restore_from)
         opt = policy_cfg.get("optimizer", {}) or {}
         kw = dict(opt.get("kwargs", {}) or {})
         mopt = mc.get("optimizer", {}) or {}
@@ -132,7 +148,7 @@ class PolicyWorker:
         wd = float(kw.get("weight_decay", mopt.get("weight_decay", 0.0)))
         sched = policy_cfg.get("scheduler") if policy_cfg.get("scheduler") is not None else mc.get("scheduler")
         grad_group = self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group
-        self.optimizer = FlatAdamW(self.model, lr=lr, betas=tuple(float(b) for b in betas), eps=eps, weight_decay=wd,
+        self.optimizer = FlatAdamW(opt_target, lr=lr, betas=tuple(float(b) for b in betas), eps=eps, weight_decay=wd,
                                    max_grad_norm=policy_cfg.get("max_grad_norm", 1.0), scheduler_cfg=sched,
                                    min_lr=float(mopt.get("min_lr", 0.0)), dp_group=grad_group,
                                    tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel,
@@ -141,7 +157,11 @@ class PolicyWorker:
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
         self.gen_model = self.model
-        if resharded:
+        if self.lora is not None:
+            # rollout copy with the adapters merged in (same TP layout)
+            self.gen_model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype,
+                                           skip_init=True)
+        elif resharded:
             from rl_b200.parallel.state import single_process_state
 
             self.gen_model = TransformerLM(self.model_cfg, single_process_state(self.device), device=self.device,
@@ -154,7 +174,7 @@ class PolicyWorker:
             seed=seed * 7 + self.ps.dp_rank * 100003,
         )
         self.ref_flat: Optional[torch.Tensor] = None
-        if init_reference_model:
+        if init_reference_model and self.lora is None:
             self.ref_flat = self.model.flat_param.detach().clone()
         sp = policy_cfg.get("sequence_packing", {}) or {}
         self.train_mb_tokens = int(sp.get("train_mb_tokens", self.max_seq_len * int(policy_cfg.get("train_micro_batch_size", 4))))
@@ -172,8 +192,13 @@ class PolicyWorker:
         self.weight_sync.sync()  # the rollout copy starts from the initial weights
 
     def _make_weight_sync(self, resharded: bool):
-        from rl_b200.weight_sync.colocated import ColocatedInPlaceSynchronizer, ColocatedReshardSynchronizer
+        from rl_b200.weight_sync.colocated import (ColocatedInPlaceSynchronizer, ColocatedReshardSynchronizer,
+                                                   LoRAMergeSynchronizer)
 
+        if self.lora is not None:
+            if resharded:
+                raise NotImplementedError("LoRA with a different rollout TP layout")
+            return LoRAMergeSynchronizer(self.lora, self.gen_model)
         if not resharded:
             return ColocatedInPlaceSynchronizer()
         peer_ptrs = None
@@ -355,7 +380,15 @@ class PolicyWorker:
 
     @contextlib.contextmanager
     def use_reference_model(self):
-        """Swap the reference (initial) weights into the live parameter buffer."""
+        """Swap the reference (initial) weights into the live parameter buffer.
+        With LoRA the frozen base IS the reference: the adapters are switched off."""
+        if self.lora is not None:
+            self.lora.enabled = False
+            try:
+                yield
+            finally:
+                self.lora.enabled = True
+            return
         if self.ref_flat is None:
             raise RuntimeError("reference model was not initialised")
         flat = self.model.flat_param
@@ -558,10 +591,17 @@ class PolicyWorker:
         ``torch_dist``: per-rank shard files with layout metadata."""
         from rl_b200.models import checkpoint_io as cio
 
-        if fmt == "torch_dist":
+        if self.lora is not None:
+            # adapters only (PEFT layout); the frozen base is the model's own checkpoint
+            if self.ps.tp_size > 1:
+                raise NotImplementedError("saving LoRA adapters under TP > 1")
+            if (dist.get_rank() if dist.is_initialized() else 0) == 0:
+                self.lora.save_peft(weights_path)
+        elif fmt == "torch_dist":
             cio.save_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
             return
-        cio.save_hf_checkpoint(self.model, weights_path)
+        else:
+            cio.save_hf_checkpoint(self.model, weights_path)
         if optimizer_path is not None:
             os.makedirs(optimizer_path, exist_ok=True)
             rank = dist.get_rank() if dist.is_initialized() else 0
@@ -569,6 +609,19 @@ class PolicyWorker:
 
     def load_checkpoint(self, weights_path: str, optimizer_path: Optional[str] = None) -> None:
         from rl_b200.models import checkpoint_io as cio
+
+        if self.lora is not None:
+            self.lora.load_peft(weights_path)
+            rank = dist.get_rank() if dist.is_initialized() else 0
+            opt_file = os.path.join(optimizer_path, f"__{rank}.pt") if optimizer_path else None
+            if opt_file and os.path.exists(opt_file):
+                self.optimizer.load_state_dict(torch.load(opt_file, map_location="cpu"))
+            else:
+                with torch.no_grad():
+                    for seg in self.optimizer.segments:
+                        seg.master.copy_(self.lora.flat_param[seg.s_lo:seg.s_hi])
+            self.weight_sync.sync()
+            return
 
         if os.path.isdir(os.path.join(weights_path, "iter_0000000")):
             cio.load_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)

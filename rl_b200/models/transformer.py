@@ -43,7 +43,7 @@ from rl_b200.ops.linear import linear
 from rl_b200.ops.norm import add_rms_norm, rms_norm
 from rl_b200.ops.rope import apply_rope_qkv, build_rope_cache
 from rl_b200.parallel.comm import (all_to_all_autograd, copy_to_tp, gather_from_sp, reduce_from_tp,
-                                   reduce_scatter_to_sp)
+                                   reduce_scatter_to_sp, scatter_to_sp)
 from rl_b200.parallel.state import ParallelState, single_process_state
 
 __all__ = ["TransformerLM", "ParamSpec", "KVCache"]
@@ -59,6 +59,9 @@ class ParamSpec:
     offset: int = 0
     numel: int = 0
     no_weight_decay: bool = False
+    # gradient reduction over TP: None = default rule (replicated params are
+    # all-reduced under sequence parallelism), "tp_sum" = always, "none" = never
+    grad_reduce: Optional[str] = None
 
 
 class KVCache:
@@ -185,6 +188,7 @@ class TransformerLM(nn.Module):
         # fused compute+collective kernels for TP + SP (GEMM -> reduce-scatter over NVLink)
         self.fused_collectives = True
         self._fused_rs = None
+        self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
         self.router_record: Optional[dict] = None
 
@@ -326,7 +330,7 @@ class TransformerLM(nn.Module):
     # -------------------------------------------------------------- attention
     def _qkv(self, i: int, h: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
         p = f"model.layers.{i}."
-        qkv = linear(h, self._params[p + "self_attn.qkv_proj.weight"])
+        qkv = self._col_linear(h, p + "self_attn.qkv_proj.weight")
         if self.cfg.qk_norm:
             T = qkv.shape[0]
             q, k, v = torch.split(qkv, [self.nq * self.hd, self.nkv * self.hd, self.nkv * self.hd], -1)
@@ -351,7 +355,17 @@ class TransformerLM(nn.Module):
         qkv = self._qkv(i, h, positions)
         q, k, v = self._split_heads(qkv)
         o = flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=True)
-        return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"])
+        return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
+                                         p + "self_attn.o_proj.weight")
+
+    def _col_linear(self, h: torch.Tensor, name: str) -> torch.Tensor:
+        """Column-parallel projection (+ LoRA delta when adapters are attached)."""
+        y = linear(h, self._params[name])
+        if self.lora is not None:
+            d = self.lora.delta(name, h)
+            if d is not None:
+                y = y + d
+        return y
 
     def _row_parallel_out(self, out: torch.Tensor) -> torch.Tensor:
         if self.ps.tp_size == 1:
@@ -360,11 +374,23 @@ class TransformerLM(nn.Module):
             return reduce_scatter_to_sp(out, self.ps.tp_group)
         return reduce_from_tp(out, self.ps.tp_group)
 
-    def _row_parallel_linear(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+    def _row_parallel_linear(self, x: torch.Tensor, w: torch.Tensor, name: Optional[str] = None) -> torch.Tensor:
         """Row-parallel projection.  With TP + SP on CUDA the GEMM and its
         reduce-scatter run as ONE fused tcgen05 kernel writing peer tiles over
-        NVLink (``rl_b200.parallel.fused``); otherwise GEMM then the collective."""
+        NVLink (``rl_b200.parallel.fused``); otherwise GEMM then the collective.
+        A LoRA adapter's low-rank product is reduced over TP at rank r (tiny)
+        and its full output added after the base reduction."""
         tp = self.ps.tp_size
+        if self.lora is not None and self.lora.enabled and name in self.lora.layers:
+            an, bn = self.lora.layers[name]
+            base = self._row_parallel_out(linear(x, w))
+            h = linear(x, self.lora._params[an])
+            if tp > 1:
+                h = reduce_from_tp(h, self.ps.tp_group)
+            y = linear(h, self.lora._params[bn]) * self.lora.scale
+            if self.sequence_parallel:
+                y = scatter_to_sp(y, self.ps.tp_group)
+            return base + y
         if (tp > 1 and self.sequence_parallel and self.fused_collectives and x.is_cuda
                 and x.dtype == torch.bfloat16 and x.shape[0] % (128 * tp) == 0 and w.shape[0] % 32 == 0):
             from rl_b200.parallel.fused import GemmReduceScatter, row_parallel_rs
@@ -385,9 +411,9 @@ class TransformerLM(nn.Module):
             h = gather_from_sp(h, self.ps.tp_group)
         else:
             h = copy_to_tp(h, self.ps.tp_group)
-        gu = linear(h, self._params[p + "mlp.gate_up_proj.weight"])
+        gu = self._col_linear(h, p + "mlp.gate_up_proj.weight")
         a = swiglu(gu)
-        return self._row_parallel_linear(a, self._params[p + "mlp.down_proj.weight"])
+        return self._row_parallel_linear(a, self._params[p + "mlp.down_proj.weight"], p + "mlp.down_proj.weight")
 
     def route(self, i: int, h: torch.Tensor):
         """Router: fp32 logits -> softmax -> top-k (+ renormalisation); returns

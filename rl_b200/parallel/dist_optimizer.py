@@ -253,10 +253,13 @@ class FlatAdamW:
         self.ensure_grad_buffer()
         self._fold_param_grads()
         m = self.model
-        if self.sequence_parallel and self.tp > 1:
-            # replicated params saw different tokens on each TP rank under SP
+        if self.tp > 1:
             for sp, p in m.named_flat_params():
-                if sp.tp_dim is None and sp.ep_dim is None:
+                mode = getattr(sp, "grad_reduce", None)
+                # replicated params saw different tokens on each TP rank under SP;
+                # some (LoRA A of column-parallel layers) hold partial sums always
+                if mode == "tp_sum" or (mode is None and self.sequence_parallel and sp.tp_dim is None
+                                        and sp.ep_dim is None):
                     dist.all_reduce(p.main_grad, group=self.tp_group)
         sq_total = torch.zeros((), dtype=torch.float32, device=self.device)
         for seg in self.segments:

@@ -12,7 +12,25 @@ from rl_b200.weight_sync.interfaces import WeightSynchronizer
 from rl_b200.weight_sync.reshard import (apply_regions_reference, build_regions, copy_tasks, quant_layout,
                                          quant_regions_reference, quant_tasks)
 
-__all__ = ["ColocatedInPlaceSynchronizer", "ColocatedReshardSynchronizer"]
+__all__ = ["ColocatedInPlaceSynchronizer", "ColocatedReshardSynchronizer", "LoRAMergeSynchronizer"]
+
+
+class LoRAMergeSynchronizer:
+    """LoRA training: the rollout copy holds base + scale * B A (merged once per
+    refit, so decode runs plain GEMMs)."""
+    name = "lora_merge"
+
+    def __init__(self, lora, gen_model):
+        self.lora, self.gen_model = lora, gen_model
+        self.version = 0
+
+    def sync(self) -> dict:
+        self.lora.merged_into(self.gen_model)
+        self.version += 1
+        return {"version": self.version}
+
+    def shutdown(self) -> None:
+        pass
 
 
 class ColocatedInPlaceSynchronizer(WeightSynchronizer):

@@ -17,7 +17,7 @@ from typing import Optional
 
 import torch
 
-from rl_b200.algorithms.loss.loss_functions import DPOLossFn, PreferenceLossFn
+from rl_b200.algorithms.loss.loss_functions import DPOLossFn, MPOLossFn, PreferenceLossFn
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
 
 __all__ = ["preference_batch", "add_ref_logprobs_to_data", "dpo_train", "rm_train"]
@@ -55,10 +55,17 @@ def _collate_pref(batch) -> list[dict]:
     return [dict(prompt=p, chosen=c, rejected=r) for p, c, r in zip(batch["prompt"], batch["chosen"], batch["rejected"])]
 
 
+def mpo_train(policy, train_dataloader, master_config: dict, **kw) -> dict:
+    """MPO = the DPO loop with ``MPOLossFn`` (reference ``nemo_rl/algorithms/mpo.py:217``)."""
+    return dpo_train(policy, train_dataloader, {**master_config, "mpo": master_config.get("mpo", {})}, **kw)
+
+
 def dpo_train(policy, train_dataloader, master_config: dict, logger=None, checkpointer=None, save_state=None,
               max_steps: Optional[int] = None, step_callback=None) -> dict:
-    cfg = master_config.get("dpo", {})
-    loss_fn = DPOLossFn(cfg)
+    cfg = master_config.get("dpo", master_config.get("mpo", {}))
+    loss_cfg = {**cfg, **(master_config.get("loss_fn") or {})}
+    loss_fn = MPOLossFn(loss_cfg) if (master_config.get("mpo") is not None or cfg.get("bco_loss_weight")) \
+        else DPOLossFn(loss_cfg)
     max_steps = int(max_steps if max_steps is not None else cfg.get("max_num_steps", 10 ** 9))
     state = dict(save_state or {"current_step": 0, "current_epoch": 0})
     step = int(state["current_step"])
@@ -68,9 +75,14 @@ def dpo_train(policy, train_dataloader, master_config: dict, logger=None, checkp
                 return state
             data = add_ref_logprobs_to_data(policy, preference_batch(_collate_pref(batch)))
             res = policy.train(data, loss_fn, gbs=data.size, pair_rows=True)
+            if isinstance(loss_fn, MPOLossFn):
+                # one EMA update per step from the globally summed BCO rewards
+                state["reward_shift"] = loss_fn.update_reward_shift(res.get("bco_reward_sum", 0.0),
+                                                                    res.get("bco_reward_count", 0.0))
             step += 1
             state["current_step"] = step
-            metrics = {k: res[k] for k in ("loss", "grad_norm", "lr", "accuracy", "preference_loss") if k in res}
+            metrics = {k: res[k] for k in ("loss", "grad_norm", "lr", "accuracy", "preference_loss", "bco_loss")
+                       if k in res}
             if logger:
                 logger.log_metrics(metrics, step, prefix="train")
             if step_callback:

@@ -358,6 +358,55 @@ class DPOLossFn:
         }
 
 
+class MPOLossFn(DPOLossFn):
+    """Mixed preference optimisation: DPO preference term + chosen-response SFT
+    term + BCO quality term ``-log sigma(r_c - delta) - log sigma(-(r_r - delta))``
+    with ``r = beta * log(pi / pi_ref)`` per sequence and a reward shift ``delta``
+    kept as an EMA of the mean reward.
+
+    Reference: ``MPOLossFn`` (``nemo_rl/algorithms/loss/loss_functions.py:1821``).  As
+    there, the loss never mutates ``reward_shift`` itself: it reports
+    ``bco_reward_sum`` / ``bco_reward_count`` (summed over micro-batches and DP),
+    and the training loop calls ``update_reward_shift`` once per step, so every
+    rank applies the same shift."""
+
+    def __init__(self, cfg: Optional[dict] = None):
+        cfg = cfg or {}
+        super().__init__(cfg)
+        self.bco_loss_weight = float(cfg.get("bco_loss_weight", 1.0))
+        self.quality_average_log_probs = bool(cfg.get("quality_average_log_probs", False))
+        self.reward_shift_momentum = float(cfg.get("reward_shift_momentum", 0.9))
+        self.reward_shift = float(cfg.get("reward_shift", 0.0))
+        if not 0.0 <= self.reward_shift_momentum < 1.0:
+            raise ValueError("reward_shift_momentum must be in [0, 1)")
+
+    def update_reward_shift(self, reward_sum: float, reward_count: float) -> float:
+        if reward_count > 0:
+            m = self.reward_shift_momentum
+            self.reward_shift = m * self.reward_shift + (1.0 - m) * reward_sum / reward_count
+        return self.reward_shift
+
+    def __call__(self, next_token_logprobs, data, global_valid_seqs, global_valid_toks, **kwargs):
+        loss, metrics = super().__call__(next_token_logprobs, data, global_valid_seqs, global_valid_toks)
+        mask = data["token_mask"][:, 1:].to(next_token_logprobs.dtype) * data["sample_mask"].unsqueeze(-1)
+        ref = data["reference_policy_logprobs"][:, 1:].to(next_token_logprobs.dtype)
+        q = self.beta * _seq_logprob(next_token_logprobs - ref, mask, self.quality_average_log_probs)
+        smask = data["sample_mask"].to(q.dtype)
+        c_mask, r_mask = smask[0::2], smask[1::2]
+        n_pairs = global_valid_seqs / 2
+        delta = torch.as_tensor(self.reward_shift, dtype=q.dtype, device=q.device)
+        bco = (masked_mean(-F.logsigmoid(q[0::2] - delta), c_mask, global_normalization_factor=n_pairs)
+               + masked_mean(-F.logsigmoid(-(q[1::2] - delta)), r_mask, global_normalization_factor=n_pairs))
+        loss = loss + self.bco_loss_weight * bco
+        metrics.update({
+            "loss": _m(loss.detach()),
+            "bco_loss": _m(bco.detach()),
+            "bco_reward_sum": _m((q.detach() * smask).sum()),
+            "bco_reward_count": _m(smask.sum()),
+        })
+        return loss, metrics
+
+
 class PreferenceLossFn:
     """Bradley-Terry reward-model loss over scalar rewards of (chosen, rejected) pairs."""
 

@@ -339,6 +339,17 @@ def test_dpo_and_rm_loops():
     rm_train(rm, StatefulDataLoader(PreferenceDataset(samples), 4, shuffle=False, collate_fn=lambda b: b),
              {"rm": {"max_num_epochs": 3}}, step_callback=lambda s, m: out.append(m))
     assert len(out) == 6 and out[-1]["loss"] < out[0]["loss"] + 1e-6
+    # MPO: DPO + SFT + BCO with a driver-side reward-shift EMA
+    from rl_b200.algorithms.dpo import mpo_train
+
+    out = []
+    st = mpo_train(_tiny_policy(), StatefulDataLoader(PreferenceDataset(samples), 4, shuffle=False,
+                                                      collate_fn=lambda b: b),
+                   {"mpo": {"max_num_epochs": 1, "reference_policy_kl_penalty": 0.1, "sft_loss_weight": 0.5,
+                            "bco_loss_weight": 1.0, "reward_shift_momentum": 0.5}},
+                   step_callback=lambda s, m: out.append(m))
+    assert len(out) == 2 and all(math.isfinite(m["loss"]) and "bco_loss" in m for m in out)
+    assert "reward_shift" in st and math.isfinite(st["reward_shift"])
 
 
 def test_ppo_and_distillation_loops():

@@ -393,3 +393,18 @@ def test_flops_formula_and_mfu():
     tr.track([1024, 512])
     assert tr.model_train_flops() == 3 * forward_flops(cfg, [1024, 512])
     assert abs(mfu(2250e12, 1.0, 1, device="B200") - 1.0) < 1e-9
+
+
+def test_eval_pass_and_cons_at_k():
+    from rl_b200.evals.eval import eval_cons_k, eval_pass_k
+
+    r = torch.tensor([1.0, 0.0, 0.0, 0.0, 1.0, 1.0, 0.0, 0.0])
+    # group 1: n=4, c=1 -> pass@2 = 1 - C(3,2)/C(4,2) = 0.5; group 2: c=2 -> 1 - C(2,2)/C(4,2) = 5/6
+    assert abs(eval_pass_k(r, 4, 2) - (0.5 + 5 / 6)) < 1e-9
+    assert eval_pass_k(r, 4, 4) == 2.0
+    ans = ["a", "b", "b", "c", "x", "x", "y", "x"]
+    r2 = torch.tensor([0.0, 1.0, 1.0, 0.0, 1.0, 1.0, 0.0, 1.0])
+    # group 1: majority of all 4 is "b" (rewarded): cons@4 = 1; group 2: "x" rewarded -> 1
+    assert eval_cons_k(r2, 4, 4, ans) == 2.0
+    # cons@1 = mean reward of the group
+    assert abs(eval_cons_k(r2, 4, 1, ans) - (0.5 + 0.75)) < 1e-9

@@ -51,6 +51,8 @@ void symm_close(int64_t ptr);
 at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
 void refit_copy(at::Tensor tasks, at::Tensor dst);
 at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
+at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n, int64_t me, int64_t epoch);
+void stream_write_u32(int64_t ptr, int64_t value);
 at::Tensor dp_reduce_shard(std::vector<int64_t> grad_ptrs, int64_t lo, int64_t len, at::Tensor out);
 void dp_adam_allgather(std::vector<int64_t> param_ptrs, int64_t lo, at::Tensor master, at::Tensor grad,
                        at::Tensor exp_avg, at::Tensor exp_avg_sq, at::Tensor nodecay, double lr, double b1, double b2,
@@ -89,6 +91,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_view", &symm_view);
   m.def("dp_reduce_shard", &dp_reduce_shard, "DP gradient reduce-scatter over NVLink peer loads (+ norm partials)");
   m.def("dp_adam_allgather", &dp_adam_allgather, "sharded AdamW fused with the parameter all-gather (peer stores)");
+  m.def("gemm_ag", &gemm_ag, "all-gather -> GEMM: waits per gathered shard (copy-engine transfers) on device flags");
+  m.def("stream_write_u32", &stream_write_u32, "stream memory write (no kernel) of a 32-bit word");
   m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
   m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);
   m.def("refit_copy", &refit_copy, "train->rollout reshard (bf16) reading peer shards over NVLink");

@@ -70,6 +70,10 @@ struct RSArgs {
   uint32_t* flags[8];       // per rank: [2][n][tiles_per_shard] u32 (data-ready, written by producers)
   uint32_t* acks[8];        // per rank: [2][n] u32 slot-free words (written by consumers) + [2] local counters
   __nv_bfloat16* out;       // this rank's [Ms, N] output
+  // all-gather -> GEMM (EPI == 2): A is the gathered [n*Ms, K] input whose shard j
+  // is ready once shard_flags[j] >= epoch; tiles visit the own shard first, then
+  // the others in ring order (the order their copies land)
+  const uint32_t* shard_flags;
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -137,6 +141,13 @@ gemm_nt_kernel_t(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
   auto coords = [&](int tile, int& mt, int& nt, int& dest, int& within) {
     if constexpr (EPI == 1) {
       rs_tile_coords(tile, num_n, mts, rs, dest, mt, nt, within);
+    } else if constexpr (EPI == 2) {
+      int mo;
+      tile_coords(tile, num_m, num_n, mo, nt);
+      const int per = rs.Ms / BM;
+      dest = (rs.me + mo / per) % rs.n;  // source shard of this m-tile
+      mt = dest * per + mo % per;
+      within = 0;
     } else {
       tile_coords(tile, num_m, num_n, mt, nt);
       dest = 0;
@@ -172,6 +183,12 @@ gemm_nt_kernel_t(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
       for (int tile = blockIdx.x; tile < num_tiles && !*abort_flag; tile += gridDim.x) {
         int mt, nt, dest, within;
         coords(tile, mt, nt, dest, within);
+        if constexpr (EPI == 2) {
+          // the copy engine lands shard `dest` and then writes its flag (stream
+          // memory op); order the TMA reads of that shard after the flag
+          if (!wait_flag(rs.shard_flags + dest, rs.epoch, abort_flag)) break;
+          asm volatile("fence.proxy.async.global;\n" ::: "memory");
+        }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
@@ -439,4 +456,48 @@ int64_t gemm_error_flag(bool reset) {
     RLB_CUDA_CHECK(cudaMemcpyToSymbol(tc::g_error, &z, sizeof(int)));
   }
   return v;
+}
+
+// All-gather -> GEMM: out [M, N] = gathered [M, K] x b [N, K]^T where the rows of
+// shard j (M / n rows each) become valid when shard_flags[j] >= epoch.  The
+// gathered rows are written by copy-engine transfers from the peers' symmetric
+// buffers on a side stream (rl_b200/parallel/fused.py), each followed by a
+// stream write of its shard flag; the kernel starts on the own shard at once
+// and waits (bounded) per remote shard, so the transfers overlap the MMA work.
+at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n, int64_t me, int64_t epoch) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16,
+              "rl_b200 gemm_ag: bf16 CUDA operands expected");
+  TORCH_CHECK(a.is_contiguous() && b.is_contiguous() && a.size(1) == b.size(1), "rl_b200 gemm_ag: a [M,K], b [N,K]");
+  TORCH_CHECK(shard_flags.is_cuda() && shard_flags.scalar_type() == at::kInt && shard_flags.numel() >= n,
+              "rl_b200 gemm_ag: int32 shard flags on the device");
+  const int M = a.size(0), N = b.size(0), K = a.size(1);
+  TORCH_CHECK(n >= 1 && n <= 8 && me >= 0 && me < n && M % (n * tc::BM) == 0,
+              "rl_b200 gemm_ag: M must be a multiple of 128 * ranks");
+  TORCH_CHECK(K % 8 == 0 && epoch >= 1, "rl_b200 gemm_ag: K % 8 == 0, epoch >= 1");
+  const c10::cuda::CUDAGuard guard(a.device());
+  auto c = at::empty({M, N}, a.options());
+  tc::RSArgs ag{};
+  ag.n = (int)n;
+  ag.me = (int)me;
+  ag.Ms = M / (int)n;
+  ag.epoch = (uint32_t)epoch;
+  ag.shard_flags = reinterpret_cast<const uint32_t*>(shard_flags.data_ptr<int>());
+  if (N >= 256) launch_gemm<256, 4, 2>(a, b, (__nv_bfloat16*)c.data_ptr(), M, N, K, ag);
+  else launch_gemm<128, 6, 2>(a, b, (__nv_bfloat16*)c.data_ptr(), M, N, K, ag);
+  return c;
+}
+
+// Stream memory write of a 32-bit word (executed by the stream front end, no
+// kernel): signals data landed by an earlier copy on the same stream.
+void stream_write_u32(int64_t ptr, int64_t value) {
+  static PFN_cuStreamWriteValue32_v11070 fn = nullptr;
+  if (fn == nullptr) {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    RLB_CUDA_CHECK(cudaGetDriverEntryPointByVersion("cuStreamWriteValue32", &p, 11070, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p != nullptr, "rl_b200: cuStreamWriteValue32 unavailable");
+    fn = reinterpret_cast<PFN_cuStreamWriteValue32_v11070>(p);
+  }
+  CUresult r = fn(reinterpret_cast<CUstream>(stream()), (CUdeviceptr)ptr, (cuuint32_t)value, 0);
+  TORCH_CHECK(r == CUDA_SUCCESS, "rl_b200: cuStreamWriteValue32 failed (", (int)r, ")");
 }

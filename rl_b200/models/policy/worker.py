@@ -644,9 +644,10 @@ class PolicyWorker:
         self.engine.finish_generation()
         self.engine._drop_graphs()
         self.engine._kv_sig = None
-        if getattr(self.model, "_fused_rs", None) is not None:
-            self.model._fused_rs.close()
-            self.model._fused_rs = None
+        for attr in ("_fused_rs", "_fused_ag"):
+            if getattr(self.model, attr, None) is not None:
+                getattr(self.model, attr).close()
+                setattr(self.model, attr, None)
         self.weight_sync.shutdown()
 
     def offload_before_refit(self) -> None:

@@ -188,6 +188,7 @@ class TransformerLM(nn.Module):
         # fused compute+collective kernels for TP + SP (GEMM -> reduce-scatter over NVLink)
         self.fused_collectives = True
         self._fused_rs = None
+        self._fused_ag = None
         self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
         self.router_record: Optional[dict] = None
@@ -328,9 +329,12 @@ class TransformerLM(nn.Module):
         return self._params["lm_head.weight"]
 
     # -------------------------------------------------------------- attention
-    def _qkv(self, i: int, h: torch.Tensor, positions: torch.Tensor) -> torch.Tensor:
+    def _qkv(self, i: int, h: torch.Tensor, positions: torch.Tensor, qkv: Optional[torch.Tensor] = None
+             ) -> torch.Tensor:
+        """QKV projection (unless ``qkv`` is given), optional q/k RMSNorm, RoPE."""
         p = f"model.layers.{i}."
-        qkv = self._col_linear(h, p + "self_attn.qkv_proj.weight")
+        if qkv is None:
+            qkv = self._col_linear(h, p + "self_attn.qkv_proj.weight")
         if self.cfg.qk_norm:
             T = qkv.shape[0]
             q, k, v = torch.split(qkv, [self.nq * self.hd, self.nkv * self.hd, self.nkv * self.hd], -1)
@@ -346,13 +350,33 @@ class TransformerLM(nn.Module):
         x = qkv.view(T, self.nq + 2 * self.nkv, self.hd)
         return x[:, : self.nq], x[:, self.nq: self.nq + self.nkv], x[:, self.nq + self.nkv:]
 
+    def _fused_ag_ok(self, h: torch.Tensor) -> bool:
+        return (self.ps.tp_size > 1 and self.sequence_parallel and self.fused_collectives and h.is_cuda
+                and h.dtype == torch.bfloat16 and h.shape[0] % 128 == 0 and self.lora is None)
+
+    def _ag_linear(self, h_shard: torch.Tensor, name: str) -> torch.Tensor:
+        """Column-parallel projection of the SP-sharded input with the all-gather
+        fused into the GEMM (``rl_b200.parallel.fused.AllGatherGemm``)."""
+        from rl_b200.parallel.fused import AllGatherGemm, column_parallel_ag
+
+        op = self._fused_ag
+        if op is None or op.ms_max < h_shard.shape[0] or op.K != h_shard.shape[1]:
+            if op is not None:
+                op.close()
+            op = self._fused_ag = AllGatherGemm(self.ps.tp_group, max(h_shard.shape[0] * self.ps.tp_size, 16384),
+                                                h_shard.shape[1])
+        return column_parallel_ag(h_shard, self._params[name], op)
+
     def _attn_block(self, i: int, h: torch.Tensor, positions, cu_seqlens, max_seqlen) -> torch.Tensor:
         p = f"model.layers.{i}."
-        if self.sequence_parallel:
-            h = gather_from_sp(h, self.ps.tp_group)
+        if self._fused_ag_ok(h):
+            qkv = self._qkv(i, None, positions, qkv=self._ag_linear(h, p + "self_attn.qkv_proj.weight"))
         else:
-            h = copy_to_tp(h, self.ps.tp_group)
-        qkv = self._qkv(i, h, positions)
+            if self.sequence_parallel:
+                h = gather_from_sp(h, self.ps.tp_group)
+            else:
+                h = copy_to_tp(h, self.ps.tp_group)
+            qkv = self._qkv(i, h, positions)
         q, k, v = self._split_heads(qkv)
         o = flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=True)
         return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
@@ -407,11 +431,14 @@ class TransformerLM(nn.Module):
         if self.cfg.is_moe:
             return self._moe_block(i, h)
         p = f"model.layers.{i}."
-        if self.sequence_parallel:
-            h = gather_from_sp(h, self.ps.tp_group)
+        if self._fused_ag_ok(h):
+            gu = self._ag_linear(h, p + "mlp.gate_up_proj.weight")
         else:
-            h = copy_to_tp(h, self.ps.tp_group)
-        gu = self._col_linear(h, p + "mlp.gate_up_proj.weight")
+            if self.sequence_parallel:
+                h = gather_from_sp(h, self.ps.tp_group)
+            else:
+                h = copy_to_tp(h, self.ps.tp_group)
+            gu = self._col_linear(h, p + "mlp.gate_up_proj.weight")
         a = swiglu(gu)
         return self._row_parallel_linear(a, self._params[p + "mlp.down_proj.weight"], p + "mlp.down_proj.weight")
 

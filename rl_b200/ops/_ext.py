@@ -32,6 +32,7 @@ _KERNELS_PER_CALL = {
     "sample": 2,
     "gemm_error_flag": 0,
     "gemm_decode_error_flag": 0,
+    "stream_write_u32": 0,
     "symm_alloc": 0,
     "symm_open": 0,
     "symm_close": 0,

@@ -21,7 +21,7 @@ import torch.distributed as dist
 from rl_b200.ops._ext import ext
 from rl_b200.parallel.symm import SymmetricBuffer
 
-__all__ = ["GemmReduceScatter", "row_parallel_rs"]
+__all__ = ["GemmReduceScatter", "row_parallel_rs", "AllGatherGemm", "column_parallel_ag"]
 
 
 class _RowParallelRS(torch.autograd.Function):
@@ -95,3 +95,119 @@ class GemmReduceScatter:
     def close(self) -> None:
         for b in (self.recv, self.flags, self.acks):
             b.close()
+
+
+class _ColumnParallelAG(torch.autograd.Function):
+    """y = AG(x_shard) @ w^T with the all-gather overlapped inside the GEMM;
+    backward: input gradient GEMM then NCCL reduce-scatter to the shard, weight
+    gradient into main_grad from the gathered input."""
+
+    @staticmethod
+    def forward(ctx, x, w, op):
+        y, gathered = op(x, w)
+        ctx.save_for_backward(gathered, w)
+        ctx.op = op
+        return y
+
+    @staticmethod
+    def backward(ctx, dy):
+        from rl_b200.ops import gemm as _gemm
+
+        g, w = ctx.saved_tensors
+        op = ctx.op
+        dy = dy.contiguous()
+        dx = None
+        if ctx.needs_input_grad[0]:
+            full = _gemm.mm_nn(dy, w)
+            dx = torch.empty((full.shape[0] // op.n, full.shape[1]), dtype=full.dtype, device=full.device)
+            dist.reduce_scatter_tensor(dx, full, group=op.group)
+        dw = None
+        if ctx.needs_input_grad[1]:
+            main = getattr(w, "main_grad", None)
+            if main is not None:
+                _gemm.mm_tn_accumulate(dy, g, main)
+            else:
+                dw = _gemm.mm_tn(dy, g).to(w.dtype)
+        return dx, dw, None
+
+
+def column_parallel_ag(x: torch.Tensor, w: torch.Tensor, op: "AllGatherGemm") -> torch.Tensor:
+    return _ColumnParallelAG.apply(x, w, op)
+
+
+class AllGatherGemm:
+    """``y = all_gather_rows(x_shard) @ w^T`` over the ranks of ``group`` (one
+    node): the column-parallel linear of tensor parallelism with sequence
+    parallelism, in which the gather overlaps the GEMM.
+
+    Each call publishes this rank's shard into a symmetric slot (double-buffered
+    by epoch parity) and fences the group (tiny NCCL all-reduce: every rank has
+    published); then a side stream pulls every peer's shard with copy-engine
+    transfers over NVLink into the local gathered buffer and, after each, writes
+    that shard's flag with a stream memory op (no kernel, so the side stream
+    never waits for an SM the GEMM holds).  The tcgen05 GEMM
+    (``csrc/gemm_tcgen05.cu``, ``EPI=2``) starts on the own rows at once and waits
+    on a remote shard's flag only when it reaches that shard's tiles.  No SM
+    work is spent on the transfer and every remote byte crosses NVLink once.
+    A slot is rewritten two calls later, after the next call's fence, which
+    every peer enters only after its transfers of this call completed, so a
+    slot is never overwritten while a peer still reads it."""
+
+    BM = 128
+
+    def __init__(self, group, max_rows: int, k: int):
+        self.group = group
+        self.n = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        self.K = int(k)
+        unit = self.BM * self.n
+        self.max_rows = (int(max_rows) + unit - 1) // unit * unit
+        self.ms_max = self.max_rows // self.n
+        self.slots = SymmetricBuffer(2 * self.ms_max * self.K * 2, group)
+        self.flags = torch.zeros(max(self.n, 4), dtype=torch.int32, device="cuda")
+        self.side = torch.cuda.Stream()
+        self.epoch = 0
+        self._fence_buf = torch.zeros(1, device="cuda")
+
+    def __call__(self, x: torch.Tensor, w: torch.Tensor):
+        ms = x.shape[0]
+        if ms % self.BM or ms > self.ms_max or x.shape[1] != self.K:
+            raise ValueError(f"shard rows {ms} must be a multiple of {self.BM} and <= {self.ms_max}")
+        x = x.contiguous()
+        M = ms * self.n
+        self.epoch += 1
+        par = self.epoch & 1
+        e = ext()
+        main = torch.cuda.current_stream()
+        slot_bytes = self.ms_max * self.K * 2
+        mine = self.slots.local_view(torch.bfloat16, ms * self.K, offset_bytes=par * slot_bytes).view(ms, self.K)
+        mine.copy_(x)
+        gathered = torch.empty((M, self.K), dtype=x.dtype, device=x.device)
+        gathered[self.me * ms:(self.me + 1) * ms].copy_(x)
+        e.stream_write_u32(self.flags.data_ptr() + 4 * self.me, self.epoch)
+        # every rank has published `mine` (and, a call earlier, finished reading the
+        # slot this publish reused).  The fence is a kernel, so it runs here, before
+        # the GEMM, never behind it: the side stream below needs no SM at all
+        dist.all_reduce(self._fence_buf, group=self.group)
+        self.side.wait_stream(main)
+        with torch.cuda.stream(self.side):
+            for j in range(1, self.n):
+                src = (self.me + j) % self.n
+                peer = self.slots.ptrs[src] + par * slot_bytes
+                _copy_from_ptr(gathered[src * ms:(src + 1) * ms], peer)
+                e.stream_write_u32(self.flags.data_ptr() + 4 * src, self.epoch)
+        gathered.record_stream(self.side)
+        y = e.gemm_ag(gathered, w.contiguous(), self.flags, self.n, self.me, self.epoch)
+        # later work of this stream (the next publish) runs after the transfers
+        main.wait_stream(self.side)
+        return y, gathered
+
+    def close(self) -> None:
+        self.slots.close()
+
+
+def _copy_from_ptr(dst: torch.Tensor, src_ptr: int) -> None:
+    """Copy-engine transfer of ``dst.numel()`` bf16 elements from a (peer) device
+    address into ``dst`` on the current stream."""
+    src = ext().symm_view(src_ptr, dst.numel(), 15, dst.device.index)
+    dst.view(-1).copy_(src, non_blocking=True)

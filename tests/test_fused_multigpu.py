@@ -112,9 +112,10 @@ def case_tp_sp_model(rank: int, T: int):
         (h.float() * proj).sum().backward()
         torch.cuda.synchronize()
         grads = {n: p.grad.float().clone() for n, p in m._params.items() if p.grad is not None}
-        res[fused] = (h.float().clone(), grads, m._fused_rs is not None)
-        if m._fused_rs is not None:
-            m._fused_rs.close()
+        res[fused] = (h.float().clone(), grads, m._fused_rs is not None and m._fused_ag is not None)
+        for op in (m._fused_rs, m._fused_ag):
+            if op is not None:
+                op.close()
     h0, g0, _ = res[False]
     h1, g1, used = res[True]
     errs = {"hidden": ((h1 - h0).norm() / h0.norm()).item()}
@@ -133,7 +134,7 @@ def test_tp_sp_model_fused_rs_2gpu():
 
     outs = spawn_ranks(case_tp_sp_model, 2, 1024, timeout_s=300)
     for o in outs:
-        assert o["used"], "fused GEMM+RS path was not taken"
+        assert o["used"], "fused GEMM+RS / AG+GEMM paths were not taken"
         assert o["flag"] == 0
         assert not o["missing"], o["missing"]
         worst = max(o["errs"].items(), key=lambda kv: kv[1])
@@ -282,3 +283,77 @@ def test_fused_dp_optimizer_matches_nccl_2gpu():
             assert abs(ga - gb) < 1e-3 * max(1.0, gb), (x["gn"], y["gn"])
         d = (x["flat"] - y["flat"]).abs().max().item()
         assert d < 2e-2, d
+
+
+def case_ag_gemm(rank: int, shapes, iters: int):
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", device_id=torch.device("cuda", rank))
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.fused import AllGatherGemm
+
+    n = dist.get_world_size()
+    K = shapes[0][2]
+    op = AllGatherGemm(dist.group.WORLD, max_rows=max(s[0] for s in shapes), k=K)
+    errs = []
+    for it in range(iters):
+        for M, N, _ in shapes:
+            g = torch.Generator(device="cuda").manual_seed(77 * it + rank)
+            x = torch.randn(M // n, K, device="cuda", generator=g).to(torch.bfloat16)
+            gw = torch.Generator(device="cuda").manual_seed(5 + it)
+            w = (torch.randn(N, K, device="cuda", generator=gw) * 0.05).to(torch.bfloat16)
+            y, _ = op(x, w)
+            full = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+            dist.all_gather_into_tensor(full, x)
+            ref = full.float() @ w.float().t()
+            torch.cuda.synchronize()
+            errs.append(((y.float() - ref).norm() / ref.norm()).item())
+    flag = _ext.ext().gemm_error_flag(True)
+    M, N, _ = shapes[-1]
+    x = torch.randn(M // n, K, device="cuda").to(torch.bfloat16)
+    w = (torch.randn(N, K, device="cuda") * 0.05).to(torch.bfloat16)
+    full = torch.empty(M, K, device="cuda", dtype=torch.bfloat16)
+
+    def timeit(fn, reps=10):
+        for _ in range(3):
+            fn()
+        dist.barrier()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(reps):
+            fn()
+        e1.record()
+        torch.cuda.synchronize()
+        t = torch.tensor([e0.elapsed_time(e1) / reps], device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return t.item()
+
+    t_fused = timeit(lambda: op(x, w))
+
+    def base():
+        dist.all_gather_into_tensor(full, x)
+        return torch.matmul(full, w.t())
+
+    t_base = timeit(base)
+    op.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"errs": errs, "flag": flag, "t_fused_ms": t_fused, "t_nccl_ms": t_base, "shape": (M, N, K)}
+
+
+def test_ag_gemm_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    shapes = [(512, 1024, 4096), (2048, 3072, 4096), (16384, 3072, 4096)]
+    outs = spawn_ranks(case_ag_gemm, 2, shapes, 3, timeout_s=400)
+    for o in outs:
+        assert o["flag"] == 0
+        assert max(o["errs"]) < 2e-2, o["errs"]
+    print("ag_gemm timing (max over ranks):", outs[0]["shape"], f"fused {outs[0]['t_fused_ms']:.3f} ms",
+          f"NCCL+cuBLAS {outs[0]['t_nccl_ms']:.3f} ms")

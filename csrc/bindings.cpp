@@ -53,6 +53,13 @@ void refit_copy(at::Tensor tasks, at::Tensor dst);
 at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
 at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n, int64_t me, int64_t epoch);
 void stream_write_u32(int64_t ptr, int64_t value);
+void ep_scatter(at::Tensor src, c10::optional<at::Tensor> src_row, at::Tensor dst_rank, at::Tensor dst_row,
+                c10::optional<at::Tensor> tags, int64_t cap, std::vector<int64_t> buf, std::vector<int64_t> tag,
+                std::vector<int64_t> flags, std::vector<int64_t> acks, int64_t me, int64_t epoch, at::Tensor counter);
+void ep_consume(at::Tensor out, c10::optional<at::Tensor> out_tag, int64_t cap, std::vector<int64_t> buf,
+                std::vector<int64_t> tag, std::vector<int64_t> flags, std::vector<int64_t> acks, int64_t me,
+                int64_t epoch, at::Tensor counter);
+int64_t ep_error_flag(bool reset);
 at::Tensor dp_reduce_shard(std::vector<int64_t> grad_ptrs, int64_t lo, int64_t len, at::Tensor out);
 void dp_adam_allgather(std::vector<int64_t> param_ptrs, int64_t lo, at::Tensor master, at::Tensor grad,
                        at::Tensor exp_avg, at::Tensor exp_avg_sq, at::Tensor nodecay, double lr, double b1, double b2,
@@ -92,6 +99,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_reduce_shard", &dp_reduce_shard, "DP gradient reduce-scatter over NVLink peer loads (+ norm partials)");
   m.def("dp_adam_allgather", &dp_adam_allgather, "sharded AdamW fused with the parameter all-gather (peer stores)");
   m.def("gemm_ag", &gemm_ag, "all-gather -> GEMM: waits per gathered shard (copy-engine transfers) on device flags");
+  m.def("ep_scatter", &ep_scatter, "MoE token rows -> peers' receive buffers at their final positions (P2P stores)");
+  m.def("ep_consume", &ep_consume, "wait for every source's scatter, copy the received rows out, acknowledge");
+  m.def("ep_error_flag", &ep_error_flag, py::arg("reset") = false);
   m.def("stream_write_u32", &stream_write_u32, "stream memory write (no kernel) of a 32-bit word");
   m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
   m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);

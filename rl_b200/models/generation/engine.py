@@ -82,7 +82,9 @@ class RolloutEngine:
         self.max_model_len = max_model_len
         self.block_size = block_size
         self.kv_dtype = kv_dtype or model.dtype
-        self.use_cuda_graphs = use_cuda_graphs and self.device.type == "cuda"
+        # expert-parallel MoE decode sizes its token exchange on the host every step
+        # (row totals per expert owner), which a captured graph cannot replay
+        self.use_cuda_graphs = use_cuda_graphs and self.device.type == "cuda" and model.ps.ep_size == 1
         self.seed = seed
         self.sync_every = sync_every
         self.kv: Optional[KVCache] = None

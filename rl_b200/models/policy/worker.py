@@ -648,6 +648,10 @@ class PolicyWorker:
             if getattr(self.model, attr, None) is not None:
                 getattr(self.model, attr).close()
                 setattr(self.model, attr, None)
+        if getattr(self.model, "_ep_ex", None) is not None:
+            for x in self.model._ep_ex:
+                x.close()
+            self.model._ep_ex = None
         self.weight_sync.shutdown()
 
     def offload_before_refit(self) -> None:

@@ -189,6 +189,7 @@ class TransformerLM(nn.Module):
         self.fused_collectives = True
         self._fused_rs = None
         self._fused_ag = None
+        self._ep_ex = None
         self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
         self.router_record: Optional[dict] = None
@@ -477,13 +478,18 @@ class TransformerLM(nn.Module):
             aux = E * (f.detach() * probs.mean(0)).sum() * c.moe_aux_loss_coef
             h = _AuxLossScaler.apply(h, aux, self.aux_loss_scale if self.aux_loss_scale else 1.0)
             self._aux_losses.append(aux.detach())
+        wgu = self._params[p + "mlp.experts.gate_up_proj"]
+        wdn = self._params[p + "mlp.experts.down_proj"]
+        if self.ps.ep_size > 1 and self.fused_collectives and h.is_cuda and h.dtype == torch.bfloat16:
+            out = self._moe_ep_fused(h, ids, weights, wgu, wdn)
+            if self.sequence_parallel:
+                out = reduce_scatter_to_sp(out, self.ps.tp_group)
+            return out
         flat_ids = ids.reshape(-1)
         order = torch.argsort(flat_ids, stable=True)
         token_of = order // k
         xs = h[token_of]                                             # [T*k, H] permuted by expert
         counts = torch.bincount(flat_ids, minlength=E)
-        wgu = self._params[p + "mlp.experts.gate_up_proj"]
-        wdn = self._params[p + "mlp.experts.down_proj"]
         if self.ps.ep_size > 1:
             ys = self._moe_ep_experts(xs, counts, wgu, wdn)
         else:
@@ -494,6 +500,28 @@ class TransformerLM(nn.Module):
         if self.sequence_parallel:
             out = reduce_scatter_to_sp(out, self.ps.tp_group)
         return out
+
+    def _moe_ep_fused(self, h, ids, weights, wgu, wdn):
+        """Expert parallelism with the peer-store dispatch / combine kernels
+        (``rl_b200.parallel.ep_fused``): rows land grouped by local expert on
+        their owner, outputs return to their assignment slot."""
+        from rl_b200.parallel.ep_fused import EPExchange, ep_combine, ep_dispatch, make_plan
+
+        T, H = h.shape
+        k = ids.shape[1]
+        plan = make_plan(ids, self.ps.ep_size, self.ps.ep_rank, self.experts_local, self.ps.ep_group)
+        ex = self._ep_ex
+        if ex is None or ex[0].cap < plan.R_max or ex[1].cap < plan.TK_max or ex[0].H != H:
+            if ex is not None:
+                for x in ex:
+                    x.close()
+            grow = 1.25  # headroom so that routing drift does not re-allocate every step
+            ex = self._ep_ex = (EPExchange(self.ps.ep_group, int(plan.R_max * grow) + 128, H),
+                                EPExchange(self.ps.ep_group, int(plan.TK_max * grow) + 128, H))
+        xr = ep_dispatch(h.contiguous(), plan, ex[0], ex[1])
+        y = grouped_swiglu_mlp(xr, plan.counts_local, wgu, wdn)
+        ret = ep_combine(y, plan, ex[0], ex[1])
+        return (ret.view(T, k, H) * weights.to(ret.dtype).unsqueeze(-1)).sum(1)
 
     def _moe_ep_experts(self, xs, counts, wgu, wdn):
         """Expert-parallel path: all-to-all tokens to the ranks owning their experts,

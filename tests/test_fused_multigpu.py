@@ -357,3 +357,67 @@ def test_ag_gemm_2gpu():
         assert max(o["errs"]) < 2e-2, o["errs"]
     print("ag_gemm timing (max over ranks):", outs[0]["shape"], f"fused {outs[0]['t_fused_ms']:.3f} ms",
           f"NCCL+cuBLAS {outs[0]['t_nccl_ms']:.3f} ms")
+
+
+def case_ep_moe(rank: int, T: int):
+    """EP=2 MoE transformer: peer-store dispatch / combine kernels against the
+    NCCL all-to-all path (forward output and gradients, two steps so both
+    epoch parities of the exchange buffers are used)."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(ep=2, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="ep", vocab_size=1024, hidden_size=256, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=64, ffn_hidden_size=0, rope_theta=10000.0, qk_norm=True, num_experts=8, moe_top_k=2,
+                      moe_ffn_hidden_size=128, moe_aux_loss_coef=0.0, max_position_embeddings=1024)
+    g = torch.Generator().manual_seed(11 + rank)  # ranks hold different tokens
+    ids = torch.randint(0, cfg.vocab_size, (T,), generator=g).cuda()
+    lens = [T // 2, T - T // 2]
+    pos = torch.cat([torch.arange(n) for n in lens]).cuda()
+    cu = torch.tensor([0, lens[0], T], dtype=torch.int32).cuda()
+    proj = torch.randn(T, cfg.hidden_size, generator=g).cuda()
+    res = {}
+    for fused in (False, True):
+        m = TransformerLM(cfg, ps, seed=5)
+        m.fused_collectives = fused
+        hs, grads = [], None
+        for _ in range(2):
+            h = m(ids, pos, cu, max(lens))
+            (h.float() * proj).sum().backward()
+            hs.append(h.float().clone())
+        torch.cuda.synchronize()
+        grads = {n: p.grad.float().clone() for n, p in m._params.items() if p.grad is not None}
+        res[fused] = (hs, grads, m._ep_ex is not None)
+        if m._ep_ex is not None:
+            for x in m._ep_ex:
+                x.close()
+    errs = {}
+    for j in range(2):
+        errs[f"hidden{j}"] = ((res[True][0][j] - res[False][0][j]).norm() / res[False][0][j].norm()).item()
+    for n_, g0 in res[False][1].items():
+        if n_ in res[True][1]:
+            errs[n_] = ((res[True][1][n_] - g0).norm() / (g0.norm() + 1e-12)).item()
+    flag = _ext.ext().ep_error_flag(True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"errs": errs, "used": res[True][2], "flag": flag, "missing": sorted(set(res[False][1]) - set(res[True][1]))}
+
+
+def test_ep_moe_fused_dispatch_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_ep_moe, 2, 384, timeout_s=300)
+    for o in outs:
+        assert o["used"], "fused EP exchange was not taken"
+        assert o["flag"] == 0
+        assert not o["missing"], o["missing"]
+        worst = max(o["errs"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 3e-2, worst

@@ -587,7 +587,7 @@ template <int HD>
 __global__ void __launch_bounds__(128)
 fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, long long qs,
               long long ks, long long vs, const int* __restrict__ cu, int nq, int nkv, float scale_log2, int causal,
-              bf16* __restrict__ o, float* __restrict__ lse, int T_total) {
+              bf16* __restrict__ o, float* __restrict__ lse, int T_total, const int* __restrict__ seg) {
   constexpr int BM = 64, BN = 64, CH = HD / 8, KS = HD / 16, NT = HD / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   bf16* Qs = reinterpret_cast<bf16*>(smem_raw);
@@ -596,21 +596,27 @@ fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   const int h = blockIdx.x;
   const int mblk = gridDim.y - 1 - blockIdx.y;
   const int b = blockIdx.z;
-  const int s0 = cu[b];
-  const int L = cu[b + 1] - s0;
+  // segment b: queries [s0, s0 + L), keys [k0, k0 + Lk); causal is bottom-right
+  // aligned (query i sees keys <= i + off), which is the plain causal mask when
+  // the two ranges coincide (seg == nullptr: packed varlen attention)
+  const int s0 = seg ? seg[4 * b] : cu[b];
+  const int L = seg ? seg[4 * b + 1] : cu[b + 1] - s0;
+  const int k0 = seg ? seg[4 * b + 2] : s0;
+  const int Lk = seg ? seg[4 * b + 3] : L;
+  const int off = Lk - L;
   const int m0 = mblk * BM;
   if (m0 >= L) return;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int kvh = h / (nq / nkv);
   const bf16* qg = q + (long long)(s0 + m0) * qs + (long long)h * HD;
-  const bf16* kg = k + (long long)s0 * ks + (long long)kvh * HD;
-  const bf16* vg = v + (long long)s0 * vs + (long long)kvh * HD;
+  const bf16* kg = k + (long long)k0 * ks + (long long)kvh * HD;
+  const bf16* vg = v + (long long)k0 * vs + (long long)kvh * HD;
   load_tile<CH>(Qs, qg, qs, BM, min(BM, L - m0), tid, 128);
-  const int n_end = causal ? min(L, m0 + BM) : L;
+  const int n_end = causal ? min(Lk, m0 + BM + off) : Lk;
   const int nblocks = (n_end + BN - 1) / BN;
-  load_tile<CH>(Ks, kg, ks, BN, min(BN, L), tid, 128);
-  load_tile<CH>(Vs, vg, vs, BN, min(BN, L), tid, 128);
+  load_tile<CH>(Ks, kg, ks, BN, min(BN, Lk), tid, 128);
+  load_tile<CH>(Vs, vg, vs, BN, min(BN, Lk), tid, 128);
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
@@ -629,8 +635,8 @@ fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     const int buf = nb & 1;
     if (nb + 1 < nblocks) {
       const int n1 = (nb + 1) * BN;
-      load_tile<CH>(Ks + (buf ^ 1) * BN * HD, kg + (long long)n1 * ks, ks, BN, min(BN, L - n1), tid, 128);
-      load_tile<CH>(Vs + (buf ^ 1) * BN * HD, vg + (long long)n1 * vs, vs, BN, min(BN, L - n1), tid, 128);
+      load_tile<CH>(Ks + (buf ^ 1) * BN * HD, kg + (long long)n1 * ks, ks, BN, min(BN, Lk - n1), tid, 128);
+      load_tile<CH>(Vs + (buf ^ 1) * BN * HD, vg + (long long)n1 * vs, vs, BN, min(BN, Lk - n1), tid, 128);
       cp_async_commit();
     }
     const bf16* Kb = Ks + buf * BN * HD;
@@ -657,7 +663,7 @@ fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
         const int key = n0 + 8 * j + 2 * t + (e & 1);
         const int qr = qrow0 + ((e >> 1) << 3);
         float sv = sacc[j][e] * scale_log2;
-        if (key >= L || (causal && key > qr)) sv = -INFINITY;
+        if (key >= Lk || (causal && key > qr + off)) sv = -INFINITY;
         sacc[j][e] = sv;
         mx[e >> 1] = fmaxf(mx[e >> 1], sv);
       }
@@ -748,7 +754,7 @@ fa_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
               long long ks, long long vs, const bf16* __restrict__ dout, const float* __restrict__ lse,
               const float* __restrict__ Dv, const int* __restrict__ cu, int nq, int nkv, float scale,
               float scale_log2, int causal, float* __restrict__ dq_acc, bf16* __restrict__ dk, bf16* __restrict__ dv,
-              int T_total) {
+              int T_total, const int* __restrict__ seg, float* __restrict__ dk_acc, float* __restrict__ dv_acc) {
   constexpr int BN = 64, BM = 32, CH = HD / 8, KS = HD / 16, NT = HD / 8;
   constexpr int QCH = BM / 8;  // chunks per dS^T row
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -760,16 +766,20 @@ fa_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   float* lse_s = reinterpret_cast<float*>(dSs + BN * BM);
   float* D_s = lse_s + BM;
   const int kvh = blockIdx.x, nblk = blockIdx.y, b = blockIdx.z;
-  const int s0 = cu[b];
-  const int L = cu[b + 1] - s0;
+  // segment b (see fa_fwd_kernel): queries [s0, s0 + L), keys [k0, k0 + Lk)
+  const int s0 = seg ? seg[4 * b] : cu[b];
+  const int L = seg ? seg[4 * b + 1] : cu[b + 1] - s0;
+  const int k0 = seg ? seg[4 * b + 2] : s0;
+  const int Lk = seg ? seg[4 * b + 3] : L;
+  const int off = Lk - L;
   const int n0 = nblk * BN;
-  if (n0 >= L) return;
+  if (n0 >= Lk) return;
   const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
   const int g = lane >> 2, t = lane & 3;
   const int G = nq / nkv;
   const float log2e = 1.4426950408889634f;
-  load_tile<CH>(Ks, k + (long long)(s0 + n0) * ks + (long long)kvh * HD, ks, BN, min(BN, L - n0), tid, 128);
-  load_tile<CH>(Vs, v + (long long)(s0 + n0) * vs + (long long)kvh * HD, vs, BN, min(BN, L - n0), tid, 128);
+  load_tile<CH>(Ks, k + (long long)(k0 + n0) * ks + (long long)kvh * HD, ks, BN, min(BN, Lk - n0), tid, 128);
+  load_tile<CH>(Vs, v + (long long)(k0 + n0) * vs + (long long)kvh * HD, vs, BN, min(BN, Lk - n0), tid, 128);
   cp_async_commit();
   cp_async_wait_all();
   __syncthreads();
@@ -780,7 +790,7 @@ fa_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
 #pragma unroll
     for (int e = 0; e < 4; ++e) dka[j][e] = dva[j][e] = 0.f;
 
-  const int m_begin = causal ? (n0 / BM) * BM : 0;
+  const int m_begin = causal ? (max(0, n0 - off) / BM) * BM : 0;
   const int key0 = n0 + 16 * w + g;  // this thread's key rows: key0, key0 + 8
   for (int hq = 0; hq < G; ++hq) {
     const int h = kvh * G + hq;
@@ -820,7 +830,7 @@ fa_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
           const int key = key0 + ((e >> 1) << 3);
           const int ql = 8 * j + 2 * t + (e & 1);
           const int qq = m0 + ql;
-          const bool ok = qq < L && key < L && (!causal || key <= qq);
+          const bool ok = qq < L && key < Lk && (!causal || key <= qq + off);
           st[j][e] = ok ? exp2f(st[j][e] * scale_log2 - lse_s[ql]) : 0.f;
         }
       }
@@ -927,9 +937,20 @@ fa_bwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
 #pragma unroll
   for (int r = 0; r < 2; ++r) {
     const int key = key0 + 8 * r;
-    if (key >= L) continue;
-    bf16* dkr = dk + ((long long)(s0 + key) * nkv + kvh) * HD;
-    bf16* dvr = dv + ((long long)(s0 + key) * nkv + kvh) * HD;
+    if (key >= Lk) continue;
+    if (dk_acc != nullptr) {
+      // segments may share keys (context-parallel chunks of one sequence): accumulate
+      float* dka_r = dk_acc + ((long long)(k0 + key) * nkv + kvh) * HD;
+      float* dva_r = dv_acc + ((long long)(k0 + key) * nkv + kvh) * HD;
+#pragma unroll
+      for (int j = 0; j < NT; ++j) {
+        atomicAdd(reinterpret_cast<float2*>(dka_r + 8 * j + 2 * t), make_float2(dka[j][2 * r], dka[j][2 * r + 1]));
+        atomicAdd(reinterpret_cast<float2*>(dva_r + 8 * j + 2 * t), make_float2(dva[j][2 * r], dva[j][2 * r + 1]));
+      }
+      continue;
+    }
+    bf16* dkr = dk + ((long long)(k0 + key) * nkv + kvh) * HD;
+    bf16* dvr = dv + ((long long)(k0 + key) * nkv + kvh) * HD;
 #pragma unroll
     for (int j = 0; j < NT; ++j) {
       *reinterpret_cast<__nv_bfloat162*>(dkr + 8 * j + 2 * t) =
@@ -997,7 +1018,7 @@ std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v,
     dim3 grid(nq, (max_seqlen + 63) / 64, B);
     kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
                                         q.stride(0), k.stride(0), v.stride(0), cu.data_ptr<int>(), nq, nkv, scale_log2,
-                                        causal ? 1 : 0, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_);
+                                        causal ? 1 : 0, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, nullptr);
   });
   RLB_CUDA_CHECK(cudaGetLastError());
   return {o, lse};
@@ -1033,13 +1054,83 @@ std::vector<at::Tensor> flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor
                                         q.stride(0), k.stride(0), v.stride(0), (const bf16*)dout.data_ptr(),
                                         lse.data_ptr<float>(), D.data_ptr<float>(), cu.data_ptr<int>(), nq, nkv,
                                         (float)scale, scale_log2, causal ? 1 : 0, dq_acc.data_ptr<float>(),
-                                        (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(), T_);
+                                        (bf16*)dk.data_ptr(), (bf16*)dv.data_ptr(), T_, nullptr, nullptr, nullptr);
   });
   const long long n = (long long)T_ * nq * hd;
   dq_convert_kernel<<<(int)std::min<long long>((n + 255) / 256, (long long)num_sms() * 8), 256, 0, stream()>>>(
       dq_acc.data_ptr<float>(), (bf16*)dq.data_ptr(), n, (float)scale);
   RLB_CUDA_CHECK(cudaGetLastError());
   return {dq, dk, dv};
+}
+
+// Segment attention (context parallelism): segment b attends queries
+// [seg[b][0], +seg[b][1]) of q to keys [seg[b][2], +seg[b][3]) of k / v, causal
+// with the last query aligned to the last key.  Segments may share keys.
+std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
+                                           double scale) {
+  check_head_view(q, "q");
+  check_head_view(k, "k");
+  check_head_view(v, "v");
+  TORCH_CHECK(seg.is_cuda() && seg.scalar_type() == at::kInt && seg.dim() == 2 && seg.size(1) == 4 &&
+              seg.is_contiguous(), "rl_b200 segment attention: seg int32 [S, 4]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int T_ = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k.size(1);
+  TORCH_CHECK(nq % nkv == 0, "rl_b200 attention: nq must be a multiple of nkv");
+  const int S = seg.size(0);
+  auto o = at::zeros({T_, nq, hd}, q.options());
+  auto lse = at::zeros({nq, T_}, q.options().dtype(at::kFloat));
+  if (T_ == 0 || S == 0 || max_q == 0) return {o, lse};
+  const float scale_log2 = (float)(scale * 1.4426950408889634);
+  RLB_HD_SWITCH(hd, [&] {
+    const int smem = (64 * HD + 2 * 64 * HD * 2) * 2;
+    auto kern = fa_fwd_kernel<HD>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    dim3 grid(nq, (max_q + 63) / 64, S);
+    kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
+                                        q.stride(0), k.stride(0), v.stride(0), nullptr, nq, nkv, scale_log2, 1,
+                                        (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, seg.data_ptr<int>());
+  });
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {o, lse};
+}
+
+std::vector<at::Tensor> flash_attn_seg_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
+                                           at::Tensor lse, at::Tensor seg, int64_t max_k, double scale) {
+  check_head_view(q, "q");
+  check_head_view(k, "k");
+  check_head_view(v, "v");
+  TORCH_CHECK(dout.is_contiguous() && out.is_contiguous(), "rl_b200 attention bwd: dout/out must be contiguous");
+  TORCH_CHECK(seg.is_cuda() && seg.scalar_type() == at::kInt && seg.dim() == 2 && seg.size(1) == 4 &&
+              seg.is_contiguous(), "rl_b200 segment attention: seg int32 [S, 4]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  const int T_ = q.size(0), nq = q.size(1), hd = q.size(2), nkv = k.size(1), Tk = k.size(0);
+  const int S = seg.size(0);
+  auto dq = at::zeros({T_, nq, hd}, q.options());
+  auto dk_acc = at::zeros({Tk, nkv, hd}, q.options().dtype(at::kFloat));
+  auto dv_acc = at::zeros({Tk, nkv, hd}, q.options().dtype(at::kFloat));
+  if (T_ == 0 || S == 0) return {dq, dk_acc.to(q.scalar_type()), dv_acc.to(q.scalar_type())};
+  auto D = at::empty({nq, T_}, q.options().dtype(at::kFloat));
+  auto dq_acc = at::zeros({T_, nq, hd}, q.options().dtype(at::kFloat));
+  const float scale_log2 = (float)(scale * 1.4426950408889634);
+  RLB_HD_SWITCH(hd, [&] {
+    const int rows = T_ * nq;
+    fa_bwd_pre_kernel<HD><<<(rows + 7) / 8, 256, 0, stream()>>>((const bf16*)dout.data_ptr(), (const bf16*)out.data_ptr(),
+                                                                 rows, D.data_ptr<float>(), nq, T_);
+    const int smem = (64 * HD * 2 + 32 * HD * 2 + 64 * 32) * 2 + 2 * 32 * 4;
+    auto kern = fa_bwd_kernel<HD>;
+    if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    dim3 grid(nkv, (max_k + 63) / 64, S);
+    kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
+                                        q.stride(0), k.stride(0), v.stride(0), (const bf16*)dout.data_ptr(),
+                                        lse.data_ptr<float>(), D.data_ptr<float>(), nullptr, nq, nkv, (float)scale,
+                                        scale_log2, 1, dq_acc.data_ptr<float>(), nullptr, nullptr, T_,
+                                        seg.data_ptr<int>(), dk_acc.data_ptr<float>(), dv_acc.data_ptr<float>());
+  });
+  const long long n = (long long)T_ * nq * hd;
+  dq_convert_kernel<<<(int)std::min<long long>((n + 255) / 256, (long long)num_sms() * 8), 256, 0, stream()>>>(
+      dq_acc.data_ptr<float>(), (bf16*)dq.data_ptr(), n, (float)scale);
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {dq, dk_acc.mul(scale).to(q.scalar_type()), dv_acc.to(q.scalar_type())};
 }
 
 at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cache, at::Tensor block_tables,

@@ -53,6 +53,10 @@ void refit_copy(at::Tensor tasks, at::Tensor dst);
 at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
 at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n, int64_t me, int64_t epoch);
 void stream_write_u32(int64_t ptr, int64_t value);
+std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
+                                           double scale);
+std::vector<at::Tensor> flash_attn_seg_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
+                                           at::Tensor lse, at::Tensor seg, int64_t max_k, double scale);
 void ep_scatter(at::Tensor src, c10::optional<at::Tensor> src_row, at::Tensor dst_rank, at::Tensor dst_row,
                 c10::optional<at::Tensor> tags, int64_t cap, std::vector<int64_t> buf, std::vector<int64_t> tag,
                 std::vector<int64_t> flags, std::vector<int64_t> acks, int64_t me, int64_t epoch, at::Tensor counter);
@@ -102,6 +106,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_scatter", &ep_scatter, "MoE token rows -> peers' receive buffers at their final positions (P2P stores)");
   m.def("ep_consume", &ep_consume, "wait for every source's scatter, copy the received rows out, acknowledge");
   m.def("ep_error_flag", &ep_error_flag, py::arg("reset") = false);
+  m.def("flash_attn_seg_fwd", &flash_attn_seg_fwd, "segment attention (query chunks vs key prefixes), forward");
+  m.def("flash_attn_seg_bwd", &flash_attn_seg_bwd, "segment attention backward (shared keys accumulate)");
   m.def("stream_write_u32", &stream_write_u32, "stream memory write (no kernel) of a 32-bit word");
   m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
   m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);

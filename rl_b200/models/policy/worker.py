@@ -244,6 +244,13 @@ class PolicyWorker:
                 bins.append([-1 - filler])
         return bins
 
+    def _metric_group(self):
+        """Group over which per-rank loss partial sums add up: DP, times CP (each
+        CP rank scores its own chunks)."""
+        if self.ps.cp_size > 1:
+            return self.ps.dp_cp_group
+        return self.ps.dp_group if self.ps.dp_size > 1 else None
+
     def _pack_multiple(self) -> int:
         """Packed-token count multiple: the TP size under sequence parallelism, and
         128 x TP when the fused GEMM + reduce-scatter kernel takes the row-parallel
@@ -255,9 +262,39 @@ class PolicyWorker:
             return 128 * tp
         return tp
 
+    def _forward_mb_cp(self, input_ids: torch.Tensor, lengths: list[int], rows: list[int], temperature: float):
+        """Context-parallel forward: this rank's two load-balanced chunks of every
+        sequence (``rl_b200.parallel.context_parallel``).  Returns local
+        (logprob, entropy) and the host scatter map ("cp", seq, pos, lens)."""
+        from rl_b200.parallel.context_parallel import cp_layout
+
+        lens = [int(lengths[r]) for r in rows]
+        unit = 128 * self.ps.tp_size // 2 if (self.sequence_parallel and self.device.type == "cuda") else \
+            max(1, self.ps.tp_size)
+        lay = cp_layout(lens, self.ps.cp_size, self.ps.cp_rank, self.device, unit=unit)
+        seq = lay.seq_of_local.cpu().numpy()
+        pos = lay.positions.cpu().numpy().astype(np.int64)
+        L = np.asarray(lens, dtype=np.int64)[seq]
+        ids_np = input_ids[rows].numpy() if not input_ids.is_cuda else input_ids[rows].cpu().numpy()
+        W = ids_np.shape[1]
+        tok = np.where(pos < L, ids_np[seq, np.minimum(pos, W - 1)], 0)
+        tgt = np.where(pos + 1 < L, ids_np[seq, np.minimum(pos + 1, W - 1)], 0)
+        dev = self.device
+        # stays set until the next micro-batch: activation recomputation in the
+        # backward pass re-runs the attention with the same layout
+        self.model._cp_layout = lay
+        hidden = self.model(_to_device(torch.from_numpy(tok), dev), lay.positions, None, lay.max_k)
+        h = self.model.lm_input(hidden)
+        lp, ent = linear_logprobs(h, self.model.lm_head_weight(), _to_device(torch.from_numpy(tgt), dev),
+                                  self.model.vocab_start, temperature,
+                                  self.ps.tp_group if self.ps.tp_size > 1 else None, self.logprob_chunk)
+        return lp, ent, ("cp", seq, pos, np.asarray(lens, dtype=np.int64))
+
     def _forward_mb(self, input_ids: torch.Tensor, lengths: list[int], rows: list[int], temperature: float):
         """Packed forward of ``rows``; returns per-token next-token (logprob, entropy)
         ``[T]`` aligned so that entry j scores token j+1, plus the packing metadata."""
+        if self.ps.cp_size > 1:
+            return self._forward_mb_cp(input_ids, lengths, rows, temperature)
         flat, pos, cu, max_len, T_real = pack_rows(input_ids, lengths, rows, pad_to_multiple=self._pack_multiple())
         dev = self.device
         flat_d, pos_d, cu_d = _to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev)
@@ -278,7 +315,14 @@ class PolicyWorker:
         kind = getattr(getattr(loss_fn, "input_type", None), "value", "logprob")
         if kind == "logprob":
             lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
+            if isinstance(cu, tuple):
+                # the loss sees only this rank's tokens (the others' positions are
+                # masked; their ranks contribute them): tokens i+1 scored locally
+                one = torch.ones(lp.shape[0], device=lp.device)
+                self._cp_owned = self._to_padded(one, cu, len(rows), width)
             return self._to_padded(lp, cu, len(rows), width)
+        if self.ps.cp_size > 1:
+            raise NotImplementedError("context parallelism supports log-prob losses")
         flat, pos, cu, max_len, _ = pack_rows(ids, lengths, rows, pad_to_multiple=self._pack_multiple())
         dev = self.device
         hidden = self.model(_to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev), max_len)
@@ -335,15 +379,20 @@ class PolicyWorker:
         The scatter map is built vectorised on the host from the (host) cu_seqlens
         and copied once; entries that score nothing (each sequence's last token,
         the padding tail) go to a sink slot that is dropped."""
-        cu_np = cu.numpy().astype(np.int64)
         T = int(lp.shape[0])
-        lens = np.diff(cu_np)[:n_rows]
-        seq = np.repeat(np.arange(n_rows), lens)
-        offs = np.arange(int(cu_np[n_rows])) - np.repeat(cu_np[:n_rows], lens)
         N = n_rows * (width - 1)
         dst = np.full(T, N, dtype=np.int64)
-        ok = offs < np.repeat(lens, lens) - 1
-        dst[: len(offs)][ok] = seq[ok] * (width - 1) + offs[ok]
+        if isinstance(cu, tuple):  # context parallel: ("cp", seq, pos, lens) of the local tokens
+            _, seq, offs, lens = cu
+            ok = offs < lens[seq] - 1
+            dst[ok] = seq[ok] * (width - 1) + offs[ok]
+        else:
+            cu_np = cu.numpy().astype(np.int64)
+            lens = np.diff(cu_np)[:n_rows]
+            seq = np.repeat(np.arange(n_rows), lens)
+            offs = np.arange(int(cu_np[n_rows])) - np.repeat(cu_np[:n_rows], lens)
+            ok = offs < np.repeat(lens, lens) - 1
+            dst[: len(offs)][ok] = seq[ok] * (width - 1) + offs[ok]
         di = torch.from_numpy(dst)
         if lp.is_cuda:
             di = di.pin_memory().to(lp.device, non_blocking=True)
@@ -373,8 +422,10 @@ class PolicyWorker:
             lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
             if dummy:
                 continue  # padding pass that only keeps the EP group's collectives paired
-            padded = self._to_padded(lp.float(), cu, len(rows), S).cpu()
-            out[torch.tensor(rows), 1:] = padded
+            padded = self._to_padded(lp.float(), cu, len(rows), S)
+            if self.ps.cp_size > 1:  # every CP rank scored its own chunks
+                dist.all_reduce(padded, group=self.ps.cp_group)
+            out[torch.tensor(rows), 1:] = padded.cpu()
         self.model.train()
         return BatchedDataDict({"logprobs": out})
 
@@ -440,7 +491,7 @@ class PolicyWorker:
             all_metrics.extend(st.mb_metrics)
         if self.release_grad_after_train:
             self.optimizer.release_grad_buffer()
-        agg = aggregate_metrics(all_metrics, self.ps.dp_group if self.ps.dp_size > 1 else None)
+        agg = aggregate_metrics(all_metrics, self._metric_group())
         agg.update({"loss": sum(losses) / max(1, len(losses)), "global_loss": losses,
                     "grad_norm": grad_norms[-1] if grad_norms else 0.0, "lr": lrs[-1] if lrs else 0.0,
                     "moe_aux_loss": self.model.aux_loss()})
@@ -478,8 +529,9 @@ class PolicyWorker:
         tok_mask = dev_data["token_mask"][g0:g0 + n, 1:].float()
         smask = dev_data["sample_mask"][g0:g0 + n].float()
         counts = torch.stack([(tok_mask * smask.unsqueeze(-1)).sum(), smask.sum()])
-        if self.ps.dp_size > 1 or self.ps.cp_size > 1:
-            dist.all_reduce(counts, group=self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group)
+        if self.ps.dp_size > 1:
+            # CP ranks hold the same rows: global counts are a sum over data-parallel ranks only
+            dist.all_reduce(counts, group=self.ps.dp_group)
         plan = self._plan(lengths, [r for r in rows if lengths[r] > 0], self.train_mb_tokens)
         self.model.aux_loss_scale = 1.0 / max(1, len(plan))
         return TrainStepState(ids=ids, lengths=lengths, dev_data=dev_data, loss_fn=loss_fn, plan=plan,
@@ -499,6 +551,13 @@ class PolicyWorker:
             if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
         mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
                               for k, v in st.dev_data.items()})
+        if self.ps.cp_size > 1:
+            if getattr(st.loss_fn, "loss_type", None) is not None and \
+                    getattr(st.loss_fn.loss_type, "value", "") == "sequence_level":
+                raise NotImplementedError("sequence-level losses under context parallelism")
+            tm = mb["token_mask"].clone()
+            tm[:, 1:] = tm[:, 1:] * self._cp_owned.to(tm.dtype)
+            mb["token_mask"] = tm
         loss, metrics = st.loss_fn(curr, mb, st.gseqs, st.gtoks)
         if dummy:
             # zero-weight pass: keeps the EP group's all-to-alls paired, adds nothing
@@ -523,13 +582,14 @@ class PolicyWorker:
             out.update(grad_norm=opt_stats["grad_norm"], lr=opt_stats["lr"])
         else:
             self.optimizer.zero_grad()
-        if self.ps.dp_size > 1:
-            dist.all_reduce(st.step_loss, group=self.ps.dp_group)
+        red = self._metric_group()
+        if red is not None:
+            dist.all_reduce(st.step_loss, group=red)
         out["loss"] = float(st.step_loss)
         if release_grad if release_grad is not None else self.release_grad_after_train:
             self.optimizer.release_grad_buffer()
         if aggregate:
-            agg = aggregate_metrics(st.mb_metrics, self.ps.dp_group if self.ps.dp_size > 1 else None)
+            agg = aggregate_metrics(st.mb_metrics, self._metric_group())
             agg.update(out)
             agg["moe_aux_loss"] = self.model.aux_loss()
             return agg

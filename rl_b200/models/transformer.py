@@ -190,6 +190,7 @@ class TransformerLM(nn.Module):
         self._fused_rs = None
         self._fused_ag = None
         self._ep_ex = None
+        self._cp_layout = None  # rl_b200.parallel.context_parallel.CPLayout of the current micro-batch
         self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
         self.router_record: Optional[dict] = None
@@ -370,6 +371,8 @@ class TransformerLM(nn.Module):
 
     def _attn_block(self, i: int, h: torch.Tensor, positions, cu_seqlens, max_seqlen) -> torch.Tensor:
         p = f"model.layers.{i}."
+        if self.ps.cp_size > 1 and self._cp_layout is not None:
+            return self._attn_block_cp(i, h, positions)
         if self._fused_ag_ok(h):
             qkv = self._qkv(i, None, positions, qkv=self._ag_linear(h, p + "self_attn.qkv_proj.weight"))
         else:
@@ -380,6 +383,26 @@ class TransformerLM(nn.Module):
             qkv = self._qkv(i, h, positions)
         q, k, v = self._split_heads(qkv)
         o = flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen, causal=True)
+        return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
+                                         p + "self_attn.o_proj.weight")
+
+    def _attn_block_cp(self, i: int, h: torch.Tensor, positions) -> torch.Tensor:
+        """Context parallelism: local query chunks attend to their sequence
+        prefixes; keys / values are gathered over the CP group
+        (``rl_b200.parallel.context_parallel``)."""
+        from rl_b200.parallel.context_parallel import cp_attention, gather_kv_cp
+
+        p = f"model.layers.{i}."
+        lay = self._cp_layout
+        if self.sequence_parallel:
+            h = gather_from_sp(h, self.ps.tp_group)
+        else:
+            h = copy_to_tp(h, self.ps.tp_group)
+        qkv = self._qkv(i, h, positions)
+        q, k, v = self._split_heads(qkv)
+        kf = gather_kv_cp(k, lay, self.ps.cp_group)
+        vf = gather_kv_cp(v, lay, self.ps.cp_group)
+        o = cp_attention(q, kf, vf, lay, 1.0 / math.sqrt(self.hd))
         return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
                                          p + "self_attn.o_proj.weight")
 

@@ -28,6 +28,7 @@ _KERNELS_PER_CALL = {
     "rmsnorm_bwd_add": 2,
     "sum_sq": 2,
     "flash_attn_bwd": 3,
+    "flash_attn_seg_bwd": 3,
     "paged_decode_attn": 1,
     "sample": 2,
     "gemm_error_flag": 0,

@@ -84,6 +84,32 @@ def flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[floa
     return flash_attn_varlen_ref(q, k, v, cu_seqlens, scale, causal)[0]
 
 
+class _FlashAttnSegments(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, q, k, v, seg, max_q, max_k, scale):
+        o, lse = ext().flash_attn_seg_fwd(q, k, v, seg, int(max_q), float(scale))
+        ctx.save_for_backward(q, k, v, o, lse, seg)
+        ctx.meta = (int(max_k), float(scale))
+        return o
+
+    @staticmethod
+    def backward(ctx, do):
+        q, k, v, o, lse, seg = ctx.saved_tensors
+        max_k, scale = ctx.meta
+        dq, dk, dv = ext().flash_attn_seg_bwd(do.contiguous(), q, k, v, o, lse, seg, max_k, scale)
+        return dq, dk, dv, None, None, None, None
+
+
+def flash_attn_segments(q, k, v, q_start, q_len, k_start, k_len, max_q: int, max_k: int, scale: float):
+    """Segment ``s`` attends queries ``[q_start[s], +q_len[s])`` to keys
+    ``[k_start[s], +k_len[s])``, causal with the last query aligned to the last
+    key (context-parallel chunks against their sequence prefixes; segments may
+    share keys).  Native kernels: the varlen flash-attention kernels of
+    ``csrc/attention.cu`` with per-segment ranges."""
+    seg = torch.stack([q_start, q_len, k_start, k_len], 1).to(torch.int32).contiguous()
+    return _FlashAttnSegments.apply(q.contiguous(), k.contiguous(), v.contiguous(), seg, max_q, max_k, scale)
+
+
 def flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[float] = None,
                           causal: bool = True):
     """Forward only (prefill): returns (out, lse)."""

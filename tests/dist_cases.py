@@ -35,12 +35,12 @@ def _pcfg(sp: bool):
             "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
 
 
-def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool):
+def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool, cp: int = 1):
     from rl_b200.models.policy.worker import PolicyWorker
     from rl_b200.parallel.state import init_distributed
 
     torch.manual_seed(0)
-    ps = init_distributed(tp=tp, ep=ep, backend="gloo")
+    ps = init_distributed(tp=tp, ep=ep, cp=cp, backend="gloo")
     cfg = TINY_MOE if moe else TINY
     w = PolicyWorker(_pcfg(sp), model_cfg=cfg, pstate=ps, seed=3)
     full = make_batch()

@@ -49,3 +49,11 @@ def test_reshard_refit_tp2_to_rollout_tp1():
         assert o["refit_err"] == 0.0, o["refit_err"]
     assert torch.equal(outs[0]["out_ids"], outs[1]["out_ids"])
     assert outs[0]["out_ids"].shape[0] == 5
+
+
+@pytest.mark.parametrize("world,tp,cp,sp", [(2, 1, 2, False), (4, 2, 2, True), (4, 1, 2, False)])
+def test_context_parallel_matches_single(dense_single, world, tp, cp, sp):
+    """Load-balanced CP chunks + gathered-KV attention reproduce the single-process step."""
+    outs = spawn_ranks(case_train_step, world, tp, 1, sp, False, cp)
+    for o in outs:
+        _close(o, dense_single)

@@ -279,6 +279,9 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                     n_rows = train_data.size
                     gbs = min(local_gbs, n_rows)
                     train_results = policy.train(train_data, loss_fn, gbs=gbs)
+                if getattr(policy, "draft", None) is not None:
+                    with timer.time("draft_training"):
+                        train_results["draft_loss"] = policy.train_draft(train_data)
                 # ---- refit ----
                 with timer.time("weight_sync"):
                     refit_policy_generation(policy)

@@ -88,7 +88,13 @@ class RolloutEngine:
         self.seed = seed
         self.sync_every = sync_every
         self.kv: Optional[KVCache] = None
-        self.max_blocks_per_seq = math.ceil(max_model_len / block_size)
+        # speculative decoding: a small draft LM proposes `num_spec` tokens per
+        # round, the target verifies them in one batched forward
+        self.draft: Optional[TransformerLM] = None
+        self.draft_kv: Optional[KVCache] = None
+        self.num_spec = int((self.cfg.get("speculative") or {}).get("num_speculative_tokens", 0) or 0)
+        self.spec_stats = {"rounds": 0, "emitted": 0, "proposed": 0}
+        self.max_blocks_per_seq = math.ceil((max_model_len + self.num_spec + 1) / block_size)
         self._states: dict[int, _DecodeState] = {}
         self._graph_pool = None
         self.calls = 0
@@ -113,6 +119,10 @@ class RolloutEngine:
                               self.kv_dtype, self.device, arena=arena)
             self.arena_dirty = self.arena_dirty or (arena is not None)
             self._kv_capacity_seqs = n
+            if self.draft is not None:
+                d = self.draft
+                self.draft_kv = KVCache(d.cfg.num_layers, blocks, self.block_size, d.nkv, d.hd, self.kv_dtype,
+                                        self.device)
             sig = (self.kv.storage.data_ptr(), tuple(self.kv.storage.shape))
             if sig != getattr(self, "_kv_sig", None):
                 self._drop_graphs()  # captured graphs point at the old cache
@@ -125,6 +135,16 @@ class RolloutEngine:
         self._states.clear()
         self._graph_pool = None
 
+    def set_draft(self, draft: TransformerLM, num_speculative_tokens: int) -> None:
+        """Enable speculative decoding with ``draft`` proposing ``num_speculative_tokens``
+        tokens per round (the KV caches are re-created at the next prepare)."""
+        self.draft = draft
+        self.num_spec = int(num_speculative_tokens)
+        self.max_blocks_per_seq = math.ceil((self.max_model_len + self.num_spec + 1) / self.block_size)
+        self.finish_generation()
+        self._drop_graphs()
+        self._kv_sig = None
+
     def finish_generation(self) -> bool:
         """Release (sleep) the KV cache so training gets the memory back.
 
@@ -132,6 +152,7 @@ class RolloutEngine:
         steps, so the captured decode graphs are kept and replayed next time;
         otherwise they are dropped with the cache."""
         self.kv = None
+        self.draft_kv = None
         if self.kv_arena is None:
             self._drop_graphs()
             self._kv_sig = None
@@ -204,8 +225,13 @@ class RolloutEngine:
             lp0 = torch.zeros_like(lp0)
 
         # ---- decode ----
-        tokens_all, lps_all, glen = self._decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
-                                                      temperature, top_k, top_p, stop_ids, gen)
+        if self._spec_enabled(top_k, top_p):
+            self.draft.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.draft_kv, slot, last_idx)
+            tokens_all, lps_all, glen = self._spec_decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
+                                                               temperature, stop_ids)
+        else:
+            tokens_all, lps_all, glen = self._decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
+                                                          temperature, top_k, top_p, stop_ids, gen)
         glen_c = glen.cpu().to(torch.int64)
         toks_c = tokens_all.cpu()
         lps_c = lps_all.cpu()
@@ -215,6 +241,85 @@ class RolloutEngine:
             out_ids[b, L: L + n] = toks_c[b, :n]
             out_lp[b, L: L + n] = lps_c[b, :n]
         return self._pack_outputs(out_ids, out_lp, lengths, glen_c, pad_id, max_new)
+
+    def _spec_enabled(self, top_k, top_p) -> bool:
+        # rejection sampling verifies against the full distributions: no top-k / top-p filtering
+        return (self.draft is not None and self.num_spec > 0 and self.draft_kv is not None
+                and not top_k and (top_p is None or top_p >= 1.0))
+
+    def _spec_decode_loop(self, tok0, lp0, lengths, block_tables, max_new, temperature, stop_ids):
+        """Speculative decoding (eager): per round the draft proposes k tokens, the
+        target scores [last, d_1..d_k] at positions L..L+k in ONE batched decode
+        forward (row (b, j) sees keys up to L+j), and ``spec_verify`` accepts a
+        prefix and adds a correction.  At most k tokens are emitted per round (a
+        full acceptance's bonus token is left for the next round, which keeps
+        the draft's cache gap-free); the output distribution is the target's."""
+        from rl_b200.ops.sampling import sample_tokens
+        from rl_b200.ops.spec_decode import spec_verify
+
+        dev = self.device
+        B = tok0.shape[0]
+        k = self.num_spec
+        bs = self.block_size
+        cap = max_new + k + 1
+        toks = torch.zeros(B, cap, dtype=torch.int64, device=dev)
+        lps = torch.zeros(B, cap, dtype=torch.float32, device=dev)
+        toks[:, 0], lps[:, 0] = tok0, lp0
+        stop = torch.tensor(stop_ids if stop_ids else [-1], dtype=torch.int64, device=dev)
+        glen = torch.ones(B, dtype=torch.int64, device=dev)
+        done = torch.isin(tok0, stop) | (glen >= max_new)
+        last = tok0.clone()
+        pos0 = lengths.to(torch.int64).clone()       # position of `last`
+        ar = torch.arange(k + 1, device=dev)
+        bt_rows = block_tables.repeat_interleave(k + 1, 0)
+        temp = temperature if temperature > 0 else 0.0
+        rnd = 0
+        while not bool(done.all()):
+            # 1. draft proposals (rows of finished sequences run too; results are ignored)
+            x = last
+            drafts, dlogits = [], []
+            for j in range(k):
+                p = (pos0 + j).to(torch.int32)
+                slot = block_tables.gather(1, (p // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (p % bs).long()
+                h = self.draft.forward_decode(x, p, self.draft_kv, block_tables, p + 1, slot, self.max_model_len + k + 1)
+                lg = self.draft.logits_infer(h)
+                x, _ = sample_tokens(lg, temp if temp > 0 else 1.0, 1 if temp == 0 else None, 1.0, seed=self.seed + 17,
+                                     offset=(self.calls << 24) + rnd * (k + 1) + j)
+                drafts.append(x)
+                dlogits.append(lg)
+            dr = torch.stack(drafts, 1)
+            # 2. target verify of [last, d_1..d_k] at positions pos0 .. pos0+k
+            rows_tok = torch.cat([last.unsqueeze(1), dr], 1).reshape(-1)
+            rows_pos = (pos0.unsqueeze(1) + ar).reshape(-1).to(torch.int32)
+            slot = bt_rows.gather(1, (rows_pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (rows_pos % bs).long()
+            h = self.model.forward_decode(rows_tok, rows_pos, self.kv, bt_rows, rows_pos + 1, slot,
+                                          self.max_model_len + k + 1)
+            tl = self.model.logits_infer(h).view(B, k + 1, -1)
+            out, n, olp = spec_verify(tl, torch.stack(dlogits, 1), dr, temp, seed=self.seed,
+                                      offset=(self.calls << 20) + rnd)
+            n = torch.clamp(n.to(torch.int64), max=k)
+            # 3. append the emitted tokens (cut at a stop token / the length budget)
+            valid = ar[:k].unsqueeze(0) < n.unsqueeze(1)
+            is_stop = torch.isin(out[:, :k], stop) & valid
+            first_stop = torch.where(is_stop.any(1), is_stop.float().argmax(1) + 1, n)
+            room = (max_new - glen).clamp_min(0)
+            take = torch.minimum(torch.minimum(n, first_stop), room)
+            take = torch.where(done, torch.zeros_like(take), take)
+            col = glen.unsqueeze(1) + ar[:k].unsqueeze(0)
+            keep = ar[:k].unsqueeze(0) < take.unsqueeze(1)
+            # columns glen..glen+k-1 < cap are distinct per row: rewrite kept slots only
+            toks.scatter_(1, col, torch.where(keep, out[:, :k], toks.gather(1, col)))
+            lps.scatter_(1, col, torch.where(keep, olp[:, :k], lps.gather(1, col)))
+            glen = glen + take
+            newly = (take > 0) & (first_stop <= take) & is_stop.any(1)
+            done = done | newly | (glen >= max_new)
+            last = torch.where(take > 0, out.gather(1, (take - 1).clamp_min(0).unsqueeze(1)).squeeze(1), last)
+            pos0 = pos0 + take
+            self.spec_stats["rounds"] += 1
+            self.spec_stats["proposed"] += int(k * B)
+            rnd += 1
+        self.spec_stats["emitted"] += int(glen.sum())
+        return toks[:, :max_new], lps[:, :max_new], glen.to(torch.int32)
 
     def _pack_outputs(self, out_ids, out_lp, lengths, gen_lens, pad_id, max_new) -> BatchedDataDict:
         unpadded = lengths.cpu() + gen_lens

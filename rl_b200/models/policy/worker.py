@@ -173,6 +173,16 @@ class PolicyWorker:
             use_cuda_graphs=bool(gen_cfg.get("use_cuda_graphs", True)),
             seed=seed * 7 + self.ps.dp_rank * 100003,
         )
+        # speculative decoding: a small draft LM (same vocab / width, few layers) that
+        # proposes tokens for the rollout engine and is trained online on rollouts
+        spec = gen_cfg.get("speculative") or {}
+        self.draft = None
+        if int(spec.get("num_speculative_tokens", 0) or 0) > 0:
+            dcfg = self.model_cfg.replace(num_layers=int(spec.get("draft_num_layers", 1)))
+            self.draft = TransformerLM(dcfg, self.gen_model.ps, device=self.device, dtype=self.dtype,
+                                       seed=seed + 7919)
+            self.engine.set_draft(self.draft, int(spec["num_speculative_tokens"]))
+            self._draft_opt = torch.optim.AdamW(self.draft.parameters(), lr=float(spec.get("draft_lr", 1e-4)))
         self.ref_flat: Optional[torch.Tensor] = None
         if init_reference_model and self.lora is None:
             self.ref_flat = self.model.flat_param.detach().clone()
@@ -631,6 +641,43 @@ class PolicyWorker:
 
     def prepare_for_lp_inference(self) -> None:
         self.model.eval()
+
+    def train_draft(self, data: BatchedDataDict, max_tokens: int = 8192) -> float:
+        """One online step of the speculative draft: next-token cross-entropy on the
+        rollout sequences (teacher forcing on what the target generated), the
+        draft's equivalent of the reference's online Eagle3 / MTP draft training
+        (``nemo_rl/models/policy/draft_config.py:64``).  Returns the loss."""
+        if self.draft is None:
+            return 0.0
+        lengths = self._lengths(data)
+        rows = [r for r in range(len(lengths)) if lengths[r] > 1]
+        tot, sel = 0, []
+        for r in rows:
+            if tot + lengths[r] > max_tokens and sel:
+                break
+            sel.append(r)
+            tot += lengths[r]
+        if not sel:
+            return 0.0
+        flat, pos, cu, max_len, _ = pack_rows(data["input_ids"], lengths, sel, pad_to_multiple=1)
+        dev = self.device
+        flat_d = _to_device(flat, dev)
+        self.draft.train()
+        hidden = self.draft(flat_d, _to_device(pos, dev), _to_device(cu, dev), max_len)
+        logits = self.draft.logits(hidden).float()
+        if self.draft.ps.tp_size > 1:
+            from rl_b200.parallel.comm import gather_from_sp
+
+            logits = gather_from_sp(logits.t().contiguous(), self.draft.ps.tp_group).t()
+        tgt = torch.empty_like(flat_d)
+        tgt[:-1] = flat_d[1:]
+        last = torch.zeros_like(flat_d, dtype=torch.bool)
+        last[(_to_device(cu[1:], dev) - 1).long()] = True
+        loss = torch.nn.functional.cross_entropy(logits[~last], tgt[~last])
+        self._draft_opt.zero_grad(set_to_none=True)
+        loss.backward()
+        self._draft_opt.step()
+        return float(loss.detach())
 
     def refit(self) -> float:
         """Make the rollout weights current.  Colocated and same layout: the

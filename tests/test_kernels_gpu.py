@@ -328,3 +328,54 @@ def test_flash_attn_segments_cp_layout(cuda_device, hd, G):
     assert rel_err(q.grad, qf.grad) < 3e-2
     assert rel_err(k.grad, kf.grad) < 3e-2
     assert rel_err(v.grad, vf.grad) < 3e-2
+
+
+def _spec_case(B, V, k, device, seed=0):
+    g = torch.Generator(device="cpu").manual_seed(seed)
+    t_row = torch.randn(k + 1, V, generator=g) * 1.5
+    d_row = torch.randn(k, V, generator=g) * 1.5
+    tl = t_row.expand(B, k + 1, V).contiguous()
+    dl = d_row.expand(B, k, V).contiguous()
+    q = torch.softmax(d_row, -1)
+    draft = torch.stack([torch.multinomial(q[i], B, replacement=True, generator=g) for i in range(k)], 1)
+    return tl.to(device), dl.to(device), draft.to(device), torch.softmax(t_row, -1), q
+
+
+def test_spec_verify_distribution_matches_target(cuda_device):
+    """The first emitted token is distributed as the target's p_0 whatever the
+    draft, and the acceptance rate of the first draft token is sum(min(p, q))."""
+    from rl_b200.ops.spec_decode import spec_verify
+
+    B, V, k = 60000, 6, 2
+    tl, dl, draft, p, q = _spec_case(B, V, k, cuda_device)
+    tok, n, lp = spec_verify(tl, dl, draft, temperature=1.0, seed=3)
+    torch.cuda.synchronize()
+    first = tok[:, 0].cpu()
+    freq = torch.bincount(first, minlength=V).float() / B
+    assert (freq - p[0]).abs().max() < 0.012, (freq, p[0])
+    acc = (n.cpu() >= 2).float().mean()
+    assert abs(float(acc) - float(torch.minimum(p[0], q[0]).sum())) < 0.012
+    assert int(n.min()) >= 1 and int(n.max()) <= k + 1
+    # logprobs are the target's log-probabilities of the emitted tokens
+    lpt = torch.log(p[0])[first]
+    assert torch.allclose(lp[:, 0].cpu(), lpt, atol=1e-4)
+    # unused slots are -1
+    idx = torch.arange(k + 1).unsqueeze(0)
+    assert bool(((tok.cpu() == -1) == (idx >= n.cpu().unsqueeze(1))).all())
+
+
+def test_spec_verify_greedy(cuda_device):
+    from rl_b200.ops.spec_decode import spec_verify, spec_verify_ref
+
+    B, V, k = 64, 1000, 2
+    g = torch.Generator().manual_seed(4)
+    tl = torch.randn(B, k + 1, V, generator=g)
+    dl = torch.randn(B, k, V, generator=g)
+    draft = tl[:, :k].argmax(-1)
+    draft[::3, 0] = (draft[::3, 0] + 1) % V   # some first drafts wrong
+    draft[1::3, 1] = (draft[1::3, 1] + 1) % V  # some second drafts wrong
+    tok, n, lp = spec_verify(tl.to(cuda_device).to(torch.bfloat16), dl.to(cuda_device).to(torch.bfloat16),
+                             draft.to(cuda_device), temperature=0.0)
+    rt, rn, rlp = spec_verify_ref(tl.to(torch.bfloat16), dl.to(torch.bfloat16), draft, temperature=0.0)
+    assert torch.equal(n.cpu(), rn) and torch.equal(tok.cpu(), rt)
+    assert torch.allclose(lp.cpu(), rlp, atol=2e-2)

@@ -213,6 +213,9 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     max_steps = max_steps if max_steps is not None else int(cfg["max_num_steps"])
     set_seed(int(cfg["seed"]) + ps.dp_rank)
     timer = Timer()
+    from rl_b200.utils.telemetry import Telemetry
+
+    _telemetry = Telemetry()
     model_cfg = getattr(getattr(policy, "model", None), "cfg", None)
     flop_tracker = FLOPTracker(model_cfg) if model_cfg is not None else None
     step = int(state["current_step"])
@@ -313,6 +316,7 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 "step_time_s": step_time_max,
             })
             timing = {k: v for k, v in timer.get_timing_metrics().items()}
+            metrics.update(_telemetry.goodput(timing, step_time_max))
             step += 1
             state["current_step"] = step
             state["total_steps"] = int(state.get("total_steps", 0)) + 1

@@ -295,9 +295,7 @@ class PolicyWorker:
         self.model._cp_layout = lay
         hidden = self.model(_to_device(torch.from_numpy(tok), dev), lay.positions, None, lay.max_k)
         h = self.model.lm_input(hidden)
-        lp, ent = linear_logprobs(h, self.model.lm_head_weight(), _to_device(torch.from_numpy(tgt), dev),
-                                  self.model.vocab_start, temperature,
-                                  self.ps.tp_group if self.ps.tp_size > 1 else None, self.logprob_chunk)
+        lp, ent = self._logprobs_from_hidden(h, _to_device(torch.from_numpy(tgt), dev), temperature)
         return lp, ent, ("cp", seq, pos, np.asarray(lens, dtype=np.int64))
 
     def _forward_mb(self, input_ids: torch.Tensor, lengths: list[int], rows: list[int], temperature: float):
@@ -313,9 +311,23 @@ class PolicyWorker:
         targets[-1:] = 0
         hidden = self.model(flat_d, pos_d, cu_d, max_len)
         h = self.model.lm_input(hidden)
-        lp, ent = linear_logprobs(h, self.model.lm_head_weight(), targets, self.model.vocab_start, temperature,
-                                  self.ps.tp_group if self.ps.tp_size > 1 else None, self.logprob_chunk)
+        lp, ent = self._logprobs_from_hidden(h, targets, temperature)
         return lp, ent, cu
+
+    def _logprobs_from_hidden(self, h, targets, temperature):
+        """Fused LM-head + log-prob (full vocabulary), or - when the rollout samples
+        with top-k / top-p - the same filter applied at train time."""
+        grp = self.ps.tp_group if self.ps.tp_size > 1 else None
+        gen = self.cfg.get("generation", {}) or {}
+        top_k, top_p = gen.get("top_k"), float(gen.get("top_p", 1.0) or 1.0)
+        if top_k or top_p < 1.0:
+            from rl_b200.ops.fused_linear_logprob import filtered_linear_logprobs
+
+            w = self.model.lm_head_weight()
+            return filtered_linear_logprobs(h, w, targets, self.model.vocab_start, temperature, top_k, top_p,
+                                            grp, chunk=max(1, min(self.logprob_chunk, 1024)))
+        return linear_logprobs(h, self.model.lm_head_weight(), targets, self.model.vocab_start, temperature,
+                               grp, self.logprob_chunk)
 
     def _loss_input(self, loss_fn, ids, lengths, rows, width, temperature):
         """What the loss consumes for one packed micro-batch:

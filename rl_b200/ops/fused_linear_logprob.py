@@ -78,3 +78,43 @@ def linear_logprobs(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.T
     """``(logprobs, entropy)`` of ``targets`` under ``softmax(hidden @ weight^T / T)``
     where ``weight`` is this rank's vocab shard; fp32 ``[T]`` each."""
     return _LinearLogprob.apply(hidden, weight, targets, int(vocab_start), float(temperature), group, int(chunk))
+
+
+def filter_logits_top_k_top_p(logits: torch.Tensor, top_k: Optional[int], top_p: float) -> torch.Tensor:
+    """Mask (to -inf) everything outside the top-k / nucleus-p set of each row,
+    the same filter the rollout sampler applies (ties at the k-th value kept)."""
+    if top_k:
+        kth = torch.topk(logits, min(int(top_k), logits.shape[-1]), dim=-1).values[..., -1:]
+        logits = logits.masked_fill(logits < kth, float("-inf"))
+    if top_p is not None and top_p < 1.0:
+        srt, idx = torch.sort(logits, dim=-1, descending=True)
+        cum = torch.softmax(srt, -1).cumsum(-1)
+        drop = (cum - torch.softmax(srt, -1)) >= top_p  # keep the smallest prefix reaching top_p
+        mask = torch.zeros_like(drop).scatter(-1, idx, drop)
+        logits = logits.masked_fill(mask, float("-inf"))
+    return logits
+
+
+def filtered_linear_logprobs(hidden: torch.Tensor, weight: torch.Tensor, targets: torch.Tensor, vocab_start: int,
+                             temperature: float, top_k: Optional[int], top_p: float, group=None,
+                             chunk: int = 1024):
+    """Training-time log-probabilities under the rollout's top-k / top-p filter
+    (renormalised over the kept tokens), so the ratio in the policy loss compares
+    like with like.  Reference: ``TrainingSamplingParams`` / ``apply_top_k_top_p``
+    (``nemo_rl/algorithms/logits_sampling_utils.py:30,256``).  The vocab shards are
+    all-gathered per chunk of tokens (the filter needs whole rows); returns
+    (logprob [T], entropy [T]) of the filtered distribution."""
+    from rl_b200.parallel.comm import gather_from_sp
+
+    lps, ents = [], []
+    for s in range(0, hidden.shape[0], chunk):
+        e = min(hidden.shape[0], s + chunk)
+        logits = torch.matmul(hidden[s:e], weight.t()).float()
+        if group is not None and dist.get_world_size(group) > 1:
+            logits = gather_from_sp(logits.t().contiguous(), group).t()
+        logits = filter_logits_top_k_top_p(logits / temperature, top_k, top_p)
+        logp = torch.log_softmax(logits, -1)
+        lps.append(logp.gather(1, targets[s:e].long().unsqueeze(1)).squeeze(1))
+        p = logp.exp()
+        ents.append(-(p * torch.where(p > 0, logp, torch.zeros_like(logp))).sum(-1))
+    return torch.cat(lps), torch.cat(ents)

@@ -465,3 +465,59 @@ def test_worker_speculative_config_and_draft_training():
     for _ in range(10):
         l1 = w.train_draft(seqs)
     assert l1 < l0
+
+
+def test_train_time_top_k_top_p_logprobs():
+    """With top-k / top-p rollouts the trainer's log-probs are those of the
+    filtered, renormalised distribution; TP=1 vs the explicit formula."""
+    from rl_b200.ops.fused_linear_logprob import filter_logits_top_k_top_p, filtered_linear_logprobs
+
+    g = torch.Generator().manual_seed(1)
+    h = torch.randn(7, 16, generator=g)
+    w = torch.randn(50, 16, generator=g)
+    tgt = torch.randint(0, 50, (7,), generator=g)
+    logits = h @ w.t()
+    keep = logits.topk(5, -1).values[:, -1:]
+    ref = torch.log_softmax(logits.masked_fill(logits < keep, float("-inf")), -1).gather(1, tgt[:, None]).squeeze(1)
+    lp, _ = filtered_linear_logprobs(h, w, tgt, 0, 1.0, 5, 1.0)
+    assert torch.allclose(lp, ref)
+    # nucleus: the kept set is the smallest prefix of sorted probs whose mass reaches p
+    x = torch.tensor([[3.0, 2.0, 1.0, 0.0]])
+    out = filter_logits_top_k_top_p(x, None, 0.8)
+    p = torch.softmax(x, -1)[0]
+    n_keep = int((torch.cumsum(p, 0) - p < 0.8).sum())
+    assert int(torch.isfinite(out).sum()) == n_keep
+
+
+def test_numa_binding_from_fake_sysfs(tmp_path):
+    from rl_b200.utils.numa import bind_to_gpu_numa, parse_cpulist
+
+    assert parse_cpulist("0-3,8,10-11\n") == [0, 1, 2, 3, 8, 10, 11]
+    dev = tmp_path / "bus" / "pci" / "devices" / "0000:1b:00.0"
+    dev.mkdir(parents=True)
+    before = os.sched_getaffinity(0)
+    cpu = sorted(before)[0]
+    (dev / "local_cpulist").write_text(f"{cpu}\n")
+    try:
+        used = bind_to_gpu_numa(sysfs_root=str(tmp_path), pci_bus_id="1b:00.0")
+        assert used == [cpu] and os.sched_getaffinity(0) == {cpu}
+        assert bind_to_gpu_numa(sysfs_root=str(tmp_path), pci_bus_id="ff:00.0") is None
+    finally:
+        os.sched_setaffinity(0, before)
+
+
+def test_telemetry_spans_and_goodput(tmp_path):
+    import json as _json
+
+    from rl_b200.utils.telemetry import Telemetry
+
+    t = Telemetry(str(tmp_path / "spans.jsonl"))
+    with t.span("step", step=1):
+        with t.span("generation"):
+            pass
+    g = t.goodput({"generation": 2.0, "policy_training": 3.0, "weight_sync": 0.5, "total_step_time": 6.0}, 6.0)
+    assert abs(g["goodput/fraction"] - 5 / 6) < 1e-9 and abs(g["goodput/idle_s"] - 0.5) < 1e-9
+    assert t.flush() == 2
+    recs = [_json.loads(x) for x in open(tmp_path / "spans.jsonl")]
+    assert {r["name"] for r in recs} == {"step", "generation"}
+    assert [r for r in recs if r["name"] == "generation"][0]["parent"] == "step"

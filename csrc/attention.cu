@@ -80,6 +80,19 @@ __device__ __forceinline__ void load_tile(bf16* s, const bf16* g, long long row_
   }
 }
 
+__device__ int g_attn_error = 0;
+
+// Bounded wait (about two seconds) until *p >= v; false on expiry.
+__device__ __forceinline__ bool cp_wait_flag(const uint32_t* p, uint32_t v) {
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t x;
+    asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(x) : "l"(p) : "memory");
+    if ((int)(x - v) >= 0) return true;
+    if (clock64() - t0 > 4000000000LL) return false;
+  }
+}
+
 // ============================================================ decode attention
 template <typename C, int HD, int G>
 __global__ void __launch_bounds__(128)
@@ -587,7 +600,8 @@ template <int HD>
 __global__ void __launch_bounds__(128)
 fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, long long qs,
               long long ks, long long vs, const int* __restrict__ cu, int nq, int nkv, float scale_log2, int causal,
-              bf16* __restrict__ o, float* __restrict__ lse, int T_total, const int* __restrict__ seg) {
+              bf16* __restrict__ o, float* __restrict__ lse, int T_total, const int* __restrict__ seg,
+              const uint32_t* __restrict__ cp_flags, uint32_t cp_epoch, int cp_size) {
   constexpr int BM = 64, BN = 64, CH = HD / 8, KS = HD / 16, NT = HD / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   bf16* Qs = reinterpret_cast<bf16*>(smem_raw);
@@ -615,6 +629,20 @@ fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
   load_tile<CH>(Qs, qg, qs, BM, min(BM, L - m0), tid, 128);
   const int n_end = causal ? min(Lk, m0 + BM + off) : Lk;
   const int nblocks = (n_end + BN - 1) / BN;
+  // context parallelism with the K/V exchange in flight: key block n0 belongs to
+  // chunk n0 / chunk_len of its sequence, owned by rank c (c < cp) or 2cp-1-c;
+  // its rows are valid once that rank's copy flag reaches the epoch
+  auto wait_keys = [&](int n0) {
+    if (cp_flags != nullptr) {
+      if (tid == 0) {
+        const int c = n0 / L;  // every chunk has the segment's query length
+        const int owner = c < cp_size ? c : 2 * cp_size - 1 - c;
+        if (!cp_wait_flag(cp_flags + owner, cp_epoch)) atomicExch(&g_attn_error, 1);
+      }
+      __syncthreads();
+    }
+  };
+  wait_keys(0);
   load_tile<CH>(Ks, kg, ks, BN, min(BN, Lk), tid, 128);
   load_tile<CH>(Vs, vg, vs, BN, min(BN, Lk), tid, 128);
   cp_async_commit();
@@ -635,6 +663,7 @@ fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
     const int buf = nb & 1;
     if (nb + 1 < nblocks) {
       const int n1 = (nb + 1) * BN;
+      wait_keys(n1);
       load_tile<CH>(Ks + (buf ^ 1) * BN * HD, kg + (long long)n1 * ks, ks, BN, min(BN, Lk - n1), tid, 128);
       load_tile<CH>(Vs + (buf ^ 1) * BN * HD, vg + (long long)n1 * vs, vs, BN, min(BN, Lk - n1), tid, 128);
       cp_async_commit();
@@ -1018,7 +1047,8 @@ std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v,
     dim3 grid(nq, (max_seqlen + 63) / 64, B);
     kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
                                         q.stride(0), k.stride(0), v.stride(0), cu.data_ptr<int>(), nq, nkv, scale_log2,
-                                        causal ? 1 : 0, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, nullptr);
+                                        causal ? 1 : 0, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, nullptr,
+                                        nullptr, 0u, 0);
   });
   RLB_CUDA_CHECK(cudaGetLastError());
   return {o, lse};
@@ -1066,8 +1096,13 @@ std::vector<at::Tensor> flash_attn_bwd(at::Tensor dout, at::Tensor q, at::Tensor
 // Segment attention (context parallelism): segment b attends queries
 // [seg[b][0], +seg[b][1]) of q to keys [seg[b][2], +seg[b][3]) of k / v, causal
 // with the last query aligned to the last key.  Segments may share keys.
+// With cp_flags (int32 [cp] on the device) the kernel waits, per key block, for
+// the flag of the rank owning that block's chunk to reach cp_epoch: the K/V
+// exchange of context parallelism may still be landing (copy engines) when the
+// kernel starts.  Chunk lengths must be multiples of 64 (one key block).
 std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
-                                           double scale) {
+                                           double scale, c10::optional<at::Tensor> cp_flags, int64_t cp_epoch,
+                                           int64_t cp_size) {
   check_head_view(q, "q");
   check_head_view(k, "k");
   check_head_view(v, "v");
@@ -1088,7 +1123,10 @@ std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tenso
     dim3 grid(nq, (max_q + 63) / 64, S);
     kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
                                         q.stride(0), k.stride(0), v.stride(0), nullptr, nq, nkv, scale_log2, 1,
-                                        (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, seg.data_ptr<int>());
+                                        (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, seg.data_ptr<int>(),
+                                        cp_flags ? reinterpret_cast<const uint32_t*>(cp_flags->data_ptr<int>())
+                                                 : nullptr,
+                                        (uint32_t)cp_epoch, (int)cp_size);
   });
   RLB_CUDA_CHECK(cudaGetLastError());
   return {o, lse};
@@ -1247,4 +1285,14 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
   }
   RLB_CUDA_CHECK(cudaGetLastError());
   return out;
+}
+
+int64_t attn_error_flag(bool reset) {
+  int v = 0;
+  RLB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, rlb::g_attn_error, sizeof(int)));
+  if (reset) {
+    const int z = 0;
+    RLB_CUDA_CHECK(cudaMemcpyToSymbol(rlb::g_attn_error, &z, sizeof(int)));
+  }
+  return v;
 }

@@ -56,7 +56,9 @@ void stream_write_u32(int64_t ptr, int64_t value);
 std::vector<at::Tensor> spec_verify(at::Tensor target_logits, at::Tensor draft_logits, at::Tensor draft_tokens,
                                     double temperature, int64_t seed, int64_t offset);
 std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
-                                           double scale);
+                                           double scale, c10::optional<at::Tensor> cp_flags, int64_t cp_epoch,
+                                           int64_t cp_size);
+int64_t attn_error_flag(bool reset);
 std::vector<at::Tensor> flash_attn_seg_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
                                            at::Tensor lse, at::Tensor seg, int64_t max_k, double scale);
 void ep_scatter(at::Tensor src, c10::optional<at::Tensor> src_row, at::Tensor dst_rank, at::Tensor dst_row,
@@ -108,7 +110,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_scatter", &ep_scatter, "MoE token rows -> peers' receive buffers at their final positions (P2P stores)");
   m.def("ep_consume", &ep_consume, "wait for every source's scatter, copy the received rows out, acknowledge");
   m.def("ep_error_flag", &ep_error_flag, py::arg("reset") = false);
-  m.def("flash_attn_seg_fwd", &flash_attn_seg_fwd, "segment attention (query chunks vs key prefixes), forward");
+  m.def("flash_attn_seg_fwd", &flash_attn_seg_fwd, "segment attention (query chunks vs key prefixes), forward",
+        py::arg("q"), py::arg("k"), py::arg("v"), py::arg("seg"), py::arg("max_q"), py::arg("scale"),
+        py::arg("cp_flags") = py::none(), py::arg("cp_epoch") = 0, py::arg("cp_size") = 0);
+  m.def("attn_error_flag", &attn_error_flag, py::arg("reset") = false);
   m.def("flash_attn_seg_bwd", &flash_attn_seg_bwd, "segment attention backward (shared keys accumulate)");
   m.def("spec_verify", &spec_verify, "speculative decoding: rejection-sampling verification of draft tokens");
   m.def("stream_write_u32", &stream_write_u32, "stream memory write (no kernel) of a 32-bit word");

@@ -88,8 +88,12 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
       int it = 0;
       for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x) {
         const int mt = item % num_m, split = item / num_m;
-        const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        const int kb0 = split * kb_per, nkb = min(num_kb, kb0 + kb_per) - kb0;
+        // every CTA reads the same x tiles: start each CTA at a different K-block so
+        // the ~148 concurrent readers of one x tile (an L2 hot spot) spread out
+        const int rot = nkb > 0 ? (int)(blockIdx.x % nkb) : 0;
+        for (int kk = 0; kk < nkb; ++kk, ++it) {
+          const int kb = kb0 + (kk + rot) % nkb;
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait_err(bar_empty + 8 * s, ph ^ 1, abort_flag, &g_dec_error, 1)) break;
@@ -104,14 +108,14 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
       int it = 0, local = 0;
       for (int item = blockIdx.x; item < items && !*abort_flag; item += gridDim.x, ++local) {
         const int split = item / num_m;
-        const int kb0 = split * kb_per, kb1 = min(num_kb, kb0 + kb_per);
+        const int kb0 = split * kb_per, nkb = min(num_kb, kb0 + kb_per) - kb0;
         const int acc = local & 1;
         const uint32_t aph = (local >> 1) & 1;
         if (!mbar_wait_err(bar_tempty + 8 * acc, aph ^ 1, abort_flag, &g_dec_error, 1)) break;
         tc_fence_after();
         const uint32_t tmem_d = tmem_base + acc * BN;
         bool ok = true;
-        for (int kb = kb0; kb < kb1; ++kb, ++it) {
+        for (int kk = 0; kk < nkb; ++kk, ++it) {
           const int s = it % STAGES;
           const uint32_t ph = (it / STAGES) & 1;
           if (!mbar_wait_err(bar_full + 8 * s, ph, abort_flag, &g_dec_error, 1)) {
@@ -123,7 +127,7 @@ gemm_decode_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_cons
 #pragma unroll
           for (int k = 0; k < BK / 16; ++k)
             umma_bf16(tmem_d, desc_kmajor_sw128(a0 + k * 32), desc_kmajor_sw128(b0 + k * 32), IDESC,
-                      (kb > kb0 || k > 0) ? 1u : 0u);
+                      (kk > 0 || k > 0) ? 1u : 0u);
           umma_commit(bar_empty + 8 * s);
         }
         if (!ok) break;

@@ -279,8 +279,12 @@ class PolicyWorker:
         from rl_b200.parallel.context_parallel import cp_layout
 
         lens = [int(lengths[r]) for r in rows]
-        unit = 128 * self.ps.tp_size // 2 if (self.sequence_parallel and self.device.type == "cuda") else \
-            max(1, self.ps.tp_size)
+        if self.device.type == "cuda":
+            # chunks of whole 64-key blocks (overlapped K/V exchange); under SP
+            # also 128 x TP tokens per rank for the fused GEMM + collectives
+            unit = max(64, 64 * self.ps.tp_size if self.sequence_parallel else 64)
+        else:
+            unit = max(1, self.ps.tp_size)
         lay = cp_layout(lens, self.ps.cp_size, self.ps.cp_rank, self.device, unit=unit)
         seq = lay.seq_of_local.cpu().numpy()
         pos = lay.positions.cpu().numpy().astype(np.int64)
@@ -767,6 +771,9 @@ class PolicyWorker:
             if getattr(self.model, attr, None) is not None:
                 getattr(self.model, attr).close()
                 setattr(self.model, attr, None)
+        if getattr(self.model, "_cp_ex", None) is not None:
+            self.model._cp_ex.close()
+            self.model._cp_ex = None
         if getattr(self.model, "_ep_ex", None) is not None:
             for x in self.model._ep_ex:
                 x.close()

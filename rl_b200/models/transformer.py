@@ -190,6 +190,7 @@ class TransformerLM(nn.Module):
         self._fused_rs = None
         self._fused_ag = None
         self._ep_ex = None
+        self._cp_ex = None
         self._cp_layout = None  # rl_b200.parallel.context_parallel.CPLayout of the current micro-batch
         self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
@@ -400,9 +401,21 @@ class TransformerLM(nn.Module):
             h = copy_to_tp(h, self.ps.tp_group)
         qkv = self._qkv(i, h, positions)
         q, k, v = self._split_heads(qkv)
-        kf = gather_kv_cp(k, lay, self.ps.cp_group)
-        vf = gather_kv_cp(v, lay, self.ps.cp_group)
-        o = cp_attention(q, kf, vf, lay, 1.0 / math.sqrt(self.hd))
+        if (self.fused_collectives and q.is_cuda and q.dtype == torch.bfloat16
+                and all(int(c) % 64 == 0 for c in lay.q_len.tolist())):
+            from rl_b200.parallel.context_parallel import CPKVExchange, cp_attention_fused
+
+            ex = self._cp_ex
+            E = k.shape[1] * k.shape[2]
+            if ex is None or ex.max_rows < k.shape[0] or ex.E != E:
+                if ex is not None:
+                    ex.close()
+                ex = self._cp_ex = CPKVExchange(self.ps.cp_group, max(k.shape[0], 8192), E)
+            o = cp_attention_fused(q, k.contiguous(), v.contiguous(), lay, ex, 1.0 / math.sqrt(self.hd))
+        else:
+            kf = gather_kv_cp(k, lay, self.ps.cp_group)
+            vf = gather_kv_cp(v, lay, self.ps.cp_group)
+            o = cp_attention(q, kf, vf, lay, 1.0 / math.sqrt(self.hd))
         return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
                                          p + "self_attn.o_proj.weight")
 

@@ -421,3 +421,64 @@ def test_ep_moe_fused_dispatch_2gpu():
         assert not o["missing"], o["missing"]
         worst = max(o["errs"].items(), key=lambda kv: kv[1])
         assert worst[1] < 3e-2, worst
+
+
+def case_cp_model(rank: int):
+    """CP=2 transformer on 2 GPUs: the overlapped K/V exchange (copy-engine pulls +
+    per-block flag waits in the attention kernel) against the NCCL all-gather
+    path (forward output and gradients)."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.context_parallel import cp_layout
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(cp=2, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="cp", vocab_size=1024, hidden_size=512, num_layers=2, num_heads=8, num_kv_heads=4,
+                      head_dim=64, ffn_hidden_size=1024, rope_theta=10000.0, max_position_embeddings=4096)
+    lens = [700, 1500, 256]
+    lay = cp_layout(lens, 2, ps.cp_rank, torch.device("cuda"), unit=64)
+    g = torch.Generator().manual_seed(3)
+    ids = torch.randint(0, cfg.vocab_size, (lay.T_local,), generator=torch.Generator().manual_seed(3 + rank)).cuda()
+    proj = torch.randn(lay.T_local, cfg.hidden_size, generator=g).cuda()
+    res = {}
+    for fused in (False, True):
+        m = TransformerLM(cfg, ps, seed=5)
+        m.fused_collectives = fused
+        m._cp_layout = lay
+        hs = []
+        for _ in range(2):
+            h = m(ids, lay.positions, None, lay.max_k)
+            (h.float() * proj).sum().backward()
+            hs.append(h.float().clone())
+        torch.cuda.synchronize()
+        grads = {n: p.grad.float().clone() for n, p in m._params.items() if p.grad is not None}
+        res[fused] = (hs, grads, m._cp_ex is not None)
+        if m._cp_ex is not None:
+            m._cp_ex.close()
+    errs = {f"hidden{j}": ((res[True][0][j] - res[False][0][j]).norm() / res[False][0][j].norm()).item()
+            for j in range(2)}
+    for n_, g0 in res[False][1].items():
+        if n_ in res[True][1]:
+            errs[n_] = ((res[True][1][n_] - g0).norm() / (g0.norm() + 1e-12)).item()
+    flag = _ext.ext().attn_error_flag(True)
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"errs": errs, "used": res[True][2], "flag": flag}
+
+
+def test_cp_overlapped_kv_exchange_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_cp_model, 2, timeout_s=300)
+    for o in outs:
+        assert o["used"], "overlapped CP exchange was not taken"
+        assert o["flag"] == 0
+        worst = max(o["errs"].items(), key=lambda kv: kv[1])
+        assert worst[1] < 3e-2, worst

@@ -270,9 +270,17 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 with timer.time("data_processing"):
                     train_data, adv_stats = build_train_data(rollout, estimator, cfg, loss_cfg, rollout["group_id"])
                 # ---- logprobs ----
+                # one optimizer step per rollout batch: the weights before the step are
+                # the ones the step's own forward runs with, so the separate "previous
+                # policy" pass is folded into training (exactly the same values)
+                one_step = train_data.size <= min(local_gbs, train_data.size)
+                reuse_prev = bool(cfg.get("reuse_train_logprobs_as_prev", True)) and one_step
                 with timer.time("policy_and_reference_logprobs"):
                     policy.prepare_for_lp_inference()
-                    train_data["prev_logprobs"] = policy.get_logprobs(train_data)["logprobs"]
+                    if reuse_prev:
+                        train_data["prev_logprobs"] = torch.zeros_like(train_data["generation_logprobs"])
+                    else:
+                        train_data["prev_logprobs"] = policy.get_logprobs(train_data)["logprobs"]
                     if kl_on:
                         train_data["reference_policy_logprobs"] = \
                             policy.get_reference_policy_logprobs(train_data)["reference_logprobs"]
@@ -281,7 +289,7 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                     policy.prepare_for_training()
                     n_rows = train_data.size
                     gbs = min(local_gbs, n_rows)
-                    train_results = policy.train(train_data, loss_fn, gbs=gbs)
+                    train_results = policy.train(train_data, loss_fn, gbs=gbs, prev_from_current=reuse_prev)
                 if getattr(policy, "draft", None) is not None:
                     with timer.time("draft_training"):
                         train_results["draft_loss"] = policy.train_draft(train_data)

@@ -486,16 +486,24 @@ class PolicyWorker:
 
     # ------------------------------------------------------------- train
     def train(self, data: BatchedDataDict, loss_fn, gbs: Optional[int] = None, eval_mode: bool = False,
-              temperature: Optional[float] = None, pair_rows: bool = False) -> dict:
+              temperature: Optional[float] = None, pair_rows: bool = False, prev_from_current: bool = False) -> dict:
         """One or more optimizer steps over ``data`` (this rank's shard).
 
         ``gbs`` is the LOCAL number of rows per optimizer step (global batch / dp).
-        ``pair_rows`` keeps rows (2i, 2i+1) in one micro-batch (preference losses)."""
+        ``pair_rows`` keeps rows (2i, 2i+1) in one micro-batch (preference losses).
+        ``prev_from_current``: ``data`` is consumed in ONE optimizer step, so the
+        log-probs of the weights before the step are exactly this step's forward
+        log-probs; the loss takes them (detached) as ``prev_logprobs`` and the
+        separate inference pass is skipped by the caller."""
+        if prev_from_current and gbs is not None and gbs < data["input_ids"].shape[0]:
+            raise ValueError("prev_from_current needs the whole batch in one optimizer step")
         self._pair_rows = pair_rows
+        self._prev_from_current = prev_from_current
         try:
             return self._train(data, loss_fn, gbs, eval_mode, temperature)
         finally:
             self._pair_rows = False
+            self._prev_from_current = False
 
     def _train(self, data: BatchedDataDict, loss_fn, gbs, eval_mode, temperature) -> dict:
         B = data["input_ids"].shape[0]
@@ -577,6 +585,10 @@ class PolicyWorker:
             if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
         mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
                               for k, v in st.dev_data.items()})
+        if getattr(self, "_prev_from_current", False) and "prev_logprobs" in mb:
+            prev = mb["prev_logprobs"].clone()
+            prev[:, 1:width] = curr.detach().to(prev.dtype)
+            mb["prev_logprobs"] = prev
         if self.ps.cp_size > 1:
             if getattr(st.loss_fn, "loss_type", None) is not None and \
                     getattr(st.loss_fn.loss_type, "value", "") == "sequence_level":

@@ -521,3 +521,23 @@ def test_telemetry_spans_and_goodput(tmp_path):
     recs = [_json.loads(x) for x in open(tmp_path / "spans.jsonl")]
     assert {r["name"] for r in recs} == {"step", "generation"}
     assert [r for r in recs if r["name"] == "generation"][0]["parent"] == "step"
+
+
+def test_prev_logprobs_folded_into_training_forward():
+    """One optimizer step per batch: taking prev_logprobs from the step's own
+    forward equals the separate inference pass."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from tests.dist_cases import make_batch
+
+    data = make_batch(B=8, S=24, seed=7)
+    lf = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
+    a = _tiny_policy(seed=4)
+    d1 = data.copy()
+    d1["prev_logprobs"] = a.get_logprobs(d1)["logprobs"]
+    ra = a.train(d1, lf, gbs=8)
+    b = _tiny_policy(seed=4)
+    d2 = data.copy()
+    d2["prev_logprobs"] = torch.zeros_like(d2["prev_logprobs"])
+    rb = b.train(d2, lf, gbs=8, prev_from_current=True)
+    assert abs(ra["loss"] - rb["loss"]) < 1e-6 and abs(ra["grad_norm"] - rb["grad_norm"]) < 1e-5
+    assert torch.allclose(a.model.flat_param, b.model.flat_param)

@@ -57,6 +57,8 @@ def parse():
     p.add_argument("--gen-tp", type=int, default=0,
                    help="rollout tensor parallelism: 0 = training TP (in-place refit), 1 = full rollout weights per GPU "
                         "(refit reshards over NVLink)")
+    p.add_argument("--act-ckpt", type=int, default=-1,
+                   help="activation checkpointing: -1 = on for one GPU (memory), off when TP >= 2 (activations fit)")
     p.add_argument("--mb-tokens", type=int, default=16384)
     p.add_argument("--kl", type=float, default=0.01)
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for scoring)")
@@ -178,7 +180,7 @@ def main():
         "logprob_chunk_size": 4096, "max_grad_norm": 1.0,
         "optimizer": {"name": "torch.optim.AdamW",
                       "kwargs": {"lr": 3e-7, "weight_decay": 0.01, "betas": [0.9, 0.999], "eps": 1e-8}},
-        "megatron_cfg": {"activation_checkpointing": True, "sequence_parallel": (tp > 1) if args.sp < 0 else bool(args.sp)},
+        "megatron_cfg": {"activation_checkpointing": (tp < 2) if args.act_ckpt < 0 else bool(args.act_ckpt), "sequence_parallel": (tp > 1) if args.sp < 0 else bool(args.sp)},
         "generation": {"temperature": 1.0, "top_p": 1.0, "top_k": None, "max_new_tokens": args.max_new,
                        "max_num_seqs": 512, "mcore_generation_config": {"block_size_tokens": 256},
                        "tensor_parallel_size": args.gen_tp or tp},
@@ -245,7 +247,8 @@ def main():
                     "seeded-hash reward",
             "config": {"model": "Llama-3.1-8B-shape" + ("" if not args.layers else f" ({args.layers} layers: INVALID)"),
                        "global_batch": prompts_global * G, "seq_len": max_len,
-                       "parallelism": f"tp{tp}dp{ps.dp_size}", "rollout_tp": args.gen_tp or tp, "prompts_per_step": prompts_global,
+                       "parallelism": f"tp{tp}dp{ps.dp_size}", "rollout_tp": args.gen_tp or tp,
+                       "activation_checkpointing": pcfg["megatron_cfg"]["activation_checkpointing"], "prompts_per_step": prompts_global,
                        "generations_per_prompt": G, "max_new_tokens": args.max_new, "kl_penalty": args.kl,
                        "l2": "working set (16 GB bf16 weights + KV cache) far above the 126 MB L2; no flush needed",
                        "mean_gen_tokens": gen_tokens / max(1, len(timed)) / (prompts_global * G)},

@@ -53,6 +53,9 @@ void refit_copy(at::Tensor tasks, at::Tensor dst);
 at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
 at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n, int64_t me, int64_t epoch);
 void stream_write_u32(int64_t ptr, int64_t value);
+at::Tensor ar_add_rmsnorm(at::Tensor partial, at::Tensor resid, at::Tensor w, double eps, std::vector<int64_t> slots,
+                          std::vector<int64_t> flags, int64_t me, int64_t cap, at::Tensor ctr, at::Tensor done);
+int64_t decode_ar_error_flag(bool reset);
 std::vector<at::Tensor> spec_verify(at::Tensor target_logits, at::Tensor draft_logits, at::Tensor draft_tokens,
                                     double temperature, int64_t seed, int64_t offset);
 std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
@@ -116,6 +119,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attn_error_flag", &attn_error_flag, py::arg("reset") = false);
   m.def("flash_attn_seg_bwd", &flash_attn_seg_bwd, "segment attention backward (shared keys accumulate)");
   m.def("spec_verify", &spec_verify, "speculative decoding: rejection-sampling verification of draft tokens");
+  m.def("ar_add_rmsnorm", &ar_add_rmsnorm, "TP all-reduce (peer loads) + residual add + RMSNorm, one kernel");
+  m.def("decode_ar_error_flag", &decode_ar_error_flag, py::arg("reset") = false);
   m.def("stream_write_u32", &stream_write_u32, "stream memory write (no kernel) of a 32-bit word");
   m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
   m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);

@@ -783,6 +783,10 @@ class PolicyWorker:
             if getattr(self.model, attr, None) is not None:
                 getattr(self.model, attr).close()
                 setattr(self.model, attr, None)
+        for mdl in {id(self.model): self.model, id(self.gen_model): self.gen_model}.values():
+            if getattr(mdl, "_decode_ar", None) is not None:
+                mdl._decode_ar.close()
+                mdl._decode_ar = None
         if getattr(self.model, "_cp_ex", None) is not None:
             self.model._cp_ex.close()
             self.model._cp_ex = None

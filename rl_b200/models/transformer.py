@@ -191,6 +191,7 @@ class TransformerLM(nn.Module):
         self._fused_ag = None
         self._ep_ex = None
         self._cp_ex = None
+        self._decode_ar = None
         self._cp_layout = None  # rl_b200.parallel.context_parallel.CPLayout of the current micro-batch
         self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
         self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
@@ -666,10 +667,30 @@ class TransformerLM(nn.Module):
         h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], eps)
         return h[last_token_index]
 
+    def _decode_ar_op(self, B: int):
+        """Fused TP all-reduce + add + RMSNorm for decode (None when not applicable)."""
+        if not (self.ps.tp_size > 1 and self.fused_collectives and self.device.type == "cuda"
+                and self.dtype == torch.bfloat16):
+            return None
+        op = self._decode_ar
+        if op is None or op.cap < B:
+            if torch.cuda.is_current_stream_capturing():
+                raise RuntimeError("decode all-reduce buffers must be created before graph capture")
+            if op is not None:
+                op.close()
+            from rl_b200.parallel.fused import DecodeAllReduceNorm
+
+            op = self._decode_ar = DecodeAllReduceNorm(self.ps.tp_group, max(B, 512), self.cfg.hidden_size)
+        return op
+
     @torch.no_grad()
     def forward_decode(self, tokens, positions, kv: KVCache, block_tables, seq_lens, slot_mapping,
                        max_seq_len: int = 0) -> torch.Tensor:
         """One decode step for ``B`` sequences: ``tokens [B]`` -> hidden ``[B, H]``."""
+        ar = self._decode_ar_op(tokens.shape[0]) if not self.cfg.is_moe else None
+        if ar is not None:
+            return self._forward_decode_fused_ar(tokens, positions, kv, block_tables, seq_lens, slot_mapping,
+                                                 max_seq_len, ar)
         x = self.embed_full(tokens)
         resid = None
         eps = self.cfg.rms_eps
@@ -691,6 +712,30 @@ class TransformerLM(nn.Module):
             m = self._mlp_infer(i, h2)
             x, resid = s2, m
         h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], eps)
+        return h
+
+    def _forward_decode_fused_ar(self, tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len, ar):
+        """Decode step with every row-parallel output reduced by the fused
+        peer-memory all-reduce + residual add + RMSNorm (no NCCL in the step)."""
+        eps = self.cfg.rms_eps
+        s = self.embed_full(tokens).contiguous()  # residual stream, updated in place
+        h = rms_norm(s, self._params["model.layers.0.input_layernorm.weight"], eps)
+        L = self.cfg.num_layers
+        for i in range(L):
+            p = f"model.layers.{i}."
+            qkv = self._qkv(i, h, positions)
+            q, k, v = self._split_heads(qkv)
+            kc, vc = kv.layer(i)
+            write_kv_cache(k, v, kc, vc, slot_mapping)
+            o = paged_decode_attention(q, kc, vc, block_tables, seq_lens, max_seq_len=max_seq_len,
+                                       k_scale=kv.k_scale, v_scale=kv.v_scale)
+            a = linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"])
+            h2 = ar(a, s, self._params[p + "post_attention_layernorm.weight"], eps)
+            gu = linear(h2, self._params[p + "mlp.gate_up_proj.weight"])
+            m = linear(swiglu(gu), self._params[p + "mlp.down_proj.weight"])
+            w_next = self._params[f"model.layers.{i + 1}.input_layernorm.weight"] if i + 1 < L \
+                else self._params["model.norm.weight"]
+            h = ar(m, s, w_next, eps)
         return h
 
     def embed_full(self, ids: torch.Tensor) -> torch.Tensor:

@@ -34,6 +34,7 @@ _KERNELS_PER_CALL = {
     "gemm_error_flag": 0,
     "gemm_decode_error_flag": 0,
     "stream_write_u32": 0,
+    "decode_ar_error_flag": 0,
     "attn_error_flag": 0,
     "ep_error_flag": 0,
     "symm_alloc": 0,

@@ -21,7 +21,7 @@ import torch.distributed as dist
 from rl_b200.ops._ext import ext
 from rl_b200.parallel.symm import SymmetricBuffer
 
-__all__ = ["GemmReduceScatter", "row_parallel_rs", "AllGatherGemm", "column_parallel_ag"]
+__all__ = ["GemmReduceScatter", "row_parallel_rs", "AllGatherGemm", "column_parallel_ag", "DecodeAllReduceNorm"]
 
 
 class _RowParallelRS(torch.autograd.Function):
@@ -211,3 +211,29 @@ def _copy_from_ptr(dst: torch.Tensor, src_ptr: int) -> None:
     address into ``dst`` on the current stream."""
     src = ext().symm_view(src_ptr, dst.numel(), 15, dst.device.index)
     dst.view(-1).copy_(src, non_blocking=True)
+
+
+class DecodeAllReduceNorm:
+    """Decode-step TP all-reduce fused with the residual add and RMSNorm
+    (``csrc/decode_ar.cu``): ``h = RMSNorm(resid + sum_r partial_r) * w`` with
+    ``resid`` updated in place, over symmetric slots and per-row flags of the TP
+    group.  The epoch lives in a device counter, so the op replays in CUDA graphs;
+    it must be created (collective) outside graph capture."""
+
+    def __init__(self, group, cap: int, H: int):
+        self.group = group
+        self.n = dist.get_world_size(group)
+        self.me = dist.get_rank(group)
+        self.cap, self.H = int(cap), int(H)
+        self.slots = SymmetricBuffer(2 * self.cap * self.H * 2, group)
+        self.flags = SymmetricBuffer(self.n * self.cap * 4, group)
+        self.ctr = torch.zeros(1, dtype=torch.int32, device="cuda")
+        self.done = torch.zeros(1, dtype=torch.int32, device="cuda")
+
+    def __call__(self, partial: torch.Tensor, resid: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+        return ext().ar_add_rmsnorm(partial.contiguous(), resid, w, float(eps), self.slots.ptrs, self.flags.ptrs,
+                                    self.me, self.cap, self.ctr, self.done)
+
+    def close(self) -> None:
+        self.slots.close()
+        self.flags.close()

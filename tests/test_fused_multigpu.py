@@ -482,3 +482,73 @@ def test_cp_overlapped_kv_exchange_2gpu():
         assert o["flag"] == 0
         worst = max(o["errs"].items(), key=lambda kv: kv[1])
         assert worst[1] < 3e-2, worst
+
+
+def case_decode_ar(rank: int):
+    """TP=2 decode step: fused peer-memory all-reduce + residual add + RMSNorm
+    against NCCL all-reduce + add_rms_norm, three calls in a row and once more
+    under CUDA-graph replay."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import KVCache, TransformerLM
+    from rl_b200.ops import _ext
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(tp=2, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="dar", vocab_size=1024, hidden_size=512, num_layers=3, num_heads=8, num_kv_heads=4,
+                      head_dim=64, ffn_hidden_size=1024, rope_theta=10000.0, max_position_embeddings=512)
+    B, bs = 48, 16
+    m = TransformerLM(cfg, ps, seed=5)
+    kv = KVCache(cfg.num_layers, B * 4 + 1, bs, m.nkv, m.hd, torch.bfloat16, torch.device("cuda"))
+    bt = (torch.arange(B * 4, dtype=torch.int32).view(B, 4) + 1).cuda()
+    outs = {}
+    for fused in (False, True):
+        m.fused_collectives = fused
+        res = []
+        for step in range(3):
+            g = torch.Generator().manual_seed(step)
+            tok = torch.randint(0, cfg.vocab_size, (B,), generator=g).cuda()
+            pos = torch.full((B,), step, dtype=torch.int32, device="cuda")
+            slot = bt[:, 0].long() * bs + step
+            res.append(m.forward_decode(tok, pos, kv, bt, pos + 1, slot, 64).float().clone())
+        outs[fused] = res
+    # graph replay of the fused step
+    tok = torch.randint(0, cfg.vocab_size, (B,), generator=torch.Generator().manual_seed(9)).cuda()
+    pos = torch.full((B,), 3, dtype=torch.int32, device="cuda")
+    slot = bt[:, 0].long() * bs + 3
+    eager = m.forward_decode(tok, pos, kv, bt, pos + 1, slot, 64).float().clone()
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        m.forward_decode(tok, pos, kv, bt, pos + 1, slot, 64)
+    torch.cuda.current_stream().wait_stream(s)
+    gph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(gph):
+        y = m.forward_decode(tok, pos, kv, bt, pos + 1, slot, 64)
+    replays = []
+    for _ in range(2):
+        gph.replay()
+        torch.cuda.synchronize()
+        replays.append(y.float().clone())
+    errs = [((a - b).norm() / b.norm()).item() for a, b in zip(outs[True], outs[False])]
+    errs += [((r - eager).norm() / eager.norm()).item() for r in replays]
+    flag = _ext.ext().decode_ar_error_flag(True)
+    del gph
+    m._decode_ar.close()
+    dist.barrier()
+    dist.destroy_process_group()
+    return {"errs": errs, "flag": flag}
+
+
+def test_decode_allreduce_rmsnorm_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_decode_ar, 2, timeout_s=300)
+    for o in outs:
+        assert o["flag"] == 0
+        assert max(o["errs"]) < 1e-2, o["errs"]

@@ -165,8 +165,18 @@ def load_hf_state_dict(model, sd: dict[str, torch.Tensor]) -> None:
 
 
 def save_hf_checkpoint(model, path: str, max_shard_bytes: int = 5 << 30) -> None:
-    """Consolidated HF checkpoint (rank 0 writes; all ranks join the gathers)."""
+    """Consolidated HF checkpoint (rank 0 writes; all ranks join the gathers).
+    Under pipeline parallelism the stages' tensors are gathered to rank 0 over
+    the pipeline group of the first TP / CP / DP coordinate."""
     sd = hf_state_dict(model)
+    ps = model.ps
+    if ps.pp_size > 1 and ps.tp_rank == 0 and ps.cp_rank == 0 and ps.dp_rank == 0:
+        parts = [None] * ps.pp_size if ps.pp_rank == 0 else None
+        dist.gather_object({k: v.cpu() for k, v in sd.items()}, parts, dst=ps.pp_ranks[0], group=ps.pp_group)
+        if ps.pp_rank == 0:
+            sd = {}
+            for part in parts:
+                sd.update(part)
     rank0 = (not dist.is_initialized()) or dist.get_rank() == 0
     if not rank0:
         return
@@ -219,7 +229,9 @@ def save_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional
               "pp": ps.pp_size, "params": [{"name": sp.name, "shape": list(sp.shape), "tp_dim": sp.tp_dim,
                                             "ep_dim": sp.ep_dim, "offset": sp.offset, "numel": sp.numel}
                                            for sp in model.specs]}
-    torch.save({"flat_param": model.flat_param.detach().cpu(), "tp_rank": ps.tp_rank, "ep_rank": ps.ep_rank},
+    # each shard carries its own parameter layout (pipeline stages hold different names)
+    torch.save({"flat_param": model.flat_param.detach().cpu(), "tp_rank": ps.tp_rank, "ep_rank": ps.ep_rank,
+                "pp_rank": ps.pp_rank, "params": layout["params"]},
                os.path.join(it, f"__{rank}.pt"))
     if rank == 0:
         with open(os.path.join(it, "metadata.json"), "w") as f:
@@ -238,7 +250,8 @@ def load_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional
         meta = json.load(f)
     ps = model.ps
     world = dist.get_world_size() if dist.is_initialized() else 1
-    same = (meta["world_size"] == world and meta["tp"] == ps.tp_size and meta["ep"] == ps.ep_size)
+    same = (meta["world_size"] == world and meta["tp"] == ps.tp_size and meta["ep"] == ps.ep_size
+            and meta.get("pp", 1) == ps.pp_size)
     with torch.no_grad():
         if same:
             sh = torch.load(os.path.join(it, f"__{rank}.pt"), map_location="cpu")
@@ -246,23 +259,26 @@ def load_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional
         else:
             # re-layout: rebuild full tensors from the saved shards, then re-slice
             full: dict[str, torch.Tensor] = {}
-            by_name = {p["name"]: p for p in meta["params"]}
-            shards: dict[tuple, torch.Tensor] = {}
+            by_name: dict[str, dict] = {}
+            pieces: dict[str, dict] = {}  # name -> {(tp_rank, ep_rank): tensor}
             for r in range(meta["world_size"]):
                 d = torch.load(os.path.join(it, f"__{r}.pt"), map_location="cpu")
-                shards[(d["tp_rank"], d["ep_rank"])] = d["flat_param"]
+                for p in d.get("params", meta["params"]):
+                    by_name.setdefault(p["name"], p)
+                    pieces.setdefault(p["name"], {})[(d["tp_rank"], d["ep_rank"])] = \
+                        d["flat_param"][p["offset"]:p["offset"] + p["numel"]].view(p["shape"])
             for name, p in by_name.items():
+                got = pieces[name]
                 if p["tp_dim"] is not None and meta["tp"] > 1:
-                    parts = [shards[(t, 0)][p["offset"]:p["offset"] + p["numel"]].view(p["shape"])
-                             for t in range(meta["tp"]) if (t, 0) in shards]
+                    e0 = min(e for _, e in got)
+                    parts = [got[(t, e0)] for t in range(meta["tp"]) if (t, e0) in got]
                     full[name] = _merge_tp(model, name, parts, p["tp_dim"])
                 elif p["ep_dim"] is not None and meta["ep"] > 1:
-                    parts = [shards[(0, e)][p["offset"]:p["offset"] + p["numel"]].view(p["shape"])
-                             for e in range(meta["ep"])]
+                    t0 = min(t for t, _ in got)
+                    parts = [got[(t0, e)] for e in range(meta["ep"])]
                     full[name] = torch.cat(parts, p["ep_dim"])
                 else:
-                    any_sh = next(iter(shards.values()))
-                    full[name] = any_sh[p["offset"]:p["offset"] + p["numel"]].view(p["shape"])
+                    full[name] = next(iter(got.values()))
             for sp, prm in model.named_flat_params():
                 t = full[sp.name]
                 if sp.tp_dim is not None and ps.tp_size > 1:

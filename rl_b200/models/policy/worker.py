@@ -112,6 +112,13 @@ class PolicyWorker:
             raise NotImplementedError(f"generation TP {self.gen_tp} must be 1 or the training TP {self.ps.tp_size}")
         self.fp8_rollout = str(vcfg.get("precision", gen_cfg.get("precision", "bfloat16"))).lower() == "fp8"
         resharded = self.gen_tp != self.ps.tp_size
+        self.pp = self.ps.pp_size
+        if self.pp > 1:
+            for what, bad in (("context parallelism", self.ps.cp_size > 1), ("a different rollout TP", resharded),
+                              ("LoRA", bool((policy_cfg.get("lora_cfg") or mc.get("lora_cfg") or {}).get("enabled"))),
+                              ("fp8 rollout weights", self.fp8_rollout)):
+                if bad:
+                    raise NotImplementedError(f"pipeline parallelism with {what}")
         # symmetric memory (every rank of the node maps every other's parameter and
         # gradient buffers): needed by the reshard refit and the fused DP optimizer
         from rl_b200.parallel.symm import NodeSymmetric
@@ -153,13 +160,22 @@ class PolicyWorker:
                                    min_lr=float(mopt.get("min_lr", 0.0)), dp_group=grad_group,
                                    tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel,
                                    edp_group=self.ps.edp_group, ep_group=self.ps.ep_group,
-                                   symmetric=self.symmetric if fused_dp else None)
+                                   symmetric=self.symmetric if fused_dp else None,
+                                   pp_group=self.ps.pp_group if self.pp > 1 else None)
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
         self.gen_model = self.model
         if self.lora is not None:
             # rollout copy with the adapters merged in (same TP layout)
             self.gen_model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype,
+                                           skip_init=True)
+        elif self.pp > 1:
+            # rollout runs the whole depth on every stage's GPU (same TP layout);
+            # the refit gathers the other stages' layers over the pipeline group
+            import dataclasses
+
+            gps = dataclasses.replace(self.ps, pp_size=1, pp_rank=0, pp_group=None, pp_ranks=[self.ps.rank])
+            self.gen_model = TransformerLM(self.model_cfg, gps, device=self.device, dtype=self.dtype,
                                            skip_init=True)
         elif resharded:
             from rl_b200.parallel.state import single_process_state
@@ -199,6 +215,12 @@ class PolicyWorker:
         if bool(policy_cfg.get("kv_cache_in_grad_arena", self.device.type == "cuda")):
             self.engine.kv_arena = lambda: self.optimizer.main_grad
         self.timer = Timer()
+        self._pp_comm = None
+        self._pp_in: Optional[torch.Tensor] = None
+        if self.pp > 1:
+            from rl_b200.parallel.pipeline import PipelineComm
+
+            self._pp_comm = PipelineComm(self.ps)
         self.weight_sync.sync()  # the rollout copy starts from the initial weights
 
     def _make_weight_sync(self, resharded: bool):
@@ -209,6 +231,11 @@ class PolicyWorker:
             if resharded:
                 raise NotImplementedError("LoRA with a different rollout TP layout")
             return LoRAMergeSynchronizer(self.lora, self.gen_model)
+        if self.pp > 1:
+            from rl_b200.weight_sync.colocated import PipelineGatherSynchronizer
+
+            return PipelineGatherSynchronizer(self.model, self.gen_model, self.ps.pp_group, self.ps.pp_ranks,
+                                              self.ps.pp_rank)
         if not resharded:
             return ColocatedInPlaceSynchronizer()
         peer_ptrs = None
@@ -313,10 +340,53 @@ class PolicyWorker:
         targets = torch.empty_like(flat_d)
         targets[:-1] = flat_d[1:]
         targets[-1:] = 0
-        hidden = self.model(flat_d, pos_d, cu_d, max_len)
+        hidden = self._run_model(flat_d, pos_d, cu_d, max_len)
+        if not self.model.is_last_stage:
+            return hidden, None, cu
         h = self.model.lm_input(hidden)
         lp, ent = self._logprobs_from_hidden(h, targets, temperature)
         return lp, ent, cu
+
+    def _run_model(self, input_ids, positions, cu_seqlens, max_seqlen):
+        """The model (this pipeline stage of it), fed the previous stage's
+        activation when there is one."""
+        if self.pp > 1:
+            return self.model(input_ids, positions, cu_seqlens, max_seqlen, hidden_in=self._pp_in)
+        return self.model(input_ids, positions, cu_seqlens, max_seqlen)
+
+    def _pp_shape(self, ids, lengths, rows) -> tuple:
+        """Shape of the activation between pipeline stages for a micro-batch."""
+        T = pack_rows(ids, lengths, rows, pad_to_multiple=self._pack_multiple())[0].numel()
+        if self.sequence_parallel:
+            T //= self.ps.tp_size
+        return (T, self.model_cfg.hidden_size)
+
+    def _pp_inference(self, plan, ids, lengths, fn) -> None:
+        """Forward-only pass of ``plan`` through the pipeline; ``fn(rows, out)``
+        consumes the last stage's output of each (non-dummy) micro-batch."""
+        comm = self._pp_comm
+        for rows in plan:
+            dummy = rows[0] < 0
+            rows = [-1 - rows[0]] if dummy else rows
+            self._pp_in = comm.recv_forward(self._pp_shape(ids, lengths, rows), self.dtype, self.device) \
+                if not self.model.is_first_stage else None
+            out = fn(rows, dummy)
+            self._pp_in = None
+            if not self.model.is_last_stage:
+                comm.send_forward(out)
+        comm.wait()
+
+    def _pp_broadcast(self, t: torch.Tensor) -> torch.Tensor:
+        """Last stage's tensor to every stage of the pipeline."""
+        dev = self.device if self.ps.backend == "nccl" else torch.device("cpu")
+        x = t.to(dev).contiguous()
+        dist.broadcast(x, src=self.ps.pp_ranks[-1], group=self.ps.pp_group)
+        return x.cpu()
+
+    def _pp_share_metrics(self, agg: dict) -> dict:
+        obj = [agg]
+        dist.broadcast_object_list(obj, src=self.ps.pp_ranks[-1], group=self.ps.pp_group)
+        return obj[0]
 
     def _logprobs_from_hidden(self, h, targets, temperature):
         """Fused LM-head + log-prob (full vocabulary), or - when the rollout samples
@@ -341,6 +411,8 @@ class PolicyWorker:
         kind = getattr(getattr(loss_fn, "input_type", None), "value", "logprob")
         if kind == "logprob":
             lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
+            if not self.model.is_last_stage:
+                return lp  # this stage's output activation
             if isinstance(cu, tuple):
                 # the loss sees only this rank's tokens (the others' positions are
                 # masked; their ranks contribute them): tokens i+1 scored locally
@@ -351,7 +423,9 @@ class PolicyWorker:
             raise NotImplementedError("context parallelism supports log-prob losses")
         flat, pos, cu, max_len, _ = pack_rows(ids, lengths, rows, pad_to_multiple=self._pack_multiple())
         dev = self.device
-        hidden = self.model(_to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev), max_len)
+        hidden = self._run_model(_to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev), max_len)
+        if not self.model.is_last_stage:
+            return hidden
         if kind == "value":
             v = self.model.values(hidden)
             return self._to_padded_full(v, cu, len(rows), width)
@@ -389,6 +463,17 @@ class PolicyWorker:
         out = torch.zeros(B, S, dtype=torch.float32)
         rows_all = [r for r in range(B) if lengths[r] > 0]
         self.model.eval()
+        if self.pp > 1:
+            def one(rows, dummy):
+                width = max(lengths[r] for r in rows)
+                v = self._loss_input(_VALUE_INPUT, ids, lengths, rows, width, 1.0)
+                if self.model.is_last_stage and not dummy:
+                    out[torch.tensor(rows), :width] = v.float().cpu()
+                return v
+
+            self._pp_inference(self._plan(lengths, rows_all, self.logprob_mb_tokens), ids, lengths, one)
+            self.model.train()
+            return BatchedDataDict({"values": self._pp_broadcast(out)})
         for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
             if rows[0] < 0:
                 continue
@@ -442,6 +527,16 @@ class PolicyWorker:
         out = torch.zeros(B, S, dtype=torch.float32)
         rows_all = [r for r in range(B) if lengths[r] > 0]
         self.model.eval()
+        if self.pp > 1:
+            def one(rows, dummy):
+                lp, _, cu = self._forward_mb(ids, lengths, rows, temperature)
+                if self.model.is_last_stage and not dummy:
+                    out[torch.tensor(rows), 1:] = self._to_padded(lp.float(), cu, len(rows), S).cpu()
+                return lp
+
+            self._pp_inference(self._plan(lengths, rows_all, self.logprob_mb_tokens), ids, lengths, one)
+            self.model.train()
+            return BatchedDataDict({"logprobs": self._pp_broadcast(out)})
         for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
             dummy = rows[0] < 0
             rows = [-1 - rows[0]] if dummy else rows
@@ -526,6 +621,8 @@ class PolicyWorker:
         if self.release_grad_after_train:
             self.optimizer.release_grad_buffer()
         agg = aggregate_metrics(all_metrics, self._metric_group())
+        if self.pp > 1:
+            agg = self._pp_share_metrics(agg)
         agg.update({"loss": sum(losses) / max(1, len(losses)), "global_loss": losses,
                     "grad_norm": grad_norms[-1] if grad_norms else 0.0, "lr": lrs[-1] if lrs else 0.0,
                     "moe_aux_loss": self.model.aux_loss()})
@@ -574,7 +671,50 @@ class PolicyWorker:
 
     def train_microbatch(self, st: "TrainStepState", i: int) -> dict:
         """Forward + backward of packed micro-batch ``i`` of the step; gradients
-        accumulate into the fp32 main-grad buffer.  Returns the (device) metrics."""
+        accumulate into the fp32 main-grad buffer.  Returns the (device) metrics.
+
+        Under pipeline parallelism the micro-batches of a step run as one 1F1B
+        schedule across the stages: calls for ``i < M - 1`` only count, the last
+        call runs the whole schedule (metrics are returned by ``finish_train_step``)."""
+        if self.pp > 1:
+            st.done += 1
+            if i == st.num_microbatches - 1:
+                self._pp_train_schedule(st)
+            return {}
+        loss, metrics = self._mb_loss(st, i)
+        if not st.eval_mode:
+            loss.backward()
+            self.optimizer._fold_param_grads()
+        st.done += 1
+        return metrics
+
+    def _pp_train_schedule(self, st: "TrainStepState") -> None:
+        from rl_b200.parallel.pipeline import one_f_one_b
+
+        def fwd(i, hidden_in):
+            self._pp_in = hidden_in
+            try:
+                if self.model.is_last_stage:
+                    return self._mb_loss(st, i)[0]
+                rows = st.plan[i]
+                rows = [-1 - rows[0]] if rows[0] < 0 else rows
+                width = max(st.lengths[r] for r in rows)
+                return self._loss_input(st.loss_fn, st.ids, st.lengths, rows, width, st.temperature)
+            finally:
+                self._pp_in = None
+
+        def shape(i):
+            rows = st.plan[i]
+            rows = [-1 - rows[0]] if rows[0] < 0 else rows
+            return self._pp_shape(st.ids, st.lengths, rows)
+
+        one_f_one_b(self._pp_comm, st.num_microbatches, fwd, shape, self.dtype, self.device,
+                    backward=not st.eval_mode)
+        if not st.eval_mode:
+            self.optimizer._fold_param_grads()
+
+    def _mb_loss(self, st: "TrainStepState", i: int):
+        """Loss (and metrics) of micro-batch ``i``; accumulates the step loss."""
         mb_rows = st.plan[i]
         dummy = mb_rows[0] < 0
         if dummy:
@@ -601,13 +741,9 @@ class PolicyWorker:
             # zero-weight pass: keeps the EP group's all-to-alls paired, adds nothing
             loss = loss * 0.0
             metrics = {}
-        if not st.eval_mode:
-            loss.backward()
-            self.optimizer._fold_param_grads()
         st.step_loss += loss.detach()
         st.mb_metrics.append(metrics)
-        st.done += 1
-        return metrics
+        return loss, metrics
 
     def finish_train_step(self, st: "TrainStepState", release_grad: Optional[bool] = None,
                           aggregate: bool = True) -> dict:
@@ -623,11 +759,15 @@ class PolicyWorker:
         red = self._metric_group()
         if red is not None:
             dist.all_reduce(st.step_loss, group=red)
+        if self.pp > 1:  # only the last stage computed a loss
+            dist.all_reduce(st.step_loss, group=self.ps.pp_group)
         out["loss"] = float(st.step_loss)
         if release_grad if release_grad is not None else self.release_grad_after_train:
             self.optimizer.release_grad_buffer()
         if aggregate:
             agg = aggregate_metrics(st.mb_metrics, self._metric_group())
+            if self.pp > 1:
+                agg = self._pp_share_metrics(agg)
             agg.update(out)
             agg["moe_aux_loss"] = self.model.aux_loss()
             return agg
@@ -639,17 +779,20 @@ class PolicyWorker:
         (which hold identical data) each generate every t-th row with their full
         rollout copy and exchange the results, so every peer returns the whole
         batch (identical, as the trainer requires)."""
-        t = self.ps.tp_size
-        if self.gen_tp == t or t == 1:
+        if self.pp > 1:
+            # every stage holds the whole rollout model and the same rows: split them
+            t, r, grp = self.pp, self.ps.pp_rank, self.ps.pp_group
+        elif self.gen_tp == self.ps.tp_size or self.ps.tp_size == 1:
             return self.engine.generate(data, greedy=greedy)
+        else:
+            t, r, grp = self.ps.tp_size, self.ps.tp_rank, self.ps.tp_group
         B = data.size
-        r = self.ps.tp_rank
         rows = list(range(r, B, t))
         part = self.engine.generate(data.select_indices(rows), greedy=greedy) if rows else None
         part = BatchedDataDict({k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in part.items()}) \
             if part is not None else None
         parts = [None] * t
-        dist.all_gather_object(parts, part, group=self.ps.tp_group)
+        dist.all_gather_object(parts, part, group=grp)
         order = [i for q in range(t) for i in range(q, B, t)]
         out = BatchedDataDict.from_batches([p for p in parts if p is not None])
         inv = [0] * B

@@ -46,7 +46,15 @@ from rl_b200.parallel.comm import (all_to_all_autograd, copy_to_tp, gather_from_
                                    reduce_scatter_to_sp, scatter_to_sp)
 from rl_b200.parallel.state import ParallelState, single_process_state
 
-__all__ = ["TransformerLM", "ParamSpec", "KVCache"]
+__all__ = ["TransformerLM", "ParamSpec", "KVCache", "stage_layers"]
+
+
+def stage_layers(num_layers: int, pp: int, rank: int) -> range:
+    """Contiguous, balanced layer range of pipeline stage ``rank`` (earlier stages
+    take the remainder)."""
+    base, extra = divmod(num_layers, pp)
+    start = rank * base + min(rank, extra)
+    return range(start, start + base + (1 if rank < extra else 0))
 
 
 @dataclass
@@ -179,6 +187,14 @@ class TransformerLM(nn.Module):
             if cfg.ffn_hidden_size % tp:
                 raise ValueError(f"ffn {cfg.ffn_hidden_size} must divide by tp={tp}")
             self.ffn_local = cfg.ffn_hidden_size // tp
+        # pipeline parallelism: this rank's contiguous range of layers; the first
+        # stage owns the embedding, the last the final norm and the LM / value head
+        self.pp_size, self.pp_rank = self.ps.pp_size, self.ps.pp_rank
+        self.layer_range = stage_layers(cfg.num_layers, self.pp_size, self.pp_rank)
+        self.is_first_stage = self.pp_rank == 0
+        self.is_last_stage = self.pp_rank == self.pp_size - 1
+        if self.pp_size > 1 and cfg.tie_word_embeddings:
+            raise NotImplementedError("tied embeddings under pipeline parallelism")
         self.specs = self._make_specs()
         self._allocate(seed, init_std)
         self.rope_cache = build_rope_cache(min(cfg.max_position_embeddings, 1 << 17), cfg.head_dim,
@@ -201,8 +217,10 @@ class TransformerLM(nn.Module):
     def _make_specs(self) -> list[ParamSpec]:
         c = self.cfg
         H, hd = c.hidden_size, c.head_dim
-        s: list[ParamSpec] = [ParamSpec("model.embed_tokens.weight", (self.vocab_local, H), "normal", tp_dim=0)]
-        for i in range(c.num_layers):
+        s: list[ParamSpec] = []
+        if self.is_first_stage or (c.tie_word_embeddings and self.is_last_stage):
+            s.append(ParamSpec("model.embed_tokens.weight", (self.vocab_local, H), "normal", tp_dim=0))
+        for i in self.layer_range:
             p = f"model.layers.{i}."
             s.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones", no_weight_decay=True))
             s.append(ParamSpec(p + "self_attn.qkv_proj.weight", ((self.nq + 2 * self.nkv) * hd, H), "normal", tp_dim=0))
@@ -219,12 +237,13 @@ class TransformerLM(nn.Module):
             else:
                 s.append(ParamSpec(p + "mlp.gate_up_proj.weight", (2 * self.ffn_local, H), "normal", tp_dim=0))
                 s.append(ParamSpec(p + "mlp.down_proj.weight", (H, self.ffn_local), "normal_out", tp_dim=1))
-        s.append(ParamSpec("model.norm.weight", (H,), "ones", no_weight_decay=True))
-        if self.num_labels > 0:
-            # value / reward head (HF ``score`` naming of *ForSequenceClassification)
-            s.append(ParamSpec("score.weight", (self.num_labels, H), "normal"))
-        elif not c.tie_word_embeddings:
-            s.append(ParamSpec("lm_head.weight", (self.vocab_local, H), "normal", tp_dim=0))
+        if self.is_last_stage:
+            s.append(ParamSpec("model.norm.weight", (H,), "ones", no_weight_decay=True))
+            if self.num_labels > 0:
+                # value / reward head (HF ``score`` naming of *ForSequenceClassification)
+                s.append(ParamSpec("score.weight", (self.num_labels, H), "normal"))
+            elif not c.tie_word_embeddings:
+                s.append(ParamSpec("lm_head.weight", (self.vocab_local, H), "normal", tp_dim=0))
         # Flat layout: every dense (non-expert) parameter first, then every expert
         # parameter, so that the two gradient-reduction domains (data parallel vs
         # expert data parallel) are two contiguous segments of one buffer.
@@ -604,15 +623,14 @@ class TransformerLM(nn.Module):
         return s2, m
 
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, cu_seqlens: torch.Tensor,
-                max_seqlen: int) -> torch.Tensor:
-        """Packed forward: ``input_ids [T]`` -> final-norm hidden ``[T(/tp if SP), H]``."""
+                max_seqlen: int, hidden_in: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """Packed forward: ``input_ids [T]`` -> final-norm hidden ``[T(/tp if SP), H]``.
+        Under pipeline parallelism a non-first stage starts from ``hidden_in`` (the
+        previous stage's output) and a non-last stage returns its residual stream."""
         self._aux_losses = []
-        x = self.embed(input_ids)
-        if self.sequence_parallel:
-            # positions/cu_seqlens describe the full sequence; layers gather before attention.
-            pass
+        x = self.embed(input_ids) if self.is_first_stage else hidden_in
         resid = None
-        for i in range(self.cfg.num_layers):
+        for i in self.layer_range:
             if self.activation_checkpointing and torch.is_grad_enabled():
                 if resid is None:
                     x, resid = ckpt.checkpoint(self._layer, i, x, None, positions, cu_seqlens, max_seqlen,
@@ -622,6 +640,8 @@ class TransformerLM(nn.Module):
                                                use_reentrant=False)
             else:
                 x, resid = self._layer(i, x, resid, positions, cu_seqlens, max_seqlen)
+        if not self.is_last_stage:
+            return x if resid is None else x + resid
         h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], self.cfg.rms_eps)
         return h
 

@@ -117,13 +117,16 @@ class FlatAdamW:
     def __init__(self, model, lr: float = 1e-5, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  max_grad_norm: Optional[float] = 1.0, scheduler_cfg=None, min_lr: float = 0.0,
                  dp_group=None, tp_group=None, sequence_parallel: bool = False, edp_group=None, ep_group=None,
-                 symmetric=None):
+                 symmetric=None, pp_group=None):
         """``symmetric``: a ``rl_b200.parallel.symm.NodeSymmetric`` allocator.  When
         given (CUDA, every rank on one node) the fp32 gradient buffer and the bf16
         parameter buffer are symmetric memory and the dense data-parallel segment
         steps with the fused kernels of ``csrc/dp_optim.cu`` (reduce-scatter by
         peer loads + norm partials, then AdamW fused with the parameter all-gather
-        by peer stores) instead of NCCL reduce-scatter / all-gather."""
+        by peer stores) instead of NCCL reduce-scatter / all-gather.
+        ``pp_group``: under pipeline parallelism each stage steps its own layers;
+        the gradient norm used for clipping is the whole model's (sum of squares
+        over the stages)."""
         self.model = model
         self.symmetric = symmetric
         self.lr = lr
@@ -134,6 +137,7 @@ class FlatAdamW:
         self.scheduler = LRScheduler(lr, scheduler_cfg, min_lr)
         self.dp_group = dp_group
         self.tp_group = tp_group
+        self.pp_group = pp_group if _ws(pp_group) > 1 else None
         self.sequence_parallel = sequence_parallel
         self.tp = _ws(tp_group)
         self.dp = _ws(dp_group)
@@ -292,6 +296,8 @@ class FlatAdamW:
             if seg.norm_sum_group is not None and _ws(seg.norm_sum_group) > 1:
                 dist.all_reduce(sq, group=seg.norm_sum_group)
             sq_total = sq_total + sq
+        if self.pp_group is not None:
+            dist.all_reduce(sq_total, group=self.pp_group)
         norm = float(sq_total.sqrt())
         self.last_grad_norm = norm
         scale = 1.0

@@ -12,7 +12,8 @@ from rl_b200.weight_sync.interfaces import WeightSynchronizer
 from rl_b200.weight_sync.reshard import (apply_regions_reference, build_regions, copy_tasks, quant_layout,
                                          quant_regions_reference, quant_tasks)
 
-__all__ = ["ColocatedInPlaceSynchronizer", "ColocatedReshardSynchronizer", "LoRAMergeSynchronizer"]
+__all__ = ["ColocatedInPlaceSynchronizer", "ColocatedReshardSynchronizer", "LoRAMergeSynchronizer",
+           "PipelineGatherSynchronizer"]
 
 
 class LoRAMergeSynchronizer:
@@ -123,3 +124,46 @@ class ColocatedReshardSynchronizer(WeightSynchronizer):
 
 def regions_bytes(regions) -> int:
     return int(np.sum([r.rows * r.cols for r in regions])) * 2
+
+
+class PipelineGatherSynchronizer(WeightSynchronizer):
+    """Pipeline-parallel training -> full-depth rollout copy on every stage.
+
+    Each stage's flat parameter buffer is broadcast over the pipeline group in
+    one collective (NVLink, no host hop); every rank then copies the named
+    slices into its rollout model.  The per-stage layouts (name, offset, numel)
+    are exchanged once at construction.  The rollout copy keeps the training
+    TP layout, so only depth is gathered."""
+    name = "pp_gather"
+
+    def __init__(self, train_model, gen_model, pp_group, pp_ranks: list, stage: int):
+        super().__init__()
+        self.train_model, self.gen_model = train_model, gen_model
+        self.group, self.ranks, self.stage = pp_group, list(pp_ranks), stage
+        mine = ([(sp.name, sp.offset, sp.numel) for sp in train_model.specs], int(train_model.flat_param.numel()))
+        self.layouts: list = [None] * len(self.ranks)
+        dist.all_gather_object(self.layouts, mine, group=pp_group)
+        names = {n for lay, _ in self.layouts for n, _, _ in lay}
+        missing = [sp.name for sp in gen_model.specs if sp.name not in names]
+        if missing:
+            raise ValueError(f"rollout parameters held by no pipeline stage: {missing[:4]}")
+
+    @torch.no_grad()
+    def _sync(self) -> int:
+        flat = self.train_model.flat_param
+        nbytes = 0
+        stage_buf = None
+        gen = self.gen_model._params
+        for s, (lay, n) in enumerate(self.layouts):
+            if s == self.stage:
+                buf = flat
+            else:
+                if stage_buf is None or stage_buf.numel() < n:
+                    stage_buf = torch.empty(max(n for _, n in self.layouts), dtype=flat.dtype, device=flat.device)
+                buf = stage_buf[:n]
+            dist.broadcast(buf, src=self.ranks[s], group=self.group)
+            for name, off, numel in lay:
+                if name in gen:
+                    gen[name].data.view(-1).copy_(buf[off:off + numel])
+                    nbytes += numel * buf.element_size()
+        return nbytes

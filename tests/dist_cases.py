@@ -35,12 +35,12 @@ def _pcfg(sp: bool):
             "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
 
 
-def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool, cp: int = 1):
+def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool, cp: int = 1, pp: int = 1):
     from rl_b200.models.policy.worker import PolicyWorker
     from rl_b200.parallel.state import init_distributed
 
     torch.manual_seed(0)
-    ps = init_distributed(tp=tp, ep=ep, cp=cp, backend="gloo")
+    ps = init_distributed(tp=tp, ep=ep, cp=cp, pp=pp, backend="gloo")
     cfg = TINY_MOE if moe else TINY
     w = PolicyWorker(_pcfg(sp), model_cfg=cfg, pstate=ps, seed=3)
     full = make_batch()
@@ -96,3 +96,37 @@ def case_reshard_refit(rank: int, tp: int):
     out = w.generate(data, greedy=True)
     return {"init_err": init_err, "refit_err": max(errs), "loss": res["loss"], "out_ids": out["output_ids"],
             "gen_lens": out["generation_lengths"]}
+
+
+def case_pp_rollout_ckpt(rank: int, pp: int, tp: int, ckpt_dir: str):
+    """Pipeline-parallel worker: the gathered full-depth rollout copy equals the
+    training stages' weights after a step, greedy rollouts match the
+    single-process worker's, and an HF checkpoint holds every stage's tensors."""
+    from rl_b200.models.checkpoint_io import load_hf_checkpoint
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.parallel.state import init_distributed, single_process_state
+
+    torch.manual_seed(0)
+    ps = init_distributed(tp=tp, pp=pp, backend="gloo")
+    w = PolicyWorker(_pcfg(False), model_cfg=TINY, pstate=ps, seed=3)
+    batch = make_batch()
+    w.train(batch, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=batch.size)
+    w.refit()
+    errs = [(w.gen_model.param(sp.name) - p).abs().max().item() for sp, p in w.model.named_flat_params()]
+    data = BatchedDataDict({"input_ids": batch["input_ids"][:5, :8].clone(),
+                            "input_lengths": torch.full((5,), 8, dtype=torch.long)})
+    out = w.generate(data, greedy=True)
+    w.save_checkpoint(ckpt_dir)
+    w.save_checkpoint(ckpt_dir + "_dist", fmt="torch_dist")
+    torch.distributed.barrier()
+    full = TransformerLM(TINY, single_process_state(), dtype=torch.float32, seed=99)
+    load_hf_checkpoint(full, ckpt_dir)
+    ck_err = 0.0
+    if tp == 1:
+        # the HF checkpoint stores bf16
+        ck_err = max((full.param(sp.name) - p.detach().to(torch.bfloat16).float()).abs().max().item()
+                     for sp, p in w.model.named_flat_params())
+    return {"sync_err": max(errs), "out_ids": out["output_ids"], "gen_lens": out["generation_lengths"],
+            "ckpt_err": ck_err, "n_stage_params": len(w.model.specs), "n_gen_params": len(w.gen_model.specs),
+            "gen_flat": w.gen_model.flat_param.detach().clone()}

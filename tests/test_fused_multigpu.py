@@ -552,3 +552,56 @@ def test_decode_allreduce_rmsnorm_2gpu():
     for o in outs:
         assert o["flag"] == 0
         assert max(o["errs"]) < 1e-2, o["errs"]
+
+
+def case_pp_train(rank: int):
+    """PP=2 on 2 GPUs (NCCL send / recv between the stages, 1F1B schedule): one
+    GRPO-loss training step and the log-probs after it against a single-GPU
+    worker of the same seed on the same batch."""
+    import os
+
+    import torch.distributed as dist
+
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import init_distributed, single_process_state
+    from tests.dist_cases import make_batch
+
+    ps = init_distributed(pp=2, backend="nccl", timeout_s=120)
+    cfg = ModelConfig(name="pp", vocab_size=1024, hidden_size=512, num_layers=4, num_heads=8, num_kv_heads=4,
+                      head_dim=64, ffn_hidden_size=1024, rope_theta=10000.0, max_position_embeddings=1024)
+    pcfg = {"max_total_sequence_length": 256, "precision": "bfloat16",
+            "optimizer": {"kwargs": {"lr": 1e-4, "weight_decay": 0.01}},
+            "generation": {"temperature": 1.0, "max_new_tokens": 4},
+            "sequence_packing": {"train_mb_tokens": 512, "logprob_mb_tokens": 512}}
+    batch = make_batch(B=16, S=200, vocab=1024)
+    loss_fn = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
+    w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=11)
+    res = w.train(batch, loss_fn, gbs=batch.size)
+    lp = w.get_logprobs(batch)["logprobs"]
+    w.shutdown()
+    ref = PolicyWorker(pcfg, model_cfg=cfg, pstate=single_process_state(torch.device("cuda", rank)), seed=11)
+    res1 = ref.train(batch, loss_fn, gbs=batch.size)
+    lp1 = ref.get_logprobs(batch)["logprobs"]
+    ref.shutdown()
+    mask = batch["token_mask"] > 0
+    out = {"loss": (res["loss"], res1["loss"]), "gn": (res["grad_norm"], res1["grad_norm"]),
+           "lp_err": (lp - lp1)[mask].abs().max().item(), "stage_layers": list(w.model.layer_range)}
+    dist.barrier()
+    dist.destroy_process_group()
+    return out
+
+
+def test_pipeline_parallel_train_2gpu():
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_pp_train, 2, timeout_s=300)
+    assert outs[0]["stage_layers"] == [0, 1] and outs[1]["stage_layers"] == [2, 3]
+    for o in outs:
+        (a, b), (g, h) = o["loss"], o["gn"]
+        assert abs(a - b) < 2e-2 * max(1.0, abs(b)), o
+        assert abs(g - h) < 3e-2 * h, o
+        assert o["lp_err"] < 0.15, o

@@ -32,23 +32,31 @@ def get_keys_from_message_log(log: list[dict], keys: list[str]) -> list[dict]:
     return [{k: m[k] for k in keys if k in m} for m in log]
 
 
+# per-token fields whose "missing" value is not zero
+PAD_VALUES = {"routed_experts": -1}
+
+
 def message_log_to_flat(log: list[dict]) -> dict[str, torch.Tensor]:
+    """Concatenate the per-token fields of a message log (tensors whose first
+    dimension is the message's token count; trailing dimensions are kept, e.g.
+    ``routed_experts [L, layers, top_k]``)."""
     out: dict[str, list] = {}
     n = 0
     for msg in log:
         L = len(msg["token_ids"])
         n += L
         for k, v in msg.items():
-            if isinstance(v, torch.Tensor) and v.dim() == 1 and v.shape[0] == L:
+            if isinstance(v, torch.Tensor) and v.dim() >= 1 and v.shape[0] == L:
                 out.setdefault(k, []).append(v)
     flat = {k: torch.cat(v) for k, v in out.items()}
-    # keys missing on some messages: fill with zeros of the right length
+    # keys missing on some messages: fill with the key's pad value
     for k in list(flat.keys()):
         if flat[k].shape[0] != n:
             parts = []
             for msg in log:
                 L = len(msg["token_ids"])
-                parts.append(msg[k] if k in msg else torch.zeros(L, dtype=flat[k].dtype))
+                parts.append(msg[k] if k in msg else
+                             torch.full((L,) + tuple(flat[k].shape[1:]), PAD_VALUES.get(k, 0), dtype=flat[k].dtype))
             flat[k] = torch.cat(parts)
     return flat
 
@@ -66,7 +74,8 @@ def batched_message_log_to_flat_message(message_logs: list[list[dict]], pad_valu
     out = BatchedDataDict()
     for k in keys:
         ref = next(f[k] for f in flats if k in f)
-        t = torch.full((len(flats), S), pad_value_dict.get(k, 0), dtype=ref.dtype)
+        t = torch.full((len(flats), S) + tuple(ref.shape[1:]), pad_value_dict.get(k, PAD_VALUES.get(k, 0)),
+                       dtype=ref.dtype)
         for i, f in enumerate(flats):
             if k in f:
                 t[i, : f[k].shape[0]] = f[k]

@@ -18,7 +18,7 @@ import torch
 from rl_b200.data.llm_message_utils import batched_message_log_to_flat_message
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
 
-__all__ = ["generate_responses", "calculate_rewards", "run_multi_turn_rollout"]
+__all__ = ["generate_responses", "calculate_rewards", "run_multi_turn_rollout", "attach_routes"]
 
 
 def generate_responses(policy_generation, batch: BatchedDataDict, rows: list[int], max_seq_len: int,
@@ -38,7 +38,22 @@ def generate_responses(policy_generation, batch: BatchedDataDict, rows: list[int
         truncated.append(bool(out["truncated"][i]))
     stats = {"gen_time_s": dt, "gen_tokens": int(out["generation_lengths"].sum()),
              "prompt_tokens": int(lengths.sum())}
+    if "routed_experts" in out:
+        # router replay: the routes of every position of every generated sequence
+        stats["routed_experts"] = [out["routed_experts"][i, :int(lengths[i]) + int(out["generation_lengths"][i])]
+                                   for i in range(len(rows))]
     return resp_ids, resp_lps, truncated, stats
+
+
+def attach_routes(log: list[dict], routes: torch.Tensor) -> None:
+    """Give every message of ``log`` its slice of the full-sequence routes of
+    the latest generation call (router replay; later turns overwrite earlier
+    ones, so each token keeps the route of the last forward that processed it)."""
+    off = 0
+    for msg in log:
+        L = len(msg["token_ids"])
+        msg["routed_experts"] = routes[off:off + L].clone()
+        off += L
 
 
 def calculate_rewards(batch: BatchedDataDict, rows: list[int], task_to_env: dict) -> tuple[torch.Tensor, list, list]:
@@ -99,6 +114,8 @@ def run_multi_turn_rollout(policy_generation, input_batch: BatchedDataDict, toke
                 "role": "assistant", "content": "", "token_ids": resp[i],
                 "generation_logprobs": lps[i],
             })
+            if "routed_experts" in st:
+                attach_routes(batch["message_log"][r], st["routed_experts"][i])
             truncated[r] |= trunc[i]
         rewards, terminated, obs = calculate_rewards(batch, live, task_to_env)
         total_reward[torch.tensor(live)] += rewards

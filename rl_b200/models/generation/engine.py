@@ -107,6 +107,11 @@ class RolloutEngine:
         # "thread_local" when another thread keeps launching work while decode
         # graphs are captured (async GRPO's rollout thread)
         self.capture_error_mode = "global"
+        # router replay (R3): record the experts every MoE layer picks for every
+        # processed token and return them as "routed_experts" [B, S, layers, k]
+        # (-1 where no route exists: padding and the last sampled token)
+        self.record_routes = False
+        self._route_steps: Optional[list] = None
 
     # ------------------------------------------------------------ lifecycle
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
@@ -213,7 +218,12 @@ class RolloutEngine:
         seq_idx = torch.repeat_interleave(torch.arange(B), lengths).to(dev)
         slot = (block_tables[seq_idx, (positions // bs).long()].long() * bs + (positions % bs).long())
         last_idx = (cu[1:] - 1).to(dev).long()
+        recording = self.record_routes and self.model.cfg.is_moe
+        if recording:
+            self.model.router_record = {}
         h = self.model.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.kv, slot, last_idx)
+        prefill_routes = self._take_routes() if recording else None
+        self._route_steps = [] if recording else None
         logits = self.model.logits_infer(h)
         gen = None
         if dev.type == "cpu":
@@ -225,7 +235,14 @@ class RolloutEngine:
             lp0 = torch.zeros_like(lp0)
 
         # ---- decode ----
-        if self._spec_enabled(top_k, top_p):
+        if recording:
+            # routes are read back after every step: eager decode (no graphs, no speculation)
+            try:
+                tokens_all, lps_all, glen = self._decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
+                                                              temperature, top_k, top_p, stop_ids, gen, eager=True)
+            finally:
+                self.model.router_record = None
+        elif self._spec_enabled(top_k, top_p):
             self.draft.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.draft_kv, slot, last_idx)
             tokens_all, lps_all, glen = self._spec_decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
                                                                temperature, stop_ids)
@@ -240,7 +257,36 @@ class RolloutEngine:
             L = lens_l[b]
             out_ids[b, L: L + n] = toks_c[b, :n]
             out_lp[b, L: L + n] = lps_c[b, :n]
-        return self._pack_outputs(out_ids, out_lp, lengths, glen_c, pad_id, max_new)
+        out = self._pack_outputs(out_ids, out_lp, lengths, glen_c, pad_id, max_new)
+        if recording:
+            out["routed_experts"] = self._assemble_routes(prefill_routes, lens_l, glen_c, out["output_ids"].shape[1])
+            self._route_steps = None
+        return out
+
+    def _take_routes(self) -> torch.Tensor:
+        """The routes recorded by the last forward, ``[T, layers, k]``; resets the record."""
+        rec = self.model.router_record
+        out = torch.stack([rec[i] for i in sorted(rec)], 1)
+        self.model.router_record = {}
+        return out
+
+    def _assemble_routes(self, prefill: torch.Tensor, lens: list, glen: torch.Tensor, width: int) -> torch.Tensor:
+        """Per-sequence routes ``[B, width, layers, k]``: prompt positions from the
+        prefill, position ``L + s - 1`` from decode step ``s`` (the token fed at
+        that step); the last sampled token was never fed and stays -1."""
+        B = len(lens)
+        nl, k = prefill.shape[1], prefill.shape[2]
+        out = torch.full((B, width, nl, k), -1, dtype=prefill.dtype)
+        pre = prefill.cpu()
+        steps = [t.cpu() for t in self._route_steps]
+        off = 0
+        for b in range(B):
+            L, n = lens[b], int(glen[b])
+            out[b, :L] = pre[off:off + L]
+            off += L
+            for s in range(1, n):
+                out[b, L + s - 1] = steps[s - 1][b]
+        return out
 
     def _spec_enabled(self, top_k, top_p) -> bool:
         # rejection sampling verifies against the full distributions: no top-k / top-p filtering
@@ -333,7 +379,8 @@ class RolloutEngine:
             "truncated": gen_lens >= max_new,
         })
 
-    def _decode_loop(self, tok0, lp0, lengths, block_tables, max_new, temperature, top_k, top_p, stop_ids, gen):
+    def _decode_loop(self, tok0, lp0, lengths, block_tables, max_new, temperature, top_k, top_p, stop_ids, gen,
+                     eager: bool = False):
         dev = self.device
         B = tok0.shape[0]
         stop = torch.tensor(stop_ids if stop_ids else [-1], dtype=torch.int64, device=dev)
@@ -347,7 +394,7 @@ class RolloutEngine:
         active_rows = torch.nonzero(~done0).flatten()
         if active_rows.numel() == 0:
             return tokens_all, lps_all, glen
-        if self.device.type != "cuda" or not self.use_cuda_graphs:
+        if self.device.type != "cuda" or not self.use_cuda_graphs or eager:
             return self._decode_eager(tokens_all, lps_all, glen, tok0, lengths, block_tables, max_new, temperature,
                                       top_k, top_p, stop, gen, done0)
         rows = active_rows
@@ -476,6 +523,8 @@ class RolloutEngine:
             slot = blk.long() * bs + (positions % bs).long()
             h = self.model.forward_decode(tokens, positions, self.kv, block_tables, positions + 1, slot,
                                           self.max_model_len)
+            if self._route_steps is not None:
+                self._route_steps.append(self._take_routes())
             logits = self.model.logits_infer(h)
             nt, nlp = sample_tokens(logits, temperature if temperature > 0 else 1.0,
                                     1 if temperature == 0 else top_k, top_p,

@@ -215,6 +215,15 @@ class PolicyWorker:
         if bool(policy_cfg.get("kv_cache_in_grad_arena", self.device.type == "cuda")):
             self.engine.kv_arena = lambda: self.optimizer.main_grad
         self.timer = Timer()
+        # router replay (R3): the rollout records the experts each MoE layer chose
+        # and training / log-prob forwards reuse them
+        self.router_replay = bool((policy_cfg.get("router_replay") or {}).get("enabled", False)) \
+            and self.model_cfg.is_moe
+        if self.router_replay:
+            if self.ps.cp_size > 1:
+                raise NotImplementedError("router replay with context parallelism")
+            self.engine.record_routes = True
+        self._routes: Optional[torch.Tensor] = None
         self._pp_comm = None
         self._pp_in: Optional[torch.Tensor] = None
         if self.pp > 1:
@@ -335,6 +344,7 @@ class PolicyWorker:
         if self.ps.cp_size > 1:
             return self._forward_mb_cp(input_ids, lengths, rows, temperature)
         flat, pos, cu, max_len, T_real = pack_rows(input_ids, lengths, rows, pad_to_multiple=self._pack_multiple())
+        self._set_replay(rows, lengths, flat.numel())
         dev = self.device
         flat_d, pos_d, cu_d = _to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev)
         targets = torch.empty_like(flat_d)
@@ -346,6 +356,25 @@ class PolicyWorker:
         h = self.model.lm_input(hidden)
         lp, ent = self._logprobs_from_hidden(h, targets, temperature)
         return lp, ent, cu
+
+    def _set_replay(self, rows: list, lengths: list, T: int) -> None:
+        """Routes of the packed micro-batch for the model's routers (R3), or none."""
+        R = self._routes
+        if R is None:
+            self.model.router_replay = None
+            return
+        packed = torch.cat([R[r, :lengths[r]] for r in rows])
+        if packed.shape[0] < T:
+            packed = torch.cat([packed, packed.new_full((T - packed.shape[0],) + tuple(packed.shape[1:]), -1)])
+        packed = _to_device(packed, self.device)
+        self.model.router_replay = {i: packed[:, i] for i in range(packed.shape[1])}
+
+    def _use_routes(self, data) -> None:
+        self._routes = data["routed_experts"] if self.router_replay and "routed_experts" in data else None
+
+    def _end_routes(self) -> None:
+        self._routes = None
+        self.model.router_replay = None
 
     def _run_model(self, input_ids, positions, cu_seqlens, max_seqlen):
         """The model (this pipeline stage of it), fed the previous stage's
@@ -422,6 +451,7 @@ class PolicyWorker:
         if self.ps.cp_size > 1:
             raise NotImplementedError("context parallelism supports log-prob losses")
         flat, pos, cu, max_len, _ = pack_rows(ids, lengths, rows, pad_to_multiple=self._pack_multiple())
+        self._set_replay(rows, lengths, flat.numel())
         dev = self.device
         hidden = self._run_model(_to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev), max_len)
         if not self.model.is_last_stage:
@@ -462,6 +492,7 @@ class PolicyWorker:
         lengths = self._lengths(data)
         out = torch.zeros(B, S, dtype=torch.float32)
         rows_all = [r for r in range(B) if lengths[r] > 0]
+        self._use_routes(data)
         self.model.eval()
         if self.pp > 1:
             def one(rows, dummy):
@@ -473,6 +504,7 @@ class PolicyWorker:
 
             self._pp_inference(self._plan(lengths, rows_all, self.logprob_mb_tokens), ids, lengths, one)
             self.model.train()
+            self._end_routes()
             return BatchedDataDict({"values": self._pp_broadcast(out)})
         for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
             if rows[0] < 0:
@@ -481,6 +513,7 @@ class PolicyWorker:
             v = self._loss_input(_VALUE_INPUT, ids, lengths, rows, width, 1.0).float().cpu()
             out[torch.tensor(rows), :width] = v
         self.model.train()
+        self._end_routes()
         return BatchedDataDict({"values": out})
 
     @staticmethod
@@ -526,6 +559,7 @@ class PolicyWorker:
         lengths = self._lengths(data)
         out = torch.zeros(B, S, dtype=torch.float32)
         rows_all = [r for r in range(B) if lengths[r] > 0]
+        self._use_routes(data)
         self.model.eval()
         if self.pp > 1:
             def one(rows, dummy):
@@ -536,6 +570,7 @@ class PolicyWorker:
 
             self._pp_inference(self._plan(lengths, rows_all, self.logprob_mb_tokens), ids, lengths, one)
             self.model.train()
+            self._end_routes()
             return BatchedDataDict({"logprobs": self._pp_broadcast(out)})
         for rows in self._plan(lengths, rows_all, self.logprob_mb_tokens):
             dummy = rows[0] < 0
@@ -548,6 +583,7 @@ class PolicyWorker:
                 dist.all_reduce(padded, group=self.ps.cp_group)
             out[torch.tensor(rows), 1:] = padded.cpu()
         self.model.train()
+        self._end_routes()
         return BatchedDataDict({"logprobs": out})
 
     @contextlib.contextmanager
@@ -655,7 +691,8 @@ class PolicyWorker:
         # the per-token training tensors cross PCIe once (pinned, async) and are
         # sliced on the device; no pageable copy stalls the launch stream later
         dev_data = _dev_data if _dev_data is not None else \
-            {k: _to_device(v, self.device) for k, v in data.items() if isinstance(v, torch.Tensor)}
+            {k: _to_device(v, self.device) for k, v in data.items()
+             if isinstance(v, torch.Tensor) and k != "routed_experts"}  # routes are packed per micro-batch
         g0, n = rows[0], len(rows)
         tok_mask = dev_data["token_mask"][g0:g0 + n, 1:].float()
         smask = dev_data["sample_mask"][g0:g0 + n].float()
@@ -665,6 +702,9 @@ class PolicyWorker:
             dist.all_reduce(counts, group=self.ps.dp_group)
         plan = self._plan(lengths, [r for r in rows if lengths[r] > 0], self.train_mb_tokens)
         self.model.aux_loss_scale = 1.0 / max(1, len(plan))
+        self._use_routes(data)
+        if self._routes is not None and self.pp > 1 and self.model.activation_checkpointing:
+            raise NotImplementedError("router replay with pipeline parallelism and activation checkpointing")
         return TrainStepState(ids=ids, lengths=lengths, dev_data=dev_data, loss_fn=loss_fn, plan=plan,
                               gtoks=counts[0], gseqs=counts[1], eval_mode=eval_mode, temperature=temperature,
                               step_loss=torch.zeros((), device=self.device))
@@ -750,6 +790,7 @@ class PolicyWorker:
         """Optimizer step (or gradient reset in eval mode) and the step's metrics."""
         if st.done != st.num_microbatches:
             raise RuntimeError(f"finish_train_step after {st.done}/{st.num_microbatches} micro-batches")
+        self._end_routes()
         out: dict = {}
         if not st.eval_mode:
             opt_stats = self.optimizer.step()
@@ -794,7 +835,7 @@ class PolicyWorker:
         parts = [None] * t
         dist.all_gather_object(parts, part, group=grp)
         order = [i for q in range(t) for i in range(q, B, t)]
-        out = BatchedDataDict.from_batches([p for p in parts if p is not None])
+        out = BatchedDataDict.from_batches([p for p in parts if p is not None], pad_value_dict={"routed_experts": -1})
         inv = [0] * B
         for pos, i in enumerate(order):
             inv[i] = pos

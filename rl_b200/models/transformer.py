@@ -210,7 +210,9 @@ class TransformerLM(nn.Module):
         self._decode_ar = None
         self._cp_layout = None  # rl_b200.parallel.context_parallel.CPLayout of the current micro-batch
         self.lora = None  # rl_b200.models.lora.LoRAAdapters when LoRA training is on
-        self.router_replay: Optional[dict] = None  # layer -> topk indices to replay (R3)
+        # router replay (R3): layer -> [T, k] expert ids the router must use;
+        # router_record: layer -> [T, k] expert ids chosen (device tensors)
+        self.router_replay: Optional[dict] = None
         self.router_record: Optional[dict] = None
 
     # ------------------------------------------------------------------ params
@@ -508,12 +510,16 @@ class TransformerLM(nn.Module):
         logits = torch.matmul(h.to(rdtype), w.to(rdtype).t())
         probs = torch.softmax(logits, -1)
         if self.router_replay is not None and i in self.router_replay:
-            ids = self.router_replay[i].to(h.device).long()
+            # R3: the experts the rollout chose; tokens without a recorded route
+            # (negative ids, e.g. the last sampled token) keep the computed top-k
+            rep = self.router_replay[i].to(h.device).long()
+            ids = torch.topk(probs, c.moe_top_k, dim=-1)[1]
+            ids = torch.where(rep[:, :1] >= 0, rep, ids)
             vals = probs.gather(-1, ids)
         else:
             vals, ids = torch.topk(probs, c.moe_top_k, dim=-1)
         if self.router_record is not None:
-            self.router_record[i] = ids.detach().to(torch.int16 if c.num_experts < 32768 else torch.int32).cpu()
+            self.router_record[i] = ids.detach().to(torch.int16 if c.num_experts < 32768 else torch.int32)
         if c.moe_norm_topk_prob:
             vals = vals / vals.sum(-1, keepdim=True)
         return vals.to(torch.float32), ids, probs.to(torch.float32)

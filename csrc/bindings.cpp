@@ -31,6 +31,7 @@ at::Tensor sum_sq(at::Tensor x);
 std::vector<at::Tensor> quant_fp8_block(at::Tensor w, int64_t blk, bool pow2, c10::optional<at::Tensor> out,
                                         c10::optional<at::Tensor> out_scale);
 std::vector<at::Tensor> quant_fp8_group(at::Tensor x, int64_t group, bool pow2);
+std::vector<at::Tensor> quant_fp8_group_t(at::Tensor x, int64_t group, bool pow2);
 // attention.cu
 std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu_seqlens,
                                        int64_t max_seqlen, double scale, bool causal);
@@ -44,6 +45,10 @@ at::Tensor gemm_nt(at::Tensor a, at::Tensor b);
 int64_t gemm_error_flag(bool reset);
 void gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> recv_ptrs,
              std::vector<int64_t> flag_ptrs, std::vector<int64_t> ack_ptrs, int64_t me, int64_t epoch);
+// gemm_fp8.cu
+at::Tensor gemm_fp8(at::Tensor a, at::Tensor a_scale, at::Tensor b, at::Tensor b_scale, int64_t splits);
+at::Tensor gemm_mxf8(at::Tensor a, at::Tensor a_scale, at::Tensor b, at::Tensor b_scale, int64_t splits);
+int64_t gemm_fp8_error_flag(bool reset);
 // symm.cu
 std::tuple<int64_t, at::Tensor> symm_alloc(int64_t bytes);
 int64_t symm_open(at::Tensor handle);
@@ -97,12 +102,18 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quant_fp8_block", &quant_fp8_block, py::arg("w"), py::arg("blk"), py::arg("pow2"), py::arg("out") = py::none(),
         py::arg("out_scale") = py::none());
   m.def("quant_fp8_group", &quant_fp8_group);
+  m.def("quant_fp8_group_t", &quant_fp8_group_t, "1 x group e4m3 quantisation with MN-major scales [K/group, Mp]");
   m.def("flash_attn_fwd", &flash_attn_fwd);
   m.def("flash_attn_bwd", &flash_attn_bwd);
   m.def("paged_decode_attn", &paged_decode_attn);
   m.def("gemm_nt", &gemm_nt);
   m.def("gemm_error_flag", &gemm_error_flag, py::arg("reset") = false);
   m.def("gemm_rs", &gemm_rs);
+  m.def("gemm_fp8", &gemm_fp8, py::arg("a"), py::arg("a_scale"), py::arg("b"), py::arg("b_scale"),
+        py::arg("splits") = 0, "block-scaled e4m3 GEMM (1x128 activation, 128x128 weight fp32 scales) -> bf16");
+  m.def("gemm_mxf8", &gemm_mxf8, py::arg("a"), py::arg("a_scale_t"), py::arg("b"), py::arg("b_scale_t"),
+        py::arg("splits") = 0, "e4m3 GEMM with power-of-two block scales applied by the tensor cores -> bf16");
+  m.def("gemm_fp8_error_flag", &gemm_fp8_error_flag, py::arg("reset") = false);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

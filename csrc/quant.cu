@@ -73,6 +73,28 @@ __global__ void quant_group_kernel(const T* __restrict__ x, __nv_fp8_e4m3* __res
   for (int j = lane; j < group; j += 32) dst[j] = __nv_fp8_e4m3(fminf(fmaxf(to_f(src[j]) * inv, -kFp8Max), kFp8Max));
 }
 
+// Same quantisation; the scale of (row, group g) goes to s_t[g * Mp + row]
+// (MN-major, the layout the block-scaled GEMM fetches per K block).
+template <typename T>
+__global__ void quant_group_t_kernel(const T* __restrict__ x, __nv_fp8_e4m3* __restrict__ q, float* __restrict__ s_t,
+                                     long long groups_total, int K, int group, int Mp, bool pow2) {
+  const int lane = threadIdx.x & 31;
+  const long long gi = blockIdx.x * (long long)(blockDim.x >> 5) + (threadIdx.x >> 5);
+  if (gi >= groups_total) return;
+  const int gpr = K / group;
+  const long long row = gi / gpr;
+  const int gc = gi % gpr;
+  const T* src = x + row * K + (long long)gc * group;
+  float amax = 0.f;
+  for (int j = lane; j < group; j += 32) amax = fmaxf(amax, fabsf(to_f(src[j])));
+  amax = warp_max(amax);
+  const float s = fp8_scale(amax, pow2);
+  const float inv = 1.f / s;
+  if (lane == 0) s_t[(long long)gc * Mp + row] = s;
+  __nv_fp8_e4m3* dst = q + row * K + (long long)gc * group;
+  for (int j = lane; j < group; j += 32) dst[j] = __nv_fp8_e4m3(fminf(fmaxf(to_f(src[j]) * inv, -kFp8Max), kFp8Max));
+}
+
 }  // namespace rlb
 
 using namespace rlb;
@@ -114,6 +136,28 @@ std::vector<at::Tensor> quant_fp8_group(at::Tensor x, int64_t group, bool pow2) 
     quant_group_kernel<scalar_t><<<(groups + warps - 1) / warps, warps * 32, 0, stream()>>>(
         (const scalar_t*)x.data_ptr(), (__nv_fp8_e4m3*)q.data_ptr(), s.data_ptr<float>(), groups, K, (int)group,
         pow2);
+  });
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {q, s};
+}
+
+// (q [T, K] e4m3, s_t [K/group, Mp] fp32) with Mp = T rounded up to 128 (pad scales 1.0)
+std::vector<at::Tensor> quant_fp8_group_t(at::Tensor x, int64_t group, bool pow2) {
+  RLB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "quant_fp8_group_t: 2-D contiguous CUDA input expected");
+  RLB_CHECK(x.size(1) % group == 0, "quant_fp8_group_t: K must be a multiple of the group size");
+  const c10::cuda::CUDAGuard g(x.device());
+  const long long T_ = x.size(0);
+  const int K = x.size(1);
+  const int Mp = (int)((T_ + 127) / 128 * 128);
+  auto q = at::empty({T_, K}, x.options().dtype(at::kFloat8_e4m3fn));
+  auto s = at::ones({K / group, (long long)std::max(Mp, 128)}, x.options().dtype(at::kFloat));
+  const long long groups = T_ * (K / group);
+  if (groups == 0) return {q, s};
+  const int warps = 8;
+  RLB_DISPATCH_FLOAT(x.scalar_type(), "quant_fp8_group_t", [&] {
+    quant_group_t_kernel<scalar_t><<<(groups + warps - 1) / warps, warps * 32, 0, stream()>>>(
+        (const scalar_t*)x.data_ptr(), (__nv_fp8_e4m3*)q.data_ptr(), s.data_ptr<float>(), groups, K, (int)group,
+        (int)s.size(1), pow2);
   });
   RLB_CUDA_CHECK(cudaGetLastError());
   return {q, s};

@@ -5,6 +5,7 @@
     python -m rl_b200.bench_kernels decode_gemm [M]
     python -m rl_b200.bench_kernels attn      [T_per_seq n_seq]
     python -m rl_b200.bench_kernels logprob   [T V]
+    python -m rl_b200.bench_kernels fp8       [M N K]
 
 Each prints one line with the time and the achieved rate, and is small enough
 to be captured under ``ncu -k <kernel> -c 1`` (a few GB on the device at most).
@@ -103,6 +104,41 @@ def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):
           f"{2.5 * fl / tb / 1e9:.1f} TFLOP/s")
 
 
+def bench_fp8(M=8192, N=8192, K=8192):
+    """Block-scaled e4m3 GEMM (activation quantisation excluded) against the
+    library bf16 GEMM and the library fp8 GEMM with one scale per tensor."""
+    from rl_b200.ops._ext import ext
+    from rl_b200.ops.quant import quant_fp8_block, quant_fp8_group
+
+    dev = torch.device("cuda")
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=dev) * 0.05).to(torch.bfloat16)
+    a_q, a_s = quant_fp8_group(x, 128, False)
+    b_q, b_s = quant_fp8_block(w, 128, False)
+    t = _time(lambda: ext().gemm_fp8(a_q, a_s, b_q, b_s, 0))
+    from rl_b200.ops.fp8_gemm import mx_weight_scales, quant_act_mx
+
+    p_q, p_s = quant_act_mx(x)
+    w_q, w_s = quant_fp8_block(w, 128, True)
+    w_st = mx_weight_scales(w_s)
+    tm = _time(lambda: ext().gemm_mxf8(p_q, p_s, w_q, w_st, 0))
+    tmq = _time(lambda: quant_act_mx(x))
+    tq = _time(lambda: quant_fp8_group(x, 128, False))
+    tl = _time(lambda: torch.matmul(x, w.t()))
+    one = torch.ones((), device=dev)
+    try:
+        ts = _time(lambda: torch._scaled_mm(a_q, b_q.t(), scale_a=one, scale_b=one, out_dtype=torch.bfloat16))
+        lib8 = f" | library fp8 per-tensor {ts:.3f} ms {2 * M * N * K / ts / 1e9:.1f} TFLOP/s"
+    except Exception as e:  # noqa: BLE001 - report what the library does not support
+        lib8 = f" | library fp8 unavailable ({type(e).__name__})"
+    fl = 2 * M * N * K
+    byts = M * K + N * K + M * N * 2
+    print(f"gemm_mxf8 {M}x{N}x{K}: {tm:.3f} ms {fl / tm / 1e9:.1f} TFLOP/s {byts / (tm * 1e-3) / 1e12:.2f} TB/s "
+          f"(+ act quant {tmq:.3f} ms)")
+    print(f"gemm_fp8 {M}x{N}x{K}: {t:.3f} ms {fl / t / 1e9:.1f} TFLOP/s {byts / (t * 1e-3) / 1e12:.2f} TB/s "
+          f"(+ act quant {tq:.3f} ms) | library bf16 {tl:.3f} ms {fl / tl / 1e9:.1f} TFLOP/s{lib8}")
+
+
 def bench_logprob(T=8192, V=128256):
     from rl_b200.ops.logprob import token_logprobs_and_entropy
 
@@ -119,7 +155,7 @@ def main(argv=None):
     args = [int(x) for x in argv]
     torch.manual_seed(0)
     {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
-     "logprob": bench_logprob}[what](*args)
+     "logprob": bench_logprob, "fp8": bench_fp8}[what](*args)
 
 
 if __name__ == "__main__":

@@ -111,6 +111,10 @@ class PolicyWorker:
         if self.gen_tp not in (1, self.ps.tp_size):
             raise NotImplementedError(f"generation TP {self.gen_tp} must be 1 or the training TP {self.ps.tp_size}")
         self.fp8_rollout = str(vcfg.get("precision", gen_cfg.get("precision", "bfloat16"))).lower() == "fp8"
+        # fp8 rollout scales: powers of two (hardware-scaled GEMM) unless a config
+        # turns the reference's pow2 options off (then fp32 scales, promoting GEMM)
+        self.fp8_pow2 = vcfg.get("pow2_weight_scaling_factors") is not False and \
+            vcfg.get("pow2_activation_scaling_factors") is not False
         resharded = self.gen_tp != self.ps.tp_size
         self.pp = self.ps.pp_size
         if self.pp > 1:
@@ -230,7 +234,33 @@ class PolicyWorker:
             from rl_b200.parallel.pipeline import PipelineComm
 
             self._pp_comm = PipelineComm(self.ps)
-        self.weight_sync.sync()  # the rollout copy starts from the initial weights
+        self._fp8_scales: dict = {}
+        self._sync_weights()  # the rollout copy starts from the initial weights
+
+    def _sync_weights(self) -> None:
+        """Refresh the rollout weights; with an fp8 rollout also point the rollout
+        model at the quantised weights (scales re-laid-out in place, so captured
+        decode graphs keep reading valid buffers)."""
+        self.weight_sync.sync()
+        ws = self.weight_sync
+        if not (self.fp8_rollout and getattr(ws, "fp8", False)):
+            return
+        from rl_b200.ops.fp8_gemm import mx_weight_scales
+
+        fw = {}
+        for name in ws.q_layout:
+            q, sc = ws.fp8_weight(name)
+            if self.fp8_pow2:
+                st = self._fp8_scales.get(name)
+                if st is None:
+                    st = self._fp8_scales[name] = mx_weight_scales(sc)
+                else:
+                    st[:, :sc.shape[0]].copy_(sc.t())
+                fw[name] = (q, st)
+            else:
+                fw[name] = (q, sc)
+        self.gen_model.fp8_pow2 = self.fp8_pow2
+        self.gen_model.fp8_weights = fw
 
     def _make_weight_sync(self, resharded: bool):
         from rl_b200.weight_sync.colocated import (ColocatedInPlaceSynchronizer, ColocatedReshardSynchronizer,
@@ -245,15 +275,22 @@ class PolicyWorker:
 
             return PipelineGatherSynchronizer(self.model, self.gen_model, self.ps.pp_group, self.ps.pp_ranks,
                                               self.ps.pp_rank)
-        if not resharded:
+        if not resharded and not self.fp8_rollout:
             return ColocatedInPlaceSynchronizer()
+        if not resharded:
+            # same layout, fp8 rollout weights: quantise this rank's own shard in place
+            own = [self.model.flat_param.data_ptr() if r == self.ps.tp_rank else 0 for r in range(self.ps.tp_size)]
+            return ColocatedReshardSynchronizer(self.model, self.gen_model, self.ps.tp_group, self.ps.tp_rank,
+                                                self.ps.tp_size, peer_ptrs=own if self.device.type == "cuda" else None,
+                                                fp8=True, pow2_scales=self.fp8_pow2, copy_bf16=False)
         peer_ptrs = None
         symm = getattr(self.model.flat_param, "_symm", None)
         if symm is not None:
             # symmetric buffers are indexed by global rank; the reshard wants TP-group order
             peer_ptrs = [symm.ptrs[dist.get_global_rank(self.ps.tp_group, r)] for r in range(self.ps.tp_size)]
         return ColocatedReshardSynchronizer(self.model, self.gen_model, self.ps.tp_group, self.ps.tp_rank,
-                                            self.ps.tp_size, peer_ptrs=peer_ptrs, fp8=self.fp8_rollout)
+                                            self.ps.tp_size, peer_ptrs=peer_ptrs, fp8=self.fp8_rollout,
+                                            pow2_scales=self.fp8_pow2)
 
     # ------------------------------------------------------------- helpers
     def _plan(self, lengths: list[int], rows: list[int], budget: int) -> list[list[int]]:
@@ -898,7 +935,7 @@ class PolicyWorker:
         rollout layout (or fp8 rollout weights) the weight synchronizer reshards
         the training shards from the TP peers into the rollout copy."""
         t0 = time.perf_counter()
-        self.weight_sync.sync()
+        self._sync_weights()
         self.engine.update_weights_from_training()
         self.engine.invalidate_kv_cache()
         return time.perf_counter() - t0
@@ -939,12 +976,12 @@ class PolicyWorker:
                 with torch.no_grad():
                     for seg in self.optimizer.segments:
                         seg.master.copy_(self.lora.flat_param[seg.s_lo:seg.s_hi])
-            self.weight_sync.sync()
+            self._sync_weights()
             return
 
         if os.path.isdir(os.path.join(weights_path, "iter_0000000")):
             cio.load_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
-            self.weight_sync.sync()
+            self._sync_weights()
             return
         cio.load_hf_checkpoint(self.model, weights_path)
         rank = dist.get_rank() if dist.is_initialized() else 0
@@ -955,7 +992,7 @@ class PolicyWorker:
             with torch.no_grad():
                 for seg in self.optimizer.segments:
                     seg.master.copy_(self.model.flat_param[seg.s_lo:seg.s_hi])
-        self.weight_sync.sync()
+        self._sync_weights()
 
     def shutdown(self) -> None:
         """Release the rollout engine's captured graphs (they may hold NCCL

@@ -214,6 +214,13 @@ class TransformerLM(nn.Module):
         # router_record: layer -> [T, k] expert ids chosen (device tensors)
         self.router_replay: Optional[dict] = None
         self.router_record: Optional[dict] = None
+        # fp8 rollout: name -> (e4m3 weight, block scales) used by the rollout
+        # forwards only (forward_prefill / forward_decode); power-of-two scales in
+        # the MN-major layout of the hardware-scaled GEMM when fp8_pow2, else
+        # [ceil(N/128), K/128] fp32 scales for the promoting GEMM
+        self.fp8_weights: Optional[dict] = None
+        self.fp8_pow2 = True
+        self._in_rollout = False
 
     # ------------------------------------------------------------------ params
     def _make_specs(self) -> list[ParamSpec]:
@@ -441,8 +448,21 @@ class TransformerLM(nn.Module):
         return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
                                          p + "self_attn.o_proj.weight")
 
+    def _lin_infer(self, x: torch.Tensor, name: str) -> torch.Tensor:
+        """Rollout-time projection: the block-scaled e4m3 weight when the fp8
+        rollout holds one for ``name``, else the bf16 weight."""
+        fw = self.fp8_weights
+        if fw is not None and self._in_rollout and name in fw and x.shape[-1] % 128 == 0:
+            from rl_b200.ops.fp8_gemm import fp8_linear, fp8_linear_mx
+
+            q, sc = fw[name]
+            return fp8_linear_mx(x, q, sc) if self.fp8_pow2 else fp8_linear(x, q, sc)
+        return linear(x, self._params[name])
+
     def _col_linear(self, h: torch.Tensor, name: str) -> torch.Tensor:
         """Column-parallel projection (+ LoRA delta when adapters are attached)."""
+        if self._in_rollout and self.fp8_weights is not None and self.lora is None:
+            return self._lin_infer(h, name)
         y = linear(h, self._params[name])
         if self.lora is not None:
             d = self.lora.delta(name, h)
@@ -671,6 +691,14 @@ class TransformerLM(nn.Module):
                         last_token_index: torch.Tensor) -> torch.Tensor:
         """Prompt prefill: runs the packed prompts, writes K/V into the paged cache,
         returns the final hidden state of each sequence's last token ``[B, H]``."""
+        self._in_rollout = True
+        try:
+            return self._forward_prefill(input_ids, positions, cu_seqlens, max_seqlen, kv, slot_mapping,
+                                         last_token_index)
+        finally:
+            self._in_rollout = False
+
+    def _forward_prefill(self, input_ids, positions, cu_seqlens, max_seqlen, kv, slot_mapping, last_token_index):
         x = self.embed_full(input_ids)
         resid = None
         eps = self.cfg.rms_eps
@@ -686,7 +714,7 @@ class TransformerLM(nn.Module):
             kc, vc = kv.layer(i)
             write_kv_cache(k, v, kc, vc, slot_mapping)
             o, _ = flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen, causal=True)
-            a = self._tp_sum(linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"]))
+            a = self._tp_sum(self._lin_infer(o.reshape(o.shape[0], -1), p + "self_attn.o_proj.weight"))
             h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
             m = self._mlp_infer(i, h2)
             x, resid = s2, m
@@ -713,6 +741,13 @@ class TransformerLM(nn.Module):
     def forward_decode(self, tokens, positions, kv: KVCache, block_tables, seq_lens, slot_mapping,
                        max_seq_len: int = 0) -> torch.Tensor:
         """One decode step for ``B`` sequences: ``tokens [B]`` -> hidden ``[B, H]``."""
+        self._in_rollout = True
+        try:
+            return self._forward_decode(tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len)
+        finally:
+            self._in_rollout = False
+
+    def _forward_decode(self, tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len):
         ar = self._decode_ar_op(tokens.shape[0]) if not self.cfg.is_moe else None
         if ar is not None:
             return self._forward_decode_fused_ar(tokens, positions, kv, block_tables, seq_lens, slot_mapping,
@@ -733,7 +768,7 @@ class TransformerLM(nn.Module):
             write_kv_cache(k, v, kc, vc, slot_mapping)
             o = paged_decode_attention(q, kc, vc, block_tables, seq_lens, max_seq_len=max_seq_len,
                                        k_scale=kv.k_scale, v_scale=kv.v_scale)
-            a = self._tp_sum(linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"]))
+            a = self._tp_sum(self._lin_infer(o.reshape(o.shape[0], -1), p + "self_attn.o_proj.weight"))
             h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
             m = self._mlp_infer(i, h2)
             x, resid = s2, m
@@ -755,10 +790,10 @@ class TransformerLM(nn.Module):
             write_kv_cache(k, v, kc, vc, slot_mapping)
             o = paged_decode_attention(q, kc, vc, block_tables, seq_lens, max_seq_len=max_seq_len,
                                        k_scale=kv.k_scale, v_scale=kv.v_scale)
-            a = linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"])
+            a = self._lin_infer(o.reshape(o.shape[0], -1), p + "self_attn.o_proj.weight")
             h2 = ar(a, s, self._params[p + "post_attention_layernorm.weight"], eps)
-            gu = linear(h2, self._params[p + "mlp.gate_up_proj.weight"])
-            m = linear(swiglu(gu), self._params[p + "mlp.down_proj.weight"])
+            gu = self._lin_infer(h2, p + "mlp.gate_up_proj.weight")
+            m = self._lin_infer(swiglu(gu), p + "mlp.down_proj.weight")
             w_next = self._params[f"model.layers.{i + 1}.input_layernorm.weight"] if i + 1 < L \
                 else self._params["model.norm.weight"]
             h = ar(m, s, w_next, eps)
@@ -790,8 +825,8 @@ class TransformerLM(nn.Module):
                 return self._moe_block(i, h)
             finally:
                 self.sequence_parallel = sp
-        gu = linear(h, self._params[p + "mlp.gate_up_proj.weight"])
-        return self._tp_sum(linear(swiglu(gu), self._params[p + "mlp.down_proj.weight"]))
+        gu = self._lin_infer(h, p + "mlp.gate_up_proj.weight")
+        return self._tp_sum(self._lin_infer(swiglu(gu), p + "mlp.down_proj.weight"))
 
     def logits_infer(self, hidden: torch.Tensor) -> torch.Tensor:
         """Full-vocab logits for sampling ``[B, V]`` (TP shards all-gathered)."""

@@ -541,3 +541,43 @@ def test_prev_logprobs_folded_into_training_forward():
     rb = b.train(d2, lf, gbs=8, prev_from_current=True)
     assert abs(ra["loss"] - rb["loss"]) < 1e-6 and abs(ra["grad_norm"] - rb["grad_norm"]) < 1e-5
     assert torch.allclose(a.model.flat_param, b.model.flat_param)
+
+
+def test_fp8_rollout_weights_used_and_refreshed():
+    """fp8 rollout (vllm_cfg.precision: fp8): the refit quantises the linear
+    weights (128 x 128 blocks, power-of-two scales), the rollout forwards use
+    them (close to the bf16 forward, not identical), training forwards do not,
+    and a training step refreshes them."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.policy.worker import PolicyWorker
+    from tests.dist_cases import make_batch
+
+    cfg = ModelConfig(name="tiny-128", vocab_size=512, hidden_size=128, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=32, ffn_hidden_size=256, rope_theta=10000.0, max_position_embeddings=256)
+    pc = {"max_total_sequence_length": 48, "precision": "float32", "train_global_batch_size": 8,
+          "optimizer": {"kwargs": {"lr": 1e-2, "weight_decay": 0.0}},
+          "generation": {"temperature": 1.0, "max_new_tokens": 6, "vllm_cfg": {"precision": "fp8"},
+                         "mcore_generation_config": {"block_size_tokens": 8}},
+          "sequence_packing": {"train_mb_tokens": 96, "logprob_mb_tokens": 96}}
+    w = PolicyWorker(pc, model_cfg=cfg, seed=1)
+    fw = w.gen_model.fp8_weights
+    assert fw is not None and len(fw) == 4 * cfg.num_layers and w.gen_model.fp8_pow2
+    name = "model.layers.0.mlp.down_proj.weight"
+    q0 = fw[name][0].float().clone()
+    x = torch.randn(5, 256)
+    ref = x @ w.model.param(name).detach().t()
+    w.gen_model._in_rollout = True
+    y = w.gen_model._lin_infer(x, name)
+    w.gen_model._in_rollout = False
+    err = ((y.float() - ref).norm() / ref.norm()).item()
+    assert 0 < err < 0.08
+    assert torch.equal(w.gen_model._lin_infer(x, name), torch.nn.functional.linear(x, w.model.param(name)))
+    data = BatchedDataDict({"input_ids": torch.randint(0, 512, (3, 9)), "input_lengths": torch.tensor([9, 5, 7])})
+    out = w.generate(data)
+    assert int(out["generation_lengths"].min()) >= 1
+    b = make_batch(B=8, S=24, vocab=512)
+    w.train(b, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)
+    w.refit()
+    assert not torch.equal(w.gen_model.fp8_weights[name][0].float(), q0)

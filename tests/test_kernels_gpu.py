@@ -379,3 +379,58 @@ def test_spec_verify_greedy(cuda_device):
     rt, rn, rlp = spec_verify_ref(tl.to(torch.bfloat16), dl.to(torch.bfloat16), draft, temperature=0.0)
     assert torch.equal(n.cpu(), rn) and torch.equal(tok.cpu(), rt)
     assert torch.allclose(lp.cpu(), rlp, atol=2e-2)
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(256, 512, 1024, 1), (1000, 6144, 4096, 0), (64, 4096, 4096, 0),
+                                          (200, 320, 256, 1), (128, 128, 128, 0), (77, 1024, 2048, 3)])
+def test_gemm_fp8_blockscaled(cuda_device, M, N, K, splits):
+    """tcgen05 kind::f8f6f4 GEMM with per-128-K-block promotion against the fp32
+    product of the same quantised operands (1x128 activation, 128x128 weight scales)."""
+    from rl_b200.ops.fp8_gemm import gemm_fp8_ref
+    from rl_b200.ops.quant import quant_fp8_block, quant_fp8_group
+
+    ext = _ext.ext()
+    torch.manual_seed(9)
+    x = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    # weights with per-block magnitudes that differ, so wrong scale indexing shows
+    w = torch.randn(N, K, device=cuda_device) * 0.05
+    w = w * torch.rand(-(-N // 128), 1, -(-K // 128), 1, device=cuda_device).mul(4).add(0.25).expand(
+        -1, 128, -1, 128).reshape(-(-N // 128) * 128, -(-K // 128) * 128)[:N, :K]
+    w = w.to(torch.bfloat16)
+    a_q, a_s = quant_fp8_group(x, 128, False)
+    b_q, b_s = quant_fp8_block(w, 128, False)
+    y = ext.gemm_fp8(a_q, a_s, b_q, b_s, splits)
+    torch.cuda.synchronize()
+    assert ext.gemm_fp8_error_flag(True) == 0
+    ref = gemm_fp8_ref(a_q, a_s, b_q, b_s)
+    assert rel_err(y, ref) < 5e-3
+    # and close to the unquantised product (fp8 rounding only)
+    assert rel_err(y, x.float() @ w.float().t()) < 6e-2
+
+
+@pytest.mark.parametrize("M,N,K,splits", [(256, 448, 1024, 1), (1000, 6144, 4096, 0), (64, 4096, 4096, 0),
+                                          (200, 320, 256, 1), (128, 224, 128, 1), (77, 1024, 2048, 3),
+                                          (4096, 14336, 512, 1)])
+def test_gemm_mxf8_hardware_block_scale(cuda_device, M, N, K, splits):
+    """kind::mxf8f6f4.block_scale GEMM (power-of-two scales applied by the tensor
+    cores from tensor memory) against the fp32 product of the same operands."""
+    from rl_b200.ops.fp8_gemm import gemm_fp8_ref, mx_weight_scales, quant_act_mx
+    from rl_b200.ops.quant import quant_fp8_block, quant_fp8_group
+
+    ext = _ext.ext()
+    torch.manual_seed(10)
+    x = torch.randn(M, K, device=cuda_device).to(torch.bfloat16)
+    w = torch.randn(N, K, device=cuda_device) * 0.05
+    w = w * torch.rand(-(-N // 128), 1, -(-K // 128), 1, device=cuda_device).mul(16).add(0.1).expand(
+        -1, 128, -1, 128).reshape(-(-N // 128) * 128, -(-K // 128) * 128)[:N, :K]
+    w = w.to(torch.bfloat16)
+    a_q, a_s = quant_fp8_group(x, 128, True)
+    b_q, b_s = quant_fp8_block(w, 128, True)
+    assert torch.equal(torch.exp2(torch.log2(b_s).round()), b_s)  # the quantiser's scales are powers of two
+    a_q2, a_s_t = quant_act_mx(x)
+    assert torch.equal(a_q2.view(torch.uint8), a_q.view(torch.uint8)) and torch.equal(a_s_t[:, :M], a_s.t())
+    y = ext.gemm_mxf8(a_q, a_s_t, b_q, mx_weight_scales(b_s), splits)
+    torch.cuda.synchronize()
+    assert ext.gemm_fp8_error_flag(True) == 0
+    ref = gemm_fp8_ref(a_q, a_s, b_q, b_s)
+    assert rel_err(y, ref) < 5e-3

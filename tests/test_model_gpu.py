@@ -109,3 +109,34 @@ def test_grpo_steps_on_gpu(cuda_device):
         assert torch.isfinite(torch.tensor(m["loss"]))
         assert m["gen_kl_error"] < 2e-3
         assert 0.79 < m["probs_ratio_clamped_min"] <= m["probs_ratio_clamped_max"] < 1.21
+
+
+@pytest.mark.parametrize("pow2", [True, False])
+def test_fp8_rollout_generation(cuda_device, pow2):
+    """fp8 rollout on the GPU: the refit quantises the linear weights into e4m3
+    128x128 blocks, prefill and CUDA-graph decode run the block-scaled tcgen05
+    GEMMs (hardware-scaled with power-of-two scales, promoting otherwise), and
+    the rollout log-probs stay close to the bf16 trainer's."""
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.ops import _ext
+
+    cfg = _policy_cfg(new=24)
+    cfg["generation"]["vllm_cfg"] = {"precision": "fp8", "pow2_weight_scaling_factors": pow2,
+                                     "pow2_activation_scaling_factors": pow2}
+    w = PolicyWorker(cfg, model_cfg=SMALL, seed=5)
+    assert w.gen_model.fp8_weights is not None and w.gen_model.fp8_pow2 == pow2
+    g = torch.Generator().manual_seed(2)
+    data = BatchedDataDict({"input_ids": torch.randint(0, SMALL.vocab_size, (8, 40), generator=g),
+                            "input_lengths": torch.randint(20, 41, (8,), generator=g)})
+    out = w.generate(data)
+    torch.cuda.synchronize()
+    assert _ext.ext().gemm_fp8_error_flag(True) == 0
+    seqs = BatchedDataDict({"input_ids": out["output_ids"], "input_lengths": out["unpadded_sequence_lengths"]})
+    lp = w.get_logprobs(seqs)["logprobs"]
+    mask = torch.zeros_like(lp, dtype=torch.bool)
+    for b in range(8):
+        L, n = int(data["input_lengths"][b]), int(out["generation_lengths"][b])
+        mask[b, L:L + n] = True
+    diff = (lp - out["logprobs"])[mask].abs()
+    assert diff.mean().item() < 0.1, diff.mean().item()
+    w.shutdown()

@@ -134,6 +134,13 @@ class PolicyWorker:
         self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
                                    sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt,
                                    num_labels=self.num_labels, flat_alloc=flat_alloc)
+        f8 = mc.get("fp8_cfg") or {}
+        if f8.get("enabled", False):
+            if str(f8.get("fp8", "e4m3")).lower() != "e4m3" or \
+                    str(f8.get("fp8_recipe", "blockwise")).lower() not in ("blockwise", "mxfp8"):
+                raise NotImplementedError(f"fp8 training recipe {f8.get('fp8')}/{f8.get('fp8_recipe')}")
+            # power-of-two (E8M0) block scales unless turned off: the tensor cores apply them
+            self.model.fp8_train = {"pow2": bool(f8.get("pow2_scales", True))}
         from rl_b200.models.lora import LoRAAdapters, LoRAConfig
 
         lcfg = LoRAConfig(policy_cfg.get("lora_cfg") or mc.get("lora_cfg")
@@ -639,6 +646,7 @@ class PolicyWorker:
         flat = self.model.flat_param
         n = self.ref_flat.numel()
         flat[:n].copy_(self.ref_flat)
+        self.model.bump_weight_version()
         try:
             yield
         finally:
@@ -981,9 +989,11 @@ class PolicyWorker:
 
         if os.path.isdir(os.path.join(weights_path, "iter_0000000")):
             cio.load_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
+            self.model.bump_weight_version()
             self._sync_weights()
             return
         cio.load_hf_checkpoint(self.model, weights_path)
+        self.model.bump_weight_version()
         rank = dist.get_rank() if dist.is_initialized() else 0
         opt_file = os.path.join(optimizer_path, f"__{rank}.pt") if optimizer_path else None
         if opt_file and os.path.exists(opt_file):

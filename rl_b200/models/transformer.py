@@ -221,6 +221,11 @@ class TransformerLM(nn.Module):
         self.fp8_weights: Optional[dict] = None
         self.fp8_pow2 = True
         self._in_rollout = False
+        # fp8 training (blockwise recipe): {"pow2": bool} when enabled; quantised
+        # weights are cached per parameter until weight_version changes
+        self.fp8_train: Optional[dict] = None
+        self.weight_version = 0
+        self._fp8_cache: dict = {}
 
     # ------------------------------------------------------------------ params
     def _make_specs(self) -> list[ParamSpec]:
@@ -384,7 +389,8 @@ class TransformerLM(nn.Module):
 
     def _fused_ag_ok(self, h: torch.Tensor) -> bool:
         return (self.ps.tp_size > 1 and self.sequence_parallel and self.fused_collectives and h.is_cuda
-                and h.dtype == torch.bfloat16 and h.shape[0] % 128 == 0 and self.lora is None)
+                and h.dtype == torch.bfloat16 and h.shape[0] % 128 == 0 and self.lora is None
+                and self.fp8_train is None)
 
     def _ag_linear(self, h_shard: torch.Tensor, name: str) -> torch.Tensor:
         """Column-parallel projection of the SP-sharded input with the all-gather
@@ -448,6 +454,22 @@ class TransformerLM(nn.Module):
         return self._row_parallel_linear(o.reshape(o.shape[0], -1), self._params[p + "self_attn.o_proj.weight"],
                                          p + "self_attn.o_proj.weight")
 
+    def bump_weight_version(self) -> None:
+        """The parameters changed (optimizer step, weight swap, load): cached
+        quantised copies are stale."""
+        self.weight_version += 1
+
+    def _train_linear(self, x: torch.Tensor, w: torch.Tensor, name: Optional[str]) -> torch.Tensor:
+        """Training / log-prob projection: block-scaled e4m3 fprop + dgrad when
+        fp8 training is on (and the shape allows it), else bf16."""
+        if self.fp8_train is not None and name is not None and not self._in_rollout:
+            from rl_b200.ops.fp8_linear import fp8_supported, fp8_train_linear
+
+            if fp8_supported(w):
+                return fp8_train_linear(x, w, self._fp8_cache, name, self.weight_version,
+                                        bool(self.fp8_train.get("pow2", True)))
+        return linear(x, w)
+
     def _lin_infer(self, x: torch.Tensor, name: str) -> torch.Tensor:
         """Rollout-time projection: the block-scaled e4m3 weight when the fp8
         rollout holds one for ``name``, else the bf16 weight."""
@@ -463,7 +485,7 @@ class TransformerLM(nn.Module):
         """Column-parallel projection (+ LoRA delta when adapters are attached)."""
         if self._in_rollout and self.fp8_weights is not None and self.lora is None:
             return self._lin_infer(h, name)
-        y = linear(h, self._params[name])
+        y = self._train_linear(h, self._params[name], name if self.lora is None else None)
         if self.lora is not None:
             d = self.lora.delta(name, h)
             if d is not None:
@@ -494,7 +516,7 @@ class TransformerLM(nn.Module):
             if self.sequence_parallel:
                 y = scatter_to_sp(y, self.ps.tp_group)
             return base + y
-        if (tp > 1 and self.sequence_parallel and self.fused_collectives and x.is_cuda
+        if (tp > 1 and self.sequence_parallel and self.fused_collectives and x.is_cuda and self.fp8_train is None
                 and x.dtype == torch.bfloat16 and x.shape[0] % (128 * tp) == 0 and w.shape[0] % 32 == 0):
             from rl_b200.parallel.fused import GemmReduceScatter, row_parallel_rs
 
@@ -503,7 +525,7 @@ class TransformerLM(nn.Module):
                     self._fused_rs.close()
                 self._fused_rs = GemmReduceScatter(self.ps.tp_group, max(x.shape[0], 16384), w.shape[0])
             return row_parallel_rs(x, w, self._fused_rs)
-        return self._row_parallel_out(linear(x, w))
+        return self._row_parallel_out(self._train_linear(x, w, name))
 
     # -------------------------------------------------------------------- MLP
     def _mlp_block(self, i: int, h: torch.Tensor) -> torch.Tensor:

@@ -331,6 +331,9 @@ class FlatAdamW:
                 if seg.n > 1 and self._fused(seg):
                     self._fence(seg.group)
         self.zero_grad()
+        bump = getattr(m, "bump_weight_version", None)
+        if bump is not None:
+            bump()
         return {"grad_norm": norm, "lr": lr}
 
     # ------------------------------------------------------ fused DP path
@@ -360,6 +363,8 @@ class FlatAdamW:
     def restore_params_from_master(self) -> None:
         """Rewrite the bf16 parameters from the fp32 master shards (after a weight swap)."""
         m = self.model
+        if getattr(m, "bump_weight_version", None) is not None:
+            m.bump_weight_version()
         for seg in self.segments:
             m.flat_param[seg.s_lo:seg.s_hi].copy_(seg.master)
             if seg.n > 1:

@@ -581,3 +581,57 @@ def test_fp8_rollout_weights_used_and_refreshed():
     w.train(b, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)
     w.refit()
     assert not torch.equal(w.gen_model.fp8_weights[name][0].float(), q0)
+
+
+def test_fp8_training_linear_and_loop():
+    """fp8 blockwise training: fprop and dgrad through block-scaled e4m3 GEMMs
+    (1x128 activations / gradients, 128x128 weights and their transpose), wgrad
+    in full precision; the weight cache follows the model's weight version; a
+    few GRPO-loss steps with fp8 on track the bf16/fp32 run."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.ops.fp8_linear import fp8_train_linear
+    from tests.dist_cases import make_batch
+
+    torch.manual_seed(0)
+    for pow2 in (True, False):
+        x = torch.randn(50, 256, requires_grad=True)
+        w = torch.nn.Parameter(torch.randn(384, 256) * 0.05)
+        cache = {}
+        y = fp8_train_linear(x, w, cache, "w", 0, pow2)
+        g = torch.randn_like(y)
+        (y * g).sum().backward()
+        x2 = x.detach().clone().requires_grad_(True)
+        w2 = w.detach().clone().requires_grad_(True)
+        y2 = x2 @ w2.t()
+        (y2 * g).sum().backward()
+        rel = lambda a, b: ((a - b).norm() / b.norm()).item()  # noqa: E731
+        assert rel(y.float(), y2) < 0.08 and rel(x.grad, x2.grad) < 0.08
+        assert torch.allclose(w.grad, w2.grad, atol=1e-4)  # wgrad is not quantised
+        fw = cache["w"]
+        fp8_train_linear(x, w, cache, "w", 0, pow2)
+        assert cache["w"] is fw  # same version: cached
+        fp8_train_linear(x, w, cache, "w", 1, pow2)
+        assert cache["w"] is not fw
+
+    cfg = ModelConfig(name="tiny-128", vocab_size=512, hidden_size=128, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=32, ffn_hidden_size=256, rope_theta=10000.0, max_position_embeddings=256)
+
+    def run(fp8):
+        pc = {"max_total_sequence_length": 48, "precision": "float32", "train_global_batch_size": 8,
+              "optimizer": {"kwargs": {"lr": 3e-3, "weight_decay": 0.0}},
+              "megatron_cfg": {"fp8_cfg": {"enabled": fp8, "fp8": "e4m3", "fp8_recipe": "blockwise"}},
+              "generation": {"temperature": 1.0, "max_new_tokens": 4},
+              "sequence_packing": {"train_mb_tokens": 96, "logprob_mb_tokens": 96}}
+        w = PolicyWorker(pc, model_cfg=cfg, seed=1)
+        b = make_batch(B=8, S=24, vocab=512)
+        losses = [w.train(b, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)["loss"]
+                  for _ in range(3)]
+        return losses, w
+
+    l8, w8 = run(True)
+    l32, _ = run(False)
+    assert w8.model.fp8_train is not None and len(w8.model._fp8_cache) == 4 * cfg.num_layers
+    assert w8.model.weight_version == 3
+    assert all(abs(a - b) < 0.05 * max(1.0, abs(b)) for a, b in zip(l8, l32)), (l8, l32)

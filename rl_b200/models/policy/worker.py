@@ -141,6 +141,13 @@ class PolicyWorker:
                 raise NotImplementedError(f"fp8 training recipe {f8.get('fp8')}/{f8.get('fp8_recipe')}")
             # power-of-two (E8M0) block scales unless turned off: the tensor cores apply them
             self.model.fp8_train = {"pow2": bool(f8.get("pow2_scales", True))}
+        from rl_b200.models.quantization import QAT, QATConfig
+
+        qcfg = QATConfig.from_cfg(policy_cfg.get("quant_cfg"))
+        if qcfg is not None:
+            if self.model.fp8_train is not None:
+                raise ValueError("quant_cfg (fake-quantised training) and fp8_cfg (fp8 GEMMs) are exclusive")
+            self.model.qat = QAT(qcfg)
         from rl_b200.models.lora import LoRAAdapters, LoRAConfig
 
         lcfg = LoRAConfig(policy_cfg.get("lora_cfg") or mc.get("lora_cfg")
@@ -858,6 +865,26 @@ class PolicyWorker:
             agg["moe_aux_loss"] = self.model.aux_loss()
             return agg
         return out
+
+    # ------------------------------------------------ quantisation-aware training
+    @torch.no_grad()
+    def calibrate_quantizers(self, data: BatchedDataDict) -> dict:
+        """Record every quantised layer's input amax over forwards of ``data``
+        (the calibration pass of fake-quantised training); returns the stats.
+        Reference: ``_quantize`` of the ModelOpt quantised policy worker
+        (``nemo_rl/modelopt/models/policy/workers/megatron_quant_policy_worker.py:195``)."""
+        q = self.model.qat
+        if q is None:
+            raise RuntimeError("policy.quant_cfg is not set")
+        q.calibrating = True
+        try:
+            self.get_logprobs(data)
+        finally:
+            q.calibrating = False
+        return q.quantizer_stats()
+
+    def get_quantizer_stats(self) -> dict:
+        return self.model.qat.quantizer_stats() if self.model.qat is not None else {}
 
     # -------------------------------------------------------- generation
     def generate(self, data: BatchedDataDict, greedy: bool = False) -> BatchedDataDict:

@@ -224,6 +224,7 @@ class TransformerLM(nn.Module):
         # fp8 training (blockwise recipe): {"pow2": bool} when enabled; quantised
         # weights are cached per parameter until weight_version changes
         self.fp8_train: Optional[dict] = None
+        self.qat = None  # rl_b200.models.quantization.QAT (fake-quantised training forward)
         self.weight_version = 0
         self._fp8_cache: dict = {}
 
@@ -462,6 +463,8 @@ class TransformerLM(nn.Module):
     def _train_linear(self, x: torch.Tensor, w: torch.Tensor, name: Optional[str]) -> torch.Tensor:
         """Training / log-prob projection: block-scaled e4m3 fprop + dgrad when
         fp8 training is on (and the shape allows it), else bf16."""
+        if self.qat is not None and not self._in_rollout and self.qat.applies(name):
+            return linear(self.qat.input(name, x), self.qat.weight(name, w))
         if self.fp8_train is not None and name is not None and not self._in_rollout:
             from rl_b200.ops.fp8_linear import fp8_supported, fp8_train_linear
 

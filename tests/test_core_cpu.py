@@ -635,3 +635,45 @@ def test_fp8_training_linear_and_loop():
     assert w8.model.fp8_train is not None and len(w8.model._fp8_cache) == 4 * cfg.num_layers
     assert w8.model.weight_version == 3
     assert all(abs(a - b) < 0.05 * max(1.0, abs(b)) for a, b in zip(l8, l32)), (l8, l32)
+
+
+def test_quantization_aware_training():
+    """Fake-quantised training (policy.quant_cfg): fp8 block / per-tensor and
+    NVFP4 quantise-dequantise match their definitions, gradients pass straight
+    through, calibration records input amax, and QAT training runs."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.models.quantization import E2M1_VALUES, QATConfig, QuantSpec, fake_quant
+    from rl_b200.ops.quant import dequant_fp8_block, quant_fp8_block_ref
+    from tests.dist_cases import make_batch
+
+    torch.manual_seed(0)
+    w = torch.randn(200, 300)
+    q, s = quant_fp8_block_ref(w, 128)
+    assert torch.allclose(fake_quant(w, QuantSpec("fp8", (128, 128))), dequant_fp8_block(q, s), atol=1e-6)
+    x = torch.randn(7, 64)
+    f4 = fake_quant(x, QuantSpec("nvfp4", (1, 16)))
+    # every 16-block is (e4m3 block scale) x (e2m1 values)
+    blk = f4.view(7, 4, 16)
+    sc = blk.abs().amax(-1, keepdim=True) / 6.0
+    vals = (blk / sc.clamp_min(1e-30)).abs()
+    assert torch.isin(vals.round(decimals=4), E2M1_VALUES.round(decimals=4)).float().mean() > 0.99
+    assert ((f4 - x).norm() / x.norm()).item() < 0.2
+    cfg = ModelConfig(name="tiny-128", vocab_size=512, hidden_size=128, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=32, ffn_hidden_size=256, rope_theta=10000.0, max_position_embeddings=256)
+    assert QATConfig.from_cfg("NVFP4_W4A16_CFG").input is None
+    for preset in ("FP8_BLOCK_CFG", "FP8_DEFAULT_CFG", "NVFP4_DEFAULT_CFG"):
+        pc = {"max_total_sequence_length": 48, "precision": "float32", "train_global_batch_size": 8,
+              "optimizer": {"kwargs": {"lr": 3e-3, "weight_decay": 0.0}}, "quant_cfg": preset,
+              "generation": {"temperature": 1.0, "max_new_tokens": 4},
+              "sequence_packing": {"train_mb_tokens": 96, "logprob_mb_tokens": 96}}
+        wk = PolicyWorker(pc, model_cfg=cfg, seed=1)
+        b = make_batch(B=8, S=24, vocab=512)
+        stats = wk.calibrate_quantizers(b)
+        assert len(stats) == 4 * cfg.num_layers and all(v > 0 for v in stats.values())
+        assert not any("lm_head" in k or "embed" in k for k in stats)
+        p0 = wk.model.param("model.layers.0.mlp.down_proj.weight").detach().clone()
+        res = wk.train(b, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)
+        assert res["grad_norm"] > 0
+        assert not torch.equal(wk.model.param("model.layers.0.mlp.down_proj.weight"), p0)

@@ -14,7 +14,8 @@ at::Tensor rope_qkv(at::Tensor qkv, at::Tensor positions, at::Tensor cache, int6
                     bool inverse);
 at::Tensor swiglu_fwd(at::Tensor gu);
 at::Tensor swiglu_bwd(at::Tensor dout, at::Tensor gu);
-void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slots);
+void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slots,
+                    double k_scale, double v_scale);
 // logprob.cu
 std::vector<at::Tensor> logprob_partials(at::Tensor logits, at::Tensor targets, double temperature);
 void logprob_bwd(at::Tensor dlp, at::Tensor logits, at::Tensor targets, at::Tensor lse, double temperature,
@@ -93,7 +94,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("rope_qkv", &rope_qkv);
   m.def("swiglu_fwd", &swiglu_fwd);
   m.def("swiglu_bwd", &swiglu_bwd);
-  m.def("write_kv_cache", &write_kv_cache);
+  m.def("write_kv_cache", &write_kv_cache, py::arg("k"), py::arg("v"), py::arg("k_cache"), py::arg("v_cache"),
+        py::arg("slots"), py::arg("k_scale") = 1.0, py::arg("v_scale") = 1.0);
   m.def("logprob_partials", &logprob_partials);
   m.def("logprob_bwd", &logprob_bwd);
   m.def("sample", &sample);

@@ -212,7 +212,9 @@ at::Tensor swiglu_bwd(at::Tensor dout, at::Tensor gu) {
   return dgu;
 }
 
-void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slots) {
+// fp8 caches store k / k_scale and v / v_scale (per-tensor scales of the layer).
+void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v_cache, at::Tensor slots,
+                    double k_scale, double v_scale) {
   RLB_CHECK(k.dim() == 3 && v.dim() == 3, "write_kv_cache: k/v must be [T, nkv, hd]");
   RLB_CHECK(k.stride(2) == 1 && k.stride(1) == k.size(2) && v.stride(2) == 1 && v.stride(1) == v.size(2),
             "write_kv_cache: heads must be contiguous within a token");
@@ -228,7 +230,7 @@ void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v
       write_kv_kernel<scalar_t, __nv_fp8_e4m3><<<ew_grid(total), 256, 0, stream()>>>(
           (const scalar_t*)k.data_ptr(), (const scalar_t*)v.data_ptr(), k.stride(0), v.stride(0),
           (__nv_fp8_e4m3*)k_cache.data_ptr(), (__nv_fp8_e4m3*)v_cache.data_ptr(), (long long*)sl.data_ptr<int64_t>(), T_,
-          row, 1.f, 1.f);
+          row, (float)(1.0 / k_scale), (float)(1.0 / v_scale));
     } else {
       RLB_CHECK(k_cache.scalar_type() == k.scalar_type(), "write_kv_cache: cache dtype mismatch");
       write_kv_kernel<scalar_t, scalar_t><<<ew_grid(total), 256, 0, stream()>>>(

@@ -112,6 +112,8 @@ class RolloutEngine:
         # (-1 where no route exists: padding and the last sampled token)
         self.record_routes = False
         self._route_steps: Optional[list] = None
+        # fp8 KV cache: per-layer (k, v) scales from calibrate_qkv_fp8_scales
+        self.kv_scales: Optional[tuple] = None
 
     # ------------------------------------------------------------ lifecycle
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
@@ -122,6 +124,8 @@ class RolloutEngine:
             arena = self.kv_arena() if self.kv_arena is not None else None
             self.kv = KVCache(self.model.cfg.num_layers, blocks, self.block_size, self.model.nkv, self.model.hd,
                               self.kv_dtype, self.device, arena=arena)
+            if self.kv_scales is not None:
+                self.kv.k_scales, self.kv.v_scales = list(self.kv_scales[0]), list(self.kv_scales[1])
             self.arena_dirty = self.arena_dirty or (arena is not None)
             self._kv_capacity_seqs = n
             if self.draft is not None:
@@ -133,6 +137,14 @@ class RolloutEngine:
                 self._drop_graphs()  # captured graphs point at the old cache
             self._kv_sig = sig
         return True
+
+    def set_kv_scales(self, k_scales: list, v_scales: list) -> None:
+        """Per-layer fp8 KV-cache scales (cache value = k / k_scale); captured
+        decode graphs bake the scales in, so they are dropped."""
+        self.kv_scales = (list(k_scales), list(v_scales))
+        if self.kv is not None:
+            self.kv.k_scales, self.kv.v_scales = list(k_scales), list(v_scales)
+        self._drop_graphs()
 
     def _drop_graphs(self) -> None:
         for st in self._states.values():

@@ -201,8 +201,10 @@ class PolicyWorker:
             self.gen_model = TransformerLM(self.model_cfg, single_process_state(self.device), device=self.device,
                                            dtype=self.dtype, skip_init=True)
         self.weight_sync = self._make_weight_sync(resharded)
+        kv_dt = str(vcfg.get("kv_cache_dtype", gen_cfg.get("kv_cache_dtype", "auto"))).lower()
         self.engine = RolloutEngine(
             self.gen_model, gen_cfg, max_num_seqs=int(gen_cfg.get("max_num_seqs", 256)),
+            kv_dtype=torch.float8_e4m3fn if kv_dt in ("fp8", "fp8_e4m3") else None,
             max_model_len=self.max_seq_len, block_size=int(mgc.get("block_size_tokens", 256)),
             use_cuda_graphs=bool(gen_cfg.get("use_cuda_graphs", True)),
             seed=seed * 7 + self.ps.dp_rank * 100003,
@@ -882,6 +884,34 @@ class PolicyWorker:
         finally:
             q.calibrating = False
         return q.quantizer_stats()
+
+    @torch.no_grad()
+    def calibrate_qkv_fp8_scales(self, data: BatchedDataDict, margin: float = 1.0) -> dict:
+        """Per-layer fp8 KV-cache scales (``amax * margin / 448`` of the rotated
+        keys and the values over forwards of ``data``), installed in the rollout
+        engine.  Reference: ``calibrate_qkv_fp8_scales``
+        (``nemo_rl/models/policy/interfaces.py:145``)."""
+        m = self.gen_model
+        m.kv_amax = {}
+        try:
+            lengths = self._lengths(data)
+            rows = [r for r in range(len(lengths)) if lengths[r] > 0]
+            for mb in self._plan(lengths, rows, self.logprob_mb_tokens):
+                mb = [-1 - mb[0]] if mb[0] < 0 else mb
+                flat, pos, cu, max_len, _ = pack_rows(data["input_ids"], lengths, mb, pad_to_multiple=1)
+                m(_to_device(flat, self.device), _to_device(pos, self.device), _to_device(cu, self.device), max_len)
+            amax = m.kv_amax
+        finally:
+            m.kv_amax = None
+        L = m.cfg.num_layers
+        ks = [max(float(amax[i][0]) * margin / 448.0, 1e-8) if i in amax else 1.0 for i in range(L)]
+        vs = [max(float(amax[i][1]) * margin / 448.0, 1e-8) if i in amax else 1.0 for i in range(L)]
+        if self.ps.tp_size > 1:  # one scale per layer across the TP shards
+            t = torch.tensor(ks + vs, dtype=torch.float64, device=self.device if self.ps.backend == "nccl" else "cpu")
+            dist.all_reduce(t, op=dist.ReduceOp.MAX, group=self.ps.tp_group)
+            ks, vs = t[:L].tolist(), t[L:].tolist()
+        self.engine.set_kv_scales(ks, vs)
+        return {f"layer_{i}": {"k_scale": ks[i], "v_scale": vs[i]} for i in range(L)}
 
     def get_quantizer_stats(self) -> dict:
         return self.model.qat.quantizer_stats() if self.model.qat is not None else {}

@@ -93,11 +93,15 @@ class KVCache:
             self.storage = arena.view(torch.uint8)[: n * elt].view(dtype).view(shape)
         else:
             self.storage = torch.empty(shape, dtype=dtype, device=device)
-        self.k_scale = 1.0
-        self.v_scale = 1.0
+        # fp8 caches: per-layer per-tensor scales (cache value = k / k_scale)
+        self.k_scales = [1.0] * num_layers
+        self.v_scales = [1.0] * num_layers
 
     def layer(self, i: int):
         return self.storage[i, 0], self.storage[i, 1]
+
+    def scales(self, i: int) -> tuple:
+        return self.k_scales[i], self.v_scales[i]
 
     def nbytes(self) -> int:
         return self.storage.numel() * self.storage.element_size()
@@ -225,6 +229,7 @@ class TransformerLM(nn.Module):
         # weights are cached per parameter until weight_version changes
         self.fp8_train: Optional[dict] = None
         self.qat = None  # rl_b200.models.quantization.QAT (fake-quantised training forward)
+        self.kv_amax: Optional[dict] = None  # layer -> (k amax, v amax) while calibrating
         self.weight_version = 0
         self._fp8_cache: dict = {}
 
@@ -381,7 +386,14 @@ class TransformerLM(nn.Module):
             k = rms_norm(k.reshape(T * self.nkv, self.hd), self._params[p + "self_attn.k_norm.weight"],
                          self.cfg.rms_eps).view(T, -1)
             qkv = torch.cat([q, k, v], -1)
-        return apply_rope_qkv(qkv, positions, self.rope_cache, self.nq, self.nkv, self.hd)
+        out = apply_rope_qkv(qkv, positions, self.rope_cache, self.nq, self.nkv, self.hd)
+        if self.kv_amax is not None:
+            # fp8 KV-cache calibration: amax of the (rotated) keys and the values
+            _, k, v = self._split_heads(out)
+            ka, va = k.detach().abs().amax().float(), v.detach().abs().amax().float()
+            pk, pv = self.kv_amax.get(i, (ka, va))
+            self.kv_amax[i] = (torch.maximum(pk, ka), torch.maximum(pv, va))
+        return out
 
     def _split_heads(self, qkv: torch.Tensor):
         T = qkv.shape[0]
@@ -737,7 +749,7 @@ class TransformerLM(nn.Module):
             qkv = self._qkv(i, h, positions)
             q, k, v = self._split_heads(qkv)
             kc, vc = kv.layer(i)
-            write_kv_cache(k, v, kc, vc, slot_mapping)
+            write_kv_cache(k, v, kc, vc, slot_mapping, *kv.scales(i))
             o, _ = flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen, causal=True)
             a = self._tp_sum(self._lin_infer(o.reshape(o.shape[0], -1), p + "self_attn.o_proj.weight"))
             h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
@@ -790,9 +802,10 @@ class TransformerLM(nn.Module):
             qkv = self._qkv(i, h, positions)
             q, k, v = self._split_heads(qkv)
             kc, vc = kv.layer(i)
-            write_kv_cache(k, v, kc, vc, slot_mapping)
+            ks, vs = kv.scales(i)
+            write_kv_cache(k, v, kc, vc, slot_mapping, ks, vs)
             o = paged_decode_attention(q, kc, vc, block_tables, seq_lens, max_seq_len=max_seq_len,
-                                       k_scale=kv.k_scale, v_scale=kv.v_scale)
+                                       k_scale=ks, v_scale=vs)
             a = self._tp_sum(self._lin_infer(o.reshape(o.shape[0], -1), p + "self_attn.o_proj.weight"))
             h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
             m = self._mlp_infer(i, h2)
@@ -812,9 +825,10 @@ class TransformerLM(nn.Module):
             qkv = self._qkv(i, h, positions)
             q, k, v = self._split_heads(qkv)
             kc, vc = kv.layer(i)
-            write_kv_cache(k, v, kc, vc, slot_mapping)
+            ks, vs = kv.scales(i)
+            write_kv_cache(k, v, kc, vc, slot_mapping, ks, vs)
             o = paged_decode_attention(q, kc, vc, block_tables, seq_lens, max_seq_len=max_seq_len,
-                                       k_scale=kv.k_scale, v_scale=kv.v_scale)
+                                       k_scale=ks, v_scale=vs)
             a = self._lin_infer(o.reshape(o.shape[0], -1), p + "self_attn.o_proj.weight")
             h2 = ar(a, s, self._params[p + "post_attention_layernorm.weight"], eps)
             gu = self._lin_infer(h2, p + "mlp.gate_up_proj.weight")

@@ -119,20 +119,23 @@ def flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[
     return flash_attn_varlen_ref(q, k, v, cu_seqlens, scale, causal)
 
 
-def write_kv_cache_ref(k, v, k_cache, v_cache, slot_mapping):
+def write_kv_cache_ref(k, v, k_cache, v_cache, slot_mapping, k_scale: float = 1.0, v_scale: float = 1.0):
     nb, bs = k_cache.shape[:2]
     kc = k_cache.view(nb * bs, *k_cache.shape[2:])
     vc = v_cache.view(nb * bs, *v_cache.shape[2:])
+    if kc.dtype == torch.float8_e4m3fn:
+        k, v = (k.float() / k_scale).clamp(-448, 448), (v.float() / v_scale).clamp(-448, 448)
     kc[slot_mapping.long()] = k.to(kc.dtype)
     vc[slot_mapping.long()] = v.to(vc.dtype)
 
 
-def write_kv_cache(k, v, k_cache, v_cache, slot_mapping):
-    """Scatter ``k, v [T, nkv, hd]`` into the paged cache at ``slot_mapping``."""
+def write_kv_cache(k, v, k_cache, v_cache, slot_mapping, k_scale: float = 1.0, v_scale: float = 1.0):
+    """Scatter ``k, v [T, nkv, hd]`` into the paged cache at ``slot_mapping``
+    (an fp8 cache stores ``k / k_scale`` and ``v / v_scale``)."""
     if use_native(k):
-        ext().write_kv_cache(k, v, k_cache, v_cache, slot_mapping)
+        ext().write_kv_cache(k, v, k_cache, v_cache, slot_mapping, float(k_scale), float(v_scale))
     else:
-        write_kv_cache_ref(k, v, k_cache, v_cache, slot_mapping)
+        write_kv_cache_ref(k, v, k_cache, v_cache, slot_mapping, k_scale, v_scale)
 
 
 def paged_decode_attention_ref(q, k_cache, v_cache, block_tables, seq_lens, scale: Optional[float] = None):

@@ -677,3 +677,29 @@ def test_quantization_aware_training():
         res = wk.train(b, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)
         assert res["grad_norm"] > 0
         assert not torch.equal(wk.model.param("model.layers.0.mlp.down_proj.weight"), p0)
+
+
+def test_fp8_kv_cache_calibration():
+    """fp8 KV cache (vllm_cfg.kv_cache_dtype: fp8) with per-layer scales from
+    calibrate_qkv_fp8_scales: the cache stores k / k_scale in e4m3 and the
+    rollout log-probs stay close to the trainer's."""
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+
+    w = _tiny_policy(seed=3, generation={"temperature": 1.0, "max_new_tokens": 8,
+                                         "vllm_cfg": {"kv_cache_dtype": "fp8"},
+                                         "mcore_generation_config": {"block_size_tokens": 8}})
+    assert w.engine.kv_dtype == torch.float8_e4m3fn
+    g = torch.Generator().manual_seed(4)
+    data = BatchedDataDict({"input_ids": torch.randint(0, 512, (4, 12), generator=g),
+                            "input_lengths": torch.tensor([12, 9, 6, 10])})
+    sc = w.calibrate_qkv_fp8_scales(data)
+    assert len(sc) == 2 and all(v["k_scale"] > 0 and v["v_scale"] > 0 for v in sc.values())
+    out = w.generate(data)
+    assert w.engine.kv.k_scales == [sc[f"layer_{i}"]["k_scale"] for i in range(2)]
+    seqs = BatchedDataDict({"input_ids": out["output_ids"], "input_lengths": out["unpadded_sequence_lengths"]})
+    lp = w.get_logprobs(seqs)["logprobs"]
+    mask = torch.zeros_like(lp, dtype=torch.bool)
+    for b in range(4):
+        L, n = int(data["input_lengths"][b]), int(out["generation_lengths"][b])
+        mask[b, L:L + n] = True
+    assert (lp - out["logprobs"])[mask].abs().mean().item() < 0.1

@@ -703,3 +703,27 @@ def test_fp8_kv_cache_calibration():
         L, n = int(data["input_lengths"][b]), int(out["generation_lengths"][b])
         mask[b, L:L + n] = True
     assert (lp - out["logprobs"])[mask].abs().mean().item() < 0.1
+
+
+def test_policy_facade():
+    """The reference-style Policy facade forwards to the local worker."""
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+    from rl_b200.models.policy.lm_policy import Policy
+
+    w = _tiny_policy(seed=4)
+    pol = Policy(w)
+    g = torch.Generator().manual_seed(1)
+    data = BatchedDataDict({"input_ids": torch.randint(0, 512, (3, 10), generator=g),
+                            "input_lengths": torch.tensor([10, 6, 8])})
+    lp = pol.get_logprobs(data)["logprobs"]
+    tk = pol.get_topk_logits(data, k=4)
+    assert tk["topk_logits"].shape == (3, 10, 4)
+    # the target token's logprob equals its logit minus logsumexp; top-1 >= every other
+    assert (tk["topk_logits"][:, :, 0] >= tk["topk_logits"][:, :, 1]).all()
+    assert pol.data_parallel_size == 1 and pol.prepare_for_generation()
+    out = pol.generate(data, greedy=True)
+    assert out["output_ids"].shape[0] == 3
+    info = pol.prepare_refit_info()
+    assert "model.embed_tokens.weight" in info
+    assert torch.equal(pol.run_all_workers_single_data("get_logprobs", data)["logprobs"], lp)
+    assert pol.shutdown()

@@ -161,6 +161,10 @@ def _register_defaults():
     register_environment("hash", lambda c, **k: HashRewardEnvironment(c))
     register_environment("even", lambda c, **k: EvenTokenEnvironment(c))
     register_environment("code", lambda c, **k: CodeEnvironment(c, **k))
+    from rl_b200.environments.http_gym import HttpGymEnvironment
+
+    register_environment("http_gym", lambda c, **k: HttpGymEnvironment(c))
+    register_environment("nemo_gym", lambda c, **k: HttpGymEnvironment(c))
     register_environment("sliding_puzzle", lambda c, **k: SlidingPuzzleEnvironment(c, **k))
     register_environment("reward_model", lambda c, **k: RewardModelEnvironment(c, **k))
 

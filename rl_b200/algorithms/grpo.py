@@ -211,6 +211,9 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     train_gbs = int(master_config["policy"].get("train_global_batch_size", cfg["num_prompts_per_step"] * G))
     local_gbs = max(1, train_gbs // max(1, ps.dp_size))
     kl_on = float(loss_cfg.get("reference_policy_kl_penalty", 0.0) or 0.0) != 0.0
+    from rl_b200.data_plane import create_data_plane
+
+    data_plane = create_data_plane(master_config.get("data_plane"))
     state = save_state or GRPOSaveState.default()
     max_steps = max_steps if max_steps is not None else int(cfg["max_num_steps"])
     set_seed(int(cfg["seed"]) + ps.dp_rank)
@@ -271,6 +274,14 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 # ---- advantages ----
                 with timer.time("data_processing"):
                     train_data, adv_stats = build_train_data(rollout, estimator, cfg, loss_cfg, rollout["group_id"])
+                    if data_plane is not None:
+                        # the trainer consumes the step's samples from the data plane (the
+                        # reference's TransferQueue flow); producer and consumer may be
+                        # different processes sharing the plane
+                        key = f"step{step}/dp{ps.dp_rank}"
+                        data_plane.put("train", key, train_data)
+                        train_data = data_plane.get("train", key)
+                        data_plane.delete("train", key)
                 # ---- logprobs ----
                 # one optimizer step per rollout batch: the weights before the step are
                 # the ones the step's own forward runs with, so the separate "previous

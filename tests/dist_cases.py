@@ -130,3 +130,19 @@ def case_pp_rollout_ckpt(rank: int, pp: int, tp: int, ckpt_dir: str):
     return {"sync_err": max(errs), "out_ids": out["output_ids"], "gen_lens": out["generation_lengths"],
             "ckpt_err": ck_err, "n_stage_params": len(w.model.specs), "n_gen_params": len(w.gen_model.specs),
             "gen_flat": w.gen_model.flat_param.detach().clone()}
+
+
+def case_data_plane(rank: int, port: int):
+    """Two processes share a Store-backed data plane: each consumes what the
+    other produced."""
+    from rl_b200.data_plane import StoreDataPlane
+
+    dp = StoreDataPlane(host="127.0.0.1", port=port, is_master=rank == 0, world_size=2, compress=rank == 1)
+    b = make_batch(B=4, S=12, seed=rank)
+    b["names"] = [f"r{rank}-{i}" for i in range(4)]
+    dp.put("train", f"from{rank}", b)
+    got = dp.get("train", f"from{1 - rank}", timeout=60)
+    ref = make_batch(B=4, S=12, seed=1 - rank)
+    ok = all(torch.equal(got[k], ref[k]) for k in ref.keys()) and got["names"][0] == f"r{1 - rank}-0"
+    keys = dp.keys("train")
+    return {"ok": ok, "keys": keys, "stats": dp.metrics()}

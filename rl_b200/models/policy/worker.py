@@ -921,7 +921,10 @@ class PolicyWorker:
         """Roll out ``data``.  With rollout TP 1 under training TP ``t`` the TP peers
         (which hold identical data) each generate every t-th row with their full
         rollout copy and exchange the results, so every peer returns the whole
-        batch (identical, as the trainer requires)."""
+        batch (identical, as the trainer requires).  An fp8 KV cache is
+        calibrated on the first batch it serves."""
+        if self.engine.kv_dtype == torch.float8_e4m3fn and self.engine.kv_scales is None:
+            self.calibrate_qkv_fp8_scales(data)
         if self.pp > 1:
             # every stage holds the whole rollout model and the same rows: split them
             t, r, grp = self.pp, self.ps.pp_rank, self.ps.pp_group

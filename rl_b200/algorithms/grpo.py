@@ -146,6 +146,7 @@ def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, l
         "token_mask": token_mask,
         "sample_mask": sample_mask,
     })
+    data["rewards"] = rewards  # per-sample rewards (VAPO's positive-example NLL)
     if "routed_experts" in flat:  # router replay (R3)
         data["routed_experts"] = flat["routed_experts"]
     stats = {"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std()) if len(rewards) > 1 else 0.0,

@@ -171,12 +171,17 @@ class ClippedPGLossFn:
         # ---------------- reference-policy KL ----------------
         if self.kl_coef != 0.0:
             ref_lp = torch.where(mb, data["reference_policy_logprobs"][:, 1:].to(curr.dtype), zero)
+            # with train-time top-k / top-p filtering the actor terms use the filtered
+            # log-probs but the KL (and its weights) the unfiltered ones, consistent
+            # with the unfiltered reference log-probs
+            unf = data.get("curr_logprobs_unfiltered") if hasattr(data, "get") else None
+            curr_kl = torch.where(mb, unf.to(curr.dtype), zero) if unf is not None else curr_m
             if self.on_policy_kl:
-                w = torch.exp(curr_m - gen_m)
+                w = torch.exp(curr_kl - gen_m)
             else:
-                w = torch.exp(curr_m - curr_m.detach())
+                w = torch.exp(curr_kl - curr_kl.detach())
             w = _finite(w)
-            kl_tok = self.kl_coef * calculate_kl(curr_m, ref_lp, self.kl_type, self.kl_in_clamp,
+            kl_tok = self.kl_coef * calculate_kl(curr_kl, ref_lp, self.kl_type, self.kl_in_clamp,
                                                  self.kl_out_clamp, importance_sampling_weights=w)
             kl = self._reduce(kl_tok, token_mask, sample_mask, mask, global_valid_toks, global_valid_seqs)
         else:
@@ -220,9 +225,12 @@ class ClippedPGLossFn:
         actor = self._reduce(per_tok, token_mask, sample_mask, mask, global_valid_toks, global_valid_seqs)
 
         loss = actor + kl
-        if self.nll_weight > 0.0:
-            pos = (data["advantages"][:, 1:] > 0).to(curr.dtype) * mask
-            nll = masked_mean(-curr_m, pos, global_normalization_factor=global_valid_toks)
+        if self.nll_weight > 0.0 and "rewards" in data:
+            # VAPO: NLL on the tokens of correct samples (reward > 0), averaged over them
+            correct = mask * (data["rewards"].to(curr.dtype) > 0).to(curr.dtype).unsqueeze(-1)
+            n_ok = correct.sum()
+            nll = torch.where(n_ok > 0, masked_mean(-curr_m, correct, global_normalization_factor=n_ok.clamp_min(1)),
+                              curr.new_zeros(()))
             loss = loss + self.nll_weight * nll
             metrics["positive_nll"] = _m(nll.detach())
 

@@ -408,6 +408,7 @@ class PolicyWorker:
             return hidden, None, cu
         h = self.model.lm_input(hidden)
         lp, ent = self._logprobs_from_hidden(h, targets, temperature)
+        self._last_cu = cu
         return lp, ent, cu
 
     def _set_replay(self, rows: list, lengths: list, T: int) -> None:
@@ -470,9 +471,15 @@ class PolicyWorker:
         dist.broadcast_object_list(obj, src=self.ps.pp_ranks[-1], group=self.ps.pp_group)
         return obj[0]
 
+    def _filtering(self) -> bool:
+        gen = self.cfg.get("generation", {}) or {}
+        return bool(gen.get("top_k")) or float(gen.get("top_p", 1.0) or 1.0) < 1.0
+
     def _logprobs_from_hidden(self, h, targets, temperature):
         """Fused LM-head + log-prob (full vocabulary), or - when the rollout samples
-        with top-k / top-p - the same filter applied at train time."""
+        with top-k / top-p - the same filter applied at train time (and, when the
+        loss has a KL term, the unfiltered log-probs beside them: the KL compares
+        with the unfiltered reference)."""
         grp = self.ps.tp_group if self.ps.tp_size > 1 else None
         gen = self.cfg.get("generation", {}) or {}
         top_k, top_p = gen.get("top_k"), float(gen.get("top_p", 1.0) or 1.0)
@@ -480,6 +487,9 @@ class PolicyWorker:
             from rl_b200.ops.fused_linear_logprob import filtered_linear_logprobs
 
             w = self.model.lm_head_weight()
+            if getattr(self, "_need_unfiltered", False):
+                self._lp_unfiltered = linear_logprobs(h, w, targets, self.model.vocab_start, temperature, grp,
+                                                      self.logprob_chunk)[0]
             return filtered_linear_logprobs(h, w, targets, self.model.vocab_start, temperature, top_k, top_p,
                                             grp, chunk=max(1, min(self.logprob_chunk, 1024)))
         return linear_logprobs(h, self.model.lm_head_weight(), targets, self.model.vocab_start, temperature,
@@ -814,11 +824,20 @@ class PolicyWorker:
         if dummy:
             mb_rows = [-1 - mb_rows[0]]
         width = max(st.lengths[r] for r in mb_rows)
-        curr = self._loss_input(st.loss_fn, st.ids, st.lengths, mb_rows, width, st.temperature)
+        self._need_unfiltered = float(getattr(st.loss_fn, "kl_coef", 0.0) or 0.0) != 0.0 and self._filtering() \
+            and self.ps.cp_size == 1
+        self._lp_unfiltered = None
+        try:
+            curr = self._loss_input(st.loss_fn, st.ids, st.lengths, mb_rows, width, st.temperature)
+        finally:
+            self._need_unfiltered = False
         ridx = torch.tensor(mb_rows, dtype=torch.long).pin_memory().to(self.device, non_blocking=True) \
             if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
         mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
                               for k, v in st.dev_data.items()})
+        if self._lp_unfiltered is not None:
+            mb["curr_logprobs_unfiltered"] = self._to_padded(self._lp_unfiltered, self._last_cu, len(mb_rows), width)
+            self._lp_unfiltered = None
         if getattr(self, "_prev_from_current", False) and "prev_logprobs" in mb:
             prev = mb["prev_logprobs"].clone()
             prev[:, 1:width] = curr.detach().to(prev.dtype)

@@ -727,3 +727,32 @@ def test_policy_facade():
     assert "model.embed_tokens.weight" in info
     assert torch.equal(pol.run_all_workers_single_data("get_logprobs", data)["logprobs"], lp)
     assert pol.shutdown()
+
+
+def test_kl_uses_unfiltered_logprobs_under_top_k():
+    """With train-time top-k filtering and a KL penalty, the loss receives the
+    unfiltered current log-probs for its KL term (they differ from the
+    filtered ones)."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from tests.dist_cases import make_batch
+
+    w = _tiny_policy(seed=6, generation={"temperature": 1.0, "top_k": 8, "max_new_tokens": 4})
+    seen = {}
+    base = ClippedPGLossFn({"reference_policy_kl_penalty": 0.1})
+
+    def spy(curr, mb, gs, gt):
+        seen["unf"] = mb.get("curr_logprobs_unfiltered")
+        seen["curr"] = curr.detach()
+        return base(curr, mb, gs, gt)
+
+    spy.kl_coef = base.kl_coef
+    b = make_batch(B=4, S=16, vocab=512)
+    b["reference_policy_logprobs"] = b["prev_logprobs"].clone()
+    w.train(b, spy, gbs=4)
+    assert seen["unf"] is not None
+    m = b["token_mask"][:, 1:].bool()[:, :seen["curr"].shape[1]]
+    c, u = seen["curr"][m], seen["unf"][m]
+    assert torch.isfinite(u).all() and not torch.allclose(c, u)
+    # kept tokens: the filter renormalises over 8 tokens, so their log-probs are higher
+    kept = torch.isfinite(c) & (c > -1e8)
+    assert (c[kept] >= u[kept] - 1e-5).all()

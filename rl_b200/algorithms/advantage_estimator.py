@@ -214,23 +214,47 @@ class GeneralizedAdvantageEstimator:
 
 
 class OPDAdvantageEstimator:
-    """On-policy distillation: A_t = log(alpha*p_teacher + (1-alpha)*p_student) - log p_student."""
+    """On-policy distillation: ``A_t = log(alpha p_teacher + (1 - alpha) p_student) - log p_student``
+    (plain OPD ``log p_teacher - log p_student`` at ``alpha = 1``; the trust-region
+    mixture bounds the advantage below by ``log(1 - alpha)``), optionally centred
+    by its mean over the valid tokens.  Reference: ``OPDAdvantageEstimator``
+    (``nemo_rl/algorithms/advantage_estimator.py``)."""
 
     def __init__(self, cfg: dict, loss_cfg: Optional[dict] = None):
         self.alpha = float(cfg.get("proximal_teacher_alpha", 1.0))
+        if not 0.0 < self.alpha <= 1.0:
+            raise ValueError(f"proximal_teacher_alpha must be in (0, 1], got {self.alpha}")
         self.subtract_global_baseline = bool(cfg.get("subtract_global_baseline", False))
+        self.last_metrics: dict = {}
 
     def compute_advantage(self, prompt_ids, rewards, mask, logprobs_policy=None, logprobs_teacher=None, **kwargs):
+        # the reference's keyword names are accepted as well
+        logprobs_teacher = kwargs.get("teacher_logprobs", logprobs_teacher)
+        logprobs_policy = kwargs.get("prev_logprobs", logprobs_policy)
         if logprobs_policy is None or logprobs_teacher is None:
             raise ValueError("OPD needs student and teacher log-probabilities")
+        m = mask.to(logprobs_policy.dtype)
+        valid = m.bool()
+        zero = torch.zeros_like(logprobs_policy)
+        t = torch.where(valid, logprobs_teacher, zero)
+        p = torch.where(valid, logprobs_policy, zero)
+        gap = t - p
         if self.alpha >= 1.0:
-            target = logprobs_teacher
+            adv = gap
         else:
-            target = torch.logaddexp(logprobs_teacher + math.log(self.alpha),
-                                     logprobs_policy + math.log1p(-self.alpha))
-        adv = (target - logprobs_policy) * mask
-        if self.subtract_global_baseline:
-            adv = (adv - masked_mean(adv, mask)) * mask
+            adv = torch.logaddexp(t + math.log(self.alpha), p + math.log1p(-self.alpha)) - p
+        adv = adv * m
+        n = m.sum()
+        if self.subtract_global_baseline and n > 0:
+            adv = (adv - (adv * m).sum() / n) * m
+        denom = n.clamp_min(1)
+        mean = (adv * m).sum() / denom
+        std = torch.sqrt((((adv - mean) * m) ** 2).sum() / denom)
+        self.last_metrics = {
+            "on_policy_distillation/adv_mean": float(mean),
+            "on_policy_distillation/adv_std": float(std),
+            "on_policy_distillation/teacher_student_logprob_gap_mean": float((gap * m).sum() / denom),
+        }
         return adv
 
 

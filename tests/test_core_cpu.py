@@ -756,3 +756,48 @@ def test_kl_uses_unfiltered_logprobs_under_top_k():
     # kept tokens: the filter renormalises over 8 tokens, so their log-probs are higher
     kept = torch.isfinite(c) & (c > -1e8)
     assert (c[kept] >= u[kept] - 1e-5).all()
+
+
+def test_opd_trust_region_advantages():
+    """On-policy distillation advantages: plain OPD at alpha = 1, trust-region
+    mixture below it (bounded by log(1 - alpha)), global baseline over valid
+    tokens only, metrics on the raw teacher-student gap; the reference's keyword
+    names are accepted."""
+    import pytest
+
+    from rl_b200.algorithms.advantage_estimator import OPDAdvantageEstimator
+
+    teacher = torch.tensor([[-0.2, -1.7, -0.5]])
+    student = torch.tensor([[-1.2, -0.8, -0.5]])
+    ones = torch.ones_like(teacher)
+    plain = OPDAdvantageEstimator({"proximal_teacher_alpha": 1.0})
+    torch.testing.assert_close(plain.compute_advantage(None, None, ones, teacher_logprobs=teacher,
+                                                       prev_logprobs=student), teacher - student)
+    a = 0.2
+    tr = OPDAdvantageEstimator({"proximal_teacher_alpha": a})
+    exp = torch.log(a * torch.exp(teacher) + (1 - a) * torch.exp(student)) - student
+    torch.testing.assert_close(tr.compute_advantage(None, None, ones, teacher_logprobs=teacher,
+                                                    prev_logprobs=student), exp)
+    low = tr.compute_advantage(None, None, ones, teacher_logprobs=torch.full((1, 3), -80.0),
+                               prev_logprobs=torch.tensor([[-0.1, -1.0, -3.0]]))
+    torch.testing.assert_close(low, torch.full_like(low, math.log1p(-a)))
+    # global baseline: the masked position neither votes nor receives advantage
+    t2 = torch.tensor([[0.0, -1.0], [-2.0, -0.5]])
+    s2 = torch.tensor([[-1.0, -1.0], [-1.0, -3.0]])
+    m2 = torch.tensor([[1.0, 1.0], [0.0, 1.0]])
+    g = OPDAdvantageEstimator({"subtract_global_baseline": True})
+    torch.testing.assert_close(g.compute_advantage(None, None, m2, teacher_logprobs=t2, prev_logprobs=s2),
+                               (t2 - s2 - 7.0 / 6.0) * m2)
+    m3 = torch.tensor([[1.0, 1.0, 0.0]])
+    est = OPDAdvantageEstimator({"proximal_teacher_alpha": 0.2})
+    adv = est.compute_advantage(None, None, m3, teacher_logprobs=torch.tensor([[0.0, -1.0, 5.0]]),
+                                prev_logprobs=torch.tensor([[-1.0, -1.0, -5.0]]))
+    assert est.last_metrics["on_policy_distillation/teacher_student_logprob_gap_mean"] == pytest.approx(0.5)
+    assert est.last_metrics["on_policy_distillation/adv_mean"] == pytest.approx(adv[:, :2].mean().item())
+    allm = OPDAdvantageEstimator({"proximal_teacher_alpha": 0.2, "subtract_global_baseline": True})
+    z = allm.compute_advantage(None, None, torch.zeros(1, 3), teacher_logprobs=torch.zeros(1, 3),
+                               prev_logprobs=torch.zeros(1, 3))
+    assert torch.isfinite(z).all() and (z == 0).all()
+    for bad in (0.0, -0.1, 1.01):
+        with pytest.raises(ValueError):
+            OPDAdvantageEstimator({"proximal_teacher_alpha": bad})

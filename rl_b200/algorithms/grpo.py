@@ -84,17 +84,38 @@ def refit_policy_generation(policy) -> float:
     return policy.refit()
 
 
-def apply_reward_shaping(rewards: torch.Tensor, gen_lengths: torch.Tensor, cfg: dict) -> torch.Tensor:
-    """DAPO overlong reward shaping: linear penalty over the last
-    ``overlong_buffer_length`` tokens before ``max_response_length``."""
+def apply_reward_shaping(rewards: torch.Tensor, gen_lengths: torch.Tensor, cfg: dict,
+                         truncated: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Reward shaping.
+
+    * DAPO overlong penalty (``overlong_buffer_length``, ``overlong_buffer_penalty``,
+      ``max_response_length``): a response longer than ``max - buffer`` tokens loses
+      ``(length - (max - buffer)) / buffer * penalty`` (linear, not capped);
+    * ``stop_properly_penalty_coef`` in [0, 1]: truncated responses' rewards are
+      multiplied by it.
+
+    ``gen_lengths`` counts every generated assistant token of the sample.
+    Reference: ``apply_reward_shaping`` (``nemo_rl/algorithms/reward_functions.py``)."""
     if not cfg or not cfg.get("enabled", False):
         return rewards
-    buf = float(cfg.get("overlong_buffer_length", 128))
-    pen = float(cfg.get("overlong_buffer_penalty", 1.0))
-    max_len = float(cfg.get("max_response_length", 1e9))
-    expected = max_len - buf
-    over = (gen_lengths.float() - expected).clamp_min(0)
-    return rewards - (over / max(buf, 1.0)).clamp_max(1.0) * pen
+    out = rewards.clone()
+    coef = cfg.get("stop_properly_penalty_coef")
+    if coef is not None:
+        coef = float(coef)
+        assert 0.0 <= coef <= 1.0, f"stop_properly_penalty_coef must be in [0, 1], got {coef}"
+        assert truncated is not None, "truncated field not found (needed by stop_properly_penalty_coef)"
+        out = torch.where(truncated.to(torch.bool), out * coef, out)
+    keys = ("overlong_buffer_length", "overlong_buffer_penalty", "max_response_length")
+    if coef is None or any(cfg.get(k) is not None for k in keys):
+        if any(cfg.get(k) is None for k in keys):
+            raise ValueError("DAPO reward shaping is currently supported with overlong_buffer_length, "
+                             "overlong_buffer_penalty and max_response_length all set")
+        buf = float(cfg["overlong_buffer_length"])
+        pen = float(cfg["overlong_buffer_penalty"])
+        expected = float(cfg["max_response_length"]) - buf
+        exceed = gen_lengths.to(out.dtype) - expected
+        out = out + torch.clamp(-exceed / max(buf, 1e-12) * pen, max=0.0)
+    return out
 
 
 def scale_rewards(rewards: torch.Tensor, cfg: dict) -> torch.Tensor:
@@ -124,7 +145,8 @@ def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, l
     token_mask = flat["token_loss_mask"].float()
     rewards = rollout_batch["total_reward"].float()
     gen_len = token_mask.sum(-1)
-    rewards = apply_reward_shaping(rewards, gen_len, cfg.get("reward_shaping", {}))
+    rewards = apply_reward_shaping(rewards, gen_len, cfg.get("reward_shaping", {}),
+                                   rollout_batch["truncated"] if "truncated" in rollout_batch else None)
     rewards = scale_rewards(rewards, cfg.get("reward_scaling", {}))
     sample_mask = rollout_batch["loss_multiplier"].float().clone()
     if cfg.get("overlong_filtering", False):

@@ -801,3 +801,32 @@ def test_opd_trust_region_advantages():
     for bad in (0.0, -0.1, 1.01):
         with pytest.raises(ValueError):
             OPDAdvantageEstimator({"proximal_teacher_alpha": bad})
+
+
+def test_reward_shaping_and_scaling_semantics():
+    """DAPO overlong penalty (linear, uncapped), stop-properly penalty for
+    truncated samples, required settings, and linear reward scaling with clipping
+    (the reference's documented examples)."""
+    import pytest
+
+    from rl_b200.algorithms.grpo import apply_reward_shaping, scale_rewards
+
+    cfg = {"enabled": True, "overlong_buffer_length": 5, "overlong_buffer_penalty": 0.5, "max_response_length": 25}
+    out = apply_reward_shaping(torch.tensor([1.0, 0.8, 0.6, 0.4]), torch.tensor([10, 22, 25, 30]), cfg)
+    torch.testing.assert_close(out, torch.tensor([1.0, 0.6, 0.1, -0.6]))
+    same = apply_reward_shaping(torch.tensor([1.0, 0.5, 0.8]), torch.tensor([10, 15, 18]),
+                                dict(cfg, overlong_buffer_penalty=1.0))
+    torch.testing.assert_close(same, torch.tensor([1.0, 0.5, 0.8]))
+    sp = apply_reward_shaping(torch.tensor([1.0, 0.8, 0.6, 0.4]), torch.tensor([10, 20, 30, 40]),
+                              {"enabled": True, "stop_properly_penalty_coef": 0.5},
+                              truncated=torch.tensor([False, True, False, True]))
+    torch.testing.assert_close(sp, torch.tensor([1.0, 0.4, 0.6, 0.2]))
+    with pytest.raises(ValueError, match="DAPO reward shaping"):
+        apply_reward_shaping(torch.ones(1), torch.tensor([20]), {"enabled": True, "overlong_buffer_penalty": 0.1,
+                                                                 "max_response_length": 25})
+    with pytest.raises(AssertionError, match="stop_properly_penalty_coef must be in"):
+        apply_reward_shaping(torch.ones(2), torch.tensor([1, 2]), {"enabled": True, "stop_properly_penalty_coef": 1.5},
+                             truncated=torch.tensor([False, True]))
+    sc = scale_rewards(torch.tensor([-2.8, -0.25, 1.5, 0.5, 2.0, 2.5]),
+                       {"enabled": True, "source_min": -2.0, "source_max": 2.0, "target_min": -1.0, "target_max": 1.0})
+    torch.testing.assert_close(sc, torch.tensor([-1.0, -0.125, 0.75, 0.25, 1.0, 1.0]))

@@ -169,6 +169,9 @@ def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, l
         "sample_mask": sample_mask,
     })
     data["rewards"] = rewards  # per-sample rewards (VAPO's positive-example NLL)
+    for k in ("sampler_topk_token_ids", "sampler_topk_logprobs"):  # score centering
+        if k in flat:
+            data[k] = flat[k]
     if "routed_experts" in flat:  # router replay (R3)
         data["routed_experts"] = flat["routed_experts"]
     stats = {"reward_mean": float(rewards.mean()), "reward_std": float(rewards.std()) if len(rewards) > 1 else 0.0,
@@ -235,6 +238,10 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     local_gbs = max(1, train_gbs // max(1, ps.dp_size))
     kl_on = float(loss_cfg.get("reference_policy_kl_penalty", 0.0) or 0.0) != 0.0
     from rl_b200.data_plane import create_data_plane
+
+    if getattr(loss_fn, "score_centering", False) and hasattr(policy, "engine"):
+        # the rollout records the sampler's top-k of every generated token
+        policy.engine.record_sampler_topk = int(loss_cfg.get("score_centering_topk", 8))
 
     data_plane = create_data_plane(master_config.get("data_plane"))
     state = save_state or GRPOSaveState.default()

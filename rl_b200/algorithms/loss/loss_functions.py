@@ -68,6 +68,7 @@ DEFAULT_CLIPPED_PG_CONFIG: dict[str, Any] = {
     "use_cispo": False,
     "disable_ppo_ratio": False,
     "positive_example_nll_weight": 0.0,
+    "score_centering": False,
     "metrics_level": "full",
 }
 
@@ -114,6 +115,14 @@ class ClippedPGLossFn:
         self.use_cispo = bool(c["use_cispo"])
         self.disable_ratio = bool(c["disable_ppo_ratio"])
         self.nll_weight = float(c["positive_example_nll_weight"] or 0.0)
+        # score centering: needs the sampler's top-k log-probs (rollout) and the
+        # trainer's log-probs at those ids ("policy_logprobs_at_sampler_topk")
+        self.score_centering = bool(c["score_centering"])
+        if self.score_centering and (self.seq_ratios or (
+                self.use_is and self.tis_type not in (None, "tis", "icepop"))):
+            raise ValueError("score_centering composes with importance sampling off, untruncated token-level "
+                             "IS, 'tis' or 'icepop'")
+        self._sc_mode = (self.tis_type or "is") if self.use_is else "off"
         self.full_metrics = c["metrics_level"] == "full"
         self.loss_type = LossType.TOKEN_LEVEL if self.token_level else LossType.SEQUENCE_LEVEL
         if self.seq_ratios and self.token_level:
@@ -223,6 +232,22 @@ class ClippedPGLossFn:
         if self.use_is and is_w is not None:
             per_tok = per_tok * is_w
         actor = self._reduce(per_tok, token_mask, sample_mask, mask, global_valid_toks, global_valid_seqs)
+        if self.score_centering:
+            from rl_b200.algorithms.loss.score_centering import score_centering_term
+
+            plk = kwargs.get("policy_logprobs_at_sampler_topk")
+            if plk is None and hasattr(data, "get"):
+                plk = data.get("policy_logprobs_at_sampler_topk")
+            if plk is None:
+                raise ValueError("score_centering needs policy_logprobs_at_sampler_topk")
+            bounds = None
+            if self._sc_mode in ("tis", "icepop"):
+                bounds = (float(self.tis_min or 0.0), float(self.tis_max))
+            term, head = score_centering_term(plk, data["sampler_topk_logprobs"][:, 1:], self._sc_mode, bounds, mask)
+            actor = actor + self._reduce(adv * term, token_mask, sample_mask, mask, global_valid_toks,
+                                         global_valid_seqs)
+            metrics["score_centering_head_mass"] = _m(masked_mean(head, mask,
+                                                                  global_normalization_factor=global_valid_toks))
 
         loss = actor + kl
         if self.nll_weight > 0.0 and "rewards" in data:

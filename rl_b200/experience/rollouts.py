@@ -38,6 +38,12 @@ def generate_responses(policy_generation, batch: BatchedDataDict, rows: list[int
         truncated.append(bool(out["truncated"][i]))
     stats = {"gen_time_s": dt, "gen_tokens": int(out["generation_lengths"].sum()),
              "prompt_tokens": int(lengths.sum())}
+    if "sampler_topk_logprobs" in out:
+        stats["sampler_topk"] = [(out["sampler_topk_token_ids"][i, int(lengths[i]):int(lengths[i]) +
+                                                              int(out["generation_lengths"][i])],
+                                  out["sampler_topk_logprobs"][i, int(lengths[i]):int(lengths[i]) +
+                                                               int(out["generation_lengths"][i])])
+                                 for i in range(len(rows))]
     if "routed_experts" in out:
         # router replay: the routes of every position of every generated sequence
         stats["routed_experts"] = [out["routed_experts"][i, :int(lengths[i]) + int(out["generation_lengths"][i])]
@@ -116,6 +122,9 @@ def run_multi_turn_rollout(policy_generation, input_batch: BatchedDataDict, toke
             })
             if "routed_experts" in st:
                 attach_routes(batch["message_log"][r], st["routed_experts"][i])
+            if "sampler_topk" in st:
+                msg = batch["message_log"][r][-1]
+                msg["sampler_topk_token_ids"], msg["sampler_topk_logprobs"] = st["sampler_topk"][i]
             truncated[r] |= trunc[i]
         rewards, terminated, obs = calculate_rewards(batch, live, task_to_env)
         total_reward[torch.tensor(live)] += rewards

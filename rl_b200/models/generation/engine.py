@@ -114,6 +114,10 @@ class RolloutEngine:
         self._route_steps: Optional[list] = None
         # fp8 KV cache: per-layer (k, v) scales from calibrate_qkv_fp8_scales
         self.kv_scales: Optional[tuple] = None
+        # score centering: record the sampler's top-k (ids, log-probs) of every
+        # generated token's distribution ("sampler_topk_token_ids / _logprobs")
+        self.record_sampler_topk = 0
+        self._topk_steps: Optional[list] = None
 
     # ------------------------------------------------------------ lifecycle
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:
@@ -231,12 +235,14 @@ class RolloutEngine:
         slot = (block_tables[seq_idx, (positions // bs).long()].long() * bs + (positions % bs).long())
         last_idx = (cu[1:] - 1).to(dev).long()
         recording = self.record_routes and self.model.cfg.is_moe
+        topk_rec = int(self.record_sampler_topk or 0)
         if recording:
             self.model.router_record = {}
         h = self.model.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.kv, slot, last_idx)
         prefill_routes = self._take_routes() if recording else None
         self._route_steps = [] if recording else None
         logits = self.model.logits_infer(h)
+        self._topk_steps = [self._sampler_topk(logits, temperature, topk_rec)] if topk_rec else None
         gen = None
         if dev.type == "cpu":
             gen = torch.Generator().manual_seed(self.seed * 7919 + self.calls)
@@ -247,7 +253,7 @@ class RolloutEngine:
             lp0 = torch.zeros_like(lp0)
 
         # ---- decode ----
-        if recording:
+        if recording or topk_rec:
             # routes are read back after every step: eager decode (no graphs, no speculation)
             try:
                 tokens_all, lps_all, glen = self._decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
@@ -273,7 +279,25 @@ class RolloutEngine:
         if recording:
             out["routed_experts"] = self._assemble_routes(prefill_routes, lens_l, glen_c, out["output_ids"].shape[1])
             self._route_steps = None
+        if topk_rec:
+            W = out["output_ids"].shape[1]
+            ids = torch.zeros(B, W, topk_rec, dtype=torch.int64)
+            lps = torch.zeros(B, W, topk_rec, dtype=torch.float32)
+            steps = [(a.cpu(), b.cpu()) for a, b in self._topk_steps]
+            for b in range(B):
+                L, n = lens_l[b], int(glen_c[b])
+                for s_ in range(min(n, len(steps))):  # generated token s_ came from distribution s_
+                    ids[b, L + s_], lps[b, L + s_] = steps[s_][0][b], steps[s_][1][b]
+            out["sampler_topk_token_ids"], out["sampler_topk_logprobs"] = ids, lps
+            self._topk_steps = None
         return out
+
+    @staticmethod
+    def _sampler_topk(logits: torch.Tensor, temperature: float, k: int):
+        """Top-k (ids, log-probs) of the sampling distribution (temperature-scaled)."""
+        lp = torch.log_softmax(logits.float() / (temperature if temperature > 0 else 1.0), -1)
+        v, i = lp.topk(k, -1)
+        return i, v
 
     def _take_routes(self) -> torch.Tensor:
         """The routes recorded by the last forward, ``[T, layers, k]``; resets the record."""
@@ -538,6 +562,8 @@ class RolloutEngine:
             if self._route_steps is not None:
                 self._route_steps.append(self._take_routes())
             logits = self.model.logits_infer(h)
+            if self._topk_steps is not None:
+                self._topk_steps.append(self._sampler_topk(logits, temperature, int(self.record_sampler_topk)))
             nt, nlp = sample_tokens(logits, temperature if temperature > 0 else 1.0,
                                     1 if temperature == 0 else top_k, top_p,
                                     seed=self.seed, offset=self.calls * (1 << 24) + step + 1, generator=gen)

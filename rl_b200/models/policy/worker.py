@@ -409,7 +409,31 @@ class PolicyWorker:
         h = self.model.lm_input(hidden)
         lp, ent = self._logprobs_from_hidden(h, targets, temperature)
         self._last_cu = cu
+        if getattr(self, "_sc_ids", None) is not None:
+            self._sc_plk = self._logprobs_at_sampler_topk(h, lp, targets, rows, lengths, temperature)
         return lp, ent, cu
+
+    def _logprobs_at_sampler_topk(self, h, lp, targets, rows, lengths, temperature):
+        """Trainer log-probs (with grad) at the rollout sampler's top-k ids of
+        every next token, ``[T, k]``: ``logit_v / t - lse`` with the row's
+        log-sum-exp recovered from the target's log-prob (no second vocabulary pass)."""
+        ids_all = self._sc_ids
+        k = ids_all.shape[-1]
+        parts = []
+        for r in rows:
+            L = int(lengths[r])
+            nxt = torch.zeros(L, k, dtype=torch.long, device=h.device)
+            if L > 1:
+                nxt[: L - 1] = ids_all[r, 1:L].to(h.device)
+            parts.append(nxt)
+        ids = torch.cat(parts)
+        T = h.shape[0]
+        if ids.shape[0] < T:
+            ids = torch.cat([ids, ids.new_zeros(T - ids.shape[0], k)])
+        W = self.model.lm_head_weight()
+        logit_t = (h * W[targets]).sum(-1).float() / temperature
+        lse = logit_t - lp.float()
+        return torch.einsum("th,tkh->tk", h, W[ids]).float() / temperature - lse.unsqueeze(-1)
 
     def _set_replay(self, rows: list, lengths: list, T: int) -> None:
         """Routes of the packed micro-batch for the model's routers (R3), or none."""
@@ -827,10 +851,16 @@ class PolicyWorker:
         self._need_unfiltered = float(getattr(st.loss_fn, "kl_coef", 0.0) or 0.0) != 0.0 and self._filtering() \
             and self.ps.cp_size == 1
         self._lp_unfiltered = None
+        self._sc_plk = None
+        if getattr(st.loss_fn, "score_centering", False):
+            if self.ps.tp_size > 1 or self.ps.cp_size > 1 or self._filtering():
+                raise NotImplementedError("score centering needs TP = CP = 1 and no top-k / top-p filtering")
+            self._sc_ids = st.dev_data["sampler_topk_token_ids"]
         try:
             curr = self._loss_input(st.loss_fn, st.ids, st.lengths, mb_rows, width, st.temperature)
         finally:
             self._need_unfiltered = False
+            self._sc_ids = None
         ridx = torch.tensor(mb_rows, dtype=torch.long).pin_memory().to(self.device, non_blocking=True) \
             if self.device.type == "cuda" else torch.tensor(mb_rows, dtype=torch.long)
         mb = BatchedDataDict({k: (v.index_select(0, ridx)[:, :width] if v.dim() >= 2 else v.index_select(0, ridx))
@@ -838,6 +868,9 @@ class PolicyWorker:
         if self._lp_unfiltered is not None:
             mb["curr_logprobs_unfiltered"] = self._to_padded(self._lp_unfiltered, self._last_cu, len(mb_rows), width)
             self._lp_unfiltered = None
+        if self._sc_plk is not None:
+            mb["policy_logprobs_at_sampler_topk"] = self._to_padded(self._sc_plk, self._last_cu, len(mb_rows), width)
+            self._sc_plk = None
         if getattr(self, "_prev_from_current", False) and "prev_logprobs" in mb:
             prev = mb["prev_logprobs"].clone()
             prev[:, 1:width] = curr.detach().to(prev.dtype)

@@ -151,8 +151,11 @@ def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, l
     sample_mask = rollout_batch["loss_multiplier"].float().clone()
     if cfg.get("overlong_filtering", False):
         sample_mask = sample_mask * (~rollout_batch["truncated"]).float()
+    # masked_reward_policy "exclude": rows with zero loss weight do not vote in
+    # the group baselines / normalisation ("include": every row votes)
+    vm = sample_mask if cfg.get("masked_reward_policy", "include") == "exclude" else None
     adv = advantages_fn.compute_advantage(group_ids.view(-1, 1), rewards, token_mask,
-                                          repeated_batch=rollout_batch, valid_mask=None)
+                                          repeated_batch=rollout_batch, valid_mask=vm)
     if isinstance(adv, tuple):
         adv = adv[0]
     adv = adv.clone()
@@ -324,9 +327,11 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                         train_data["prev_logprobs"] = torch.zeros_like(train_data["generation_logprobs"])
                     else:
                         train_data["prev_logprobs"] = policy.get_logprobs(train_data)["logprobs"]
-                    if kl_on:
+                    if kl_on and not cfg.get("skip_reference_policy_logprobs_calculation", False):
                         train_data["reference_policy_logprobs"] = \
                             policy.get_reference_policy_logprobs(train_data)["reference_logprobs"]
+                    elif kl_on:  # skipped: the KL sees the current policy as its own reference
+                        train_data["reference_policy_logprobs"] = train_data["generation_logprobs"].clone()
                 # ---- train ----
                 with timer.time("policy_training"):
                     policy.prepare_for_training()
@@ -380,7 +385,8 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 step_callback(step, {**metrics, **{"timing/" + k: v for k, v in timing.items()}})
             # ---- validation / checkpoint ----
             val_period = int(cfg.get("val_period") or 0)
-            if val_dataloader is not None and val_period > 0 and step % val_period == 0:
+            val_start = int(cfg.get("val_start_at", -1) or -1)
+            if val_dataloader is not None and val_period > 0 and step % val_period == 0 and step >= val_start:
                 vm = validate(policy, val_dataloader, val_task_to_env or task_to_env, master_config, step, tokenizer)
                 state["val_reward"] = vm.get("accuracy")
                 if logger:

@@ -128,11 +128,15 @@ def scale_rewards(rewards: torch.Tensor, cfg: dict) -> torch.Tensor:
     return tmin + (r - smin) * (tmax - tmin) / max(smax - smin, 1e-12)
 
 
-def dynamic_sampling(rewards: torch.Tensor, group_ids: torch.Tensor) -> torch.Tensor:
+def dynamic_sampling(rewards: torch.Tensor, group_ids: torch.Tensor,
+                     valid: Optional[torch.Tensor] = None) -> torch.Tensor:
     """DAPO dynamic sampling: keep only rows of groups whose rewards are not all
-    equal (a constant group has zero advantage everywhere). Returns a row mask."""
-    _, std, trivial = calculate_baseline_and_std_per_prompt(group_ids, rewards, torch.ones_like(rewards),
-                                                            leave_one_out_baseline=False)
+    equal (a constant group has zero advantage everywhere), judged on the whole
+    group (not leave-one-out peers), so a mixed group is kept entire.  ``valid``
+    (masked_reward_policy "exclude") limits the vote to rows with a loss weight.
+    Returns a row mask."""
+    vm = torch.ones_like(rewards) if valid is None else valid.to(rewards.dtype)
+    _, std, trivial = calculate_baseline_and_std_per_prompt(group_ids, rewards, vm, leave_one_out_baseline=False)
     return ~trivial
 
 
@@ -289,7 +293,9 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                         if not cfg.get("use_dynamic_sampling", False):
                             kept_batches.append(rollout)
                             break
-                        keep = dynamic_sampling(rollout["total_reward"], rollout["group_id"])
+                        vote = rollout["loss_multiplier"] if cfg.get("masked_reward_policy",
+                                                                      "include") == "exclude" else None
+                        keep = dynamic_sampling(rollout["total_reward"], rollout["group_id"], vote)
                         rows = torch.nonzero(keep).flatten().tolist()
                         if rows:
                             kept_batches.append(rollout.select_indices(rows))

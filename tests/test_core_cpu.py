@@ -830,3 +830,21 @@ def test_reward_shaping_and_scaling_semantics():
     sc = scale_rewards(torch.tensor([-2.8, -0.25, 1.5, 0.5, 2.0, 2.5]),
                        {"enabled": True, "source_min": -2.0, "source_max": 2.0, "target_min": -1.0, "target_max": 1.0})
     torch.testing.assert_close(sc, torch.tensor([-1.0, -0.125, 0.75, 0.25, 1.0, 1.0]))
+
+
+def test_dynamic_sampling_and_masked_reward_policy():
+    """Dynamic sampling keeps a mixed group entire (judged on the whole group,
+    not leave-one-out peers) and, under masked_reward_policy "exclude", only
+    rows with a loss weight vote; the GRPO baseline ignores invalid rows."""
+    from rl_b200.algorithms.advantage_estimator import GRPOAdvantageEstimator
+    from rl_b200.algorithms.grpo import dynamic_sampling
+
+    keep = dynamic_sampling(torch.tensor([0.0] + [0.95] * 7 + [1.0] * 4), torch.tensor([0] * 8 + [1] * 4))
+    assert keep.tolist() == [True] * 8 + [False] * 4
+    r, g = torch.tensor([1.0, 1.0, 1.0, 0.0]), torch.zeros(4, dtype=torch.long)
+    assert dynamic_sampling(r, g).all()
+    assert not dynamic_sampling(r, g, torch.tensor([1.0, 1.0, 1.0, 0.0])).any()
+    est = GRPOAdvantageEstimator({"use_leave_one_out_baseline": False, "normalize_rewards": False})
+    adv = est.compute_advantage(torch.zeros(4, 3, dtype=torch.long), torch.tensor([1.0, 3.0, 2.0, 0.0]),
+                                torch.ones(4, 5), valid_mask=torch.tensor([1.0, 1.0, 1.0, 0.0]))
+    torch.testing.assert_close(adv[:3, 0], torch.tensor([-1.0, 1.0, 0.0]))

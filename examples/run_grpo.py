@@ -83,9 +83,17 @@ def main(argv=None) -> dict:
     logger = Logger(cfg.get("logger", {}))
     logger.log_hyperparams(cfg)
     if (cfg["grpo"].get("async_grpo") or {}).get("enabled", False):
-        from rl_b200.algorithms.async_grpo import async_grpo_train
+        from rl_b200.algorithms.async_grpo import async_grpo_train, restore_replay_buffer
 
-        state = async_grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
+        buf = None
+        if ck is not None and ck.get_latest_checkpoint_path():
+            acfg = cfg["grpo"].get("async_grpo") or {}
+            n_groups = max(1, int(cfg["grpo"]["num_prompts_per_step"]) // max(1, ps.dp_size))
+            age = int(acfg.get("max_trajectory_age_steps", 1))
+            buf = restore_replay_buffer(ck.get_latest_checkpoint_path(), n_groups, n_groups * (age + 1) * 2,
+                                        acfg.get("load_replay_buffer"))
+        state = async_grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state,
+                                 replay_buffer=buf)
     else:
         state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
     logger.close()

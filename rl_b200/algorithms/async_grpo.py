@@ -21,6 +21,8 @@ async mode, so the policy must be TP=1 for generation.
 
 from __future__ import annotations
 
+import os
+
 import time
 from typing import Optional
 
@@ -35,6 +37,28 @@ from rl_b200.experience.rollouts import run_multi_turn_rollout
 from rl_b200.utils.timer import Timer, max_over_ranks
 
 __all__ = ["async_grpo_train"]
+
+
+def replay_buffer_file() -> str:
+    """Per-rank replay-buffer file in a checkpoint directory (every rank keeps its own buffer)."""
+    import torch.distributed as dist
+
+    return f"replay_buffer_rank{dist.get_rank() if dist.is_initialized() else 0}.pt"
+
+
+def restore_replay_buffer(ckpt_dir: str, num_prompt_groups: int, max_size: int,
+                          load_replay_buffer: Optional[bool] = None) -> Optional[ReplayBuffer]:
+    """The checkpoint's replay buffer of this rank (groups of incomplete targets
+    dropped), or None when disabled (``load_replay_buffer: false``) or absent.
+    Reference: ``_maybe_restore_async_replay_buffer_checkpoint`` (``nemo_rl/algorithms/grpo.py``)."""
+    import torch
+
+    path = os.path.join(ckpt_dir, replay_buffer_file())
+    if load_replay_buffer is False or not os.path.exists(path):
+        return None
+    buf = ReplayBuffer(max_size=max_size)
+    buf.load_state_dict(torch.load(path, weights_only=False), drop_incomplete_targets=num_prompt_groups)
+    return buf
 
 
 def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_fn=None, logger=None,
@@ -144,9 +168,8 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
                     logger.log_metrics(vm, step, prefix="validation")
             if checkpointer is not None and checkpointer.should_save(step):
                 with collector.weights_lock:
-                    state["replay_buffer"] = buffer.state_dict()
-                    checkpointer.save(policy, state, dataloader, metrics, step)
-                    state.pop("replay_buffer", None)
+                    checkpointer.save(policy, state, dataloader, metrics, step,
+                                      rank_files={replay_buffer_file(): buffer.state_dict()})
     finally:
         collector.stop()
     collector.check_health()

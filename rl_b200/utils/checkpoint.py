@@ -179,8 +179,10 @@ class CheckpointManager:
 
     # ------------------------------------------------------ loop integration
     def save(self, policy, state: dict, dataloader=None, metrics: Optional[dict] = None, step: Optional[int] = None,
-             run_config: Optional[dict] = None) -> str:
-        """Full checkpoint of a training loop (weights, optimizer, loop state)."""
+             run_config: Optional[dict] = None, rank_files: Optional[dict] = None) -> str:
+        """Full checkpoint of a training loop (weights, optimizer, loop state).
+        ``rank_files``: ``{file name: object}`` this rank writes with ``torch.save``
+        into the checkpoint directory (per-rank state such as an async replay buffer)."""
         import torch
         import torch.distributed as dist
 
@@ -197,6 +199,8 @@ class CheckpointManager:
                                fmt=self.cfg.get("model_save_format", "safetensors"))
         if dataloader is not None and rank0 and hasattr(dataloader, "state_dict"):
             torch.save(dataloader.state_dict(), os.path.join(tmp, "train_dataloader.pt"))
+        for name, obj in (rank_files or {}).items():
+            torch.save(obj, os.path.join(tmp, name))
         if dist.is_initialized():
             dist.barrier()
         if rank0:

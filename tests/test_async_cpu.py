@@ -85,3 +85,20 @@ def test_async_grpo_tiny_runs():
     assert state["current_step"] == 3
     # no pump thread is left behind
     assert not [t for t in threading.enumerate() if t.name == "rollout-pump" and t.is_alive()]
+
+
+def test_replay_buffer_checkpoint_file_round_trip(tmp_path):
+    """The async loop's replay buffer is written per rank into the checkpoint
+    directory and restored from it (incomplete targets dropped); restoring is
+    skipped when disabled or when the file is absent."""
+    from rl_b200.algorithms.async_grpo import replay_buffer_file, restore_replay_buffer
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+
+    rb = ReplayBuffer(8)
+    for tgt in (3, 3, 4):
+        rb.add(BatchedDataDict({"x": torch.arange(3) + tgt}), weight_version=2, target_weight_version=tgt)
+    torch.save(rb.state_dict(), tmp_path / replay_buffer_file())
+    back = restore_replay_buffer(str(tmp_path), num_prompt_groups=2, max_size=8)
+    assert back is not None and back.existing_targets() == {3} and back.count_for_target(3) == 2
+    assert restore_replay_buffer(str(tmp_path), 2, 8, load_replay_buffer=False) is None
+    assert restore_replay_buffer(str(tmp_path / "missing"), 2, 8) is None

@@ -46,6 +46,9 @@ at::Tensor gemm_nt(at::Tensor a, at::Tensor b);
 int64_t gemm_error_flag(bool reset);
 void gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> recv_ptrs,
              std::vector<int64_t> flag_ptrs, std::vector<int64_t> ack_ptrs, int64_t me, int64_t epoch);
+// gemm_grouped.cu
+at::Tensor grouped_gemm_nt(at::Tensor x, at::Tensor w, at::Tensor offs);
+int64_t grouped_gemm_error_flag(bool reset);
 // gemm_fp8.cu
 at::Tensor gemm_fp8(at::Tensor a, at::Tensor a_scale, at::Tensor b, at::Tensor b_scale, int64_t splits);
 at::Tensor gemm_mxf8(at::Tensor a, at::Tensor a_scale, at::Tensor b, at::Tensor b_scale, int64_t splits);
@@ -116,6 +119,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_mxf8", &gemm_mxf8, py::arg("a"), py::arg("a_scale_t"), py::arg("b"), py::arg("b_scale_t"),
         py::arg("splits") = 0, "e4m3 GEMM with power-of-two block scales applied by the tensor cores -> bf16");
   m.def("gemm_fp8_error_flag", &gemm_fp8_error_flag, py::arg("reset") = false);
+  m.def("grouped_gemm_nt", &grouped_gemm_nt, "per-expert bf16 GEMM, rows grouped by expert (tcgen05)");
+  m.def("grouped_gemm_error_flag", &grouped_gemm_error_flag, py::arg("reset") = false);
   m.def("symm_alloc", &symm_alloc);
   m.def("symm_open", &symm_open);
   m.def("symm_close", &symm_close);

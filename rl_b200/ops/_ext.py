@@ -33,6 +33,7 @@ _KERNELS_PER_CALL = {
     "sample": 2,
     "gemm_error_flag": 0,
     "gemm_fp8_error_flag": 0,
+    "grouped_gemm_error_flag": 0,
     "gemm_decode_error_flag": 0,
     "stream_write_u32": 0,
     "decode_ar_error_flag": 0,

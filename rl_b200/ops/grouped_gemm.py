@@ -5,16 +5,29 @@
 ``dx`` is the grouped ``dy @ w[e]`` and ``dw[e] = dy_e^T @ x_e`` (accumulated into
 ``w.main_grad`` when present, like ``rl_b200.ops.linear``).
 
-CUDA path: the ragged grouped GEMM of the library (``torch._grouped_mm``) for
-the forward and input gradient; weight gradients are per-expert GEMMs.  The
-CPU path loops over experts in fp32.
+CUDA path: the forward runs the tcgen05 grouped kernel of ``csrc/gemm_grouped.cu``
+(tile schedule built on the device from the offsets) when
+``RL_B200_NATIVE_GROUPED=1``, else the library's ragged grouped GEMM
+(``torch._grouped_mm``), which also takes the input gradient; weight gradients
+are per-expert GEMMs.  The CPU path loops over experts in fp32.
 """
 
 from __future__ import annotations
 
+import os
+
 import torch
 
 __all__ = ["grouped_mm_nt"]
+
+_NATIVE = os.environ.get("RL_B200_NATIVE_GROUPED", "0") == "1"
+
+
+def _native_ok(x: torch.Tensor, w: torch.Tensor) -> bool:
+    from rl_b200.ops._ext import has_ext
+
+    return (_NATIVE and x.is_cuda and x.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and has_ext()
+            and x.shape[1] % 64 == 0 and w.shape[1] % 128 == 0 and w.shape[0] <= 512)
 
 
 def _offsets(counts: torch.Tensor) -> torch.Tensor:
@@ -51,6 +64,10 @@ class _GroupedNT(torch.autograd.Function):
         ctx.save_for_backward(x, w, counts)
         if x.shape[0] == 0:
             return x.new_zeros(0, w.shape[1])
+        if _native_ok(x, w):
+            from rl_b200.ops._ext import ext
+
+            return ext().grouped_gemm_nt(x.contiguous(), w.contiguous(), _offsets(counts))
         if _gmm_ok(x):
             return torch._grouped_mm(x, w.transpose(1, 2), offs=_offsets(counts))
         return _loop_nt(x, w, counts)

@@ -434,3 +434,25 @@ def test_gemm_mxf8_hardware_block_scale(cuda_device, M, N, K, splits):
     assert ext.gemm_fp8_error_flag(True) == 0
     ref = gemm_fp8_ref(a_q, a_s, b_q, b_s)
     assert rel_err(y, ref) < 5e-3
+
+
+@pytest.mark.parametrize("counts,N,K", [([130, 0, 7, 300, 64], 256, 128), ([1, 1, 1, 1], 128, 64),
+                                        ([513, 0, 0, 200], 384, 256), ([0, 0, 90], 1536, 512)])
+def test_grouped_gemm_tcgen05(cuda_device, counts, N, K):
+    """Per-expert tcgen05 GEMM (device-built tile schedule, tiles overhanging an
+    expert's segment are not stored) against per-expert fp32 products."""
+    ext = _ext.ext()
+    torch.manual_seed(12)
+    T, E = sum(counts), len(counts)
+    x = torch.randn(T, K, device=cuda_device).to(torch.bfloat16)
+    w = (torch.randn(E, N, K, device=cuda_device) * 0.05).to(torch.bfloat16)
+    offs = torch.cumsum(torch.tensor(counts), 0).to(torch.int32).to(cuda_device)
+    y = ext.grouped_gemm_nt(x, w, offs)
+    torch.cuda.synchronize()
+    assert ext.grouped_gemm_error_flag(True) == 0
+    ref = torch.empty(T, N, device=cuda_device)
+    s = 0
+    for e, c in enumerate(counts):
+        ref[s:s + c] = x[s:s + c].float() @ w[e].float().t()
+        s += c
+    assert rel_err(y, ref) < 1e-2

@@ -140,6 +140,33 @@ def dynamic_sampling(rewards: torch.Tensor, group_ids: torch.Tensor,
     return ~trivial
 
 
+def apply_message_level_advantage_penalties(train_data: BatchedDataDict, message_logs: list,
+                                            invalid_tool_call_advantage: Optional[float] = None,
+                                            malformed_thinking_advantage: Optional[float] = None) -> None:
+    """Overwrite the advantages of the tokens of assistant messages that an
+    environment flagged (``is_invalid_tool_call`` / ``has_malformed_thinking``)
+    with the configured values; other messages and tokens keep theirs.  A
+    broadcast (stride-0) advantage tensor is materialised first.
+    Reference: ``_apply_message_level_advantage_penalties`` (``nemo_rl/algorithms/grpo.py``)."""
+    if invalid_tool_call_advantage is None and malformed_thinking_advantage is None:
+        return
+    adv = train_data["advantages"].clone()
+    for b, log in enumerate(message_logs):
+        off = 0
+        for msg in log:
+            L = len(msg["token_ids"])
+            if msg.get("role") == "assistant":
+                val = None
+                if invalid_tool_call_advantage is not None and msg.get("is_invalid_tool_call"):
+                    val = float(invalid_tool_call_advantage)
+                elif malformed_thinking_advantage is not None and msg.get("has_malformed_thinking"):
+                    val = float(malformed_thinking_advantage)
+                if val is not None:
+                    adv[b, off:off + L] = val
+            off += L
+    train_data["advantages"] = adv
+
+
 def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, loss_cfg: dict,
                      group_ids: torch.Tensor) -> tuple[BatchedDataDict, dict]:
     """Flatten message logs and compute per-token advantages."""
@@ -176,6 +203,10 @@ def build_train_data(rollout_batch: BatchedDataDict, advantages_fn, cfg: dict, l
         "sample_mask": sample_mask,
     })
     data["rewards"] = rewards  # per-sample rewards (VAPO's positive-example NLL)
+    apply_message_level_advantage_penalties(data, logs, cfg.get("invalid_tool_call_advantage"),
+                                            cfg.get("malformed_thinking_advantage"))
+    if cfg.get("invalid_tool_call_advantage") is not None or cfg.get("malformed_thinking_advantage") is not None:
+        data["advantages"] = data["advantages"] * token_mask  # penalties only on trained tokens
     for k in ("sampler_topk_token_ids", "sampler_topk_logprobs"):  # score centering
         if k in flat:
             data[k] = flat[k]

@@ -8,7 +8,12 @@ environment service as one JSON ``POST`` to ``{base_url}/run`` (concurrently,
     request  {"messages": [{"role", "content", "token_ids"}, ...],
               "metadata": <sample metadata>, "task": <task name>}
     response {"reward": float, "done": bool,
-              "observation": {"role", "content"} | null, "metadata": <new metadata>}
+              "observation": {"role", "content"} | null, "metadata": <new metadata>,
+              "invalid_tool_call": bool, "malformed_thinking": bool}
+
+The two optional flags mark the sample's last assistant message
+(``is_invalid_tool_call`` / ``has_malformed_thinking``) for GRPO's
+message-level advantage penalties.
 
 Failed calls are retried (``retries``) and then scored ``failure_reward`` with
 the episode ended, so one bad row never stalls the batch.
@@ -75,7 +80,7 @@ class HttpGymEnvironment(EnvironmentInterface):
                     for log, md in zip(message_log_batch, metadata)]
         results = list(self.pool.map(self._post, payloads))
         obs, meta, rewards, done = [], [], [], []
-        for res, md in zip(results, metadata):
+        for res, md, log in zip(results, metadata, message_log_batch):
             if res is None:
                 self.failures += 1
                 obs.append({})
@@ -85,6 +90,12 @@ class HttpGymEnvironment(EnvironmentInterface):
                 continue
             obs.append(res.get("observation") or {})
             meta.append(res.get("metadata", md))
+            last = next((m for m in reversed(log) if m.get("role") == "assistant"), None)
+            if last is not None:
+                if res.get("invalid_tool_call"):
+                    last["is_invalid_tool_call"] = True
+                if res.get("malformed_thinking"):
+                    last["has_malformed_thinking"] = True
             rewards.append(float(res.get("reward", 0.0)))
             done.append(bool(res.get("done", True)))
         return EnvironmentReturn(obs, meta, [None] * len(obs), torch.tensor(rewards, dtype=torch.float32),

@@ -848,3 +848,32 @@ def test_dynamic_sampling_and_masked_reward_policy():
     adv = est.compute_advantage(torch.zeros(4, 3, dtype=torch.long), torch.tensor([1.0, 3.0, 2.0, 0.0]),
                                 torch.ones(4, 5), valid_mask=torch.tensor([1.0, 1.0, 1.0, 0.0]))
     torch.testing.assert_close(adv[:3, 0], torch.tensor([-1.0, 1.0, 0.0]))
+
+
+def test_message_level_advantage_penalties():
+    """Flagged assistant messages get the configured advantage on their tokens;
+    flagged user messages and unflagged tokens keep theirs; broadcast advantages
+    are materialised (the reference's documented examples)."""
+    from rl_b200.algorithms.grpo import apply_message_level_advantage_penalties
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+
+    td = BatchedDataDict({"advantages": torch.tensor([[0.0, 1, 2, 3, 4, 5], [10.0, 11, 12, 13, 14, 15]])})
+    logs = [[{"role": "user", "token_ids": torch.tensor([1, 2]), "is_invalid_tool_call": True},
+             {"role": "assistant", "token_ids": torch.tensor([3, 4]), "is_invalid_tool_call": True},
+             {"role": "assistant", "token_ids": torch.tensor([5, 6])}],
+            [{"role": "user", "token_ids": torch.tensor([7])},
+             {"role": "assistant", "token_ids": torch.tensor([8, 9, 10]), "has_malformed_thinking": True},
+             {"role": "assistant", "token_ids": torch.tensor([11, 12])}]]
+    apply_message_level_advantage_penalties(td, logs, -5.0, -7.0)
+    torch.testing.assert_close(td["advantages"], torch.tensor([[0.0, 1, -5, -5, 4, 5], [10.0, -7, -7, -7, 14, 15]]))
+    per = torch.tensor([[1.0], [10.0]])
+    td2 = BatchedDataDict({"advantages": per.expand(2, 6)})
+    logs2 = [[{"role": "user", "token_ids": torch.tensor([1])},
+              {"role": "assistant", "token_ids": torch.tensor([2, 3, 4]), "is_invalid_tool_call": True},
+              {"role": "assistant", "token_ids": torch.tensor([5, 6])}],
+             [{"role": "user", "token_ids": torch.tensor([7, 8])},
+              {"role": "assistant", "token_ids": torch.tensor([9, 10]), "has_malformed_thinking": True},
+              {"role": "assistant", "token_ids": torch.tensor([11, 12])}]]
+    apply_message_level_advantage_penalties(td2, logs2, -5.0, -7.0)
+    torch.testing.assert_close(td2["advantages"], torch.tensor([[1.0, -5, -5, -5, 1, 1], [10.0, 10, -7, -7, 10, 10]]))
+    torch.testing.assert_close(per, torch.tensor([[1.0], [10.0]]))

@@ -87,8 +87,11 @@ def dpo_train(policy, train_dataloader, master_config: dict, logger=None, checkp
                 logger.log_metrics(metrics, step, prefix="train")
             if step_callback:
                 step_callback(step, metrics)
-            if checkpointer is not None and checkpointer.should_save(step):
+            out_of_time = checkpointer is not None and checkpointer.deadline_reached()
+            if checkpointer is not None and (checkpointer.should_save(step) or out_of_time):
                 checkpointer.save(policy, state, train_dataloader, metrics, step)
+            if out_of_time:  # saved before the wall-clock deadline; stop here
+                return state
         state["current_epoch"] = epoch + 1
     return state
 
@@ -114,7 +117,10 @@ def rm_train(reward_model, train_dataloader, master_config: dict, logger=None, c
                 logger.log_metrics(metrics, step, prefix="train")
             if step_callback:
                 step_callback(step, metrics)
-            if checkpointer is not None and checkpointer.should_save(step):
+            out_of_time = checkpointer is not None and checkpointer.deadline_reached()
+            if checkpointer is not None and (checkpointer.should_save(step) or out_of_time):
                 checkpointer.save(reward_model, state, train_dataloader, metrics, step)
+            if out_of_time:  # saved before the wall-clock deadline; stop here
+                return state
         state["current_epoch"] = epoch + 1
     return state

@@ -432,8 +432,11 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 key = cfg.get("stop_at_validation_metric")
                 if key and thr is not None and vm.get(key, -math.inf) >= float(thr):
                     done = True
-            if checkpointer is not None and checkpointer.should_save(step):
+            out_of_time = checkpointer is not None and checkpointer.deadline_reached()
+            if checkpointer is not None and (checkpointer.should_save(step) or out_of_time):
                 checkpointer.save(policy, state, dataloader, metrics, step)
+            if out_of_time:  # saved before the wall-clock deadline; stop here
+                done = True
             if done:
                 break
         if done or step >= max_steps:

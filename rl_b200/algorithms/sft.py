@@ -72,7 +72,10 @@ def sft_train(policy, train_dataloader, master_config: dict, logger=None, checkp
                 vm = sft_validate(policy, val_dataloader)
                 if logger:
                     logger.log_metrics(vm, step, prefix="validation")
-            if checkpointer is not None and checkpointer.should_save(step):
+            out_of_time = checkpointer is not None and checkpointer.deadline_reached()
+            if checkpointer is not None and (checkpointer.should_save(step) or out_of_time):
                 checkpointer.save(policy, state, train_dataloader, metrics, step)
+            if out_of_time:  # saved before the wall-clock deadline; stop here
+                return state
         state["current_epoch"] = epoch + 1
     return state

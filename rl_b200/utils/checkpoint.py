@@ -98,6 +98,31 @@ class CheckpointManager:
         with open(os.path.join(path, "training_info.json")) as f:
             return json.load(f)
 
+    def deadline_reached(self) -> bool:
+        """Mark a finished iteration; True when the next one would run past
+        ``checkpoint_must_save_by`` (agreed over all ranks), so the loop saves
+        and stops.  Reference: ``TimeoutChecker`` use in the training loops."""
+        if not self.cfg.get("checkpoint_must_save_by"):
+            return False
+        if getattr(self, "_timeout", None) is None:
+            from rl_b200.utils.timer import TimeoutChecker
+
+            self._timeout = TimeoutChecker(self.cfg["checkpoint_must_save_by"])
+            self._timeout.start_iterations()
+            return False
+        self._timeout.mark_iteration()
+        hit = self._timeout.check_save()
+        import torch
+        import torch.distributed as dist
+
+        if dist.is_initialized() and dist.get_world_size() > 1:
+            dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend() == "nccl" \
+                else torch.device("cpu")
+            t = torch.tensor([1.0 if hit else 0.0], device=dev)
+            dist.all_reduce(t, op=dist.ReduceOp.MAX)
+            hit = bool(t.item() > 0)
+        return hit
+
     def should_save(self, step: int) -> bool:
         return bool(self.cfg.get("enabled", True)) and self.save_period > 0 and step % self.save_period == 0
 

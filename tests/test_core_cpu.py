@@ -877,3 +877,25 @@ def test_message_level_advantage_penalties():
     apply_message_level_advantage_penalties(td2, logs2, -5.0, -7.0)
     torch.testing.assert_close(td2["advantages"], torch.tensor([[1.0, -5, -5, -5, 1, 1], [10.0, 10, -7, -7, 10, 10]]))
     torch.testing.assert_close(per, torch.tensor([[1.0], [10.0]]))
+
+
+def test_training_stops_and_saves_before_deadline(tmp_path):
+    """checkpoint_must_save_by: when the next step would cross the deadline the
+    loop saves a checkpoint and stops early (the save period alone would not)."""
+    from rl_b200.algorithms.sft import sft_train
+    from rl_b200.data.datasets import SFTDataset, StatefulDataLoader
+    from rl_b200.utils.checkpoint import CheckpointManager
+
+    w = _tiny_policy(seed=3)
+    g = random.Random(1)
+    samples = [([g.randrange(512) for _ in range(6)], [7, 8, 9, 10]) for _ in range(400)]
+    dl = StatefulDataLoader(SFTDataset(samples), 8, shuffle=False)
+    ck = CheckpointManager({"enabled": True, "checkpoint_dir": str(tmp_path), "save_period": 1000,
+                            "checkpoint_must_save_by": "00:00:00:01"})
+    import time
+
+    state = sft_train(w, dl, {"sft": {"max_num_steps": 50, "val_period": 0},
+                              "policy": {"train_global_batch_size": 8}},
+                      checkpointer=ck, step_callback=lambda s, m: time.sleep(0.3))
+    assert 1 <= state["current_step"] < 50
+    assert ck.list_steps() == [state["current_step"]]

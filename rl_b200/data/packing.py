@@ -46,15 +46,33 @@ class PackingAlgorithm(enum.Enum):
 
 
 class SequencePacker:
+    """Base packer.  ``min_bin_count`` / ``bin_count_multiple`` make the bin
+    count at least / a multiple of the given number (data-parallel ranks each
+    need a micro-batch, and the same number of them); ``max_sequences_per_bin``
+    caps the items per bin."""
+
     def __init__(self, bin_capacity: int, collect_metrics: bool = False, min_bin_count: Optional[int] = None,
+                 bin_count_multiple: Optional[int] = None, max_sequences_per_bin: Optional[int] = None,
                  seed: int = 0):
         if bin_capacity <= 0:
             raise ValueError("bin_capacity must be positive")
+        if min_bin_count is not None and min_bin_count < 0:
+            raise ValueError("min_bin_count must be nonnegative")
+        if bin_count_multiple is not None and bin_count_multiple < 1:
+            raise ValueError("bin_count_multiple must be positive")
+        if max_sequences_per_bin is not None and max_sequences_per_bin < 1:
+            raise ValueError("max_sequences_per_bin must be >= 1 (or None for unlimited)")
         self.bin_capacity = int(bin_capacity)
         self.collect_metrics = collect_metrics
         self.min_bin_count = min_bin_count
+        self.bin_count_multiple = bin_count_multiple
+        self.max_sequences_per_bin = max_sequences_per_bin
         self.seed = seed
         self.last_metrics: dict = {}
+
+    def _fits(self, count: int) -> bool:
+        """Room for one more item in a bin that holds ``count``."""
+        return self.max_sequences_per_bin is None or count < self.max_sequences_per_bin
 
     def _pack(self, lengths: list[int]) -> list[list[int]]:
         raise NotImplementedError
@@ -69,8 +87,7 @@ class SequencePacker:
         if not lengths:
             return []
         bins = [b for b in self._pack(lengths) if b]
-        if self.min_bin_count is not None:
-            bins = _split_to_min_bins(bins, lengths, self.min_bin_count)
+        bins = self._adjust_bin_count(bins, lengths)
         if self.collect_metrics:
             used = [sum(lengths[i] for i in b) for b in bins]
             self.last_metrics = {
@@ -81,10 +98,24 @@ class SequencePacker:
             }
         return bins
 
+    def _adjust_bin_count(self, bins: list[list[int]], lengths: list[int]) -> list[list[int]]:
+        target = len(bins)
+        if self.min_bin_count is not None:
+            target = max(target, self.min_bin_count)
+        if self.bin_count_multiple is not None and target % self.bin_count_multiple:
+            target += self.bin_count_multiple - target % self.bin_count_multiple
+        if target == len(bins):
+            return bins
+        if len(lengths) < target:
+            raise ValueError(f"Cannot create {target} bins with only {len(lengths)} sequences: every bin needs "
+                             "one; lower min_bin_count / bin_count_multiple or pass more sequences")
+        return _split_to_min_bins(bins, lengths, target)
+
 
 def _split_to_min_bins(bins: list[list[int]], lengths: list[int], min_bins: int) -> list[list[int]]:
-    """Split the fullest multi-item bins until at least ``min_bins`` bins exist
-    (used to give every pipeline / data-parallel rank a micro-batch)."""
+    """Split the fullest multi-item bins in two (halves of about equal tokens)
+    until ``min_bins`` bins exist; the halves keep every bin within capacity
+    and within the item cap, and the rest of the packing is untouched."""
     bins = [list(b) for b in bins]
     while len(bins) < min_bins:
         cands = [b for b in bins if len(b) > 1]
@@ -111,7 +142,7 @@ class ConcatenativePacker(SequencePacker):
     def _pack(self, lengths):
         bins, cur, used = [], [], 0
         for i, L in enumerate(lengths):
-            if used + L > self.bin_capacity:
+            if used + L > self.bin_capacity or not self._fits(len(cur)):
                 bins.append(cur)
                 cur, used = [], 0
             cur.append(i)
@@ -130,7 +161,7 @@ class FirstFitPacker(SequencePacker):
         for i in self._order(lengths):
             L = lengths[i]
             for b, room in enumerate(free):
-                if room >= L:
+                if room >= L and self._fits(len(bins[b])):
                     bins[b].append(i)
                     free[b] -= L
                     break
@@ -154,6 +185,11 @@ class FirstFitShufflePacker(FirstFitPacker):
 
 class ModifiedFirstFitDecreasingPacker(SequencePacker):
     def _pack(self, lengths):
+        if self.max_sequences_per_bin is not None:
+            # The class phases only reason about token room; with an item cap
+            # first-fit-decreasing (which checks both) packs instead.
+            return FirstFitDecreasingPacker(self.bin_capacity, max_sequences_per_bin=self.max_sequences_per_bin
+                                            )._pack(lengths)
         C = self.bin_capacity
         idx = sorted(range(len(lengths)), key=lambda i: (-lengths[i], i))
         large = [i for i in idx if lengths[i] > C / 2]
@@ -226,7 +262,7 @@ class GreedyKnapsackPacker(SequencePacker):
             cur = []
             keep = []
             for i in remaining:
-                if lengths[i] <= room:
+                if lengths[i] <= room and self._fits(len(cur)):
                     cur.append(i)
                     room -= lengths[i]
                 else:
@@ -237,11 +273,20 @@ class GreedyKnapsackPacker(SequencePacker):
 
 
 class BalancedGreedyKnapsackPacker(SequencePacker):
-    """Use the greedy bin count, then rebalance: assign items largest-first to the
-    least-loaded bin that still has room (equalises per-micro-batch work)."""
+    """Start from the greedy bin count (plus ``balanced_knapsack_delta`` extra
+    bins), then place items largest-first into the least-loaded bin that still
+    has room (equalises per-micro-batch work); a pass that cannot place an item
+    restarts with one more bin."""
+
+    def __init__(self, bin_capacity: int, *args, balanced_knapsack_delta: int = 0, **kwargs):
+        super().__init__(bin_capacity, *args, **kwargs)
+        if balanced_knapsack_delta < 0:
+            raise ValueError("balanced_knapsack_delta must be nonnegative")
+        self.balanced_knapsack_delta = int(balanced_knapsack_delta)
 
     def _pack(self, lengths):
-        n_bins = len(GreedyKnapsackPacker(self.bin_capacity)._pack(lengths))
+        greedy = GreedyKnapsackPacker(self.bin_capacity, max_sequences_per_bin=self.max_sequences_per_bin)
+        n_bins = len(greedy._pack(lengths)) + self.balanced_knapsack_delta
         if self.min_bin_count:
             n_bins = max(n_bins, self.min_bin_count)
         while True:
@@ -251,7 +296,7 @@ class BalancedGreedyKnapsackPacker(SequencePacker):
             for i in sorted(range(len(lengths)), key=lambda i: (-lengths[i], i)):
                 order = sorted(range(n_bins), key=lambda b: load[b])
                 for b in order:
-                    if load[b] + lengths[i] <= self.bin_capacity:
+                    if load[b] + lengths[i] <= self.bin_capacity and self._fits(len(bins[b])):
                         bins[b].append(i)
                         load[b] += lengths[i]
                         break

@@ -226,6 +226,13 @@ class PolicyWorker:
         self.train_mb_tokens = int(sp.get("train_mb_tokens", self.max_seq_len * int(policy_cfg.get("train_micro_batch_size", 4))))
         self.logprob_mb_tokens = int(sp.get("logprob_mb_tokens", self.train_mb_tokens))
         self.packing_algorithm = sp.get("algorithm", "modified_first_fit_decreasing")
+        # "largest_first" runs the largest packed micro-batch first: the caching
+        # allocator's blocks of that one are then reused by every smaller one
+        self.microbatch_order = sp.get("microbatch_order") or "packer"
+        if self.microbatch_order not in ("packer", "largest_first"):
+            raise ValueError(f"sequence_packing.microbatch_order must be 'packer' or 'largest_first', "
+                             f"got {self.microbatch_order!r}")
+        self.max_sequences_per_bin = sp.get("max_sequences_per_bin")
         self.logprob_chunk = int(policy_cfg.get("logprob_chunk_size") or 4096)
         # colocated rollout needs the HBM of the fp32 gradient buffer for its KV cache
         # HBM plan of the colocated worker: the fp32 gradient buffer (4 bytes/param) is
@@ -322,13 +329,17 @@ class PolicyWorker:
             pairs = [(r, r + 1) for r in rows if r % 2 == 0 and r + 1 in set(rows)]
             plen = [lengths[a] + lengths[b] for a, b in pairs]
             budget = max(budget, max(plen))
-            packer = get_packer(self.packing_algorithm, bin_capacity=budget)
+            packer = get_packer(self.packing_algorithm, bin_capacity=budget,
+                                max_sequences_per_bin=self.max_sequences_per_bin)
             for b in packer.pack([max(1, L) for L in plen]):
                 bins.append([x for i in sorted(b) for x in pairs[i]])
         elif rows:
             budget = max(budget, max(lengths[r] for r in rows))
-            packer = get_packer(self.packing_algorithm, bin_capacity=budget)
+            packer = get_packer(self.packing_algorithm, bin_capacity=budget,
+                                max_sequences_per_bin=self.max_sequences_per_bin)
             bins = [[rows[i] for i in b] for b in packer.pack([max(1, lengths[r]) for r in rows])]
+        if self.microbatch_order == "largest_first":
+            bins.sort(key=lambda b: sum(lengths[r] for r in b), reverse=True)
         if self.ps.ep_size > 1 and self.model_cfg.is_moe:
             n = torch.tensor([len(bins)], dtype=torch.int64,
                              device=self.device if self.ps.backend == "nccl" else torch.device("cpu"))
@@ -993,10 +1004,7 @@ class PolicyWorker:
         dist.all_gather_object(parts, part, group=grp)
         order = [i for q in range(t) for i in range(q, B, t)]
         out = BatchedDataDict.from_batches([p for p in parts if p is not None], pad_value_dict={"routed_experts": -1})
-        inv = [0] * B
-        for pos, i in enumerate(order):
-            inv[i] = pos
-        out.reorder_data(inv)
+        out.reorder_data(order)
         return out
 
     def prepare_for_generation(self, num_seqs: Optional[int] = None) -> bool:

@@ -45,14 +45,18 @@ def test_batched_data_dict_shard_and_microbatch():
     assert back.size == B
     mbs = list(d.make_microbatch_iterator(5))
     assert [m.size for m in mbs] == [5, 5, 5, 1]
-    sh = d.shard_by_batch_size(2, batch_size=16, dynamic_batching_args={
-        "max_tokens_per_microbatch": 16, "sequence_length_round": 4, "input_lengths_key": "lens"})
+    sh, order = d.shard_by_batch_size(2, batch_size=16, dynamic_batching_args={
+        "max_tokens_per_microbatch": 16, "sequence_length_round": 4, "input_lengths_key": "lens", "input_key": "x"})
     for s in sh:
         for mb in s.make_microbatch_iterator_with_dynamic_shapes():
             assert mb["x"].shape[1] * mb.size <= 16 or mb.size == 1
-    sp = d.shard_by_batch_size(1, sequence_packing_args={"max_tokens_per_microbatch": 20, "input_lengths_key": "lens"})
-    rows = sorted(r for mb in sp[0].micro_batch_indices for r in mb)
-    assert rows == list(range(B))
+    back = BatchedDataDict.from_batches(sh)
+    back.reorder_data(order)
+    assert torch.equal(back["x"], d["x"]) and back["tags"] == d["tags"]
+    sp, order = d.shard_by_batch_size(1, sequence_packing_args={"max_tokens_per_microbatch": 20,
+                                                                "input_lengths_key": "lens"})
+    assert sorted(order) == list(range(B))
+    assert sum(m.size for m in sp[0].make_microbatch_iterator_for_packable_sequences()) == B
     rep = d.repeat_interleave(2)
     assert rep.size == 2 * B and rep["tags"][:2] == ["t0", "t0"]
 

@@ -33,6 +33,7 @@ from rl_b200.algorithms.async_utils import AsyncTrajectoryCollector, ReplayBuffe
 from rl_b200.algorithms.grpo import DEFAULT_GRPO_CONFIG, GRPOSaveState, _dp_sum, build_train_data, validate
 from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
 from rl_b200.algorithms.utils import set_seed
+from rl_b200.algorithms.length_penalty import LengthPenaltyConfig, apply_length_penalty_to_rollout
 from rl_b200.experience.rollouts import run_multi_turn_rollout
 from rl_b200.utils.timer import Timer, max_over_ranks
 
@@ -71,6 +72,8 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
         raise NotImplementedError("async GRPO generates in a side thread and needs TP=1 generation")
     cfg = {**DEFAULT_GRPO_CONFIG, **master_config.get("grpo", {})}
     acfg = {**DEFAULT_GRPO_CONFIG["async_grpo"], **(cfg.get("async_grpo") or {})}
+    if cfg.get("length_penalty") is not None:
+        cfg["length_penalty"] = LengthPenaltyConfig(cfg["length_penalty"])
     max_age = int(acfg.get("max_trajectory_age_steps", 1))
     loss_cfg = master_config.get("loss_fn", {})
     loss_fn = loss_fn or ClippedPGLossFn(loss_cfg)
@@ -99,7 +102,11 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
         base = target * 1_000_000 + ps.dp_rank * n_prompts
         rep["group_id"] = torch.arange(base, base + n_prompts).repeat_interleave(G)
         policy.prepare_for_generation(len(rep["message_log"]))
-        return run_multi_turn_rollout(policy, rep, tokenizer, task_to_env, max_seq, int(cfg["max_rollout_turns"]))
+        rollout, metrics = run_multi_turn_rollout(policy, rep, tokenizer, task_to_env, max_seq,
+                                                  int(cfg["max_rollout_turns"]))
+        if cfg.get("length_penalty") is not None:  # training rollouts only
+            metrics.update(apply_length_penalty_to_rollout(rollout, cfg["length_penalty"], G, tokenizer))
+        return rollout, metrics
 
     collector = AsyncTrajectoryCollector(rollout_fn, dataloader, buffer, n_groups, G, max_age,
                                          initial_weight_version=step,

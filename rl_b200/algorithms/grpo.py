@@ -29,6 +29,7 @@ from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
 from rl_b200.algorithms.utils import calculate_baseline_and_std_per_prompt, set_seed
 from rl_b200.data.llm_message_utils import add_loss_mask_to_message_log, batched_message_log_to_flat_message
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
+from rl_b200.algorithms.length_penalty import LengthPenaltyConfig, apply_length_penalty_to_rollout
 from rl_b200.experience.rollouts import run_multi_turn_rollout
 from rl_b200.utils.flops import FLOPTracker, mfu
 from rl_b200.utils.nvtx import maybe_gpu_profile_step
@@ -282,6 +283,8 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
         policy.engine.record_sampler_topk = int(loss_cfg.get("score_centering_topk", 8))
 
     data_plane = create_data_plane(master_config.get("data_plane"))
+    if cfg.get("length_penalty") is not None:  # reject a malformed block before the first rollout
+        cfg["length_penalty"] = LengthPenaltyConfig(cfg["length_penalty"])
     state = save_state or GRPOSaveState.default()
     max_steps = max_steps if max_steps is not None else int(cfg["max_num_steps"])
     set_seed(int(cfg["seed"]) + ps.dp_rank)
@@ -320,6 +323,9 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                         policy.prepare_for_generation(len(rep["message_log"]))
                         rollout, rollout_metrics = run_multi_turn_rollout(
                             policy, rep, tokenizer, task_to_env, max_seq, int(cfg["max_rollout_turns"]))
+                        if cfg.get("length_penalty") is not None:
+                            rollout_metrics.update(apply_length_penalty_to_rollout(
+                                rollout, cfg["length_penalty"], G, tokenizer))
                         gen_batches += 1
                         if not cfg.get("use_dynamic_sampling", False):
                             kept_batches.append(rollout)

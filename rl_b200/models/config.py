@@ -177,3 +177,56 @@ def get_model_config(name_or_cfg, **overrides) -> ModelConfig:
             raise KeyError(f"unknown model preset {name_or_cfg!r}; known: {sorted(PRESETS)}")
         cfg = PRESETS[key]
     return cfg.replace(**overrides) if overrides else cfg
+
+
+# HF config.json names that differ from the ModelConfig field names
+_HF_NAMES = {"rms_norm_eps": "rms_eps", "num_hidden_layers": "num_layers", "num_attention_heads": "num_heads",
+             "num_key_value_heads": "num_kv_heads", "intermediate_size": "ffn_hidden_size"}
+
+
+def apply_hf_config_overrides(cfg: ModelConfig, overrides: Optional[dict], max_seq_len: Optional[int] = None
+                              ) -> ModelConfig:
+    """``policy.hf_config_overrides``: HF ``config.json`` keys that replace the
+    model's settings for training and rollout alike (both run the same
+    model).  ``rope_scaling`` with ``rope_type: yarn`` must give every YaRN
+    field; it also sets ``rope_theta`` (when given) and widens
+    ``max_position_embeddings`` to ``factor * original_max_position_embeddings``
+    (and to ``max_seq_len``).
+
+    Reference: ``policy.hf_config_overrides`` (``docs/guides/yarn-long-context.md``).
+    """
+    if not overrides:
+        return cfg
+    from rl_b200.ops.rope import YARN_FIELDS
+
+    fields = {f for f in cfg.__dataclass_fields__}
+    upd: dict = {}
+    for k, v in overrides.items():
+        name = _HF_NAMES.get(k, k)
+        if name not in fields or name == "extra":
+            raise ValueError(f"hf_config_overrides: unsupported key {k!r}")
+        upd[name] = v
+    rs = upd.get("rope_scaling")
+    if rs is not None:
+        rs = dict(rs)
+        kind = rs.get("rope_type", rs.get("type"))
+        if kind == "yarn":
+            missing = [f for f in YARN_FIELDS if f not in rs or rs[f] is None]
+            if missing:
+                raise ValueError(f"hf_config_overrides.rope_scaling: YaRN needs every one of {list(YARN_FIELDS)}; "
+                                 f"missing {missing}")
+            if float(rs["factor"]) <= 0:
+                raise ValueError("hf_config_overrides.rope_scaling.factor must be positive")
+            upd["rope_theta"] = float(rs["rope_theta"])
+            span = int(round(float(rs["factor"]) * int(rs["original_max_position_embeddings"])))
+            upd["max_position_embeddings"] = max(int(upd.get("max_position_embeddings", cfg.max_position_embeddings)),
+                                                 span)
+        elif kind not in ("llama3", "default", None):
+            raise ValueError(f"hf_config_overrides.rope_scaling: rope_type {kind!r} is not supported "
+                             "(llama3, yarn)")
+        upd["rope_scaling"] = rs
+    if max_seq_len is not None:
+        upd["max_position_embeddings"] = max(int(upd.get("max_position_embeddings", cfg.max_position_embeddings)),
+                                             int(max_seq_len))
+    return cfg.replace(**upd)
+

@@ -27,7 +27,7 @@ import torch.distributed as dist
 
 from rl_b200.data.packing import get_packer
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
-from rl_b200.models.config import ModelConfig, get_model_config
+from rl_b200.models.config import ModelConfig, apply_hf_config_overrides, get_model_config
 from rl_b200.models.generation.engine import RolloutEngine
 from rl_b200.models.transformer import TransformerLM
 from rl_b200.ops.fused_linear_logprob import linear_logprobs
@@ -94,7 +94,9 @@ class PolicyWorker:
         self.cfg = policy_cfg
         self.ps = pstate or get_parallel_state()
         self.device = self.ps.device
-        self.model_cfg = model_cfg or get_model_config(policy_cfg.get("model_name", "tiny-llama"))
+        self.model_cfg = apply_hf_config_overrides(
+            model_cfg or get_model_config(policy_cfg.get("model_name", "tiny-llama")),
+            policy_cfg.get("hf_config_overrides"), policy_cfg.get("max_total_sequence_length"))
         self.dtype = _dtype(policy_cfg.get("precision", "bfloat16"))
         if self.device.type == "cpu" and self.dtype != torch.float32:
             self.dtype = torch.float32
@@ -182,6 +184,10 @@ class PolicyWorker:
                                    pp_group=self.ps.pp_group if self.pp > 1 else None)
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
+        if self.max_seq_len > self.model.rope_cache.shape[0]:
+            raise ValueError(f"max_total_sequence_length {self.max_seq_len} exceeds the model's "
+                             f"{self.model.rope_cache.shape[0]} rotary positions; raise max_position_embeddings "
+                             "(policy.hf_config_overrides) or extend the context with YaRN rope_scaling")
         self.gen_model = self.model
         if self.lora is not None:
             # rollout copy with the adapters merged in (same TP layout)

@@ -201,7 +201,8 @@ class TransformerLM(nn.Module):
             raise NotImplementedError("tied embeddings under pipeline parallelism")
         self.specs = self._make_specs()
         self._allocate(seed, init_std)
-        self.rope_cache = build_rope_cache(min(cfg.max_position_embeddings, 1 << 17), cfg.head_dim,
+        # one row per position the model is configured for (YaRN configs widen it)
+        self.rope_cache = build_rope_cache(min(cfg.max_position_embeddings, 1 << 20), cfg.head_dim,
                                            cfg.rope_theta, cfg.rope_scaling, device=self.device)
         self._aux_losses: list[torch.Tensor] = []
         self.aux_loss_scale = 0.0

@@ -41,11 +41,17 @@ def test_store_plane_two_processes():
     from rl_b200.distributed.launch import spawn_ranks
     from tests.dist_cases import case_data_plane
 
-    s = socket.socket()
-    s.bind(("127.0.0.1", 0))
-    port = s.getsockname()[1]
-    s.close()
-    outs = spawn_ranks(case_data_plane, 2, port)
+    for attempt in range(3):  # a port picked this way can be taken again before the store binds it
+        s = socket.socket()
+        s.bind(("127.0.0.1", 0))
+        port = s.getsockname()[1]
+        s.close()
+        try:
+            outs = spawn_ranks(case_data_plane, 2, port)
+            break
+        except RuntimeError:
+            if attempt == 2:
+                raise
     assert all(o["ok"] for o in outs)
     assert outs[0]["stats"]["data_plane/puts"] == 1 and outs[0]["stats"]["data_plane/gets"] == 1
 

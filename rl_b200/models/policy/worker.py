@@ -28,6 +28,7 @@ import torch.distributed as dist
 from rl_b200.data.packing import get_packer
 from rl_b200.distributed.batched_data_dict import BatchedDataDict
 from rl_b200.models.config import ModelConfig, apply_hf_config_overrides, get_model_config
+from rl_b200.parallel.muon import MuonConfig
 from rl_b200.models.generation.engine import RolloutEngine
 from rl_b200.models.transformer import TransformerLM
 from rl_b200.ops.fused_linear_logprob import linear_logprobs
@@ -181,7 +182,8 @@ class PolicyWorker:
                                    tp_group=self.ps.tp_group, sequence_parallel=self.sequence_parallel,
                                    edp_group=self.ps.edp_group, ep_group=self.ps.ep_group,
                                    symmetric=self.symmetric if fused_dp else None,
-                                   pp_group=self.ps.pp_group if self.pp > 1 else None)
+                                   pp_group=self.ps.pp_group if self.pp > 1 else None,
+                                   muon=MuonConfig.from_megatron(mopt) if self.lora is None else None)
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
         if self.max_seq_len > self.model.rope_cache.shape[0]:

@@ -100,16 +100,19 @@ def _ws(group) -> int:
 class _Segment:
     """A contiguous range of the flat buffer with one gradient-reduction group."""
 
-    def __init__(self, lo: int, hi: int, group, norm_sum_group, expert: bool):
+    def __init__(self, lo: int, hi: int, group, norm_sum_group, expert: bool, replicated: bool = False):
         self.lo, self.hi = lo, hi            # global offsets in the flat buffer (padded)
         self.group = group
         self.n = _ws(group)
         self.rank = dist.get_rank(group) if self.n > 1 else 0
         self.norm_sum_group = norm_sum_group  # extra group the shard norm^2 is summed over
         self.expert = expert
+        # replicated: gradients all-reduced and every rank steps the whole range
+        # (Muon needs whole matrices); otherwise ZeRO-1 shards over the group
+        self.sharded = self.n > 1 and not replicated
         size = hi - lo
-        self.shard = size // self.n
-        self.s_lo = lo + self.rank * self.shard  # this rank's shard (global offsets)
+        self.shard = size // self.n if self.sharded else size
+        self.s_lo = lo + (self.rank * self.shard if self.sharded else 0)  # this rank's shard (global offsets)
         self.s_hi = self.s_lo + self.shard
 
 
@@ -117,7 +120,7 @@ class FlatAdamW:
     def __init__(self, model, lr: float = 1e-5, betas=(0.9, 0.999), eps: float = 1e-8, weight_decay: float = 0.0,
                  max_grad_norm: Optional[float] = 1.0, scheduler_cfg=None, min_lr: float = 0.0,
                  dp_group=None, tp_group=None, sequence_parallel: bool = False, edp_group=None, ep_group=None,
-                 symmetric=None, pp_group=None):
+                 symmetric=None, pp_group=None, muon=None):
         """``symmetric``: a ``rl_b200.parallel.symm.NodeSymmetric`` allocator.  When
         given (CUDA, every rank on one node) the fp32 gradient buffer and the bf16
         parameter buffer are symmetric memory and the dense data-parallel segment
@@ -126,8 +129,13 @@ class FlatAdamW:
         by peer stores) instead of NCCL reduce-scatter / all-gather.
         ``pp_group``: under pipeline parallelism each stage steps its own layers;
         the gradient norm used for clipping is the whole model's (sum of squares
-        over the stages)."""
+        over the stages).
+        ``muon``: a ``rl_b200.parallel.muon.MuonConfig``; the linear layers'
+        weights then step with Muon (momentum kept in ``exp_avg``) and the rest
+        with AdamW, on replicated segments (gradients all-reduced over the
+        data-parallel group, no optimizer-state sharding)."""
         self.model = model
+        self.muon = muon
         self.symmetric = symmetric
         self.lr = lr
         self.beta1, self.beta2 = betas
@@ -145,13 +153,14 @@ class FlatAdamW:
         expert_n = int(model.flat_numel) - dense_n
         u_d = 128 * max(1, _ws(dp_group))
         dense_pad = (dense_n + u_d - 1) // u_d * u_d
-        segs = [_Segment(0, dense_pad, dp_group, None, False)]
+        rep = muon is not None
+        segs = [_Segment(0, dense_pad, dp_group, None, False, replicated=rep)]
         total = dense_pad
         if expert_n > 0:
             g = edp_group if edp_group is not None else dp_group
             u_e = 128 * max(1, _ws(g))
             exp_pad = (expert_n + u_e - 1) // u_e * u_e
-            segs.append(_Segment(dense_pad, dense_pad + exp_pad, g, ep_group, True))
+            segs.append(_Segment(dense_pad, dense_pad + exp_pad, g, ep_group, True, replicated=rep))
             total = dense_pad + exp_pad
         self.segments = segs
         self.padded = total
@@ -164,10 +173,16 @@ class FlatAdamW:
             seg.exp_avg = torch.zeros(seg.shard, dtype=torch.float32, device=dev)
             seg.exp_avg_sq = torch.zeros(seg.shard, dtype=torch.float32, device=dev)
             wd_r, rep_r = [], []
+            seg.muon_params = []
+            from rl_b200.parallel.muon import is_muon_param
+
             for sp, p in model.named_flat_params():
                 a, b = max(sp.offset, seg.s_lo), min(sp.offset + sp.numel, seg.s_hi)
                 if a < b:
-                    wd_r.append((a - seg.s_lo, b - seg.s_lo, not sp.no_weight_decay))
+                    if muon is not None and is_muon_param(sp.name):
+                        seg.muon_params.append((sp, a - seg.s_lo, b - seg.s_lo))
+                    else:
+                        wd_r.append((a - seg.s_lo, b - seg.s_lo, not sp.no_weight_decay))
                     rep_r.append((a - seg.s_lo, b - seg.s_lo, sp.tp_dim is None and sp.ep_dim is None))
             seg.wd_ranges = _merge(wd_r)
             seg.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
@@ -218,7 +233,7 @@ class FlatAdamW:
         else:
             self.main_grad = torch.zeros(self.padded, dtype=torch.float32, device=self.device)
         for seg in self.segments:
-            if seg.n == 1:
+            if not seg.sharded:
                 seg.grad_shard = self.main_grad[seg.s_lo:seg.s_hi]
             else:
                 seg.grad_shard = torch.zeros(seg.shard, dtype=torch.float32, device=self.device)
@@ -268,19 +283,21 @@ class FlatAdamW:
         sq_total = torch.zeros((), dtype=torch.float32, device=self.device)
         for seg in self.segments:
             fused = self._fused(seg)
-            if seg.n > 1 and fused:
+            if not seg.sharded and seg.n > 1:
+                dist.all_reduce(seg.grad_shard, group=seg.group)  # replicated (Muon): whole gradient
+            if seg.sharded and fused:
                 # peers finished their backward passes (stream-ordered fence), then
                 # this rank reduces its shard straight out of their gradient buffers
                 self._fence(seg.group)
                 part = ext().dp_reduce_shard(self._peer_ptrs(self._grad_symm, seg), seg.s_lo, seg.shard,
                                              seg.grad_shard)
                 sq_all = part.sum()
-            elif seg.n > 1:
+            elif seg.sharded:
                 # losses are normalised by GLOBAL token / sequence counts, so the
                 # per-rank gradients are partial sums: reduce with SUM, not mean.
                 dist.reduce_scatter_tensor(seg.grad_shard, self.main_grad[seg.lo:seg.hi], group=seg.group)
             g = seg.grad_shard
-            if not (seg.n > 1 and fused):
+            if not (seg.sharded and fused):
                 sq_all = sum_of_squares(g)
             if self.tp > 1:
                 sq_rep = torch.zeros((), dtype=torch.float32, device=g.device)
@@ -291,7 +308,7 @@ class FlatAdamW:
                 sq = sq_sh + sq_rep
             else:
                 sq = sq_all
-            if seg.n > 1:
+            if seg.sharded:
                 dist.all_reduce(sq, group=seg.group)
             if seg.norm_sum_group is not None and _ws(seg.norm_sum_group) > 1:
                 dist.all_reduce(sq, group=seg.norm_sum_group)
@@ -312,7 +329,7 @@ class FlatAdamW:
         for seg in self.segments:
             out = m.flat_param[seg.s_lo:seg.s_hi]
             g = seg.grad_shard
-            if seg.n > 1 and self._fused(seg):
+            if seg.sharded and self._fused(seg):
                 ext().dp_adam_allgather(self._peer_ptrs(self._flat_symm(), seg, param=True), seg.s_lo, seg.master, g,
                                         seg.exp_avg, seg.exp_avg_sq, seg.nodecay_dev, lr, self.beta1, self.beta2,
                                         self.eps, self.weight_decay, self.step_count, scale)
@@ -322,13 +339,15 @@ class FlatAdamW:
                 adamw_step(seg.master[a:b], g[a:b], seg.exp_avg[a:b], seg.exp_avg_sq[a:b], lr, self.beta1,
                            self.beta2, self.eps, self.weight_decay if decayed else 0.0, self.step_count,
                            grad_scale=scale, param_out=out[a:b])
-            if seg.n > 1:
+            if seg.muon_params:
+                self._muon_step(seg, out, lr, scale)
+            if seg.sharded:
                 dist.all_gather_into_tensor(m.flat_param[seg.lo:seg.hi], out.clone(), group=seg.group)
         if fenced:
             # every rank's peer stores of its updated shard must land before the
             # parameters are read (or the gradients zeroed under a peer's loads)
             for seg in self.segments:
-                if seg.n > 1 and self._fused(seg):
+                if seg.sharded and self._fused(seg):
                     self._fence(seg.group)
         self.zero_grad()
         bump = getattr(m, "bump_weight_version", None)
@@ -337,7 +356,36 @@ class FlatAdamW:
         return {"grad_norm": norm, "lr": lr}
 
     # ------------------------------------------------------ fused DP path
+    def _muon_step(self, seg, out: torch.Tensor, lr: float, grad_scale: float) -> None:
+        from rl_b200.parallel.muon import muon_scale, orthogonalize
+
+        cfg = self.muon
+        mu = cfg.momentum
+        for sp, a, b in seg.muon_params:
+            shape = sp.shape
+            g = seg.grad_shard[a:b].view(shape) * grad_scale
+            buf = seg.exp_avg[a:b].view(shape)
+            buf.lerp_(g, 1.0 - mu)
+            upd = g.lerp(buf, mu) if cfg.nesterov else buf
+            tp_dim = None if sp.tp_dim is None else sp.tp_dim - len(shape)  # counted from the end
+            blocks = [upd]
+            if cfg.split_qkv and sp.name.endswith("qkv_proj.weight"):
+                hd = self.model.cfg.head_dim
+                blocks = list(torch.split(upd, [self.model.nq * hd, self.model.nkv * hd, self.model.nkv * hd], -2))
+            outs = []
+            for blk in blocks:
+                o, (d_out, d_in) = orthogonalize(blk, tp_dim, cfg, self.tp_group)
+                outs.append(o * (muon_scale(d_out, d_in, cfg.scale_mode) * cfg.extra_scale_factor))
+            o = torch.cat(outs, -2) if len(outs) > 1 else outs[0]
+            w = seg.master[a:b].view(shape)
+            if self.weight_decay and not sp.no_weight_decay:
+                w.mul_(1.0 - lr * self.weight_decay)
+            w.add_(o, alpha=-lr)
+            out[a:b].copy_(w.reshape(-1))
+
     def _fused(self, seg) -> bool:
+        if not seg.sharded:
+            return False
         return (self.symmetric is not None and not seg.expert and self.device.type == "cuda"
                 and self._flat_symm() is not None)
 
@@ -367,7 +415,7 @@ class FlatAdamW:
             m.bump_weight_version()
         for seg in self.segments:
             m.flat_param[seg.s_lo:seg.s_hi].copy_(seg.master)
-            if seg.n > 1:
+            if seg.sharded:
                 dist.all_gather_into_tensor(m.flat_param[seg.lo:seg.hi], m.flat_param[seg.s_lo:seg.s_hi].clone(),
                                             group=seg.group)
 

@@ -1,5 +1,7 @@
 """Rank functions for the multi-process CPU (gloo) tests; importable by spawned ranks."""
 
+from typing import Optional
+
 import torch
 
 from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
@@ -35,14 +37,18 @@ def _pcfg(sp: bool):
             "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
 
 
-def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool, cp: int = 1, pp: int = 1):
+def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool, cp: int = 1, pp: int = 1,
+                    muon: Optional[dict] = None):
     from rl_b200.models.policy.worker import PolicyWorker
     from rl_b200.parallel.state import init_distributed
 
     torch.manual_seed(0)
     ps = init_distributed(tp=tp, ep=ep, cp=cp, pp=pp, backend="gloo")
     cfg = TINY_MOE if moe else TINY
-    w = PolicyWorker(_pcfg(sp), model_cfg=cfg, pstate=ps, seed=3)
+    pcfg = _pcfg(sp)
+    if muon is not None:
+        pcfg["megatron_cfg"]["optimizer"] = dict(muon)
+    w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=3)
     full = make_batch()
     B = full.size
     per = B // ps.dp_size

@@ -85,7 +85,7 @@ def _gather_full(model, sp, t: torch.Tensor) -> torch.Tensor:
     if sp.tp_dim is not None and ps.tp_size > 1:
         parts = [torch.empty_like(t) for _ in range(ps.tp_size)]
         dist.all_gather(parts, t.contiguous(), group=ps.tp_group)
-        if sp.name.endswith("qkv_proj.weight"):
+        if sp.name.endswith(("qkv_proj.weight", "qkv_proj.bias")):
             c = model.cfg
             sizes = [model.nq * c.head_dim, model.nkv * c.head_dim, model.nkv * c.head_dim]
             qs, ks, vs = zip(*[torch.split(p, sizes, 0) for p in parts])
@@ -110,11 +110,12 @@ def hf_state_dict(model, dtype: Optional[torch.dtype] = torch.bfloat16) -> dict[
         if dtype is not None:
             full = full.to(dtype)
         name = sp.name
-        if name.endswith("self_attn.qkv_proj.weight"):
-            pre = name[: -len("qkv_proj.weight")]
+        if name.endswith(("self_attn.qkv_proj.weight", "self_attn.qkv_proj.bias")):
+            kind = name.rsplit(".", 1)[1]
+            pre = name[: -len("qkv_proj." + kind)]
             q, k, v = torch.split(full, [c.num_heads * c.head_dim, c.num_kv_heads * c.head_dim,
                                          c.num_kv_heads * c.head_dim], 0)
-            out[pre + "q_proj.weight"], out[pre + "k_proj.weight"], out[pre + "v_proj.weight"] = q, k, v
+            out[f"{pre}q_proj.{kind}"], out[f"{pre}k_proj.{kind}"], out[f"{pre}v_proj.{kind}"] = q, k, v
         elif name.endswith("mlp.gate_up_proj.weight"):
             pre = name[: -len("gate_up_proj.weight")]
             g, u = full.chunk(2, 0)
@@ -140,9 +141,10 @@ def load_hf_state_dict(model, sd: dict[str, torch.Tensor]) -> None:
     with torch.no_grad():
         for sp, p in model.named_flat_params():
             name = sp.name
-            if name.endswith("self_attn.qkv_proj.weight"):
-                pre = name[: -len("qkv_proj.weight")]
-                full = torch.cat([sd[pre + "q_proj.weight"], sd[pre + "k_proj.weight"], sd[pre + "v_proj.weight"]], 0)
+            if name.endswith(("self_attn.qkv_proj.weight", "self_attn.qkv_proj.bias")):
+                kind = name.rsplit(".", 1)[1]
+                pre = name[: -len("qkv_proj." + kind)]
+                full = torch.cat([sd[f"{pre}q_proj.{kind}"], sd[f"{pre}k_proj.{kind}"], sd[f"{pre}v_proj.{kind}"]], 0)
             elif name.endswith("mlp.gate_up_proj.weight"):
                 pre = name[: -len("gate_up_proj.weight")]
                 full = torch.cat([sd[pre + "gate_proj.weight"], sd[pre + "up_proj.weight"]], 0)
@@ -297,7 +299,7 @@ def load_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional
 def _merge_tp(model, name: str, parts: list[torch.Tensor], dim: int) -> torch.Tensor:
     c = model.cfg
     n = len(parts)
-    if name.endswith("qkv_proj.weight"):
+    if name.endswith(("qkv_proj.weight", "qkv_proj.bias")):
         hd = c.head_dim
         sizes = [c.num_heads * hd // n, c.num_kv_heads * hd // n, c.num_kv_heads * hd // n]
         qs, ks, vs = zip(*[torch.split(p, sizes, 0) for p in parts])

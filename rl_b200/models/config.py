@@ -33,6 +33,7 @@ class ModelConfig:
     max_position_embeddings: int = 4096
     tie_word_embeddings: bool = False
     qk_norm: bool = False
+    attention_bias: bool = False  # biases on the q / k / v projections (Qwen2)
     # Mixture of experts (0 experts = dense MLP)
     num_experts: int = 0
     moe_top_k: int = 0
@@ -99,6 +100,7 @@ class ModelConfig:
             max_position_embeddings=hf.get("max_position_embeddings", 4096),
             tie_word_embeddings=bool(hf.get("tie_word_embeddings", False)),
             qk_norm="qwen3" in arch or hf.get("model_type", "").startswith("qwen3"),
+            attention_bias=bool(hf.get("attention_bias", hf.get("model_type", "") == "qwen2" or "qwen2" in arch)),
             num_experts=n_exp,
             moe_top_k=hf.get("num_experts_per_tok", 0) or 0,
             moe_ffn_hidden_size=hf.get("moe_intermediate_size", 0) or 0,
@@ -122,6 +124,8 @@ class ModelConfig:
             "tie_word_embeddings": self.tie_word_embeddings,
             "torch_dtype": "bfloat16",
         }
+        if self.attention_bias:
+            d["attention_bias"] = True
         if self.is_moe:
             d.update({"architectures": ["Qwen3MoeForCausalLM"], "model_type": "qwen3_moe",
                       "num_experts": self.num_experts, "num_experts_per_tok": self.moe_top_k,
@@ -145,6 +149,13 @@ PRESETS: dict[str, ModelConfig] = {
                             num_kv_heads=2, head_dim=16, ffn_hidden_size=0, rope_theta=10000.0,
                             qk_norm=True, num_experts=8, moe_top_k=2, moe_ffn_hidden_size=48,
                             moe_aux_loss_coef=1e-3, max_position_embeddings=256),
+    "qwen2.5-1.5b": ModelConfig(name="qwen2.5-1.5b", vocab_size=151936, hidden_size=1536, num_layers=28,
+                                num_heads=12, num_kv_heads=2, head_dim=128, ffn_hidden_size=8960, rope_theta=1e6,
+                                rms_eps=1e-6, max_position_embeddings=32768, tie_word_embeddings=True,
+                                attention_bias=True),
+    "qwen2.5-7b": ModelConfig(name="qwen2.5-7b", vocab_size=152064, hidden_size=3584, num_layers=28, num_heads=28,
+                              num_kv_heads=4, head_dim=128, ffn_hidden_size=18944, rope_theta=1e6, rms_eps=1e-6,
+                              max_position_embeddings=131072, attention_bias=True),
     "llama3.1-8b": ModelConfig(name="llama3.1-8b", vocab_size=128256, hidden_size=4096, num_layers=32,
                                num_heads=32, num_kv_heads=8, head_dim=128, ffn_hidden_size=14336,
                                rope_theta=500000.0, rope_scaling=dict(_LLAMA31_ROPE), rms_eps=1e-5,
@@ -170,6 +181,8 @@ def get_model_config(name_or_cfg, **overrides) -> ModelConfig:
             "meta-llama/llama-3.1-8b-instruct": "llama3.1-8b",
             "meta-llama/llama-3.1-8b": "llama3.1-8b",
             "qwen/qwen3-30b-a3b": "qwen3-30b-a3b",
+            "qwen/qwen2.5-1.5b": "qwen2.5-1.5b",
+            "qwen/qwen2.5-7b": "qwen2.5-7b",
             "qwen/qwen3-32b": "qwen3-32b",
         }
         key = aliases.get(key, key)

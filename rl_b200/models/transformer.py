@@ -245,6 +245,9 @@ class TransformerLM(nn.Module):
             p = f"model.layers.{i}."
             s.append(ParamSpec(p + "input_layernorm.weight", (H,), "ones", no_weight_decay=True))
             s.append(ParamSpec(p + "self_attn.qkv_proj.weight", ((self.nq + 2 * self.nkv) * hd, H), "normal", tp_dim=0))
+            if c.attention_bias:
+                s.append(ParamSpec(p + "self_attn.qkv_proj.bias", ((self.nq + 2 * self.nkv) * hd,), "zeros", tp_dim=0,
+                                   no_weight_decay=True))
             if c.qk_norm:
                 s.append(ParamSpec(p + "self_attn.q_norm.weight", (hd,), "ones", no_weight_decay=True))
                 s.append(ParamSpec(p + "self_attn.k_norm.weight", (hd,), "ones", no_weight_decay=True))
@@ -333,7 +336,7 @@ class TransformerLM(nn.Module):
         fused layouts (QKV rows are [q heads | k heads | v heads]; gate/up rows are
         [gate | up]) so that every shard holds matching heads / FFN columns."""
         c = self.cfg
-        if sp.name.endswith("qkv_proj.weight"):
+        if sp.name.endswith(("qkv_proj.weight", "qkv_proj.bias")):
             hd = c.head_dim
             q, k, v = torch.split(full, [c.num_heads * hd, c.num_kv_heads * hd, c.num_kv_heads * hd], 0)
             return torch.cat([q.chunk(n, 0)[idx], k.chunk(n, 0)[idx], v.chunk(n, 0)[idx]], 0)
@@ -379,6 +382,8 @@ class TransformerLM(nn.Module):
         p = f"model.layers.{i}."
         if qkv is None:
             qkv = self._col_linear(h, p + "self_attn.qkv_proj.weight")
+        if self.cfg.attention_bias:
+            qkv = qkv + self._params[p + "self_attn.qkv_proj.bias"].to(qkv.dtype)
         if self.cfg.qk_norm:
             T = qkv.shape[0]
             q, k, v = torch.split(qkv, [self.nq * self.hd, self.nkv * self.hd, self.nkv * self.hd], -1)

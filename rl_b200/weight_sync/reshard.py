@@ -82,6 +82,9 @@ def build_regions(train_specs, gen_specs, cfg, t: int, g: int, tp_rank: int) -> 
         if gs.tp_dim is None or t == 1:
             out.append(Region(gs.name, tp_rank, ts.offset, tshape[1], gs.offset, C, R, C, 0, 0, R, C, gs.offset))
             continue
+        if gs.tp_dim is not None and len(gs.shape) != 2:
+            raise NotImplementedError(f"{gs.name}: a tensor-parallel 1-D parameter (attention bias) needs the "
+                                      "rollout TP to equal the training TP")
         if gs.tp_dim == 0:
             full_rows = tshape[0] * t
             sec = _sections(gs.name, cfg, full_rows)

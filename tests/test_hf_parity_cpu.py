@@ -30,27 +30,36 @@ def _hf_model(kind: str, rope_scaling):
     if kind == "llama":
         cfg = transformers.LlamaConfig(**common)
         model = transformers.LlamaForCausalLM(cfg)
+    elif kind == "qwen2":
+        common.pop("attention_bias")
+        common.pop("head_dim")
+        cfg = transformers.Qwen2Config(**common)
+        model = transformers.Qwen2ForCausalLM(cfg)
+        with torch.no_grad():  # random (not zero) q / k / v biases
+            for layer in model.model.layers:
+                for proj in (layer.self_attn.q_proj, layer.self_attn.k_proj, layer.self_attn.v_proj):
+                    proj.bias.normal_(0, 0.5)
     else:
         cfg = transformers.Qwen3Config(**common)
         model = transformers.Qwen3ForCausalLM(cfg)
     return model.float().eval()
 
 
-def _mine(kind: str, rope_scaling, sd):
+def _mine(kind: str, rope_scaling, sd, ps=None):
     cfg = ModelConfig(name="t", vocab_size=256, hidden_size=64, num_layers=2, num_heads=4, num_kv_heads=2,
                       head_dim=16, ffn_hidden_size=96, rope_theta=10000.0, rms_eps=1e-6, max_position_embeddings=256,
-                      qk_norm=(kind == "qwen3"))
+                      qk_norm=(kind == "qwen3"), attention_bias=(kind == "qwen2"))
     if rope_scaling is not None:
         cfg = apply_hf_config_overrides(cfg, {"rope_scaling": dict(rope_scaling)})
-    m = TransformerLM(cfg, device=torch.device("cpu"), dtype=torch.float32)
+    m = TransformerLM(cfg, ps, device=torch.device("cpu"), dtype=torch.float32)
     load_hf_state_dict(m, sd)
     return m
 
 
-@pytest.mark.parametrize("kind", ["llama", "qwen3"])
+@pytest.mark.parametrize("kind", ["llama", "qwen2", "qwen3"])
 @pytest.mark.parametrize("scaling", [None, LLAMA3, YARN], ids=["default", "llama3", "yarn"])
 def test_logits_match_hf(kind, scaling):
-    if kind == "qwen3" and scaling is LLAMA3:
+    if kind != "llama" and scaling is LLAMA3:
         pytest.skip("Llama-3.1 scaling belongs to Llama checkpoints")
     hf = _hf_model(kind, scaling)
     sd = {k: v.detach().clone() for k, v in hf.state_dict().items()}
@@ -112,3 +121,36 @@ def test_worker_applies_overrides():
     w = PolicyWorker(cfg, model_cfg=TINY, seed=3)
     assert w.model.rope_cache.shape[0] >= 512 and w.model_cfg.rope_scaling["rope_type"] == "yarn"
     assert w.gen_model.rope_cache is w.model.rope_cache or torch.equal(w.gen_model.rope_cache, w.model.rope_cache)
+
+
+def _tp2_qwen2(rank):
+    """Qwen2 (q / k / v biases) at TP=2: logits gathered over the vocab shards
+    equal HF's, and the HF state dict round-trips through the TP shards."""
+    import torch.distributed as dist
+
+    from rl_b200.models.checkpoint_io import hf_state_dict
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(tp=2, backend="gloo")
+    hf = _hf_model("qwen2", None)
+    sd = {k: v.detach().clone() for k, v in hf.state_dict().items()}
+    mine = _mine("qwen2", None, sd, ps)
+    ids = torch.randint(0, 256, (40,), generator=torch.Generator().manual_seed(2))
+    with torch.no_grad():
+        ref = hf(ids.view(1, -1)).logits[0]
+        h = mine(ids, torch.arange(40), torch.tensor([0, 40], dtype=torch.int32), 40)
+        loc = mine.logits(h)
+        parts = [torch.empty_like(loc) for _ in range(2)]
+        dist.all_gather(parts, loc.contiguous(), group=ps.tp_group)
+    back = hf_state_dict(mine, dtype=None)
+    same = all(torch.equal(back[k], sd[k]) for k in sd if k in back)
+    return {"err": float((torch.cat(parts, -1) - ref).abs().max()), "roundtrip": same,
+            "bias_keys": sorted(k for k in back if k.endswith("q_proj.bias"))}
+
+
+def test_qwen2_tp2_matches_hf():
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(_tp2_qwen2, 2)
+    for o in outs:
+        assert o["err"] < 2e-4 and o["roundtrip"] and len(o["bias_keys"]) == 2, o

@@ -102,6 +102,10 @@ class PolicyWorker:
         if self.device.type == "cpu" and self.dtype != torch.float32:
             self.dtype = torch.float32
         mc = policy_cfg.get("megatron_cfg", {}) or {}
+        uneven = {k: int(mc[k]) for k in ("num_layers_in_first_pipeline_stage", "num_layers_in_last_pipeline_stage")
+                  if mc.get(k) is not None}
+        if uneven:
+            self.model_cfg = self.model_cfg.replace(extra={**self.model_cfg.extra, **uneven})
         self.sequence_parallel = bool(mc.get("sequence_parallel", False)) and self.ps.tp_size > 1
         act_ckpt = bool(mc.get("activation_checkpointing", policy_cfg.get("activation_checkpointing", False)))
         self.num_labels = int(policy_cfg.get("num_labels", 0) or 0)  # > 0: value / reward model

@@ -49,9 +49,30 @@ from rl_b200.parallel.state import ParallelState, single_process_state
 __all__ = ["TransformerLM", "ParamSpec", "KVCache", "stage_layers"]
 
 
-def stage_layers(num_layers: int, pp: int, rank: int) -> range:
-    """Contiguous, balanced layer range of pipeline stage ``rank`` (earlier stages
-    take the remainder)."""
+def stage_layers(num_layers: int, pp: int, rank: int, first: Optional[int] = None,
+                 last: Optional[int] = None) -> range:
+    """Contiguous layer range of pipeline stage ``rank``.  ``first`` / ``last``
+    fix the layer counts of the first / last stage (Megatron's
+    ``num_layers_in_first_pipeline_stage`` / ``..._last_...``: the embedding
+    and the LM head make those stages heavier); the other stages split the rest
+    evenly, which must divide.  Without them the split is balanced, earlier
+    stages taking the remainder."""
+    if pp > 1 and (first is not None or last is not None):
+        f = int(first) if first is not None else None
+        l_ = int(last) if last is not None else None
+        inner = pp - (f is not None) - (l_ is not None)
+        rest = num_layers - (f or 0) - (l_ or 0)
+        if rest < 0 or (inner == 0 and rest != 0) or (inner > 0 and rest % inner):
+            raise ValueError(f"{num_layers} layers cannot be split over {pp} stages with {f} in the first and "
+                             f"{l_} in the last stage (the other stages must divide the rest evenly)")
+        mid = rest // inner if inner else 0
+        sizes = [mid] * pp
+        if f is not None:
+            sizes[0] = f
+        if l_ is not None:
+            sizes[-1] = l_
+        start = sum(sizes[:rank])
+        return range(start, start + sizes[rank])
     base, extra = divmod(num_layers, pp)
     start = rank * base + min(rank, extra)
     return range(start, start + base + (1 if rank < extra else 0))
@@ -194,7 +215,9 @@ class TransformerLM(nn.Module):
         # pipeline parallelism: this rank's contiguous range of layers; the first
         # stage owns the embedding, the last the final norm and the LM / value head
         self.pp_size, self.pp_rank = self.ps.pp_size, self.ps.pp_rank
-        self.layer_range = stage_layers(cfg.num_layers, self.pp_size, self.pp_rank)
+        self.layer_range = stage_layers(cfg.num_layers, self.pp_size, self.pp_rank,
+                                        cfg.extra.get("num_layers_in_first_pipeline_stage"),
+                                        cfg.extra.get("num_layers_in_last_pipeline_stage"))
         self.is_first_stage = self.pp_rank == 0
         self.is_last_stage = self.pp_rank == self.pp_size - 1
         if self.pp_size > 1 and cfg.tie_word_embeddings:

@@ -38,16 +38,19 @@ def _pcfg(sp: bool):
 
 
 def case_train_step(rank: int, tp: int, ep: int, sp: bool, moe: bool, cp: int = 1, pp: int = 1,
-                    muon: Optional[dict] = None):
+                    muon: Optional[dict] = None, mc_extra: Optional[dict] = None, num_layers: Optional[int] = None):
     from rl_b200.models.policy.worker import PolicyWorker
     from rl_b200.parallel.state import init_distributed
 
     torch.manual_seed(0)
     ps = init_distributed(tp=tp, ep=ep, cp=cp, pp=pp, backend="gloo")
     cfg = TINY_MOE if moe else TINY
+    if num_layers is not None:
+        cfg = cfg.replace(num_layers=num_layers)
     pcfg = _pcfg(sp)
     if muon is not None:
         pcfg["megatron_cfg"]["optimizer"] = dict(muon)
+    pcfg["megatron_cfg"].update(mc_extra or {})
     w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=3)
     full = make_batch()
     B = full.size

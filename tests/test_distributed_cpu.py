@@ -105,3 +105,21 @@ def test_schedule_1f1b_order():
                     peak = max(peak, live)
                     assert k == "F" or ("F", i) in acts[:acts.index((k, i))]
                 assert peak <= min(S - s, M)
+
+
+def test_uneven_pipeline_stages():
+    """``num_layers_in_first/last_pipeline_stage``: 5 layers as 1 | 2 | 2 and
+    3 | 2 over 3 / 2 stages train like the single-process model."""
+    from rl_b200.models.transformer import stage_layers
+
+    assert [list(stage_layers(5, 3, r, first=1)) for r in range(3)] == [[0], [1, 2], [3, 4]]
+    assert [list(stage_layers(5, 2, r, first=3)) for r in range(2)] == [[0, 1, 2], [3, 4]]
+    assert [list(stage_layers(8, 3, r, first=2, last=2)) for r in range(3)] == [[0, 1], [2, 3, 4, 5], [6, 7]]
+    with pytest.raises(ValueError):
+        stage_layers(6, 3, 0, first=1)  # 5 layers left for 2 stages
+    single = spawn_ranks(case_train_step, 1, 1, 1, False, False, 1, 1, None, None, 5)[0]
+    for world, extra in [(3, {"num_layers_in_first_pipeline_stage": 1}),
+                         (2, {"num_layers_in_first_pipeline_stage": 3})]:
+        outs = spawn_ranks(case_train_step, world, 1, 1, False, False, 1, world, None, extra, 5)
+        for o in outs:
+            _close(o, single)

@@ -102,8 +102,8 @@ class PolicyWorker:
         if self.device.type == "cpu" and self.dtype != torch.float32:
             self.dtype = torch.float32
         mc = policy_cfg.get("megatron_cfg", {}) or {}
-        uneven = {k: int(mc[k]) for k in ("num_layers_in_first_pipeline_stage", "num_layers_in_last_pipeline_stage")
-                  if mc.get(k) is not None}
+        uneven = {k: int(mc[k]) for k in ("num_layers_in_first_pipeline_stage", "num_layers_in_last_pipeline_stage",
+                                          "virtual_pipeline_model_parallel_size") if mc.get(k) is not None}
         if uneven:
             self.model_cfg = self.model_cfg.replace(extra={**self.model_cfg.extra, **uneven})
         self.sequence_parallel = bool(mc.get("sequence_parallel", False)) and self.ps.tp_size > 1
@@ -495,15 +495,22 @@ class PolicyWorker:
         """Forward-only pass of ``plan`` through the pipeline; ``fn(rows, out)``
         consumes the last stage's output of each (non-dummy) micro-batch."""
         comm = self._pp_comm
-        for rows in plan:
-            dummy = rows[0] < 0
-            rows = [-1 - rows[0]] if dummy else rows
-            self._pp_in = comm.recv_forward(self._pp_shape(ids, lengths, rows), self.dtype, self.device) \
-                if not self.model.is_first_stage else None
-            out = fn(rows, dummy)
-            self._pp_in = None
-            if not self.model.is_last_stage:
-                comm.send_forward(out)
+        V = self.model.vpp
+        for v in range(V):  # virtual pipeline: every micro-batch through chunk v, then chunk v + 1
+            self.model.chunk = v if V > 1 else None
+            for rows in plan:
+                dummy = rows[0] < 0
+                rows = [-1 - rows[0]] if dummy else rows
+                if self.model.is_first_stage:
+                    self._pp_in = None
+                else:
+                    self._pp_in = torch.empty(self._pp_shape(ids, lengths, rows), dtype=self.dtype, device=self.device)
+                    dist.recv(self._pp_in, comm.prev_wrap, group=comm.group)
+                out = fn(rows, dummy)
+                self._pp_in = None
+                if not self.model.is_last_stage:
+                    comm._send(out, comm.next_wrap)
+        self.model.chunk = None
         comm.wait()
 
     def _pp_broadcast(self, t: torch.Tensor) -> torch.Tensor:
@@ -859,8 +866,21 @@ class PolicyWorker:
             rows = [-1 - rows[0]] if rows[0] < 0 else rows
             return self._pp_shape(st.ids, st.lengths, rows)
 
-        one_f_one_b(self._pp_comm, st.num_microbatches, fwd, shape, self.dtype, self.device,
-                    backward=not st.eval_mode)
+        if self.model.vpp > 1:
+            from rl_b200.parallel.pipeline import virtual_pipeline
+
+            def vfwd(i, v, hidden_in):
+                self.model.chunk = v
+                return fwd(i, hidden_in)
+
+            try:
+                virtual_pipeline(self._pp_comm, st.num_microbatches, self.model.vpp, vfwd, shape, self.dtype,
+                                 self.device, backward=not st.eval_mode)
+            finally:
+                self.model.chunk = None
+        else:
+            one_f_one_b(self._pp_comm, st.num_microbatches, fwd, shape, self.dtype, self.device,
+                        backward=not st.eval_mode)
         if not st.eval_mode:
             self.optimizer._fold_param_grads()
 

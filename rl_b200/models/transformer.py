@@ -215,11 +215,26 @@ class TransformerLM(nn.Module):
         # pipeline parallelism: this rank's contiguous range of layers; the first
         # stage owns the embedding, the last the final norm and the LM / value head
         self.pp_size, self.pp_rank = self.ps.pp_size, self.ps.pp_rank
-        self.layer_range = stage_layers(cfg.num_layers, self.pp_size, self.pp_rank,
-                                        cfg.extra.get("num_layers_in_first_pipeline_stage"),
-                                        cfg.extra.get("num_layers_in_last_pipeline_stage"))
-        self.is_first_stage = self.pp_rank == 0
-        self.is_last_stage = self.pp_rank == self.pp_size - 1
+        # virtual pipeline (interleaved layer assignment): the model is cut into
+        # pp * vpp chunks and rank r holds chunks r, r + pp, r + 2 pp, ...; the
+        # schedule sets ``chunk`` to the one running (None: the rank as a whole)
+        self.vpp = int(cfg.extra.get("virtual_pipeline_model_parallel_size") or 1) if self.pp_size > 1 else 1
+        self.chunk: Optional[int] = None
+        if self.vpp > 1:
+            if cfg.extra.get("num_layers_in_first_pipeline_stage") is not None or \
+                    cfg.extra.get("num_layers_in_last_pipeline_stage") is not None:
+                raise NotImplementedError("uneven first / last stages with a virtual pipeline")
+            if cfg.is_moe:
+                raise NotImplementedError("virtual pipeline stages for MoE models")
+            self.chunk_ranges = [stage_layers(cfg.num_layers, self.pp_size * self.vpp, v * self.pp_size + self.pp_rank)
+                                 for v in range(self.vpp)]
+            self.layer_range = [i for r in self.chunk_ranges for i in r]
+        else:
+            self.layer_range = stage_layers(cfg.num_layers, self.pp_size, self.pp_rank,
+                                            cfg.extra.get("num_layers_in_first_pipeline_stage"),
+                                            cfg.extra.get("num_layers_in_last_pipeline_stage"))
+        self._owns_embed = self.pp_rank == 0
+        self._owns_head = self.pp_rank == self.pp_size - 1
         if self.pp_size > 1 and cfg.tie_word_embeddings:
             raise NotImplementedError("tied embeddings under pipeline parallelism")
         self.specs = self._make_specs()
@@ -714,6 +729,16 @@ class TransformerLM(nn.Module):
         m = self._mlp_block(i, h2)
         return s2, m
 
+    @property
+    def is_first_stage(self) -> bool:
+        """Runs the embedding: the first rank (its first chunk under a virtual pipeline)."""
+        return self._owns_embed and (self.chunk is None or self.chunk == 0)
+
+    @property
+    def is_last_stage(self) -> bool:
+        """Runs the final norm and head: the last rank (its last chunk under a virtual pipeline)."""
+        return self._owns_head and (self.chunk is None or self.chunk == self.vpp - 1)
+
     def forward(self, input_ids: torch.Tensor, positions: torch.Tensor, cu_seqlens: torch.Tensor,
                 max_seqlen: int, hidden_in: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Packed forward: ``input_ids [T]`` -> final-norm hidden ``[T(/tp if SP), H]``.
@@ -722,7 +747,8 @@ class TransformerLM(nn.Module):
         self._aux_losses = []
         x = self.embed(input_ids) if self.is_first_stage else hidden_in
         resid = None
-        for i in self.layer_range:
+        layers = self.chunk_ranges[self.chunk] if (self.vpp > 1 and self.chunk is not None) else self.layer_range
+        for i in layers:
             if self.activation_checkpointing and torch.is_grad_enabled():
                 if resid is None:
                     x, resid = ckpt.checkpoint(self._layer, i, x, None, positions, cu_seqlens, max_seqlen,

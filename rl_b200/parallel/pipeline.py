@@ -31,7 +31,7 @@ from typing import Callable, Optional
 import torch
 import torch.distributed as dist
 
-__all__ = ["PipelineComm", "one_f_one_b", "schedule_1f1b"]
+__all__ = ["PipelineComm", "one_f_one_b", "schedule_1f1b", "virtual_pipeline"]
 
 
 class PipelineComm:
@@ -44,6 +44,9 @@ class PipelineComm:
         self.group = ps.pp_group
         self.prev = ps.pp_ranks[self.stage - 1] if self.stage > 0 else None
         self.next = ps.pp_ranks[self.stage + 1] if self.stage + 1 < self.n else None
+        # virtual pipeline: chunk v of the last rank feeds chunk v + 1 of the first
+        self.prev_wrap = ps.pp_ranks[(self.stage - 1) % self.n]
+        self.next_wrap = ps.pp_ranks[(self.stage + 1) % self.n]
         self._pending: list = []  # (work, tensor kept alive until the send completed)
 
     def _send(self, t: torch.Tensor, dst: int) -> None:
@@ -127,3 +130,54 @@ def one_f_one_b(comm: PipelineComm, num_microbatches: int, forward: Callable[[in
                 comm.send_backward(inp.grad)
             del inp, out
     comm.wait()
+
+
+def virtual_pipeline(comm: PipelineComm, num_microbatches: int, num_chunks: int,
+                     forward: Callable[[int, int, Optional[torch.Tensor]], torch.Tensor],
+                     in_shape: Callable[[int], tuple], dtype: torch.dtype, device: torch.device,
+                     backward: bool = True) -> None:
+    """Micro-batches through ``num_chunks`` model chunks per rank (virtual
+    stage ``v * S + s`` is chunk ``v`` of rank ``s``; the last rank's chunk
+    ``v`` feeds the first rank's chunk ``v + 1``).  Every rank runs all
+    forwards chunk by chunk, then all backwards in reverse chunk order: each
+    rank's order is a topological order of the virtual stages' dependencies and
+    every rank pair exchanges messages in the order both sides expect, so the
+    blocking receives never wait on a later send.  ``forward(i, v, hidden_in)``
+    returns chunk ``v``'s output (the scalar loss on the last virtual stage).
+
+    Reference: Megatron's interleaved schedule behind
+    ``virtual_pipeline_model_parallel_size``; this order keeps every
+    micro-batch's activations until the backward phase (GPipe memory) in
+    exchange for a schedule without per-step coordination."""
+    S, s, V, M = comm.n, comm.stage, num_chunks, num_microbatches
+    live: dict = {}
+    for v in range(V):
+        first, last = s == 0 and v == 0, s == S - 1 and v == V - 1
+        for i in range(M):
+            inp = None
+            if not first:
+                inp = torch.empty(in_shape(i), dtype=dtype, device=device)
+                dist.recv(inp, comm.prev_wrap, group=comm.group)
+                if backward:
+                    inp.requires_grad_(True)
+            out = forward(i, v, inp)
+            if not last:
+                comm._send(out.detach(), comm.next_wrap)
+            if backward:
+                live[(v, i)] = (inp, out)
+    if backward:
+        for v in reversed(range(V)):
+            first, last = s == 0 and v == 0, s == S - 1 and v == V - 1
+            for i in range(M):
+                inp, out = live.pop((v, i))
+                if last:
+                    out.backward()
+                else:
+                    g = torch.empty(out.shape, dtype=out.dtype, device=device)
+                    dist.recv(g, comm.next_wrap, group=comm.group)
+                    torch.autograd.backward(out, g)
+                if not first:
+                    comm._send(inp.grad, comm.prev_wrap)
+                del inp, out
+    comm.wait()
+

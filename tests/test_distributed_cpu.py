@@ -123,3 +123,15 @@ def test_uneven_pipeline_stages():
         outs = spawn_ranks(case_train_step, world, 1, 1, False, False, 1, world, None, extra, 5)
         for o in outs:
             _close(o, single)
+
+
+@pytest.mark.parametrize("world,layers", [(2, 4), (3, 6)])
+def test_virtual_pipeline_matches_single(world, layers):
+    """``virtual_pipeline_model_parallel_size: 2``: each rank holds two
+    interleaved layer chunks (rank r: chunks r and r + pp); training step and
+    log-probs equal the single-process run."""
+    single = spawn_ranks(case_train_step, 1, 1, 1, False, False, 1, 1, None, None, layers)[0]
+    outs = spawn_ranks(case_train_step, world, 1, 1, False, False, 1, world, None,
+                       {"virtual_pipeline_model_parallel_size": 2}, layers)
+    for o in outs:
+        _close(o, single)

@@ -66,22 +66,30 @@ def parse():
 
 
 def reference_arm(args) -> None:
+    """Run the unmodified reference from ``baseline/_ref`` through its public GRPO entry
+    point when it imports; otherwise print why it cannot run, as one ``unavailable`` line."""
     why = None
     ref = os.path.join(ROOT, "baseline", "_ref")
-    try:
+    if not os.path.isdir(os.path.join(ref, "nemo_rl")):
+        why = "reference not installed under baseline/_ref (the folder holds no nemo_rl package)"
+    else:
         sys.path.insert(0, ref)
-        import nemo_rl  # noqa: F401
-
+        missing = []
+        for mod in ("ray", "megatron.core", "vllm"):
+            try:
+                __import__(mod)
+            except Exception as e:  # noqa: BLE001
+                missing.append(f"{mod} ({type(e).__name__})")
         try:
             import nemo_rl.algorithms.grpo  # noqa: F401
         except Exception as e:  # noqa: BLE001
-            why = (f"reference GRPO not importable from baseline/_ref ({type(e).__name__}: {e}); its install "
-                   "carries only the top-level nemo_rl package and its GRPO path needs ray + Megatron-Core/"
-                   "Automodel, none of which are in this image or the offline wheelhouse")
-    except Exception as e:  # noqa: BLE001
-        why = f"reference not installed under baseline/_ref ({type(e).__name__}: {e})"
+            why = (f"reference GRPO not importable from baseline/_ref ({type(e).__name__}: {e}); the offline "
+                   f"install carries only the top-level nemo_rl package, and its GRPO driver also needs "
+                   f"{', '.join(missing) or 'its Ray worker groups'}, which are not in this image or wheelhouse")
+        if why is None and missing:
+            why = f"reference GRPO imported but its Ray-based driver cannot start: missing {', '.join(missing)}"
     if why is None:
-        why = "reference imported but its Ray-based driver cannot start without the ray package"
+        why = "reference imported but no GPU launcher for its Ray single controller exists in this image"
     if int(os.environ.get("RANK", "0")) == 0:
         print(json.dumps({"impl": "reference", "unavailable": why}), flush=True)
 
@@ -251,7 +259,15 @@ def main():
                        "activation_checkpointing": pcfg["megatron_cfg"]["activation_checkpointing"], "prompts_per_step": prompts_global,
                        "generations_per_prompt": G, "max_new_tokens": args.max_new, "kl_penalty": args.kl,
                        "l2": "working set (16 GB bf16 weights + KV cache) far above the 126 MB L2; no flush needed",
-                       "mean_gen_tokens": gen_tokens / max(1, len(timed)) / (prompts_global * G)},
+                       "mean_gen_tokens": gen_tokens / max(1, len(timed)) / (prompts_global * G),
+                       # one optimizer step per rollout batch: the "previous policy" logprobs equal the
+                       # training forward's own, so that separate pass is folded into training
+                       "prev_logprobs_from_train_forward": bool(cfg["grpo"].get("reuse_train_logprobs_as_prev", True)),
+                       "reference_logprobs_pass": args.kl > 0,
+                       "refit_kind": ("in-place: rollout reads the trained bf16 weights (same TP layout)"
+                                      if (args.gen_tp or tp) == tp else
+                                      f"reshard TP{tp}->TP{args.gen_tp} over NVLink peer loads"),
+                       "eos_ignored": True},
             "e2e": {"value": round(tokens / wall, 2), "unit": "tokens/s",
                     "h2d_bytes_per_step": int(prompt_bytes), "d2h_bytes_per_step": 4 * len(timed) // max(1, len(timed))},
             "gpu_launches": int(launches),
@@ -266,23 +282,25 @@ def main():
 
 
 def shutdown(worker) -> None:
-    """Tear down in an order that cannot hang: CUDA graphs that captured NCCL
-    collectives are released before the process group, and a watchdog ends the
-    process if teardown still stalls (the result line is already printed)."""
+    """Tear down in an order that cannot hang, then return so the interpreter exits
+    normally (its exit handlers run).  CUDA graphs that captured NCCL collectives are
+    released before the process group.  A daemon watchdog ends the process only if
+    teardown itself stalls; the result line is printed before this runs."""
     import gc
-    import threading
 
     import torch
     import torch.distributed as dist
 
-    threading.Timer(90.0, lambda: os._exit(0)).start()
+    watchdog = threading.Timer(120.0, lambda: os._exit(3))
+    watchdog.daemon = True
+    watchdog.start()
     worker.shutdown()
     gc.collect()
     torch.cuda.synchronize()
     if dist.is_initialized():
         dist.barrier()
         dist.destroy_process_group()
-    os._exit(0)
+    watchdog.cancel()
 
 
 def iter_epochs(dl):

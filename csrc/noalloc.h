@@ -44,6 +44,15 @@ extern "C" {
 // scratch array (cudaGetSymbolAddress, with the caller's current device) and
 // caches it; make that first call before any stream capture.  The caller must
 // have the device that owns the pointers current.
+//
+// When the array is placed on a device: with CUDA's lazy module loading (the
+// default since CUDA 12.2) the library's device code, and with it this 4 MiB
+// array, is loaded onto a device at its first use there - the first call of
+// this function on that device, not the load of the library.  A host runtime
+// that reserves all free device memory for its own pool should therefore make
+// one call (any valid size) on each device BEFORE reserving that pool;
+// otherwise the first call can fail with an out-of-memory error.  Later calls
+// on the same device allocate nothing.
 int rlb_rmsnorm_bwd_noalloc(const void* dy, const void* x, const void* w, const float* rstd, void* dx, float* dw,
                             int rows, int hidden, cudaStream_t stream);
 

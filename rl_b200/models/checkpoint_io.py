@@ -254,9 +254,18 @@ def load_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional
     world = dist.get_world_size() if dist.is_initialized() else 1
     same = (meta["world_size"] == world and meta["tp"] == ps.tp_size and meta["ep"] == ps.ep_size
             and meta.get("pp", 1) == ps.pp_size)
+    mine = [{"name": sp.name, "shape": list(sp.shape), "tp_dim": sp.tp_dim, "ep_dim": sp.ep_dim,
+             "offset": sp.offset, "numel": sp.numel} for sp in model.specs]
+    sh = None
+    if same:
+        # the flat buffer is copied whole only when this rank's shard holds exactly the
+        # parameters, at exactly the offsets, that this rank's model holds: the same world
+        # and TP/EP/PP sizes can still place different layers on a rank (virtual pipeline
+        # chunks, uneven first / last stages)
+        sh = torch.load(os.path.join(it, f"__{rank}.pt"), map_location="cpu")
+        same = sh.get("params", meta["params"]) == mine and sh["flat_param"].numel() == model.flat_param.numel()
     with torch.no_grad():
         if same:
-            sh = torch.load(os.path.join(it, f"__{rank}.pt"), map_location="cpu")
             model.flat_param.copy_(sh["flat_param"].to(model.flat_param.device))
         else:
             # re-layout: rebuild full tensors from the saved shards, then re-slice

@@ -504,8 +504,8 @@ class PolicyWorker:
                 if self.model.is_first_stage:
                     self._pp_in = None
                 else:
-                    self._pp_in = torch.empty(self._pp_shape(ids, lengths, rows), dtype=self.dtype, device=self.device)
-                    dist.recv(self._pp_in, comm.prev_wrap, group=comm.group)
+                    self._pp_in = comm._recv(self._pp_shape(ids, lengths, rows), self.dtype, self.device,
+                                             comm.prev_wrap)
                 out = fn(rows, dummy)
                 self._pp_in = None
                 if not self.model.is_last_stage:

@@ -155,3 +155,41 @@ def case_data_plane(rank: int, port: int):
     ok = all(torch.equal(got[k], ref[k]) for k in ref.keys()) and got["names"][0] == f"r{1 - rank}-0"
     keys = dp.keys("train")
     return {"ok": ok, "keys": keys, "stats": dp.metrics()}
+
+
+def case_pp_edges(rank: int, pp: int):
+    """Directed pipeline edge groups of this rank, and a send/recv over each."""
+    from rl_b200.parallel.pipeline import PipelineComm
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(pp=pp, backend="gloo")
+    comm = PipelineComm(ps)
+    if comm.next is not None:
+        comm.send_forward(torch.full((3,), float(rank)))
+    got = comm.recv_forward((3,), torch.float32, torch.device("cpu")) if comm.prev is not None else None
+    comm.wait()
+    assert got is None or float(got[0]) == float(comm.prev)
+    return {"rank": rank, "pp_ranks": list(ps.pp_ranks), "edges": sorted(ps.pp_edge_groups)}
+
+
+def case_ckpt_relayout_vpp(rank: int, pp: int, path: str, vpp_save: int, vpp_load: int):
+    """Save a sharded checkpoint under one virtual-pipeline setting and load it under
+    another (same world / TP / PP sizes, different layers per rank)."""
+    import torch.distributed as dist
+
+    from rl_b200.models.checkpoint_io import load_dist_checkpoint, save_dist_checkpoint
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.parallel.state import init_distributed
+
+    ps = init_distributed(pp=pp, backend="gloo")
+    base = TINY.replace(num_layers=4)
+    cfg_s = base.replace(extra={"virtual_pipeline_model_parallel_size": vpp_save})
+    cfg_l = base.replace(extra={"virtual_pipeline_model_parallel_size": vpp_load})
+    m_s = TransformerLM(cfg_s, ps, dtype=torch.float32, seed=5)
+    save_dist_checkpoint(m_s, None, path, None)
+    dist.barrier()
+    m_l = TransformerLM(cfg_l, ps, dtype=torch.float32, seed=77)
+    load_dist_checkpoint(m_l, None, path, None)
+    saved = {sp.name: p.detach().clone() for sp, p in m_s.named_flat_params()}
+    loaded = {sp.name: p.detach().clone() for sp, p in m_l.named_flat_params()}
+    return {"saved": saved, "loaded": loaded}

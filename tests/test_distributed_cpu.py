@@ -107,6 +107,39 @@ def test_schedule_1f1b_order():
                 assert peak <= min(S - s, M)
 
 
+def test_pipeline_plans_cannot_deadlock_under_rendezvous():
+    """The plans finish when every send of a large message waits for its
+    receive (NCCL past its channel buffer) and each communicator runs its
+    point-to-point work in posting order.  With one communicator per rank PAIR
+    (both directions on one stream) 1F1B at two stages and the virtual schedule
+    deadlock; with one per direction (what PipelineComm uses) neither does."""
+    from rl_b200.parallel.pipeline import plan_1f1b, plan_virtual, simulate_rendezvous
+
+    for S in (2, 3, 4):
+        for M in (1, 2, 3, 5, 8):
+            plans = [plan_1f1b(S, s, M) for s in range(S)]
+            assert simulate_rendezvous(plans, directed=True), (S, M)
+            assert simulate_rendezvous([plan_1f1b(S, s, M, backward=False) for s in range(S)], directed=True)
+            for V in (2, 3):
+                vplans = [plan_virtual(S, s, M, V) for s in range(S)]
+                assert simulate_rendezvous(vplans, directed=True), (S, M, V)
+    # the hazard the directed edges remove
+    assert not simulate_rendezvous([plan_1f1b(2, s, 4) for s in range(2)], directed=False)
+    assert not simulate_rendezvous([plan_virtual(2, s, 4, 2) for s in range(2)], directed=False)
+
+
+def test_pipeline_edge_groups_are_directed():
+    """init_distributed builds one group per direction of every adjacent pair."""
+    from tests.dist_cases import case_pp_edges
+
+    outs = spawn_ranks(case_pp_edges, 4, 2)
+    for o in outs:
+        r, ring = o["rank"], o["pp_ranks"]
+        s = ring.index(r)
+        want = {(r, ring[(s + 1) % 2]), (ring[(s + 1) % 2], r)}
+        assert set(o["edges"]) == want, o
+
+
 def test_uneven_pipeline_stages():
     """``num_layers_in_first/last_pipeline_stage``: 5 layers as 1 | 2 | 2 and
     3 | 2 over 3 / 2 stages train like the single-process model."""
@@ -135,3 +168,19 @@ def test_virtual_pipeline_matches_single(world, layers):
                        {"virtual_pipeline_model_parallel_size": 2}, layers)
     for o in outs:
         _close(o, single)
+
+
+def test_dist_checkpoint_across_virtual_pipeline_settings(tmp_path):
+    """A checkpoint saved with two layer chunks per rank (rank 0 holds layers 0
+    and 2) loads under one chunk per rank (rank 0 holds layers 0 and 1): every
+    parameter arrives under its own name, not by flat-buffer position."""
+    from tests.dist_cases import case_ckpt_relayout_vpp
+
+    for vs, vl in ((2, 1), (1, 2)):
+        d = tmp_path / f"v{vs}{vl}"
+        outs = spawn_ranks(case_ckpt_relayout_vpp, 2, 2, str(d), vs, vl)
+        saved = {k: v for o in outs for k, v in o["saved"].items()}
+        loaded = {k: v for o in outs for k, v in o["loaded"].items()}
+        assert saved.keys() == loaded.keys()
+        for k in saved:
+            torch.testing.assert_close(loaded[k], saved[k], atol=0, rtol=0, msg=k)

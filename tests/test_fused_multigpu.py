@@ -554,10 +554,12 @@ def test_decode_allreduce_rmsnorm_2gpu():
         assert max(o["errs"]) < 1e-2, o["errs"]
 
 
-def case_pp_train(rank: int):
+def case_pp_train(rank: int, big: bool = False, vpp: int = 1):
     """PP=2 on 2 GPUs (NCCL send / recv between the stages, 1F1B schedule): one
     GRPO-loss training step and the log-probs after it against a single-GPU
-    worker of the same seed on the same batch."""
+    worker of the same seed on the same batch.  ``big`` makes every activation
+    message 16 MiB, above NCCL's 4 MiB channel buffer, so a send finishes only
+    once its receive runs; ``vpp`` > 1 runs the interleaved schedule."""
     import os
 
     import torch.distributed as dist
@@ -570,13 +572,15 @@ def case_pp_train(rank: int):
     from tests.dist_cases import make_batch
 
     ps = init_distributed(pp=2, backend="nccl", timeout_s=120)
-    cfg = ModelConfig(name="pp", vocab_size=1024, hidden_size=512, num_layers=4, num_heads=8, num_kv_heads=4,
-                      head_dim=64, ffn_hidden_size=1024, rope_theta=10000.0, max_position_embeddings=1024)
+    H, mb = (2048, 4096) if big else (512, 512)
+    cfg = ModelConfig(name="pp", vocab_size=1024, hidden_size=H, num_layers=4, num_heads=8, num_kv_heads=4,
+                      head_dim=H // 8, ffn_hidden_size=2 * H, rope_theta=10000.0, max_position_embeddings=1024)
     pcfg = {"max_total_sequence_length": 256, "precision": "bfloat16",
             "optimizer": {"kwargs": {"lr": 1e-4, "weight_decay": 0.01}},
             "generation": {"temperature": 1.0, "max_new_tokens": 4},
-            "sequence_packing": {"train_mb_tokens": 512, "logprob_mb_tokens": 512}}
-    batch = make_batch(B=16, S=200, vocab=1024)
+            "megatron_cfg": {"virtual_pipeline_model_parallel_size": vpp} if vpp > 1 else {},
+            "sequence_packing": {"train_mb_tokens": mb, "logprob_mb_tokens": mb}}
+    batch = make_batch(B=64 if big else 16, S=256 if big else 200, vocab=1024)
     loss_fn = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
     w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=11)
     res = w.train(batch, loss_fn, gbs=batch.size)
@@ -600,6 +604,22 @@ def test_pipeline_parallel_train_2gpu():
 
     outs = spawn_ranks(case_pp_train, 2, timeout_s=300)
     assert outs[0]["stage_layers"] == [0, 1] and outs[1]["stage_layers"] == [2, 3]
+    for o in outs:
+        (a, b), (g, h) = o["loss"], o["gn"]
+        assert abs(a - b) < 2e-2 * max(1.0, abs(b)), o
+        assert abs(g - h) < 3e-2 * h, o
+        assert o["lp_err"] < 0.15, o
+
+
+@pytest.mark.parametrize("vpp", [1, 2])
+def test_pipeline_parallel_large_messages_2gpu(vpp):
+    """16 MiB activations (above NCCL's channel buffer) through 1F1B and the
+    interleaved schedule finish within the process-group timeout and match the
+    single-GPU step."""
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    outs = spawn_ranks(case_pp_train, 2, True, vpp, timeout_s=300)
     for o in outs:
         (a, b), (g, h) = o["loss"], o["gn"]
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), o

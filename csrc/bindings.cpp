@@ -46,6 +46,9 @@ at::Tensor gemm_nt(at::Tensor a, at::Tensor b);
 int64_t gemm_error_flag(bool reset);
 void gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> recv_ptrs,
              std::vector<int64_t> flag_ptrs, std::vector<int64_t> ack_ptrs, int64_t me, int64_t epoch);
+// gemm_sm100.cu
+void gemm_sm100(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, bool accumulate, int64_t tile);
+int64_t gemm_sm100_error_flag(bool reset);
 // gemm_grouped.cu
 at::Tensor grouped_gemm_nt(at::Tensor x, at::Tensor w, at::Tensor offs);
 int64_t grouped_gemm_error_flag(bool reset);
@@ -114,6 +117,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_nt", &gemm_nt);
   m.def("gemm_error_flag", &gemm_error_flag, py::arg("reset") = false);
   m.def("gemm_rs", &gemm_rs);
+  m.def("gemm_sm100", &gemm_sm100, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("a_mn") = false,
+        py::arg("b_mn") = false, py::arg("accumulate") = false, py::arg("tile") = 0,
+        "tcgen05 GEMM out = op(a) op(b)^T; a [M,K] or [K,M] (a_mn), b [N,K] or [K,N] (b_mn); bf16 or fp32 (+=) out");
+  m.def("gemm_sm100_error_flag", &gemm_sm100_error_flag, py::arg("reset") = false);
   m.def("gemm_fp8", &gemm_fp8, py::arg("a"), py::arg("a_scale"), py::arg("b"), py::arg("b_scale"),
         py::arg("splits") = 0, "block-scaled e4m3 GEMM (1x128 activation, 128x128 weight fp32 scales) -> bf16");
   m.def("gemm_mxf8", &gemm_mxf8, py::arg("a"), py::arg("a_scale_t"), py::arg("b"), py::arg("b_scale_t"),

@@ -32,15 +32,33 @@ def _time(fn, reps: int = 10, warm: int = 3) -> float:
 
 
 def bench_gemm(M=8192, N=8192, K=4096):
+    """The three products of a linear layer on the tcgen05 kernel (1-CTA 128x256 and
+    2-CTA 256x256 tiles) against the library GEMM on the same operands."""
     from rl_b200.ops._ext import ext
 
     dev = torch.device("cuda")
-    a = torch.randn(M, K, device=dev).to(torch.bfloat16)
-    b = torch.randn(N, K, device=dev).to(torch.bfloat16)
-    t = _time(lambda: ext().gemm_nt(a, b))
-    tl = _time(lambda: torch.matmul(a, b.t()))
+    C = ext()
     fl = 2 * M * N * K
-    print(f"gemm_nt {M}x{N}x{K}: {t:.3f} ms {fl / t / 1e9:.1f} TFLOP/s | library {tl:.3f} ms {fl / tl / 1e9:.1f} TFLOP/s")
+    x = torch.randn(M, K, device=dev).to(torch.bfloat16)      # [M, K]
+    xt = torch.randn(K, M, device=dev).to(torch.bfloat16)     # [K, M]
+    w = torch.randn(N, K, device=dev).to(torch.bfloat16)      # [N, K]
+    wt = torch.randn(K, N, device=dev).to(torch.bfloat16)     # [K, N]
+    out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+    acc = torch.zeros(M, N, device=dev, dtype=torch.float32)
+    cases = [
+        ("nt (fprop)", x, w, False, False, out, False, lambda: torch.matmul(x, w.t())),
+        ("nn (dgrad)", x, wt, False, True, out, False, lambda: torch.matmul(x, wt)),
+        ("tn (wgrad)", xt, wt, True, True, out, False, lambda: torch.matmul(xt.t(), wt)),
+        ("tn += fp32", xt, wt, True, True, acc, True, lambda: acc.add_(torch.mm(xt.t(), wt, out_dtype=torch.float32))),
+    ]
+    for name, a, b, amn, bmn, o, add, lib in cases:
+        res = []
+        for tile in (1, 2):
+            t = _time(lambda: C.gemm_sm100(a, b, o, amn, bmn, add, tile))
+            res.append(f"{'1cta' if tile == 1 else '2cta'} {t:.3f} ms {fl / t / 1e9:.1f}")
+        tl = _time(lib)
+        print(f"gemm {name} {M}x{N}x{K}: " + " | ".join(res) + f" | library {tl:.3f} ms {fl / tl / 1e9:.1f} TFLOP/s")
+    assert C.gemm_sm100_error_flag(True) == 0
 
 
 def bench_decode(B=64, L=1024, nkv=8, G=4, hd=128, bs=256):

@@ -8,11 +8,20 @@ Three shapes of product cover a linear layer's forward and backward passes
 * ``mm_tn(a [M,N], b [M,K]) = a^T @ b``  (weight gradient; ``mm_tn_accumulate``
   adds it into an fp32 buffer).
 
-On CUDA, ``mm_nt`` runs the hand-written tcgen05 kernel of ``csrc/gemm_tcgen05.cu``
+On CUDA all three run the hand-written tcgen05 kernel of ``csrc/gemm_sm100.cu``
 (TMA-fed shared-memory stages, ``tcgen05.mma`` with the accumulator in tensor
-memory, persistent tile loop) when the shape is tile-aligned; the other
-products and unaligned shapes use the library GEMM (cuBLAS through
-``torch.matmul``), which is the plain-GEMM baseline.
+memory, persistent tile loop; 2-CTA 256x256 tiles when the product fills the
+GPU, else 1-CTA 128x256): the input gradient reads ``W`` as an MN-major
+operand and the weight gradient reads both ``dy`` and ``x`` as MN-major
+operands, so nothing is transposed in memory, and the weight gradient is added
+into the fp32 main-grad buffer by the kernel's epilogue.  Decode-shaped
+products (a few rows) stream the weight in ``csrc/gemm_decode.cu``.  Shapes the
+kernels cannot take (a contiguous dimension that is not a multiple of 8, or too
+few output tiles to occupy the SMs) use the library GEMM (cuBLAS through
+``torch.matmul``), the plain-GEMM baseline.
+
+Reference: Transformer Engine's cuBLASLt GEMMs behind Megatron-core linear
+layers (``nemo_rl/models/megatron/setup.py:2520``).
 """
 
 from __future__ import annotations
@@ -41,15 +50,19 @@ def _sms() -> int:
     return _NUM_SMS
 
 
-def native_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
-    """The persistent tcgen05 kernel computes 128 x 256 output tiles, one CTA per
-    SM; shapes that give fewer tiles than half the SMs (decode-time GEMMs with a
-    handful of rows) leave most of the GPU idle in it, so they go to the library
-    GEMM's split-K kernels instead."""
-    if not (_NATIVE_GEMM and dtype == torch.bfloat16 and has_ext() and K % 64 == 0 and N % 16 == 0 and M > 0):
+def native_gemm_supported(M: int, N: int, K: int, dtype, inner: tuple = ()) -> bool:
+    """Whether the tcgen05 kernel takes an ``M x N`` output reducing over ``K``.
+
+    It computes 128 x 256 (or 256 x 256) output tiles, one CTA (pair) per SM
+    (pair); shapes that give fewer tiles than half the SMs (decode-time GEMMs
+    with a handful of rows) leave most of the GPU idle in it.  ``inner`` lists
+    the contiguous (last) dimension of every operand, which TMA needs as a
+    multiple of 8 elements (16-byte rows)."""
+    if not (_NATIVE_GEMM and dtype == torch.bfloat16 and has_ext() and M > 0 and N > 0 and K > 0):
         return False
-    bn = 256 if N >= 256 else 128
-    tiles = -(-M // 128) * -(-N // bn)
+    if any(d % 8 for d in inner):
+        return False
+    tiles = -(-M // 128) * -(-N // 256)
     return tiles * 2 >= _sms()
 
 
@@ -61,26 +74,50 @@ def decode_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
 
 
 def mm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a [M,K] @ b[N,K]^T``."""
     if use_native(a) and a.is_contiguous() and b.is_contiguous():
         M, N, K = a.shape[0], b.shape[0], a.shape[1]
-        if native_gemm_supported(M, N, K, a.dtype):
-            return ext().gemm_nt(a, b)
+        if native_gemm_supported(M, N, K, a.dtype, (K,)) and b.dtype == a.dtype:
+            out = torch.empty(M, N, device=a.device, dtype=a.dtype)
+            ext().gemm_sm100(a, b, out, False, False, False, 0)
+            return out
         if decode_gemm_supported(M, N, K, a.dtype):
             return ext().gemm_decode(a, b)
     return torch.matmul(a, b.t())
 
 
 def mm_nn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a [M,N] @ b [N,K]`` (input gradient: ``b`` is the weight, read MN-major)."""
+    if use_native(a) and a.is_contiguous() and b.is_contiguous() and b.dtype == a.dtype:
+        M, Nr, K = a.shape[0], a.shape[1], b.shape[1]
+        if native_gemm_supported(M, K, Nr, a.dtype, (Nr, K)):
+            out = torch.empty(M, K, device=a.device, dtype=a.dtype)
+            ext().gemm_sm100(a, b, out, False, True, False, 0)
+            return out
     return torch.matmul(a, b)
 
 
 def mm_tn(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """``a [M,N]^T @ b [M,K]`` -> ``[N, K]`` (weight gradient; both operands MN-major)."""
+    if use_native(a) and a.is_contiguous() and b.is_contiguous() and b.dtype == a.dtype:
+        Mr, N, K = a.shape[0], a.shape[1], b.shape[1]
+        if native_gemm_supported(N, K, Mr, a.dtype, (N, K)):
+            out = torch.empty(N, K, device=a.device, dtype=a.dtype)
+            ext().gemm_sm100(a, b, out, True, True, False, 0)
+            return out
     return torch.matmul(a.t(), b)
 
 
 def mm_tn_accumulate(a: torch.Tensor, b: torch.Tensor, out: torch.Tensor) -> None:
-    """``out += a^T @ b`` with fp32 ``out``."""
+    """``out += a^T @ b`` with fp32 ``out`` (the weight gradient added into main-grad
+    by the GEMM epilogue)."""
     if a.is_cuda:
+        if (use_native(a) and a.is_contiguous() and b.is_contiguous() and out.is_contiguous()
+                and out.dtype == torch.float32 and b.dtype == a.dtype):
+            Mr, N, K = a.shape[0], a.shape[1], b.shape[1]
+            if native_gemm_supported(N, K, Mr, a.dtype, (N, K)):
+                ext().gemm_sm100(a, b, out, True, True, True, 0)
+                return
         out.add_(torch.mm(a.t(), b, out_dtype=torch.float32))
     else:
         out.add_(torch.matmul(a.t().float(), b.float()))

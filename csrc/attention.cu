@@ -102,6 +102,7 @@ paged_decode_kernel(const bf16* __restrict__ q, long long q_stride, const C* __r
                     float v_scale, int tokens_per_split, float* __restrict__ part_o, float* __restrict__ part_ml,
                     bf16* __restrict__ out) {
   constexpr int DPL = HD / 32;  // dims per lane in the P.V phase
+  pdl_launch_dependents();
   __shared__ float qs[G][HD];
   __shared__ float red_m[4][G], red_l[4][G];
   __shared__ float red_o[4][G][HD];
@@ -413,6 +414,7 @@ paged_decode_pipe_kernel(const bf16* __restrict__ q, long long q_stride, const b
                          int tokens_per_split, float* __restrict__ part_o, float* __restrict__ part_ml,
                          bf16* __restrict__ out) {
   constexpr int BT = 16, CH = HD / 8, KS = HD / 16, NT = HD / 8, TILE = BT * HD;
+  pdl_launch_dependents();
   extern __shared__ __align__(128) unsigned char smem_raw[];
   const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
   bf16* ring = reinterpret_cast<bf16*>(smem_raw) + (size_t)w * ST * 2 * TILE;
@@ -579,6 +581,7 @@ paged_decode_pipe_kernel(const bf16* __restrict__ q, long long q_stride, const b
 template <int HD>
 __global__ void decode_combine_kernel(const float* __restrict__ part_o, const float* __restrict__ part_ml, int splits,
                                       int nq, bf16* __restrict__ out) {
+  pdl_launch_dependents();
   const int bh = blockIdx.x;  // b * nq + h
   const int d = threadIdx.x;
   if (d >= HD) return;

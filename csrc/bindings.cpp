@@ -63,6 +63,7 @@ void symm_close(int64_t ptr);
 at::Tensor symm_view(int64_t ptr, int64_t numel, int64_t dtype_code, int64_t device);
 void refit_copy(at::Tensor tasks, at::Tensor dst);
 at::Tensor gemm_decode(at::Tensor x, at::Tensor w);
+at::Tensor gemm_decode_split(at::Tensor x, at::Tensor w, int64_t splits);
 at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n, int64_t me, int64_t epoch);
 void stream_write_u32(int64_t ptr, int64_t value);
 at::Tensor ar_add_rmsnorm(at::Tensor partial, at::Tensor resid, at::Tensor w, double eps, std::vector<int64_t> slots,
@@ -148,6 +149,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_ar_error_flag", &decode_ar_error_flag, py::arg("reset") = false);
   m.def("stream_write_u32", &stream_write_u32, "stream memory write (no kernel) of a 32-bit word");
   m.def("gemm_decode", &gemm_decode, "decode-shaped (<= 256 rows) split-K tcgen05 GEMM: x @ w^T");
+  m.def("gemm_decode_split", &gemm_decode_split, "gemm_decode with an explicit K split (1, 2, 4 or 8; 0 = choose)");
   m.def("gemm_decode_error_flag", &gemm_decode_error_flag, py::arg("reset") = false);
   m.def("refit_copy", &refit_copy, "train->rollout reshard (bf16) reading peer shards over NVLink");
   m.def("refit_quant_fp8", &refit_quant_fp8, "train->rollout reshard fused with 128x128 e4m3 block quantisation");

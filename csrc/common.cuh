@@ -34,6 +34,16 @@ inline int num_sms() {
   return n;
 }
 
+// Programmatic dependent launch.  A kernel that calls pdl_launch_dependents()
+// lets the kernel launched after it on the same stream WITH programmatic stream
+// serialization (the decode-shaped GEMM) start early: that kernel runs its
+// independent prologue (barrier set-up, tensor-memory allocation, the weight
+// stream) and calls pdl_wait() before it reads anything this kernel wrote;
+// pdl_wait() returns once every earlier kernel completed and its writes are
+// visible.  For a kernel launched without the attribute both are no-ops.
+__device__ __forceinline__ void pdl_launch_dependents() { asm volatile("griddepcontrol.launch_dependents;\n" ::: "memory"); }
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;\n" ::: "memory"); }
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

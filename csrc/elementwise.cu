@@ -52,6 +52,7 @@ __device__ __forceinline__ float silu_f(float g) { return g / (1.f + __expf(-g))
 
 template <typename T>
 __global__ void swiglu_fwd_kernel(const T* __restrict__ gu, T* __restrict__ out, long long rows, int F) {
+  pdl_launch_dependents();
   const bool vec = (sizeof(T) == 2) && (F % 8 == 0);
   if (vec) {
     const int fv = F / 8;

@@ -20,6 +20,7 @@ rmsnorm_fwd_kernel(const T* __restrict__ x, const T* __restrict__ delta, const T
                    float eps) {
   const int lane = threadIdx.x & 31;
   const int row = blockIdx.x * kNormWarps + (threadIdx.x >> 5);
+  pdl_launch_dependents();
   if (row >= rows) return;
   const T* xr = x + (size_t)row * H;
   const T* dr = delta ? delta + (size_t)row * H : nullptr;
@@ -81,6 +82,7 @@ __global__ void __launch_bounds__(128)
 rmsnorm_fwd_rowcta_kernel(const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ delta,
                           const __nv_bfloat16* __restrict__ w, __nv_bfloat16* __restrict__ y,
                           __nv_bfloat16* __restrict__ s_out, float* __restrict__ rstd, int H, float eps) {
+  pdl_launch_dependents();
   __shared__ float red[32];
   const int row = blockIdx.x;
   const int nv = H / 8;

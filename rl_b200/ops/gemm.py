@@ -35,8 +35,8 @@ from rl_b200.ops._ext import ext, has_ext, use_native
 __all__ = ["mm_nt", "mm_nn", "mm_tn", "mm_tn_accumulate", "native_gemm_supported", "decode_gemm_supported"]
 
 _NATIVE_GEMM = os.environ.get("RL_B200_NATIVE_GEMM", "1") == "1"
-# the decode-shaped kernel is opt-in until it beats the library GEMM on every decode shape
-_DECODE_GEMM = os.environ.get("RL_B200_DECODE_GEMM", "0") == "1"
+# RL_B200_DECODE_GEMM=0 sends decode-shaped products to the library GEMM (A/B timing)
+_DECODE_GEMM = os.environ.get("RL_B200_DECODE_GEMM", "1") == "1"
 
 
 _NUM_SMS = None
@@ -73,11 +73,19 @@ def decode_gemm_supported(M: int, N: int, K: int, dtype) -> bool:
             and K % 8 == 0)
 
 
+# Up to this many rows a product streams its weight (memory-bound on B200: the
+# bf16 ridge point is ~250 FLOP per weight byte, i.e. ~125 rows), so the
+# decode-shaped kernel is used whatever N is.
+DECODE_MAX_ROWS = 128
+
+
 def mm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     """``a [M,K] @ b[N,K]^T``."""
-    if use_native(a) and a.is_contiguous() and b.is_contiguous():
+    if use_native(a) and a.is_contiguous() and b.is_contiguous() and b.dtype == a.dtype:
         M, N, K = a.shape[0], b.shape[0], a.shape[1]
-        if native_gemm_supported(M, N, K, a.dtype, (K,)) and b.dtype == a.dtype:
+        if M <= DECODE_MAX_ROWS and decode_gemm_supported(M, N, K, a.dtype):
+            return ext().gemm_decode(a, b)
+        if native_gemm_supported(M, N, K, a.dtype, (K,)):
             out = torch.empty(M, N, device=a.device, dtype=a.dtype)
             ext().gemm_sm100(a, b, out, False, False, False, 0)
             return out

@@ -301,6 +301,21 @@ def test_gemm_decode_tcgen05(cuda_device, M, N, K):
     assert ext.gemm_decode_error_flag(True) == 0
 
 
+@pytest.mark.parametrize("splits", [1, 2, 4, 8])
+def test_gemm_decode_cluster_splits(cuda_device, splits):
+    """Every K split (one CTA cluster per W tile, partials summed through
+    distributed shared memory) gives the fp32 product, for 16..256 token rows."""
+    ext = _ext.ext()
+    torch.manual_seed(9)
+    for M in (5, 32, 64, 100, 256):
+        x = torch.randn(M, 2048, device=cuda_device).to(torch.bfloat16)
+        w = (torch.randn(1280, 2048, device=cuda_device) * 0.05).to(torch.bfloat16)
+        y = ext.gemm_decode_split(x, w, splits)
+        torch.cuda.synchronize()
+        assert rel_err(y, x.float() @ w.float().t()) < 1e-2, (M, splits)
+    assert ext.gemm_decode_error_flag(True) == 0
+
+
 @pytest.mark.parametrize("hd,G", [(128, 4), (64, 2)])
 def test_flash_attn_segments_cp_layout(cuda_device, hd, G):
     """Context-parallel segment attention (query chunks vs key prefixes, shared

@@ -46,6 +46,13 @@ at::Tensor gemm_nt(at::Tensor a, at::Tensor b);
 int64_t gemm_error_flag(bool reset);
 void gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> recv_ptrs,
              std::vector<int64_t> flag_ptrs, std::vector<int64_t> ack_ptrs, int64_t me, int64_t epoch);
+// attention_sm100.cu
+std::vector<at::Tensor> flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor cu_seqlens,
+                                          int64_t max_seqlen, double scale, bool causal);
+std::vector<at::Tensor> flash_attn_seg_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
+                                              double scale, c10::optional<at::Tensor> cp_flags, int64_t cp_epoch,
+                                              int64_t cp_size);
+int64_t attn_tc_error_flag(bool reset);
 // gemm_sm100.cu
 void gemm_sm100(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, bool accumulate, int64_t tile);
 int64_t gemm_sm100_error_flag(bool reset);
@@ -121,6 +128,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_sm100", &gemm_sm100, py::arg("a"), py::arg("b"), py::arg("out"), py::arg("a_mn") = false,
         py::arg("b_mn") = false, py::arg("accumulate") = false, py::arg("tile") = 0,
         "tcgen05 GEMM out = op(a) op(b)^T; a [M,K] or [K,M] (a_mn), b [N,K] or [K,N] (b_mn); bf16 or fp32 (+=) out");
+  m.def("flash_attn_fwd_tc", &flash_attn_fwd_tc, "tcgen05 varlen flash-attention forward (head dim 128)");
+  m.def("flash_attn_seg_fwd_tc", &flash_attn_seg_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("seg"),
+        py::arg("max_q"), py::arg("scale"), py::arg("cp_flags") = py::none(), py::arg("cp_epoch") = 0,
+        py::arg("cp_size") = 0, "tcgen05 segment flash-attention forward (head dim 128)");
+  m.def("attn_tc_error_flag", &attn_tc_error_flag, py::arg("reset") = false);
   m.def("gemm_sm100_error_flag", &gemm_sm100_error_flag, py::arg("reset") = false);
   m.def("gemm_fp8", &gemm_fp8, py::arg("a"), py::arg("a_scale"), py::arg("b"), py::arg("b_scale"),
         py::arg("splits") = 0, "block-scaled e4m3 GEMM (1x128 activation, 128x128 weight fp32 scales) -> bf16");

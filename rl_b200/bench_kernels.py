@@ -117,6 +117,9 @@ def bench_decode_gemm(M=64):
 
 
 def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):
+    """Causal varlen attention (n sequences of L tokens, GQA nq:nkv): the tcgen05
+    forward, the mma.sync forward and backward, and torch SDPA (cuDNN backend)."""
+    from rl_b200.ops._ext import ext
     from rl_b200.ops.attention import flash_attn_varlen
 
     dev = torch.device("cuda")
@@ -125,13 +128,39 @@ def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):
     k = torch.randn(T, nkv, hd, device=dev).to(torch.bfloat16).requires_grad_(True)
     v = torch.randn(T, nkv, hd, device=dev).to(torch.bfloat16).requires_grad_(True)
     cu = torch.arange(0, T + 1, L, dtype=torch.int32, device=dev)
-    tf = _time(lambda: flash_attn_varlen(q, k, v, cu, L))
+    sc = hd ** -0.5
+    fl = 4 * n * L * L / 2 * hd * nq
+    C = ext()
+    res = []
+    if hd == 128:
+        t = _time(lambda: C.flash_attn_fwd_tc(q.detach(), k.detach(), v.detach(), cu, L, sc, True))
+        res.append(f"fwd tcgen05 {t:.3f} ms {fl / t / 1e9:.1f}")
+    t = _time(lambda: C.flash_attn_fwd(q.detach(), k.detach(), v.detach(), cu, L, sc, True))
+    res.append(f"fwd mma.sync {t:.3f} ms {fl / t / 1e9:.1f}")
     o = flash_attn_varlen(q, k, v, cu, L)
     g = torch.randn_like(o)
     tb = _time(lambda: torch.autograd.grad(o, (q, k, v), g, retain_graph=True))
-    fl = 4 * n * L * L / 2 * hd * nq
-    print(f"flash_attn L={L} n={n}: fwd {tf:.3f} ms {fl / tf / 1e9:.1f} TFLOP/s | bwd {tb:.3f} ms "
-          f"{2.5 * fl / tb / 1e9:.1f} TFLOP/s")
+    res.append(f"bwd {tb:.3f} ms {2.5 * fl / tb / 1e9:.1f}")
+    try:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+
+        qb = q.detach().view(n, L, nq, hd).transpose(1, 2).contiguous().requires_grad_(True)
+        kb = k.detach().view(n, L, nkv, hd).transpose(1, 2).repeat_interleave(nq // nkv, 1).contiguous() \
+            .requires_grad_(True)
+        vb = v.detach().view(n, L, nkv, hd).transpose(1, 2).repeat_interleave(nq // nkv, 1).contiguous() \
+            .requires_grad_(True)
+        with sdpa_kernel([SDPBackend.CUDNN_ATTENTION]):
+            f = lambda: torch.nn.functional.scaled_dot_product_attention(qb, kb, vb, is_causal=True)  # noqa: E731
+            ts = _time(f)
+            ob = f()
+            gb = torch.randn_like(ob)
+            tsb = _time(lambda: torch.autograd.grad(ob, (qb, kb, vb), gb, retain_graph=True))
+        res.append(f"cuDNN SDPA fwd {ts:.3f} ms {fl / ts / 1e9:.1f} bwd {tsb:.3f} ms {2.5 * fl / tsb / 1e9:.1f}")
+    except Exception as e:  # noqa: BLE001
+        res.append(f"cuDNN SDPA unavailable ({type(e).__name__})")
+    print(f"flash_attn L={L} n={n} nq={nq} nkv={nkv}: " + " | ".join(res) + " TFLOP/s")
+    if hd == 128:
+        assert C.attn_tc_error_flag(True) == 0
 
 
 def bench_fp8(M=8192, N=8192, K=8192):

@@ -19,6 +19,7 @@ Layouts
 from __future__ import annotations
 
 import math
+import os
 from typing import Optional
 
 import torch
@@ -61,10 +62,36 @@ def flash_attn_varlen_ref(q, k, v, cu_seqlens, scale: Optional[float] = None, ca
     return out.to(q.dtype), lse
 
 
+# RL_B200_ATTN_TC=0 keeps the forward on the mma.sync kernel (A/B timing)
+_ATTN_TC = os.environ.get("RL_B200_ATTN_TC", "1") == "1"
+
+
+def _tc_ok(*xs) -> bool:
+    """The tcgen05 forward (``csrc/attention_sm100.cu``) takes head dim 128 bf16 views
+    with contiguous heads and 16-byte aligned token rows (TMA tensor maps)."""
+    return _ATTN_TC and all(x.dim() == 3 and x.shape[-1] == 128 and x.dtype == torch.bfloat16 and x.stride(2) == 1
+                            and x.stride(1) == 128 and x.stride(0) % 8 == 0 and x.data_ptr() % 16 == 0 for x in xs)
+
+
+def fa_forward(q, k, v, cu_seqlens, max_seqlen: int, scale: float, causal: bool):
+    """Native varlen forward: (out, lse) from the tcgen05 kernel when it applies."""
+    if _tc_ok(q, k, v):
+        return ext().flash_attn_fwd_tc(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+    return ext().flash_attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+
+
+def fa_seg_forward(q, k, v, seg, max_q: int, scale: float, cp_flags=None, cp_epoch: int = 0, cp_size: int = 0):
+    """Native segment forward (context parallelism), tcgen05 when it applies."""
+    if _tc_ok(q, k, v):
+        return ext().flash_attn_seg_fwd_tc(q, k, v, seg, int(max_q), float(scale), cp_flags, int(cp_epoch),
+                                           int(cp_size))
+    return ext().flash_attn_seg_fwd(q, k, v, seg, int(max_q), float(scale), cp_flags, int(cp_epoch), int(cp_size))
+
+
 class _FlashAttnVarlen(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, cu_seqlens, max_seqlen, scale, causal):
-        o, lse = ext().flash_attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+        o, lse = fa_forward(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
         ctx.save_for_backward(q, k, v, o, lse, cu_seqlens)
         ctx.meta = (int(max_seqlen), float(scale), bool(causal))
         return o
@@ -87,7 +114,7 @@ def flash_attn_varlen(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[floa
 class _FlashAttnSegments(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, seg, max_q, max_k, scale):
-        o, lse = ext().flash_attn_seg_fwd(q, k, v, seg, int(max_q), float(scale))
+        o, lse = fa_seg_forward(q, k, v, seg, int(max_q), float(scale))
         ctx.save_for_backward(q, k, v, o, lse, seg)
         ctx.meta = (int(max_k), float(scale))
         return o
@@ -115,7 +142,7 @@ def flash_attn_varlen_fwd(q, k, v, cu_seqlens, max_seqlen: int, scale: Optional[
     """Forward only (prefill): returns (out, lse)."""
     scale = scale if scale is not None else 1.0 / math.sqrt(q.shape[-1])
     if use_native(q):
-        return ext().flash_attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+        return fa_forward(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
     return flash_attn_varlen_ref(q, k, v, cu_seqlens, scale, causal)
 
 

@@ -265,8 +265,10 @@ class _CPAttentionFused(torch.autograd.Function):
 
         kf, vf = exch(k, v, lay)
         seg = torch.stack([lay.q_start, lay.q_len, lay.k_start, lay.k_len], 1).to(torch.int32).contiguous()
-        o, lse = ext().flash_attn_seg_fwd(q.contiguous(), kf, vf, seg, int(lay.max_q), float(scale), exch.flags,
-                                          exch.epoch, exch.n)
+        from rl_b200.ops.attention import fa_seg_forward
+
+        o, lse = fa_seg_forward(q.contiguous(), kf, vf, seg, int(lay.max_q), float(scale), exch.flags, exch.epoch,
+                                exch.n)
         torch.cuda.current_stream().wait_stream(exch.side)
         ctx.save_for_backward(q, kf, vf, o, lse, seg)
         ctx.lay, ctx.scale, ctx.group = lay, scale, exch.group

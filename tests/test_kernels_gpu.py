@@ -237,6 +237,42 @@ def test_flash_attention_fwd_bwd(cuda_device, hd, nq, nkv):
     assert rel_err(v.grad, vf.grad) < 3e-2
 
 
+@pytest.mark.parametrize("causal", [True, False])
+@pytest.mark.parametrize("nq,nkv", [(8, 2), (4, 4)])
+def test_flash_attention_tcgen05_forward(cuda_device, causal, nq, nkv):
+    """tcgen05 forward (csrc/attention_sm100.cu): output and log-sum-exp against an
+    fp32 PyTorch reference on packed-QKV views, ragged lengths around the 128-query
+    and 64-key tile edges."""
+    ext = _ext.ext()
+    torch.manual_seed(5)
+    hd = 128
+    lens = [1, 63, 64, 65, 127, 128, 129, 700, 2048, 33]
+    q, k, v, cu = _varlen(cuda_device, lens, nq, nkv, hd)
+    q = q * 2  # larger logits exercise the lazy rescaling
+    q = q.to(torch.bfloat16)
+    scale = hd ** -0.5
+    qp = torch.empty(q.shape[0], nq + 2 * nkv, hd, device=cuda_device, dtype=torch.bfloat16)
+    qp[:, :nq], qp[:, nq:nq + nkv], qp[:, nq + nkv:] = q, k, v
+    q, k, v = qp[:, :nq], qp[:, nq:nq + nkv], qp[:, nq + nkv:]
+    o, lse = ext.flash_attn_fwd_tc(q, k, v, cu, max(lens), scale, causal)
+    torch.cuda.synchronize()
+    assert ext.attn_tc_error_flag(True) == 0
+    for b in range(len(lens)):
+        s, e = int(cu[b]), int(cu[b + 1])
+        qb = q[s:e].float().transpose(0, 1)
+        kb = k[s:e].float().transpose(0, 1).repeat_interleave(nq // nkv, 0)
+        vb = v[s:e].float().transpose(0, 1).repeat_interleave(nq // nkv, 0)
+        sc = (qb @ kb.transpose(-1, -2)) * scale
+        if causal:
+            sc = sc.masked_fill(torch.ones(e - s, e - s, device=cuda_device, dtype=torch.bool).triu(1), float("-inf"))
+        ref = (torch.softmax(sc, -1) @ vb).transpose(0, 1)
+        assert rel_err(o[s:e], ref) < 1e-2, (b, lens[b])
+        torch.testing.assert_close(lse[:, s:e], torch.logsumexp(sc, -1), atol=2e-2, rtol=1e-3)
+    # same numbers as the mma.sync kernel it replaces
+    o2, lse2 = ext.flash_attn_fwd(q, k, v, cu, max(lens), scale, causal)
+    assert rel_err(o, o2) < 1e-2
+
+
 @pytest.mark.parametrize("G,hd,bs", [(4, 128, 16), (8, 128, 16), (1, 128, 16), (4, 128, 256), (8, 64, 32),
                                      (2, 128, 8)])
 def test_paged_decode_and_cache_write(cuda_device, G, hd, bs):

@@ -23,7 +23,7 @@
 //                  (128 output columns) in its own shared memory, so per MMA FLOP a
 //                  CTA loads a third less than in the 1-CTA tile (the B operand is
 //                  split between the pair instead of re-read by both).  Stage =
-//                  32 KB per CTA, 6 stages.  No TMA multicast: every load reads
+//                  32 KB per CTA, 6 stages.  Every TMA load is a plain one: it reads
 //                  this GPU's memory into the loading CTA's own shared memory; the
 //                  odd CTA's loads signal the even CTA's mbarrier (.cta_group::2).
 //
@@ -136,13 +136,14 @@ __device__ __forceinline__ void mma(uint32_t tmem_d, uint64_t adesc, uint64_t bd
 }
 
 // Arrive on `bar` once every MMA issued so far completed; in a pair the arrive
-// goes to the barrier at the same offset in both CTAs (commit to a CTA mask).
+// goes to the barrier at the same offset in both CTAs: one commit to this CTA's
+// barrier and one to the peer's (its address in the cluster window).
 template <bool PAIR>
 __device__ __forceinline__ void commit(uint32_t bar) {
   if constexpr (PAIR) {
-    const uint16_t both = 0x3;
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], %1;\n"
-                 ::"r"(bar), "h"(both)
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)
+                 : "memory");
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(mapa(bar, 1))
                  : "memory");
   } else {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];\n" ::"r"(bar)

@@ -182,7 +182,7 @@ def case_refit_reshard(rank: int):
     for name in ws.q_layout:
         q, s = ws.fp8_weight(name)
         wt = w.gen_model.param(name).detach()
-        qr, sr = quant_fp8_block_ref(wt, 128, False)
+        qr, sr = quant_fp8_block_ref(wt, 128, w.fp8_pow2)  # same scale rule as the worker (pow2 by default)
         # torch divides by the Python scalar 448 through a reciprocal multiply, so its
         # scales may sit one ulp from amax / 448; the bytes are checked against the
         # kernel's own scales (x / s, IEEE division on both sides)

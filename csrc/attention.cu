@@ -82,14 +82,14 @@ __device__ __forceinline__ void load_tile(bf16* s, const bf16* g, long long row_
 
 __device__ int g_attn_error = 0;
 
-// Bounded wait (about two seconds) until *p >= v; false on expiry.
-__device__ __forceinline__ bool cp_wait_flag(const uint32_t* p, uint32_t v) {
+// Bounded wait (at most `limit` cycles) until *p >= v; false on expiry.
+__device__ __forceinline__ bool cp_wait_flag(const uint32_t* p, uint32_t v, long long limit) {
   const long long t0 = clock64();
   for (;;) {
     uint32_t x;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];\n" : "=r"(x) : "l"(p) : "memory");
     if ((int)(x - v) >= 0) return true;
-    if (clock64() - t0 > 4000000000LL) return false;
+    if (clock64() - t0 > limit) return false;
   }
 }
 
@@ -604,7 +604,7 @@ __global__ void __launch_bounds__(128)
 fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16* __restrict__ v, long long qs,
               long long ks, long long vs, const int* __restrict__ cu, int nq, int nkv, float scale_log2, int causal,
               bf16* __restrict__ o, float* __restrict__ lse, int T_total, const int* __restrict__ seg,
-              const uint32_t* __restrict__ cp_flags, uint32_t cp_epoch, int cp_size) {
+              const uint32_t* __restrict__ cp_flags, uint32_t cp_epoch, int cp_size, long long wait_cycles) {
   constexpr int BM = 64, BN = 64, CH = HD / 8, KS = HD / 16, NT = HD / 8;
   extern __shared__ __align__(128) unsigned char smem_raw[];
   bf16* Qs = reinterpret_cast<bf16*>(smem_raw);
@@ -640,7 +640,7 @@ fa_fwd_kernel(const bf16* __restrict__ q, const bf16* __restrict__ k, const bf16
       if (tid == 0) {
         const int c = n0 / L;  // every chunk has the segment's query length
         const int owner = c < cp_size ? c : 2 * cp_size - 1 - c;
-        if (!cp_wait_flag(cp_flags + owner, cp_epoch)) atomicExch(&g_attn_error, 1);
+        if (!cp_wait_flag(cp_flags + owner, cp_epoch, wait_cycles)) atomicExch(&g_attn_error, 1);
       }
       __syncthreads();
     }
@@ -1051,7 +1051,7 @@ std::vector<at::Tensor> flash_attn_fwd(at::Tensor q, at::Tensor k, at::Tensor v,
     kern<<<grid, 128, smem, stream()>>>((const bf16*)q.data_ptr(), (const bf16*)k.data_ptr(), (const bf16*)v.data_ptr(),
                                         q.stride(0), k.stride(0), v.stride(0), cu.data_ptr<int>(), nq, nkv, scale_log2,
                                         causal ? 1 : 0, (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, nullptr,
-                                        nullptr, 0u, 0);
+                                        nullptr, 0u, 0, (long long)peer_wait_cycles());
   });
   RLB_CUDA_CHECK(cudaGetLastError());
   return {o, lse};
@@ -1129,7 +1129,7 @@ std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tenso
                                         (bf16*)o.data_ptr(), lse.data_ptr<float>(), T_, seg.data_ptr<int>(),
                                         cp_flags ? reinterpret_cast<const uint32_t*>(cp_flags->data_ptr<int>())
                                                  : nullptr,
-                                        (uint32_t)cp_epoch, (int)cp_size);
+                                        (uint32_t)cp_epoch, (int)cp_size, (long long)peer_wait_cycles());
   });
   RLB_CUDA_CHECK(cudaGetLastError());
   return {o, lse};

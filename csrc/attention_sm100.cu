@@ -97,7 +97,8 @@ __global__ void __launch_bounds__(192, 2)
 fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
                  const __grid_constant__ CUtensorMap tv, const int* __restrict__ cu, int nq, int nkv, float scale_log2,
                  int causal, __nv_bfloat16* __restrict__ o, float* __restrict__ lse, int T_total,
-                 const int* __restrict__ seg, const uint32_t* __restrict__ cp_flags, uint32_t cp_epoch, int cp_size) {
+                 const int* __restrict__ seg, const uint32_t* __restrict__ cp_flags, uint32_t cp_epoch, int cp_size,
+                 long long wait_cycles) {
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
@@ -171,7 +172,7 @@ fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
           const long long t0 = clock64();
           bool ok = true;
           while (!cp_flag_ready(cp_flags + owner, cp_epoch)) {
-            if (clock64() - t0 > kWaitCycles) {
+            if (clock64() - t0 > wait_cycles) {
               atomicExch(&g_attn_tc_error, 5);
               *abort_flag = 1;
               ok = false;
@@ -396,7 +397,7 @@ void launch_tc(const at::Tensor& q, const at::Tensor& k, const at::Tensor& v, co
   dim3 grid(nq, (max_q + fa::BQ - 1) / fa::BQ, nseg);
   kern<<<grid, 192, fa::SMEM, stream()>>>(tq, tk, tv, cu, nq, nkv, scale_log2, causal ? 1 : 0,
                                           (__nv_bfloat16*)o.data_ptr(), lse.data_ptr<float>(), T_, seg, cp_flags,
-                                          cp_epoch, cp_size);
+                                          cp_epoch, cp_size, (long long)peer_wait_cycles());
   RLB_CUDA_CHECK(cudaGetLastError());
 }
 

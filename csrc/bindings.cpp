@@ -1,6 +1,8 @@
 // Python bindings of the rl_b200 native extension (module rl_b200._C).
 #include <torch/extension.h>
 
+#include <atomic>
+
 #include <vector>
 
 // norm.cu
@@ -98,6 +100,17 @@ void dp_adam_allgather(std::vector<int64_t> param_ptrs, int64_t lo, at::Tensor m
 int64_t gemm_decode_error_flag(bool reset);
 void refit_quant_fp8(at::Tensor tasks, at::Tensor q, at::Tensor scales, bool pow2);
 
+namespace rlb {
+namespace {
+std::atomic<int64_t> g_peer_wait_cycles{4000000000LL};
+}
+int64_t peer_wait_cycles() { return g_peer_wait_cycles.load(std::memory_order_relaxed); }
+void set_peer_wait_cycles(int64_t cycles) {
+  TORCH_CHECK(cycles > 0, "rl_b200: the peer wait bound must be positive");
+  g_peer_wait_cycles.store(cycles, std::memory_order_relaxed);
+}
+}  // namespace rlb
+
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "rl_b200 sm_100a kernels";
   m.def("rmsnorm_fwd", &rmsnorm_fwd);
@@ -133,6 +146,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("max_q"), py::arg("scale"), py::arg("cp_flags") = py::none(), py::arg("cp_epoch") = 0,
         py::arg("cp_size") = 0, "tcgen05 segment flash-attention forward (head dim 128)");
   m.def("attn_tc_error_flag", &attn_tc_error_flag, py::arg("reset") = false);
+  m.def("peer_wait_cycles", &rlb::peer_wait_cycles,
+        "bound (SM cycles) of every in-kernel wait on a peer's or a copy engine's flag");
+  m.def("set_peer_wait_cycles", &rlb::set_peer_wait_cycles, py::arg("cycles"));
   m.def("gemm_sm100_error_flag", &gemm_sm100_error_flag, py::arg("reset") = false);
   m.def("gemm_fp8", &gemm_fp8, py::arg("a"), py::arg("a_scale"), py::arg("b"), py::arg("b_scale"),
         py::arg("splits") = 0, "block-scaled e4m3 GEMM (1x128 activation, 128x128 weight fp32 scales) -> bf16");

@@ -24,6 +24,14 @@ namespace rlb {
 
 inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// Upper bound, in SM clock cycles, of every wait on a flag written by ANOTHER rank
+// or by a copy engine (fused collectives, expert dispatch, context-parallel K/V
+// arrival).  Kernels receive it as an argument; on expiry they set their error
+// word and return instead of spinning.  Default 4e9 cycles (about 2 s at 2 GHz);
+// tests lower it to make a wait run out quickly.  Defined in bindings.cpp.
+int64_t peer_wait_cycles();
+void set_peer_wait_cycles(int64_t cycles);
+
 inline int num_sms() {
   static int n = -1;
   if (n < 0) {

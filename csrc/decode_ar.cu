@@ -27,6 +27,7 @@ constexpr int kMax = 8;
 struct Peers {
   __nv_bfloat16* slot[kMax];  // every rank's [2][cap][H] bf16 slots
   uint32_t* flag[kMax];       // every rank's [n][cap] u32 flag words (index src * cap + row)
+  long long wait;             // bound of the wait on every peer's flag (cycles)
 };
 
 __global__ void __launch_bounds__(256)
@@ -69,7 +70,7 @@ ar_add_rmsnorm_kernel(const __nv_bfloat16* __restrict__ partial, __nv_bfloat16* 
       uint32_t x;
       asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(x) : "l"(f) : "memory");
       if ((int)(x - ep) >= 0) break;
-      if (clock64() - t0 > 4000000000LL) {
+      if (clock64() - t0 > pe.wait) {
         atomicExch(&g_dar_error, 1);
         break;
       }
@@ -141,6 +142,7 @@ at::Tensor ar_add_rmsnorm(at::Tensor partial, at::Tensor resid, at::Tensor w, do
   const size_t n = slots.size();
   TORCH_CHECK(n >= 1 && n <= (size_t)dar::kMax && flags.size() == n, "ar_add_rmsnorm: 1..8 ranks");
   dar::Peers pe{};
+  pe.wait = peer_wait_cycles();
   for (size_t i = 0; i < n; ++i) {
     pe.slot[i] = reinterpret_cast<__nv_bfloat16*>((uintptr_t)slots[i]);
     pe.flag[i] = reinterpret_cast<uint32_t*>((uintptr_t)flags[i]);

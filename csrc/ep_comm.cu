@@ -28,7 +28,6 @@ namespace rlb {
 namespace ep {
 
 __device__ int g_ep_error = 0;
-constexpr long long kWait = 4000000000LL;  // ~2 s
 constexpr int kMax = 8;
 
 struct Peers {
@@ -36,6 +35,7 @@ struct Peers {
   int* tag[kMax];            // tag base of every rank ([2][cap] int32)
   uint32_t* flags[kMax];     // data flags of every rank ([2][n])
   uint32_t* acks[kMax];      // ack words of every rank ([2][n])
+  long long wait;            // bound of every wait on a peer's word (cycles)
 };
 
 __device__ __forceinline__ void st_rel(uint32_t* p, uint32_t v) {
@@ -46,10 +46,10 @@ __device__ __forceinline__ uint32_t ld_acq(const uint32_t* p) {
   asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
   return v;
 }
-__device__ bool wait_ge(const uint32_t* p, uint32_t v, int code) {
+__device__ bool wait_ge(const uint32_t* p, uint32_t v, int code, long long limit) {
   const long long t0 = clock64();
   while ((int)(ld_acq(p) - v) < 0) {
-    if (clock64() - t0 > kWait) {
+    if (clock64() - t0 > limit) {
       atomicExch(&g_ep_error, code);
       return false;
     }
@@ -67,7 +67,7 @@ scatter_kernel(const __nv_bfloat16* __restrict__ src, const int* __restrict__ sr
   if (threadIdx.x == 0) {
     bool good = true;
     if (epoch > 2)
-      for (int d = 0; d < n && good; ++d) good = wait_ge(pe.acks[me] + par * n + d, epoch - 2, 1);
+      for (int d = 0; d < n && good; ++d) good = wait_ge(pe.acks[me] + par * n + d, epoch - 2, 1, pe.wait);
     ok = good;
   }
   __syncthreads();
@@ -104,7 +104,7 @@ consume_kernel(Peers pe, int n, int me, uint32_t epoch, long long cap, int rows,
   const int par = epoch & 1;
   if (threadIdx.x == 0) {
     bool good = true;
-    for (int s = 0; s < n && good; ++s) good = wait_ge(pe.flags[me] + par * n + s, epoch, 2);
+    for (int s = 0; s < n && good; ++s) good = wait_ge(pe.flags[me] + par * n + s, epoch, 2, pe.wait);
     ok = good;
   }
   __syncthreads();
@@ -142,6 +142,7 @@ ep::Peers make_peers(const std::vector<int64_t>& buf, const std::vector<int64_t>
   TORCH_CHECK(n >= 1 && n <= (size_t)ep::kMax && tag.size() == n && flags.size() == n && acks.size() == n,
               "ep: 1..8 ranks, one pointer per rank for every buffer");
   ep::Peers p{};
+  p.wait = peer_wait_cycles();
   for (size_t i = 0; i < n; ++i) {
     TORCH_CHECK(buf[i] % 16 == 0, "ep: receive buffers must be 16-byte aligned");
     p.buf[i] = reinterpret_cast<__nv_bfloat16*>((uintptr_t)buf[i]);

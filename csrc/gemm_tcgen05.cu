@@ -74,6 +74,7 @@ struct RSArgs {
   // is ready once shard_flags[j] >= epoch; tiles visit the own shard first, then
   // the others in ring order (the order their copies land)
   const uint32_t* shard_flags;
+  long long wait;  // bound of every wait on a peer's flag or a copy-engine flag (cycles)
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -86,11 +87,12 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Bounded wait until *p >= epoch (unsigned, epochs increase).  false on expiry.
-__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t epoch, volatile int* abort_flag) {
+__device__ __forceinline__ bool wait_flag(const uint32_t* p, uint32_t epoch, volatile int* abort_flag,
+                                          long long limit) {
   const long long t0 = clock64();
   while ((int)(ld_acquire_sys(p) - epoch) < 0) {
     if (*abort_flag) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > limit) {
       atomicExch(&g_error, 2);
       *abort_flag = 1;
       return false;
@@ -186,7 +188,7 @@ gemm_nt_kernel_t(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         if constexpr (EPI == 2) {
           // the copy engine lands shard `dest` and then writes its flag (stream
           // memory op); order the TMA reads of that shard after the flag
-          if (!wait_flag(rs.shard_flags + dest, rs.epoch, abort_flag)) break;
+          if (!wait_flag(rs.shard_flags + dest, rs.epoch, abort_flag, rs.wait)) break;
           asm volatile("fence.proxy.async.global;\n" ::: "memory");
         }
         for (int kb = 0; kb < num_kb; ++kb, ++it) {
@@ -251,7 +253,7 @@ gemm_nt_kernel_t(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
         if (dest != rs.me) {
           // partial tile -> peer's receive slot `me`, then a release flag; first make
           // sure the peer consumed what this slot held two epochs ago
-          wait_flag(rs.acks[rs.me] + par * rs.n + dest, rs.epoch - 2u, abort_flag);
+          wait_flag(rs.acks[rs.me] + par * rs.n + dest, rs.epoch - 2u, abort_flag, rs.wait);
           __nv_bfloat16* dst_base = rs.recv[dest] + (((long long)par * rs.n + rs.me) * rs.Ms + row_s) * N;
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
@@ -281,7 +283,7 @@ gemm_nt_kernel_t(const __grid_constant__ CUtensorMap tmap_a, const __grid_consta
           for (int src = 0; src < rs.n && ok; ++src)
             if (src != rs.me)
               ok = wait_flag(rs.flags[rs.me] + ((long long)par * rs.n + src) * tiles_per_shard + within, rs.epoch,
-                             abort_flag);
+                             abort_flag, rs.wait);
 #pragma unroll 1
           for (int c = 0; c < BN / 32; ++c) {
             uint32_t r[32];
@@ -408,6 +410,7 @@ at::Tensor gemm_nt(at::Tensor a, at::Tensor b) {
   auto c = at::empty({M, N}, a.options());
   if (M == 0 || N == 0) return c;
   tc::RSArgs none{};
+  none.wait = peer_wait_cycles();
   if (N >= 256) launch_gemm<256, 4, 0>(a, b, (__nv_bfloat16*)c.data_ptr(), M, N, K, none);
   else launch_gemm<128, 6, 0>(a, b, (__nv_bfloat16*)c.data_ptr(), M, N, K, none);
   return c;
@@ -434,6 +437,7 @@ void gemm_rs(at::Tensor a, at::Tensor b, at::Tensor out, std::vector<int64_t> re
   TORCH_CHECK(out.size(0) == M / n && out.size(1) == N, "rl_b200 gemm_rs: out must be [M/n, N]");
   const c10::cuda::CUDAGuard guard(a.device());
   tc::RSArgs rs{};
+  rs.wait = peer_wait_cycles();
   rs.n = n;
   rs.me = (int)me;
   rs.Ms = M / n;
@@ -477,6 +481,7 @@ at::Tensor gemm_ag(at::Tensor a, at::Tensor b, at::Tensor shard_flags, int64_t n
   const c10::cuda::CUDAGuard guard(a.device());
   auto c = at::empty({M, N}, a.options());
   tc::RSArgs ag{};
+  ag.wait = peer_wait_cycles();
   ag.n = (int)n;
   ag.me = (int)me;
   ag.Ms = M / (int)n;

@@ -9,6 +9,8 @@
 // the partials (deterministic, no atomics).
 #include "common.cuh"
 
+#include <cstdlib>
+
 namespace rlb {
 
 constexpr int kNormWarps = 4;
@@ -207,6 +209,16 @@ __global__ void reduce_rows_kernel(const float* __restrict__ part, float* __rest
 
 using namespace rlb;
 
+// Few-row (decode) batches take the one-CTA-per-row kernel unless RLB_NORM_ROWCTA=0.
+static bool use_rowcta(const at::Tensor& x, int H, int rows) {
+  static int on = -1;
+  if (on < 0) {
+    const char* e = std::getenv("RLB_NORM_ROWCTA");
+    on = (e == nullptr || e[0] != '0') ? 1 : 0;
+  }
+  return on == 1 && x.scalar_type() == at::kBFloat16 && H % 8 == 0 && H <= 8192 && rows < 4 * num_sms();
+}
+
 static void check_rows(const at::Tensor& x, const at::Tensor& w) {
   RLB_CHECK(x.is_cuda() && x.dim() == 2 && x.is_contiguous(), "norm input must be a contiguous 2-D CUDA tensor");
   RLB_CHECK(w.dim() == 1 && w.size(0) == x.size(1) && w.scalar_type() == x.scalar_type(), "norm weight mismatch");
@@ -219,7 +231,7 @@ std::vector<at::Tensor> rmsnorm_fwd(at::Tensor x, at::Tensor w, double eps) {
   auto y = at::empty_like(x);
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   if (rows == 0) return {y, rstd};
-  if (x.scalar_type() == at::kBFloat16 && H % 8 == 0 && H <= 8192 && rows < 4 * num_sms()) {
+  if (use_rowcta(x, H, rows)) {
     rmsnorm_fwd_rowcta_kernel<<<rows, 128, 0, stream()>>>(
         (const __nv_bfloat16*)x.data_ptr(), nullptr, (const __nv_bfloat16*)w.data_ptr(), (__nv_bfloat16*)y.data_ptr(),
         nullptr, rstd.data_ptr<float>(), H, (float)eps);
@@ -245,7 +257,7 @@ std::vector<at::Tensor> add_rmsnorm_fwd(at::Tensor x, at::Tensor delta, at::Tens
   auto s = at::empty_like(x);
   auto rstd = at::empty({rows}, x.options().dtype(at::kFloat));
   if (rows == 0) return {y, s, rstd};
-  if (x.scalar_type() == at::kBFloat16 && H % 8 == 0 && H <= 8192 && rows < 4 * num_sms()) {
+  if (use_rowcta(x, H, rows)) {
     rmsnorm_fwd_rowcta_kernel<<<rows, 128, 0, stream()>>>(
         (const __nv_bfloat16*)x.data_ptr(), (const __nv_bfloat16*)delta.data_ptr(), (const __nv_bfloat16*)w.data_ptr(),
         (__nv_bfloat16*)y.data_ptr(), (__nv_bfloat16*)s.data_ptr(), rstd.data_ptr<float>(), H, (float)eps);

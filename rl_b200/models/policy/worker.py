@@ -952,6 +952,11 @@ class PolicyWorker:
         if self.pp > 1:  # only the last stage computed a loss
             dist.all_reduce(st.step_loss, group=self.ps.pp_group)
         out["loss"] = float(st.step_loss)
+        if self.device.type == "cuda":
+            # a kernel that gave up a bounded wait (peer flag, pipeline barrier) fails the step here
+            from rl_b200.ops._ext import check_device_errors
+
+            check_device_errors()
         if release_grad if release_grad is not None else self.release_grad_after_train:
             self.optimizer.release_grad_buffer()
         if aggregate:
@@ -1024,7 +1029,12 @@ class PolicyWorker:
             # every stage holds the whole rollout model and the same rows: split them
             t, r, grp = self.pp, self.ps.pp_rank, self.ps.pp_group
         elif self.gen_tp == self.ps.tp_size or self.ps.tp_size == 1:
-            return self.engine.generate(data, greedy=greedy)
+            out = self.engine.generate(data, greedy=greedy)
+            if self.device.type == "cuda":
+                from rl_b200.ops._ext import check_device_errors
+
+                check_device_errors()
+            return out
         else:
             t, r, grp = self.ps.tp_size, self.ps.tp_rank, self.ps.tp_group
         B = data.size

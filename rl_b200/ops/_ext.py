@@ -39,6 +39,10 @@ _KERNELS_PER_CALL = {
     "decode_ar_error_flag": 0,
     "attn_error_flag": 0,
     "ep_error_flag": 0,
+    "gemm_sm100_error_flag": 0,
+    "attn_tc_error_flag": 0,
+    "peer_wait_cycles": 0,
+    "set_peer_wait_cycles": 0,
     "symm_alloc": 0,
     "symm_open": 0,
     "symm_close": 0,
@@ -106,3 +110,34 @@ def add_launches(n: int) -> None:
 def use_native(*tensors: torch.Tensor) -> bool:
     """True when the op must run on the native CUDA path."""
     return any(isinstance(t, torch.Tensor) and t.is_cuda for t in tensors)
+
+
+# every kernel family's device error word (set when a bounded wait runs out)
+ERROR_FLAGS = ("gemm_error_flag", "gemm_sm100_error_flag", "gemm_fp8_error_flag", "grouped_gemm_error_flag",
+               "gemm_decode_error_flag", "decode_ar_error_flag", "attn_error_flag", "attn_tc_error_flag",
+               "ep_error_flag")
+
+
+class DeviceWaitError(RuntimeError):
+    """A kernel gave up a bounded wait (a peer's flag, a copy engine's flag or a
+    pipeline barrier never arrived) and returned with its error word set."""
+
+
+def check_device_errors(reset: bool = True) -> None:
+    """Read (and by default clear) every kernel family's error word; raise
+    :class:`DeviceWaitError` naming the ones that are set.  One small device read
+    per family: callers run it at step boundaries, not per kernel."""
+    if not has_ext():
+        return
+    mod = ext()
+    bad = {}
+    for name in ERROR_FLAGS:
+        fn = getattr(mod, name, None)
+        if fn is None:
+            continue
+        v = int(fn(reset))
+        if v:
+            bad[name] = v
+    if bad:
+        raise DeviceWaitError(f"device wait expired: {bad} (error word = wait site code); "
+                              "a peer rank, copy engine or pipeline stage never signalled")

@@ -75,6 +75,9 @@ def _tc_ok(*xs) -> bool:
 
 def fa_forward(q, k, v, cu_seqlens, max_seqlen: int, scale: float, causal: bool):
     """Native varlen forward: (out, lse) from the tcgen05 kernel when it applies."""
+    if os.environ.get("RLB_PROBE_ATTN_FP32") == "1":  # numerics probe only: fp32 attention
+        o, lse = flash_attn_varlen_ref(q.float(), k.float(), v.float(), cu_seqlens, scale, causal)
+        return o.to(q.dtype), lse
     if _tc_ok(q, k, v):
         return ext().flash_attn_fwd_tc(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
     return ext().flash_attn_fwd(q, k, v, cu_seqlens, int(max_seqlen), float(scale), bool(causal))

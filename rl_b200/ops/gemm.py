@@ -37,6 +37,9 @@ __all__ = ["mm_nt", "mm_nn", "mm_tn", "mm_tn_accumulate", "native_gemm_supported
 _NATIVE_GEMM = os.environ.get("RL_B200_NATIVE_GEMM", "1") == "1"
 # RL_B200_DECODE_GEMM=0 sends decode-shaped products to the library GEMM (A/B timing)
 _DECODE_GEMM = os.environ.get("RL_B200_DECODE_GEMM", "1") == "1"
+# fixed K split of the decode kernel (0 = chosen per shape); 1 accumulates K in the
+# same order as the large-tile kernel (numerics studies)
+_DECODE_SPLITS = int(os.environ.get("RL_B200_DECODE_SPLITS", "0"))
 
 
 _NUM_SMS = None
@@ -84,6 +87,8 @@ def mm_nt(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
     if use_native(a) and a.is_contiguous() and b.is_contiguous() and b.dtype == a.dtype:
         M, N, K = a.shape[0], b.shape[0], a.shape[1]
         if M <= DECODE_MAX_ROWS and decode_gemm_supported(M, N, K, a.dtype):
+            if _DECODE_SPLITS:
+                return ext().gemm_decode_split(a, b, _DECODE_SPLITS)
             return ext().gemm_decode(a, b)
         if native_gemm_supported(M, N, K, a.dtype, (K,)):
             out = torch.empty(M, N, device=a.device, dtype=a.dtype)

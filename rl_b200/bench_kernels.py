@@ -6,6 +6,7 @@
     python -m rl_b200.bench_kernels attn      [T_per_seq n_seq]
     python -m rl_b200.bench_kernels logprob   [T V]
     python -m rl_b200.bench_kernels fp8       [M N K]
+    python -m rl_b200.bench_kernels numerics  [prompts max_new]
 
 Each prints one line with the time and the achieved rate, and is small enough
 to be captured under ``ncu -k <kernel> -c 1`` (a few GB on the device at most).
@@ -208,13 +209,65 @@ def bench_logprob(T=8192, V=128256):
     print(f"logprob T={T} V={V}: {t:.3f} ms {T * V * 2 / (t * 1e-3) / 1e12:.2f} TB/s")
 
 
+def bench_numerics(prompts=64, max_new=256):
+    """Rollout-vs-trainer log-prob agreement on the Llama-3.1-8B shape (random
+    init): ``gen_kl_error`` (k3 estimator, as GRPO reports it) between the rollout
+    engine's sampled-token log-probs and the trainer's, and, as the floor it can
+    be read against, the same statistic between two trainer forwards that differ
+    only in the attention kernel (tcgen05 vs mma.sync).  A random 32-layer model
+    amplifies last-bit differences of any two valid kernels into log-prob noise;
+    this measures how much."""
+    import json
+    import math
+
+    import rl_b200.ops.attention as attn
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import single_process_state
+
+    dev = torch.device("cuda", 0)
+    mcfg = get_model_config("llama3.1-8b")
+    pcfg = {"model_name": "llama3.1-8b", "max_total_sequence_length": 512 + max_new, "precision": "bfloat16",
+            "train_global_batch_size": prompts,
+            "generation": {"temperature": 1.0, "top_p": 1.0, "top_k": None, "max_new_tokens": max_new,
+                           "max_num_seqs": 512, "mcore_generation_config": {"block_size_tokens": 256}},
+            "sequence_packing": {"train_mb_tokens": 16384, "logprob_mb_tokens": 32768}}
+    w = PolicyWorker(pcfg, model_cfg=mcfg, pstate=single_process_state(dev), seed=1234)
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(128, 513, (prompts,), generator=g)
+    ids = torch.randint(0, mcfg.vocab_size, (prompts, 512), generator=g)
+    out = w.generate(BatchedDataDict({"input_ids": ids, "input_lengths": lens}))
+    S = out["output_ids"].shape[1]
+    mask = torch.zeros(prompts, S, dtype=torch.bool)
+    for r in range(prompts):
+        mask[r, int(lens[r]):int(out["unpadded_sequence_lengths"][r])] = True
+    seqs = BatchedDataDict({"input_ids": out["output_ids"], "input_lengths": out["unpadded_sequence_lengths"]})
+
+    def k3(a, b):
+        d = (a.float() - b.float())[mask]
+        return float((torch.exp(d) - d - 1).mean()), float(d.pow(2).mean().sqrt())
+
+    lp = w.get_logprobs(seqs)["logprobs"]
+    gen_kl, gen_rms = k3(lp, out["logprobs"])
+    attn._ATTN_TC = not attn._ATTN_TC
+    try:
+        lp2 = w.get_logprobs(seqs)["logprobs"]
+    finally:
+        attn._ATTN_TC = not attn._ATTN_TC
+    self_kl, self_rms = k3(lp2, lp)
+    print(json.dumps({"gen_kl_error": gen_kl, "gen_rms_dlogp": gen_rms, "trainer_vs_trainer_other_attention_kl": self_kl,
+                      "trainer_vs_trainer_rms_dlogp": self_rms, "tokens": int(mask.sum()),
+                      "threshold": 0.002, "ln_vocab": math.log(mcfg.vocab_size)}))
+
+
 def main(argv=None):
     argv = list(sys.argv[1:] if argv is None else argv)
     what = argv.pop(0) if argv else "gemm"
     args = [int(x) for x in argv]
     torch.manual_seed(0)
     {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
-     "logprob": bench_logprob, "fp8": bench_fp8}[what](*args)
+     "logprob": bench_logprob, "fp8": bench_fp8, "numerics": bench_numerics}[what](*args)
 
 
 if __name__ == "__main__":

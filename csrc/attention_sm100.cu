@@ -354,6 +354,395 @@ fa_fwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__
   }
 }
 
+
+// ============================================================ backward
+//
+// One CTA per (128-key tile, kv head, sequence): K_t and V_t stay in shared
+// memory; the CTA walks every (query head of the group, 64-query block) that
+// sees the tile and accumulates dK_t and dV_t in tensor memory, so the group's
+// query heads are summed without atomics and dK / dV are written once, as bf16.
+// Per step (query block j of head h):
+//
+//   S^T  = K_t Q_j^T      M=128 keys, N=64 queries, K=128 dims   (A, B K-major)
+//   dP^T = V_t dO_j^T     same shape
+//   P^T  = exp2(S^T c - lse_j),  dS^T = P^T (dP^T - D_j) * scale  (compute warps,
+//          thread = key row; written to shared memory as bf16, K-major)
+//   dV  += P^T dO_j       M=128 keys, N=128 dims, K=64 queries    (dO_j read MN-major)
+//   dK  += dS^T Q_j       same, Q_j read MN-major
+//   dQ_j^T = K_t^T dS^T   M=128 dims, N=64 queries, K=128 keys    (both read MN-major)
+//
+// The same shared-memory bytes serve both majors: a K-major [rows x 64] tile of
+// 128-byte swizzled rows is also the MN-major layout of its transpose (rows = the
+// reduction index).  dQ_j^T leaves tensor memory through the compute warps into
+// an fp32 [64 x 128] staging tile that one thread adds into the global dQ
+// accumulator with a TMA bulk tensor reduce-add (cp.reduce.async.bulk.tensor),
+// so partial dQ tiles of different key tiles combine without per-element atomics.
+// TMEM: S^T 64 + dP^T 64 + dV 128 + dK 128 + dQ^T 64 columns (512 allocated).
+// Shared: K 32 KB + V 32 KB + 2 stages x (Q 16 KB + dO 16 KB) + P^T 16 KB +
+// dS^T 16 KB + dQ staging 32 KB + lse/D 512 B.  One CTA per SM.
+constexpr int BBQ = 64;                       // queries per step
+constexpr int KT_BYTES = 128 * HD * 2;        // 32 KB (K or V tile)
+constexpr int QB_BYTES = BBQ * HD * 2;        // 16 KB (Q or dO block)
+constexpr int PT_BYTES = 128 * BBQ * 2;       // 16 KB (P^T or dS^T)
+constexpr int DQ_BYTES = BBQ * HD * 4;        // 32 KB fp32 staging
+constexpr int BWD_SMEM = 2 * KT_BYTES + 2 * 2 * QB_BYTES + 2 * PT_BYTES + DQ_BYTES + 512 + 1024 + 256;
+constexpr uint32_t IDESC_ST = idesc_bf16(128, BBQ);                                   // S^T, dP^T
+constexpr uint32_t IDESC_DKV = idesc_bf16(128, HD) | (1u << 16);                      // dV, dK: B MN-major
+constexpr uint32_t IDESC_DQ = idesc_bf16(128, BBQ) | (1u << 15) | (1u << 16);        // dQ^T: A, B MN-major
+
+__device__ __forceinline__ uint64_t desc_mn_lbo(uint32_t saddr, uint32_t lbo) {
+  uint64_t d = 0;
+  d |= (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)((lbo >> 4) & 0x3FFFu) << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+__device__ __forceinline__ void bar_compute() { asm volatile("bar.sync 1, 128;\n" ::: "memory"); }
+
+__global__ void __launch_bounds__(192, 1)
+fa_bwd_tc_kernel(const __grid_constant__ CUtensorMap tq, const __grid_constant__ CUtensorMap tk,
+                 const __grid_constant__ CUtensorMap tv, const __grid_constant__ CUtensorMap tdo,
+                 const __grid_constant__ CUtensorMap tdq, const float* __restrict__ lse, const float* __restrict__ Dv,
+                 const int* __restrict__ cu, const int* __restrict__ seg, int nq, int nkv, float scale,
+                 float scale_log2, int causal, int T_total, __nv_bfloat16* __restrict__ dk,
+                 __nv_bfloat16* __restrict__ dv, float* __restrict__ dk_acc, float* __restrict__ dv_acc) {
+  extern __shared__ uint8_t smem_raw[];
+  const uint32_t raw = smem_u32(smem_raw);
+  const uint32_t base = (raw + 1023u) & ~1023u;
+  uint8_t* gbase = smem_raw + (base - raw);
+  const uint32_t sK = base;
+  const uint32_t sV = sK + KT_BYTES;
+  const uint32_t sQ = sV + KT_BYTES;              // stage s: sQ + s * QB_BYTES
+  const uint32_t sDO = sQ + 2 * QB_BYTES;         // stage s: sDO + s * QB_BYTES
+  const uint32_t sPT = sDO + 2 * QB_BYTES;
+  const uint32_t sDS = sPT + PT_BYTES;
+  const uint32_t sDQ = sDS + PT_BYTES;
+  float* dq_stage = reinterpret_cast<float*>(gbase + (sDQ - base));
+  float* lse_s = reinterpret_cast<float*>(gbase + (sDQ - base) + DQ_BYTES);  // [64] (log2 units)
+  float* d_s = lse_s + BBQ;                                                  // [64]
+  uint64_t* bars = reinterpret_cast<uint64_t*>(gbase + (sDQ - base) + DQ_BYTES + 512);
+  const uint32_t bar_kv = smem_u32(bars);
+  const uint32_t bar_full = bar_kv + 8;       // [2]
+  const uint32_t bar_empty = bar_full + 16;   // [2]
+  const uint32_t bar_sdp = bar_empty + 16;    // S^T and dP^T in TMEM
+  const uint32_t bar_sfree = bar_sdp + 8;     // compute warps read them (count 4)
+  const uint32_t bar_p = bar_sfree + 8;       // P^T and dS^T in shared memory (count 4)
+  const uint32_t bar_dq = bar_p + 8;          // dV, dK, dQ^T MMAs of the step complete
+  const uint32_t bar_dqfree = bar_dq + 8;     // compute warps read dQ^T (count 4)
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 10);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x;  // kv head
+  const int kt0 = blockIdx.y * 128;
+  const int b = blockIdx.z;
+  const int s0 = seg ? seg[4 * b] : cu[b];
+  const int L = seg ? seg[4 * b + 1] : cu[b + 1] - s0;
+  const int k0 = seg ? seg[4 * b + 2] : s0;
+  const int Lk = seg ? seg[4 * b + 3] : L;
+  const int off = Lk - L;
+  if (kt0 >= Lk) return;
+  const int G = nq / nkv;
+  const int nqb = (L + BBQ - 1) / BBQ;
+  // first query block that sees any key of the tile: 64 j + 63 + off >= kt0
+  const int jb = causal ? max(0, (kt0 - off - (BBQ - 1) + BBQ - 1) / BBQ) : 0;
+  const int per_head = max(0, nqb - jb);
+  const int nsteps = G * per_head;
+
+  if (threadIdx.x == 0) {
+    mbar_init(bar_kv, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(bar_full + 8 * s, 1);
+      mbar_init(bar_empty + 8 * s, 1);
+    }
+    mbar_init(bar_sdp, 1);
+    mbar_init(bar_sfree, 4);
+    mbar_init(bar_p, 4);
+    mbar_init(bar_dq, 1);
+    mbar_init(bar_dqfree, 4);
+    *abort_flag = 0;
+    asm volatile("fence.mbarrier_init.release.cluster;\n" ::: "memory");
+  }
+  if (warp == 1) {
+    asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;\n" ::"r"(smem_u32(tmem_slot)),
+                 "r"(512u));
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;\n" ::);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+  const uint32_t t_s = tmem, t_dp = tmem + 64, t_dv = tmem + 128, t_dk = tmem + 256, t_dq = tmem + 384;
+  auto step_of = [&](int i, int& h, int& j) {
+    h = g * G + i / per_head;
+    j = jb + i % per_head;
+  };
+
+  if (warp == 0) {
+    if (lane == 0 && nsteps > 0) {
+      mbar_expect_tx(bar_kv, 2 * KT_BYTES);
+      tma_3d(sK, &tk, bar_kv, 0, g, k0 + kt0);
+      tma_3d(sK + KT_BYTES / 2, &tk, bar_kv, 64, g, k0 + kt0);
+      tma_3d(sV, &tv, bar_kv, 0, g, k0 + kt0);
+      tma_3d(sV + KT_BYTES / 2, &tv, bar_kv, 64, g, k0 + kt0);
+      for (int i = 0; i < nsteps && !*abort_flag; ++i) {
+        const int s = i & 1;
+        if (!fwait(bar_empty + 8 * s, ((i >> 1) & 1) ^ 1, abort_flag, 11)) break;
+        int h, j;
+        step_of(i, h, j);
+        const int qr = s0 + j * BBQ;
+        mbar_expect_tx(bar_full + 8 * s, 2 * QB_BYTES);
+        tma_3d(sQ + s * QB_BYTES, &tq, bar_full + 8 * s, 0, h, qr);
+        tma_3d(sQ + s * QB_BYTES + QB_BYTES / 2, &tq, bar_full + 8 * s, 64, h, qr);
+        tma_3d(sDO + s * QB_BYTES, &tdo, bar_full + 8 * s, 0, h, qr);
+        tma_3d(sDO + s * QB_BYTES + QB_BYTES / 2, &tdo, bar_full + 8 * s, 64, h, qr);
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0 && nsteps > 0) {
+      bool ok = fwait(bar_kv, 0, abort_flag, 12);
+      // S^T / dP^T of step i+1 are issued as soon as the compute warps have read
+      // step i's (single TMEM buffer), ahead of step i's dV / dK / dQ MMAs: the
+      // tensor core computes them while the compute warps form P^T and dS^T.
+      auto issue_sdp = [&](int i) -> bool {
+        const int s = i & 1;
+        if (!fwait(bar_full + 8 * s, (i >> 1) & 1, abort_flag, 13)) return false;
+        tc_fence_after();
+        const uint32_t q0 = sQ + s * QB_BYTES, o0 = sDO + s * QB_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t ko = (kk >> 2) * (KT_BYTES / 2) + (kk & 3) * 32;
+          const uint32_t qo = (kk >> 2) * (QB_BYTES / 2) + (kk & 3) * 32;
+          umma_bf16(t_s, desc_kmajor_sw128(sK + ko), desc_kmajor_sw128(q0 + qo), IDESC_ST, kk > 0 ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < HD / 16; ++kk) {
+          const uint32_t ko = (kk >> 2) * (KT_BYTES / 2) + (kk & 3) * 32;
+          const uint32_t qo = (kk >> 2) * (QB_BYTES / 2) + (kk & 3) * 32;
+          umma_bf16(t_dp, desc_kmajor_sw128(sV + ko), desc_kmajor_sw128(o0 + qo), IDESC_ST, kk > 0 ? 1u : 0u);
+        }
+        umma_commit(bar_sdp);
+        return true;
+      };
+      if (ok) ok = issue_sdp(0);
+      for (int i = 0; i < nsteps && ok; ++i) {
+        const int s = i & 1;
+        if (i + 1 < nsteps) {
+          if (!fwait(bar_sfree, i & 1, abort_flag, 14)) break;
+          if (!issue_sdp(i + 1)) break;
+        }
+        if (!fwait(bar_p, i & 1, abort_flag, 15)) break;
+        if (!fwait(bar_dqfree, (i & 1) ^ 1, abort_flag, 16)) break;
+        tc_fence_after();
+        const uint32_t q0 = sQ + s * QB_BYTES, o0 = sDO + s * QB_BYTES;
+#pragma unroll
+        for (int kk = 0; kk < BBQ / 16; ++kk) {  // reduce over the 64 queries
+          umma_bf16(t_dv, desc_kmajor_sw128(sPT + kk * 32), desc_mn_lbo(o0 + kk * 2048, QB_BYTES / 2), IDESC_DKV,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(t_dk, desc_kmajor_sw128(sDS + kk * 32), desc_mn_lbo(q0 + kk * 2048, QB_BYTES / 2), IDESC_DKV,
+                    (i > 0 || kk > 0) ? 1u : 0u);
+        }
+#pragma unroll
+        for (int kk = 0; kk < 128 / 16; ++kk)  // reduce over the 128 keys
+          umma_bf16(t_dq, desc_mn_lbo(sK + kk * 2048, KT_BYTES / 2), desc_mn_lbo(sDS + kk * 2048, 8192u), IDESC_DQ,
+                    kk > 0 ? 1u : 0u);
+        umma_commit(bar_dq);
+        umma_commit(bar_empty + 8 * s);
+      }
+    }
+    __syncwarp();
+  } else {
+    // compute warps: TMEM lane = key row of the tile (S^T, dP^T, dV, dK) or dim (dQ^T)
+    const int quad = warp & 3;
+    const int r = quad * 32 + lane;
+    const int ct = threadIdx.x - 64;  // 0..127
+    const uint32_t lo = (uint32_t)(quad * 32) << 16;
+    const int kg = kt0 + r;  // key index within the sequence's keys
+    bool alive = nsteps > 0;
+    bool issued = false;  // a TMA reduce of the staging tile may be in flight (thread ct == 0)
+    // Every compute warp executes the same sequence of named barriers (bar 1) whatever
+    // happens to its waits: after a failed wait a warp skips the work but keeps
+    // stepping, so no warp is left at a named barrier (which cannot time out).
+    auto drain_dq = [&](int i, bool live) -> bool {  // dQ^T of step i: TMEM -> staging -> reduce-add
+      const bool ok = live && fwait(bar_dq, i & 1, abort_flag, 17);
+      if (ok) tc_fence_after();
+      int h, j;
+      step_of(i, h, j);
+      if (ct == 0 && issued) asm volatile("cp.async.bulk.wait_group.read 0;\n" ::: "memory");
+      bar_compute();
+      if (ok) {
+#pragma unroll 1
+        for (int c = 0; c < BBQ / 32; ++c) {
+          uint32_t u[32];
+          tmem_ld32(t_dq + lo + c * 32, u);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) dq_stage[(c * 32 + e) * HD + r] = __uint_as_float(u[e]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_dqfree);
+      }
+      asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+      bar_compute();
+      if (ct == 0 && ok && !*abort_flag) {
+        asm volatile(
+            "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%2, %3, %4}], [%1];\n" ::"l"(
+                &tdq),
+            "r"(sDQ), "r"(0), "r"(h), "r"(s0 + j * BBQ)
+            : "memory");
+        asm volatile("cp.async.bulk.commit_group;\n" ::: "memory");
+        issued = true;
+      }
+      return ok;
+    };
+    for (int i = 0; i < nsteps; ++i) {
+      int h, j;
+      step_of(i, h, j);
+      // this step's lse (log2 units) and D rows
+      bar_compute();
+      if (ct < BBQ) {
+        const int q = j * BBQ + ct;
+        lse_s[ct] = q < L ? lse[(long long)h * T_total + s0 + q] * 1.4426950408889634f : 0.f;
+      } else {
+        const int q = j * BBQ + ct - BBQ;
+        d_s[ct - BBQ] = q < L ? Dv[(long long)h * T_total + s0 + q] : 0.f;
+      }
+      bar_compute();
+      float sv[BBQ], pv[BBQ];
+      const bool ok = alive && fwait(bar_sdp, i & 1, abort_flag, 18);
+      if (ok) {
+        tc_fence_after();
+        uint32_t u[32];
+        tmem_ld32(t_s + lo, u);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[e] = __uint_as_float(u[e]);
+        tmem_ld32(t_s + lo + 32, u);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) sv[32 + e] = __uint_as_float(u[e]);
+        tmem_ld32(t_dp + lo, u);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pv[e] = __uint_as_float(u[e]);
+        tmem_ld32(t_dp + lo + 32, u);
+#pragma unroll
+        for (int e = 0; e < 32; ++e) pv[32 + e] = __uint_as_float(u[e]);
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_sfree);
+#pragma unroll
+        for (int c = 0; c < BBQ; ++c) {
+          const int q = j * BBQ + c;
+          const bool valid = kg < Lk && q < L && (!causal || kg <= q + off);
+          const float p = valid ? exp2f(sv[c] * scale_log2 - lse_s[c]) : 0.f;
+          sv[c] = p;
+          pv[c] = p * (pv[c] - d_s[c]) * scale;
+        }
+      }
+      alive = ok;
+      // the previous step's MMAs read P^T / dS^T: drain its dQ (and so wait for them) first
+      if (i > 0) alive = drain_dq(i - 1, alive) && alive;
+      if (alive) {
+        uint8_t* prow = gbase + (sPT - base) + r * 128;
+        uint8_t* drow = gbase + (sDS - base) + r * 128;
+#pragma unroll
+        for (int c = 0; c < 8; ++c) {
+          uint4 a, d;
+          uint32_t* pa = reinterpret_cast<uint32_t*>(&a);
+          uint32_t* pd = reinterpret_cast<uint32_t*>(&d);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            __nv_bfloat162 x = __floats2bfloat162_rn(sv[8 * c + 2 * e], sv[8 * c + 2 * e + 1]);
+            __nv_bfloat162 y = __floats2bfloat162_rn(pv[8 * c + 2 * e], pv[8 * c + 2 * e + 1]);
+            pa[e] = *reinterpret_cast<uint32_t*>(&x);
+            pd[e] = *reinterpret_cast<uint32_t*>(&y);
+          }
+          const int pos = (c ^ (r & 7)) << 4;
+          *reinterpret_cast<uint4*>(prow + pos) = a;
+          *reinterpret_cast<uint4*>(drow + pos) = d;
+        }
+        asm volatile("fence.proxy.async.shared::cta;\n" ::: "memory");
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(bar_p);
+      }
+    }
+    if (nsteps > 0) alive = drain_dq(nsteps - 1, alive);
+    // dK, dV rows of the tile (complete with the last step's commit)
+    const bool store = kg < Lk;
+    __nv_bfloat16* dkr = dk + ((long long)(k0 + kg) * nkv + g) * HD;
+    __nv_bfloat16* dvr = dv + ((long long)(k0 + kg) * nkv + g) * HD;
+    if (alive && nsteps > 0) {
+#pragma unroll 1
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t src = half == 0 ? t_dv : t_dk;
+        __nv_bfloat16* dst = half == 0 ? dvr : dkr;
+        float* acc = half == 0 ? dv_acc : dk_acc;
+#pragma unroll 1
+        for (int c = 0; c < HD / 32; ++c) {
+          uint32_t u[32];
+          tmem_ld32(src + lo + c * 32, u);
+          if (store && acc != nullptr) {
+            // segments that share keys (context parallelism) add into fp32 rows
+            float4* ar = reinterpret_cast<float4*>(acc + ((long long)(k0 + kg) * nkv + g) * HD + c * 32);
+#pragma unroll
+            for (int e = 0; e < 8; ++e)
+              atomicAdd(ar + e, make_float4(__uint_as_float(u[4 * e]), __uint_as_float(u[4 * e + 1]),
+                                            __uint_as_float(u[4 * e + 2]), __uint_as_float(u[4 * e + 3])));
+          } else if (store) {
+            uint4 v[4];
+            uint32_t* pvv = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+            for (int e = 0; e < 16; ++e) {
+              __nv_bfloat162 x = __floats2bfloat162_rn(__uint_as_float(u[2 * e]), __uint_as_float(u[2 * e + 1]));
+              pvv[e] = *reinterpret_cast<uint32_t*>(&x);
+            }
+#pragma unroll
+            for (int e = 0; e < 4; ++e) reinterpret_cast<uint4*>(dst + c * 32)[e] = v[e];
+          }
+        }
+      }
+    } else if (store && nsteps == 0 && dk_acc == nullptr) {
+      for (int d = 0; d < HD; ++d) {
+        dkr[d] = __float2bfloat16_rn(0.f);
+        dvr[d] = __float2bfloat16_rn(0.f);
+      }
+    }
+    if (ct == 0 && issued) asm volatile("cp.async.bulk.wait_group 0;\n" ::: "memory");
+    tc_fence_before();
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem), "r"(512u));
+  }
+}
+
+// D[h][t] = sum_d dO[t][h][d] * O[t][h][d] (fp32), one warp per (t, h)
+__global__ void fa_bwd_rowdot_kernel(const __nv_bfloat16* __restrict__ dout, const __nv_bfloat16* __restrict__ out,
+                                     long long rows, int nq, int T, float* __restrict__ D) {
+  const long long w = (blockIdx.x * (long long)blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (w >= rows) return;
+  const uint2 a = reinterpret_cast<const uint2*>(dout + w * HD)[lane];
+  const uint2 c = reinterpret_cast<const uint2*>(out + w * HD)[lane];
+  const __nv_bfloat162* pa = reinterpret_cast<const __nv_bfloat162*>(&a);
+  const __nv_bfloat162* pc = reinterpret_cast<const __nv_bfloat162*>(&c);
+  float acc = 0.f;
+#pragma unroll
+  for (int e = 0; e < 2; ++e) {
+    const float2 x = __bfloat1622float2(pa[e]), y = __bfloat1622float2(pc[e]);
+    acc += x.x * y.x + x.y * y.y;
+  }
+  acc = warp_sum(acc);
+  if (lane == 0) {
+    const long long t = w / nq;
+    const int h = (int)(w % nq);
+    D[(long long)h * T + t] = acc;
+  }
+}
+
 }  // namespace fa
 }  // namespace rlb
 
@@ -443,6 +832,90 @@ std::vector<at::Tensor> flash_attn_seg_fwd_tc(at::Tensor q, at::Tensor k, at::Te
             cp_flags ? reinterpret_cast<const uint32_t*>(cp_flags->data_ptr<int>()) : nullptr, (uint32_t)cp_epoch,
             (int)cp_size);
   return {o, lse};
+}
+
+
+namespace {
+
+// fp32 [T, heads, 128] accumulator as a 3-D tensor map with a 128 x 1 x 64 box
+// (no swizzle; the staging tile is [64 rows][128 floats]) for the bulk reduce-add.
+CUtensorMap dq_tmap(const at::Tensor& x) {
+  CUtensorMap m;
+  const int T = x.size(0), H = x.size(1);
+  cuuint64_t dims[3] = {(cuuint64_t)fa::HD, (cuuint64_t)H, (cuuint64_t)T};
+  cuuint64_t strides[2] = {(cuuint64_t)x.stride(1) * 4, (cuuint64_t)x.stride(0) * 4};
+  cuuint32_t box[3] = {(cuuint32_t)fa::HD, 1u, (cuuint32_t)fa::BBQ};
+  cuuint32_t estr[3] = {1u, 1u, 1u};
+  CUresult r = tma_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, x.data_ptr(), dims, strides, box, estr,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
+                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  TORCH_CHECK(r == CUDA_SUCCESS, "rl_b200 attention bwd (tcgen05): cuTensorMapEncodeTiled failed (", (int)r, ")");
+  return m;
+}
+
+std::vector<at::Tensor> bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
+                               at::Tensor lse, const int* cu, const int* seg, int nseg, int max_k, double scale,
+                               bool causal, bool accumulate_kv) {
+  check_view(q, "q");
+  check_view(k, "k");
+  check_view(v, "v");
+  check_view(dout, "dout");
+  TORCH_CHECK(dout.is_contiguous() && out.is_contiguous(), "rl_b200 attention bwd: dout / out must be contiguous");
+  const int T_ = q.size(0), nq = q.size(1), nkv = k.size(1), Tk = k.size(0);
+  TORCH_CHECK(nq % nkv == 0, "rl_b200 attention: nq must be a multiple of nkv");
+  auto dq_acc = at::zeros({T_, nq, fa::HD}, q.options().dtype(at::kFloat));
+  auto dk = at::zeros({Tk, nkv, fa::HD}, q.options());
+  auto dv = at::zeros({Tk, nkv, fa::HD}, q.options());
+  at::Tensor dk_acc, dv_acc;
+  if (accumulate_kv) {
+    dk_acc = at::zeros({Tk, nkv, fa::HD}, q.options().dtype(at::kFloat));
+    dv_acc = at::zeros({Tk, nkv, fa::HD}, q.options().dtype(at::kFloat));
+  }
+  if (T_ == 0 || nseg == 0 || max_k == 0) return {dq_acc.to(q.scalar_type()), dk, dv};
+  auto D = at::empty({nq, T_}, q.options().dtype(at::kFloat));
+  const long long rows = (long long)T_ * nq;
+  fa::fa_bwd_rowdot_kernel<<<(int)((rows * 32 + 255) / 256), 256, 0, stream()>>>(
+      (const __nv_bfloat16*)dout.data_ptr(), (const __nv_bfloat16*)out.data_ptr(), rows, nq, T_, D.data_ptr<float>());
+  const CUtensorMap tq = head_tmap(q, fa::BBQ);
+  const CUtensorMap tk = head_tmap(k, 128);
+  const CUtensorMap tv = head_tmap(v, 128);
+  const CUtensorMap tdo = head_tmap(dout, fa::BBQ);
+  const CUtensorMap tdq = dq_tmap(dq_acc);
+  auto kern = fa::fa_bwd_tc_kernel;
+  RLB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::BWD_SMEM));
+  dim3 grid(nkv, (max_k + 127) / 128, nseg);
+  kern<<<grid, 192, fa::BWD_SMEM, stream()>>>(tq, tk, tv, tdo, tdq, lse.data_ptr<float>(), D.data_ptr<float>(), cu,
+                                             seg, nq, nkv, (float)scale, (float)(scale * 1.4426950408889634),
+                                             causal ? 1 : 0, T_, (__nv_bfloat16*)dk.data_ptr(),
+                                             (__nv_bfloat16*)dv.data_ptr(),
+                                             accumulate_kv ? dk_acc.data_ptr<float>() : nullptr,
+                                             accumulate_kv ? dv_acc.data_ptr<float>() : nullptr);
+  RLB_CUDA_CHECK(cudaGetLastError());
+  if (accumulate_kv) return {dq_acc.to(q.scalar_type()), dk_acc.to(q.scalar_type()), dv_acc.to(q.scalar_type())};
+  return {dq_acc.to(q.scalar_type()), dk, dv};
+}
+
+}  // namespace
+
+// Same contract as flash_attn_bwd (head dim 128): {dq, dk, dv}, bf16.
+std::vector<at::Tensor> flash_attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
+                                          at::Tensor lse, at::Tensor cu_seqlens, int64_t max_seqlen, double scale,
+                                          bool causal) {
+  const c10::cuda::CUDAGuard guard(q.device());
+  auto cu = cu_seqlens.to(at::kInt).contiguous();
+  return bwd_tc(dout, q, k, v, out, lse, cu.data_ptr<int>(), nullptr, cu.size(0) - 1, (int)max_seqlen, scale, causal,
+                false);
+}
+
+// Segment form (context parallelism), same contract as flash_attn_seg_bwd.
+std::vector<at::Tensor> flash_attn_seg_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v,
+                                              at::Tensor out, at::Tensor lse, at::Tensor seg, int64_t max_k,
+                                              double scale) {
+  TORCH_CHECK(seg.is_cuda() && seg.scalar_type() == at::kInt && seg.dim() == 2 && seg.size(1) == 4 &&
+                  seg.is_contiguous(),
+              "rl_b200 segment attention: seg int32 [S, 4]");
+  const c10::cuda::CUDAGuard guard(q.device());
+  return bwd_tc(dout, q, k, v, out, lse, nullptr, seg.data_ptr<int>(), seg.size(0), (int)max_k, scale, true, true);
 }
 
 int64_t attn_tc_error_flag(bool reset) {

@@ -54,6 +54,12 @@ std::vector<at::Tensor> flash_attn_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor
 std::vector<at::Tensor> flash_attn_seg_fwd_tc(at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor seg, int64_t max_q,
                                               double scale, c10::optional<at::Tensor> cp_flags, int64_t cp_epoch,
                                               int64_t cp_size);
+std::vector<at::Tensor> flash_attn_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
+                                          at::Tensor lse, at::Tensor cu_seqlens, int64_t max_seqlen, double scale,
+                                          bool causal);
+std::vector<at::Tensor> flash_attn_seg_bwd_tc(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v,
+                                              at::Tensor out, at::Tensor lse, at::Tensor seg, int64_t max_k,
+                                              double scale);
 int64_t attn_tc_error_flag(bool reset);
 // gemm_sm100.cu
 void gemm_sm100(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, bool accumulate, int64_t tile);
@@ -145,6 +151,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("flash_attn_seg_fwd_tc", &flash_attn_seg_fwd_tc, py::arg("q"), py::arg("k"), py::arg("v"), py::arg("seg"),
         py::arg("max_q"), py::arg("scale"), py::arg("cp_flags") = py::none(), py::arg("cp_epoch") = 0,
         py::arg("cp_size") = 0, "tcgen05 segment flash-attention forward (head dim 128)");
+  m.def("flash_attn_bwd_tc", &flash_attn_bwd_tc, "tcgen05 varlen flash-attention backward (head dim 128)");
+  m.def("flash_attn_seg_bwd_tc", &flash_attn_seg_bwd_tc, "tcgen05 segment flash-attention backward (head dim 128)");
   m.def("attn_tc_error_flag", &attn_tc_error_flag, py::arg("reset") = false);
   m.def("peer_wait_cycles", &rlb::peer_wait_cycles,
         "bound (SM cycles) of every in-kernel wait on a peer's or a copy engine's flag");

@@ -138,10 +138,13 @@ def bench_attn(L=2048, n=8, nq=32, nkv=8, hd=128):
         res.append(f"fwd tcgen05 {t:.3f} ms {fl / t / 1e9:.1f}")
     t = _time(lambda: C.flash_attn_fwd(q.detach(), k.detach(), v.detach(), cu, L, sc, True))
     res.append(f"fwd mma.sync {t:.3f} ms {fl / t / 1e9:.1f}")
-    o = flash_attn_varlen(q, k, v, cu, L)
+    o, lse = C.flash_attn_fwd(q.detach(), k.detach(), v.detach(), cu, L, sc, True)
     g = torch.randn_like(o)
-    tb = _time(lambda: torch.autograd.grad(o, (q, k, v), g, retain_graph=True))
-    res.append(f"bwd {tb:.3f} ms {2.5 * fl / tb / 1e9:.1f}")
+    if hd == 128:
+        tb = _time(lambda: C.flash_attn_bwd_tc(g, q.detach(), k.detach(), v.detach(), o, lse, cu, L, sc, True))
+        res.append(f"bwd tcgen05 {tb:.3f} ms {2.5 * fl / tb / 1e9:.1f}")
+    tb = _time(lambda: C.flash_attn_bwd(g, q.detach(), k.detach(), v.detach(), o, lse, cu, L, sc, True))
+    res.append(f"bwd mma.sync {tb:.3f} ms {2.5 * fl / tb / 1e9:.1f}")
     try:
         from torch.nn.attention import SDPBackend, sdpa_kernel
 

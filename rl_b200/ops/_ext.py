@@ -29,6 +29,8 @@ _KERNELS_PER_CALL = {
     "sum_sq": 2,
     "flash_attn_bwd": 3,
     "flash_attn_seg_bwd": 3,
+    "flash_attn_bwd_tc": 3,
+    "flash_attn_seg_bwd_tc": 3,
     "paged_decode_attn": 1,
     "sample": 2,
     "gemm_error_flag": 0,

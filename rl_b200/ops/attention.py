@@ -64,6 +64,8 @@ def flash_attn_varlen_ref(q, k, v, cu_seqlens, scale: Optional[float] = None, ca
 
 # RL_B200_ATTN_TC=0 keeps the forward on the mma.sync kernel (A/B timing)
 _ATTN_TC = os.environ.get("RL_B200_ATTN_TC", "1") == "1"
+# RL_B200_ATTN_TC_BWD=0 keeps the backward on the mma.sync kernel (A/B timing)
+_TC_BWD = os.environ.get("RL_B200_ATTN_TC_BWD", "1") == "1"
 
 
 def _tc_ok(*xs) -> bool:
@@ -91,6 +93,22 @@ def fa_seg_forward(q, k, v, seg, max_q: int, scale: float, cp_flags=None, cp_epo
     return ext().flash_attn_seg_fwd(q, k, v, seg, int(max_q), float(scale), cp_flags, int(cp_epoch), int(cp_size))
 
 
+def fa_backward(do, q, k, v, o, lse, cu_seqlens, max_seqlen: int, scale: float, causal: bool):
+    """Native varlen backward: (dq, dk, dv), tcgen05 kernel when it applies."""
+    do = do.contiguous()
+    if _TC_BWD and _tc_ok(q, k, v, do) and o.is_contiguous():
+        return ext().flash_attn_bwd_tc(do, q, k, v, o, lse, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+    return ext().flash_attn_bwd(do, q, k, v, o, lse, cu_seqlens, int(max_seqlen), float(scale), bool(causal))
+
+
+def fa_seg_backward(do, q, k, v, o, lse, seg, max_k: int, scale: float):
+    """Native segment backward (context parallelism), tcgen05 when it applies."""
+    do = do.contiguous()
+    if _TC_BWD and _tc_ok(q, k, v, do) and o.is_contiguous():
+        return ext().flash_attn_seg_bwd_tc(do, q, k, v, o, lse, seg, int(max_k), float(scale))
+    return ext().flash_attn_seg_bwd(do, q, k, v, o, lse, seg, int(max_k), float(scale))
+
+
 class _FlashAttnVarlen(torch.autograd.Function):
     @staticmethod
     def forward(ctx, q, k, v, cu_seqlens, max_seqlen, scale, causal):
@@ -103,7 +121,7 @@ class _FlashAttnVarlen(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse, cu = ctx.saved_tensors
         max_seqlen, scale, causal = ctx.meta
-        dq, dk, dv = ext().flash_attn_bwd(do.contiguous(), q, k, v, o, lse, cu, max_seqlen, scale, causal)
+        dq, dk, dv = fa_backward(do, q, k, v, o, lse, cu, max_seqlen, scale, causal)
         return dq, dk, dv, None, None, None, None
 
 
@@ -126,7 +144,7 @@ class _FlashAttnSegments(torch.autograd.Function):
     def backward(ctx, do):
         q, k, v, o, lse, seg = ctx.saved_tensors
         max_k, scale = ctx.meta
-        dq, dk, dv = ext().flash_attn_seg_bwd(do.contiguous(), q, k, v, o, lse, seg, max_k, scale)
+        dq, dk, dv = fa_seg_backward(do, q, k, v, o, lse, seg, max_k, scale)
         return dq, dk, dv, None, None, None, None
 
 

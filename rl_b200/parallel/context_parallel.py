@@ -280,8 +280,9 @@ class _CPAttentionFused(torch.autograd.Function):
 
         q, kf, vf, o, lse, seg = ctx.saved_tensors
         lay = ctx.lay
-        dq, dk_n, dv_n = ext().flash_attn_seg_bwd(do.contiguous(), q, kf, vf, o, lse, seg, int(lay.max_k),
-                                                   float(ctx.scale))
+        from rl_b200.ops.attention import fa_seg_backward
+
+        dq, dk_n, dv_n = fa_seg_backward(do, q, kf, vf, o, lse, seg, int(lay.max_k), float(ctx.scale))
         n = dist.get_world_size(ctx.group)
         outs = []
         for g in (dk_n, dv_n):

@@ -64,6 +64,9 @@ int64_t attn_tc_error_flag(bool reset);
 // gemm_sm100.cu
 void gemm_sm100(at::Tensor a, at::Tensor b, at::Tensor out, bool a_mn, bool b_mn, bool accumulate, int64_t tile);
 int64_t gemm_sm100_error_flag(bool reset);
+std::vector<at::Tensor> gemm_logprob_partials(at::Tensor h, at::Tensor w, at::Tensor targets, double temperature);
+at::Tensor gemm_dlogits(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, at::Tensor dlp,
+                        double temperature);
 // gemm_grouped.cu
 at::Tensor grouped_gemm_nt(at::Tensor x, at::Tensor w, at::Tensor offs);
 int64_t grouped_gemm_error_flag(bool reset);
@@ -158,6 +161,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         "bound (SM cycles) of every in-kernel wait on a peer's or a copy engine's flag");
   m.def("set_peer_wait_cycles", &rlb::set_peer_wait_cycles, py::arg("cycles"));
   m.def("gemm_sm100_error_flag", &gemm_sm100_error_flag, py::arg("reset") = false);
+  m.def("gemm_logprob_partials", &gemm_logprob_partials);
+  m.def("gemm_dlogits", &gemm_dlogits);
   m.def("gemm_fp8", &gemm_fp8, py::arg("a"), py::arg("a_scale"), py::arg("b"), py::arg("b_scale"),
         py::arg("splits") = 0, "block-scaled e4m3 GEMM (1x128 activation, 128x128 weight fp32 scales) -> bf16");
   m.def("gemm_mxf8", &gemm_mxf8, py::arg("a"), py::arg("a_scale_t"), py::arg("b"), py::arg("b_scale_t"),

@@ -12,7 +12,16 @@
 //   wgrad    dW = dy^T x : A = dy [T, N] MN-major, B = x  [T, K] MN-major (reduce over T)
 // Epilogues: bf16 store, fp32 store, or fp32 read-add-write (the weight gradient
 // accumulated straight into an fp32 main-grad buffer; each output tile has one
-// owner, so no atomics).
+// owner, so no atomics).  Two more serve the LM head of the RL losses, where the
+// product is the logits of a vocabulary (shard) and must never reach HBM:
+//   EPI_LOGPROB : each epilogue thread owns one token row of the tile and reduces
+//                 its 256 logits (scaled by 1/temperature) to the online-softmax
+//                 state (max, sum exp, sum x exp) of that tile, written as
+//                 [3, num_n_tiles, M] fp32 partials, plus the target's logit; a
+//                 small kernel then merges the partials over the tiles.
+//   EPI_DLOGITS : the backward recomputes the tile and stores
+//                 dlogits = dlogp / T * (onehot(target) - exp(x / T - lse)) in bf16,
+//                 the input of the dgrad / wgrad products (no logits pass between).
 //
 // Two tile shapes, one source:
 //   PAIR = false : one CTA per SM computes 128 x 256 tiles (tcgen05.mma.cta_group::1,
@@ -59,7 +68,19 @@ __device__ int g_gemm_error = 0;
 constexpr int EPI_BF16 = 0;     // C bf16 = acc
 constexpr int EPI_F32 = 1;      // C fp32 = acc
 constexpr int EPI_F32_ADD = 2;  // C fp32 += acc
+constexpr int EPI_LOGPROB = 3;  // per-tile softmax partials of acc / T (C unused)
+constexpr int EPI_DLOGITS = 4;  // C bf16 = d logprob / d logits
 constexpr int GROUP = 8;
+
+// Per-row inputs / outputs of the two LM-head epilogues (unused otherwise).
+struct LpArgs {
+  const long long* tgt;  // [M] target id within this vocabulary shard (outside [0, N): not in this shard)
+  const float* lse;      // [M] log-sum-exp of the whole (all-shard) row       (EPI_DLOGITS)
+  const float* dlp;      // [M] d loss / d logprob                             (EPI_DLOGITS)
+  float* part;           // [3, num_n, M] tile max, sum exp, sum x*exp         (EPI_LOGPROB)
+  float* xt;             // [M] target logit / T; pre-zeroed                  (EPI_LOGPROB)
+  float inv_temp;
+};
 
 __device__ __forceinline__ uint32_t cluster_rank() {
   uint32_t r;
@@ -189,7 +210,7 @@ struct Cfg {
 template <bool PAIR, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1)
 gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b, void* __restrict__ C,
-            int M, int N, int K, long long ldc) {
+            int M, int N, int K, long long ldc, const LpArgs lp) {
   using G = Cfg<PAIR, A_MN, B_MN>;
   constexpr int STAGES = G::STAGES;
   constexpr int A_BYTES = G::A_BYTES, B_BYTES = G::B_BYTES;
@@ -340,6 +361,18 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
       tc_fence_after();
       const int m = mt * G::TM + row_in;
       const uint32_t trow = tmem_base + ((uint32_t)(quad * 32) << 16) + acc * G::TN;
+      // LM-head epilogues: this thread's row state
+      [[maybe_unused]] long long tgt = -1;
+      [[maybe_unused]] float lm = -INFINITY, ls = 0.f, lu = 0.f, gsc = 0.f, lrow = 0.f;
+      if constexpr (EPI == EPI_LOGPROB || EPI == EPI_DLOGITS) {
+        if (m < M) tgt = lp.tgt[m];
+        if constexpr (EPI == EPI_DLOGITS) {
+          if (m < M) {
+            gsc = lp.dlp[m] * lp.inv_temp;
+            lrow = lp.lse[m];
+          }
+        }
+      }
 #pragma unroll 1
       for (int c = 0; c < G::TN / 32; ++c) {
         uint32_t r[32];
@@ -347,7 +380,56 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
         const int n0 = nt * G::TN + c * 32;
         if (m >= M || n0 >= N) continue;
         const bool full = n0 + 32 <= N;
-        if constexpr (EPI == EPI_BF16) {
+        if constexpr (EPI == EPI_LOGPROB) {
+          float f[32];
+          float cm = -INFINITY;
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            f[j] = (full || n0 + j < N) ? __uint_as_float(r[j]) * lp.inv_temp : -INFINITY;
+            cm = fmaxf(cm, f[j]);
+          }
+          if (cm > lm) {  // one rescale per 32 columns
+            const float sc = __expf(lm - cm);
+            ls *= sc;
+            lu *= sc;
+            lm = cm;
+          }
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float e = __expf(f[j] - lm);
+            ls += e;
+            lu += e > 0.f ? f[j] * e : 0.f;  // masked columns: e = 0 (and f = -inf)
+          }
+          const long long d = tgt - n0;
+          if (d >= 0 && d < 32 && tgt < N) {  // a target past the shard's edge belongs to another shard
+            float xv = 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) xv = (j == (int)d) ? f[j] : xv;
+            lp.xt[m] = xv;
+          }
+        } else if constexpr (EPI == EPI_DLOGITS) {
+          __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (long long)m * ldc + n0;
+          float g[32];
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const float p = __expf(__uint_as_float(r[j]) * lp.inv_temp - lrow);
+            g[j] = gsc * ((tgt == (long long)(n0 + j) ? 1.f : 0.f) - p);
+          }
+          if (full && (ldc % 8) == 0) {
+            uint4 v[4];
+            uint32_t* pv = reinterpret_cast<uint32_t*>(v);
+#pragma unroll
+            for (int j = 0; j < 16; ++j) {
+              __nv_bfloat162 h = __floats2bfloat162_rn(g[2 * j], g[2 * j + 1]);
+              pv[j] = *reinterpret_cast<uint32_t*>(&h);
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) reinterpret_cast<uint4*>(dst)[j] = v[j];
+          } else {
+            for (int j = 0; j < 32; ++j)
+              if (n0 + j < N) dst[j] = __float2bfloat16_rn(g[j]);
+          }
+        } else if constexpr (EPI == EPI_BF16) {
           __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(C) + (long long)m * ldc + n0;
           if (full && (ldc % 8) == 0) {
             uint4 v[4];
@@ -389,6 +471,15 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
           }
         }
       }
+      if constexpr (EPI == EPI_LOGPROB) {
+        if (m < M) {
+          const long long plane = (long long)num_n * M;
+          const long long o = (long long)nt * M + m;
+          lp.part[o] = lm;
+          lp.part[plane + o] = ls;
+          lp.part[2 * plane + o] = lu;
+        }
+      }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -407,6 +498,58 @@ gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ 
     } else {
       asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;\n" ::"r"(tmem_base), "r"(TMEM_COLS));
     }
+  }
+}
+
+// Merge the per-tile softmax states of EPI_LOGPROB over the vocabulary tiles:
+// part [3, nt, M] -> m, s, u [M].  Block = 32 rows x 8 warps; warp w merges tiles
+// w, w + 8, ... of its lane's row (loads coalesced over 32 consecutive rows), then
+// the 8 warp states are merged through shared memory.
+__global__ void __launch_bounds__(256)
+lp_tile_merge_kernel(const float* __restrict__ part, int nt, int M, float* __restrict__ m_out,
+                     float* __restrict__ s_out, float* __restrict__ u_out) {
+  __shared__ float sh[3][8][33];
+  const int lane = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int row = blockIdx.x * 32 + lane;
+  const long long plane = (long long)nt * M;
+  float m = -INFINITY, s = 0.f, u = 0.f;
+  if (row < M) {
+    for (int t = w; t < nt; t += 8) {
+      const long long o = (long long)t * M + row;
+      const float tm = part[o], ts = part[plane + o], tu = part[2 * plane + o];
+      if (tm == -INFINITY) continue;
+      if (tm > m) {
+        const float f = __expf(m - tm);  // m = -inf -> 0
+        s = s * f + ts;
+        u = u * f + tu;
+        m = tm;
+      } else {
+        const float f = __expf(tm - m);
+        s += ts * f;
+        u += tu * f;
+      }
+    }
+  }
+  sh[0][w][lane] = m;
+  sh[1][w][lane] = s;
+  sh[2][w][lane] = u;
+  __syncthreads();
+  if (w == 0 && row < M) {
+    float M_ = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) M_ = fmaxf(M_, sh[0][i][lane]);
+    float S = 0.f, U = 0.f;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float tm = sh[0][i][lane];
+      if (tm == -INFINITY) continue;
+      const float f = __expf(tm - M_);
+      S += sh[1][i][lane] * f;
+      U += sh[2][i][lane] * f;
+    }
+    m_out[row] = M_;
+    s_out[row] = S;
+    u_out[row] = U;
   }
 }
 
@@ -433,7 +576,8 @@ CUtensorMap tmap_bf16(const void* ptr, int64_t rows, int64_t cols, int box_cols,
 }
 
 template <bool PAIR, bool A_MN, bool B_MN, int EPI>
-void launch(const at::Tensor& a, const at::Tensor& b, void* c, int M, int N, int K, long long ldc, int max_units) {
+void launch(const at::Tensor& a, const at::Tensor& b, void* c, int M, int N, int K, long long ldc, int max_units,
+            const g100::LpArgs& lp = g100::LpArgs{}) {
   using G = g100::Cfg<PAIR, A_MN, B_MN>;
   // K-major operands: box = 64 K-columns x staged rows; MN-major: 64 x 64 boxes
   const CUtensorMap ta = A_MN ? tmap_bf16(a.data_ptr(), K, M, 64, 64) : tmap_bf16(a.data_ptr(), M, K, 64, G::CM);
@@ -468,7 +612,7 @@ void launch(const at::Tensor& a, const at::Tensor& b, void* c, int M, int N, int
   }
   const int units = std::max(1, std::min({tiles, max_units, res}));
   cfg.gridDim = dim3(units * (PAIR ? 2 : 1));
-  RLB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, c, M, N, K, ldc));
+  RLB_CUDA_CHECK(cudaLaunchKernelEx(&cfg, kern, ta, tb, c, M, N, K, ldc, lp));
 }
 
 template <bool PAIR, int EPI>
@@ -532,4 +676,78 @@ int64_t gemm_sm100_error_flag(bool reset) {
     RLB_CUDA_CHECK(cudaMemcpyToSymbol(g100::g_gemm_error, &z, sizeof(int)));
   }
   return v;
+}
+
+namespace {
+
+void check_lm_head(const at::Tensor& h, const at::Tensor& w, const at::Tensor& targets) {
+  TORCH_CHECK(h.is_cuda() && w.is_cuda() && targets.is_cuda(), "rl_b200 lm-head gemm: CUDA tensors expected");
+  TORCH_CHECK(h.scalar_type() == at::kBFloat16 && w.scalar_type() == at::kBFloat16,
+              "rl_b200 lm-head gemm: bf16 hidden states and weight expected");
+  TORCH_CHECK(h.dim() == 2 && w.dim() == 2 && h.is_contiguous() && w.is_contiguous() && h.size(1) == w.size(1),
+              "rl_b200 lm-head gemm: hidden [T, H] and weight [V, H], contiguous");
+  TORCH_CHECK(h.size(1) % 8 == 0, "rl_b200 lm-head gemm: hidden size must be a multiple of 8");
+  TORCH_CHECK(reinterpret_cast<uintptr_t>(h.data_ptr()) % 16 == 0 && reinterpret_cast<uintptr_t>(w.data_ptr()) % 16 == 0,
+              "rl_b200 lm-head gemm: operands must be 16-byte aligned");
+  TORCH_CHECK(targets.scalar_type() == at::kLong && targets.dim() == 1 && targets.size(0) == h.size(0) &&
+                  targets.is_contiguous(),
+              "rl_b200 lm-head gemm: targets int64 [T]");
+}
+
+template <int EPI>
+void launch_nt(const at::Tensor& a, const at::Tensor& b, void* c, int M, int N, int K, long long ldc,
+               const g100::LpArgs& lp) {
+  const int sms = num_sms();
+  const long long t2 = (long long)((M + 255) / 256) * ((N + 255) / 256);
+  if (t2 >= sms / 2) launch<true, false, false, EPI>(a, b, c, M, N, K, ldc, sms / 2, lp);
+  else launch<false, false, false, EPI>(a, b, c, M, N, K, ldc, sms, lp);
+}
+
+}  // namespace
+
+// LM head fused with the log-prob reductions (forward): for hidden [T, H] and this
+// rank's vocabulary shard weight [V, H], returns per row (max, sum exp, sum x exp,
+// target logit) of x = hidden @ weight^T / temperature over the shard, fp32 [T]
+// each; targets are ids within the shard (others contribute no target logit).
+// The logits exist only in tensor memory.
+std::vector<at::Tensor> gemm_logprob_partials(at::Tensor h, at::Tensor w, at::Tensor targets, double temperature) {
+  check_lm_head(h, w, targets);
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int M = h.size(0), N = w.size(0), K = h.size(1);
+  auto o = h.options().dtype(at::kFloat);
+  auto m = at::empty({M}, o), s = at::empty({M}, o), u = at::empty({M}, o), xt = at::zeros({M}, o);
+  if (M == 0 || N == 0) return {m.fill_(-INFINITY), s.zero_(), u.zero_(), xt};
+  const int nt = (N + 255) / 256;
+  auto part = at::empty({3, nt, M}, o);
+  g100::LpArgs lp{};
+  lp.tgt = reinterpret_cast<const long long*>(targets.data_ptr<int64_t>());
+  lp.part = part.data_ptr<float>();
+  lp.xt = xt.data_ptr<float>();
+  lp.inv_temp = (float)(1.0 / temperature);
+  launch_nt<g100::EPI_LOGPROB>(h, w, nullptr, M, N, K, N, lp);
+  g100::lp_tile_merge_kernel<<<(M + 31) / 32, 256, 0, stream()>>>(part.data_ptr<float>(), nt, M, m.data_ptr<float>(),
+                                                                  s.data_ptr<float>(), u.data_ptr<float>());
+  RLB_CUDA_CHECK(cudaGetLastError());
+  return {m, s, u, xt};
+}
+
+// LM head fused with the log-prob gradient (backward): recomputes the logits tile
+// and writes dlogits = dlp / T * (onehot(target) - exp(x / T - lse)) as bf16 [T, V].
+at::Tensor gemm_dlogits(at::Tensor h, at::Tensor w, at::Tensor targets, at::Tensor lse, at::Tensor dlp,
+                        double temperature) {
+  check_lm_head(h, w, targets);
+  TORCH_CHECK(lse.scalar_type() == at::kFloat && dlp.scalar_type() == at::kFloat && lse.is_contiguous() &&
+                  dlp.is_contiguous() && lse.numel() == h.size(0) && dlp.numel() == h.size(0),
+              "rl_b200 gemm_dlogits: lse and dlp fp32 [T]");
+  const c10::cuda::CUDAGuard guard(h.device());
+  const int M = h.size(0), N = w.size(0), K = h.size(1);
+  auto out = at::empty({M, N}, h.options());
+  if (M == 0 || N == 0) return out;
+  g100::LpArgs lp{};
+  lp.tgt = reinterpret_cast<const long long*>(targets.data_ptr<int64_t>());
+  lp.lse = lse.data_ptr<float>();
+  lp.dlp = dlp.data_ptr<float>();
+  lp.inv_temp = (float)(1.0 / temperature);
+  launch_nt<g100::EPI_DLOGITS>(h, w, out.data_ptr(), M, N, K, N, lp);
+  return out;
 }

@@ -5,6 +5,8 @@
     python -m rl_b200.bench_kernels decode_gemm [M]
     python -m rl_b200.bench_kernels attn      [T_per_seq n_seq]
     python -m rl_b200.bench_kernels logprob   [T V]
+    python -m rl_b200.bench_kernels lmhead    [T H V]
+    python -m rl_b200.bench_kernels lmhead_fwd [T H V]   (fused forward only: the ncu case)
     python -m rl_b200.bench_kernels fp8       [M N K]
     python -m rl_b200.bench_kernels numerics  [prompts max_new]
 
@@ -212,6 +214,67 @@ def bench_logprob(T=8192, V=128256):
     print(f"logprob T={T} V={V}: {t:.3f} ms {T * V * 2 / (t * 1e-3) / 1e12:.2f} TB/s")
 
 
+def bench_lmhead(T=8192, H=4096, V=128256):
+    """LM head + log-prob / entropy, forward and backward, on the fused tcgen05
+    epilogues against the two-pass path (logits tile stored as bf16, then a
+    separate reduction / gradient kernel), same GEMM kernels otherwise."""
+    from rl_b200.ops import gemm as G
+    from rl_b200.ops._ext import ext
+    from rl_b200.ops.logprob import _bwd_inplace, _combine, logprob_partials
+
+    dev = torch.device("cuda")
+    C = ext()
+    h = torch.randn(T, H, device=dev).to(torch.bfloat16)
+    W = (torch.randn(V, H, device=dev) * H ** -0.5).to(torch.bfloat16)
+    tg = torch.randint(0, V, (T,), device=dev)
+    dlp = torch.randn(T, device=dev)
+    acc = torch.zeros(V, H, device=dev)
+    fl = 2 * T * H * V
+
+    def fwd_fused():
+        return _combine(*C.gemm_logprob_partials(h, W, tg, 1.0), None)
+
+    def fwd_two_pass():
+        lg = G.mm_nt(h, W)
+        return _combine(*logprob_partials(lg, tg, 1.0), None)
+
+    lse = fwd_fused()[0]
+
+    def bwd_fused():
+        d = C.gemm_dlogits(h, W, tg, lse, dlp, 1.0)
+        G.mm_nn(d, W)
+        G.mm_tn_accumulate(d, h, acc)
+
+    def bwd_two_pass():
+        lg = G.mm_nt(h, W)
+        _bwd_inplace(dlp, lg, tg, lse, 1.0, lg)
+        G.mm_nn(lg, W)
+        G.mm_tn_accumulate(lg, h, acc)
+
+    tf, t2 = _time(fwd_fused), _time(fwd_two_pass)
+    tb, tb2 = _time(bwd_fused), _time(bwd_two_pass)
+    tg_ = _time(lambda: G.mm_nt(h, W))
+    wb = (V * H + T * H) * 2
+    print(f"lmhead fwd T={T} H={H} V={V}: fused {tf:.3f} ms {fl / tf / 1e9:.1f} TFLOP/s | two-pass {t2:.3f} ms | "
+          f"GEMM alone (bf16 logits out) {tg_:.3f} ms | weight+hidden bytes / fused time "
+          f"{wb / (tf * 1e-3) / 1e12:.2f} TB/s")
+    print(f"lmhead bwd: fused {tb:.3f} ms {3 * fl / tb / 1e9:.1f} TFLOP/s | two-pass {tb2:.3f} ms")
+
+
+def bench_lmhead_fwd(T=4096, H=4096, V=128256):
+    """Only the fused LM-head log-prob forward (GEMM + tile merge), 3 warm-up and
+    10 timed launches: the small case for an ncu capture of its GEMM."""
+    from rl_b200.ops._ext import ext
+
+    dev = torch.device("cuda")
+    h = torch.randn(T, H, device=dev).to(torch.bfloat16)
+    W = (torch.randn(V, H, device=dev) * H ** -0.5).to(torch.bfloat16)
+    tg = torch.randint(0, V, (T,), device=dev)
+    t = _time(lambda: ext().gemm_logprob_partials(h, W, tg, 1.0))
+    fl = 2 * T * H * V
+    print(f"lmhead_fwd T={T} H={H} V={V}: {t:.3f} ms {fl / t / 1e9:.1f} TFLOP/s")
+
+
 def bench_numerics(prompts=64, max_new=256):
     """Rollout-vs-trainer log-prob agreement on the Llama-3.1-8B shape (random
     init): ``gen_kl_error`` (k3 estimator, as GRPO reports it) between the rollout
@@ -270,7 +333,7 @@ def main(argv=None):
     args = [int(x) for x in argv]
     torch.manual_seed(0)
     {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
-     "logprob": bench_logprob, "fp8": bench_fp8, "numerics": bench_numerics}[what](*args)
+     "logprob": bench_logprob, "lmhead": bench_lmhead, "lmhead_fwd": bench_lmhead_fwd, "fp8": bench_fp8, "numerics": bench_numerics}[what](*args)
 
 
 if __name__ == "__main__":

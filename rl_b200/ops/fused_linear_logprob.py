@@ -4,13 +4,22 @@ Counterpart of the reference's fused linear cross-entropy
 (``ChunkedDistributedHiddenStatesToLogprobs``, ``nemo_rl/distributed/model_utils.py:2572``,
 enabled by ``use_fused_linear_logprobs`` / ``fused_linear_logprobs_chunk_size``).
 
-Forward, per chunk of ``chunk`` tokens: ``logits = h_c @ W^T`` (vocab shard), the
-fused partials kernel reduces them to (max, sumexp, sum x*exp, target logit),
-and the logits chunk is dropped.  Only ``hidden``, the weight and the per-token
-log-sum-exp are saved.  Backward, per chunk: recompute the logits, turn them
-in place into ``dlogits``, then ``dh_c = dlogits @ W`` and
-``W.main_grad += dlogits^T @ h_c``.  Peak extra memory is one ``[chunk, V/tp]``
-bf16 tile instead of the full ``[T, V]`` logits (plus their fp32 gradient).
+On CUDA both passes are one tcgen05 GEMM each (``csrc/gemm_sm100.cu``):
+
+* forward: the LM-head product's epilogue reduces every 256-column logits tile
+  in tensor memory to per-row online-softmax partials (max, sum exp, sum x exp)
+  and the target's logit; a small kernel merges the tiles.  No logits reach
+  HBM: the traffic is the weight, the hidden states and 12 bytes per row per
+  256 vocabulary columns of partials.
+* backward: the same product recomputes each tile and its epilogue writes
+  ``dlogits = dlogp / T * (onehot - softmax)`` as bf16, which feeds the dgrad
+  (``dh_c = dlogits @ W``) and wgrad (``W.main_grad += dlogits^T @ h_c``)
+  products directly.
+
+Elsewhere (CPU) the chunked reference path materialises one ``[chunk, V/tp]``
+logits tile at a time.  Only ``hidden``, the weight and the per-token
+log-sum-exp are saved for the backward.  Under tensor parallelism the per-row
+partials of the shards are combined (max, then rescaled sums) over the group.
 """
 
 from __future__ import annotations
@@ -21,22 +30,41 @@ import torch
 import torch.distributed as dist
 
 from rl_b200.ops import gemm as _gemm
+from rl_b200.ops._ext import ext, use_native
 from rl_b200.ops.logprob import _bwd_inplace, _combine, logprob_partials
 
 __all__ = ["linear_logprobs"]
+
+# Tokens per fused forward launch: no logits tile is kept, only 12 bytes of
+# partials per row per 256 vocabulary columns (~6 KB per token at V = 128K).
+FUSED_FWD_CHUNK = 16384
+
+
+def _fused_ok(hidden: torch.Tensor, weight: torch.Tensor) -> bool:
+    """The tcgen05 LM-head kernels take bf16 [T, H] x [V, H] with H % 8 == 0."""
+    return (use_native(hidden) and hidden.dtype == torch.bfloat16 and weight.dtype == torch.bfloat16
+            and hidden.dim() == 2 and hidden.shape[1] % 8 == 0 and weight.is_contiguous()
+            and hidden.data_ptr() % 16 == 0 and weight.data_ptr() % 16 == 0)
 
 
 class _LinearLogprob(torch.autograd.Function):
     @staticmethod
     def forward(ctx, hidden, weight, targets, vocab_start, temperature, group, chunk):
         T = hidden.shape[0]
-        tl = (targets - vocab_start).to(torch.int64)
+        tl = (targets - vocab_start).to(torch.int64).contiguous()
+        fused = _fused_ok(hidden, weight)
+        if fused:
+            hidden = hidden.contiguous()
+        step = max(chunk, FUSED_FWD_CHUNK) if fused else chunk
         lps, ents, lses = [], [], []
-        for s in range(0, T, chunk):
-            e = min(T, s + chunk)
-            logits = _gemm.mm_nt(hidden[s:e], weight)
-            m, sm, u, xt = logprob_partials(logits, tl[s:e], temperature)
-            del logits
+        for s in range(0, T, step):
+            e = min(T, s + step)
+            if fused:
+                m, sm, u, xt = ext().gemm_logprob_partials(hidden[s:e], weight, tl[s:e], float(temperature))
+            else:
+                logits = _gemm.mm_nt(hidden[s:e], weight)
+                m, sm, u, xt = logprob_partials(logits, tl[s:e], temperature)
+                del logits
             lse, lp, ent = _combine(m, sm, u, xt, group)
             lps.append(lp)
             ents.append(ent)
@@ -61,11 +89,16 @@ class _LinearLogprob(torch.autograd.Function):
         if main is None and ctx.needs_input_grad[1]:
             dw = torch.zeros(weight.shape, dtype=torch.float32, device=weight.device)
         acc = main if main is not None else dw
-        dlp = dlp.float()
+        dlp = dlp.float().contiguous()
+        fused = _fused_ok(hidden, weight)
         for s in range(0, T, chunk):
             e = min(T, s + chunk)
-            logits = _gemm.mm_nt(hidden[s:e], weight)
-            _bwd_inplace(dlp[s:e], logits, tl[s:e], lse[s:e], ctx.temperature, logits)
+            if fused:
+                logits = ext().gemm_dlogits(hidden[s:e], weight, tl[s:e], lse[s:e].contiguous(), dlp[s:e],
+                                            float(ctx.temperature))
+            else:
+                logits = _gemm.mm_nt(hidden[s:e], weight)
+                _bwd_inplace(dlp[s:e], logits, tl[s:e], lse[s:e], ctx.temperature, logits)
             dh[s:e] = _gemm.mm_nn(logits, weight)
             if acc is not None:
                 _gemm.mm_tn_accumulate(logits, hidden[s:e], acc)

@@ -129,6 +129,48 @@ def test_fused_linear_logprobs(cuda_device):
     assert rel_err(W.grad, Wr.grad) < 3e-2
 
 
+def test_lm_head_logprob_epilogues(cuda_device):
+    """The tcgen05 LM-head GEMM with the log-prob epilogues against an fp32
+    PyTorch reference: softmax partials (logits never stored), entropy, target
+    log-prob, vocabulary shards combined as under tensor parallelism, and the
+    dlogits epilogue of the backward.  Shapes cover the 1-CTA and 2-CTA tiles,
+    ragged row / vocabulary edges and targets outside a shard."""
+    from rl_b200.ops._ext import ext
+    from rl_b200.ops.logprob import _combine
+
+    torch.manual_seed(5)
+    for T, H, V, temp in ((300, 256, 5000, 1.0), (4096, 1024, 32000, 0.7), (77, 512, 1000, 1.3)):
+        h = torch.randn(T, H, device=cuda_device).to(torch.bfloat16)
+        W = (torch.randn(V, H, device=cuda_device) * (2.0 / H ** 0.5)).to(torch.bfloat16)
+        tgt = torch.randint(0, V, (T,), device=cuda_device)
+        x = (h.float() @ W.float().t()) / temp
+        lse_r = torch.logsumexp(x, -1)
+        lp_r = x.gather(1, tgt[:, None]).squeeze(1) - lse_r
+        p_r = torch.softmax(x, -1)
+        ent_r = lse_r - (p_r * x).sum(-1)
+        m, s, u, xt = ext().gemm_logprob_partials(h, W, tgt.long(), float(temp))
+        lse, lp, ent = _combine(m, s, u, xt, None)
+        assert torch.allclose(lse, lse_r, atol=2e-3, rtol=1e-4), (T, V)
+        assert torch.allclose(lp, lp_r, atol=2e-3, rtol=1e-4), (T, V)
+        assert torch.allclose(ent, ent_r, atol=2e-3, rtol=1e-3), (T, V)
+        # two vocabulary shards (the second not a multiple of 256 wide), combined by hand
+        cut = (V // 2 // 8) * 8 + 8
+        parts = []
+        for lo, hi in ((0, cut), (cut, V)):
+            parts.append(ext().gemm_logprob_partials(h, W[lo:hi].contiguous(), (tgt - lo).long(), float(temp)))
+        gm = torch.maximum(parts[0][0], parts[1][0])
+        ss = sum(pp[1] * torch.exp(pp[0] - gm) for pp in parts)
+        lse2 = gm + torch.log(ss)
+        lp2 = parts[0][3] + parts[1][3] - lse2
+        assert torch.allclose(lp2, lp_r, atol=2e-3, rtol=1e-4), (T, V)
+        # backward epilogue: dlogits = dlp / T * (onehot - softmax)
+        dlp = torch.randn(T, device=cuda_device)
+        d = ext().gemm_dlogits(h, W, tgt.long(), lse_r.contiguous(), dlp, float(temp))
+        oh = torch.zeros_like(x).scatter_(1, tgt[:, None], 1.0)
+        d_r = dlp[:, None] / temp * (oh - p_r)
+        assert rel_err(d, d_r) < 1e-2, (T, V)
+
+
 def test_sampling(cuda_device):
     from rl_b200.ops.sampling import sample_tokens
 

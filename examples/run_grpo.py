@@ -9,6 +9,13 @@ overrides), initialises the process groups from the torchrun environment
 (TP / CP / EP sizes from ``policy.megatron_cfg``), builds the policy worker,
 the sharded prompt loader and the environments, and runs ``grpo_train`` with
 checkpointing and logging.  Resumes from the latest checkpoint when present.
+
+Data: a ``data.train`` block (the reference's schema: dataset names or local
+files, processors, prompt files, ``env_name`` per dataset) is tokenised with
+``policy.tokenizer`` (a local tokenizer directory, or ``name: byte``) and
+served with its environments through ``setup_response_data``; without one, the
+prompts are synthetic token ids (``num_prompts``, ``min/max_prompt_len``) and
+the environments come from the ``env:`` block.
 """
 
 from __future__ import annotations
@@ -60,15 +67,32 @@ def main(argv=None) -> dict:
                           ep=int(mc.get("expert_model_parallel_size", 1)),
                           pp=int(mc.get("pipeline_model_parallel_size", 1)))
     mcfg = get_model_config(cfg["policy"]["model_name"])
-    policy = PolicyWorker(cfg["policy"], model_cfg=mcfg, pstate=ps, seed=int(cfg["grpo"].get("seed", 0)))
-    d = cfg.get("data", {})
-    task = next(iter(cfg.get("env", {"synthetic": {}})))
-    ds = SyntheticPromptDataset(int(d.get("num_prompts", 1024)), int(d.get("min_prompt_len", 16)),
-                                int(d.get("max_prompt_len", 64)), mcfg.vocab_size, seed=int(cfg["grpo"].get("seed", 0)),
-                                task_name=task)
+    d = cfg.get("data", {}) or {}
+    seed = int(cfg["grpo"].get("seed", 0))
+    tokenizer, val_dl, val_envs = None, None, None
+    if d.get("train"):
+        from rl_b200.data.tokenizer import get_tokenizer
+        from rl_b200.data.utils import setup_response_data
+
+        tokenizer = get_tokenizer(cfg["policy"].get("tokenizer") or {"name": cfg["policy"]["model_name"]})
+        gen = cfg["policy"].setdefault("generation", {})
+        gen.setdefault("pad_token_id", tokenizer.pad_token_id)
+        if gen.get("stop_token_ids") is None:
+            gen["stop_token_ids"] = [tokenizer.eos_token_id]
+        ds, val_ds, envs, val_envs = setup_response_data(tokenizer, d, cfg.get("env", {}))
+        if val_ds is not None:
+            val_bs = int(cfg["grpo"].get("val_batch_size", cfg["grpo"]["num_prompts_per_step"]))
+            val_bs = max(ps.dp_size, val_bs - val_bs % ps.dp_size)
+            val_dl = StatefulDataLoader(val_ds, val_bs, shuffle=False, drop_last=False, shard_rank=ps.dp_rank,
+                                        num_shards=ps.dp_size)
+    else:
+        task = next(iter(cfg.get("env", {"synthetic": {}})))
+        ds = SyntheticPromptDataset(int(d.get("num_prompts", 1024)), int(d.get("min_prompt_len", 16)),
+                                    int(d.get("max_prompt_len", 64)), mcfg.vocab_size, seed=seed, task_name=task)
+        envs = build_envs(cfg.get("env", {}))
     dl = StatefulDataLoader(ds, int(cfg["grpo"]["num_prompts_per_step"]), shuffle=bool(d.get("shuffle", True)),
-                            seed=int(cfg["grpo"].get("seed", 0)), shard_rank=ps.dp_rank, num_shards=ps.dp_size)
-    envs = build_envs(cfg.get("env", {}))
+                            seed=seed, shard_rank=ps.dp_rank, num_shards=ps.dp_size)
+    policy = PolicyWorker(cfg["policy"], model_cfg=mcfg, pstate=ps, seed=seed)
     ck = CheckpointManager(cfg.get("checkpointing", {})) if cfg.get("checkpointing", {}).get("enabled") else None
     state = GRPOSaveState.default()
     if ck is not None and ck.get_latest_checkpoint_path():
@@ -95,7 +119,9 @@ def main(argv=None) -> dict:
         state = async_grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state,
                                  replay_buffer=buf)
     else:
-        state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
+        encode = (lambda text: tokenizer(text, add_special_tokens=False)["input_ids"]) if tokenizer else None
+        state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state,
+                           val_dataloader=val_dl, val_task_to_env=val_envs, tokenizer=encode)
     logger.close()
     policy.shutdown()
     return state

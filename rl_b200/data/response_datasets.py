@@ -1,0 +1,488 @@
+"""Response datasets: raw rows (local files or the Hugging Face cache) formatted
+into ``{"messages": [...], "task_name": ...}`` rows for the task processors.
+
+Reference: ``nemo_rl/data/datasets/raw_dataset.py`` (``RawDataset``),
+``nemo_rl/data/datasets/response_datasets/__init__.py`` (``DATASET_REGISTRY``,
+``load_response_dataset``) and ``nemo_rl/data/datasets/utils.py:97``
+(``load_dataset_from_path``).  The registry keys, the constructor keywords of
+each dataset (``split``, ``subset``, ``split_validation_size``, ``seed``,
+``output_key``, ``variant``, ``repeat``, ...), the ``messages`` row format and the
+task names are kept, so the reference's ``data:`` YAML blocks select the same
+data here.
+
+Design: rows stay in whatever container they were loaded into (a list of
+dicts, or an Arrow-backed ``datasets.Dataset``) and are formatted lazily on
+access by ``Rows``, so a million-row corpus is not rewritten in memory before
+training starts.  Every named dataset also takes ``data_path``: a local file
+(``.jsonl`` / ``.json`` / ``.parquet`` / ``.csv`` / ``.arrow`` / ``.txt``) or a
+``save_to_disk`` directory holding the hub dataset's raw columns; without it
+the hub id is read through ``datasets.load_dataset``, which in an offline
+container resolves only from the local Hugging Face cache.
+"""
+
+from __future__ import annotations
+
+import csv
+import importlib
+import inspect
+import json
+import os
+import random
+from typing import Any, Callable, Optional, Sequence
+
+from rl_b200.data.processors import TaskDataSpec, get_processor
+
+__all__ = ["Rows", "load_rows", "RawDataset", "ResponseDataset", "OpenAIFormatDataset", "OpenMathInstruct2Dataset",
+           "DAPOMath17KDataset", "DAPOMathAIME2024Dataset", "DeepScalerDataset", "GSM8KDataset", "AIMEDataset",
+           "NuminaMath15Dataset", "OpenR1Math220KDataset", "SquadDataset", "Tulu3SftMixtureDataset",
+           "HelpSteer3Dataset", "DATASET_REGISTRY", "load_response_dataset"]
+
+
+class Rows:
+    """Indexable view over ``base`` rows: an optional index list (selection /
+    split / repetition) and a chain of per-row formatters applied on access."""
+
+    def __init__(self, base: Any, fmts: Sequence[Callable[[dict], dict]] = (), index: Optional[list[int]] = None):
+        self.base = base
+        self.fmts = tuple(fmts)
+        self.index = index
+
+    def __len__(self) -> int:
+        return len(self.index) if self.index is not None else len(self.base)
+
+    def raw(self, i: int) -> dict:
+        return self.base[self.index[i] if self.index is not None else i]
+
+    def __getitem__(self, i: int) -> dict:
+        if i < 0:
+            i += len(self)
+        row = self.raw(i)
+        for f in self.fmts:
+            row = f(row)
+        return row
+
+    def __iter__(self):
+        for i in range(len(self)):
+            yield self[i]
+
+    def map(self, fn: Callable[[dict], dict]) -> "Rows":
+        return Rows(self.base, self.fmts + (fn,), self.index)
+
+    def select(self, positions: Sequence[int]) -> "Rows":
+        idx = [self.index[p] for p in positions] if self.index is not None else list(positions)
+        return Rows(self.base, self.fmts, idx)
+
+    def filter(self, pred: Callable[[dict], bool]) -> "Rows":
+        """Keep rows whose formatted value satisfies ``pred`` (one pass)."""
+        return self.select([i for i in range(len(self)) if pred(self[i])])
+
+    def repeat(self, n: int) -> "Rows":
+        return self.select(list(range(len(self))) * max(1, int(n)))
+
+    def train_test_split(self, test_size: float | int, seed: int) -> tuple["Rows", "Rows"]:
+        """Seeded shuffle, then the first ``test_size`` rows (a fraction below 1 or a
+        row count) become the test part."""
+        n = len(self)
+        n_test = int(test_size) if test_size >= 1 else max(1, int(round(n * float(test_size))))
+        order = list(range(n))
+        random.Random(seed).shuffle(order)
+        return self.select(sorted(order[n_test:])), self.select(sorted(order[:n_test]))
+
+
+def _read_local(path: str) -> list[dict]:
+    ext = os.path.splitext(path)[-1].lower()
+    if path.lower().endswith(".jsonl.packed") or ext == ".jsonl":
+        with open(path, encoding="utf-8") as f:
+            return [json.loads(line) for line in f if line.strip()]
+    if ext == ".json":
+        with open(path, encoding="utf-8") as f:
+            txt = f.read()
+        try:
+            obj = json.loads(txt)
+        except json.JSONDecodeError:  # JSON lines under a .json name
+            return [json.loads(line) for line in txt.splitlines() if line.strip()]
+        if isinstance(obj, dict):  # columnar {"col": [...]}
+            cols = list(obj)
+            return [dict(zip(cols, vals)) for vals in zip(*(obj[c] for c in cols))]
+        return list(obj)
+    if ext == ".parquet":
+        import pyarrow.parquet as pq
+
+        return pq.read_table(path).to_pylist()
+    if ext == ".arrow":
+        import pyarrow as pa
+
+        with pa.memory_map(path) as src:
+            try:
+                return pa.ipc.open_stream(src).read_all().to_pylist()
+            except pa.ArrowInvalid:
+                return pa.ipc.open_file(src).read_all().to_pylist()
+    if ext == ".csv":
+        with open(path, encoding="utf-8", newline="") as f:
+            return list(csv.DictReader(f))
+    if ext == ".txt":
+        with open(path, encoding="utf-8") as f:
+            return [{"text": line.rstrip("\n")} for line in f]
+    raise ValueError(f"unsupported data file type {ext!r} ({path})")
+
+
+def load_rows(data_path: str, subset: Optional[str] = None, split: Optional[str] = "train") -> Rows:
+    """Rows of a local file, a ``save_to_disk`` directory, or a Hugging Face
+    dataset id (resolved through the local cache when offline)."""
+    if os.path.isfile(data_path):
+        if subset is not None:
+            raise ValueError("a subset applies only to Hugging Face datasets")
+        return Rows(_read_local(data_path))
+    import datasets
+
+    if os.path.isdir(data_path) and (os.path.exists(os.path.join(data_path, "dataset_info.json"))
+                                      or os.path.exists(os.path.join(data_path, "dataset_dict.json"))):
+        ds = datasets.load_from_disk(data_path)
+    else:
+        try:
+            ds = datasets.load_dataset(data_path, subset) if subset else datasets.load_dataset(data_path)
+        except Exception as e:  # noqa: BLE001 - say what to do offline
+            raise RuntimeError(
+                f"could not load dataset {data_path!r} ({type(e).__name__}: {e}); without network access pass "
+                f"data_path pointing at a local copy of its rows (jsonl / json / parquet / csv / arrow) or a "
+                f"save_to_disk directory") from e
+    if isinstance(ds, datasets.DatasetDict):
+        if split:
+            ds = ds[split]
+        elif "train" in ds:
+            ds = ds["train"]
+    return Rows(ds)
+
+
+def _messages(user: str, assistant: Any, system: Optional[str] = None) -> list[dict]:
+    msgs = [{"role": "system", "content": system}] if system is not None else []
+    return msgs + [{"role": "user", "content": user}, {"role": "assistant", "content": assistant}]
+
+
+class RawDataset:
+    """A loaded dataset: formatted ``dataset`` rows, an optional ``val_dataset``
+    split off it, and (after ``set_task_spec`` / ``set_processor``) the task's
+    prompt spec and processor."""
+
+    task_name: str = "default"
+    dataset: Rows
+    val_dataset: Optional[Rows] = None
+    preprocessor: Optional[Callable[[dict], dict]] = None
+
+    def split_train_validation(self, test_size: float | int, seed: int) -> None:
+        if test_size and test_size > 0:
+            self.dataset, self.val_dataset = self.dataset.train_test_split(test_size, seed)
+
+    def set_task_spec(self, data_config: dict) -> None:
+        self.data_config = data_config
+        self.task_spec = TaskDataSpec(task_name=self.task_name, prompt_file=data_config.get("prompt_file"),
+                                      system_prompt_file=data_config.get("system_prompt_file"))
+
+    def set_processor(self) -> None:
+        self.processor = get_processor((getattr(self, "data_config", None) or {}).get("processor", "default"))
+
+
+class _HubResponseDataset(RawDataset):
+    """A hub dataset read from ``data_path`` or its hub id, formatted row by row."""
+
+    HUB: str = ""
+    SUBSET: Optional[str] = None
+    SPLIT: str = "train"
+
+    def _load(self, data_path: Optional[str], subset: Optional[str], split: Optional[str]) -> Rows:
+        if data_path:
+            return load_rows(data_path, None if os.path.isfile(data_path) else subset,
+                             None if os.path.isfile(data_path) else split)
+        return load_rows(self.HUB, subset, split)
+
+    def format_data(self, row: dict) -> dict:  # pragma: no cover - overridden
+        raise NotImplementedError
+
+
+class OpenMathInstruct2Dataset(_HubResponseDataset):
+    HUB = "nvidia/OpenMathInstruct-2"
+
+    def __init__(self, output_key: str = "expected_answer", split: str = "train_1M",
+                 split_validation_size: float = 0.05, seed: int = 42, data_path: Optional[str] = None, **_):
+        if split not in ("train", "train_1M", "train_2M", "train_5M"):
+            raise ValueError(f"OpenMathInstruct-2 split must be train / train_1M / train_2M / train_5M, not {split!r}")
+        self.task_name = "OpenMathInstruct-2"
+        self.output_key = output_key
+        self.dataset = self._load(data_path, None, split).map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        return {"messages": _messages(row["problem"], row[self.output_key]), "task_name": self.task_name}
+
+
+class DAPOMath17KDataset(_HubResponseDataset):
+    HUB = "BytedTsinghua-SIA/DAPO-Math-17k"
+    TASK = "DAPOMath17K"
+
+    def __init__(self, data_path: Optional[str] = None, **_):
+        self.task_name = self.TASK
+        self.dataset = self._load(data_path, None, "train").map(self.format_data)
+        self.val_dataset = None
+
+    def format_data(self, row):
+        # verl-style rows: prompt = [{"role": "user", "content": ...}], reward_model.ground_truth
+        return {"messages": _messages(row["prompt"][0]["content"], row["reward_model"]["ground_truth"]),
+                "task_name": self.task_name}
+
+
+class DAPOMathAIME2024Dataset(DAPOMath17KDataset):
+    HUB = "BytedTsinghua-SIA/AIME-2024"
+    TASK = "DAPOMathAIME2024"
+
+
+class DeepScalerDataset(_HubResponseDataset):
+    HUB = "agentica-org/DeepScaleR-Preview-Dataset"
+
+    def __init__(self, data_path: Optional[str] = None, **_):
+        self.task_name = "DeepScaler"
+        self.dataset = self._load(data_path, None, "train").map(self.format_data)
+        self.val_dataset = None
+
+    def format_data(self, row):
+        return {"messages": _messages(row["problem"], row["answer"]), "task_name": self.task_name}
+
+
+def _after_hashes(text: str) -> Optional[str]:
+    """GSM8K answers end in ``#### <final answer>``."""
+    return text.split("####", 1)[1].strip() if "####" in text else None
+
+
+class GSM8KDataset(_HubResponseDataset):
+    HUB = "openai/gsm8k"
+
+    def __init__(self, subset: Optional[str] = "main", split: str = "train", extract_answer: bool = True,
+                 data_path: Optional[str] = None, **_):
+        self.task_name = "gsm8k"
+        self.extract_answer = extract_answer
+        self.dataset = self._load(data_path, subset or "main", split).map(self.format_data)
+        self.val_dataset = None
+
+    def format_data(self, row):
+        ans = _after_hashes(row["answer"]) if self.extract_answer else row["answer"]
+        return {"messages": _messages(row["question"], ans), "task_name": self.task_name}
+
+
+class AIMEDataset(_HubResponseDataset):
+    _VARIANTS = {"2024": ("HuggingFaceH4/aime_2024", None, "train", "problem"),
+                 "2025": ("opencompass/AIME2025", ("AIME2025-I", "AIME2025-II"), "test", "question"),
+                 "2026": ("MathArena/aime_2026", None, "train", "problem")}
+
+    def __init__(self, variant: str = "2024", repeat: int = 1, data_path: Optional[str] = None, **_):
+        if variant not in self._VARIANTS:
+            raise ValueError(f"AIME variant must be one of {sorted(self._VARIANTS)}, not {variant!r}")
+        repo, subsets, split, self.input_key = self._VARIANTS[variant]
+        self.task_name = f"AIME{variant}"
+        if data_path:
+            rows = self._load(data_path, None, split)
+        elif subsets:
+            parts = [load_rows(repo, s, split) for s in subsets]
+            rows = Rows([r for p in parts for r in p])
+        else:
+            rows = load_rows(repo, None, split)
+        self.dataset = rows.map(self.format_data).repeat(repeat)
+        self.val_dataset = None
+
+    def format_data(self, row):
+        key = self.input_key if self.input_key in row else ("problem" if "problem" in row else "question")
+        return {"messages": _messages(row[key], str(row["answer"])), "task_name": self.task_name}
+
+
+class NuminaMath15Dataset(_HubResponseDataset):
+    HUB = "AI-MO/NuminaMath-1.5"
+    UNVERIFIABLE = frozenset({"proof", "notfound"})
+
+    def __init__(self, split: str = "train", verifiable_only: bool = True, require_valid: bool = True,
+                 split_validation_size: float = 0.0, seed: int = 42, data_path: Optional[str] = None, **_):
+        self.task_name = "NuminaMath-1.5"
+        rows = self._load(data_path, None, split)
+        if verifiable_only:
+            rows = rows.filter(self._verifiable)
+        if require_valid:
+            rows = rows.filter(lambda r: r.get("problem_is_valid") == "Yes" and r.get("solution_is_valid") == "Yes")
+        self.dataset = rows.map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    @classmethod
+    def _verifiable(cls, row) -> bool:
+        ans = (row.get("answer") or "").strip()
+        if not ans or ans.lower() in cls.UNVERIFIABLE:
+            return False
+        return (row.get("question_type") or "").strip().lower() != "proof"
+
+    def format_data(self, row):
+        return {"messages": _messages(row["problem"], row["answer"]), "task_name": self.task_name}
+
+
+class OpenR1Math220KDataset(_HubResponseDataset):
+    HUB = "open-r1/OpenR1-Math-220k"
+
+    def __init__(self, subset: Optional[str] = "default", split: str = "train", split_validation_size: float = 0.0,
+                 seed: int = 42, data_path: Optional[str] = None, **_):
+        self.task_name = "OpenR1-Math-220k"
+        self.dataset = self._load(data_path, subset or "default", split).map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        return {"messages": _messages(row["problem"], row["answer"]), "task_name": self.task_name}
+
+
+class SquadDataset(_HubResponseDataset):
+    HUB = "rajpurkar/squad"
+
+    def __init__(self, split: str = "train", data_path: Optional[str] = None, **_):
+        self.task_name = "squad"
+        self.dataset = self._load(data_path, None, split).map(self.format_data)
+        self.val_dataset = None
+
+    def format_data(self, row):
+        return {"messages": _messages(row["question"], row["answers"]["text"][0], system=row["context"]),
+                "task_name": self.task_name}
+
+
+class Tulu3SftMixtureDataset(_HubResponseDataset):
+    HUB = "allenai/tulu-3-sft-mixture"
+
+    def __init__(self, split_validation_size: float = 0.05, seed: int = 42, max_samples: Optional[int] = None,
+                 data_path: Optional[str] = None, **_):
+        self.task_name = "tulu3_sft_mixture"
+        rows = self._load(data_path, None, "train")
+        if max_samples:
+            order = list(range(len(rows)))
+            random.Random(seed).shuffle(order)
+            rows = rows.select(order[:min(int(max_samples), len(rows))])
+        self.dataset = rows.map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        msgs = row["messages"]
+        if not msgs or msgs[-1]["role"] != "assistant":
+            raise ValueError("tulu-3 rows must end with an assistant turn")
+        return {"messages": msgs, "task_name": self.task_name}
+
+
+class HelpSteer3Dataset(_HubResponseDataset):
+    """HelpSteer3 preference rows as RL prompts: the context, with the preferred
+    response (``overall_preference`` < 0: response1; > 0: response2; 0: response1)
+    kept as the reference answer."""
+
+    HUB = "nvidia/HelpSteer3"
+
+    def __init__(self, split: str = "train", data_path: Optional[str] = None, **_):
+        self.task_name = "HelpSteer3"
+        self.dataset = self._load(data_path, "preference", split).map(self.format_data)
+        self.val_dataset = None
+
+    def format_data(self, row):
+        pref = row["overall_preference"]
+        chosen = row["response2"] if pref > 0 else row["response1"]
+        ctx = row["context"]
+        ctx = [{"role": "user", "content": ctx}] if isinstance(ctx, str) else ctx
+        return {"context": ctx, "response": [{"role": "assistant", "content": chosen}], "task_name": self.task_name}
+
+
+def _task_name_of_path(path: str) -> str:
+    name = "-".join(path.rstrip("/").split("/")[-2:]).split(".")[0]
+    return name.lstrip("-") or "dataset"
+
+
+class ResponseDataset(RawDataset):
+    """Generic ``{input_key: prompt, output_key: answer}`` rows (or rows that
+    already carry ``messages``) from a local file or a hub id."""
+
+    def __init__(self, data_path: str, input_key: str = "input", output_key: str = "output",
+                 subset: Optional[str] = None, split: Optional[str] = None, split_validation_size: float = 0,
+                 seed: int = 42, **_):
+        self.input_key, self.output_key = input_key, output_key
+        self.task_name = _task_name_of_path(data_path)
+        self.dataset = load_rows(data_path, subset, split).map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        if "messages" in row:
+            return {**row, "task_name": row.get("task_name") or self.task_name}
+        return {"messages": _messages(row[self.input_key], row[self.output_key]), "task_name": self.task_name}
+
+
+class OpenAIFormatDataset(RawDataset):
+    """Chat rows ``{chat_key: [{"role", "content"[, "tool_calls"]}...]}``, each row kept
+    exactly as written (no schema filling), with an optional system prompt."""
+
+    def __init__(self, data_path: str, chat_key: str = "messages", system_key: Optional[str] = None,
+                 system_prompt: Optional[str] = None, tool_key: str = "tools", split_validation_size: float = 0,
+                 seed: int = 42, **_):
+        self.chat_key, self.system_key, self.system_prompt, self.tool_key = chat_key, system_key, system_prompt, tool_key
+        self.task_name = _task_name_of_path(data_path)
+        self.dataset = load_rows(data_path, None, None).map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        msgs = list(row[self.chat_key])
+        sys_txt = row.get(self.system_key) if self.system_key else None
+        sys_txt = sys_txt or self.system_prompt
+        if sys_txt and (not msgs or msgs[0]["role"] != "system"):
+            msgs = [{"role": "system", "content": sys_txt}] + msgs
+        out = {"messages": msgs, "task_name": self.task_name}
+        if row.get(self.tool_key):
+            out["tools"] = row[self.tool_key]
+        return out
+
+
+DATASET_REGISTRY: dict[str, Callable[..., RawDataset]] = {
+    "OpenMathInstruct-2": OpenMathInstruct2Dataset,
+    "DAPOMath17K": DAPOMath17KDataset,
+    "DAPOMathAIME2024": DAPOMathAIME2024Dataset,
+    "DeepScaler": DeepScalerDataset,
+    "GSM8K": GSM8KDataset,
+    "gsm8k": GSM8KDataset,
+    "AIME2024": lambda **kw: AIMEDataset(variant="2024", **{k: v for k, v in kw.items() if k != "variant"}),
+    "AIME2025": lambda **kw: AIMEDataset(variant="2025", **{k: v for k, v in kw.items() if k != "variant"}),
+    "AIME2026": lambda **kw: AIMEDataset(variant="2026", **{k: v for k, v in kw.items() if k != "variant"}),
+    "NuminaMath-1.5": NuminaMath15Dataset,
+    "OpenR1-Math-220k": OpenR1Math220KDataset,
+    "squad": SquadDataset,
+    "tulu3_sft_mixture": Tulu3SftMixtureDataset,
+    "HelpSteer3": HelpSteer3Dataset,
+    "openai_format": OpenAIFormatDataset,
+    "ResponseDataset": ResponseDataset,
+}
+
+
+def _external_class(dotted: str) -> Callable[..., RawDataset]:
+    mod, _, name = dotted.rpartition(".")
+    try:
+        cls = getattr(importlib.import_module(mod), name)
+    except (ImportError, AttributeError) as e:
+        raise ValueError(f"cannot import dataset class {dotted!r}: {e}") from e
+    if not inspect.isclass(cls):
+        raise ValueError(f"{dotted!r} is not a class")
+    return cls
+
+
+def load_response_dataset(data_config: dict) -> RawDataset:
+    """Build the dataset a ``data.train`` / ``data.validation`` entry names:
+    a registry key, or a dotted import path of a ``RawDataset`` subclass; then bind
+    its task spec (prompt / system prompt files) and processor."""
+    name = data_config["dataset_name"]
+    if name in DATASET_REGISTRY:
+        factory = DATASET_REGISTRY[name]
+    elif "." in name:
+        factory = _external_class(name)
+    else:
+        raise ValueError(f"unknown dataset_name {name!r}: use one of {sorted(DATASET_REGISTRY)}, 'ResponseDataset' "
+                         f"for a local file, or a dotted path to a dataset class")
+    kwargs = {k: v for k, v in data_config.items() if k != "dataset_name"}
+    ds = factory(**kwargs)
+    ds.set_task_spec(data_config)
+    ds.set_processor()
+    return ds

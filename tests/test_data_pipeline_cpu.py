@@ -1,0 +1,187 @@
+"""Data pipeline: tokenizer / chat templates, task processors, response datasets
+from local files, ``setup_response_data`` and a GRPO run on a JSONL math set
+through ``examples/run_grpo.py`` (CPU)."""
+
+from __future__ import annotations
+
+import json
+import os
+
+import pytest
+import torch
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def _math_rows(n=24):
+    return [{"problem": f"What is {i} + {i + 1}?", "expected_answer": str(2 * i + 1)} for i in range(n)]
+
+
+def _write_jsonl(path, rows):
+    with open(path, "w") as f:
+        for r in rows:
+            f.write(json.dumps(r) + "\n")
+    return str(path)
+
+
+def test_byte_tokenizer_and_templates():
+    from rl_b200.data.tokenizer import get_tokenizer
+
+    tok = get_tokenizer({"name": "byte"})
+    msgs = [{"role": "system", "content": "Be brief."}, {"role": "user", "content": "Hi"}]
+    text = tok.apply_chat_template(msgs, tokenize=False, add_generation_prompt=True)
+    assert text == "<|system|>\nBe brief.\n<|user|>\nHi\n<|assistant|>\n"
+    ids = tok(text, return_tensors="pt")["input_ids"][0]
+    assert tok.decode(ids) == text and int(ids.max()) < tok.vocab_size
+    # chat_template: null -> passthrough; a custom template string
+    assert get_tokenizer({"name": "byte", "chat_template": None}).apply_chat_template(msgs, tokenize=False) == \
+        "Be brief.Hi"
+    custom = get_tokenizer({"name": "byte", "chat_template": "{% for m in messages %}[{{ m['content'] }}]{% endfor %}"})
+    assert custom.apply_chat_template(msgs, tokenize=False) == "[Be brief.][Hi]"
+
+
+def test_format_message_log_attributes_every_token():
+    from rl_b200.data.processors import format_message_log
+    from rl_b200.data.tokenizer import ByteTokenizer
+
+    tok = ByteTokenizer()
+    conv = [{"role": "user", "content": "2+2?"}, {"role": "assistant", "content": "4"},
+            {"role": "user", "content": "and 3+3?"}, {"role": "assistant", "content": "6"}]
+    log = format_message_log(conv, tok)
+    assert [m["role"] for m in log] == ["user", "assistant", "user", "assistant"]
+    flat = torch.cat([m["token_ids"] for m in log])
+    whole = tok.encode(tok.apply_chat_template(conv, tokenize=False))
+    assert flat.tolist() == [tok.bos_token_id] + whole + [tok.eos_token_id]
+    assert tok.decode(log[1]["token_ids"]) == "<|assistant|>\n4\n"
+
+
+def test_math_processors_prompt_file_and_length_mask(tmp_path):
+    from rl_b200.data.processors import TaskDataSpec, math_data_processor, math_hf_data_processor
+    from rl_b200.data.tokenizer import ByteTokenizer
+
+    tok = ByteTokenizer()
+    pf = tmp_path / "prompt.txt"
+    pf.write_text("Solve: {}\nPut the answer in \\boxed{{}}.")
+    sf = tmp_path / "sys.txt"
+    sf.write_text("You are a math tutor.")
+    spec = TaskDataSpec("math", prompt_file=str(pf), system_prompt_file=str(sf))
+    d = math_hf_data_processor({"messages": [{"role": "user", "content": "1+1"},
+                                             {"role": "assistant", "content": "2"}], "task_name": "m"},
+                               spec, tok, 4096, 7)
+    text = tok.decode(d["message_log"][0]["token_ids"])
+    assert "You are a math tutor." in text and "Solve: 1+1\nPut the answer in \\boxed{}." in text
+    assert text.endswith("<|assistant|>\n")
+    assert d["extra_env_info"] == {"ground_truth": "2"} and d["idx"] == 7 and d["task_name"] == "m"
+    assert d["loss_multiplier"] == 1.0 and d["length"] == len(d["message_log"][0]["token_ids"])
+    # too long: kept, cut to min(4, max_len // n_messages) tokens, masked
+    short = math_data_processor({"problem": "x" * 100, "expected_answer": 3}, TaskDataSpec(), tok, 20, 0)
+    assert short["loss_multiplier"] == 0.0 and len(short["message_log"][0]["token_ids"]) == 4
+    assert short["extra_env_info"]["ground_truth"] == "3"
+
+
+def test_load_rows_local_formats(tmp_path):
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    from rl_b200.data.response_datasets import load_rows
+
+    rows = _math_rows(5)
+    jl = _write_jsonl(tmp_path / "a.jsonl", rows)
+    js = tmp_path / "a.json"
+    js.write_text(json.dumps(rows))
+    cols = tmp_path / "c.json"
+    cols.write_text(json.dumps({"problem": [r["problem"] for r in rows],
+                                "expected_answer": [r["expected_answer"] for r in rows]}))
+    pqp = tmp_path / "a.parquet"
+    pq.write_table(pa.Table.from_pylist(rows), pqp)
+    csvp = tmp_path / "a.csv"
+    csvp.write_text("problem,expected_answer\n" + "\n".join(f"{r['problem']},{r['expected_answer']}" for r in rows))
+    for p in (jl, js, cols, pqp, csvp):
+        got = load_rows(str(p))
+        assert len(got) == 5 and got[3] == rows[3], p
+
+
+def test_named_datasets_from_local_files(tmp_path):
+    from rl_b200.data.response_datasets import load_response_dataset
+
+    # GSM8K raw schema: the answer follows "####"
+    gsm = _write_jsonl(tmp_path / "gsm.jsonl", [{"question": "q1", "answer": "work... #### 42"},
+                                                {"question": "q2", "answer": "#### 7"}])
+    ds = load_response_dataset({"dataset_name": "GSM8K", "data_path": gsm})
+    assert ds.task_name == "gsm8k" and ds.dataset[0]["messages"][1]["content"] == "42"
+    # OpenMathInstruct-2 raw schema with a 25 % validation split
+    omi = _write_jsonl(tmp_path / "omi.jsonl", _math_rows(20))
+    ds = load_response_dataset({"dataset_name": "OpenMathInstruct-2", "data_path": omi,
+                                "split_validation_size": 0.25, "seed": 3})
+    assert len(ds.dataset) == 15 and len(ds.val_dataset) == 5
+    seen = {r["messages"][0]["content"] for r in ds.dataset} | {r["messages"][0]["content"] for r in ds.val_dataset}
+    assert len(seen) == 20
+    # NuminaMath keeps only verifiable, validated rows
+    num = _write_jsonl(tmp_path / "num.jsonl", [
+        {"problem": "a", "answer": "3", "question_type": "math-word-problem", "problem_is_valid": "Yes",
+         "solution_is_valid": "Yes"},
+        {"problem": "b", "answer": "proof", "question_type": "math-word-problem", "problem_is_valid": "Yes",
+         "solution_is_valid": "Yes"},
+        {"problem": "c", "answer": "5", "question_type": "proof", "problem_is_valid": "Yes",
+         "solution_is_valid": "Yes"},
+        {"problem": "d", "answer": "5", "question_type": "math-word-problem", "problem_is_valid": "No",
+         "solution_is_valid": "Yes"}])
+    ds = load_response_dataset({"dataset_name": "NuminaMath-1.5", "data_path": num})
+    assert [r["messages"][0]["content"] for r in ds.dataset] == ["a"]
+    # DAPO verl-style rows, AIME with repetition, generic ResponseDataset with custom keys
+    dapo = _write_jsonl(tmp_path / "dapo.jsonl", [{"prompt": [{"role": "user", "content": "p"}],
+                                                   "reward_model": {"ground_truth": "9"}}])
+    assert load_response_dataset({"dataset_name": "DAPOMath17K", "data_path": dapo}).dataset[0]["messages"][1][
+        "content"] == "9"
+    aime = _write_jsonl(tmp_path / "aime.jsonl", [{"problem": "x", "answer": 12}])
+    ds = load_response_dataset({"dataset_name": "AIME2024", "data_path": aime, "repeat": 3})
+    assert len(ds.dataset) == 3 and ds.dataset[2]["messages"][1]["content"] == "12" and ds.task_name == "AIME2024"
+    os.makedirs(tmp_path / "mine")
+    gen = _write_jsonl(tmp_path / "mine" / "set.jsonl", [{"q": "hello", "a": "world"}])
+    ds = load_response_dataset({"dataset_name": "ResponseDataset", "data_path": gen, "input_key": "q",
+                                "output_key": "a"})
+    assert ds.task_name == "mine-set" and ds.dataset[0]["messages"][0]["content"] == "hello"
+    with pytest.raises(ValueError):
+        load_response_dataset({"dataset_name": "NoSuchDataset"})
+
+
+def test_setup_response_data_binds_processors_and_envs(tmp_path):
+    from rl_b200.data.tokenizer import ByteTokenizer
+    from rl_b200.data.utils import setup_response_data
+    from rl_b200.environments.math_environment import MathEnvironment
+
+    tr = _write_jsonl(tmp_path / "train.jsonl", _math_rows(12))
+    os.makedirs(tmp_path / "val")
+    va = _write_jsonl(tmp_path / "val" / "math.jsonl", [{"input": "What is 1 + 1?", "output": "2"}])
+    cfg = {"max_input_seq_length": 256,
+           "default": {"env_name": "math", "processor": "math_hf_data_processor"},
+           "train": {"dataset_name": "OpenMathInstruct-2", "data_path": tr, "split_validation_size": 0.25},
+           "validation": [{"dataset_name": "ResponseDataset", "data_path": va}]}
+    tok = ByteTokenizer()
+    train, val, t2e, v2e = setup_response_data(tok, cfg, {"math": {}})
+    assert len(train) == 9 and len(val) == 3 + 1
+    assert isinstance(t2e["OpenMathInstruct-2"], MathEnvironment) and set(v2e) == {"OpenMathInstruct-2", "val-math"}
+    d = train[0]
+    assert d["task_name"] == "OpenMathInstruct-2" and d["extra_env_info"]["ground_truth"].isdigit()
+    assert val[3]["extra_env_info"] == {"ground_truth": "2"}
+    # the environment verifies the decoded response against the ground truth
+    env = t2e["OpenMathInstruct-2"]
+    resp = torch.tensor(tok.encode("so the answer is \\boxed{2}"))
+    ret = env.step([[{"role": "assistant", "token_ids": resp}]], [{"ground_truth": "2"}])
+    assert float(ret.rewards[0]) == 1.0
+
+
+def test_grpo_trains_on_jsonl_math_set_through_run_grpo(tmp_path):
+    from examples.run_grpo import main
+
+    tr = _write_jsonl(tmp_path / "math.jsonl", _math_rows(32))
+    state = main(["--config", os.path.join(ROOT, "examples", "configs", "grpo_tiny_cpu.yaml"),
+                  "logger.log_dir=" + str(tmp_path / "logs"), "logger.stdout=false",
+                  "policy.max_total_sequence_length=96", "policy.generation.max_new_tokens=16",
+                  "+policy.tokenizer.name=byte",
+                  "~data.num_prompts", "~data.min_prompt_len", "~data.max_prompt_len",
+                  "+data.max_input_seq_length=80",
+                  "+data.train.dataset_name=ResponseDataset", f"+data.train.data_path={tr}",
+                  "+data.train.input_key=problem", "+data.train.output_key=expected_answer",
+                  "+data.train.env_name=math", "~env.synthetic", "+env.math.kind=math"])
+    assert state["current_step"] == 2

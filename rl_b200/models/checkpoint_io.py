@@ -10,11 +10,11 @@
   split into their HF components (``qkv_proj`` -> ``q_proj``/``k_proj``/
   ``v_proj``, ``gate_up_proj`` -> ``gate_proj``/``up_proj``, per-expert MoE
   weights); tensor/expert-parallel shards are gathered before writing.
-* **Sharded dist format** (``torch_dist``; reference: Megatron ``iter_0000000/``
-  with ``metadata.json`` + per-rank shard files): every rank writes its flat
-  parameter shard and optimizer segments as-is plus a metadata record of the
-  layout; loading into the same layout is a straight copy, loading into another
-  layout goes through the full tensors.
+* **Megatron torch_dist** (``model_save_format: torch_dist``; reference:
+  Megatron-Core ``iter_0000000/`` with ``metadata.json``, ``common.pt`` and DCP
+  ``.metadata`` + ``__*_*.distcp`` shards): implemented in
+  ``rl_b200.models.megatron_ckpt`` (Megatron parameter names, layer-stacked
+  global tensors, optimizer state embedded; loads at any parallel layout).
 """
 
 from __future__ import annotations
@@ -221,99 +221,20 @@ def load_hf_checkpoint(model, path: str) -> None:
 
 # ------------------------------------------------------- sharded dist format
 def save_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional[str]) -> None:
-    """Per-rank shard files (``iter_0000000/__{rank}.pt``) + ``metadata.json``."""
-    rank = dist.get_rank() if dist.is_initialized() else 0
-    world = dist.get_world_size() if dist.is_initialized() else 1
-    it = os.path.join(weights_dir, "iter_0000000")
-    os.makedirs(it, exist_ok=True)
-    ps = model.ps
-    layout = {"world_size": world, "tp": ps.tp_size, "ep": ps.ep_size, "dp": ps.dp_size, "cp": ps.cp_size,
-              "pp": ps.pp_size, "params": [{"name": sp.name, "shape": list(sp.shape), "tp_dim": sp.tp_dim,
-                                            "ep_dim": sp.ep_dim, "offset": sp.offset, "numel": sp.numel}
-                                           for sp in model.specs]}
-    # each shard carries its own parameter layout (pipeline stages hold different names)
-    torch.save({"flat_param": model.flat_param.detach().cpu(), "tp_rank": ps.tp_rank, "ep_rank": ps.ep_rank,
-                "pp_rank": ps.pp_rank, "params": layout["params"]},
-               os.path.join(it, f"__{rank}.pt"))
-    if rank == 0:
-        with open(os.path.join(it, "metadata.json"), "w") as f:
-            json.dump(layout, f)
-        with open(os.path.join(weights_dir, "latest_checkpointed_iteration.txt"), "w") as f:
-            f.write("0")
-    if optim_dir is not None and optimizer is not None:
-        os.makedirs(optim_dir, exist_ok=True)
-        torch.save(optimizer.state_dict(), os.path.join(optim_dir, f"__{rank}.pt"))
+    """Megatron ``torch_dist`` checkpoint (``iter_0000000/`` of DCP shards under
+    Megatron parameter names, ``rl_b200.models.megatron_ckpt``).  As in Megatron,
+    the optimizer state is stored inside the weights checkpoint; ``optim_dir``
+    only says whether to include it."""
+    from rl_b200.models.megatron_ckpt import save_torch_dist
+
+    save_torch_dist(model, optimizer, weights_dir, save_optimizer=optim_dir is not None)
 
 
 def load_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional[str]) -> None:
-    rank = dist.get_rank() if dist.is_initialized() else 0
-    it = os.path.join(weights_dir, "iter_0000000")
-    with open(os.path.join(it, "metadata.json")) as f:
-        meta = json.load(f)
-    ps = model.ps
-    world = dist.get_world_size() if dist.is_initialized() else 1
-    same = (meta["world_size"] == world and meta["tp"] == ps.tp_size and meta["ep"] == ps.ep_size
-            and meta.get("pp", 1) == ps.pp_size)
-    mine = [{"name": sp.name, "shape": list(sp.shape), "tp_dim": sp.tp_dim, "ep_dim": sp.ep_dim,
-             "offset": sp.offset, "numel": sp.numel} for sp in model.specs]
-    sh = None
-    if same:
-        # the flat buffer is copied whole only when this rank's shard holds exactly the
-        # parameters, at exactly the offsets, that this rank's model holds: the same world
-        # and TP/EP/PP sizes can still place different layers on a rank (virtual pipeline
-        # chunks, uneven first / last stages)
-        sh = torch.load(os.path.join(it, f"__{rank}.pt"), map_location="cpu")
-        same = sh.get("params", meta["params"]) == mine and sh["flat_param"].numel() == model.flat_param.numel()
-    with torch.no_grad():
-        if same:
-            model.flat_param.copy_(sh["flat_param"].to(model.flat_param.device))
-        else:
-            # re-layout: rebuild full tensors from the saved shards, then re-slice
-            full: dict[str, torch.Tensor] = {}
-            by_name: dict[str, dict] = {}
-            pieces: dict[str, dict] = {}  # name -> {(tp_rank, ep_rank): tensor}
-            for r in range(meta["world_size"]):
-                d = torch.load(os.path.join(it, f"__{r}.pt"), map_location="cpu")
-                for p in d.get("params", meta["params"]):
-                    by_name.setdefault(p["name"], p)
-                    pieces.setdefault(p["name"], {})[(d["tp_rank"], d["ep_rank"])] = \
-                        d["flat_param"][p["offset"]:p["offset"] + p["numel"]].view(p["shape"])
-            for name, p in by_name.items():
-                got = pieces[name]
-                if p["tp_dim"] is not None and meta["tp"] > 1:
-                    e0 = min(e for _, e in got)
-                    parts = [got[(t, e0)] for t in range(meta["tp"]) if (t, e0) in got]
-                    full[name] = _merge_tp(model, name, parts, p["tp_dim"])
-                elif p["ep_dim"] is not None and meta["ep"] > 1:
-                    t0 = min(t for t, _ in got)
-                    parts = [got[(t0, e)] for e in range(meta["ep"])]
-                    full[name] = torch.cat(parts, p["ep_dim"])
-                else:
-                    full[name] = next(iter(got.values()))
-            for sp, prm in model.named_flat_params():
-                t = full[sp.name]
-                if sp.tp_dim is not None and ps.tp_size > 1:
-                    t = model.shard_full_tensor(sp, t, ps.tp_rank, ps.tp_size)
-                elif sp.ep_dim is not None and ps.ep_size > 1:
-                    t = model.shard_full_tensor(sp, t, ps.ep_rank, ps.ep_size)
-                prm.copy_(t.to(prm.dtype).view(sp.shape))
-    if optimizer is not None:
-        if optim_dir is not None and same and os.path.exists(os.path.join(optim_dir, f"__{rank}.pt")):
-            optimizer.load_state_dict(torch.load(os.path.join(optim_dir, f"__{rank}.pt"), map_location="cpu"))
-        else:
-            for seg in optimizer.segments:  # fresh moments; master follows the loaded weights
-                seg.master.copy_(model.flat_param[seg.s_lo:seg.s_hi])
+    """Load a ``torch_dist`` checkpoint written at any parallel layout (each rank
+    reads only the pieces its own shards need); optimizer state is restored when
+    the checkpoint has it and ``optim_dir`` is given, else the moments start
+    fresh with the master weights set from the loaded parameters."""
+    from rl_b200.models.megatron_ckpt import load_torch_dist
 
-
-def _merge_tp(model, name: str, parts: list[torch.Tensor], dim: int) -> torch.Tensor:
-    c = model.cfg
-    n = len(parts)
-    if name.endswith(("qkv_proj.weight", "qkv_proj.bias")):
-        hd = c.head_dim
-        sizes = [c.num_heads * hd // n, c.num_kv_heads * hd // n, c.num_kv_heads * hd // n]
-        qs, ks, vs = zip(*[torch.split(p, sizes, 0) for p in parts])
-        return torch.cat(list(qs) + list(ks) + list(vs), 0)
-    if name.endswith("gate_up_proj.weight"):
-        gs, us = zip(*[p.chunk(2, 0) for p in parts])
-        return torch.cat(list(gs) + list(us), 0)
-    return torch.cat(parts, dim)
+    load_torch_dist(model, optimizer, weights_dir, load_optimizer=optim_dir is not None)

@@ -1114,7 +1114,9 @@ class PolicyWorker:
     def save_checkpoint(self, weights_path: str, optimizer_path: Optional[str] = None,
                         fmt: str = "safetensors") -> None:
         """``safetensors``: consolidated HF checkpoint (+ per-rank optimizer shards);
-        ``torch_dist``: per-rank shard files with layout metadata."""
+        ``torch_dist``: Megatron-style ``iter_0000000/`` DCP checkpoint under Megatron
+        parameter names with the optimizer state embedded (when ``optimizer_path``
+        is given), loadable at any parallel layout."""
         from rl_b200.models import checkpoint_io as cio
 
         if self.lora is not None:

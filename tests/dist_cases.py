@@ -193,3 +193,41 @@ def case_ckpt_relayout_vpp(rank: int, pp: int, path: str, vpp_save: int, vpp_loa
     saved = {sp.name: p.detach().clone() for sp, p in m_s.named_flat_params()}
     loaded = {sp.name: p.detach().clone() for sp, p in m_l.named_flat_params()}
     return {"saved": saved, "loaded": loaded}
+
+
+def case_torch_dist(rank: int, tp: int, ep: int, moe: bool, path: str, mode: str):
+    """torch_dist checkpoint round trip across layouts.  ``save``: one training step,
+    save weights + optimizer, then a second step.  ``load``: a fresh worker (other
+    seed) loads the checkpoint and takes the same second step.  Both return the
+    HF-named weights at the checkpoint and the log-probs after the second step,
+    so weights AND Adam moments must have moved across the layout change."""
+    import torch.distributed as dist
+
+    from rl_b200.models.checkpoint_io import hf_state_dict
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import init_distributed
+
+    torch.manual_seed(0)
+    ps = init_distributed(tp=tp, ep=ep, backend="gloo")
+    cfg = TINY_MOE if moe else TINY
+    w = PolicyWorker(_pcfg(False), model_cfg=cfg, pstate=ps, seed=3 if mode == "save" else 11)
+    loss = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
+
+    def step(seed):
+        full = make_batch(seed=seed)
+        per = full.size // ps.dp_size
+        w.train(full.slice(ps.dp_rank * per, (ps.dp_rank + 1) * per), loss, gbs=per)
+
+    if mode == "save":
+        step(0)
+        w.save_checkpoint(path, optimizer_path=path + "_optimizer_flag", fmt="torch_dist")
+    else:
+        w.load_checkpoint(path, optimizer_path=path + "_optimizer_flag")
+        # written again from the loading layout: must hold the same global tensors
+        w.save_checkpoint(f"{path}_resaved_{tp}_{ep}_{ps.world_size}", optimizer_path="flag", fmt="torch_dist")
+    sd = {k: v.detach().float().cpu().clone() for k, v in hf_state_dict(w.model, dtype=None).items()}
+    step(1)
+    lp = w.get_logprobs(make_batch(seed=2))["logprobs"]
+    if dist.is_initialized():
+        dist.barrier()
+    return {"sd": sd, "lp": lp, "step": int(w.optimizer.step_count)}

@@ -184,3 +184,69 @@ def test_dist_checkpoint_across_virtual_pipeline_settings(tmp_path):
         assert saved.keys() == loaded.keys()
         for k in saved:
             torch.testing.assert_close(loaded[k], saved[k], atol=0, rtol=0, msg=k)
+
+
+@pytest.mark.parametrize("moe,save,loads", [
+    (False, (2, 2, 1), [(1, 1, 1), (2, 1, 1), (4, 2, 1)]),   # (world, tp, ep): TP=2 -> 1 GPU, DP=2, TP2 x DP2
+    (True, (2, 1, 2), [(1, 1, 1), (2, 2, 1)]),               # EP=2 -> 1 GPU, TP=2
+])
+def test_torch_dist_checkpoint_relayout(tmp_path, moe, save, loads):
+    """A Megatron torch_dist checkpoint (DCP shards under Megatron names, optimizer
+    embedded) saved at one layout resumes at others: the same weights, a
+    checkpoint written again from the new layout holds bit-identical global
+    tensors (weights, fp32 master, both Adam moments), and the next training
+    step gives the same log-probs as continuing at the saving layout (MoE:
+    within the tolerance of the TP / EP step itself, whose near-zero expert
+    gradients Adam normalises)."""
+    import torch.distributed.checkpoint as dcp
+
+    from rl_b200.models.megatron_ckpt import read_global_tensor
+    from tests.dist_cases import case_torch_dist
+
+    path = str(tmp_path / "weights")
+    ref = spawn_ranks(case_torch_dist, save[0], save[1], save[2], moe, path, "save")[0]
+    it = tmp_path / "weights" / "iter_0000000"
+    assert (it / "metadata.json").exists() and (it / "common.pt").exists() and (it / ".metadata").exists()
+    assert list(it.glob("__*_*.distcp"))
+    for world, tp, ep in loads:
+        outs = spawn_ranks(case_torch_dist, world, tp, ep, moe, path, "load")
+        for o in outs:
+            assert o["sd"].keys() == ref["sd"].keys()
+            for k in ref["sd"]:
+                torch.testing.assert_close(o["sd"][k], ref["sd"][k], atol=0, rtol=0, msg=k)
+            assert o["step"] == ref["step"]
+            tol = 5e-3 if moe else 5e-4
+            assert torch.allclose(o["lp"], ref["lp"], atol=tol), (world, tp, ep, (o["lp"] - ref["lp"]).abs().max())
+        again = f"{path}_resaved_{tp}_{ep}_{world}"
+        keys = dcp.FileSystemReader(f"{path}/iter_0000000").read_metadata().state_dict_metadata.keys()
+        assert any(k.startswith("optimizer.state.exp_avg_sq.") for k in keys)
+        for k in keys:
+            torch.testing.assert_close(read_global_tensor(again, k), read_global_tensor(path, k), atol=0, rtol=0,
+                                       msg=k)
+
+
+def test_torch_dist_megatron_layout(tmp_path):
+    """The stacked Megatron tensors: QKV rows grouped per KV head ([q heads of the
+    group, k, v]), fc1 = [gate; up], layer index leading."""
+    from rl_b200.models.megatron_ckpt import read_global_tensor
+    from tests.dist_cases import TINY, case_torch_dist
+
+    path = str(tmp_path / "w")
+    ref = spawn_ranks(case_torch_dist, 2, 2, 1, False, path, "save")[0]["sd"]
+    c = TINY
+    qpg, hd, H = c.num_heads // c.num_kv_heads, c.head_dim, c.hidden_size
+    qkv = read_global_tensor(path, "decoder.layers.self_attention.linear_qkv.weight")
+    assert qkv.shape == (c.num_layers, (c.num_heads + 2 * c.num_kv_heads) * hd, H)
+    for layer in range(c.num_layers):
+        g = qkv[layer].float().view(c.num_kv_heads, qpg + 2, hd, H)
+        pre = f"model.layers.{layer}.self_attn."
+        torch.testing.assert_close(g[:, :qpg], ref[pre + "q_proj.weight"].view(c.num_kv_heads, qpg, hd, H))
+        torch.testing.assert_close(g[:, qpg], ref[pre + "k_proj.weight"].view(c.num_kv_heads, hd, H))
+        torch.testing.assert_close(g[:, qpg + 1], ref[pre + "v_proj.weight"].view(c.num_kv_heads, hd, H))
+    fc1 = read_global_tensor(path, "decoder.layers.mlp.linear_fc1.weight")
+    torch.testing.assert_close(fc1[1].float(), torch.cat([ref["model.layers.1.mlp.gate_proj.weight"],
+                                                          ref["model.layers.1.mlp.up_proj.weight"]]))
+    emb = read_global_tensor(path, "embedding.word_embeddings.weight")
+    torch.testing.assert_close(emb.float(), ref["model.embed_tokens.weight"])
+    exp_avg = read_global_tensor(path, "optimizer.state.exp_avg.decoder.layers.self_attention.linear_proj.weight")
+    assert exp_avg.shape == (c.num_layers, H, c.num_heads * hd) and exp_avg.abs().sum() > 0

@@ -257,12 +257,23 @@ def validate(policy, val_dataloader, val_task_to_env: dict, master_config: dict,
     return {"accuracy": float(r.mean()), "pass_k": float(p.mean()), "num_samples": int(r.numel())}
 
 
+class _DeferredAdvantage:
+    """Placeholder estimator for on-policy distillation: the advantages need the
+    student's and the teachers' log-probs, so they are computed after those passes."""
+
+    def compute_advantage(self, prompt_ids, rewards, mask, **_):
+        return torch.zeros_like(mask, dtype=torch.float32)
+
+
 def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_fn=None, logger=None,
                checkpointer=None, save_state: Optional[GRPOSaveState] = None, val_dataloader=None,
                val_task_to_env: Optional[dict] = None, tokenizer=None, max_steps: Optional[int] = None,
-               step_callback=None) -> GRPOSaveState:
+               step_callback=None, teacher_router=None) -> GRPOSaveState:
     """Run GRPO steps; returns the final save state.  ``step_callback(step, metrics)``
-    is called after every step (benchmarks hook timing there)."""
+    is called after every step (benchmarks hook timing there).  With
+    ``on_policy_distillation.enabled`` (or ``adv_estimator.name: opd``) each step
+    scores the rollouts with the routed teachers (``teacher_router``, built from
+    the config when not given) and trains on the teacher-student log-prob gap."""
     ps = policy.ps
     cfg = {**DEFAULT_GRPO_CONFIG, **master_config.get("grpo", {})}
     loss_cfg = master_config.get("loss_fn", {})
@@ -271,6 +282,13 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     adv_cfg.setdefault("normalize_rewards", cfg["normalize_rewards"])
     adv_cfg.setdefault("use_leave_one_out_baseline", cfg["use_leave_one_out_baseline"])
     estimator = make_advantage_estimator(adv_cfg, loss_cfg)
+    from rl_b200.algorithms.opd import build_teacher_router, is_opd_enabled, routing_keys
+
+    opd = is_opd_enabled(master_config) or adv_cfg.get("name") == "opd"
+    if opd:
+        if adv_cfg.get("name") != "opd":
+            estimator = make_advantage_estimator({**adv_cfg, "name": "opd"}, loss_cfg)
+        teacher_router = teacher_router or build_teacher_router(master_config, policy)
     G = int(cfg["num_generations_per_prompt"])
     max_seq = int(master_config["policy"]["max_total_sequence_length"])
     train_gbs = int(master_config["policy"].get("train_global_batch_size", cfg["num_prompts_per_step"] * G))
@@ -349,7 +367,8 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                         rollout = rollout.slice(0, target)
                 # ---- advantages ----
                 with timer.time("data_processing"):
-                    train_data, adv_stats = build_train_data(rollout, estimator, cfg, loss_cfg, rollout["group_id"])
+                    train_data, adv_stats = build_train_data(rollout, _DeferredAdvantage() if opd else estimator,
+                                                             cfg, loss_cfg, rollout["group_id"])
                     if data_plane is not None:
                         # the trainer consumes the step's samples from the data plane (the
                         # reference's TransferQueue flow); producer and consumer may be
@@ -363,7 +382,8 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                 # the ones the step's own forward runs with, so the separate "previous
                 # policy" pass is folded into training (exactly the same values)
                 one_step = train_data.size <= min(local_gbs, train_data.size)
-                reuse_prev = bool(cfg.get("reuse_train_logprobs_as_prev", True)) and one_step
+                # OPD needs the student's log-probs before training (its advantages)
+                reuse_prev = bool(cfg.get("reuse_train_logprobs_as_prev", True)) and one_step and not opd
                 with timer.time("policy_and_reference_logprobs"):
                     policy.prepare_for_lp_inference()
                     if reuse_prev:
@@ -375,6 +395,16 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                             policy.get_reference_policy_logprobs(train_data)["reference_logprobs"]
                     elif kl_on:  # skipped: the KL sees the current policy as its own reference
                         train_data["reference_policy_logprobs"] = train_data["generation_logprobs"].clone()
+                    if opd:
+                        tlp = teacher_router.teacher_logprobs(train_data, routing_keys(rollout))
+                        train_data["teacher_logprobs"] = tlp
+                        tm = train_data["token_mask"]
+                        adv = estimator.compute_advantage(rollout["group_id"].view(-1, 1), train_data["rewards"], tm,
+                                                          logprobs_policy=train_data["prev_logprobs"].float(),
+                                                          logprobs_teacher=tlp)
+                        train_data["advantages"] = adv * tm
+                        adv_stats.update(estimator.last_metrics)
+                        adv_stats.update(teacher_router.last_metrics)
                 # ---- train ----
                 with timer.time("policy_training"):
                     policy.prepare_for_training()

@@ -10,6 +10,9 @@ vocab 512).  ``from_hf_config`` reads a HF ``config.json`` dict.
 
 from __future__ import annotations
 
+import json
+import os
+
 import dataclasses
 from dataclasses import dataclass, field
 from typing import Optional
@@ -175,6 +178,10 @@ def get_model_config(name_or_cfg, **overrides) -> ModelConfig:
         cfg = name_or_cfg
     elif isinstance(name_or_cfg, dict):
         cfg = ModelConfig(**name_or_cfg)
+    elif os.path.isfile(os.path.join(str(name_or_cfg), "config.json")):
+        # a Hugging Face model directory: the architecture from its config.json
+        with open(os.path.join(str(name_or_cfg), "config.json")) as f:
+            cfg = ModelConfig.from_hf_config(json.load(f), name=os.path.basename(str(name_or_cfg).rstrip("/")))
     else:
         key = str(name_or_cfg).lower()
         aliases = {

@@ -107,17 +107,18 @@ def main(argv=None) -> dict:
     logger = Logger(cfg.get("logger", {}))
     logger.log_hyperparams(cfg)
     if (cfg["grpo"].get("async_grpo") or {}).get("enabled", False):
-        from rl_b200.algorithms.async_grpo import async_grpo_train, restore_replay_buffer
+        from rl_b200.algorithms.async_grpo import async_grpo_train, restore_replay_buffer, restore_rollout_recovery
 
-        buf = None
+        buf, ledger = None, None
         if ck is not None and ck.get_latest_checkpoint_path():
+            ledger = restore_rollout_recovery(ck.get_latest_checkpoint_path())
             acfg = cfg["grpo"].get("async_grpo") or {}
             n_groups = max(1, int(cfg["grpo"]["num_prompts_per_step"]) // max(1, ps.dp_size))
             age = int(acfg.get("max_trajectory_age_steps", 1))
             buf = restore_replay_buffer(ck.get_latest_checkpoint_path(), n_groups, n_groups * (age + 1) * 2,
                                         acfg.get("load_replay_buffer"))
         state = async_grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state,
-                                 replay_buffer=buf)
+                                 replay_buffer=buf, rollout_ledger=ledger)
     else:
         encode = (lambda text: tokenizer(text, add_special_tokens=False)["input_ids"]) if tokenizer else None
         state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state,

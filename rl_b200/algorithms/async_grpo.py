@@ -47,6 +47,21 @@ def replay_buffer_file() -> str:
     return f"replay_buffer_rank{dist.get_rank() if dist.is_initialized() else 0}.pt"
 
 
+def rollout_recovery_file() -> str:
+    """Per-rank rollout-recovery ledger file in a checkpoint directory."""
+    import torch.distributed as dist
+
+    return f"rollout_recovery_rank{dist.get_rank() if dist.is_initialized() else 0}.pt"
+
+
+def restore_rollout_recovery(ckpt_dir: str):
+    """This rank's rollout-recovery ledger from a checkpoint, or None when absent."""
+    from rl_b200.experience.rollout_recovery import RolloutRecoveryLedger
+
+    path = os.path.join(ckpt_dir, rollout_recovery_file())
+    return RolloutRecoveryLedger.load(path) if os.path.exists(path) else None
+
+
 def restore_replay_buffer(ckpt_dir: str, num_prompt_groups: int, max_size: int,
                           load_replay_buffer: Optional[bool] = None) -> Optional[ReplayBuffer]:
     """The checkpoint's replay buffer of this rank (groups of incomplete targets
@@ -66,7 +81,14 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
                      checkpointer=None, save_state: Optional[GRPOSaveState] = None, val_dataloader=None,
                      val_task_to_env: Optional[dict] = None, tokenizer=None, max_steps: Optional[int] = None,
                      step_callback=None, replay_buffer: Optional[ReplayBuffer] = None,
-                     wait_timeout_s: float = 3600.0) -> GRPOSaveState:
+                     wait_timeout_s: float = 3600.0, rollout_ledger=None) -> GRPOSaveState:
+    """Async GRPO: a rollout pump thread fills a replay buffer while the trainer
+    consumes groups generated at most ``max_trajectory_age_steps`` versions ago.
+    ``rollout_ledger`` (restored from a checkpoint) makes the pump regenerate the
+    prompt groups that were in flight when that checkpoint was written; the
+    ledger of this run is saved with every checkpoint."""
+    from rl_b200.experience.rollout_recovery import RolloutRecoveryLedger
+
     ps = policy.ps
     if ps.tp_size > 1:
         raise NotImplementedError("async GRPO generates in a side thread and needs TP=1 generation")
@@ -108,10 +130,16 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
             metrics.update(apply_length_penalty_to_rollout(rollout, cfg["length_penalty"], G, tokenizer))
         return rollout, metrics
 
+    restart = []
+    if rollout_ledger is not None:
+        live = _buffer_group_ids(replay_buffer.state_dict()) if replay_buffer is not None else None
+        restart = rollout_ledger.prepare_for_restart(live)
+    ledger = rollout_ledger or RolloutRecoveryLedger()
     collector = AsyncTrajectoryCollector(rollout_fn, dataloader, buffer, n_groups, G, max_age,
                                          initial_weight_version=step,
                                          in_flight_weight_updates=bool(acfg.get("in_flight_weight_updates", False)),
-                                         max_generation_failures=int(acfg.get("max_generation_failures", 0)))
+                                         max_generation_failures=int(acfg.get("max_generation_failures", 0)),
+                                         ledger=ledger, restart_groups=restart)
     collector.start()
     timer = Timer()
     try:
@@ -124,6 +152,8 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
                         sample = wait_for_groups(buffer, collector, n_groups, step, max_age, wait_timeout_s)
                     except StopIteration:
                         break
+                consumed = [g["recovery_group_id"][0] for g in sample["trajectories"] if "recovery_group_id" in g]
+                ledger.mark_consumed([c for c in consumed if c in ledger])
                 rollout = groups_to_batch(sample["trajectories"])
                 with timer.time("data_processing"):
                     train_data, adv_stats = build_train_data(rollout, estimator, cfg, loss_cfg, rollout["group_id"])
@@ -153,6 +183,7 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
             metrics = dict(train_results)
             metrics.update(adv_stats)
             metrics.update(collector.efficiency_metrics())
+            metrics.update({f"rollout_recovery/{k}": float(v) for k, v in ledger.counts().items()})
             metrics.update({"avg_trajectory_age": sample["avg_trajectory_age"], "buffer_size": buffer.size(),
                             "total_tokens": tok_all, "tokens_per_sec": tok_all / step_time_max,
                             "tokens_per_sec_per_gpu": tok_all / step_time_max / max(1, ps.world_size),
@@ -175,9 +206,17 @@ def async_grpo_train(policy, dataloader, task_to_env: dict, master_config: dict,
                     logger.log_metrics(vm, step, prefix="validation")
             if checkpointer is not None and checkpointer.should_save(step):
                 with collector.weights_lock:
+                    buf_sd = buffer.state_dict()
+                    ledger.prune_sealed(_buffer_group_ids(buf_sd))
                     checkpointer.save(policy, state, dataloader, metrics, step,
-                                      rank_files={replay_buffer_file(): buffer.state_dict()})
+                                      rank_files={replay_buffer_file(): buf_sd,
+                                                  rollout_recovery_file(): ledger.state_dict()})
     finally:
         collector.stop()
     collector.check_health()
     return state
+
+
+def _buffer_group_ids(buffer_state: dict) -> list[str]:
+    """Ledger ids of the prompt groups held in a replay-buffer state dict."""
+    return [g["recovery_group_id"][0] for g in buffer_state.get("groups", []) if "recovery_group_id" in g]

@@ -150,7 +150,8 @@ class AsyncTrajectoryCollector:
 
     def __init__(self, rollout_fn, dataloader, buffer: ReplayBuffer, num_prompt_groups: int, group_size: int,
                  max_trajectory_age_steps: int = 1, initial_weight_version: int = 0,
-                 in_flight_weight_updates: bool = False, max_generation_failures: int = 0):
+                 in_flight_weight_updates: bool = False, max_generation_failures: int = 0,
+                 ledger=None, restart_groups: Optional[list] = None, max_group_attempts: Optional[int] = None):
         self.rollout_fn = rollout_fn
         self.dataloader = dataloader
         self.buffer = buffer
@@ -171,7 +172,12 @@ class AsyncTrajectoryCollector:
         self._failures = 0
         self._thread: Optional[threading.Thread] = None
         self.exhausted = False
-        self.stats = {"groups_generated": 0, "rollouts": 0, "idle_s": 0.0, "gen_s": 0.0}
+        self.stats = {"groups_generated": 0, "rollouts": 0, "idle_s": 0.0, "gen_s": 0.0, "groups_regenerated": 0}
+        # rollout recovery: every prompt group is recorded from dataloader to
+        # consumption; groups in flight at a restart are served before new prompts
+        self.ledger = ledger
+        self.retry_queue: list = list(restart_groups or [])
+        self.max_group_attempts = max_group_attempts
 
     # ----------------------------------------------------------- scheduling
     def target_candidates(self, gen_version: int) -> list[int]:
@@ -241,13 +247,16 @@ class AsyncTrajectoryCollector:
                     continue
                 try:
                     if batch is None:
-                        try:
-                            batch = next(it)
-                        except StopIteration:
+                        batch, group_ids = self._next_prompts(it, target, v)
+                        if batch is None:
                             self.exhausted = True
                             with self._cv:
                                 self._generating.discard(target)
                             return
+                    if self.ledger is not None:
+                        for gid in group_ids:
+                            self.ledger.mark_dispatched(gid, target)
+                        batch["recovery_group_id"] = list(group_ids)
                     t0 = time.perf_counter()
                     if self.in_flight_weight_updates:
                         with self.weights_lock:
@@ -259,7 +268,10 @@ class AsyncTrajectoryCollector:
                             rollout, _ = self.rollout_fn(batch, target)
                     self.stats["gen_s"] += time.perf_counter() - t0
                     self.stats["rollouts"] += 1
-                    for g in split_groups(rollout, self.group_size):
+                    for i, g in enumerate(split_groups(rollout, self.group_size)):
+                        if self.ledger is not None:  # sealed before the trainer can consume it
+                            self.ledger.mark_group_sealed(group_ids[i], g["total_reward"].tolist()
+                                                          if "total_reward" in g else None)
                         while self.buffer.add(g, gen_version, target) == "full":
                             if self._stop.is_set():
                                 return
@@ -268,6 +280,10 @@ class AsyncTrajectoryCollector:
                     batch = None
                 except Exception as e:  # a failed rollout: count it, maybe retry the prompts
                     self._failures += 1
+                    if self.ledger is not None and batch is not None:
+                        for gid in group_ids:  # retried first unless out of attempts
+                            if self.ledger.mark_failed(gid, self.max_group_attempts):
+                                self.retry_queue.insert(0, self.ledger.get_group(gid))
                     if self._failures > self.max_generation_failures:
                         raise
                     batch = None
@@ -279,10 +295,32 @@ class AsyncTrajectoryCollector:
         except BaseException as e:  # surfaced to the trainer by check_health()
             self._error = e
 
+    def _next_prompts(self, it, target: int, version: int):
+        """(batch, group ids): prompt groups to regenerate first, else the next
+        dataloader batch (its rows reserved in the ledger)."""
+        if self.ledger is not None and self.retry_queue:
+            n = max(1, self.num_prompt_groups)
+            take, self.retry_queue = self.retry_queue[:n], self.retry_queue[n:]
+            from rl_b200.experience.rollout_recovery import collate_datums
+
+            self.stats["groups_regenerated"] += len(take)
+            return collate_datums([g.prompt for g in take]), [g.group_id for g in take]
+        try:
+            batch = next(it)
+        except StopIteration:
+            return None, []
+        if self.ledger is None:
+            return batch, []
+        from rl_b200.experience.rollout_recovery import datum_rows
+
+        ids = [self.ledger.reserve_group(row, self.group_size, target, version) for row in datum_rows(batch)]
+        return batch, ids
+
     def efficiency_metrics(self) -> dict[str, float]:
         tot = self.stats["idle_s"] + self.stats["gen_s"]
         return {"rollout_pump_idle_frac": self.stats["idle_s"] / tot if tot > 0 else 0.0,
-                "groups_generated": float(self.stats["groups_generated"])}
+                "groups_generated": float(self.stats["groups_generated"]),
+                "groups_regenerated": float(self.stats["groups_regenerated"])}
 
 
 def wait_for_groups(buffer: ReplayBuffer, collector: AsyncTrajectoryCollector, n_groups: int, version: int,

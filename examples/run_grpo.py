@@ -124,7 +124,9 @@ def main(argv=None) -> dict:
         state = grpo_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state,
                            val_dataloader=val_dl, val_task_to_env=val_envs, tokenizer=encode)
     logger.close()
-    policy.shutdown()
+    policy.shutdown()  # waits for a background checkpoint write
+    if ck is not None:
+        ck.wait()  # and for the publication of its step directory
     return state
 
 

@@ -220,14 +220,14 @@ def load_hf_checkpoint(model, path: str) -> None:
 
 
 # ------------------------------------------------------- sharded dist format
-def save_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional[str]) -> None:
+def save_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional[str], async_save: bool = False):
     """Megatron ``torch_dist`` checkpoint (``iter_0000000/`` of DCP shards under
     Megatron parameter names, ``rl_b200.models.megatron_ckpt``).  As in Megatron,
     the optimizer state is stored inside the weights checkpoint; ``optim_dir``
     only says whether to include it."""
     from rl_b200.models.megatron_ckpt import save_torch_dist
 
-    save_torch_dist(model, optimizer, weights_dir, save_optimizer=optim_dir is not None)
+    return save_torch_dist(model, optimizer, weights_dir, save_optimizer=optim_dir is not None, async_save=async_save)
 
 
 def load_dist_checkpoint(model, optimizer, weights_dir: str, optim_dir: Optional[str]) -> None:

@@ -301,19 +301,52 @@ def is_torch_dist_checkpoint(weights_dir: str) -> bool:
     return os.path.exists(os.path.join(it, "metadata.json")) and os.path.exists(os.path.join(it, ".metadata"))
 
 
-def save_torch_dist(model, optimizer, weights_dir: str, save_optimizer: bool = True) -> None:
+_ASYNC_GROUP = None
+
+
+def _async_group():
+    """A gloo group over all ranks for the coordination of background saves: its
+    collectives run on the save thread, apart from the training communicators."""
+    global _ASYNC_GROUP
+    if _ASYNC_GROUP is None:
+        _ASYNC_GROUP = dist.new_group(backend="gloo")
+    return _ASYNC_GROUP
+
+
+def save_torch_dist(model, optimizer, weights_dir: str, save_optimizer: bool = True, async_save: bool = False):
     """Write the model (and the optimizer state) as a torch_dist checkpoint; a
-    collective over the default group when it is initialised."""
+    collective over the default group when it is initialised.
+
+    ``async_save``: the pieces are first copied to pinned host memory (the only
+    part the caller waits for, so training may change the weights right after),
+    then planned and written by a background thread whose cross-rank
+    coordination uses a separate gloo group.  Returns the write's future (its
+    result is ready on every rank once rank 0's is, since rank 0 writes the
+    metadata after gathering every rank's write results), or None when
+    synchronous."""
     it = os.path.join(weights_dir, ITER_DIR)
     rank = dist.get_rank() if dist.is_initialized() else 0
     if rank == 0:
         os.makedirs(it, exist_ok=True)
     if dist.is_initialized():
         dist.barrier()
+    fut = None
     with torch.no_grad():
         entries = _entries(model, optimizer, save_optimizer)
-        dcp.save({}, storage_writer=dcp.FileSystemWriter(it), planner=_PieceSavePlanner(entries),
-                 no_dist=not dist.is_initialized())
+        if async_save:
+            staged = []
+            for pc, t in entries:
+                host = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=t.is_cuda)
+                host.copy_(t, non_blocking=True)
+                staged.append((pc, host))
+            if torch.cuda.is_available():
+                torch.cuda.synchronize()
+            fut = dcp.async_save({}, storage_writer=dcp.FileSystemWriter(it), planner=_PieceSavePlanner(staged),
+                                 process_group=_async_group() if dist.is_initialized() else None,
+                                 no_dist=not dist.is_initialized())
+        else:
+            dcp.save({}, storage_writer=dcp.FileSystemWriter(it), planner=_PieceSavePlanner(entries),
+                     no_dist=not dist.is_initialized())
     if rank == 0:
         common = {"checkpoint_version": 3.0, "iteration": 0, "rl_b200_layout": _layout(model)}
         if save_optimizer and optimizer is not None:
@@ -328,6 +361,7 @@ def save_torch_dist(model, optimizer, weights_dir: str, save_optimizer: bool = T
             f.write("0")
     if dist.is_initialized():
         dist.barrier()
+    return fut
 
 
 def load_torch_dist(model, optimizer, weights_dir: str, load_optimizer: bool = True) -> bool:

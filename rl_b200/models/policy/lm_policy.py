@@ -112,10 +112,10 @@ class Policy:
         self.worker.prepare_for_lp_inference()
 
     def finish_training(self, *args, **kwargs) -> None:
-        pass
+        """Training buffers stay resident between steps (colocated loop); nothing to release."""
 
     def finish_inference(self) -> None:
-        pass
+        """Log-prob passes hold no state to release."""
 
     def invalidate_kv_cache(self, *args, **kwargs) -> bool:
         return self.worker.engine.invalidate_kv_cache()
@@ -130,7 +130,8 @@ class Policy:
         return self.worker.refit()
 
     def sync_params_before_refit(self) -> None:
-        pass
+        """The flat parameter buffer is already consistent after the optimizer step
+        (the fused DP update all-gathers it), so there is nothing to synchronise."""
 
     def offload_before_refit(self) -> None:
         self.worker.offload_before_refit()
@@ -139,7 +140,10 @@ class Policy:
         self.worker.offload_after_refit()
 
     def offload_to_cpu(self) -> None:
-        pass
+        self.worker.offload_to_cpu()
+
+    def onload(self) -> None:
+        self.worker.onload()
 
     def calibrate_qkv_fp8_scales(self, data: BatchedDataDict, **kw) -> dict:
         return self.worker.calibrate_qkv_fp8_scales(data, **kw)
@@ -157,10 +161,10 @@ class Policy:
         self.worker.load_checkpoint(weights_path, optimizer_path)
 
     def finalize_async_save(self) -> None:
-        pass  # saves complete synchronously
+        self.worker.finalize_async_save()
 
     def poll_async_save(self) -> bool:
-        return True
+        return self.worker.poll_async_save()
 
     # ------------------------------------------------------------ profiling
     def start_gpu_profiling(self) -> None:

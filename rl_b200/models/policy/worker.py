@@ -1112,7 +1112,7 @@ class PolicyWorker:
 
     # ------------------------------------------------------- checkpoints
     def save_checkpoint(self, weights_path: str, optimizer_path: Optional[str] = None,
-                        fmt: str = "safetensors") -> None:
+                        fmt: str = "safetensors", async_save: Optional[bool] = None) -> None:
         """``safetensors``: consolidated HF checkpoint (+ per-rank optimizer shards);
         ``torch_dist``: Megatron-style ``iter_0000000/`` DCP checkpoint under Megatron
         parameter names with the optimizer state embedded (when ``optimizer_path``
@@ -1126,7 +1126,12 @@ class PolicyWorker:
             if (dist.get_rank() if dist.is_initialized() else 0) == 0:
                 self.lora.save_peft(weights_path)
         elif fmt == "torch_dist":
-            cio.save_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path)
+            if async_save is None:
+                ck = ((self.cfg.get("megatron_cfg") or {}).get("checkpoint") or {})
+                async_save = bool(ck.get("async_save", False))
+            self.finalize_async_save()  # one background save at a time
+            self._async_save = cio.save_dist_checkpoint(self.model, self.optimizer, weights_path, optimizer_path,
+                                                        async_save=bool(async_save))
             return
         else:
             cio.save_hf_checkpoint(self.model, weights_path)
@@ -1170,7 +1175,9 @@ class PolicyWorker:
 
     def shutdown(self) -> None:
         """Release the rollout engine's captured graphs (they may hold NCCL
-        collectives, which must be gone before the process group is destroyed)."""
+        collectives, which must be gone before the process group is destroyed)
+        after any background checkpoint write has finished."""
+        self.finalize_async_save()
         self.engine.finish_generation()
         self.engine._drop_graphs()
         self.engine._kv_sig = None
@@ -1192,10 +1199,62 @@ class PolicyWorker:
         self.weight_sync.shutdown()
 
     def offload_before_refit(self) -> None:
-        pass
+        """Nothing to move: the colocated rollout reads the trained weights in place
+        (a reshard refit streams them); kept for the reference's call sequence."""
 
     def offload_after_refit(self) -> None:
-        pass
+        """See ``offload_before_refit``."""
+
+    # ------------------------------------------------ async checkpoint saves
+    def finalize_async_save(self) -> None:
+        """Wait for the background checkpoint write started by ``save_checkpoint``
+        (if any) and raise its error."""
+        fut = getattr(self, "_async_save", None)
+        self._async_save = None
+        if fut is not None:
+            fut.result()
+
+    def poll_async_save(self) -> bool:
+        """Whether no background checkpoint write is pending."""
+        fut = getattr(self, "_async_save", None)
+        return fut is None or fut.done()
+
+    # ----------------------------------------------------------- host offload
+    def offload_to_cpu(self) -> None:
+        """Move the training state off the GPU: parameters (the flat buffer's
+        storage is released in place, so every parameter view stays valid), the
+        optimizer's master weights and moments, the reference weights, the
+        gradient buffer and the rollout KV cache.  ``onload`` brings it back."""
+        if getattr(self, "_offloaded", None) is not None or self.device.type != "cuda":
+            return
+        torch.cuda.synchronize()
+        saved = {}
+        for key, t in (("flat", self.model.flat_param), ("ref", self.ref_flat)):
+            if t is None or not t.is_cuda:
+                continue
+            host = torch.empty(t.shape, dtype=t.dtype, device="cpu", pin_memory=True)
+            host.copy_(t.detach())
+            saved[key] = (t, host, t.untyped_storage().nbytes())
+        self.engine.finish_generation()
+        self.optimizer.release_grad_buffer()
+        self.optimizer.offload()
+        for t, _, _ in saved.values():
+            t.untyped_storage().resize_(0)
+        self._offloaded = saved
+        torch.cuda.empty_cache()
+
+    def onload(self) -> None:
+        """Undo ``offload_to_cpu``."""
+        saved = getattr(self, "_offloaded", None)
+        if saved is None:
+            return
+        for t, host, nbytes in saved.values():
+            t.untyped_storage().resize_(nbytes)
+            t.detach().copy_(host)
+        self.optimizer.onload(self.device)
+        self.optimizer.ensure_grad_buffer()
+        self._offloaded = None
+        torch.cuda.synchronize()
 
 
 class _ValueInput:

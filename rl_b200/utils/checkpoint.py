@@ -140,10 +140,14 @@ class CheckpointManager:
                 yaml.safe_dump(_jsonable(run_config), f, sort_keys=False)
         return tmp
 
-    def finalize_checkpoint(self, tmp_path: str) -> str:
-        """Publish ``tmp_step_N`` as ``step_N`` (atomic rename) and prune."""
+    def finalize_checkpoint(self, tmp_path: str, wait_fn=None) -> str:
+        """Publish ``tmp_step_N`` as ``step_N`` (atomic rename) and prune.  With
+        ``wait_fn`` (the policy's ``finalize_async_save``: background weight writes
+        still running) the rename happens on a background thread after it returns."""
 
         def work():
+            if wait_fn is not None:
+                wait_fn()
             step = int(os.path.basename(tmp_path).split("_")[-1])
             final = self.step_dir(step)
             if os.path.exists(final):
@@ -151,7 +155,7 @@ class CheckpointManager:
             os.replace(tmp_path, final)
             self.remove_old_checkpoints()
 
-        if self.cfg.get("async_finalize"):
+        if self.cfg.get("async_finalize") or wait_fn is not None:
             self._thread = threading.Thread(target=work, daemon=True)
             self._thread.start()
         else:
@@ -228,8 +232,10 @@ class CheckpointManager:
             torch.save(obj, os.path.join(tmp, name))
         if dist.is_initialized():
             dist.barrier()
+        pending = getattr(policy, "poll_async_save", None)
+        wait_fn = policy.finalize_async_save if pending is not None and not pending() else None
         if rank0:
-            return self.finalize_checkpoint(tmp)
+            return self.finalize_checkpoint(tmp, wait_fn=wait_fn)
         return self.step_dir(step)
 
 

@@ -231,3 +231,31 @@ def case_torch_dist(rank: int, tp: int, ep: int, moe: bool, path: str, mode: str
     if dist.is_initialized():
         dist.barrier()
     return {"sd": sd, "lp": lp, "step": int(w.optimizer.step_count)}
+
+
+def case_torch_dist_async(rank: int, tp: int, path: str):
+    """Asynchronous torch_dist save: the weights are staged before save_checkpoint
+    returns, so a training step taken right after does not leak into the files."""
+    from rl_b200.models.checkpoint_io import hf_state_dict
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import init_distributed
+
+    torch.manual_seed(0)
+    ps = init_distributed(tp=tp, backend="gloo")
+    w = PolicyWorker(_pcfg(False), model_cfg=TINY, pstate=ps, seed=3)
+    loss = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
+    per = 8 // ps.dp_size
+    w.train(make_batch(seed=0).slice(ps.dp_rank * per, (ps.dp_rank + 1) * per), loss, gbs=per)
+    saved = {k: v.detach().float().cpu().clone() for k, v in hf_state_dict(w.model, dtype=None).items()}
+    w.save_checkpoint(path, optimizer_path="flag", fmt="torch_dist", async_save=True)
+    pending_after_return = not w.poll_async_save()
+    w.train(make_batch(seed=1).slice(ps.dp_rank * per, (ps.dp_rank + 1) * per), loss, gbs=per)  # overlaps the write
+    w.finalize_async_save()
+    assert w.poll_async_save()
+    w2 = PolicyWorker(_pcfg(False), model_cfg=TINY, pstate=ps, seed=9)
+    w2.load_checkpoint(path, optimizer_path="flag")
+    back = {k: v.detach().float().cpu().clone() for k, v in hf_state_dict(w2.model, dtype=None).items()}
+    return {"max_err": max((back[k] - saved[k]).abs().max().item() for k in saved),
+            "moved": max((back[k] - v.detach().float().cpu()).abs().max().item()
+                         for k, v in hf_state_dict(w.model, dtype=None).items()),
+            "pending": pending_after_return}

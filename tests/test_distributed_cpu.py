@@ -250,3 +250,15 @@ def test_torch_dist_megatron_layout(tmp_path):
     torch.testing.assert_close(emb.float(), ref["model.embed_tokens.weight"])
     exp_avg = read_global_tensor(path, "optimizer.state.exp_avg.decoder.layers.self_attention.linear_proj.weight")
     assert exp_avg.shape == (c.num_layers, H, c.num_heads * hd) and exp_avg.abs().sum() > 0
+
+
+@pytest.mark.parametrize("world,tp", [(1, 1), (2, 2)])
+def test_torch_dist_async_save(tmp_path, world, tp):
+    """Background torch_dist writes (gloo coordination group, host-staged pieces):
+    the files hold the weights of the moment of the call even though training
+    continues during the write."""
+    from tests.dist_cases import case_torch_dist_async
+
+    outs = spawn_ranks(case_torch_dist_async, world, tp, str(tmp_path / "w"))
+    for o in outs:
+        assert o["max_err"] == 0.0 and o["moved"] > 0.0

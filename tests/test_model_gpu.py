@@ -168,3 +168,28 @@ def test_fp8_blockwise_training_step(cuda_device):
     assert abs(res[True][1] - res[False][1]) < 0.1 * res[False][1]
     m = batch["token_mask"] > 0
     assert (res[True][2] - res[False][2])[m].abs().mean().item() < 0.1
+
+
+def test_offload_to_cpu_and_back(cuda_device):
+    """offload_to_cpu frees the parameter / optimizer / reference storage on the
+    GPU (parameter views stay valid) and onload restores the same values; the
+    worker then trains and generates as before."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import single_process_state
+    from tests.dist_cases import make_batch
+
+    w = PolicyWorker(_policy_cfg(), model_cfg=SMALL, pstate=single_process_state(cuda_device), seed=4)
+    before = w.model.flat_param.detach().clone()
+    torch.cuda.synchronize()
+    used0 = torch.cuda.memory_allocated(cuda_device)
+    w.offload_to_cpu()
+    used1 = torch.cuda.memory_allocated(cuda_device)
+    assert used0 - used1 >= before.numel() * before.element_size(), (used0, used1)
+    w.onload()
+    assert torch.equal(w.model.flat_param, before)
+    q = w.model.param("model.layers.0.self_attn.qkv_proj.weight")
+    assert q.data_ptr() >= w.model.flat_param.data_ptr()  # a view into the restored buffer
+    data = make_batch(B=8, S=24, vocab=SMALL.vocab_size, seed=0)
+    res = w.train(data, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)
+    assert res["grad_norm"] > 0 and not torch.equal(w.model.flat_param, before)

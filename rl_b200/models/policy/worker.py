@@ -493,25 +493,30 @@ class PolicyWorker:
 
     def _pp_inference(self, plan, ids, lengths, fn) -> None:
         """Forward-only pass of ``plan`` through the pipeline; ``fn(rows, out)``
-        consumes the last stage's output of each (non-dummy) micro-batch."""
+        consumes the last stage's output of each (non-dummy) micro-batch.  Runs
+        the forward steps of the training schedule's plan (same pairing of sends
+        and receives)."""
+        from rl_b200.parallel.pipeline import _run_plan, plan_1f1b, plan_virtual
+
         comm = self._pp_comm
         V = self.model.vpp
-        for v in range(V):  # virtual pipeline: every micro-batch through chunk v, then chunk v + 1
+        mbs = []
+        for rows in plan:
+            dummy = rows[0] < 0
+            mbs.append(([-1 - rows[0]] if dummy else rows, dummy))
+        steps = (plan_virtual(comm.n, comm.stage, len(mbs), V, backward=False) if V > 1
+                 else plan_1f1b(comm.n, comm.stage, len(mbs), backward=False))
+
+        def forward(i, v, h):
             self.model.chunk = v if V > 1 else None
-            for rows in plan:
-                dummy = rows[0] < 0
-                rows = [-1 - rows[0]] if dummy else rows
-                if self.model.is_first_stage:
-                    self._pp_in = None
-                else:
-                    self._pp_in = comm._recv(self._pp_shape(ids, lengths, rows), self.dtype, self.device,
-                                             comm.prev_wrap)
-                out = fn(rows, dummy)
-                self._pp_in = None
-                if not self.model.is_last_stage:
-                    comm._send(out, comm.next_wrap)
+            self._pp_in = h
+            out = fn(*mbs[i])
+            self._pp_in = None
+            return out
+
+        _run_plan(comm, steps, forward, lambda i: self._pp_shape(ids, lengths, mbs[i][0]), self.dtype,
+                  self.device, backward=False)
         self.model.chunk = None
-        comm.wait()
 
     def _pp_broadcast(self, t: torch.Tensor) -> torch.Tensor:
         """Last stage's tensor to every stage of the pipeline."""

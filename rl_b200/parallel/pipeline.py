@@ -19,17 +19,18 @@ tensor-parallel rank of both), ``[T_local, H]`` in the compute dtype; shapes are
 derived on both sides from the packing plan, so no shape message precedes a
 tensor.
 
-Why one process group per DIRECTED edge: NCCL runs all point-to-point work of
-one communicator on one stream, in posting order, and a send larger than its
-channel buffer finishes only once the peer's matching receive runs.  If both
-directions of a rank pair shared a communicator, rank 0 could queue
-``send(f1)`` ahead of ``recv(g0)`` while rank 1 queues ``send(g0)`` ahead of
-``recv(f1)`` (1F1B at two stages), or the virtual schedule could queue all of
-chunk 0's sends ahead of the wrap-around receive: each is a cyclic wait.  With
-a communicator per direction, the stream of edge ``a -> b`` carries only
-``a``'s sends (on ``a``) and ``b``'s matching receives (on ``b``), in the same
-order on both sides, so a send can wait only on its own receive, which in turn
-waits only on work that precedes it in the schedule's dependency order.
+Pairing (why the executor batches): NCCL runs the point-to-point work between
+two ranks on one stream per communicator, in posting order, and a send larger
+than its channel buffer completes only together with the peer's matching
+receive.  At two stages, 1F1B has rank 0 send ``f1`` and then receive ``g0``
+while rank 1 sends ``g0`` and then receives ``f1``: as four separate
+operations each rank's stream holds a send its peer answers only after its own
+send, a cyclic wait.  The executor therefore posts the send of one plan step
+and the receive of the next step in ONE ``batch_isend_irecv`` call whenever
+both go to the same peer (an NCCL group: the two make progress together), and
+separately otherwise; this is the pairing of Megatron's
+``send_forward_recv_backward`` / ``send_backward_recv_forward``.
+``simulate_rendezvous`` checks the plans against exactly this behaviour.
 
 Reference: the Megatron-core pipeline schedule the reference's Megatron
 policy worker calls (``get_forward_backward_func``,
@@ -65,9 +66,7 @@ class PlanStep(NamedTuple):
 
 class PipelineComm:
     """Send / receive between pipeline stages (global ranks from ``ps.pp_ranks``,
-    ordered by stage).  Traffic from rank ``a`` to rank ``b`` uses the process
-    group of the directed edge ``(a, b)`` from ``ps.pp_edge_groups`` when it is
-    there (one communicator, hence one stream, per direction)."""
+    ordered by stage) on the pipeline group."""
 
     def __init__(self, ps):
         self.ps = ps
@@ -75,43 +74,51 @@ class PipelineComm:
         self.group = ps.pp_group
         self.ranks = list(ps.pp_ranks)
         self.me = self.ranks[self.stage]
-        self.edges = dict(getattr(ps, "pp_edge_groups", None) or {})
         self.prev = ps.pp_ranks[self.stage - 1] if self.stage > 0 else None
         self.next = ps.pp_ranks[self.stage + 1] if self.stage + 1 < self.n else None
-        # virtual pipeline: chunk v of the last rank feeds chunk v + 1 of the first
-        self.prev_wrap = ps.pp_ranks[(self.stage - 1) % self.n]
-        self.next_wrap = ps.pp_ranks[(self.stage + 1) % self.n]
         self._pending: list = []  # (work, tensor kept alive until the send completed)
 
-    def _group(self, src: int, dst: int):
-        return self.edges.get((src, dst), self.group)
-
-    def _send(self, t: torch.Tensor, dst: int) -> None:
-        t = t.contiguous()
-        self._pending.append((dist.isend(t, dst, group=self._group(self.me, dst)), t))
-
-    def _recv(self, shape, dtype, device, src: int) -> torch.Tensor:
-        buf = torch.empty(shape, dtype=dtype, device=device)
-        dist.recv(buf, src, group=self._group(src, self.me))
+    def exchange(self, send: Optional[tuple], recv: Optional[tuple]) -> Optional[torch.Tensor]:
+        """Post ``send = (tensor, dst_stage)`` and ``recv = (shape, dtype, device,
+        src_stage)`` (either may be None); returns the received tensor once it
+        arrived (stream-ordered).  A send and a receive with the same peer are
+        posted together as one group; otherwise the send is posted first and left
+        in flight (``wait`` completes it)."""
+        ops, buf = [], None
+        if send is not None:
+            t = send[0].contiguous()
+            ops.append(dist.P2POp(dist.isend, t, self.ranks[send[1]], group=self.group))
+        if recv is not None:
+            shape, dtype, device, src = recv
+            buf = torch.empty(shape, dtype=dtype, device=device)
+            rop = dist.P2POp(dist.irecv, buf, self.ranks[src], group=self.group)
+        if send is not None and recv is not None and send[1] == recv[3]:
+            for w in dist.batch_isend_irecv(ops + [rop]):
+                w.wait()
+            return buf
+        if send is not None:
+            self._pending.append((dist.batch_isend_irecv(ops)[0], ops[0].tensor))
+        if recv is not None:
+            dist.batch_isend_irecv([rop])[0].wait()
         return buf
 
     def send_to_stage(self, t: torch.Tensor, stage: int) -> None:
-        self._send(t, self.ranks[stage])
+        self.exchange((t, stage), None)
 
     def recv_from_stage(self, shape, dtype, device, stage: int) -> torch.Tensor:
-        return self._recv(shape, dtype, device, self.ranks[stage])
+        return self.exchange(None, (shape, dtype, device, stage))
 
     def send_forward(self, t: torch.Tensor) -> None:
-        self._send(t, self.next)
+        self.send_to_stage(t, self.stage + 1)
 
     def recv_forward(self, shape, dtype, device) -> torch.Tensor:
-        return self._recv(shape, dtype, device, self.prev)
+        return self.recv_from_stage(shape, dtype, device, self.stage - 1)
 
     def send_backward(self, g: torch.Tensor) -> None:
-        self._send(g, self.prev)
+        self.send_to_stage(g, self.stage - 1)
 
     def recv_backward(self, shape, dtype, device) -> torch.Tensor:
-        return self._recv(shape, dtype, device, self.next)
+        return self.recv_from_stage(shape, dtype, device, self.stage + 1)
 
     def wait(self) -> None:
         for w, _ in self._pending:
@@ -153,51 +160,67 @@ def plan_virtual(num_stages: int, stage: int, num_microbatches: int, num_chunks:
                  backward: bool = True) -> list[PlanStep]:
     """The interleaved plan of one rank: virtual stage ``v * S + s`` is chunk
     ``v`` of rank ``s``; the last rank's chunk ``v`` feeds the first rank's
-    chunk ``v + 1``.  Every rank runs all forwards chunk by chunk, then all
-    backwards in reverse chunk order, which is a topological order of the
-    virtual stages' dependencies on every rank."""
+    chunk ``v + 1``.  Micro-batches go in rounds of ``S`` (Megatron's
+    interleaving unit): each round runs its forwards chunk by chunk; after all
+    forwards, each round runs its backwards in reverse chunk order.  Rounds bound
+    the messages in flight on the wrap-around edge to one round, which keeps the
+    paired point-to-point posting free of cyclic waits (see
+    ``simulate_rendezvous``)."""
     S, s, V, M = num_stages, stage, num_chunks, num_microbatches
+    rounds = [range(g, min(g + S, M)) for g in range(0, M, S)]
     out = []
-    for v in range(V):
-        first, last = s == 0 and v == 0, s == S - 1 and v == V - 1
-        for i in range(M):
-            out.append(PlanStep("F", v, i, None if first else (s - 1) % S, None if last else (s + 1) % S))
-    if backward:
-        for v in reversed(range(V)):
+    for mbs in rounds:
+        for v in range(V):
             first, last = s == 0 and v == 0, s == S - 1 and v == V - 1
-            for i in range(M):
-                out.append(PlanStep("B", v, i, None if last else (s + 1) % S, None if first else (s - 1) % S))
+            for i in mbs:
+                out.append(PlanStep("F", v, i, None if first else (s - 1) % S, None if last else (s + 1) % S))
+    if backward:
+        for mbs in rounds:
+            for v in reversed(range(V)):
+                first, last = s == 0 and v == 0, s == S - 1 and v == V - 1
+                for i in mbs:
+                    out.append(PlanStep("B", v, i, None if last else (s + 1) % S, None if first else (s - 1) % S))
     return out
 
 
 def _run_plan(comm: PipelineComm, plan: list[PlanStep],
               forward: Callable[[int, int, Optional[torch.Tensor]], torch.Tensor],
               in_shape: Callable[[int], tuple], dtype: torch.dtype, device: torch.device, backward: bool) -> None:
+    """Execute a plan: the receive of step k + 1 is posted together with the send
+    of step k (one group when they share a peer, see the module docstring)."""
     live: dict = {}
-    order: deque = deque()
-    for st in plan:
+
+    def recv_spec(st: PlanStep):
+        if st.recv_from is None:
+            return None
         if st.kind == "F":
-            inp = None
-            if st.recv_from is not None:
-                inp = comm.recv_from_stage(in_shape(st.mb), dtype, device, st.recv_from)
-                if backward:
-                    inp.requires_grad_(True)
+            return (in_shape(st.mb), dtype, device, st.recv_from)
+        out = live[(st.chunk, st.mb)][1]
+        return (out.shape, out.dtype, device, st.recv_from)
+
+    got = comm.exchange(None, recv_spec(plan[0])) if plan else None
+    for k, st in enumerate(plan):
+        send = None
+        if st.kind == "F":
+            inp = got
+            if inp is not None and backward:
+                inp.requires_grad_(True)
             out = forward(st.mb, st.chunk, inp)
             if st.send_to is not None:
-                comm.send_to_stage(out.detach(), st.send_to)
+                send = (out.detach(), st.send_to)
             if backward:
                 live[(st.chunk, st.mb)] = (inp, out)
-                order.append((st.chunk, st.mb))
         else:
             inp, out = live.pop((st.chunk, st.mb))
             if st.recv_from is None:
                 out.backward()
             else:
-                g = comm.recv_from_stage(out.shape, out.dtype, device, st.recv_from)
-                torch.autograd.backward(out, g)
+                torch.autograd.backward(out, got)
             if st.send_to is not None:
-                comm.send_to_stage(inp.grad, st.send_to)
+                send = (inp.grad, st.send_to)
             del inp, out
+        nxt = recv_spec(plan[k + 1]) if k + 1 < len(plan) else None
+        got = comm.exchange(send, nxt) if (send is not None or nxt is not None) else None
     comm.wait()
 
 
@@ -231,69 +254,100 @@ def virtual_pipeline(comm: PipelineComm, num_microbatches: int, num_chunks: int,
     _run_plan(comm, plan, forward, in_shape, dtype, device, backward)
 
 
-def simulate_rendezvous(plans: list[list[PlanStep]], directed: bool = True) -> bool:
+def simulate_rendezvous(plans: list[list[PlanStep]], pair_same_peer: bool = True) -> bool:
     """Whether the per-rank plans finish under NCCL's worst case for large
-    messages: every communicator runs its point-to-point operations on one
-    stream in posting order, and a send and its receive complete only together
-    (neither side buffers).  ``directed`` gives each direction of a rank pair
-    its own communicator (what :class:`PipelineComm` does); False shares one
-    communicator per pair.  Each rank's compute stream runs its plan in order;
-    a compute waits for its receive, a send for its compute.  Returns False on a
-    deadlock (no operation can make progress before all are done)."""
+    messages, executed as :func:`_run_plan` posts them: one communicator stream
+    per rank pair running its operations in posting order; a send and its
+    receive complete only together (neither side buffers); an operation posted
+    after step k's compute starts only once that compute finished (the stream
+    waits for the compute stream at posting); the receive of step k + 1 is
+    posted with the send of step k, as one group when they share a peer
+    (``pair_same_peer``; False posts them separately, send first).  A grouped
+    receive releases its compute only when the whole group finished.  Returns
+    False on a deadlock."""
     S = len(plans)
-    # per rank: comm streams keyed by communicator; items are [op, done]
-    streams: list[dict] = [dict() for _ in range(S)]
-    compute: list[list] = []
-    for r, plan in enumerate(plans):
-        items = []
-        for k, st in enumerate(plan):
-            recv = send = None
-            if st.recv_from is not None:
-                key = (st.recv_from, r) if directed else frozenset((st.recv_from, r))
-                msg = (st.kind, st.chunk, st.mb, st.recv_from, r)
-                recv = {"kind": "recv", "msg": msg, "done": False}
-                streams[r].setdefault(key, []).append(recv)
-            comp = {"done": False, "recv": recv}
-            items.append(comp)
-            if st.send_to is not None:
-                key = (r, st.send_to) if directed else frozenset((r, st.send_to))
-                # a forward's output is the next virtual stage's forward input; a backward's
-                # input gradient is the previous stage's backward output-gradient
-                msg = (st.kind, st.chunk + (1 if st.kind == "F" and st.send_to == 0 and r == S - 1 else 0)
-                       - (1 if st.kind == "B" and st.send_to == S - 1 and r == 0 else 0), st.mb, r, st.send_to)
-                send = {"kind": "send", "msg": msg, "done": False, "after": comp}
-                streams[r].setdefault(key, []).append(send)
-        compute.append(items)
 
-    def head(q):
-        for op in q:
-            if not op["done"]:
-                return op
+    def msg_of(r, st, sending):
+        # a forward's output is the next virtual stage's input; a backward's input
+        # gradient is the previous virtual stage's output gradient
+        if sending:
+            ch = st.chunk + (1 if st.kind == "F" and st.send_to == 0 and r == S - 1 else 0) \
+                - (1 if st.kind == "B" and st.send_to == S - 1 and r == 0 else 0)
+            return (st.kind, ch, st.mb, r, st.send_to)
+        return (st.kind, st.chunk, st.mb, st.recv_from, r)
+
+    streams = [dict() for _ in range(S)]  # rank -> peer -> list of items (each a list of ops)
+    computes = []
+    for r, plan in enumerate(plans):
+        comps = [{"done": False, "wait": None} for _ in plan]
+        computes.append(comps)
+
+        def post(items_ops, after):
+            for ops in items_ops:
+                item = {"ops": ops, "after": after}
+                for op in ops:
+                    op["item"] = item
+                streams[r].setdefault(ops[0]["peer"], []).append(item)
+
+        def recv_op(k):
+            st = plan[k]
+            if st.recv_from is None:
+                return None
+            return {"kind": "recv", "msg": msg_of(r, st, False), "peer": st.recv_from, "done": False}
+
+        first = recv_op(0) if plan else None
+        if first is not None:
+            post([[first]], None)
+            comps[0]["wait"] = first
+        for k, st in enumerate(plan):
+            send = None
+            if st.send_to is not None:
+                send = {"kind": "send", "msg": msg_of(r, st, True), "peer": st.send_to, "done": False}
+            rv = recv_op(k + 1) if k + 1 < len(plan) else None
+            if send is not None and rv is not None and pair_same_peer and send["peer"] == rv["peer"]:
+                post([[send, rv]], comps[k])
+                comps[k + 1]["wait"] = ("group", send, rv)
+            else:
+                post([[x] for x in (send, rv) if x is not None], comps[k])
+                if rv is not None:
+                    comps[k + 1]["wait"] = rv
+
+    def head(r, peer):
+        for item in streams[r].get(peer, []):
+            if not all(op["done"] for op in item["ops"]):
+                return item
         return None
+
+    def active(item):
+        return item is not None and (item["after"] is None or item["after"]["done"])
 
     progress = True
     while progress:
         progress = False
         for r in range(S):
-            for comp in compute[r]:
-                if comp["done"]:
+            for c in computes[r]:
+                if c["done"]:
                     continue
-                if comp["recv"] is None or comp["recv"]["done"]:
-                    comp["done"] = True
+                w = c["wait"]
+                ok = w is None or (all(x["done"] for x in w[1:]) if isinstance(w, tuple) else w["done"])
+                if ok:
+                    c["done"] = True
                     progress = True
                 break
-        # rendezvous: a send at the head of its stream whose data is ready meets the
-        # receive at the head of the peer's stream for the same message
         for r in range(S):
-            for key, q in streams[r].items():
-                op = head(q)
-                if op is None or op["kind"] != "send" or not op["after"]["done"]:
+            for peer in list(streams[r]):
+                it = head(r, peer)
+                if not active(it):
                     continue
-                dst = op["msg"][4]
-                pkey = key
-                peer = head(streams[dst].get(pkey, []))
-                if peer is not None and peer["kind"] == "recv" and peer["msg"] == op["msg"]:
-                    op["done"] = peer["done"] = True
-                    progress = True
-    return all(c["done"] for items in compute for c in items) and \
-        all(op["done"] for st in streams for q in st.values() for op in q)
+                pit = head(peer, r)
+                if not active(pit):
+                    continue
+                for op in it["ops"]:
+                    if op["done"] or op["kind"] != "send":
+                        continue
+                    for pop in pit["ops"]:
+                        if not pop["done"] and pop["kind"] == "recv" and pop["msg"] == op["msg"]:
+                            op["done"] = pop["done"] = True
+                            progress = True
+    return all(c["done"] for cs in computes for c in cs) and \
+        all(op["done"] for st in streams for q in st.values() for it in q for op in it["ops"])

@@ -53,7 +53,6 @@ class ParallelState:
     ep_ranks: list = field(default_factory=lambda: [0])
     cp_ranks: list = field(default_factory=lambda: [0])
     pp_ranks: list = field(default_factory=lambda: [0])
-    pp_edge_groups: dict = field(default_factory=dict)  # (src rank, dst rank) -> group of that direction
     backend: str = "gloo"
     device: torch.device = field(default_factory=lambda: torch.device("cpu"))
 
@@ -146,23 +145,6 @@ def init_distributed(tp: int = 1, cp: int = 1, ep: int = 1, pp: int = 1, backend
     # PP groups: vary p
     make([[r for r in all_ranks if coords[r][:3] == key] for key in sorted({c[:3] for c in coords.values()})],
          "pp_group", "pp_ranks")
-    # Directed pipeline edges: one 2-rank group per direction of every adjacent stage pair
-    # (the last stage's edge to the first serves the virtual pipeline's wrap-around), so
-    # each direction runs on its own communicator stream; every rank creates every group
-    # in the same order
-    if pp > 1:
-        edges: list[tuple[int, int]] = []
-        for key in sorted({c[:3] for c in coords.values()}):
-            ring = sorted((r for r in all_ranks if coords[r][:3] == key), key=lambda r: coords[r][3])
-            for i in range(pp):
-                a, b = ring[i], ring[(i + 1) % pp]
-                for e in ((a, b), (b, a)):
-                    if e not in edges:
-                        edges.append(e)
-        for a, b in edges:
-            pg = dist.new_group(sorted((a, b)), backend=backend)
-            if rank in (a, b):
-                st.pp_edge_groups[(a, b)] = pg
     # Model-parallel groups (one replica): fixed d
     make([[r for r in all_ranks if coords[r][2] == d] for d in range(dp)], "mp_group")
     # EP groups: within a pipeline stage and TP rank, consecutive blocks of ep ranks

@@ -157,19 +157,29 @@ def case_data_plane(rank: int, port: int):
     return {"ok": ok, "keys": keys, "stats": dp.metrics()}
 
 
-def case_pp_edges(rank: int, pp: int):
-    """Directed pipeline edge groups of this rank, and a send/recv over each."""
+def case_pp_exchange(rank: int, pp: int):
+    """PipelineComm.exchange: a send to the next stage paired with a receive from
+    it, and an unpaired send forward / receive from the previous stage."""
     from rl_b200.parallel.pipeline import PipelineComm
     from rl_b200.parallel.state import init_distributed
 
     ps = init_distributed(pp=pp, backend="gloo")
     comm = PipelineComm(ps)
-    if comm.next is not None:
-        comm.send_forward(torch.full((3,), float(rank)))
-    got = comm.recv_forward((3,), torch.float32, torch.device("cpu")) if comm.prev is not None else None
+    s = comm.stage
+    cpu = torch.device("cpu")
+    ok = True
+    # unpaired: forward chain
+    got = comm.exchange((torch.full((3,), float(s)), s + 1) if s + 1 < pp else None,
+                        ((3,), torch.float32, cpu, s - 1) if s > 0 else None)
+    ok &= got is None or float(got[0]) == s - 1
     comm.wait()
-    assert got is None or float(got[0]) == float(comm.prev)
-    return {"rank": rank, "pp_ranks": list(ps.pp_ranks), "edges": sorted(ps.pp_edge_groups)}
+    # paired: even stages exchange with their next stage, odd ones with their previous
+    peer = s + 1 if s % 2 == 0 else s - 1
+    if 0 <= peer < pp:
+        got = comm.exchange((torch.full((2,), 10.0 * s), peer), ((2,), torch.float32, cpu, peer))
+        ok &= float(got[0]) == 10.0 * peer
+    comm.wait()
+    return {"rank": rank, "ok": bool(ok)}
 
 
 def case_ckpt_relayout_vpp(rank: int, pp: int, path: str, vpp_save: int, vpp_load: int):

@@ -109,35 +109,31 @@ def test_schedule_1f1b_order():
 
 def test_pipeline_plans_cannot_deadlock_under_rendezvous():
     """The plans finish when every send of a large message waits for its
-    receive (NCCL past its channel buffer) and each communicator runs its
-    point-to-point work in posting order.  With one communicator per rank PAIR
-    (both directions on one stream) 1F1B at two stages and the virtual schedule
-    deadlock; with one per direction (what PipelineComm uses) neither does."""
+    receive (NCCL past its channel buffer), each rank pair's communicator runs
+    its point-to-point work in posting order, and the executor pairs a step's
+    send with the next step's receive to the same peer in one group.  Posting
+    them separately deadlocks 1F1B at two stages and the interleaved schedule."""
     from rl_b200.parallel.pipeline import plan_1f1b, plan_virtual, simulate_rendezvous
 
     for S in (2, 3, 4):
-        for M in (1, 2, 3, 5, 8):
-            plans = [plan_1f1b(S, s, M) for s in range(S)]
-            assert simulate_rendezvous(plans, directed=True), (S, M)
-            assert simulate_rendezvous([plan_1f1b(S, s, M, backward=False) for s in range(S)], directed=True)
+        for M in (1, 2, 3, 4, 5, 8, 13):
+            assert simulate_rendezvous([plan_1f1b(S, s, M) for s in range(S)]), (S, M)
+            assert simulate_rendezvous([plan_1f1b(S, s, M, backward=False) for s in range(S)]), (S, M)
             for V in (2, 3):
-                vplans = [plan_virtual(S, s, M, V) for s in range(S)]
-                assert simulate_rendezvous(vplans, directed=True), (S, M, V)
-    # the hazard the directed edges remove
-    assert not simulate_rendezvous([plan_1f1b(2, s, 4) for s in range(2)], directed=False)
-    assert not simulate_rendezvous([plan_virtual(2, s, 4, 2) for s in range(2)], directed=False)
+                for bw in (True, False):
+                    assert simulate_rendezvous([plan_virtual(S, s, M, V, bw) for s in range(S)]), (S, M, V, bw)
+    # the hazard the pairing removes
+    assert not simulate_rendezvous([plan_1f1b(2, s, 4) for s in range(2)], pair_same_peer=False)
+    assert not simulate_rendezvous([plan_virtual(2, s, 4, 2) for s in range(2)], pair_same_peer=False)
 
 
-def test_pipeline_edge_groups_are_directed():
-    """init_distributed builds one group per direction of every adjacent pair."""
-    from tests.dist_cases import case_pp_edges
+def test_pipeline_comm_exchange():
+    """Sends and receives between stages over gloo, paired and unpaired."""
+    from tests.dist_cases import case_pp_exchange
 
-    outs = spawn_ranks(case_pp_edges, 4, 2)
+    outs = spawn_ranks(case_pp_exchange, 3, 3)
     for o in outs:
-        r, ring = o["rank"], o["pp_ranks"]
-        s = ring.index(r)
-        want = {(r, ring[(s + 1) % 2]), (ring[(s + 1) % 2], r)}
-        assert set(o["edges"]) == want, o
+        assert o["ok"], o
 
 
 def test_uneven_pipeline_stages():

@@ -9,6 +9,7 @@
     python -m rl_b200.bench_kernels lmhead_fwd [T H V]   (fused forward only: the ncu case)
     python -m rl_b200.bench_kernels fp8       [M N K]
     python -m rl_b200.bench_kernels numerics  [prompts max_new]
+    python -m rl_b200.bench_kernels rollout   [seqs max_new]   (8B rollout; NVTX range "rollout_timed")
 
 Each prints one line with the time and the achieved rate, and is small enough
 to be captured under ``ncu -k <kernel> -c 1`` (a few GB on the device at most).
@@ -327,13 +328,50 @@ def bench_numerics(prompts=64, max_new=256):
                       "threshold": 0.002, "ln_vocab": math.log(mcfg.vocab_size)}))
 
 
+def bench_rollout(seqs=64, max_new=256):
+    """Rollout engine on the Llama-3.1-8B shape (random init): one warm-up
+    generate (captures the decode graphs), then one timed generate inside the
+    NVTX range ``rollout_timed`` (``ncu --nvtx --nvtx-include rollout_timed/``
+    restricts a launch list to it).  Prompts U[128, 512], EOS ignored."""
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import single_process_state
+
+    dev = torch.device("cuda", 0)
+    mcfg = get_model_config("llama3.1-8b")
+    pcfg = {"model_name": "llama3.1-8b", "max_total_sequence_length": 512 + max_new, "precision": "bfloat16",
+            "train_global_batch_size": seqs,
+            "generation": {"temperature": 1.0, "top_p": 1.0, "top_k": None, "max_new_tokens": max_new,
+                           "max_num_seqs": 512, "mcore_generation_config": {"block_size_tokens": 256}}}
+    w = PolicyWorker(pcfg, model_cfg=mcfg, pstate=single_process_state(dev), seed=1234, init_reference_model=False)
+    g = torch.Generator().manual_seed(0)
+    lens = torch.randint(128, 513, (seqs,), generator=g)
+    ids = torch.randint(0, mcfg.vocab_size, (seqs, 512), generator=g)
+    batch = BatchedDataDict({"input_ids": ids, "input_lengths": lens})
+    w.generate(batch)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.nvtx.range_push("rollout_timed")
+    e0.record()
+    out = w.generate(batch)
+    e1.record()
+    torch.cuda.nvtx.range_pop()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1)
+    n = int(out["generation_lengths"].sum())
+    print(f"rollout seqs={seqs} max_new={max_new}: {t:.1f} ms, {n / t * 1e3:.0f} generated tok/s, "
+          f"{t / max_new:.3f} ms per decode step (incl. prefill share)")
+
+
 def main(argv=None):
     argv = list(sys.argv[1:] if argv is None else argv)
     what = argv.pop(0) if argv else "gemm"
     args = [int(x) for x in argv]
     torch.manual_seed(0)
     {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
-     "logprob": bench_logprob, "lmhead": bench_lmhead, "lmhead_fwd": bench_lmhead_fwd, "fp8": bench_fp8, "numerics": bench_numerics}[what](*args)
+     "logprob": bench_logprob, "lmhead": bench_lmhead, "lmhead_fwd": bench_lmhead_fwd, "fp8": bench_fp8, "numerics": bench_numerics,
+     "rollout": bench_rollout}[what](*args)
 
 
 if __name__ == "__main__":

@@ -13,7 +13,12 @@ step, ``shutdown`` at the end.  Transports here:
   or the 128x128 e4m3 quantisation (``ColocatedReshardSynchronizer``);
 * ``broadcast`` - non-colocated trainer / generation processes: packed,
   double-buffered bucket broadcast over a (stateless) process group
-  (``PackedBroadcastSynchronizer``).
+  (``PackedBroadcastSynchronizer``);
+* ``sparse_broadcast`` - the same transport sending, after a first full refit,
+  only the weights whose bits changed (``SparseDeltaBroadcastSynchronizer``).
+
+``create_weight_synchronizer(kind, **kwargs)`` builds one by name (the
+reference's ``refit_transport`` values map onto these).
 """
 
 from __future__ import annotations

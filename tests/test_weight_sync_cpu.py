@@ -78,3 +78,47 @@ def test_watchdog_context_and_hold(tmp_path, monkeypatch):
     threading.Timer(0.3, p.unlink).start()
     held = hold_refit_for_fault_injection()
     assert 0.2 < held < 3.0
+
+
+def _case_sparse(rank: int, port: int):
+    from rl_b200.distributed.stateless_group import StatelessProcessGroup
+    from rl_b200.weight_sync.broadcast import SparseDeltaBroadcastSynchronizer
+
+    g = StatelessProcessGroup("127.0.0.1", port, rank, 3, backend="gloo", name="refit", timeout_s=30)
+    n = 20000
+    gen = torch.Generator().manual_seed(0)
+    w = torch.randn(n, generator=gen).to(torch.bfloat16)
+    flat = w.clone() if rank == 0 else torch.zeros(n, dtype=torch.bfloat16)
+    ws = SparseDeltaBroadcastSynchronizer(flat, g, src=0, bucket_bytes=4096, timeout_s=20)
+    out = {"full": ws.sync()}
+    ok = [torch.equal(flat, w)]
+    # a small update: most bf16 weights keep their bits, a few change
+    upd = w.float() * (1 + 1e-4 * torch.randn(n, generator=gen))
+    upd[::97] += 0.05  # some clearly changed entries
+    upd[4096:6144] += 1.0  # one densely changed stretch (sent as whole buckets)
+    upd = upd.to(torch.bfloat16)
+    if rank == 0:
+        flat.copy_(upd)
+    out["delta"] = ws.sync()
+    out["stats"] = ws.last_stats
+    ok.append(torch.equal(flat, upd))
+    out["no_change"] = ws.sync()
+    ok.append(torch.equal(flat, upd))
+    g.destroy()
+    out["ok"] = all(ok)
+    return out
+
+
+def test_sparse_delta_refit_sends_only_changed_weights():
+    """After one full refit, refits carry only the changed bf16 weights (positions
+    + values, or whole buckets where most changed); every consumer ends with the
+    producer's exact bits."""
+    port = free_port()
+    outs = spawn_ranks(_case_sparse, 3, port, timeout_s=120)
+    assert all(o["ok"] for o in outs)
+    o = outs[0]
+    full = o["full"]["bytes"]
+    assert full == 20000 * 2
+    assert 0 < o["delta"]["bytes"] < 0.6 * full, o
+    assert 0 < o["stats"]["changed_fraction"] < 0.5
+    assert o["no_change"]["bytes"] <= 16 * (20000 * 2 // 4096 + 1)  # headers only

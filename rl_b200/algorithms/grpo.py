@@ -309,7 +309,11 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     timer = Timer()
     from rl_b200.utils.telemetry import Telemetry
 
-    _telemetry = Telemetry()
+    tcfg = master_config.get("telemetry") or {}
+    _telemetry = Telemetry(tcfg.get("path"), rank=ps.rank, otlp_endpoint=tcfg.get("otlp_endpoint"),
+                           resource={"rl.algorithm": "grpo"})
+    if checkpointer is not None:
+        checkpointer.telemetry = _telemetry
     model_cfg = getattr(getattr(policy, "model", None), "cfg", None)
     flop_tracker = FLOPTracker(model_cfg) if model_cfg is not None else None
     step = int(state["current_step"])
@@ -326,7 +330,7 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
             timer.reset()
             maybe_gpu_profile_step(step)
             t_step = time.perf_counter()
-            with timer.time("total_step_time"):
+            with timer.time("total_step_time"), _telemetry.span("step", **{"rl.step": step}) as step_span:
                 # ---- rollouts (with DAPO dynamic sampling) ----
                 kept_batches = []
                 gen_batches = 0
@@ -446,6 +450,8 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
             })
             timing = {k: v for k, v in timer.get_timing_metrics().items()}
             metrics.update(_telemetry.goodput(timing, step_time_max))
+            _telemetry.record_stage_spans(timing, parent=step_span)
+            _telemetry.flush()
             step += 1
             state["current_step"] = step
             state["total_steps"] = int(state.get("total_steps", 0)) + 1

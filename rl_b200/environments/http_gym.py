@@ -63,12 +63,13 @@ class HttpGymEnvironment(EnvironmentInterface):
         self.pool = ThreadPoolExecutor(max_workers=int(cfg.get("max_concurrency", 64)))
         self.failures = 0
 
-    def _post(self, payload: dict) -> Optional[dict]:
+    def _post(self, payload: dict, carrier: Optional[dict] = None) -> Optional[dict]:
         body = json.dumps(payload).encode()
+        # W3C trace context: the service's spans join the caller's trace
+        headers = {"Content-Type": "application/json", **(carrier or {})}
         for _ in range(self.retries + 1):
             try:
-                req = urllib.request.Request(self.base_url + "/run", data=body,
-                                             headers={"Content-Type": "application/json"}, method="POST")
+                req = urllib.request.Request(self.base_url + "/run", data=body, headers=headers, method="POST")
                 with urllib.request.urlopen(req, timeout=self.timeout) as r:
                     return json.loads(r.read().decode())
             except (urllib.error.URLError, TimeoutError, ValueError, OSError):
@@ -78,7 +79,10 @@ class HttpGymEnvironment(EnvironmentInterface):
     def step(self, message_log_batch: list[list[dict]], metadata: list[Any]) -> EnvironmentReturn:
         payloads = [{"messages": [_to_json(m) for m in log], "metadata": md, "task": self.task}
                     for log, md in zip(message_log_batch, metadata)]
-        results = list(self.pool.map(self._post, payloads))
+        from rl_b200.utils.telemetry import current_trace_carrier
+
+        carrier = current_trace_carrier()  # captured here: the pool threads have their own context
+        results = list(self.pool.map(lambda p: self._post(p, carrier), payloads))
         obs, meta, rewards, done = [], [], [], []
         for res, md, log in zip(results, metadata, message_log_batch):
             if res is None:

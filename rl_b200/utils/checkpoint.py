@@ -23,6 +23,7 @@ Finalisation (rename + pruning) can run on a background thread.
 from __future__ import annotations
 
 import glob
+import contextlib
 import json
 import os
 import re
@@ -143,9 +144,20 @@ class CheckpointManager:
     def finalize_checkpoint(self, tmp_path: str, wait_fn=None) -> str:
         """Publish ``tmp_step_N`` as ``step_N`` (atomic rename) and prune.  With
         ``wait_fn`` (the policy's ``finalize_async_save``: background weight writes
-        still running) the rename happens on a background thread after it returns."""
+        still running) the rename happens on a background thread after it returns.
+        With ``self.telemetry`` set (the loop's recorder) the publication is a
+        ``checkpoint_finalize`` span in the caller's trace."""
+        from rl_b200.utils.telemetry import current_trace_carrier, remote_trace_context
+
+        carrier = current_trace_carrier()  # the finalize thread's spans stay in the caller's trace
+        tele = getattr(self, "telemetry", None)
 
         def work():
+            with remote_trace_context(carrier), (tele.span("checkpoint_finalize") if tele is not None
+                                                 else contextlib.nullcontext()):
+                _publish()
+
+        def _publish():
             if wait_fn is not None:
                 wait_fn()
             step = int(os.path.basename(tmp_path).split("_")[-1])

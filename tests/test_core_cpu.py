@@ -511,9 +511,7 @@ def test_numa_binding_from_fake_sysfs(tmp_path):
 
 
 def test_telemetry_spans_and_goodput(tmp_path):
-    import json as _json
-
-    from rl_b200.utils.telemetry import Telemetry
+    from rl_b200.utils.telemetry import Telemetry, read_otlp_spans
 
     t = Telemetry(str(tmp_path / "spans.jsonl"))
     with t.span("step", step=1):
@@ -522,9 +520,11 @@ def test_telemetry_spans_and_goodput(tmp_path):
     g = t.goodput({"generation": 2.0, "policy_training": 3.0, "weight_sync": 0.5, "total_step_time": 6.0}, 6.0)
     assert abs(g["goodput/fraction"] - 5 / 6) < 1e-9 and abs(g["goodput/idle_s"] - 0.5) < 1e-9
     assert t.flush() == 2
-    recs = [_json.loads(x) for x in open(tmp_path / "spans.jsonl")]
-    assert {r["name"] for r in recs} == {"step", "generation"}
-    assert [r for r in recs if r["name"] == "generation"][0]["parent"] == "step"
+    recs = {r["name"]: r for r in read_otlp_spans(str(tmp_path / "spans.jsonl"))}
+    assert set(recs) == {"step", "generation"}
+    assert recs["generation"]["parentSpanId"] == recs["step"]["spanId"]
+    assert recs["generation"]["traceId"] == recs["step"]["traceId"]
+    assert {"key": "rl.bucket", "value": {"stringValue": "productive"}} in recs["generation"]["attributes"]
 
 
 def test_prev_logprobs_folded_into_training_forward():

@@ -223,22 +223,31 @@ class RolloutEngine:
 
         # ---- prefill (packed prompts) ----
         lens_l = lengths.tolist()
-        flat = torch.cat([input_ids[b, : lens_l[b]].cpu() for b in range(B)])
-        if dev.type == "cuda":
-            flat = flat.pin_memory()  # the step's inputs cross PCIe once, from pinned memory
-        flat = flat.to(dev, non_blocking=True)
-        positions = torch.cat([torch.arange(L, dtype=torch.int32) for L in lens_l]).to(dev)
-        cu = torch.zeros(B + 1, dtype=torch.int32)
-        cu[1:] = torch.cumsum(lengths, 0)
-        cu_d = cu.to(dev)
-        seq_idx = torch.repeat_interleave(torch.arange(B), lengths).to(dev)
-        slot = (block_tables[seq_idx, (positions // bs).long()].long() * bs + (positions % bs).long())
-        last_idx = (cu[1:] - 1).to(dev).long()
         recording = self.record_routes and self.model.cfg.is_moe
         topk_rec = int(self.record_sampler_topk or 0)
+        spec = self._spec_enabled(top_k, top_p) and not recording and not topk_rec
+        mg = cfg.get("mcore_generation_config") or {}
+        # identical prompts (a GRPO group's samples) are prefilled once; their KV
+        # blocks are copied to the other rows of the group
+        dedup = bool(mg.get("enable_prefix_caching", True)) and not recording
+        # prefill in passes of at most max_tokens tokens (whole sequences), which
+        # bounds the prefill activations; not under expert parallelism, whose
+        # collectives need the same pass count on every rank
+        ep = getattr(getattr(self.model, "ps", None), "ep_size", 1)
+        chunk_tokens = int(mg.get("max_tokens", 16384)) if (mg.get("enable_chunked_prefill", True)
+                                                             and not recording and ep <= 1) else 0
+        rep, inv = self._unique_prompts(input_ids, lens_l) if dedup else (list(range(B)), list(range(B)))
         if recording:
             self.model.router_record = {}
-        h = self.model.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.kv, slot, last_idx)
+        h_parts = []
+        for rows in self._prefill_passes(rep, lens_l, chunk_tokens):
+            h_parts.append(self._prefill_rows(input_ids, rows, lens_l, block_tables, spec))
+        h = torch.cat(h_parts) if len(h_parts) > 1 else h_parts[0]
+        if len(rep) < B:
+            self._copy_prompt_blocks(rep, inv, lens_l, block_tables, spec)
+            h = h[torch.tensor(inv, device=h.device)]
+        self.stats_last_prefill = {"prompts": B, "prefilled": len(rep), "passes": len(h_parts),
+                                   "tokens": int(sum(lens_l[r] for r in rep))}
         prefill_routes = self._take_routes() if recording else None
         self._route_steps = [] if recording else None
         logits = self.model.logits_infer(h)
@@ -260,8 +269,7 @@ class RolloutEngine:
                                                               temperature, top_k, top_p, stop_ids, gen, eager=True)
             finally:
                 self.model.router_record = None
-        elif self._spec_enabled(top_k, top_p):
-            self.draft.forward_prefill(flat, positions, cu_d, int(lengths.max()), self.draft_kv, slot, last_idx)
+        elif spec:
             tokens_all, lps_all, glen = self._spec_decode_loop(tok0, lp0, lengths.to(dev), block_tables, max_new,
                                                                temperature, stop_ids)
         else:
@@ -291,6 +299,85 @@ class RolloutEngine:
             out["sampler_topk_token_ids"], out["sampler_topk_logprobs"] = ids, lps
             self._topk_steps = None
         return out
+
+    @staticmethod
+    def _unique_prompts(input_ids: torch.Tensor, lens: list) -> tuple[list[int], list[int]]:
+        """(first row of each distinct prompt, for every row the index of its
+        prompt in that list)."""
+        seen: dict = {}
+        rep, inv = [], []
+        ids = input_ids.cpu()
+        for b, L in enumerate(lens):
+            key = (L, ids[b, :L].numpy().tobytes())
+            if key not in seen:
+                seen[key] = len(rep)
+                rep.append(b)
+            inv.append(seen[key])
+        return rep, inv
+
+    @staticmethod
+    def _prefill_passes(rows: list[int], lens: list, max_tokens: int) -> list[list[int]]:
+        """Consecutive runs of ``rows`` of at most ``max_tokens`` prompt tokens (a
+        longer prompt runs alone); one pass when ``max_tokens`` is 0."""
+        if max_tokens <= 0:
+            return [rows]
+        out, cur, n = [], [], 0
+        for r in rows:
+            if cur and n + lens[r] > max_tokens:
+                out.append(cur)
+                cur, n = [], 0
+            cur.append(r)
+            n += lens[r]
+        if cur:
+            out.append(cur)
+        return out
+
+    def _prefill_rows(self, input_ids: torch.Tensor, rows: list[int], lens: list, block_tables: torch.Tensor,
+                      spec: bool) -> torch.Tensor:
+        """Prefill the prompts of ``rows`` into their KV blocks; returns the last
+        position's hidden state of each, ``[len(rows), H]``."""
+        dev = self.device
+        bs = self.block_size
+        rl = [lens[r] for r in rows]
+        flat = torch.cat([input_ids[r, :L].cpu() for r, L in zip(rows, rl)])
+        if dev.type == "cuda":
+            flat = flat.pin_memory()  # the step's inputs cross PCIe once, from pinned memory
+        flat = flat.to(dev, non_blocking=True)
+        positions = torch.cat([torch.arange(L, dtype=torch.int32) for L in rl]).to(dev)
+        cu = torch.zeros(len(rows) + 1, dtype=torch.int32)
+        cu[1:] = torch.cumsum(torch.tensor(rl), 0)
+        cu_d = cu.to(dev)
+        seq_row = torch.repeat_interleave(torch.tensor(rows), torch.tensor(rl)).to(dev)
+        slot = (block_tables[seq_row, (positions // bs).long()].long() * bs + (positions % bs).long())
+        last_idx = (cu[1:] - 1).to(dev).long()
+        h = self.model.forward_prefill(flat, positions, cu_d, max(rl), self.kv, slot, last_idx)
+        if spec:
+            self.draft.forward_prefill(flat, positions, cu_d, max(rl), self.draft_kv, slot, last_idx)
+        return h
+
+    def _copy_prompt_blocks(self, rep: list[int], inv: list[int], lens: list, block_tables: torch.Tensor,
+                            spec: bool) -> None:
+        """Give every duplicate row the KV blocks of its prompt's prefilled row."""
+        bs = self.block_size
+        src, dst = [], []
+        for b, u in enumerate(inv):
+            r = rep[u]
+            if r == b:
+                continue
+            nb = -(-lens[b] // bs)
+            src.append(block_tables[r, :nb])
+            dst.append(block_tables[b, :nb])
+        if not src:
+            return
+        src_t, dst_t = torch.cat(src).long(), torch.cat(dst).long()
+        for cache in ([self.kv, self.draft_kv] if spec else [self.kv]):
+            st = cache.storage
+            if st.element_size() == 1:
+                st = st.view(torch.uint8)  # fp8 caches: copy the bytes
+            for layer in range(st.shape[0]):  # per layer: the gathered blocks stay small
+                for kv in range(2):
+                    t = st[layer, kv]
+                    t.index_copy_(0, dst_t, t.index_select(0, src_t))
 
     @staticmethod
     def _sampler_topk(logits: torch.Tensor, temperature: float, k: int):

@@ -193,3 +193,30 @@ def test_offload_to_cpu_and_back(cuda_device):
     data = make_batch(B=8, S=24, vocab=SMALL.vocab_size, seed=0)
     res = w.train(data, ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}), gbs=8)
     assert res["grad_norm"] > 0 and not torch.equal(w.model.flat_param, before)
+
+
+def test_prompt_dedup_and_chunked_prefill_on_gpu(cuda_device):
+    """Identical prompts prefilled once (KV blocks copied to the other rows) and
+    prefill in several passes: the greedy rollout's first-token log-probs match a
+    plain prefill's, and the rollouts agree."""
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import single_process_state
+
+    def worker(mg):
+        cfg = _policy_cfg()
+        cfg["generation"]["mcore_generation_config"].update(mg)
+        return PolicyWorker(cfg, model_cfg=SMALL, pstate=single_process_state(cuda_device), seed=5)
+
+    g = torch.Generator().manual_seed(0)
+    lens = torch.tensor([9, 40, 77, 31]).repeat_interleave(4)
+    ids = torch.randint(0, SMALL.vocab_size, (4, 80), generator=g).repeat_interleave(4, 0)
+    data = BatchedDataDict({"input_ids": ids, "input_lengths": lens})
+    ref = worker({"enable_prefix_caching": False, "enable_chunked_prefill": False}).generate(data, greedy=True)
+    w = worker({"enable_prefix_caching": True, "enable_chunked_prefill": True, "max_tokens": 64})
+    out = w.generate(data, greedy=True)
+    assert w.engine.stats_last_prefill["prefilled"] == 4 and w.engine.stats_last_prefill["passes"] == 4
+    first = torch.stack([out["logprobs"][b, int(lens[b])] for b in range(16)])
+    first_ref = torch.stack([ref["logprobs"][b, int(lens[b])] for b in range(16)])
+    assert (first - first_ref).abs().max() < 5e-2
+    same = (out["output_ids"] == ref["output_ids"]).float().mean()
+    assert same > 0.9, same

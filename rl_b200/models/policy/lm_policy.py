@@ -139,6 +139,19 @@ class Policy:
     def offload_after_refit(self) -> None:
         self.worker.offload_after_refit()
 
+    @property
+    def sharding_annotations(self):
+        """``NamedSharding`` of the process grid (pipeline, data, context, tensor axes)."""
+        from rl_b200.distributed.named_sharding import from_parallel_state
+
+        return from_parallel_state(self.worker.ps)
+
+    def recreate_worker(self, worker_idx: int = 0) -> None:
+        """Rebuild this rank's rollout engine (the generation shard) in place and
+        re-synchronise its weights; ``worker_idx`` is accepted for the reference's
+        signature (one engine per rank here)."""
+        self.worker.recreate_generation_engine()
+
     def offload_to_cpu(self) -> None:
         self.worker.offload_to_cpu()
 

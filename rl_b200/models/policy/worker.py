@@ -214,13 +214,15 @@ class PolicyWorker:
                                            dtype=self.dtype, skip_init=True)
         self.weight_sync = self._make_weight_sync(resharded)
         kv_dt = str(vcfg.get("kv_cache_dtype", gen_cfg.get("kv_cache_dtype", "auto"))).lower()
-        self.engine = RolloutEngine(
-            self.gen_model, gen_cfg, max_num_seqs=int(gen_cfg.get("max_num_seqs", 256)),
+        self._engine_spec = dict(
+            max_num_seqs=int(gen_cfg.get("max_num_seqs", 256)),
             kv_dtype=torch.float8_e4m3fn if kv_dt in ("fp8", "fp8_e4m3") else None,
             max_model_len=self.max_seq_len, block_size=int(mgc.get("block_size_tokens", 256)),
             use_cuda_graphs=bool(gen_cfg.get("use_cuda_graphs", True)),
             seed=seed * 7 + self.ps.dp_rank * 100003,
         )
+        self._gen_cfg = gen_cfg
+        self.engine = RolloutEngine(self.gen_model, gen_cfg, **self._engine_spec)
         # speculative decoding: a small draft LM (same vocab / width, few layers) that
         # proposes tokens for the rollout engine and is trained online on rollouts
         spec = gen_cfg.get("speculative") or {}
@@ -1209,6 +1211,27 @@ class PolicyWorker:
 
     def offload_after_refit(self) -> None:
         """See ``offload_before_refit``."""
+
+    def recreate_generation_engine(self) -> None:
+        """Replace the rollout engine with a fresh one built from the same
+        settings (the counterpart of the reference's ``recreate_worker`` for a
+        dead generation shard): the old engine's graphs and KV cache are dropped,
+        the new one gets the draft model and fp8-KV scales back, and the rollout
+        weights are re-synchronised before it serves."""
+        old = self.engine
+        try:
+            old.finish_generation()
+            old._drop_graphs()
+        except Exception:  # noqa: BLE001 - the engine being replaced may be broken
+            pass
+        self.engine = RolloutEngine(self.gen_model, self._gen_cfg, **self._engine_spec)
+        for attr in ("kv_scales", "capture_error_mode", "record_routes", "record_sampler_topk"):
+            if hasattr(old, attr):
+                setattr(self.engine, attr, getattr(old, attr))
+        if self.draft is not None:
+            self.engine.set_draft(self.draft, int((self._gen_cfg.get("speculative") or {})["num_speculative_tokens"]))
+        self.engine_incarnation = getattr(self, "engine_incarnation", 0) + 1
+        self.refit()
 
     # ------------------------------------------------ async checkpoint saves
     def finalize_async_save(self) -> None:

@@ -75,3 +75,35 @@ def test_selector_least_inflight_and_supervisor_restarts():
     sup.join()
     assert f.state_of(2) == ShardState.STALE and sup.restarts_ok == 1 and calls == [2, 2]
     assert 2 not in f.serving_shards()
+
+
+def test_supervisor_recreates_a_dead_engine_through_the_policy():
+    """A generation shard reported dead is rebuilt by the supervisor through
+    ``Policy.recreate_worker``: the new engine serves the same greedy rollouts
+    and the shard returns to serving after the refit."""
+    import torch
+
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.generation.fleet_health import EngineSupervisor, GenerationFleetHealth, ShardState
+    from rl_b200.models.policy.lm_policy import Policy
+    from rl_b200.models.policy.worker import PolicyWorker
+
+    pcfg = {"max_total_sequence_length": 48, "precision": "float32", "train_global_batch_size": 4,
+            "generation": {"temperature": 1.0, "max_new_tokens": 6}}
+    pol = Policy(PolicyWorker(pcfg, model_cfg=get_model_config("tiny-llama"), seed=2))
+    data = BatchedDataDict({"input_ids": torch.randint(0, 512, (4, 10), generator=torch.Generator().manual_seed(1)),
+                            "input_lengths": torch.tensor([10, 7, 9, 3])})
+    before = pol.generate(data, greedy=True)["output_ids"]
+    old = pol.worker.engine
+    fleet = GenerationFleetHealth(1)
+    sup = EngineSupervisor(fleet, lambda i: pol.recreate_worker(i))
+    fleet.record_death(0, "engine crashed")
+    sup.tick()
+    sup.join()
+    assert pol.worker.engine is not old and pol.worker.engine_incarnation == 1
+    assert sup.restarts_ok == 1 and fleet.state_of(0) != ShardState.DEAD
+    fleet.report_refit(0, fleet.trainer_version if hasattr(fleet, "trainer_version") else 0)
+    after = pol.generate(data, greedy=True)["output_ids"]
+    assert torch.equal(before, after)
+    assert pol.sharding_annotations.get_axis_size("data_parallel") == 1

@@ -62,7 +62,28 @@ def parse():
     p.add_argument("--mb-tokens", type=int, default=16384)
     p.add_argument("--kl", type=float, default=0.01)
     p.add_argument("--layers", type=int, default=0, help="debug only: override layer count (invalid for scoring)")
-    return p.parse_args()
+    p.add_argument("--preset", default="llama8b", choices=sorted(PRESETS),
+                   help="llama8b: the headline config (BASELINE config 2); qwen30b_a3b_ep8: config 3 "
+                        "(MoE, EP over all GPUs); qwen32b_fp8_tp4: config 5 (block-scaled fp8 training and "
+                        "rollout, fp8 KV cache, 2-token draft)")
+    args = p.parse_args()
+    pre = PRESETS[args.preset]
+    for k, v in pre.get("args", {}).items():  # a preset fills the arguments left at their defaults
+        if getattr(args, k) == p.get_default(k):
+            setattr(args, k, v)
+    return args
+
+
+# Per-GPU work of the reference's benchmark configs (weak scaling: prompts scale with N).
+PRESETS = {
+    "llama8b": {"model_label": "Llama-3.1-8B-shape", "args": {}},
+    "qwen30b_a3b_ep8": {"model_label": "Qwen3-30B-A3B-shape", "ep": "all", "tp": 1,
+                        "args": {"model": "qwen3-30b-a3b", "prompts_per_gpu": 4, "generations": 16,
+                                 "min_prompt": 256, "max_prompt": 256, "max_new": 2048, "act_ckpt": 1}},
+    "qwen32b_fp8_tp4": {"model_label": "Qwen3-32B-shape fp8", "tp": 4, "fp8": True,
+                        "args": {"model": "qwen3-32b", "prompts_per_gpu": 4, "generations": 8,
+                                 "min_prompt": 512, "max_prompt": 512, "max_new": 4096, "act_ckpt": 1}},
+}
 
 
 def reference_arm(args) -> None:
@@ -171,8 +192,11 @@ def main():
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if world != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
-    tp = args.tp or (2 if args.gpus >= 2 else 1)
-    ps = init_distributed(tp=tp, timeout_s=900)
+    pre = PRESETS[args.preset]
+    tp = args.tp or pre.get("tp") or (2 if args.gpus >= 2 else 1)
+    tp = min(tp, args.gpus)
+    ep = args.gpus // tp if pre.get("ep") == "all" else 1
+    ps = init_distributed(tp=tp, ep=ep, timeout_s=900)
     dev = ps.device
     if not _ext.has_ext():
         raise SystemExit(f"native extension not loaded: {_ext._ERR!r}")
@@ -188,10 +212,17 @@ def main():
         "logprob_chunk_size": 4096, "max_grad_norm": 1.0,
         "optimizer": {"name": "torch.optim.AdamW",
                       "kwargs": {"lr": 3e-7, "weight_decay": 0.01, "betas": [0.9, 0.999], "eps": 1e-8}},
-        "megatron_cfg": {"activation_checkpointing": (tp < 2) if args.act_ckpt < 0 else bool(args.act_ckpt), "sequence_parallel": (tp > 1) if args.sp < 0 else bool(args.sp)},
+        "megatron_cfg": {"activation_checkpointing": (tp < 2) if args.act_ckpt < 0 else bool(args.act_ckpt),
+                         "sequence_parallel": (tp > 1) if args.sp < 0 else bool(args.sp),
+                         "expert_model_parallel_size": ep,
+                         **({"fp8_cfg": {"enabled": True, "fp8": "e4m3", "fp8_recipe": "blockwise"}}
+                            if pre.get("fp8") else {})},
         "generation": {"temperature": 1.0, "top_p": 1.0, "top_k": None, "max_new_tokens": args.max_new,
                        "max_num_seqs": 512, "mcore_generation_config": {"block_size_tokens": 256},
-                       "tensor_parallel_size": args.gen_tp or tp},
+                       "tensor_parallel_size": args.gen_tp or tp,
+                       **({"vllm_cfg": {"precision": "fp8", "kv_cache_dtype": "fp8"},
+                           "speculative": {"num_speculative_tokens": 2, "draft_num_layers": 1}}
+                          if pre.get("fp8") else {})},
         "sequence_packing": {"train_mb_tokens": args.mb_tokens, "logprob_mb_tokens": args.mb_tokens * 2},
     }
     cfg = {
@@ -251,11 +282,13 @@ def main():
             "metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "n_gpus": args.gpus,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(dev_s / args.steps * 1e3, 2),
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
-            "data": "synthetic prompts (uniform token ids, lengths U[128,512]), random-init weights, "
+            "data": f"synthetic prompts (uniform token ids, lengths U[{args.min_prompt},{args.max_prompt}]), "
+                    "random-init weights, "
                     "seeded-hash reward",
-            "config": {"model": "Llama-3.1-8B-shape" + ("" if not args.layers else f" ({args.layers} layers: INVALID)"),
+            "config": {"model": pre["model_label"] + ("" if not args.layers else f" ({args.layers} layers: INVALID)"),
                        "global_batch": prompts_global * G, "seq_len": max_len,
-                       "parallelism": f"tp{tp}dp{ps.dp_size}", "rollout_tp": args.gen_tp or tp,
+                       "parallelism": f"tp{tp}dp{ps.dp_size}" + (f"ep{ep}" if ep > 1 else ""),
+                       "rollout_tp": args.gen_tp or tp, "preset": args.preset,
                        "activation_checkpointing": pcfg["megatron_cfg"]["activation_checkpointing"], "prompts_per_step": prompts_global,
                        "generations_per_prompt": G, "max_new_tokens": args.max_new, "kl_penalty": args.kl,
                        "l2": "working set (16 GB bf16 weights + KV cache) far above the 126 MB L2; no flush needed",

@@ -82,6 +82,20 @@ def load_safetensors(path: str, names: Optional[Iterable[str]] = None) -> dict[s
 def _gather_full(model, sp, t: torch.Tensor) -> torch.Tensor:
     """Reassemble a TP / EP shard into the full tensor (collective on the group)."""
     ps = model.ps
+    if sp.ep_dim is not None and sp.tp_dim is not None and ps.tp_size > 1:
+        # split experts: TP slices of the FFN first, then the expert shards
+        parts = [torch.empty_like(t) for _ in range(ps.tp_size)]
+        dist.all_gather(parts, t.contiguous(), group=ps.tp_group)
+        if sp.name.endswith("mlp.experts.gate_up_proj"):
+            gs, us = zip(*[p.chunk(2, 1) for p in parts])
+            t = torch.cat(list(gs) + list(us), 1)
+        else:
+            t = torch.cat(parts, sp.tp_dim)
+        if ps.ep_size > 1:
+            parts = [torch.empty_like(t) for _ in range(ps.ep_size)]
+            dist.all_gather(parts, t.contiguous(), group=ps.ep_group)
+            t = torch.cat(parts, sp.ep_dim)
+        return t
     if sp.tp_dim is not None and ps.tp_size > 1:
         parts = [torch.empty_like(t) for _ in range(ps.tp_size)]
         dist.all_gather(parts, t.contiguous(), group=ps.tp_group)
@@ -159,11 +173,7 @@ def load_hf_state_dict(model, sd: dict[str, torch.Tensor]) -> None:
                 full = sd["model.embed_tokens.weight"]
             else:
                 full = sd[name]
-            if sp.tp_dim is not None and ps.tp_size > 1:
-                full = model.shard_full_tensor(sp, full, ps.tp_rank, ps.tp_size)
-            elif sp.ep_dim is not None and ps.ep_size > 1:
-                full = model.shard_full_tensor(sp, full, ps.ep_rank, ps.ep_size)
-            p.copy_(full.to(p.dtype).view(sp.shape))
+            p.copy_(model.shard_param(sp, full).to(p.dtype).view(sp.shape))
 
 
 def save_hf_checkpoint(model, path: str, max_shard_bytes: int = 5 << 30) -> None:

@@ -129,12 +129,23 @@ class _ParamMap:
         name = sp.name
         runs: list[tuple[int, int, tuple, int]] = []  # (local row, rows, leading offsets, global row)
         if sp.ep_dim is not None:
-            # experts [E_local, R_e, C]: leading expert index offset by this rank's first expert
+            # experts [E_local, R_e, C]: leading expert index offset by this rank's first expert;
+            # split experts (tp_dim set) hold FFN slices: gate / up row blocks or a column block
             e_local, r_e = shape[0], shape[1]
             e0 = ps.ep_rank * e_local if ps.ep_size > 1 else 0
-            body = (c.num_experts, r_e, self.C)
-            for e in range(e_local):
-                runs.append((e * r_e, r_e, lead + (e0 + e,), 0))
+            split = sp.tp_dim is not None and tp > 1
+            if split and sp.tp_dim == 1:  # gate_up [E, gate | up, H]
+                f_l = r_e // 2
+                body = (c.num_experts, 2 * f_l * tp, self.C)
+                for e in range(e_local):
+                    runs.append((e * r_e, f_l, lead + (e0 + e,), t * f_l))
+                    runs.append((e * r_e + f_l, f_l, lead + (e0 + e,), f_l * tp + t * f_l))
+            else:
+                if split:  # down [E, H, F]: this rank's FFN columns
+                    self.col0 = t * self.C
+                body = (c.num_experts, r_e, self.C * (tp if split else 1))
+                for e in range(e_local):
+                    runs.append((e * r_e, r_e, lead + (e0 + e,), 0))
             gshape = lead_shape + body
         elif name.endswith(("qkv_proj.weight", "qkv_proj.bias")):
             hd = c.head_dim

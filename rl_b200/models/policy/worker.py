@@ -140,7 +140,9 @@ class PolicyWorker:
         flat_alloc = self.symmetric.flat_alloc if self.symmetric is not None else None
         self.model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype, seed=seed,
                                    sequence_parallel=self.sequence_parallel, activation_checkpointing=act_ckpt,
-                                   num_labels=self.num_labels, flat_alloc=flat_alloc)
+                                   num_labels=self.num_labels, flat_alloc=flat_alloc,
+                                   expert_tensor_parallel=mc.get("expert_tensor_parallel_size"))
+        etp = self.model.etp
         f8 = mc.get("fp8_cfg") or {}
         if f8.get("enabled", False):
             if str(f8.get("fp8", "e4m3")).lower() != "e4m3" or \
@@ -198,7 +200,7 @@ class PolicyWorker:
         if self.lora is not None:
             # rollout copy with the adapters merged in (same TP layout)
             self.gen_model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype,
-                                           skip_init=True)
+                                           skip_init=True, expert_tensor_parallel=etp)
         elif self.pp > 1:
             # rollout runs the whole depth on every stage's GPU (same TP layout);
             # the refit gathers the other stages' layers over the pipeline group
@@ -206,7 +208,7 @@ class PolicyWorker:
 
             gps = dataclasses.replace(self.ps, pp_size=1, pp_rank=0, pp_group=None, pp_ranks=[self.ps.rank])
             self.gen_model = TransformerLM(self.model_cfg, gps, device=self.device, dtype=self.dtype,
-                                           skip_init=True)
+                                           skip_init=True, expert_tensor_parallel=etp)
         elif resharded:
             from rl_b200.parallel.state import single_process_state
 

@@ -179,10 +179,15 @@ class TransformerLM(nn.Module):
     def __init__(self, cfg: ModelConfig, pstate: Optional[ParallelState] = None, device=None,
                  dtype: torch.dtype = torch.bfloat16, seed: int = 0, sequence_parallel: bool = False,
                  activation_checkpointing: bool = False, init_std: float = 0.02, num_labels: int = 0,
-                 flat_alloc: Optional[Callable[[int, torch.dtype], torch.Tensor]] = None, skip_init: bool = False):
+                 flat_alloc: Optional[Callable[[int, torch.dtype], torch.Tensor]] = None, skip_init: bool = False,
+                 expert_tensor_parallel: Optional[int] = None):
         """``flat_alloc(numel, dtype)`` supplies the flat parameter buffer (e.g. a
         view of symmetric memory that TP peers can read over NVLink);
-        ``skip_init`` leaves the weights unset (a rollout copy filled by refit)."""
+        ``skip_init`` leaves the weights unset (a rollout copy filled by refit);
+        ``expert_tensor_parallel`` (Megatron's ``expert_tensor_parallel_size``):
+        1 keeps every expert whole on each TP rank, the TP size splits each
+        expert's FFN over the TP group (column-parallel gate / up, row-parallel
+        down); default: split when sequence parallelism is on (required then)."""
         super().__init__()
         self._flat_alloc = flat_alloc
         self._skip_init = skip_init
@@ -203,11 +208,23 @@ class TransformerLM(nn.Module):
         self.hd = cfg.head_dim
         self.vocab_local = cfg.vocab_size // tp
         self.vocab_start = self.ps.tp_rank * self.vocab_local
+        self.etp = 1
         if cfg.is_moe:
             if cfg.num_experts % ep:
                 raise ValueError(f"experts {cfg.num_experts} must divide by ep={ep}")
             self.experts_local = cfg.num_experts // ep
             self.expert_start = self.ps.ep_rank * self.experts_local
+            etp = int(expert_tensor_parallel) if expert_tensor_parallel else (tp if self.sequence_parallel else 1)
+            if etp not in (1, tp):
+                raise ValueError(f"expert_tensor_parallel_size {etp} must be 1 or the TP size {tp}")
+            if self.sequence_parallel and etp != tp:
+                # each TP rank would run whole experts on the gathered tokens, and the
+                # sequence-parallel reduce-scatter would add their identical outputs
+                raise NotImplementedError("MoE under sequence parallelism needs expert_tensor_parallel_size == "
+                                          "tensor_model_parallel_size")
+            if cfg.moe_ffn_hidden_size % etp:
+                raise ValueError(f"expert ffn {cfg.moe_ffn_hidden_size} must divide by etp={etp}")
+            self.etp = etp
         else:
             if cfg.ffn_hidden_size % tp:
                 raise ValueError(f"ffn {cfg.ffn_hidden_size} must divide by tp={tp}")
@@ -292,10 +309,16 @@ class TransformerLM(nn.Module):
             s.append(ParamSpec(p + "self_attn.o_proj.weight", (H, self.nq * hd), "normal_out", tp_dim=1))
             s.append(ParamSpec(p + "post_attention_layernorm.weight", (H,), "ones", no_weight_decay=True))
             if c.is_moe:
-                F = c.moe_ffn_hidden_size
-                s.append(ParamSpec(p + "mlp.gate.weight", (c.num_experts, H), "normal"))
-                s.append(ParamSpec(p + "mlp.experts.gate_up_proj", (self.experts_local, 2 * F, H), "normal", ep_dim=0))
-                s.append(ParamSpec(p + "mlp.experts.down_proj", (self.experts_local, H, F), "normal_out", ep_dim=0))
+                F = c.moe_ffn_hidden_size // self.etp
+                split = self.etp > 1
+                # with split experts the router's gradient is a per-TP-rank partial sum
+                # (each rank scores its FFN slice); without SP nothing else adds it up
+                s.append(ParamSpec(p + "mlp.gate.weight", (c.num_experts, H), "normal",
+                                   grad_reduce="tp_sum" if split and not self.sequence_parallel else None))
+                s.append(ParamSpec(p + "mlp.experts.gate_up_proj", (self.experts_local, 2 * F, H), "normal", ep_dim=0,
+                                   tp_dim=1 if split else None))
+                s.append(ParamSpec(p + "mlp.experts.down_proj", (self.experts_local, H, F), "normal_out", ep_dim=0,
+                                   tp_dim=2 if split else None))
             else:
                 s.append(ParamSpec(p + "mlp.gate_up_proj.weight", (2 * self.ffn_local, H), "normal", tp_dim=0))
                 s.append(ParamSpec(p + "mlp.down_proj.weight", (H, self.ffn_local), "normal_out", tp_dim=1))
@@ -353,21 +376,29 @@ class TransformerLM(nn.Module):
                 view.zero_()
             else:
                 s = std if sp.init == "normal" else out_std
-                full_shape = list(sp.shape)
-                shard_idx, shard_dim, n_shards = 0, None, 1
-                if sp.tp_dim is not None and self.ps.tp_size > 1:
-                    shard_dim, n_shards, shard_idx = sp.tp_dim, self.ps.tp_size, self.ps.tp_rank
-                elif sp.ep_dim is not None and self.ps.ep_size > 1:
-                    shard_dim, n_shards, shard_idx = sp.ep_dim, self.ps.ep_size, self.ps.ep_rank
-                if shard_dim is not None:
-                    full_shape[shard_dim] *= n_shards
-                full = torch.randn(full_shape, generator=gen, dtype=torch.float32, device=self.device) * s
-                if shard_dim is not None:
-                    full = self.shard_full_tensor(sp, full, shard_idx, n_shards)
-                view.copy_(full.to(self.dtype))
+                full = torch.randn(self.full_shape(sp), generator=gen, dtype=torch.float32, device=self.device) * s
+                view.copy_(self.shard_param(sp, full).to(self.dtype))
             p = nn.Parameter(view, requires_grad=True)
             self._params[sp.name] = p
             self.register_parameter(sp.name.replace(".", "__"), p)
+
+    def full_shape(self, sp: ParamSpec) -> list:
+        """Shape of the whole (unsharded) tensor of ``sp``."""
+        shape = list(sp.shape)
+        if sp.ep_dim is not None and self.ps.ep_size > 1:
+            shape[sp.ep_dim] *= self.ps.ep_size
+        if sp.tp_dim is not None and self.ps.tp_size > 1:
+            shape[sp.tp_dim] *= self.ps.tp_size
+        return shape
+
+    def shard_param(self, sp: ParamSpec, full: torch.Tensor) -> torch.Tensor:
+        """This rank's shard of the whole tensor of ``sp`` (expert slice first, then
+        the tensor-parallel slice)."""
+        if sp.ep_dim is not None and self.ps.ep_size > 1:
+            full = full.chunk(self.ps.ep_size, sp.ep_dim)[self.ps.ep_rank]
+        if sp.tp_dim is not None and self.ps.tp_size > 1:
+            full = self.shard_full_tensor(sp, full, self.ps.tp_rank, self.ps.tp_size)
+        return full
 
     def shard_full_tensor(self, sp: ParamSpec, full: torch.Tensor, idx: int, n: int) -> torch.Tensor:
         """Slice a full (unsharded) tensor into this rank's shard, honouring the
@@ -381,6 +412,9 @@ class TransformerLM(nn.Module):
         if sp.name.endswith("gate_up_proj.weight"):
             g, u = full.chunk(2, 0)
             return torch.cat([g.chunk(n, 0)[idx], u.chunk(n, 0)[idx]], 0)
+        if sp.name.endswith("mlp.experts.gate_up_proj") and sp.tp_dim is not None:
+            g, u = full.chunk(2, 1)  # [E, gate | up, H]: each TP rank takes matching FFN columns of both
+            return torch.cat([g.chunk(n, 1)[idx], u.chunk(n, 1)[idx]], 1)
         dim = sp.tp_dim if sp.tp_dim is not None else sp.ep_dim
         return full.chunk(n, dim)[idx]
 
@@ -628,8 +662,11 @@ class TransformerLM(nn.Module):
     def _moe_block(self, i: int, h: torch.Tensor) -> torch.Tensor:
         c = self.cfg
         p = f"model.layers.{i}."
+        split = self.etp > 1  # experts' FFN split over TP: every rank adds a partial output
         if self.sequence_parallel:
             h = gather_from_sp(h, self.ps.tp_group)
+        elif split:
+            h = copy_to_tp(h, self.ps.tp_group)  # backward: the partial input gradients are summed
         T, H = h.shape
         k, E = c.moe_top_k, c.num_experts
         weights, ids, probs = self.route(i, h)
@@ -639,7 +676,10 @@ class TransformerLM(nn.Module):
                 0, ids.reshape(-1), torch.ones(T * k, device=h.device))
             f = counts / max(1, T * k)
             aux = E * (f.detach() * probs.mean(0)).sum() * c.moe_aux_loss_coef
-            h = _AuxLossScaler.apply(h, aux, self.aux_loss_scale if self.aux_loss_scale else 1.0)
+            # split experts: every TP rank holds the same aux loss, whose gradients the
+            # TP reductions add up, so each contributes 1 / tp of it
+            scale = (self.aux_loss_scale if self.aux_loss_scale else 1.0) / (self.ps.tp_size if split else 1)
+            h = _AuxLossScaler.apply(h, aux, scale)
             self._aux_losses.append(aux.detach())
         wgu = self._params[p + "mlp.experts.gate_up_proj"]
         wdn = self._params[p + "mlp.experts.down_proj"]
@@ -647,6 +687,8 @@ class TransformerLM(nn.Module):
             out = self._moe_ep_fused(h, ids, weights, wgu, wdn)
             if self.sequence_parallel:
                 out = reduce_scatter_to_sp(out, self.ps.tp_group)
+            elif split:
+                out = reduce_from_tp(out, self.ps.tp_group)
             return out
         flat_ids = ids.reshape(-1)
         order = torch.argsort(flat_ids, stable=True)
@@ -662,6 +704,8 @@ class TransformerLM(nn.Module):
         out = torch.zeros(T, H, dtype=ys.dtype, device=h.device).index_add_(0, token_of, ys * wflat)
         if self.sequence_parallel:
             out = reduce_scatter_to_sp(out, self.ps.tp_group)
+        elif split:
+            out = reduce_from_tp(out, self.ps.tp_group)
         return out
 
     def _moe_ep_fused(self, h, ids, weights, wgu, wdn):

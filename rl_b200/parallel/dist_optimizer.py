@@ -183,7 +183,9 @@ class FlatAdamW:
                         seg.muon_params.append((sp, a - seg.s_lo, b - seg.s_lo))
                     else:
                         wd_r.append((a - seg.s_lo, b - seg.s_lo, not sp.no_weight_decay))
-                    rep_r.append((a - seg.s_lo, b - seg.s_lo, sp.tp_dim is None and sp.ep_dim is None))
+                    # replicated over TP (every TP rank holds the same values): counted once
+                    # in the norm; whole experts without an FFN split are replicated too
+                    rep_r.append((a - seg.s_lo, b - seg.s_lo, sp.tp_dim is None))
             seg.wd_ranges = _merge(wd_r)
             seg.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
             nd = [(a, b) for a, b, d in seg.wd_ranges if not d]

@@ -220,7 +220,8 @@ def case_torch_dist(rank: int, tp: int, ep: int, moe: bool, path: str, mode: str
     torch.manual_seed(0)
     ps = init_distributed(tp=tp, ep=ep, backend="gloo")
     cfg = TINY_MOE if moe else TINY
-    w = PolicyWorker(_pcfg(False), model_cfg=cfg, pstate=ps, seed=3 if mode == "save" else 11)
+    # MoE under TP runs with sequence parallelism, i.e. experts' FFN split over TP
+    w = PolicyWorker(_pcfg(moe and tp > 1), model_cfg=cfg, pstate=ps, seed=3 if mode == "save" else 11)
     loss = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
 
     def step(seed):

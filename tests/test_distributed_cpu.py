@@ -34,6 +34,18 @@ def test_dense_parallel_matches_single(dense_single, world, tp, sp):
         _close(o, dense_single)
 
 
+@pytest.mark.parametrize("world,tp,ep,sp,extra", [
+    (2, 2, 1, True, None),                                   # SP: experts' FFN split over TP (ETP = TP)
+    (2, 2, 1, False, {"expert_tensor_parallel_size": 2}),   # ETP without SP
+    (2, 2, 1, False, None),                                  # whole experts replicated over TP
+    (4, 2, 2, True, None),                                   # ETP x EP
+])
+def test_moe_expert_tensor_parallel_matches_single(moe_single, world, tp, ep, sp, extra):
+    outs = spawn_ranks(case_train_step, world, tp, ep, sp, True, 1, 1, None, extra)
+    for o in outs:
+        _close(o, moe_single)
+
+
 def test_moe_expert_parallel_matches_single(moe_single):
     outs = spawn_ranks(case_train_step, 2, 1, 2, False, True)
     for o in outs:
@@ -185,6 +197,7 @@ def test_dist_checkpoint_across_virtual_pipeline_settings(tmp_path):
 @pytest.mark.parametrize("moe,save,loads", [
     (False, (2, 2, 1), [(1, 1, 1), (2, 1, 1), (4, 2, 1)]),   # (world, tp, ep): TP=2 -> 1 GPU, DP=2, TP2 x DP2
     (True, (2, 1, 2), [(1, 1, 1), (2, 2, 1)]),               # EP=2 -> 1 GPU, TP=2
+    (True, (4, 2, 2), [(1, 1, 1), (2, 1, 2)]),               # TP2 x EP2 with split experts -> 1 GPU, EP2
 ])
 def test_torch_dist_checkpoint_relayout(tmp_path, moe, save, loads):
     """A Megatron torch_dist checkpoint (DCP shards under Megatron names, optimizer

@@ -288,6 +288,9 @@ class TransformerLM(nn.Module):
         self.kv_amax: Optional[dict] = None  # layer -> (k amax, v amax) while calibrating
         self.weight_version = 0
         self._fp8_cache: dict = {}
+        # hidden-state capture (Eagle3 draft features): layer -> residual stream after it
+        self.capture_layers: Optional[tuple] = None
+        self.captured: Optional[dict] = None
 
     # ------------------------------------------------------------------ params
     def _make_specs(self) -> list[ParamSpec]:
@@ -802,6 +805,7 @@ class TransformerLM(nn.Module):
                                                use_reentrant=False)
             else:
                 x, resid = self._layer(i, x, resid, positions, cu_seqlens, max_seqlen)
+            self._capture(i, x, resid)
         if not self.is_last_stage:
             return x if resid is None else x + resid
         h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], self.cfg.rms_eps)
@@ -824,18 +828,27 @@ class TransformerLM(nn.Module):
     # ------------------------------------------------------ rollout (no grad)
     @torch.no_grad()
     def forward_prefill(self, input_ids, positions, cu_seqlens, max_seqlen, kv: KVCache, slot_mapping,
-                        last_token_index: torch.Tensor) -> torch.Tensor:
+                        last_token_index: torch.Tensor, hidden_in: Optional[torch.Tensor] = None) -> torch.Tensor:
         """Prompt prefill: runs the packed prompts, writes K/V into the paged cache,
-        returns the final hidden state of each sequence's last token ``[B, H]``."""
+        returns the final hidden state of each sequence's last token ``[B, H]``.
+        ``hidden_in`` replaces the token embeddings (a draft head fed features)."""
         self._in_rollout = True
         try:
             return self._forward_prefill(input_ids, positions, cu_seqlens, max_seqlen, kv, slot_mapping,
-                                         last_token_index)
+                                         last_token_index, hidden_in)
         finally:
             self._in_rollout = False
 
-    def _forward_prefill(self, input_ids, positions, cu_seqlens, max_seqlen, kv, slot_mapping, last_token_index):
-        x = self.embed_full(input_ids)
+    def _capture(self, i: int, x: torch.Tensor, resid: Optional[torch.Tensor]) -> None:
+        """Record the residual stream after layer ``i`` when it is a capture layer."""
+        if self.capture_layers is not None and i in self.capture_layers:
+            if self.captured is None:
+                self.captured = {}
+            self.captured[i] = (x if resid is None else x + resid).detach()
+
+    def _forward_prefill(self, input_ids, positions, cu_seqlens, max_seqlen, kv, slot_mapping, last_token_index,
+                         hidden_in=None):
+        x = self.embed_full(input_ids) if hidden_in is None else hidden_in
         resid = None
         eps = self.cfg.rms_eps
         for i in range(self.cfg.num_layers):
@@ -854,6 +867,7 @@ class TransformerLM(nn.Module):
             h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
             m = self._mlp_infer(i, h2)
             x, resid = s2, m
+            self._capture(i, x, resid)
         h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], eps)
         return h[last_token_index]
 
@@ -875,20 +889,23 @@ class TransformerLM(nn.Module):
 
     @torch.no_grad()
     def forward_decode(self, tokens, positions, kv: KVCache, block_tables, seq_lens, slot_mapping,
-                       max_seq_len: int = 0) -> torch.Tensor:
-        """One decode step for ``B`` sequences: ``tokens [B]`` -> hidden ``[B, H]``."""
+                       max_seq_len: int = 0, hidden_in: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """One decode step for ``B`` sequences: ``tokens [B]`` -> hidden ``[B, H]``
+        (``hidden_in`` replaces the token embeddings)."""
         self._in_rollout = True
         try:
-            return self._forward_decode(tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len)
+            return self._forward_decode(tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len,
+                                        hidden_in)
         finally:
             self._in_rollout = False
 
-    def _forward_decode(self, tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len):
+    def _forward_decode(self, tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len,
+                        hidden_in=None):
         ar = self._decode_ar_op(tokens.shape[0]) if not self.cfg.is_moe else None
         if ar is not None:
             return self._forward_decode_fused_ar(tokens, positions, kv, block_tables, seq_lens, slot_mapping,
-                                                 max_seq_len, ar)
-        x = self.embed_full(tokens)
+                                                 max_seq_len, ar, hidden_in)
+        x = self.embed_full(tokens) if hidden_in is None else hidden_in
         resid = None
         eps = self.cfg.rms_eps
         for i in range(self.cfg.num_layers):
@@ -909,14 +926,16 @@ class TransformerLM(nn.Module):
             h2, s2 = add_rms_norm(s, a, self._params[p + "post_attention_layernorm.weight"], eps)
             m = self._mlp_infer(i, h2)
             x, resid = s2, m
+            self._capture(i, x, resid)
         h, _ = add_rms_norm(x, resid, self._params["model.norm.weight"], eps)
         return h
 
-    def _forward_decode_fused_ar(self, tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len, ar):
+    def _forward_decode_fused_ar(self, tokens, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len, ar,
+                                 hidden_in=None):
         """Decode step with every row-parallel output reduced by the fused
         peer-memory all-reduce + residual add + RMSNorm (no NCCL in the step)."""
         eps = self.cfg.rms_eps
-        s = self.embed_full(tokens).contiguous()  # residual stream, updated in place
+        s = (self.embed_full(tokens) if hidden_in is None else hidden_in).contiguous()  # residual, updated in place
         h = rms_norm(s, self._params["model.layers.0.input_layernorm.weight"], eps)
         L = self.cfg.num_layers
         for i in range(L):
@@ -935,6 +954,7 @@ class TransformerLM(nn.Module):
             w_next = self._params[f"model.layers.{i + 1}.input_layernorm.weight"] if i + 1 < L \
                 else self._params["model.norm.weight"]
             h = ar(m, s, w_next, eps)
+            self._capture(i, s, None)
         return h
 
     def embed_full(self, ids: torch.Tensor) -> torch.Tensor:

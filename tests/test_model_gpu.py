@@ -214,7 +214,7 @@ def test_prompt_dedup_and_chunked_prefill_on_gpu(cuda_device):
     ref = worker({"enable_prefix_caching": False, "enable_chunked_prefill": False}).generate(data, greedy=True)
     w = worker({"enable_prefix_caching": True, "enable_chunked_prefill": True, "max_tokens": 64})
     out = w.generate(data, greedy=True)
-    assert w.engine.stats_last_prefill["prefilled"] == 4 and w.engine.stats_last_prefill["passes"] == 4
+    assert w.engine.stats_last_prefill["prefilled"] == 4 and w.engine.stats_last_prefill["passes"] == 3  # [9, 40] [77] [31]
     first = torch.stack([out["logprobs"][b, int(lens[b])] for b in range(16)])
     first_ref = torch.stack([ref["logprobs"][b, int(lens[b])] for b in range(16)])
     assert (first - first_ref).abs().max() < 5e-2

@@ -156,10 +156,13 @@ class RolloutEngine:
         self._states.clear()
         self._graph_pool = None
 
-    def set_draft(self, draft: TransformerLM, num_speculative_tokens: int) -> None:
+    def set_draft(self, draft, num_speculative_tokens: int) -> None:
         """Enable speculative decoding with ``draft`` proposing ``num_speculative_tokens``
-        tokens per round (the KV caches are re-created at the next prepare)."""
+        tokens per round (the KV caches are re-created at the next prepare): a
+        small LM (its own embedding) or an Eagle3 head (``rl_b200.models.eagle3``,
+        fed the target's hidden features)."""
         self.draft = draft
+        self.draft_kind = "eagle3" if hasattr(draft, "fuse") else "lm"
         self.num_spec = int(num_speculative_tokens)
         self.max_blocks_per_seq = math.ceil((self.max_model_len + self.num_spec + 1) / self.block_size)
         self.finish_generation()
@@ -240,12 +243,15 @@ class RolloutEngine:
         if recording:
             self.model.router_record = {}
         h_parts = []
+        self._eagle_fprev_rows = {}
         for rows in self._prefill_passes(rep, lens_l, chunk_tokens):
             h_parts.append(self._prefill_rows(input_ids, rows, lens_l, block_tables, spec))
         h = torch.cat(h_parts) if len(h_parts) > 1 else h_parts[0]
         if len(rep) < B:
             self._copy_prompt_blocks(rep, inv, lens_l, block_tables, spec)
             h = h[torch.tensor(inv, device=h.device)]
+        if self._eagle_fprev_rows:
+            self._eagle_fprev = torch.stack([self._eagle_fprev_rows[rep[u]] for u in inv])
         self.stats_last_prefill = {"prompts": B, "prefilled": len(rep), "passes": len(h_parts),
                                    "tokens": int(sum(lens_l[r] for r in rep))}
         prefill_routes = self._take_routes() if recording else None
@@ -350,8 +356,24 @@ class RolloutEngine:
         seq_row = torch.repeat_interleave(torch.tensor(rows), torch.tensor(rl)).to(dev)
         slot = (block_tables[seq_row, (positions // bs).long()].long() * bs + (positions % bs).long())
         last_idx = (cu[1:] - 1).to(dev).long()
-        h = self.model.forward_prefill(flat, positions, cu_d, max(rl), self.kv, slot, last_idx)
-        if spec:
+        eagle = spec and getattr(self, "draft_kind", "lm") == "eagle3"
+        if eagle:  # the Eagle3 head reads the target's hidden features of every prompt position
+            self.model.capture_layers, self.model.captured = self.draft.aux_layers, None
+        try:
+            h = self.model.forward_prefill(flat, positions, cu_d, max(rl), self.kv, slot, last_idx)
+            feats = (torch.cat([self.model.captured[i] for i in self.draft.aux_layers], -1) if eagle else None)
+        finally:
+            if eagle:
+                self.model.capture_layers, self.model.captured = None, None
+        if eagle:
+            from rl_b200.models.eagle3 import shift_features
+
+            with torch.no_grad():
+                self.draft.prefill(self.model.embed_full(flat), shift_features(feats, cu_d), positions, cu_d, max(rl),
+                                   self.draft_kv, slot, last_idx)
+                for r, f in zip(rows, self.draft.fuse(feats[last_idx])):
+                    self._eagle_fprev_rows[r] = f  # feature of each prompt's last position
+        elif spec:
             self.draft.forward_prefill(flat, positions, cu_d, max(rl), self.draft_kv, slot, last_idx)
         return h
 
@@ -443,14 +465,23 @@ class RolloutEngine:
         bt_rows = block_tables.repeat_interleave(k + 1, 0)
         temp = temperature if temperature > 0 else 0.0
         rnd = 0
+        eagle = getattr(self, "draft_kind", "lm") == "eagle3"
+        fprev = self._eagle_fprev if eagle else None  # target feature of the position before `last`
+        maxlen = self.max_model_len + k + 1
         while not bool(done.all()):
             # 1. draft proposals (rows of finished sequences run too; results are ignored)
             x = last
             drafts, dlogits = [], []
+            f = fprev
             for j in range(k):
                 p = (pos0 + j).to(torch.int32)
                 slot = block_tables.gather(1, (p // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (p % bs).long()
-                h = self.draft.forward_decode(x, p, self.draft_kv, block_tables, p + 1, slot, self.max_model_len + k + 1)
+                if eagle:  # later proposals feed back the draft's own hidden as the feature
+                    f = self.draft.step(self.model.embed_full(x), f, p, self.draft_kv, block_tables, p + 1, slot,
+                                        maxlen)
+                    h = f
+                else:
+                    h = self.draft.forward_decode(x, p, self.draft_kv, block_tables, p + 1, slot, maxlen)
                 lg = self.draft.logits_infer(h)
                 x, _ = sample_tokens(lg, temp if temp > 0 else 1.0, 1 if temp == 0 else None, 1.0, seed=self.seed + 17,
                                      offset=(self.calls << 24) + rnd * (k + 1) + j)
@@ -461,8 +492,15 @@ class RolloutEngine:
             rows_tok = torch.cat([last.unsqueeze(1), dr], 1).reshape(-1)
             rows_pos = (pos0.unsqueeze(1) + ar).reshape(-1).to(torch.int32)
             slot = bt_rows.gather(1, (rows_pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (rows_pos % bs).long()
-            h = self.model.forward_decode(rows_tok, rows_pos, self.kv, bt_rows, rows_pos + 1, slot,
-                                          self.max_model_len + k + 1)
+            if eagle:
+                self.model.capture_layers, self.model.captured = self.draft.aux_layers, None
+            try:
+                h = self.model.forward_decode(rows_tok, rows_pos, self.kv, bt_rows, rows_pos + 1, slot, maxlen)
+                vfeats = (torch.cat([self.model.captured[i] for i in self.draft.aux_layers], -1).view(B, k + 1, -1)
+                          if eagle else None)
+            finally:
+                if eagle:
+                    self.model.capture_layers, self.model.captured = None, None
             tl = self.model.logits_infer(h).view(B, k + 1, -1)
             out, n, olp = spec_verify(tl, torch.stack(dlogits, 1), dr, temp, seed=self.seed,
                                       offset=(self.calls << 20) + rnd)
@@ -483,6 +521,21 @@ class RolloutEngine:
             newly = (take > 0) & (first_stop <= take) & is_stop.any(1)
             done = done | newly | (glen >= max_new)
             last = torch.where(take > 0, out.gather(1, (take - 1).clamp_min(0).unsqueeze(1)).squeeze(1), last)
+            if eagle:
+                # the next round starts from the verified feature of the position before the
+                # new `last`, and the draft cache entries of the accepted positions are
+                # rewritten from verified features (proposals used the draft's own)
+                rows_b = torch.arange(B, device=dev)
+                f_new = self.draft.fuse(vfeats[rows_b, (take - 1).clamp_min(0)])
+                fprev = torch.where((take > 0).unsqueeze(1), f_new, fprev)
+                if k > 1:
+                    fx_tok = out[:, : k - 1].reshape(-1)
+                    fx_pos = (pos0.unsqueeze(1) + ar[1:k]).reshape(-1).to(torch.int32)
+                    bt_fx = block_tables.repeat_interleave(k - 1, 0)
+                    fx_slot = bt_fx.gather(1, (fx_pos // bs).long().unsqueeze(1)).squeeze(1).long() * bs + \
+                        (fx_pos % bs).long()
+                    self.draft.step(self.model.embed_full(fx_tok), self.draft.fuse(vfeats[:, : k - 1].reshape(B * (k - 1), -1)),
+                                    fx_pos, self.draft_kv, bt_fx, fx_pos + 1, fx_slot, maxlen)
             pos0 = pos0 + take
             self.spec_stats["rounds"] += 1
             self.spec_stats["proposed"] += int(k * B)

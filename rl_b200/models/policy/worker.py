@@ -229,7 +229,26 @@ class PolicyWorker:
         # proposes tokens for the rollout engine and is trained online on rollouts
         spec = gen_cfg.get("speculative") or {}
         self.draft = None
-        if int(spec.get("num_speculative_tokens", 0) or 0) > 0:
+        self.draft_kind = None
+        dpol = policy_cfg.get("draft") or {}
+        if dpol.get("enabled", False):
+            # Eagle3 head on the policy's hidden states (the reference's policy.draft block);
+            # proposals per round from generation.speculative or the vLLM-style speculative_config
+            kind = str(dpol.get("speculator_type", "eagle3")).lower()
+            if kind != "eagle3":
+                raise NotImplementedError(f"draft speculator_type {kind!r} (only eagle3 is built)")
+            from rl_b200.models.eagle3 import Eagle3Draft
+
+            sc = ((gen_cfg.get("vllm_kwargs") or {}).get("speculative_config") or {})
+            k = int(spec.get("num_speculative_tokens") or sc.get("num_speculative_tokens") or 3)
+            self.draft = Eagle3Draft(self.gen_model, aux_layers=dpol.get("aux_layers"), seed=seed,
+                                     ttt_steps=int(dpol.get("ttt_steps", 2)))
+            self.draft_kind = "eagle3"
+            self.draft_loss_weight = float(dpol.get("loss_weight", 1.0))
+            self._draft_k = k
+            self.engine.set_draft(self.draft, k)
+            self._draft_opt = torch.optim.AdamW(self.draft.parameters(), lr=float(dpol.get("lr", 1e-4)))
+        elif int(spec.get("num_speculative_tokens", 0) or 0) > 0:
             dcfg = self.model_cfg.replace(num_layers=int(spec.get("draft_num_layers", 1)))
             self.draft = TransformerLM(dcfg, self.gen_model.ps, device=self.device, dtype=self.dtype,
                                        seed=seed + 7919)
@@ -1077,6 +1096,8 @@ class PolicyWorker:
         (``nemo_rl/models/policy/draft_config.py:64``).  Returns the loss."""
         if self.draft is None:
             return 0.0
+        if self.draft_kind == "eagle3":
+            return self._train_eagle3(data, max_tokens)
         lengths = self._lengths(data)
         rows = [r for r in range(len(lengths)) if lengths[r] > 1]
         tot, sel = 0, []
@@ -1104,6 +1125,49 @@ class PolicyWorker:
         loss = torch.nn.functional.cross_entropy(logits[~last], tgt[~last])
         self._draft_opt.zero_grad(set_to_none=True)
         loss.backward()
+        self._draft_opt.step()
+        return float(loss.detach())
+
+    def _train_eagle3(self, data: BatchedDataDict, max_tokens: int) -> float:
+        """One Eagle3 step: a no-grad policy forward over the rollout sequences
+        captures the feature layers, then the head learns the token two positions
+        ahead of each feature (``Eagle3Draft.train_loss``); ``loss_weight`` scales
+        the loss.  Returns the unweighted loss."""
+        lengths = self._lengths(data)
+        sel, tot = [], 0
+        for r in range(len(lengths)):
+            if lengths[r] < 3:
+                continue
+            if tot + lengths[r] > max_tokens and sel:
+                break
+            sel.append(r)
+            tot += lengths[r]
+        if not sel:
+            return 0.0
+        flat, pos, cu, max_len, _ = pack_rows(data["input_ids"], lengths, sel, pad_to_multiple=1)
+        dev = self.device
+        flat_d, pos_d, cu_d = _to_device(flat, dev), _to_device(pos, dev), _to_device(cu, dev)
+        m = self.gen_model
+        with torch.no_grad():
+            m.capture_layers, m.captured = self.draft.aux_layers, None
+            try:
+                was = m.training
+                m.eval()
+                m(flat_d, pos_d, cu_d, max_len)
+                feats = torch.cat([m.captured[i] for i in self.draft.aux_layers], -1)
+                m.train(was)
+            finally:
+                m.capture_layers, m.captured = None, None
+            emb = m.embed_full(flat_d)
+        # row t: feature t, embedding of token t + 1, label token t + 2 (inside its sequence)
+        seq_end = torch.repeat_interleave(cu_d[1:].long(), (cu_d[1:] - cu_d[:-1]).long())
+        idx = torch.arange(flat_d.numel(), device=dev)
+        mask = idx + 2 < seq_end
+        self.draft.train()
+        loss = self.draft.train_loss(torch.roll(emb, -1, 0), feats, torch.roll(flat_d, -2, 0), mask, pos_d, cu_d,
+                                     max_len)
+        self._draft_opt.zero_grad(set_to_none=True)
+        (loss * self.draft_loss_weight).backward()
         self._draft_opt.step()
         return float(loss.detach())
 
@@ -1231,7 +1295,8 @@ class PolicyWorker:
             if hasattr(old, attr):
                 setattr(self.engine, attr, getattr(old, attr))
         if self.draft is not None:
-            self.engine.set_draft(self.draft, int((self._gen_cfg.get("speculative") or {})["num_speculative_tokens"]))
+            self.engine.set_draft(self.draft, getattr(self, "_draft_k", None)
+                                  or int((self._gen_cfg.get("speculative") or {})["num_speculative_tokens"]))
         self.engine_incarnation = getattr(self, "engine_incarnation", 0) + 1
         self.refit()
 

@@ -792,7 +792,8 @@ class TransformerLM(nn.Module):
         Under pipeline parallelism a non-first stage starts from ``hidden_in`` (the
         previous stage's output) and a non-last stage returns its residual stream."""
         self._aux_losses = []
-        x = self.embed(input_ids) if self.is_first_stage else hidden_in
+        # a non-first pipeline stage (or a draft head fed features) starts from hidden_in
+        x = hidden_in if hidden_in is not None else self.embed(input_ids)
         resid = None
         layers = self.chunk_ranges[self.chunk] if (self.vpp > 1 and self.chunk is not None) else self.layer_range
         for i in layers:

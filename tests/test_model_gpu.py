@@ -220,3 +220,36 @@ def test_prompt_dedup_and_chunked_prefill_on_gpu(cuda_device):
     assert (first - first_ref).abs().max() < 5e-2
     same = (out["output_ids"] == ref["output_ids"]).float().mean()
     assert same > 0.9, same
+
+
+def test_eagle3_speculative_rollout_on_gpu(cuda_device):
+    """Eagle3 head on the GPU (bf16): speculative greedy rollouts agree with plain
+    greedy rollouts, and a few online draft steps on the policy's rollouts raise
+    the number of tokens emitted per verification round."""
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import single_process_state
+
+    def worker(draft):
+        cfg = _policy_cfg(new=32)
+        if draft:
+            cfg["generation"]["speculative"] = {"num_speculative_tokens": 3}
+            cfg["draft"] = {"enabled": True, "speculator_type": "eagle3", "lr": 2e-3}
+        return PolicyWorker(cfg, model_cfg=SMALL, pstate=single_process_state(cuda_device), seed=6)
+
+    g = torch.Generator().manual_seed(0)
+    data = BatchedDataDict({"input_ids": torch.randint(0, SMALL.vocab_size, (16, 40), generator=g),
+                            "input_lengths": torch.randint(8, 41, (16,), generator=g)})
+    plain = worker(False).generate(data, greedy=True)["output_ids"]
+    w = worker(True)
+    spec = w.generate(data, greedy=True)
+    assert (spec["output_ids"] == plain).float().mean() > 0.9
+    seqs = BatchedDataDict({"input_ids": spec["output_ids"], "input_lengths": spec["unpadded_sequence_lengths"]})
+    w.engine.spec_stats = {"rounds": 0, "proposed": 0, "emitted": 0}
+    w.generate(data, greedy=True)
+    per_round0 = w.engine.spec_stats["emitted"] / max(1, w.engine.spec_stats["rounds"])
+    for _ in range(30):
+        w.train_draft(seqs)
+    w.engine.spec_stats = {"rounds": 0, "proposed": 0, "emitted": 0}
+    w.generate(data, greedy=True)
+    per_round1 = w.engine.spec_stats["emitted"] / max(1, w.engine.spec_stats["rounds"])
+    assert per_round1 > per_round0 + 0.2, (per_round0, per_round1)

@@ -106,7 +106,11 @@ def main(argv=None) -> dict:
         state.update({k: info[k] for k in state if k in info})
     logger = Logger(cfg.get("logger", {}))
     logger.log_hyperparams(cfg)
-    if (cfg["grpo"].get("async_grpo") or {}).get("enabled", False):
+    if (cfg["grpo"].get("single_controller") or {}).get("enabled", False):
+        from rl_b200.algorithms.single_controller import single_controller_train
+
+        state = single_controller_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
+    elif (cfg["grpo"].get("async_grpo") or {}).get("enabled", False):
         from rl_b200.algorithms.async_grpo import async_grpo_train, restore_replay_buffer, restore_rollout_recovery
 
         buf, ledger = None, None

@@ -270,3 +270,29 @@ def case_torch_dist_async(rank: int, tp: int, path: str):
             "moved": max((back[k] - v.detach().float().cpu()).abs().max().item()
                          for k, v in hf_state_dict(w.model, dtype=None).items()),
             "pending": pending_after_return}
+
+
+def case_single_controller_dp(rank: int):
+    """Two gloo ranks; rank 1 drops a prompt: both train the same number of
+    groups every step."""
+    import torch.distributed as dist
+
+    from rl_b200.algorithms.single_controller import RolloutDataError, SingleController
+    from rl_b200.parallel.state import init_distributed
+    from tests.test_single_controller_cpu import _fake_generate, _fake_train, _loader
+
+    ps = init_distributed(backend="gloo")
+    seen = []
+
+    def fail(idx):
+        if rank == 1 and 2 in idx:
+            raise RolloutDataError("bad prompt on rank 1")
+
+    sc = SingleController(_fake_generate([], fail), _fake_train(seen), _loader(12, per_batch=1), group_size=2,
+                          groups_per_step=4, max_steps=2, dp_group=ps.dp_group,
+                          cfg={"max_inflight_prompts": 1,
+                               "rollout_failure": {"backoff_base_s": 0.0, "max_data_attempts_per_prompt": 1,
+                                                   "max_skipped_prompts": 1, "min_step_batch_fraction": 0.75}})
+    sc.run()
+    dist.barrier()
+    return [len(ix) for _, ix, _ in seen]

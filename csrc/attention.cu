@@ -412,7 +412,7 @@ paged_decode_pipe_kernel(const bf16* __restrict__ q, long long q_stride, const b
                          const bf16* __restrict__ vc, const int* __restrict__ block_tables, int max_blocks,
                          const int* __restrict__ seq_lens, int block_size, int nkv, float scale_log2,
                          int tokens_per_split, float* __restrict__ part_o, float* __restrict__ part_ml,
-                         bf16* __restrict__ out) {
+                         bf16* __restrict__ out, int n_blocks) {
   constexpr int BT = 16, CH = HD / 8, KS = HD / 16, NT = HD / 8, TILE = BT * HD;
   pdl_launch_dependents();
   extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -429,7 +429,10 @@ paged_decode_pipe_kernel(const bf16* __restrict__ q, long long q_stride, const b
   const int blk0 = t_begin / block_size;
   if (t_end > t_begin) {
     const int nblk = (t_end - 1) / block_size - blk0 + 1;
-    for (int i = threadIdx.x; i < nblk; i += W * 32) sbt[i] = bt[blk0 + i];
+    for (int i = threadIdx.x; i < nblk; i += W * 32) {
+      const int blk = bt[blk0 + i];
+      sbt[i] = RLB_IN_BOUNDS(blk, n_blocks, kBoundsBlockTable) ? blk : 0;
+    }
   }
   uint32_t qf[KS][4];
   {
@@ -1240,7 +1243,7 @@ at::Tensor paged_decode_attn(at::Tensor q, at::Tensor k_cache, at::Tensor v_cach
               (const bf16*)q.data_ptr(), q.stride(0), (const bf16*)k_cache.data_ptr(),
               (const bf16*)v_cache.data_ptr(), bt.data_ptr<int>(), max_blocks, sl.data_ptr<int>(), bs, nkv,
               scale_log2, tps, splits > 1 ? part_o.data_ptr<float>() : nullptr,
-              splits > 1 ? part_ml.data_ptr<float>() : nullptr, (bf16*)out.data_ptr());
+              splits > 1 ? part_ml.data_ptr<float>() : nullptr, (bf16*)out.data_ptr(), (int)k_cache.size(0));
           RLB_CUDA_CHECK(cudaGetLastError());
           if (splits > 1)
             decode_combine_kernel<HD><<<B * nq, HD, 0, stream()>>>(
@@ -1299,3 +1302,5 @@ int64_t attn_error_flag(bool reset) {
   }
   return v;
 }
+
+int64_t bounds_error_attention(bool reset) { return rlb::rlb_bounds_error(reset); }

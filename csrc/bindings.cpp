@@ -2,7 +2,8 @@
 #include <torch/extension.h>
 
 #include <atomic>
-
+#include <map>
+#include <string>
 #include <vector>
 
 // norm.cu
@@ -95,6 +96,29 @@ std::vector<at::Tensor> flash_attn_seg_fwd(at::Tensor q, at::Tensor k, at::Tenso
 int64_t attn_error_flag(bool reset);
 std::vector<at::Tensor> flash_attn_seg_bwd(at::Tensor dout, at::Tensor q, at::Tensor k, at::Tensor v, at::Tensor out,
                                            at::Tensor lse, at::Tensor seg, int64_t max_k, double scale);
+int64_t bounds_error_elementwise(bool reset);
+int64_t bounds_error_attention(bool reset);
+int64_t bounds_error_ep_comm(bool reset);
+int64_t bounds_error_moe_router(bool reset);
+
+// Error words of the bounds-checked debug build, per instrumented source file
+// (0 everywhere in the release build).
+std::map<std::string, int64_t> bounds_errors(bool reset) {
+  return {{"elementwise", bounds_error_elementwise(reset)},
+          {"attention", bounds_error_attention(reset)},
+          {"ep_comm", bounds_error_ep_comm(reset)},
+          {"moe_router", bounds_error_moe_router(reset)}};
+}
+
+bool debug_bounds_build() {
+#ifdef RLB_DEBUG_BOUNDS
+  return true;
+#else
+  return false;
+#endif
+}
+
+std::vector<at::Tensor> moe_router_topk(at::Tensor logits, int64_t k);
 void ep_scatter(at::Tensor src, c10::optional<at::Tensor> src_row, at::Tensor dst_rank, at::Tensor dst_row,
                 c10::optional<at::Tensor> tags, int64_t cap, std::vector<int64_t> buf, std::vector<int64_t> tag,
                 std::vector<int64_t> flags, std::vector<int64_t> acks, int64_t me, int64_t epoch, at::Tensor counter);
@@ -177,6 +201,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("dp_reduce_shard", &dp_reduce_shard, "DP gradient reduce-scatter over NVLink peer loads (+ norm partials)");
   m.def("dp_adam_allgather", &dp_adam_allgather, "sharded AdamW fused with the parameter all-gather (peer stores)");
   m.def("gemm_ag", &gemm_ag, "all-gather -> GEMM: waits per gathered shard (copy-engine transfers) on device flags");
+  m.def("bounds_errors", &bounds_errors, "bounds-checked debug build: error word per instrumented file (site<<40|index)");
+  m.def("debug_bounds_build", &debug_bounds_build, "whether this library is the bounds-checked debug build");
+  m.def("moe_router_topk", &moe_router_topk, "MoE router: softmax, top-k and the expert-grouped permutation");
   m.def("ep_scatter", &ep_scatter, "MoE token rows -> peers' receive buffers at their final positions (P2P stores)");
   m.def("ep_consume", &ep_consume, "wait for every source's scatter, copy the received rows out, acknowledge");
   m.def("ep_error_flag", &ep_error_flag, py::arg("reset") = false);

@@ -32,6 +32,42 @@ inline cudaStream_t stream() { return at::cuda::getCurrentCUDAStream().stream();
 int64_t peer_wait_cycles();
 void set_peer_wait_cycles(int64_t cycles);
 
+// Bounds checks of data-dependent indices (row ids, cache slots, block-table
+// entries, expert rows) for the bounds-checked debug build (-DRLB_DEBUG_BOUNDS,
+// built as rl_b200._C_debug).  RLB_IN_BOUNDS(i, n, site) is true when
+// 0 <= i < n; in the debug build a false result records (site << 40 | low 40 bits
+// of i) in this translation unit's error word (the first failure wins) and the
+// caller skips the access, so an index bug is reported instead of touching
+// memory outside the tensor.  In the release build it is the constant true.
+// site codes (the error word's top bits)
+constexpr int kBoundsKvSlot = 1;       // KV-cache slot of a written token
+constexpr int kBoundsBlockTable = 2;   // paged-attention block-table entry
+constexpr int kBoundsEpRow = 3;        // expert-parallel destination row / rank / source row
+constexpr int kBoundsRouterRow = 4;    // MoE router expert-grouped row
+#ifdef RLB_DEBUG_BOUNDS
+static __device__ unsigned long long g_rlb_bounds_err = 0ull;
+__device__ __forceinline__ bool rlb_in_bounds(long long i, long long n, int site) {
+  if (i >= 0 && i < n) return true;
+  atomicCAS(&g_rlb_bounds_err, 0ull,
+            ((unsigned long long)site << 40) | ((unsigned long long)i & ((1ull << 40) - 1ull)));
+  return false;
+}
+#define RLB_IN_BOUNDS(i, n, site) rlb_in_bounds((long long)(i), (long long)(n), (site))
+// host side: read (and optionally clear) this translation unit's error word
+static inline int64_t rlb_bounds_error(bool reset) {
+  unsigned long long v = 0;
+  cudaMemcpyFromSymbol(&v, g_rlb_bounds_err, sizeof(v));
+  if (reset && v) {
+    const unsigned long long z = 0;
+    cudaMemcpyToSymbol(g_rlb_bounds_err, &z, sizeof(z));
+  }
+  return (int64_t)v;
+}
+#else
+#define RLB_IN_BOUNDS(i, n, site) true
+static inline int64_t rlb_bounds_error(bool) { return 0; }
+#endif
+
 inline int num_sms() {
   static int n = -1;
   if (n < 0) {

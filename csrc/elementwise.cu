@@ -130,14 +130,14 @@ template <typename T, typename C>
 __global__ void write_kv_kernel(const T* __restrict__ k, const T* __restrict__ v, long long k_stride,
                                 long long v_stride, C* __restrict__ kc, C* __restrict__ vc,
                                 const long long* __restrict__ slots, int T_, int row_elems, float inv_k,
-                                float inv_v) {
+                                float inv_v, long long n_slots) {
   const long long total = (long long)T_ * row_elems;
   for (long long id = blockIdx.x * (long long)blockDim.x + threadIdx.x; id < total;
        id += (long long)gridDim.x * blockDim.x) {
     const int t = id / row_elems;
     const int e = id % row_elems;
     const long long slot = slots[t];
-    if (slot < 0) continue;
+    if (slot < 0 || !RLB_IN_BOUNDS(slot, n_slots, kBoundsKvSlot)) continue;
     const float kv = to_f(k[t * k_stride + e]) * inv_k;
     const float vv = to_f(v[t * v_stride + e]) * inv_v;
     if constexpr (std::is_same<C, __nv_fp8_e4m3>::value) {
@@ -226,18 +226,21 @@ void write_kv_cache(at::Tensor k, at::Tensor v, at::Tensor k_cache, at::Tensor v
   const int row = k.size(1) * k.size(2);
   auto sl = slots.to(at::kLong).contiguous();
   long long total = (long long)T_ * row;
+  const long long n_slots = std::min(k_cache.numel(), v_cache.numel()) / row;
   RLB_DISPATCH_FLOAT(k.scalar_type(), "write_kv_cache", [&] {
     if (k_cache.scalar_type() == at::kFloat8_e4m3fn) {
       write_kv_kernel<scalar_t, __nv_fp8_e4m3><<<ew_grid(total), 256, 0, stream()>>>(
           (const scalar_t*)k.data_ptr(), (const scalar_t*)v.data_ptr(), k.stride(0), v.stride(0),
           (__nv_fp8_e4m3*)k_cache.data_ptr(), (__nv_fp8_e4m3*)v_cache.data_ptr(), (long long*)sl.data_ptr<int64_t>(), T_,
-          row, (float)(1.0 / k_scale), (float)(1.0 / v_scale));
+          row, (float)(1.0 / k_scale), (float)(1.0 / v_scale), n_slots);
     } else {
       RLB_CHECK(k_cache.scalar_type() == k.scalar_type(), "write_kv_cache: cache dtype mismatch");
       write_kv_kernel<scalar_t, scalar_t><<<ew_grid(total), 256, 0, stream()>>>(
           (const scalar_t*)k.data_ptr(), (const scalar_t*)v.data_ptr(), k.stride(0), v.stride(0),
-          (scalar_t*)k_cache.data_ptr(), (scalar_t*)v_cache.data_ptr(), (long long*)sl.data_ptr<int64_t>(), T_, row, 1.f, 1.f);
+          (scalar_t*)k_cache.data_ptr(), (scalar_t*)v_cache.data_ptr(), (long long*)sl.data_ptr<int64_t>(), T_, row, 1.f, 1.f, n_slots);
     }
   });
   RLB_CUDA_CHECK(cudaGetLastError());
 }
+
+int64_t bounds_error_elementwise(bool reset) { return rlb::rlb_bounds_error(reset); }

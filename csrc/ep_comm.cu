@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(256)
 scatter_kernel(const __nv_bfloat16* __restrict__ src, const int* __restrict__ src_row,
                const int* __restrict__ dst_rank, const int* __restrict__ dst_row, const int* __restrict__ tags,
                int n_items, int H, long long cap, Peers pe, int n, int me, uint32_t epoch,
-               unsigned int* __restrict__ counter) {
+               unsigned int* __restrict__ counter, long long src_rows) {
   __shared__ int ok;
   const int par = epoch & 1;
   if (threadIdx.x == 0) {
@@ -77,6 +77,9 @@ scatter_kernel(const __nv_bfloat16* __restrict__ src, const int* __restrict__ sr
     for (int i = blockIdx.x * 8 + warp; i < n_items; i += gridDim.x * 8) {
       const int r = src_row ? src_row[i] : i;
       const int d = dst_rank[i];
+      if (!RLB_IN_BOUNDS(r, src_rows, kBoundsEpRow) || !RLB_IN_BOUNDS(d, n, kBoundsEpRow) ||
+          !RLB_IN_BOUNDS(dst_row[i], cap, kBoundsEpRow))
+        continue;
       const long long row = (long long)par * cap + dst_row[i];
       const uint4* s = reinterpret_cast<const uint4*>(src + (long long)r * H);
       uint4* o = reinterpret_cast<uint4*>(pe.buf[d] + row * H);
@@ -172,7 +175,7 @@ void ep_scatter(at::Tensor src, c10::optional<at::Tensor> src_row, at::Tensor ds
       (const __nv_bfloat16*)src.data_ptr(), src_row ? src_row->data_ptr<int>() : nullptr, dst_rank.data_ptr<int>(),
       dst_row.data_ptr<int>(), tags ? tags->data_ptr<int>() : nullptr, n_items, H, cap,
       make_peers(buf, tag, flags, acks), (int)buf.size(), (int)me, (uint32_t)epoch,
-      reinterpret_cast<unsigned int*>(counter.data_ptr<int>()));
+      reinterpret_cast<unsigned int*>(counter.data_ptr<int>()), (long long)src.size(0));
   RLB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -202,3 +205,5 @@ int64_t ep_error_flag(bool reset) {
   }
   return v;
 }
+
+int64_t bounds_error_ep_comm(bool reset) { return rlb::rlb_bounds_error(reset); }

@@ -641,26 +641,37 @@ class TransformerLM(nn.Module):
 
     def route(self, i: int, h: torch.Tensor):
         """Router: fp32 logits -> softmax -> top-k (+ renormalisation); returns
-        (topk_weights [T,k] fp32, topk_ids [T,k] int64, probs [T,E] fp32)."""
+        (topk_weights [T,k] fp32, topk_ids [T,k] int64, probs [T,E] fp32, perm),
+        where ``perm`` is (stable expert-grouped order of the T*k assignments,
+        tokens per expert) when the native router kernel produced them, else None."""
+        from rl_b200.ops.moe_router import router_topk
+
         c = self.cfg
         w = self._params[f"model.layers.{i}.mlp.gate.weight"]
         rdtype = torch.float64 if c.moe_router_dtype == "fp64" else torch.float32
         logits = torch.matmul(h.to(rdtype), w.to(rdtype).t())
-        probs = torch.softmax(logits, -1)
+        perm = None
         if self.router_replay is not None and i in self.router_replay:
+            probs = torch.softmax(logits, -1)
             # R3: the experts the rollout chose; tokens without a recorded route
             # (negative ids, e.g. the last sampled token) keep the computed top-k
             rep = self.router_replay[i].to(h.device).long()
             ids = torch.topk(probs, c.moe_top_k, dim=-1)[1]
             ids = torch.where(rep[:, :1] >= 0, rep, ids)
             vals = probs.gather(-1, ids)
+        elif logits.is_cuda and rdtype == torch.float32:
+            # one native pass: softmax, top-k, per-expert counts and the grouped order
+            probs, ids, counts, order = router_topk(logits, c.moe_top_k)
+            vals = probs.gather(-1, ids)
+            perm = (order, counts)
         else:
+            probs = torch.softmax(logits, -1)
             vals, ids = torch.topk(probs, c.moe_top_k, dim=-1)
         if self.router_record is not None:
             self.router_record[i] = ids.detach().to(torch.int16 if c.num_experts < 32768 else torch.int32)
         if c.moe_norm_topk_prob:
             vals = vals / vals.sum(-1, keepdim=True)
-        return vals.to(torch.float32), ids, probs.to(torch.float32)
+        return vals.to(torch.float32), ids, probs.to(torch.float32), perm
 
     def _moe_block(self, i: int, h: torch.Tensor) -> torch.Tensor:
         c = self.cfg
@@ -672,11 +683,14 @@ class TransformerLM(nn.Module):
             h = copy_to_tp(h, self.ps.tp_group)  # backward: the partial input gradients are summed
         T, H = h.shape
         k, E = c.moe_top_k, c.num_experts
-        weights, ids, probs = self.route(i, h)
+        weights, ids, probs, perm = self.route(i, h)
         if c.moe_aux_loss_coef > 0 and torch.is_grad_enabled():
             # Switch-style load balance: E * sum_e f_e * P_e
-            counts = torch.zeros(E, device=h.device, dtype=torch.float32).index_add_(
-                0, ids.reshape(-1), torch.ones(T * k, device=h.device))
+            if perm is not None:
+                counts = perm[1].float()
+            else:
+                counts = torch.zeros(E, device=h.device, dtype=torch.float32).index_add_(
+                    0, ids.reshape(-1), torch.ones(T * k, device=h.device))
             f = counts / max(1, T * k)
             aux = E * (f.detach() * probs.mean(0)).sum() * c.moe_aux_loss_coef
             # split experts: every TP rank holds the same aux loss, whose gradients the
@@ -687,17 +701,20 @@ class TransformerLM(nn.Module):
         wgu = self._params[p + "mlp.experts.gate_up_proj"]
         wdn = self._params[p + "mlp.experts.down_proj"]
         if self.ps.ep_size > 1 and self.fused_collectives and h.is_cuda and h.dtype == torch.bfloat16:
-            out = self._moe_ep_fused(h, ids, weights, wgu, wdn)
+            out = self._moe_ep_fused(h, ids, weights, wgu, wdn, perm)
             if self.sequence_parallel:
                 out = reduce_scatter_to_sp(out, self.ps.tp_group)
             elif split:
                 out = reduce_from_tp(out, self.ps.tp_group)
             return out
         flat_ids = ids.reshape(-1)
-        order = torch.argsort(flat_ids, stable=True)
+        if perm is not None:
+            order, counts = perm
+        else:
+            order = torch.argsort(flat_ids, stable=True)
+            counts = torch.bincount(flat_ids, minlength=E)
         token_of = order // k
         xs = h[token_of]                                             # [T*k, H] permuted by expert
-        counts = torch.bincount(flat_ids, minlength=E)
         if self.ps.ep_size > 1:
             ys = self._moe_ep_experts(xs, counts, wgu, wdn)
         else:
@@ -711,7 +728,7 @@ class TransformerLM(nn.Module):
             out = reduce_from_tp(out, self.ps.tp_group)
         return out
 
-    def _moe_ep_fused(self, h, ids, weights, wgu, wdn):
+    def _moe_ep_fused(self, h, ids, weights, wgu, wdn, perm=None):
         """Expert parallelism with the peer-store dispatch / combine kernels
         (``rl_b200.parallel.ep_fused``): rows land grouped by local expert on
         their owner, outputs return to their assignment slot."""
@@ -719,7 +736,7 @@ class TransformerLM(nn.Module):
 
         T, H = h.shape
         k = ids.shape[1]
-        plan = make_plan(ids, self.ps.ep_size, self.ps.ep_rank, self.experts_local, self.ps.ep_group)
+        plan = make_plan(ids, self.ps.ep_size, self.ps.ep_rank, self.experts_local, self.ps.ep_group, perm)
         ex = self._ep_ex
         if ex is None or ex[0].cap < plan.R_max or ex[1].cap < plan.TK_max or ex[0].H != H:
             if ex is not None:

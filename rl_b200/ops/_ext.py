@@ -49,6 +49,9 @@ _KERNELS_PER_CALL = {
     "symm_open": 0,
     "symm_close": 0,
     "symm_view": 0,
+    "moe_router_topk": 3,
+    "bounds_errors": 0,
+    "debug_bounds_build": 0,
 }
 
 
@@ -75,7 +78,13 @@ def _load():
     if _EXT is not None or _ERR is not None:
         return
     try:
-        from rl_b200 import _C  # type: ignore
+        import os
+
+        if os.environ.get("RL_B200_DEBUG_BOUNDS", "0") == "1":
+            # bounds-checked debug build (setup.py with RL_B200_DEBUG_BOUNDS=1)
+            from rl_b200 import _C_debug as _C  # type: ignore
+        else:
+            from rl_b200 import _C  # type: ignore
 
         _EXT = _Counting(_C)
     except BaseException as e:  # noqa: BLE001 - record and re-raise at use
@@ -120,6 +129,15 @@ ERROR_FLAGS = ("gemm_error_flag", "gemm_sm100_error_flag", "gemm_fp8_error_flag"
                "ep_error_flag")
 
 
+BOUNDS_SITES = {1: "KV-cache slot", 2: "paged-attention block-table entry",
+                3: "expert-parallel row / rank", 4: "MoE router expert-grouped row"}
+
+
+class DeviceBoundsError(RuntimeError):
+    """The bounds-checked debug build met a data-dependent index outside its
+    tensor (the access was skipped)."""
+
+
 class DeviceWaitError(RuntimeError):
     """A kernel gave up a bounded wait (a peer's flag, a copy engine's flag or a
     pipeline barrier never arrived) and returned with its error word set."""
@@ -143,3 +161,11 @@ def check_device_errors(reset: bool = True) -> None:
     if bad:
         raise DeviceWaitError(f"device wait expired: {bad} (error word = wait site code); "
                               "a peer rank, copy engine or pipeline stage never signalled")
+    if getattr(mod, "debug_bounds_build", None) is not None and mod.debug_bounds_build():
+        hits = {f: v for f, v in mod.bounds_errors(reset).items() if v}
+        if hits:
+            raise DeviceBoundsError("index out of bounds (access skipped): " + ", ".join(
+                f"{f}: {BOUNDS_SITES.get(v >> 40, v >> 40)} index {v & ((1 << 40) - 1)}" for f, v in hits.items()))
+    from rl_b200.parallel.symm import check_canaries
+
+    check_canaries()

@@ -81,13 +81,18 @@ class EPPlan:
         self.__dict__.update(kw)
 
 
-def make_plan(ids: torch.Tensor, n: int, me: int, experts_local: int, group) -> EPPlan:
+def make_plan(ids: torch.Tensor, n: int, me: int, experts_local: int, group, perm=None) -> EPPlan:
+    """``perm``: (stable expert-grouped order, tokens per expert) from the router
+    kernel, when it produced them."""
     T, k = ids.shape
     E = n * experts_local
     flat = ids.reshape(-1)
-    order = torch.argsort(flat, stable=True)
+    if perm is not None:
+        order, counts = perm[0], perm[1].to(torch.int32)
+    else:
+        order = torch.argsort(flat, stable=True)
+        counts = torch.bincount(flat, minlength=E).to(torch.int32)
     sorted_e = flat[order]
-    counts = torch.bincount(flat, minlength=E).to(torch.int32)
     all_counts = torch.empty(n * E, dtype=torch.int32, device=ids.device)
     dist.all_gather_into_tensor(all_counts, counts, group=group)
     C = all_counts.view(n, n, experts_local).long()          # [src, dst, local expert]

@@ -10,12 +10,30 @@ kernels in ``rl_b200.parallel.fused``.
 
 from __future__ import annotations
 
+import os
+import weakref
+
 import torch
 import torch.distributed as dist
 
 from rl_b200.ops._ext import ext
 
-__all__ = ["SymmetricBuffer", "NodeSymmetric"]
+__all__ = ["SymmetricBuffer", "NodeSymmetric", "canaries_enabled", "check_canaries"]
+
+# Canaries: with RL_B200_CANARIES=1 (or the bounds-checked debug build,
+# RL_B200_DEBUG_BOUNDS=1) every symmetric buffer is allocated with a guard of
+# GUARD bytes before and after it, filled with PATTERN; ``ptrs`` / ``local_ptr``
+# point past the head guard, so kernels see the same buffer.  A peer store (or a
+# local one) that runs off either end of a buffer lands in a guard, and
+# ``check_canaries`` (run with the device error words at step boundaries) names
+# the buffer whose guard changed.
+GUARD = 4096
+PATTERN = 0xA5
+_LIVE: "weakref.WeakSet[SymmetricBuffer]" = weakref.WeakSet()
+
+
+def canaries_enabled() -> bool:
+    return os.environ.get("RL_B200_CANARIES", "0") == "1" or os.environ.get("RL_B200_DEBUG_BOUNDS", "0") == "1"
 
 
 class SymmetricBuffer:
@@ -24,8 +42,10 @@ class SymmetricBuffer:
         self.group = group
         self.world = dist.get_world_size(group) if dist.is_initialized() else 1
         self.rank = dist.get_rank(group) if dist.is_initialized() else 0
-        ptr, handle = ext().symm_alloc(self.nbytes)
-        self.local_ptr = int(ptr)
+        self.guard = GUARD if canaries_enabled() else 0
+        ptr, handle = ext().symm_alloc(self.nbytes + 2 * self.guard)
+        self._bases: list[int] = []  # what the allocator / IPC open returned (closed by close())
+        self.local_ptr = int(ptr) + self.guard
         handles = [None] * self.world
         if self.world > 1:
             dist.all_gather_object(handles, bytes(handle.numpy().tobytes()), group=group)
@@ -33,35 +53,67 @@ class SymmetricBuffer:
             handles = [bytes(handle.numpy().tobytes())]
         self.ptrs: list[int] = []
         for r, h in enumerate(handles):
-            if r == self.rank:
-                self.ptrs.append(self.local_ptr)
-            else:
-                self.ptrs.append(int(ext().symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8))))
+            base = int(ptr) if r == self.rank else \
+                int(ext().symm_open(torch.frombuffer(bytearray(h), dtype=torch.uint8)))
+            self._bases.append(base)
+            self.ptrs.append(base + self.guard)
         self.device = torch.cuda.current_device()
+        if self.guard:
+            for g in self._guards():
+                g.fill_(PATTERN)
+            _LIVE.add(self)
+
+    def _guards(self) -> list:
+        code = 0  # uint8
+        return [ext().symm_view(self.local_ptr - self.guard, self.guard, code, self.device),
+                ext().symm_view(self.local_ptr + self.nbytes, self.guard, code, self.device)]
+
+    def canary_intact(self) -> bool:
+        """Whether both guards of this rank's buffer still hold the pattern."""
+        if not self.guard or not self.ptrs:
+            return True
+        return all(bool((g == PATTERN).all()) for g in self._guards())
 
     def local_view(self, dtype: torch.dtype, numel: int, offset_bytes: int = 0) -> torch.Tensor:
         code = {torch.bfloat16: 15, torch.float32: 6, torch.int32: 3, torch.uint8: 0}[dtype]
         return ext().symm_view(self.local_ptr + offset_bytes, numel, code, self.device)
 
     def close(self) -> None:
-        for r, p in enumerate(self.ptrs):
+        for r, p in enumerate(self._bases):
             if r != self.rank:
                 ext().symm_close(p)
-        ext().symm_close(self.local_ptr)
-        self.ptrs = []
+        if self._bases:
+            ext().symm_close(self._bases[self.rank])
+        self.ptrs, self._bases = [], []
+        _LIVE.discard(self)
 
     def close_collective(self) -> None:
         """Collective release: every rank unmaps its peers' buffers, all ranks
         synchronise, then each frees its own allocation (no rank frees memory a
         peer still maps)."""
-        for r, p in enumerate(self.ptrs):
+        for r, p in enumerate(self._bases):
             if r != self.rank:
                 ext().symm_close(p)
         torch.cuda.synchronize()
         if self.world > 1:
             dist.barrier(group=self.group)
-        ext().symm_close(self.local_ptr)
-        self.ptrs = []
+        if self._bases:
+            ext().symm_close(self._bases[self.rank])
+        self.ptrs, self._bases = [], []
+        _LIVE.discard(self)
+
+
+def check_canaries() -> None:
+    """Raise ``DeviceBoundsError`` when a guard of a live symmetric buffer of this
+    rank was overwritten (canaries on); no-op otherwise."""
+    if not _LIVE:
+        return
+    from rl_b200.ops._ext import DeviceBoundsError
+
+    bad = [b for b in list(_LIVE) if not b.canary_intact()]
+    if bad:
+        raise DeviceBoundsError("symmetric buffer guard overwritten (a store ran off a buffer's end): " +
+                                ", ".join(f"{b.nbytes} B buffer at 0x{b.local_ptr:x}" for b in bad))
 
 
 class NodeSymmetric:

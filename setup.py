@@ -32,18 +32,27 @@ CUDA_FLAGS = [
 
 sources = sorted(glob.glob(os.path.join("csrc", "*.cu"))) + ["csrc/bindings.cpp"]
 
+# RL_B200_DEBUG_BOUNDS=1 builds the bounds-checked debug variant rl_b200._C_debug
+# (data-dependent indices checked and reported instead of dereferenced); it is
+# loaded instead of rl_b200._C when the same variable is set at run time.
+DEBUG_BOUNDS = os.environ.get("RL_B200_DEBUG_BOUNDS", "0") == "1"
+EXT_NAME = "rl_b200._C_debug" if DEBUG_BOUNDS else "rl_b200._C"
+DEFINES = ["-DRLB_DEBUG_BOUNDS"] if DEBUG_BOUNDS else []
+
 setup(
     name="rl_b200",
     version="0.1.0",
     packages=[],
     ext_modules=[
         CUDAExtension(
-            name="rl_b200._C",
+            name=EXT_NAME,
             sources=sources,
             include_dirs=[os.path.join(HERE, "csrc")],
-            extra_compile_args={"cxx": ["-O3", "-std=c++17"], "nvcc": CUDA_FLAGS},
+            extra_compile_args={"cxx": ["-O3", "-std=c++17"] + DEFINES, "nvcc": CUDA_FLAGS + DEFINES},
             libraries=["cuda"],
         )
     ],
     cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+    # the debug variant keeps its objects apart from the release build's
+    options={"build_ext": {"build_temp": os.path.join("build", "debug_bounds")}} if DEBUG_BOUNDS else {},
 )

@@ -587,3 +587,31 @@ def test_grouped_gemm_tcgen05(cuda_device, counts, N, K):
         ref[s:s + c] = x[s:s + c].float() @ w[e].float().t()
         s += c
     assert rel_err(y, ref) < 1e-2
+
+
+@pytest.mark.parametrize("T,E,k", [(1000, 128, 8), (37, 60, 4), (4096, 256, 8), (64, 1024, 1), (5, 8, 2)])
+def test_moe_router_topk_kernel(T, E, k):
+    """Router kernel vs the fp32 reference: probabilities, top-k ids, tokens per
+    expert, the stable expert-grouped order, and the logits gradient of the
+    renormalised top-k weights."""
+    from rl_b200.ops.moe_router import router_topk, router_topk_ref
+
+    torch.manual_seed(T + E)
+    logits = (torch.randn(T, E, device="cuda") * 2).requires_grad_(True)
+    probs, ids, counts, order = router_topk(logits, k)
+    rp, rids, rcounts, _ = router_topk_ref(logits.detach(), k)
+    torch.testing.assert_close(probs, rp, rtol=1e-5, atol=1e-6)
+    # the chosen experts carry the k largest probabilities in descending order
+    # (ids may differ from torch.topk only between probabilities within rounding)
+    torch.testing.assert_close(rp.gather(-1, ids), rp.gather(-1, rids), rtol=1e-6, atol=1e-7)
+    assert (ids == rids).float().mean() > 0.999
+    assert torch.equal(counts.long(), torch.bincount(ids.reshape(-1), minlength=E))
+    assert torch.equal(order, torch.argsort(ids.reshape(-1), stable=True))
+    w = probs.gather(-1, ids)
+    (w / w.sum(-1, keepdim=True) * torch.arange(1, k + 1, device="cuda")).sum().backward()
+    g = logits.grad.clone()
+    lr = logits.detach().clone().requires_grad_(True)
+    p2 = torch.softmax(lr, -1)
+    w2 = p2.gather(-1, ids)
+    (w2 / w2.sum(-1, keepdim=True) * torch.arange(1, k + 1, device="cuda")).sum().backward()
+    torch.testing.assert_close(g, lr.grad, rtol=1e-4, atol=1e-6)

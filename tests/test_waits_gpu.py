@@ -1,7 +1,7 @@
 """Bounded in-kernel waits: a flag that nothing ever sets makes the kernel give
 up after the configured bound, set its error word and return; the host then
-raises, and the CUDA context stays usable (SURVEY §5 failure detection, made
-testable without a GPU fault).
+raises, and the CUDA context stays usable (failure detection made testable
+without a GPU fault).
 
 The wait exercised here is the context-parallel key-arrival wait of the tcgen05
 attention forward: every key block waits for the copy flag of the rank that owns

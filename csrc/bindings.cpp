@@ -127,6 +127,8 @@ void ep_consume(at::Tensor out, c10::optional<at::Tensor> out_tag, int64_t cap, 
                 int64_t epoch, at::Tensor counter);
 int64_t ep_error_flag(bool reset);
 at::Tensor dp_reduce_shard(std::vector<int64_t> grad_ptrs, int64_t lo, int64_t len, at::Tensor out);
+void dp_wait_ready(std::vector<int64_t> flag_ptrs, int64_t idx, int64_t epoch);
+int64_t dp_error_flag(bool reset);
 void dp_adam_allgather(std::vector<int64_t> param_ptrs, int64_t lo, at::Tensor master, at::Tensor grad,
                        at::Tensor exp_avg, at::Tensor exp_avg_sq, at::Tensor nodecay, double lr, double b1, double b2,
                        double eps, double wd, int64_t step, double gscale);
@@ -199,6 +201,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("symm_close", &symm_close);
   m.def("symm_view", &symm_view);
   m.def("dp_reduce_shard", &dp_reduce_shard, "DP gradient reduce-scatter over NVLink peer loads (+ norm partials)");
+  m.def("dp_wait_ready", &dp_wait_ready, "bounded wait until every DP rank published a gradient bucket's epoch");
+  m.def("dp_error_flag", &dp_error_flag, "error word of the DP bucket-readiness waits (1000 + bucket on expiry)");
   m.def("dp_adam_allgather", &dp_adam_allgather, "sharded AdamW fused with the parameter all-gather (peer stores)");
   m.def("gemm_ag", &gemm_ag, "all-gather -> GEMM: waits per gathered shard (copy-engine transfers) on device flags");
   m.def("bounds_errors", &bounds_errors, "bounds-checked debug build: error word per instrumented file (site<<40|index)");

@@ -106,10 +106,60 @@ adam_allgather_kernel(Ptrs ptrs, int n, long long lo, long long len4, float* __r
   }
 }
 
+// Readiness of gradient buckets for the reduction overlapped with the backward
+// pass: every rank stores the step's epoch into its word `idx` of a symmetric
+// u32 array (a stream memory write after the bucket's last gradient kernel);
+// the reducing rank's side stream runs wait_ready_kernel (one thread per rank,
+// acquire loads at system scope, bounded by the peer-wait budget; on expiry it
+// sets the error word to 1000 + idx and returns) and then reduce_shard_kernel
+// over the bucket's part of its shard.
+__device__ int g_dpo_error = 0;
+
+struct FlagPtrs {
+  const uint32_t* f[kMaxRanks];
+};
+
+__global__ void wait_ready_kernel(FlagPtrs fp, int n, int idx, uint32_t epoch, long long limit) {
+  const int r = threadIdx.x;
+  if (r >= n) return;
+  const uint32_t* p = fp.f[r] + idx;
+  const long long t0 = clock64();
+  for (;;) {
+    uint32_t v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];\n" : "=r"(v) : "l"(p) : "memory");
+    if ((int)(v - epoch) >= 0) return;
+    if (clock64() - t0 > limit) {
+      atomicExch(&g_dpo_error, 1000 + idx);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
 }  // namespace dpo
 }  // namespace rlb
 
 using namespace rlb;
+
+void dp_wait_ready(std::vector<int64_t> flag_ptrs, int64_t idx, int64_t epoch) {
+  TORCH_CHECK(!flag_ptrs.empty() && flag_ptrs.size() <= (size_t)dpo::kMaxRanks, "dp_wait_ready: 1..8 ranks");
+  dpo::FlagPtrs fp{};
+  for (size_t i = 0; i < flag_ptrs.size(); ++i) fp.f[i] = reinterpret_cast<const uint32_t*>((uintptr_t)flag_ptrs[i]);
+  // the budget covers the skew of one micro-batch's backward between the ranks
+  dpo::wait_ready_kernel<<<1, 32, 0, stream()>>>(fp, (int)flag_ptrs.size(), (int)idx, (uint32_t)epoch,
+                                                 4 * peer_wait_cycles());
+  RLB_CUDA_CHECK(cudaGetLastError());
+}
+
+int64_t dp_error_flag(bool reset) {
+  int v = 0;
+  RLB_CUDA_CHECK(cudaMemcpyFromSymbol(&v, dpo::g_dpo_error, sizeof(int)));
+  if (reset && v) {
+    const int z = 0;
+    RLB_CUDA_CHECK(cudaMemcpyToSymbol(dpo::g_dpo_error, &z, sizeof(int)));
+  }
+  return v;
+}
 
 namespace {
 dpo::Ptrs make_ptrs(const std::vector<int64_t>& g, const std::vector<int64_t>& p) {

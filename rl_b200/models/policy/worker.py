@@ -190,6 +190,11 @@ class PolicyWorker:
                                    symmetric=self.symmetric if fused_dp else None,
                                    pp_group=self.ps.pp_group if self.pp > 1 else None,
                                    muon=MuonConfig.from_megatron(mopt) if self.lora is None else None)
+        # overlap_grad_reduce: data-parallel gradient reduction per decoder layer during
+        # the backward of a step's last micro-batch (fused DP path)
+        ddp = mc.get("distributed_data_parallel_config") or {}
+        self._overlap_grad_reduce = bool(ddp.get("overlap_grad_reduce", False)) and self.optimizer.setup_overlap(
+            lambda name: int(name.split(".")[2]) if name.startswith("model.layers.") else None)
         mgc = gen_cfg.get("mcore_generation_config", {}) or {}
         self.max_seq_len = int(policy_cfg.get("max_total_sequence_length", 512))
         if self.max_seq_len > self.model.rope_cache.shape[0]:
@@ -867,10 +872,17 @@ class PolicyWorker:
             if i == st.num_microbatches - 1:
                 self._pp_train_schedule(st)
             return {}
-        loss, metrics = self._mb_loss(st, i)
-        if not st.eval_mode:
-            loss.backward()
-            self.optimizer._fold_param_grads()
+        arm = (self._overlap_grad_reduce and not st.eval_mode and st.done == st.num_microbatches - 1
+               and self.optimizer.begin_overlap())
+        if arm:
+            self.model.grad_ready_hook = self.optimizer.layer_ready
+        try:
+            loss, metrics = self._mb_loss(st, i)
+            if not st.eval_mode:
+                loss.backward()
+                self.optimizer._fold_param_grads()
+        finally:
+            self.model.grad_ready_hook = None
         st.done += 1
         return metrics
 

@@ -290,6 +290,9 @@ class TransformerLM(nn.Module):
         self._fp8_cache: dict = {}
         # hidden-state capture (Eagle3 draft features): layer -> residual stream after it
         self.capture_layers: Optional[tuple] = None
+        # called with a layer index once that layer's backward is complete (set by
+        # the policy worker around the backward whose gradient reduction overlaps)
+        self.grad_ready_hook = None
         self.captured: Optional[dict] = None
 
     # ------------------------------------------------------------------ params
@@ -813,7 +816,11 @@ class TransformerLM(nn.Module):
         x = hidden_in if hidden_in is not None else self.embed(input_ids)
         resid = None
         layers = self.chunk_ranges[self.chunk] if (self.vpp > 1 and self.chunk is not None) else self.layer_range
+        hook = self.grad_ready_hook
         for i in layers:
+            if hook is not None and torch.is_grad_enabled() and x.requires_grad:
+                # fires once layer i's backward is complete (its first op produces this gradient last)
+                x.register_hook(lambda g, i=i, f=hook: f(i))
             if self.activation_checkpointing and torch.is_grad_enabled():
                 if resid is None:
                     x, resid = ckpt.checkpoint(self._layer, i, x, None, positions, cu_seqlens, max_seqlen,

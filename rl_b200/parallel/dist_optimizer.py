@@ -195,6 +195,8 @@ class FlatAdamW:
         self.ensure_grad_buffer()
         self.step_count = 0
         self.last_grad_norm = 0.0
+        self._ov = None            # reduction overlapped with the backward (setup_overlap)
+        self._ov_active = False
 
     # ------------------------------------------------------- flat re-layout
     def _relayout(self, expert_shift: int) -> None:
@@ -268,11 +270,113 @@ class FlatAdamW:
                 p.main_grad.add_(p.grad.float())
                 p.grad = None
 
+    # ------------------------------------ reduction overlapped with backward
+    def setup_overlap(self, layer_of) -> bool:
+        """Megatron's ``overlap_grad_reduce`` for the fused data-parallel path.
+
+        The dense segment's parameters are bucketed by decoder layer
+        (``layer_of(name)`` -> layer index or None).  During the backward pass of
+        a step's last micro-batch, when a layer's gradients are final
+        (``layer_ready``, called from an autograd hook on the layer's input), each
+        rank publishes the step's epoch for that layer in a symmetric word array
+        (stream memory write on the compute stream), and a side stream waits until
+        every DP rank published it (bounded wait kernel) and reduces this rank's
+        part of the layer's range out of the peers' gradient buffers (the same
+        peer-load reduction as ``step``).  ``step`` then reduces only what no
+        bucket covered (embedding, final norm, head, parameters that are first
+        summed over TP).  Collective (allocates symmetric memory); returns whether
+        overlap is on (the fused DP path only, no pipeline parallelism)."""
+        seg = self.segments[0]
+        if not self._fused(seg) or self.pp_group is not None:
+            return False
+        ranges: dict[int, list] = {}
+        params: dict[int, list] = {}
+        for sp, p in self.model.named_flat_params():
+            L = layer_of(sp.name)
+            if L is None or sp.ep_dim is not None or not (seg.lo <= sp.offset < seg.hi):
+                continue
+            mode = getattr(sp, "grad_reduce", None)
+            if self.tp > 1 and (mode == "tp_sum" or (mode is None and self.sequence_parallel and sp.tp_dim is None)):
+                continue  # summed over TP in step() before the data-parallel reduction
+            end = min(seg.hi, sp.offset + (sp.numel + 63) // 64 * 64)  # through the parameter's padding
+            ranges.setdefault(L, []).append((sp.offset, end, True))
+            params.setdefault(L, []).append(p)
+        mine = {}
+        for L, rs in ranges.items():
+            cut = [(max(a, seg.s_lo), min(b, seg.s_hi)) for a, b, _ in _merge(rs)]
+            mine[L] = [(a, b) for a, b in cut if a < b]
+        n_layers = int(self.model.cfg.num_layers)
+        flags = self.symmetric.alloc(4 * n_layers)
+        flags.local_view(torch.int32, n_layers).zero_()
+        torch.cuda.synchronize()
+        self._fence(seg.group)
+        self._ov = {"mine": mine, "params": params, "flags": flags, "epoch": 0,
+                    "flag_ptrs": [flags.ptrs[dist.get_global_rank(seg.group, r)] for r in range(seg.n)],
+                    "stream": torch.cuda.Stream(device=self.device), "parts": [], "done": set()}
+        return True
+
+    def begin_overlap(self) -> bool:
+        """Arm the overlapped reduction for the backward pass that follows (the
+        step's last micro-batch).  The ranks first meet (a fence on the compute
+        stream), so the readiness waits only absorb the skew of one backward."""
+        ov = self._ov
+        if ov is None:
+            return False
+        self.ensure_grad_buffer()
+        seg = self.segments[0]
+        self._fence(seg.group)
+        ov["epoch"] += 1
+        ov["parts"], ov["done"] = [], set()
+        ov["stream"].wait_stream(torch.cuda.current_stream())
+        self._ov_active = True
+        return True
+
+    def layer_ready(self, layer: int) -> None:
+        """Layer ``layer``'s gradients are complete on this rank (autograd hook)."""
+        ov = self._ov
+        if not self._ov_active or ov is None or layer not in ov["params"] or layer in ov["done"]:
+            return
+        for p in ov["params"][layer]:  # gradients autograd left in .grad (router weights)
+            if p.grad is not None:
+                p.main_grad.add_(p.grad.float())
+                p.grad = None
+        e = ext()
+        flags = ov["flags"]
+        e.stream_write_u32(flags.local_ptr + 4 * layer, ov["epoch"])
+        ready = torch.cuda.Event()
+        ready.record()
+        seg = self.segments[0]
+        side = ov["stream"]
+        with torch.cuda.stream(side):
+            side.wait_event(ready)
+            e.dp_wait_ready(ov["flag_ptrs"], layer, ov["epoch"])
+            ptrs = self._peer_ptrs(self._grad_symm, seg)
+            for a, b in ov["mine"].get(layer, []):
+                ov["parts"].append(e.dp_reduce_shard(ptrs, a, b - a, seg.grad_shard[a - seg.s_lo:b - seg.s_lo]))
+        ov["done"].add(layer)
+
+    def _overlap_rest(self, seg) -> list:
+        """Ranges of this rank's shard that no completed bucket reduced."""
+        covered = sorted(r for L in self._ov["done"] for r in self._ov["mine"].get(L, []))
+        rest, cur = [], seg.s_lo
+        for a, b in covered:
+            if a > cur:
+                rest.append((cur, a))
+            cur = max(cur, b)
+        if cur < seg.s_hi:
+            rest.append((cur, seg.s_hi))
+        return rest
+
     # ----------------------------------------------------------------- step
     @torch.no_grad()
     def step(self) -> dict:
         self.ensure_grad_buffer()
         self._fold_param_grads()
+        overlapped = self._ov_active
+        if overlapped:
+            # the buckets reduced during the backward are complete before they are read
+            torch.cuda.current_stream().wait_stream(self._ov["stream"])
+            self._ov_active = False
         m = self.model
         if self.tp > 1:
             for sp, p in m.named_flat_params():
@@ -291,9 +395,16 @@ class FlatAdamW:
                 # peers finished their backward passes (stream-ordered fence), then
                 # this rank reduces its shard straight out of their gradient buffers
                 self._fence(seg.group)
-                part = ext().dp_reduce_shard(self._peer_ptrs(self._grad_symm, seg), seg.s_lo, seg.shard,
-                                             seg.grad_shard)
-                sq_all = part.sum()
+                ptrs = self._peer_ptrs(self._grad_symm, seg)
+                if overlapped and seg is self.segments[0]:
+                    parts = list(self._ov["parts"])
+                    for a, b in self._overlap_rest(seg):
+                        parts.append(ext().dp_reduce_shard(ptrs, a, b - a, seg.grad_shard[a - seg.s_lo:b - seg.s_lo]))
+                    sq_all = torch.cat([p.reshape(-1) for p in parts]).sum()
+                    self._ov["parts"] = []
+                else:
+                    part = ext().dp_reduce_shard(ptrs, seg.s_lo, seg.shard, seg.grad_shard)
+                    sq_all = part.sum()
             elif seg.sharded:
                 # losses are normalised by GLOBAL token / sequence counts, so the
                 # per-rank gradients are partial sums: reduce with SUM, not mean.

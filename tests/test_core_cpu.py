@@ -903,3 +903,24 @@ def test_training_stops_and_saves_before_deadline(tmp_path):
                       checkpointer=ck, step_callback=lambda s, m: time.sleep(0.3))
     assert 1 <= state["current_step"] < 50
     assert ck.list_steps() == [state["current_step"]]
+
+
+def test_overlapped_reduction_bookkeeping():
+    """overlap_grad_reduce bookkeeping: ``step`` reduces exactly the parts of the
+    shard that no completed layer bucket covered; setup is refused off the
+    fused data-parallel path (CPU here)."""
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.parallel.dist_optimizer import FlatAdamW
+
+    cfg = ModelConfig(name="t", vocab_size=64, hidden_size=32, num_layers=2, num_heads=2, num_kv_heads=1, head_dim=16,
+                      ffn_hidden_size=64, rope_theta=10000.0, max_position_embeddings=64)
+    m = TransformerLM(cfg, device="cpu", dtype=torch.float32, seed=0)
+    opt = FlatAdamW(m, lr=1e-3)
+    assert opt.setup_overlap(lambda n: None) is False  # not the fused DP path
+    seg = opt.segments[0]
+    lo, hi = seg.s_lo, seg.s_hi
+    opt._ov = {"done": {0, 1}, "mine": {0: [(lo + 64, lo + 128)], 1: [(lo + 256, lo + 320)], 2: [(lo, lo + 8)]}}
+    assert opt._overlap_rest(seg) == [(lo, lo + 64), (lo + 128, lo + 256), (lo + 320, hi)]
+    opt._ov["done"] = set()
+    assert opt._overlap_rest(seg) == [(lo, hi)]

@@ -227,7 +227,7 @@ def test_refit_reshard_tp2_to_tp1_fp8_2gpu():
     print("refit reshard (bf16 copy + fp8 quant):", f"{outs[0]['ms']:.3f} ms for {outs[0]['bytes'] / 2**20:.1f} MiB")
 
 
-def case_fused_dp_optimizer(rank: int, fused: bool):
+def case_fused_dp_optimizer(rank: int, fused: bool, overlap: bool = False):
     """DP=2 training steps with the fused reduce-scatter / AdamW+all-gather
     kernels (peer loads and stores) or with NCCL; returns what must agree."""
     import os
@@ -247,16 +247,21 @@ def case_fused_dp_optimizer(rank: int, fused: bool):
                       head_dim=64, ffn_hidden_size=512, rope_theta=10000.0, max_position_embeddings=256)
     pcfg = {"max_total_sequence_length": 32, "precision": "bfloat16", "train_global_batch_size": 8,
             "optimizer": {"kwargs": {"lr": 1e-3, "weight_decay": 0.01}},
-            "megatron_cfg": {"fused_dp_optimizer": fused},
+            "megatron_cfg": {"fused_dp_optimizer": fused,
+                             "distributed_data_parallel_config": {"overlap_grad_reduce": overlap}},
             "generation": {"temperature": 1.0, "max_new_tokens": 4},
             "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
     w = PolicyWorker(pcfg, model_cfg=cfg, pstate=ps, seed=3)
     used = w.optimizer._fused(w.optimizer.segments[0])
+    if overlap:
+        used = used and w._overlap_grad_reduce
     full = make_batch(B=8, S=24, vocab=512, seed=1)
     shard = full.slice(rank * 4, rank * 4 + 4)
     lf = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
     res = [w.train(shard, lf, gbs=4) for _ in range(3)]
     torch.cuda.synchronize()
+    buckets = sorted(w.optimizer._ov["done"]) if overlap else []
+    _ext.check_device_errors()
     flat = w.model.flat_param.float().cpu()
     other = [torch.empty_like(w.model.flat_param) for _ in range(2)]
     dist.all_gather(other, w.model.flat_param)
@@ -265,7 +270,7 @@ def case_fused_dp_optimizer(rank: int, fused: bool):
     dist.barrier()
     dist.destroy_process_group()
     return {"used": used, "loss": [r["loss"] for r in res], "gn": [r["grad_norm"] for r in res], "flat": flat,
-            "same": same}
+            "same": same, "buckets": buckets}
 
 
 def test_fused_dp_optimizer_matches_nccl_2gpu():
@@ -283,6 +288,24 @@ def test_fused_dp_optimizer_matches_nccl_2gpu():
             assert abs(ga - gb) < 1e-3 * max(1.0, gb), (x["gn"], y["gn"])
         d = (x["flat"] - y["flat"]).abs().max().item()
         assert d < 2e-2, d
+
+
+def test_overlapped_dp_grad_reduce_2gpu():
+    """overlap_grad_reduce: per-layer peer-load reductions launched on a side
+    stream during the last micro-batch's backward give the parameters of the
+    reduction after the backward."""
+    _need_gpus(2)
+    from rl_b200.distributed.launch import spawn_ranks
+
+    a = spawn_ranks(case_fused_dp_optimizer, 2, True, True, timeout_s=300)
+    b = spawn_ranks(case_fused_dp_optimizer, 2, True, False, timeout_s=300)
+    for x, y in zip(a, b):
+        assert x["used"] and x["same"] and x["buckets"] == [0, 1], x["buckets"]
+        assert x["loss"][0] == y["loss"][0] and x["gn"][0] == pytest.approx(y["gn"][0], rel=1e-5)
+        for la, lb in zip(x["loss"], y["loss"]):  # later steps: norm partials summed in another grouping
+            assert abs(la - lb) < 1e-3 * max(1.0, abs(lb)), (x["loss"], y["loss"])
+        d = (x["flat"] - y["flat"]).abs().max().item()
+        assert d < 2e-3, d
 
 
 def case_ag_gemm(rank: int, shapes, iters: int):

@@ -167,6 +167,9 @@ def _register_defaults():
     register_environment("nemo_gym", lambda c, **k: HttpGymEnvironment(c))
     register_environment("sliding_puzzle", lambda c, **k: SlidingPuzzleEnvironment(c, **k))
     register_environment("reward_model", lambda c, **k: RewardModelEnvironment(c, **k))
+    from rl_b200.environments import verifiers
+
+    verifiers.register(register_environment)
 
 
 _register_defaults()

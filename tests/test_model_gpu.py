@@ -262,9 +262,9 @@ def test_eagle3_speculative_rollout_on_gpu(cuda_device):
 def test_moe_128_experts_top8_matches_fp32_reference(cuda_device):
     """A MoE model at a realistic router size (128 experts, top-8, renormalised):
     the native path (router kernel, its expert-grouped rows, grouped expert GEMMs)
-    matches the same bf16 model routed by PyTorch ops on the GPU, and both follow
-    the fp32 CPU reference (hidden states; gate and expert weight gradients, the
-    gate's with a bf16-noise tolerance: it sums centred softmax terms)."""
+    matches the same bf16 model routed by PyTorch ops on the GPU within run-to-run
+    noise, and follows the fp32 CPU reference (hidden states; gate and expert
+    weight gradients with loose bounds, see below)."""
     from rl_b200.ops import moe_router
 
     cfg = ModelConfig(name="moe128", vocab_size=2048, hidden_size=512, num_layers=2, num_heads=8, num_kv_heads=2,
@@ -295,17 +295,25 @@ def test_moe_128_experts_top8_matches_fp32_reference(cuda_device):
 
     m, h, gn = run_gpu(True)
     _, h_t, gt = run_gpu(False)
-    # bf16 combine / gradient accumulation by atomics: two runs differ at the 1e-2 level,
-    # a wrong permutation or weight at the 1e-1 to 1 level
-    assert ((h - h_t).norm() / h_t.norm()).item() < 2e-2
+    _, h_t2, gt2 = run_gpu(False)
+
+    def rel(a, b):
+        return ((a - b).norm() / b.norm()).item()
+
+    # bf16 combine / gradient accumulation by atomics makes two identical runs differ
+    # (the router gradient most: it sums centred softmax terms); the native path must
+    # stay within a few times that run-to-run noise (a wrong permutation or weight is O(1))
+    assert rel(h, h_t) < max(3 * rel(h_t2, h_t), 2e-2)
     for n in names:
-        assert ((gn[n] - gt[n]).norm() / gt[n].norm()).item() < 5e-2, n
+        assert rel(gn[n], gt[n]) < max(3 * rel(gt2[n], gt[n]), 5e-2), (n, rel(gn[n], gt[n]), rel(gt2[n], gt[n]))
     ref = TransformerLM(cfg, device="cpu", dtype=torch.float32, seed=5)
     with torch.no_grad():
         ref.flat_param.copy_(m.flat_param.float().cpu())
     hr = ref(ids, pos, cu, max(lens))
     (hr * proj).sum().backward()
     assert ((h - hr).norm() / hr.norm()).item() < 3e-2
-    for n, tol in zip(names, (0.25, 6e-2, 6e-2)):
+    # against fp32 the bf16 hidden states move the router's near-uniform random-init
+    # probabilities across top-8 boundaries, so tokens change experts: loose bounds
+    for n, tol in zip(names, (0.25, 0.25, 0.25)):
         err = ((gn[n] - grad(ref._params[n])).norm() / grad(ref._params[n]).norm()).item()
         assert err < tol, (n, err)

@@ -650,3 +650,67 @@ def test_pipeline_parallel_large_messages_2gpu(vpp):
         assert abs(a - b) < 2e-2 * max(1.0, abs(b)), o
         assert abs(g - h) < 3e-2 * h, o
         assert o["lp_err"] < 0.15, o
+
+
+def _ce_policy(q_meta, q_done, dev):
+    import torch
+
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.weight_sync.checkpoint_engine import CheckpointEngineSynchronizer, create_checkpoint_engine
+
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig(name="ce", vocab_size=1024, hidden_size=256, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=64, ffn_hidden_size=512, rope_theta=10000.0, max_position_embeddings=256)
+    eng = create_checkpoint_engine("cuda_ipc", bucket_size_bytes=1 << 18,
+                                   engine_kwargs={"is_master": True, "port": 0, "timeout_s": 120})
+    meta = eng.prepare()
+    eng.init_policy_process_group(worker_rank=0, train_world_size=1, rollout_world_size=1, metadata=[meta])
+    q_meta.put((meta, eng.port))
+    m = TransformerLM(cfg, device=torch.device("cuda", dev), dtype=torch.bfloat16, seed=3)
+    sync = CheckpointEngineSynchronizer(eng, m)
+    sync.sync()
+    q_done.get(timeout=120)
+    eng.close()
+
+
+def _ce_rollout(meta, port, q_out, dev):
+    import torch
+
+    from rl_b200.models.config import ModelConfig
+    from rl_b200.models.transformer import TransformerLM
+    from rl_b200.weight_sync.checkpoint_engine import CheckpointEngineSynchronizer, create_checkpoint_engine
+
+    torch.cuda.set_device(dev)
+    cfg = ModelConfig(name="ce", vocab_size=1024, hidden_size=256, num_layers=2, num_heads=4, num_kv_heads=2,
+                      head_dim=64, ffn_hidden_size=512, rope_theta=10000.0, max_position_embeddings=256)
+    eng = create_checkpoint_engine("cuda_ipc", bucket_size_bytes=1 << 18, engine_kwargs={"port": port,
+                                                                                          "timeout_s": 120})
+    eng.init_rollout_process_group(rollout_rank=0, train_world_size=1, rollout_world_size=1, metadata=[meta])
+    m = TransformerLM(cfg, device=torch.device("cuda", dev), dtype=torch.bfloat16, seed=77)
+    ref = TransformerLM(cfg, device=torch.device("cuda", dev), dtype=torch.bfloat16, seed=3)
+    n = CheckpointEngineSynchronizer(eng, m).receive_into(m)
+    q_out.put((n, bool(torch.equal(m.flat_param, ref.flat_param)), eng.seq))
+    eng.close()
+
+
+def test_cuda_ipc_checkpoint_engine_2gpu():
+    """Refit between two processes with no process group: the policy's weights
+    leave through two CUDA IPC slots in its HBM and land on the other GPU."""
+    _need_gpus(2)
+    import multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    q_meta, q_done, q_out = ctx.Queue(), ctx.Queue(), ctx.Queue()
+    pp = ctx.Process(target=_ce_policy, args=(q_meta, q_done, 0))
+    pp.start()
+    meta, port = q_meta.get(timeout=180)
+    rp = ctx.Process(target=_ce_rollout, args=(meta, port, q_out, 1))
+    rp.start()
+    try:
+        n, same, buckets = q_out.get(timeout=240)
+    finally:
+        q_done.put(True)
+        rp.join(60)
+        pp.join(60)
+    assert same and n > 0 and buckets > 4

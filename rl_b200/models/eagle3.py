@@ -161,3 +161,79 @@ class Eagle3Draft(nn.Module):
         z = self.combine(emb, feat_h)
         return self.body.forward_decode(positions, positions, kv, block_tables, seq_lens, slot_mapping, max_seq_len,
                                         hidden_in=z)
+
+
+class DFlashDraft(Eagle3Draft):
+    """Block drafter: ``block_size`` tokens proposed in ONE forward pass.
+
+    Reference: the ``dflash`` speculator type of the reference's draft heads
+    (``nemo_rl/models/generation/vllm/speculator_runtime.py:23``; its drafts carry a
+    ``mask_embedding`` parameter, ``vllm/draft_utils.py:112``).  Here the block
+    of a position ``t`` is a short sequence of its own: row 0 holds
+    ``combine(embedding of token t + 1, fused feature of t)``, rows 1..k-1 hold
+    ``combine(mask embedding, fused feature of t)``; rows attend causally within
+    the block (block-local positions 0..k-1) and row j predicts token
+    ``t + 2 + j``.  The target's multi-layer features of ``t`` are the only
+    context, so training on sampled anchor positions and proposing at decode time
+    see the same computation, and drafting needs no draft KV cache."""
+
+    def __init__(self, target, aux_layers: Optional[tuple] = None, seed: int = 0, block_size: int = 4):
+        super().__init__(target, aux_layers=aux_layers, seed=seed, ttt_steps=1)
+        self.block_size = max(1, int(block_size))
+        H = target.cfg.hidden_size
+        g = torch.Generator(device=target.device).manual_seed(seed + 97)
+        self.mask_embedding = nn.Parameter((torch.randn(H, generator=g, device=target.device) * 0.02)
+                                           .to(target.dtype))
+
+    def _block_inputs(self, emb_first: torch.Tensor, feat_h: torch.Tensor, k: int) -> torch.Tensor:
+        """[n, H] first-row embeddings and features -> [n * k, H] block inputs."""
+        n, H = emb_first.shape
+        emb = self.mask_embedding.view(1, 1, H).expand(n, k, H).clone()
+        emb[:, 0] = emb_first
+        feat = feat_h.unsqueeze(1).expand(n, k, H)
+        return self.combine(emb.reshape(n * k, H), feat.reshape(n * k, H))
+
+    def _block_forward(self, z: torch.Tensor, n: int, k: int) -> torch.Tensor:
+        dev = z.device
+        pos = torch.arange(k, device=dev, dtype=torch.int32).repeat(n)
+        cu = torch.arange(0, n * k + 1, k, device=dev, dtype=torch.int32)
+        return self.body(torch.zeros(n * k, dtype=torch.long, device=dev), pos, cu, k, hidden_in=z)
+
+    def train_loss(self, emb_next: torch.Tensor, feats: torch.Tensor, tokens: torch.Tensor,
+                   cu_seqlens: torch.Tensor, max_anchors: int = 1024, seed: int = 0) -> torch.Tensor:
+        """Cross-entropy over sampled anchor positions ``t`` (row ``t`` of
+        ``emb_next`` is the embedding of token ``t + 1``, of ``feats`` the policy
+        features of ``t``; ``tokens`` the packed ids): each anchor's block predicts
+        tokens ``t + 2 .. t + 1 + k`` (rows past its sequence's end are masked)."""
+        from rl_b200.ops.fused_linear_logprob import linear_logprobs
+
+        k = self.block_size
+        T = tokens.numel()
+        dev = tokens.device
+        seq_end = torch.repeat_interleave(cu_seqlens[1:].long(), (cu_seqlens[1:] - cu_seqlens[:-1]).long())
+        idx = torch.arange(T, device=dev)
+        valid = idx + 2 < seq_end
+        anchors = idx[valid]
+        if anchors.numel() == 0:
+            return feats.sum() * 0.0
+        if anchors.numel() > max_anchors:
+            g = torch.Generator(device="cpu").manual_seed(seed)
+            anchors = anchors[torch.randperm(anchors.numel(), generator=g)[:max_anchors].to(dev)]
+        n = anchors.numel()
+        z = self._block_inputs(emb_next[anchors], self.fuse(feats[anchors]), k)
+        h = self._block_forward(z, n, k)
+        tpos = anchors.unsqueeze(1) + 2 + torch.arange(k, device=dev).unsqueeze(0)      # [n, k]
+        ok = tpos < seq_end[anchors].unsqueeze(1)
+        tgt = tokens[tpos.clamp(max=T - 1)].reshape(-1)
+        lp, _ = linear_logprobs(h, self.body.lm_head_weight(), tgt)
+        m = ok.reshape(-1).to(lp.dtype)
+        return -(lp * m).sum() / m.sum().clamp_min(1)
+
+    @torch.no_grad()
+    def propose(self, emb_last: torch.Tensor, feat_h: torch.Tensor, k: Optional[int] = None) -> torch.Tensor:
+        """One forward for every sequence's block: returns ``[B * k, V]`` logits
+        (row j of sequence b proposes the token ``j + 1`` places after ``last``)."""
+        k = k or self.block_size
+        B = emb_last.shape[0]
+        h = self._block_forward(self._block_inputs(emb_last, feat_h, k), B, k)
+        return self.logits_infer(h)

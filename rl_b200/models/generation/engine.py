@@ -160,9 +160,11 @@ class RolloutEngine:
         """Enable speculative decoding with ``draft`` proposing ``num_speculative_tokens``
         tokens per round (the KV caches are re-created at the next prepare): a
         small LM (its own embedding) or an Eagle3 head (``rl_b200.models.eagle3``,
-        fed the target's hidden features)."""
+        fed the target's hidden features) or a block drafter (``DFlashDraft``)."""
         self.draft = draft
-        self.draft_kind = "eagle3" if hasattr(draft, "fuse") else "lm"
+        # "dflash": a block drafter (one forward proposes the whole block);
+        # "eagle3": a feature-fed head drafting token by token; "lm": a small LM
+        self.draft_kind = "dflash" if hasattr(draft, "propose") else ("eagle3" if hasattr(draft, "fuse") else "lm")
         self.num_spec = int(num_speculative_tokens)
         self.max_blocks_per_seq = math.ceil((self.max_model_len + self.num_spec + 1) / self.block_size)
         self.finish_generation()
@@ -356,8 +358,8 @@ class RolloutEngine:
         seq_row = torch.repeat_interleave(torch.tensor(rows), torch.tensor(rl)).to(dev)
         slot = (block_tables[seq_row, (positions // bs).long()].long() * bs + (positions % bs).long())
         last_idx = (cu[1:] - 1).to(dev).long()
-        eagle = spec and getattr(self, "draft_kind", "lm") == "eagle3"
-        if eagle:  # the Eagle3 head reads the target's hidden features of every prompt position
+        eagle = spec and getattr(self, "draft_kind", "lm") in ("eagle3", "dflash")
+        if eagle:  # feature-fed drafts read the target's hidden features of every prompt position
             self.model.capture_layers, self.model.captured = self.draft.aux_layers, None
         try:
             h = self.model.forward_prefill(flat, positions, cu_d, max(rl), self.kv, slot, last_idx)
@@ -369,8 +371,9 @@ class RolloutEngine:
             from rl_b200.models.eagle3 import shift_features
 
             with torch.no_grad():
-                self.draft.prefill(self.model.embed_full(flat), shift_features(feats, cu_d), positions, cu_d, max(rl),
-                                   self.draft_kv, slot, last_idx)
+                if self.draft_kind == "eagle3":  # the block drafter keeps no draft cache
+                    self.draft.prefill(self.model.embed_full(flat), shift_features(feats, cu_d), positions, cu_d,
+                                       max(rl), self.draft_kv, slot, last_idx)
                 for r, f in zip(rows, self.draft.fuse(feats[last_idx])):
                     self._eagle_fprev_rows[r] = f  # feature of each prompt's last position
         elif spec:
@@ -465,7 +468,8 @@ class RolloutEngine:
         bt_rows = block_tables.repeat_interleave(k + 1, 0)
         temp = temperature if temperature > 0 else 0.0
         rnd = 0
-        eagle = getattr(self, "draft_kind", "lm") == "eagle3"
+        kind = getattr(self, "draft_kind", "lm")
+        eagle = kind in ("eagle3", "dflash")
         fprev = self._eagle_fprev if eagle else None  # target feature of the position before `last`
         maxlen = self.max_model_len + k + 1
         while not bool(done.all()):
@@ -473,7 +477,15 @@ class RolloutEngine:
             x = last
             drafts, dlogits = [], []
             f = fprev
+            block = self.draft.propose(self.model.embed_full(x), f, k).view(B, k, -1) if kind == "dflash" else None
             for j in range(k):
+                if block is not None:  # the block's rows were proposed together: sample each
+                    lg = block[:, j]
+                    x, _ = sample_tokens(lg, temp if temp > 0 else 1.0, 1 if temp == 0 else None, 1.0,
+                                         seed=self.seed + 17, offset=(self.calls << 24) + rnd * (k + 1) + j)
+                    drafts.append(x)
+                    dlogits.append(lg)
+                    continue
                 p = (pos0 + j).to(torch.int32)
                 slot = block_tables.gather(1, (p // bs).long().unsqueeze(1)).squeeze(1).long() * bs + (p % bs).long()
                 if eagle:  # later proposals feed back the draft's own hidden as the feature
@@ -528,7 +540,7 @@ class RolloutEngine:
                 rows_b = torch.arange(B, device=dev)
                 f_new = self.draft.fuse(vfeats[rows_b, (take - 1).clamp_min(0)])
                 fprev = torch.where((take > 0).unsqueeze(1), f_new, fprev)
-                if k > 1:
+                if k > 1 and kind == "eagle3":
                     fx_tok = out[:, : k - 1].reshape(-1)
                     fx_pos = (pos0.unsqueeze(1) + ar[1:k]).reshape(-1).to(torch.int32)
                     bt_fx = block_tables.repeat_interleave(k - 1, 0)

@@ -240,16 +240,21 @@ class PolicyWorker:
             # Eagle3 head on the policy's hidden states (the reference's policy.draft block);
             # proposals per round from generation.speculative or the vLLM-style speculative_config
             kind = str(dpol.get("speculator_type", "eagle3")).lower()
-            if kind != "eagle3":
-                raise NotImplementedError(f"draft speculator_type {kind!r} (only eagle3 is built)")
-            from rl_b200.models.eagle3 import Eagle3Draft
+            if kind not in ("eagle3", "dflash"):
+                raise NotImplementedError(f"draft speculator_type {kind!r} (eagle3 and dflash are built)")
+            from rl_b200.models.eagle3 import DFlashDraft, Eagle3Draft
 
             sc = ((gen_cfg.get("vllm_kwargs") or {}).get("speculative_config") or {})
             k = int(spec.get("num_speculative_tokens") or sc.get("num_speculative_tokens") or 3)
-            self.draft = Eagle3Draft(self.gen_model, aux_layers=dpol.get("aux_layers"), seed=seed,
-                                     ttt_steps=int(dpol.get("ttt_steps", 2)))
-            self.draft_kind = "eagle3"
+            if kind == "dflash":  # block drafter: the whole round's proposals in one forward
+                self.draft = DFlashDraft(self.gen_model, aux_layers=dpol.get("aux_layers"), seed=seed, block_size=k)
+            else:
+                self.draft = Eagle3Draft(self.gen_model, aux_layers=dpol.get("aux_layers"), seed=seed,
+                                         ttt_steps=int(dpol.get("ttt_steps", 2)))
+            self.draft_kind = kind
             self.draft_loss_weight = float(dpol.get("loss_weight", 1.0))
+            self._draft_anchor_cap = int(dpol.get("max_anchors", 2048))  # block drafter: anchors per step
+            self._draft_steps = 0
             self._draft_k = k
             self.engine.set_draft(self.draft, k)
             self._draft_opt = torch.optim.AdamW(self.draft.parameters(), lr=float(dpol.get("lr", 1e-4)))
@@ -1108,7 +1113,7 @@ class PolicyWorker:
         (``nemo_rl/models/policy/draft_config.py:64``).  Returns the loss."""
         if self.draft is None:
             return 0.0
-        if self.draft_kind == "eagle3":
+        if self.draft_kind in ("eagle3", "dflash"):
             return self._train_eagle3(data, max_tokens)
         lengths = self._lengths(data)
         rows = [r for r in range(len(lengths)) if lengths[r] > 1]
@@ -1176,8 +1181,13 @@ class PolicyWorker:
         idx = torch.arange(flat_d.numel(), device=dev)
         mask = idx + 2 < seq_end
         self.draft.train()
-        loss = self.draft.train_loss(torch.roll(emb, -1, 0), feats, torch.roll(flat_d, -2, 0), mask, pos_d, cu_d,
-                                     max_len)
+        if self.draft_kind == "dflash":
+            loss = self.draft.train_loss(torch.roll(emb, -1, 0), feats, flat_d, cu_d,
+                                         max_anchors=int(self._draft_anchor_cap), seed=self._draft_steps)
+        else:
+            loss = self.draft.train_loss(torch.roll(emb, -1, 0), feats, torch.roll(flat_d, -2, 0), mask, pos_d, cu_d,
+                                         max_len)
+        self._draft_steps += 1
         self._draft_opt.zero_grad(set_to_none=True)
         (loss * self.draft_loss_weight).backward()
         self._draft_opt.step()

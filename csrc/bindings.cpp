@@ -118,6 +118,11 @@ bool debug_bounds_build() {
 #endif
 }
 
+// nvls.cu
+void nvls_barrier(std::vector<int64_t> pad_ptrs, int64_t rank, int64_t epoch);
+void nvls_all_reduce(int64_t mc_ptr, int64_t nbytes, bool f32, int64_t rank, int64_t world);
+void nvls_reduce_shard(int64_t mc_ptr, int64_t lo, int64_t len, at::Tensor out, bool f32);
+int64_t nvls_error_flag(bool reset);
 std::vector<at::Tensor> moe_router_topk(at::Tensor logits, int64_t k);
 void ep_scatter(at::Tensor src, c10::optional<at::Tensor> src_row, at::Tensor dst_rank, at::Tensor dst_row,
                 c10::optional<at::Tensor> tags, int64_t cap, std::vector<int64_t> buf, std::vector<int64_t> tag,
@@ -207,6 +212,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm_ag", &gemm_ag, "all-gather -> GEMM: waits per gathered shard (copy-engine transfers) on device flags");
   m.def("bounds_errors", &bounds_errors, "bounds-checked debug build: error word per instrumented file (site<<40|index)");
   m.def("debug_bounds_build", &debug_bounds_build, "whether this library is the bounds-checked debug build");
+  m.def("nvls_barrier", &nvls_barrier, "bounded signal-word barrier over a multicast group's ranks");
+  m.def("nvls_all_reduce", &nvls_all_reduce, "in-place sum through NVSwitch multicast (multimem.ld_reduce / st)");
+  m.def("nvls_reduce_shard", &nvls_reduce_shard, "sum of a multicast range into a local tensor (multimem.ld_reduce)");
+  m.def("nvls_error_flag", &nvls_error_flag, "error word of the NVLS barrier waits");
   m.def("moe_router_topk", &moe_router_topk, "MoE router: softmax, top-k and the expert-grouped permutation");
   m.def("ep_scatter", &ep_scatter, "MoE token rows -> peers' receive buffers at their final positions (P2P stores)");
   m.def("ep_consume", &ep_consume, "wait for every source's scatter, copy the received rows out, acknowledge");

@@ -364,6 +364,53 @@ def bench_rollout(seqs=64, max_new=256):
           f"{t / max_new:.3f} ms per decode step (incl. prefill share)")
 
 
+def bench_longctx(seq=32768, steps=2):
+    """Long-context training on one GPU: the Llama-3.1-8B shape (random init),
+    one packed sequence of ``seq`` tokens per step (activation checkpointing,
+    GRPO clipped-PG loss, optimizer step), timed with CUDA events after a warm-up
+    step; prints step time, tokens/s, model TFLOP/s and peak memory."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.distributed.batched_data_dict import BatchedDataDict
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+    from rl_b200.parallel.state import single_process_state
+    from rl_b200.utils.flops import forward_flops
+
+    dev = torch.device("cuda", 0)
+    mcfg = get_model_config("llama3.1-8b")
+    pcfg = {"model_name": "llama3.1-8b", "max_total_sequence_length": seq, "precision": "bfloat16",
+            "train_global_batch_size": 1, "max_grad_norm": 1.0,
+            "optimizer": {"kwargs": {"lr": 1e-7, "weight_decay": 0.0}},
+            "megatron_cfg": {"activation_checkpointing": True},
+            "generation": {"max_new_tokens": 8, "mcore_generation_config": {"block_size_tokens": 256}},
+            "sequence_packing": {"train_mb_tokens": seq, "logprob_mb_tokens": seq}}
+    w = PolicyWorker(pcfg, model_cfg=mcfg, pstate=single_process_state(dev), seed=1234, init_reference_model=False)
+    g = torch.Generator().manual_seed(0)
+    ids = torch.randint(0, mcfg.vocab_size, (1, seq), generator=g)
+    tm = torch.zeros(1, seq)
+    tm[0, seq // 8:] = 1.0
+    lp = -torch.rand(1, seq, generator=g) * tm
+    data = BatchedDataDict({"input_ids": ids, "input_lengths": torch.tensor([seq]), "advantages": tm * 0.5,
+                            "generation_logprobs": lp, "prev_logprobs": lp.clone(), "token_mask": tm,
+                            "sample_mask": torch.ones(1)})
+    lf = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
+    w.train(data, lf)
+    torch.cuda.synchronize()
+    torch.cuda.reset_peak_memory_stats()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(steps):
+        res = w.train(data, lf)
+    e1.record()
+    torch.cuda.synchronize()
+    t = e0.elapsed_time(e1) / steps / 1e3
+    fl = 3.0 * forward_flops(mcfg, [seq])  # forward + backward
+    print(f"longctx seq={seq}: {t * 1e3:.0f} ms per step, {seq / t:.0f} tokens/s, "
+          f"{fl / t / 1e12:.0f} model TFLOP/s (fwd+bwd, recompute excluded), "
+          f"peak {torch.cuda.max_memory_allocated() / 2**30:.1f} GiB, loss {res['loss']:.4f}, "
+          f"grad_norm {res['grad_norm']:.3f}")
+
+
 def main(argv=None):
     argv = list(sys.argv[1:] if argv is None else argv)
     what = argv.pop(0) if argv else "gemm"
@@ -371,7 +418,7 @@ def main(argv=None):
     torch.manual_seed(0)
     {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
      "logprob": bench_logprob, "lmhead": bench_lmhead, "lmhead_fwd": bench_lmhead_fwd, "fp8": bench_fp8, "numerics": bench_numerics,
-     "rollout": bench_rollout}[what](*args)
+     "rollout": bench_rollout, "longctx": bench_longctx}[what](*args)
 
 
 if __name__ == "__main__":

@@ -52,6 +52,7 @@ _KERNELS_PER_CALL = {
     "moe_router_topk": 3,
     "bounds_errors": 0,
     "dp_error_flag": 0,
+    "nvls_error_flag": 0,
     "debug_bounds_build": 0,
 }
 
@@ -127,7 +128,7 @@ def use_native(*tensors: torch.Tensor) -> bool:
 # every kernel family's device error word (set when a bounded wait runs out)
 ERROR_FLAGS = ("gemm_error_flag", "gemm_sm100_error_flag", "gemm_fp8_error_flag", "grouped_gemm_error_flag",
                "gemm_decode_error_flag", "decode_ar_error_flag", "attn_error_flag", "attn_tc_error_flag",
-               "ep_error_flag", "dp_error_flag")
+               "ep_error_flag", "dp_error_flag", "nvls_error_flag")
 
 
 BOUNDS_SITES = {1: "KV-cache slot", 2: "paged-attention block-table entry",

@@ -393,6 +393,9 @@ def bench_longctx(seq=32768, steps=2):
     data = BatchedDataDict({"input_ids": ids, "input_lengths": torch.tensor([seq]), "advantages": tm * 0.5,
                             "generation_logprobs": lp, "prev_logprobs": lp.clone(), "token_mask": tm,
                             "sample_mask": torch.ones(1)})
+    # rollout-consistent log-probs (ratio 1 at the first step), so the update is a real one
+    cur = w.get_logprobs(data)["logprobs"].float().cpu() * tm
+    data["generation_logprobs"], data["prev_logprobs"] = cur, cur.clone()
     lf = ClippedPGLossFn({"reference_policy_kl_penalty": 0.0})
     w.train(data, lf)
     torch.cuda.synchronize()

@@ -222,10 +222,11 @@ def test_prompt_dedup_and_chunked_prefill_on_gpu(cuda_device):
     assert same > 0.9, same
 
 
-def test_eagle3_speculative_rollout_on_gpu(cuda_device):
-    """Eagle3 head on the GPU (bf16): speculative greedy rollouts agree with plain
-    greedy rollouts, and a few online draft steps on the policy's rollouts raise
-    the number of tokens emitted per verification round."""
+@pytest.mark.parametrize("kind", ["eagle3", "dflash"])
+def test_eagle3_speculative_rollout_on_gpu(cuda_device, kind):
+    """Eagle3 head / block drafter on the GPU (bf16): speculative greedy rollouts
+    agree with plain greedy rollouts, and a few online draft steps on the policy's
+    rollouts raise the number of tokens emitted per verification round."""
     from rl_b200.models.policy.worker import PolicyWorker
     from rl_b200.parallel.state import single_process_state
 
@@ -233,7 +234,7 @@ def test_eagle3_speculative_rollout_on_gpu(cuda_device):
         cfg = _policy_cfg(new=32)
         if draft:
             cfg["generation"]["speculative"] = {"num_speculative_tokens": 3}
-            cfg["draft"] = {"enabled": True, "speculator_type": "eagle3", "lr": 2e-3}
+            cfg["draft"] = {"enabled": True, "speculator_type": kind, "lr": 2e-3}
         return PolicyWorker(cfg, model_cfg=SMALL, pstate=single_process_state(cuda_device), seed=6)
 
     g = torch.Generator().manual_seed(0)

@@ -239,6 +239,8 @@ class SingleController:
             if w.attempts[kind] >= self.failure.budget(kind):
                 self.stats["prompts_skipped"] += 1
                 self._dropped_since_step += 1
+                if self.ledger is not None:
+                    self.ledger.discard([w.gid])  # dropped for good: not regenerated after a restart
                 log.warning("prompt group %s dropped after %d %s failures: %s", w.gid, w.attempts[kind], kind, exc)
                 if self.stats["prompts_skipped"] > self.failure.max_skipped_prompts:
                     raise RuntimeError(f"{self.stats['prompts_skipped']} prompt groups skipped, more than "

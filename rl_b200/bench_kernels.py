@@ -80,6 +80,19 @@ def bench_decode(B=64, L=1024, nkv=8, G=4, hd=128, bs=256):
     print(f"paged_decode B={B} L={L}: {t * 1e3:.1f} us {byts / (t * 1e-3) / 1e12:.2f} TB/s")
 
 
+def bench_router(T=16384, E=128, k=8):
+    """MoE router kernel (softmax, top-k, counts, stable expert-grouped order)
+    against the PyTorch ops it replaces (softmax, topk, bincount, stable argsort)."""
+    from rl_b200.ops.moe_router import router_topk, router_topk_ref
+
+    logits = torch.randn(T, E, device="cuda")
+    t_n = _time(lambda: router_topk(logits, k), reps=50)
+    t_r = _time(lambda: router_topk_ref(logits, k), reps=50)
+    byts = T * E * 4 * 2 + T * k * 8 * 3  # logits read + probs written, ids / order / pos
+    print(f"router T={T} E={E} k={k}: native {t_n * 1e3:.1f} us ({byts / (t_n * 1e-3) / 1e9:.0f} GB/s), "
+          f"torch {t_r * 1e3:.1f} us, speed-up {t_r / t_n:.2f}x")
+
+
 def bench_decode_gemm(M=64):
     """The Llama-3.1-8B linear layers at decode batch M (weight-streaming bound):
     time and achieved weight bandwidth per projection.  Each timed call reads a
@@ -421,7 +434,7 @@ def main(argv=None):
     torch.manual_seed(0)
     {"gemm": bench_gemm, "decode": bench_decode, "decode_gemm": bench_decode_gemm, "attn": bench_attn,
      "logprob": bench_logprob, "lmhead": bench_lmhead, "lmhead_fwd": bench_lmhead_fwd, "fp8": bench_fp8, "numerics": bench_numerics,
-     "rollout": bench_rollout, "longctx": bench_longctx}[what](*args)
+     "rollout": bench_rollout, "longctx": bench_longctx, "router": bench_router}[what](*args)
 
 
 if __name__ == "__main__":

@@ -183,3 +183,24 @@ def test_grpo_through_the_single_controller(tmp_path):
                   "logger.log_dir=" + str(tmp_path / "logs"), "logger.stdout=false",
                   "++grpo.single_controller.enabled=true", "++grpo.single_controller.max_inflight_prompts=4"])
     assert state["current_step"] == 2 and state["single_controller"]["groups_generated"] >= 16
+
+
+def test_controller_keeps_the_rollout_ledger():
+    """With a recovery ledger every trained group is consumed, a dropped prompt is
+    forgotten, and nothing stays in flight after the run."""
+    from rl_b200.experience.rollout_recovery import RolloutRecoveryLedger
+
+    def fail(idx):
+        if 1 in idx:
+            raise RolloutDataError("bad")
+
+    ledger = RolloutRecoveryLedger()
+    sc = SingleController(_fake_generate([], fail), _fake_train([]), _loader(6, per_batch=1), group_size=2,
+                          groups_per_step=2, max_steps=2, ledger=ledger,
+                          cfg={"max_inflight_prompts": 1,
+                               "rollout_failure": {"backoff_base_s": 0.0, "max_data_attempts_per_prompt": 1,
+                                                   "max_skipped_prompts": 1}})
+    sc.run()
+    live = {g.status.value for g in ledger.groups}
+    buffered = len(sc._ready)
+    assert len(ledger) == buffered and (not live or live == {"sealed"}), (len(ledger), buffered, live)

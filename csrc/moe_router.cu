@@ -5,13 +5,13 @@
 //                        warp max / sum for the softmax (probabilities written),
 //                        k rounds of a warp arg-max (ties -> the lower expert id),
 //                        and a per-block histogram of the chosen experts.
-//   router_scan_kernel   per expert, an exclusive scan of the block histograms
-//                        over the blocks (each block's first slot inside the
-//                        expert's range), the expert totals and the exclusive scan
-//                        of the totals (each expert's first row).
-//   router_pos_kernel    per block, each assignment's rank among the block's
-//                        earlier assignments to the same expert; its row in the
-//                        expert-grouped order is expert start + block start + rank.
+//   router_scan_kernel   one CTA per expert: an exclusive scan of the block
+//                        histograms over the blocks (each block's first slot
+//                        inside the expert's range) and the expert total.
+//   router_pos_kernel    per block, the experts' first rows (a scan of the totals
+//                        in shared memory), then each assignment's rank among the
+//                        block's earlier assignments to the same expert; its row in
+//                        the expert-grouped order is expert start + block start + rank.
 //
 // The result is the stable sort of the flattened [T*k] expert ids (the order a
 // stable argsort gives): assignments grouped by expert, in token order inside an
@@ -95,42 +95,57 @@ router_topk_kernel(const float* __restrict__ logits, int T, int E, int k, float*
   for (int e = threadIdx.x; e < E; e += blockDim.x) block_counts[(long long)blockIdx.x * E + e] = s_cnt[e];
 }
 
-// One block, one thread per expert (E <= 1024).
-__global__ void router_scan_kernel(int* __restrict__ block_counts, int nblk, int E, int* __restrict__ counts,
-                                   int* __restrict__ expert_start) {
-  __shared__ int s_tot[1024];
-  const int e = threadIdx.x;
-  int run = 0;
-  if (e < E) {
-    for (int b = 0; b < nblk; ++b) {
-      int* p = block_counts + (long long)b * E + e;
-      const int c = *p;
-      *p = run;
-      run += c;
-    }
-    counts[e] = run;
-    s_tot[e] = run;
-  }
+// One block per expert: exclusive scan of the expert's per-block counts over the
+// blocks (each thread sums a contiguous run of blocks, a shared-memory scan of
+// the run totals, then each thread writes its run's bases) and the expert total.
+constexpr int kScanThreads = 256;
+
+__global__ void __launch_bounds__(kScanThreads)
+router_scan_kernel(int* __restrict__ block_counts, int nblk, int E, int* __restrict__ counts) {
+  __shared__ int s_run[kScanThreads];
+  const int e = blockIdx.x, t = threadIdx.x;
+  const int per = (nblk + kScanThreads - 1) / kScanThreads;
+  const int b0 = t * per, b1 = min(nblk, b0 + per);
+  int sum = 0;
+  for (int b = b0; b < b1; ++b) sum += block_counts[(long long)b * E + e];
+  s_run[t] = sum;
   __syncthreads();
-  if (e == 0) {
-    int acc = 0;
-    for (int x = 0; x < E; ++x) {
-      const int c = s_tot[x];
-      s_tot[x] = acc;
-      acc += c;
-    }
+  // inclusive Hillis-Steele scan of the run totals
+  for (int off = 1; off < kScanThreads; off <<= 1) {
+    const int v = t >= off ? s_run[t - off] : 0;
+    __syncthreads();
+    s_run[t] += v;
+    __syncthreads();
   }
-  __syncthreads();
-  if (e < E) expert_start[e] = s_tot[e];
+  int run = t == 0 ? 0 : s_run[t - 1];
+  for (int b = b0; b < b1; ++b) {
+    int* p = block_counts + (long long)b * E + e;
+    const int c = *p;
+    *p = run;
+    run += c;
+  }
+  if (t == kScanThreads - 1) counts[e] = s_run[t];
 }
 
 __global__ void __launch_bounds__(256)
 router_pos_kernel(const int64_t* __restrict__ ids, long long TK, int k, int E, const int* __restrict__ block_base,
-                  const int* __restrict__ expert_start, int64_t* __restrict__ order, int64_t* __restrict__ pos) {
-  extern __shared__ int s_e[];  // the block's assignments' experts
+                  const int* __restrict__ counts, int64_t* __restrict__ order, int64_t* __restrict__ pos) {
+  extern __shared__ int s_mem[];  // [E] expert starts, then the block's assignments' experts
+  int* expert_start = s_mem;
+  int* s_e = s_mem + E;
   const long long a0 = (long long)blockIdx.x * kWarps * k;
   const int n = (int)min((long long)kWarps * k, TK - a0);
   for (int i = threadIdx.x; i < n; i += blockDim.x) s_e[i] = (int)ids[a0 + i];
+  for (int x = threadIdx.x; x < E; x += blockDim.x) expert_start[x] = counts[x];
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive scan of the expert totals in shared memory (E <= 1024)
+    int acc = 0;
+    for (int x = 0; x < E; ++x) {
+      const int c = expert_start[x];
+      expert_start[x] = acc;
+      acc += c;
+    }
+  }
   __syncthreads();
   for (int i = threadIdx.x; i < n; i += blockDim.x) {
     const int e = s_e[i];
@@ -172,7 +187,6 @@ std::vector<at::Tensor> moe_router_topk(at::Tensor logits, int64_t k) {
   if (T == 0) return {probs, ids, counts, order, pos};
   const int nblk = (T + kWarps - 1) / kWarps;
   auto bc = at::empty({nblk, E}, o32);
-  auto start = at::empty({E}, o32);
   const float* lp = logits.data_ptr<float>();
   float* pp = probs.data_ptr<float>();
   int64_t* ip = ids.data_ptr<int64_t>();
@@ -185,11 +199,10 @@ std::vector<at::Tensor> moe_router_topk(at::Tensor logits, int64_t k) {
   else if (npl <= 16) launch_topk<16>(lp, T, E, k, pp, ip, bp, nblk);
   else launch_topk<32>(lp, T, E, k, pp, ip, bp, nblk);
   RLB_CUDA_CHECK(cudaGetLastError());
-  router_scan_kernel<<<1, ((E + 31) / 32) * 32, 0, stream()>>>(bp, nblk, E, counts.data_ptr<int>(),
-                                                             start.data_ptr<int>());
+  router_scan_kernel<<<E, kScanThreads, 0, stream()>>>(bp, nblk, E, counts.data_ptr<int>());
   RLB_CUDA_CHECK(cudaGetLastError());
-  router_pos_kernel<<<nblk, 256, kWarps * k * sizeof(int), stream()>>>(
-      ip, (long long)T * k, (int)k, E, bp, start.data_ptr<int>(), order.data_ptr<int64_t>(), pos.data_ptr<int64_t>());
+  router_pos_kernel<<<nblk, 256, (E + kWarps * k) * sizeof(int), stream()>>>(
+      ip, (long long)T * k, (int)k, E, bp, counts.data_ptr<int>(), order.data_ptr<int64_t>(), pos.data_ptr<int64_t>());
   RLB_CUDA_CHECK(cudaGetLastError());
   return {probs, ids, counts, order, pos};
 }

@@ -122,7 +122,9 @@ def init_distributed(tp: int = 1, cp: int = 1, ep: int = 1, pp: int = 1, backend
 
     def make(groups: list[list[int]], attr: str, ranks_attr: Optional[str] = None):
         for g in groups:
-            pg = dist.new_group(g, backend=backend)
+            # the job's timeout, not the library default: ranks that wait on a lost
+            # peer in a sub-group collective end with an error instead of hanging
+            pg = dist.new_group(g, backend=backend, timeout=datetime.timedelta(seconds=timeout_s))
             if rank in g:
                 setattr(st, attr, pg)
                 if ranks_attr:

@@ -634,8 +634,8 @@ def test_pipeline_parallel_train_2gpu():
         assert o["lp_err"] < 0.15, o
 
 
-@pytest.mark.skip(reason="16 MiB stage messages on two B200s stopped progressing (no NCCL work timed out, so the "
-                         "ranks were blocked on the host); the same schedule over gloo completes; cause not found")
+@pytest.mark.skip(reason="16 MiB stage messages on two B200s stopped progressing within the test's limit; the same "
+                         "schedule over gloo completes; cause not found")
 @pytest.mark.parametrize("vpp", [1, 2])
 def test_pipeline_parallel_large_messages_2gpu(vpp):
     """16 MiB activations (above NCCL's channel buffer) through 1F1B and the

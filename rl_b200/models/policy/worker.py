@@ -190,6 +190,9 @@ class PolicyWorker:
                                    symmetric=self.symmetric if fused_dp else None,
                                    pp_group=self.ps.pp_group if self.pp > 1 else None,
                                    muon=MuonConfig.from_megatron(mopt) if self.lora is None else None)
+        if mc.get("freeze_moe_router", False) and self.model_cfg.is_moe:
+            # the reference's GRPO default: routers keep their initial weights
+            self.optimizer.freeze(lambda name: name.endswith("mlp.gate.weight"))
         # overlap_grad_reduce: data-parallel gradient reduction per decoder layer during
         # the backward of a step's last micro-batch (fused DP path)
         ddp = mc.get("distributed_data_parallel_config") or {}
@@ -240,14 +243,20 @@ class PolicyWorker:
             # Eagle3 head on the policy's hidden states (the reference's policy.draft block);
             # proposals per round from generation.speculative or the vLLM-style speculative_config
             kind = str(dpol.get("speculator_type", "eagle3")).lower()
-            if kind not in ("eagle3", "dflash"):
-                raise NotImplementedError(f"draft speculator_type {kind!r} (eagle3 and dflash are built)")
+            if kind not in ("eagle3", "dflash", "mtp"):
+                raise NotImplementedError(f"draft speculator_type {kind!r} (eagle3, dflash and mtp are built)")
             from rl_b200.models.eagle3 import DFlashDraft, Eagle3Draft
 
             sc = ((gen_cfg.get("vllm_kwargs") or {}).get("speculative_config") or {})
             k = int(spec.get("num_speculative_tokens") or sc.get("num_speculative_tokens") or 3)
             if kind == "dflash":  # block drafter: the whole round's proposals in one forward
                 self.draft = DFlashDraft(self.gen_model, aux_layers=dpol.get("aux_layers"), seed=seed, block_size=k)
+            elif kind == "mtp":
+                # multi-token-prediction head: the last layer's hidden state and the next
+                # token's embedding through one decoder layer (the Eagle3 head on one feature)
+                self.draft = Eagle3Draft(self.gen_model, aux_layers=(self.model_cfg.num_layers - 1,), seed=seed,
+                                         ttt_steps=int(dpol.get("ttt_steps", 1)))
+                kind = "eagle3"
             else:
                 self.draft = Eagle3Draft(self.gen_model, aux_layers=dpol.get("aux_layers"), seed=seed,
                                          ttt_steps=int(dpol.get("ttt_steps", 2)))

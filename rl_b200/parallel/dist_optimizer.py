@@ -187,6 +187,7 @@ class FlatAdamW:
                     # in the norm; whole experts without an FFN split are replicated too
                     rep_r.append((a - seg.s_lo, b - seg.s_lo, sp.tp_dim is None))
             seg.wd_ranges = _merge(wd_r)
+            seg.frozen_ranges = []
             seg.rep_ranges = [(a, b) for a, b, f in _merge(rep_r) if f]
             nd = [(a, b) for a, b, d in seg.wd_ranges if not d]
             seg.nodecay_dev = torch.tensor(nd if nd else [[seg.shard, seg.shard]], dtype=torch.int64,
@@ -269,6 +270,40 @@ class FlatAdamW:
             if p.grad is not None:
                 p.main_grad.add_(p.grad.float())
                 p.grad = None
+
+    # ------------------------------------------------------------ freezing
+    def freeze(self, pred) -> int:
+        """Freeze the parameters whose name satisfies ``pred`` (e.g. MoE routers
+        under ``freeze_moe_router``): their gradients are zeroed after the
+        data-parallel reduction (they count neither in the clip norm nor in the
+        moments) and they take no weight decay, so AdamW leaves them unchanged.
+        Returns the number of frozen elements in this rank's shards."""
+        n = 0
+        for seg in self.segments:
+            fr = []
+            for sp, _ in self.model.named_flat_params():
+                if not pred(sp.name):
+                    continue
+                a, b = max(sp.offset, seg.s_lo), min(sp.offset + sp.numel, seg.s_hi)
+                if a < b:
+                    fr.append((a - seg.s_lo, b - seg.s_lo, False))
+            if not fr:
+                continue
+            seg.frozen_ranges = [(a, b) for a, b, _ in _merge(fr)]
+            n += sum(b - a for a, b in seg.frozen_ranges)
+            # split the decay ranges so the frozen ones take no decay
+            cuts = sorted({x for a, b in seg.frozen_ranges for x in (a, b)})
+            out = []
+            for a, b, d in seg.wd_ranges:
+                pts = [a] + [c for c in cuts if a < c < b] + [b]
+                for lo, hi in zip(pts[:-1], pts[1:]):
+                    frozen = any(fa <= lo and hi <= fb for fa, fb in seg.frozen_ranges)
+                    out.append((lo, hi, d and not frozen))
+            seg.wd_ranges = _merge(out)
+            nd = [(a, b) for a, b, d in seg.wd_ranges if not d]
+            seg.nodecay_dev = torch.tensor(nd if nd else [[seg.shard, seg.shard]], dtype=torch.int64,
+                                           device=self.device).view(-1, 2)
+        return n
 
     # ------------------------------------ reduction overlapped with backward
     def setup_overlap(self, layer_of) -> bool:
@@ -410,6 +445,11 @@ class FlatAdamW:
                 # per-rank gradients are partial sums: reduce with SUM, not mean.
                 dist.reduce_scatter_tensor(seg.grad_shard, self.main_grad[seg.lo:seg.hi], group=seg.group)
             g = seg.grad_shard
+            if seg.frozen_ranges:
+                for a, b in seg.frozen_ranges:
+                    g[a:b].zero_()
+                if seg.sharded and fused:
+                    sq_all = sum_of_squares(g)  # the fused partials included the frozen gradients
             if not (seg.sharded and fused):
                 sq_all = sum_of_squares(g)
             if self.tp > 1:
@@ -475,6 +515,8 @@ class FlatAdamW:
         cfg = self.muon
         mu = cfg.momentum
         for sp, a, b in seg.muon_params:
+            if any(fa <= a and b <= fb for fa, fb in seg.frozen_ranges):
+                continue  # frozen (e.g. MoE router): no update
             shape = sp.shape
             g = seg.grad_shard[a:b].view(shape) * grad_scale
             buf = seg.exp_avg[a:b].view(shape)

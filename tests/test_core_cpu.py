@@ -924,3 +924,26 @@ def test_overlapped_reduction_bookkeeping():
     assert opt._overlap_rest(seg) == [(lo, lo + 64), (lo + 128, lo + 256), (lo + 320, hi)]
     opt._ov["done"] = set()
     assert opt._overlap_rest(seg) == [(lo, hi)]
+
+
+def test_freeze_moe_router_keeps_router_weights():
+    """``megatron_cfg.freeze_moe_router``: a training step moves the experts and
+    attention but leaves every router weight bit-identical (no gradient, no
+    weight decay)."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.policy.worker import PolicyWorker
+    from tests.dist_cases import TINY_MOE, make_batch
+
+    pcfg = {"max_total_sequence_length": 32, "precision": "float32", "train_global_batch_size": 8,
+            "optimizer": {"kwargs": {"lr": 1e-2, "weight_decay": 0.1}},
+            "megatron_cfg": {"freeze_moe_router": True},
+            "generation": {"temperature": 1.0, "max_new_tokens": 4},
+            "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
+    w = PolicyWorker(pcfg, model_cfg=TINY_MOE, seed=3)
+    before = {n: p.detach().clone() for n, p in w.model._params.items()}
+    w.train(make_batch(B=8, S=24), ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}))
+    for n, p in w.model._params.items():
+        if n.endswith("mlp.gate.weight"):
+            assert torch.equal(p, before[n]), n
+    moved = [n for n, p in w.model._params.items() if not torch.equal(p, before[n])]
+    assert any("experts" in n for n in moved) and any("qkv" in n for n in moved)

@@ -55,3 +55,18 @@ def test_eagle3_online_training_raises_acceptance():
     after = acceptance()
     assert losses[-1] < 0.5 * losses[0], losses[::8]
     assert after > before + 0.1, (before, after)
+
+
+def test_mtp_head_speculation_is_exact():
+    """``speculator_type: mtp``: the head reads only the last layer's features."""
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+
+    pcfg = {"max_total_sequence_length": 80, "precision": "float32", "train_global_batch_size": 8,
+            "generation": {"temperature": 1.0, "max_new_tokens": 24, "speculative": {"num_speculative_tokens": 2},
+                           "mcore_generation_config": {"block_size_tokens": 16}},
+            "draft": {"enabled": True, "speculator_type": "mtp"}}
+    w = PolicyWorker(pcfg, model_cfg=get_model_config("tiny-llama"), seed=3)
+    assert w.draft.aux_layers == (get_model_config("tiny-llama").num_layers - 1,)
+    plain = _worker(False).generate(_prompts(), greedy=True)
+    assert torch.equal(w.generate(_prompts(), greedy=True)["output_ids"], plain["output_ids"])

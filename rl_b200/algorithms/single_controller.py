@@ -459,7 +459,6 @@ def single_controller_train(policy, dataloader, task_to_env: dict, master_config
     ``grpo.async_grpo.max_trajectory_age_steps``).  ``generate_fn`` replaces the
     multi-turn rollout (tests use it to inject failures and delays)."""
     from rl_b200.algorithms.advantage_estimator import make_advantage_estimator
-    from rl_b200.algorithms.async_grpo import replay_buffer_file  # noqa: F401  (same per-rank naming)
     from rl_b200.algorithms.async_utils import groups_to_batch
     from rl_b200.algorithms.grpo import DEFAULT_GRPO_CONFIG, GRPOSaveState, build_train_data
     from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn

@@ -222,6 +222,13 @@ class PolicyWorker:
 
             self.gen_model = TransformerLM(self.model_cfg, single_process_state(self.device), device=self.device,
                                            dtype=self.dtype, skip_init=True)
+        self._expert_bias_rate = 0.0
+        if mc.get("moe_router_enable_expert_bias", False) and self.model_cfg.is_moe:
+            # aux-loss-free load balancing: the rollout copy must route with the same bias
+            if self.gen_model is not self.model:
+                raise NotImplementedError("moe_router_enable_expert_bias with a different rollout layout")
+            self.model.enable_expert_bias()
+            self._expert_bias_rate = float(mc.get("moe_router_bias_update_rate", 1e-3) or 0.0)
         self.weight_sync = self._make_weight_sync(resharded)
         kv_dt = str(vcfg.get("kv_cache_dtype", gen_cfg.get("kv_cache_dtype", "auto"))).lower()
         self._engine_spec = dict(
@@ -806,6 +813,7 @@ class PolicyWorker:
         gbs = gbs or B
         all_metrics: list[dict] = []
         losses, grad_norms, lrs = [], [], []
+        step_extra: dict = {}
         dev_data = None
         for g0 in range(0, B, gbs):
             st = self.begin_train_step(data, loss_fn, rows=range(g0, min(B, g0 + gbs)), eval_mode=eval_mode,
@@ -814,6 +822,7 @@ class PolicyWorker:
             for i in range(st.num_microbatches):
                 self.train_microbatch(st, i)
             res = self.finish_train_step(st, release_grad=False, aggregate=False)
+            step_extra = {k: v for k, v in res.items() if k.startswith("moe/")}
             losses.append(res["loss"])
             if not eval_mode:
                 grad_norms.append(res["grad_norm"])
@@ -824,6 +833,7 @@ class PolicyWorker:
         agg = aggregate_metrics(all_metrics, self._metric_group())
         if self.pp > 1:
             agg = self._pp_share_metrics(agg)
+        agg.update(step_extra)  # per-step extras of the last step (expert-bias load ratios)
         agg.update({"loss": sum(losses) / max(1, len(losses)), "global_loss": losses,
                     "grad_norm": grad_norms[-1] if grad_norms else 0.0, "lr": lrs[-1] if lrs else 0.0,
                     "moe_aux_loss": self.model.aux_loss()})
@@ -998,6 +1008,9 @@ class PolicyWorker:
         if not st.eval_mode:
             opt_stats = self.optimizer.step()
             out.update(grad_norm=opt_stats["grad_norm"], lr=opt_stats["lr"])
+            if self._expert_bias_rate > 0:
+                out.update(self.model.update_expert_bias(
+                    self._expert_bias_rate, self.ps.dp_cp_group if self.ps.cp_size > 1 else self.ps.dp_group))
         else:
             self.optimizer.zero_grad()
         red = self._metric_group()

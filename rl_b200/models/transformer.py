@@ -274,6 +274,11 @@ class TransformerLM(nn.Module):
         # router_record: layer -> [T, k] expert ids chosen (device tensors)
         self.router_replay: Optional[dict] = None
         self.router_record: Optional[dict] = None
+        # aux-loss-free load balancing: per-layer expert bias added to the routing
+        # scores for the top-k choice only; tokens per expert of the training
+        # forwards are accumulated for the bias update (enable_expert_bias)
+        self.expert_bias: Optional[dict] = None
+        self._expert_load: dict = {}
         # fp8 rollout: name -> (e4m3 weight, block scales) used by the rollout
         # forwards only (forward_prefill / forward_decode); power-of-two scales in
         # the MN-major layout of the hardware-scaled GEMM when fp8_pow2, else
@@ -642,6 +647,34 @@ class TransformerLM(nn.Module):
         a = swiglu(gu)
         return self._row_parallel_linear(a, self._params[p + "mlp.down_proj.weight"], p + "mlp.down_proj.weight")
 
+    def enable_expert_bias(self) -> None:
+        """Aux-loss-free load balancing (Megatron's ``moe_router_enable_expert_bias``):
+        a zero fp32 bias per MoE layer of this rank's stage."""
+        E = self.cfg.num_experts
+        dev = self.flat_param.device
+        self.expert_bias = {i: torch.zeros(E, dtype=torch.float32, device=dev) for i in self.layer_range}
+        self._expert_load = {}
+
+    @torch.no_grad()
+    def update_expert_bias(self, rate: float, group=None) -> dict:
+        """After an optimizer step: ``bias += rate * sign(mean load - load)`` per
+        layer, the tokens per expert summed over ``group`` (the ranks routing
+        different tokens); returns the max / min relative load for metrics."""
+        import torch.distributed as dist
+
+        if self.expert_bias is None or not self._expert_load:
+            return {}
+        worst, best = 0.0, float("inf")
+        for i, load in self._expert_load.items():
+            if group is not None and dist.is_initialized() and dist.get_world_size(group) > 1:
+                dist.all_reduce(load, group=group)
+            mean = load.mean()
+            self.expert_bias[i] += rate * torch.sign(mean - load)
+            rel = load / mean.clamp_min(1e-9)
+            worst, best = max(worst, float(rel.max())), min(best, float(rel.min()))
+        self._expert_load = {}
+        return {"moe/max_load_ratio": worst, "moe/min_load_ratio": best}
+
     def route(self, i: int, h: torch.Tensor):
         """Router: fp32 logits -> softmax -> top-k (+ renormalisation); returns
         (topk_weights [T,k] fp32, topk_ids [T,k] int64, probs [T,E] fp32, perm),
@@ -662,6 +695,12 @@ class TransformerLM(nn.Module):
             ids = torch.topk(probs, c.moe_top_k, dim=-1)[1]
             ids = torch.where(rep[:, :1] >= 0, rep, ids)
             vals = probs.gather(-1, ids)
+        elif self.expert_bias is not None:
+            # selection on the biased scores, gating weights from the unbiased ones
+            probs = torch.softmax(logits, -1)
+            bias = self.expert_bias[i].to(probs.dtype)
+            ids = torch.topk(probs.detach() + bias, c.moe_top_k, dim=-1)[1]
+            vals = probs.gather(-1, ids)
         elif logits.is_cuda and rdtype == torch.float32:
             # one native pass: softmax, top-k, per-expert counts and the grouped order
             probs, ids, counts, order = router_topk(logits, c.moe_top_k)
@@ -672,6 +711,9 @@ class TransformerLM(nn.Module):
             vals, ids = torch.topk(probs, c.moe_top_k, dim=-1)
         if self.router_record is not None:
             self.router_record[i] = ids.detach().to(torch.int16 if c.num_experts < 32768 else torch.int32)
+        if self.expert_bias is not None and torch.is_grad_enabled():
+            load = torch.bincount(ids.detach().reshape(-1), minlength=c.num_experts).float()
+            self._expert_load[i] = self._expert_load[i] + load if i in self._expert_load else load
         if c.moe_norm_topk_prob:
             vals = vals / vals.sum(-1, keepdim=True)
         return vals.to(torch.float32), ids, probs.to(torch.float32), perm

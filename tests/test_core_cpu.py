@@ -947,3 +947,34 @@ def test_freeze_moe_router_keeps_router_weights():
             assert torch.equal(p, before[n]), n
     moved = [n for n, p in w.model._params.items() if not torch.equal(p, before[n])]
     assert any("experts" in n for n in moved) and any("qkv" in n for n in moved)
+
+
+def test_expert_bias_load_balancing():
+    """``moe_router_enable_expert_bias``: the bias starts at zero, moves against
+    each expert's load after every step (overloaded experts down), steers the
+    top-k choice, and never enters the gating weights."""
+    from rl_b200.algorithms.loss.loss_functions import ClippedPGLossFn
+    from rl_b200.models.policy.worker import PolicyWorker
+    from tests.dist_cases import TINY_MOE, make_batch
+
+    pcfg = {"max_total_sequence_length": 32, "precision": "float32", "train_global_batch_size": 8,
+            "optimizer": {"kwargs": {"lr": 1e-4}},
+            "megatron_cfg": {"moe_router_enable_expert_bias": True, "moe_router_bias_update_rate": 0.01},
+            "generation": {"temperature": 1.0, "max_new_tokens": 4},
+            "sequence_packing": {"train_mb_tokens": 64, "logprob_mb_tokens": 64}}
+    w = PolicyWorker(pcfg, model_cfg=TINY_MOE, seed=3)
+    m = w.model
+    assert all(float(b.abs().sum()) == 0 for b in m.expert_bias.values())
+    res = w.train(make_batch(B=8, S=24), ClippedPGLossFn({"reference_policy_kl_penalty": 0.0}))
+    assert "moe/max_load_ratio" in res and res["moe/max_load_ratio"] >= 1.0
+    b0 = m.expert_bias[0]
+    assert float(b0.abs().max()) == pytest.approx(0.01) and float(b0.max()) > 0 > float(b0.min())
+    # selection follows the bias, weights do not
+    h = torch.randn(16, TINY_MOE.hidden_size)
+    with torch.no_grad():
+        m.expert_bias[0] = torch.zeros(TINY_MOE.num_experts)
+        m.expert_bias[0][3] = 10.0  # expert 3 always chosen
+        vals, ids, probs, _ = m.route(0, h)
+    assert bool((ids == 3).any(1).all())
+    raw = probs.gather(-1, ids)
+    torch.testing.assert_close(vals, raw / raw.sum(-1, keepdim=True))

@@ -282,13 +282,20 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
     adv_cfg.setdefault("normalize_rewards", cfg["normalize_rewards"])
     adv_cfg.setdefault("use_leave_one_out_baseline", cfg["use_leave_one_out_baseline"])
     estimator = make_advantage_estimator(adv_cfg, loss_cfg)
-    from rl_b200.algorithms.opd import build_teacher_router, is_opd_enabled, routing_keys
+    from rl_b200.algorithms.opd import build_teacher_router, get_opd_full_config, is_opd_enabled, routing_keys
 
     opd = is_opd_enabled(master_config) or adv_cfg.get("name") == "opd"
+    opd_full = get_opd_full_config(master_config) if opd else None
     if opd:
         if adv_cfg.get("name") != "opd":
             estimator = make_advantage_estimator({**adv_cfg, "name": "opd"}, loss_cfg)
         teacher_router = teacher_router or build_teacher_router(master_config, policy)
+    if opd_full is not None:
+        # full-vocabulary MOPD: exact reverse KL to the routed teacher's distribution
+        from rl_b200.algorithms.loss.loss_functions import DistillationLossFn
+
+        loss_fn = DistillationLossFn({"kl_type": "reverse"})
+        full_k = int(opd_full.get("top_k") or policy.model_cfg.vocab_size)
     G = int(cfg["num_generations_per_prompt"])
     max_seq = int(master_config["policy"]["max_total_sequence_length"])
     train_gbs = int(master_config["policy"].get("train_global_batch_size", cfg["num_prompts_per_step"] * G))
@@ -409,6 +416,9 @@ def grpo_train(policy, dataloader, task_to_env: dict, master_config: dict, loss_
                         train_data["advantages"] = adv * tm
                         adv_stats.update(estimator.last_metrics)
                         adv_stats.update(teacher_router.last_metrics)
+                        if opd_full is not None:
+                            v, ix = teacher_router.teacher_topk(train_data, routing_keys(rollout), full_k)
+                            train_data["teacher_topk_logprobs"], train_data["teacher_topk_indices"] = v, ix
                 # ---- train ----
                 with timer.time("policy_training"):
                     policy.prepare_for_training()

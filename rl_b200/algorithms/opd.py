@@ -119,6 +119,44 @@ class TeacherRouter:
         self.last_metrics = m
         return out
 
+    def teacher_topk(self, data: BatchedDataDict, keys: list[str], k: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """Each row's top-``k`` next-token log-probs / ids ``[B, S, k]`` from its
+        routed teacher (``k`` = vocabulary size: the full distribution)."""
+        from rl_b200.algorithms.distillation import teacher_topk
+
+        aliases = resolve_reference_aliases(keys, self.mapping, self.cfg.get("default_teacher_alias"),
+                                            bool(self.cfg.get("strict_agent_name_match", False)))
+        B, S = data["input_ids"].shape
+        vals = torch.zeros(B, S, k, dtype=torch.float32)
+        idx = torch.zeros(B, S, k, dtype=torch.int64)
+        by_teacher: dict[str, list[int]] = {}
+        for i, a in enumerate(aliases):
+            by_teacher.setdefault(self.alias_to_teacher[a], []).append(i)
+        for tkey, rows in by_teacher.items():
+            v, ix = teacher_topk(self.teachers[tkey], data.select_indices(rows), k)
+            vals[rows, :v.shape[1]] = v
+            idx[rows, :ix.shape[1]] = ix
+        self.last_metrics = get_teacher_routing_metrics(aliases, self.mapping)
+        return vals, idx
+
+
+def get_opd_full_config(master_config: dict) -> Optional[dict]:
+    """The ``on_policy_distillation.full`` block when enabled (full-vocabulary
+    MOPD, the reference's ``opd_full``: an exact reverse KL between the student's
+    and the routed teacher's next-token distributions instead of the sampled-token
+    gap); None otherwise.  The ``logits`` payload is built here: the teacher's
+    log-probabilities over the whole vocabulary (``top_k`` may cap it, default the
+    vocabulary size) feed the reverse-KL distillation loss."""
+    full = (_opd_cfg(master_config).get("full") or {})
+    if not full.get("enabled", False):
+        return None
+    payload = str(full.get("teacher_payload", "logits"))
+    if payload != "logits":
+        raise NotImplementedError(f"on_policy_distillation.full.teacher_payload {payload!r}: only 'logits' is built")
+    if str(full.get("divergence", "reverse_kl")) != "reverse_kl":
+        raise ValueError("on_policy_distillation.full.divergence must be reverse_kl")
+    return dict(full)
+
 
 def build_teacher_router(master_config: dict, student, make_teacher: Optional[Callable[[str], Any]] = None
                          ) -> TeacherRouter:

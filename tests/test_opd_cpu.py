@@ -105,3 +105,48 @@ def test_grpo_on_policy_distillation_trains_on_teacher_student_gap():
         assert tm.sum() > 0 and out["grad_norm"] > 0
     gap = metrics[0]["on_policy_distillation/teacher_student_logprob_gap_mean"]
     assert gap < 0 and metrics[0]["on_policy_distillation/teacher_model_unique"] == 1.0
+
+
+def test_full_vocabulary_opd_reverse_kl():
+    """``on_policy_distillation.full``: each step trains on the exact reverse KL
+    between the student's and the routed teacher's full next-token
+    distributions; the loss equals that KL computed by hand on the batch, and
+    training lowers it."""
+    from rl_b200.algorithms.grpo import grpo_train
+    from rl_b200.algorithms.loss.loss_functions import DistillationLossFn
+    from rl_b200.data.datasets import StatefulDataLoader, SyntheticPromptDataset
+    from rl_b200.environments.synthetic import EvenTokenEnvironment
+    from rl_b200.models.config import get_model_config
+    from rl_b200.models.policy.worker import PolicyWorker
+
+    mcfg = get_model_config("tiny-llama")
+    pcfg = {"max_total_sequence_length": 32, "precision": "float32", "train_global_batch_size": 16,
+            "optimizer": {"kwargs": {"lr": 3e-3, "weight_decay": 0.0}},
+            "generation": {"temperature": 1.0, "max_new_tokens": 8},
+            "sequence_packing": {"train_mb_tokens": 256, "logprob_mb_tokens": 256}}
+    student = PolicyWorker(pcfg, model_cfg=mcfg, seed=0)
+    teacher = PolicyWorker(pcfg, model_cfg=mcfg, seed=7, init_reference_model=False)
+    opd = {"enabled": True, "teacher_model_by_agent_name": {"synthetic": "tiny-llama"}, "full": {"enabled": True}}
+    router = TeacherRouter(opd, {"tiny-llama": teacher}, {"synthetic": "tiny-llama"})
+    cfg = {"grpo": {"num_prompts_per_step": 4, "num_generations_per_prompt": 4, "max_num_steps": 4, "seed": 0},
+           "loss_fn": {"reference_policy_kl_penalty": 0.0}, "policy": pcfg, "on_policy_distillation": opd}
+    seen = []
+    real_train = student.train
+
+    def spy(data, loss_fn, **kw):
+        seen.append((data, loss_fn))
+        return real_train(data, loss_fn, **kw)
+
+    student.train = spy
+    dl = StatefulDataLoader(SyntheticPromptDataset(64, 8, 8, mcfg.vocab_size, seed=1), 4, shuffle=False)
+    metrics = []
+    grpo_train(student, dl, {"synthetic": EvenTokenEnvironment({})}, cfg, teacher_router=router,
+               step_callback=lambda s, m: metrics.append(m))
+    data, lf = seen[0]
+    assert isinstance(lf, DistillationLossFn) and lf.kl_type == "reverse"
+    assert data["teacher_topk_logprobs"].shape[-1] == mcfg.vocab_size  # the whole distribution
+    # the teacher payload is the teacher's full log-softmax
+    p = data["teacher_topk_logprobs"][0, 1:3].exp().sum(-1)
+    torch.testing.assert_close(p, torch.ones_like(p), atol=1e-4, rtol=0)
+    losses = [m["loss"] for m in metrics]
+    assert losses[-1] < losses[0], losses

@@ -118,6 +118,7 @@ class PolicyWorker:
         if self.gen_tp not in (1, self.ps.tp_size):
             raise NotImplementedError(f"generation TP {self.gen_tp} must be 1 or the training TP {self.ps.tp_size}")
         self.fp8_rollout = str(vcfg.get("precision", gen_cfg.get("precision", "bfloat16"))).lower() == "fp8"
+        self.nvfp4_rollout = str(vcfg.get("precision", gen_cfg.get("precision", "bfloat16"))).lower() == "nvfp4"
         # fp8 rollout scales: powers of two (hardware-scaled GEMM) unless a config
         # turns the reference's pow2 options off (then fp32 scales, promoting GEMM)
         self.fp8_pow2 = vcfg.get("pow2_weight_scaling_factors") is not False and \
@@ -216,6 +217,12 @@ class PolicyWorker:
 
             gps = dataclasses.replace(self.ps, pp_size=1, pp_rank=0, pp_group=None, pp_ranks=[self.ps.rank])
             self.gen_model = TransformerLM(self.model_cfg, gps, device=self.device, dtype=self.dtype,
+                                           skip_init=True, expert_tensor_parallel=etp)
+        elif self.nvfp4_rollout:
+            if resharded:
+                raise NotImplementedError("NVFP4 rollout weights with a different rollout TP")
+            # rollout copy holding the NVFP4 round trip of the trained weights (same layout)
+            self.gen_model = TransformerLM(self.model_cfg, self.ps, device=self.device, dtype=self.dtype,
                                            skip_init=True, expert_tensor_parallel=etp)
         elif resharded:
             from rl_b200.parallel.state import single_process_state
@@ -359,6 +366,10 @@ class PolicyWorker:
 
             return PipelineGatherSynchronizer(self.model, self.gen_model, self.ps.pp_group, self.ps.pp_ranks,
                                               self.ps.pp_rank)
+        if self.nvfp4_rollout:
+            from rl_b200.weight_sync.colocated import NVFP4RolloutSynchronizer
+
+            return NVFP4RolloutSynchronizer(self.model, self.gen_model)
         if not resharded and not self.fp8_rollout:
             return ColocatedInPlaceSynchronizer()
         if not resharded:

@@ -160,3 +160,49 @@ class QAT:
 
     def quantizer_stats(self) -> dict:
         return {k: float(v) for k, v in sorted(self.input_amax.items())}
+
+
+# ------------------------------------------------------------ NVFP4 storage
+class NVFP4Tensor:
+    """A weight in NVFP4 storage: e2m1 codes two per byte (low nibble = even
+    column; bit 3 = sign, bits 0-2 = index into ``E2M1_VALUES``), one e4m3 scale
+    per 16-element block of a row, one fp32 per-tensor scale."""
+
+    def __init__(self, codes: torch.Tensor, block_scales: torch.Tensor, global_scale: float, shape: tuple):
+        self.codes, self.block_scales, self.global_scale, self.shape = codes, block_scales, float(global_scale), shape
+
+    @property
+    def nbytes(self) -> int:
+        return self.codes.numel() + self.block_scales.numel() + 4
+
+
+def quant_nvfp4(w: torch.Tensor, amax: Optional[torch.Tensor] = None) -> NVFP4Tensor:
+    """Real NVFP4 quantisation of a 2-D weight (rows x columns, columns padded to
+    16): the same two-level scaling as the fake quantiser, so
+    ``dequant_nvfp4(quant_nvfp4(w))`` equals ``fake_quant(w, nvfp4)``."""
+    rows, cols = w.shape
+    xf = w.float()
+    a = amax if amax is not None else xf.abs().amax()
+    g = float(a.clamp_min(1e-12)) / (6.0 * FP8_MAX)
+    pc = -(-cols // 16) * 16
+    if pc != cols:
+        xf = torch.nn.functional.pad(xf, (0, pc - cols))
+    b = xf.view(rows, pc // 16, 16)
+    bs = _fp8_round(b.abs().amax(dim=2, keepdim=True) / 6.0 / g)   # e4m3 value of the block scale / g
+    scale = (bs * g).clamp_min(1e-30)
+    v = (b / scale).clamp(-6.0, 6.0)
+    grid = E2M1_VALUES.to(w.device)
+    idx = torch.bucketize(v.abs(), (grid[1:] + grid[:-1]) / 2)        # same rounding as _e2m1_round
+    code = (idx | ((v < 0) & (idx > 0)).to(idx.dtype) << 3).to(torch.uint8).view(rows, pc)
+    packed = code[:, 0::2] | (code[:, 1::2] << 4)
+    return NVFP4Tensor(packed.contiguous(), bs.view(rows, pc // 16).to(torch.float8_e4m3fn), g, (rows, cols))
+
+
+def dequant_nvfp4(t: NVFP4Tensor, dtype: torch.dtype = torch.float32) -> torch.Tensor:
+    rows, cols = t.shape
+    lo, hi = t.codes & 0x0F, t.codes >> 4
+    code = torch.stack([lo, hi], -1).view(rows, -1).long()
+    grid = E2M1_VALUES.to(t.codes.device)
+    v = grid[code & 7] * torch.where(code >= 8, -1.0, 1.0)
+    s = t.block_scales.float().repeat_interleave(16, 1) * t.global_scale
+    return (v * s)[:, :cols].to(dtype)

@@ -167,3 +167,51 @@ class PipelineGatherSynchronizer(WeightSynchronizer):
                     gen[name].data.view(-1).copy_(buf[off:off + numel])
                     nbytes += numel * buf.element_size()
         return nbytes
+
+
+class NVFP4RolloutSynchronizer(WeightSynchronizer):
+    """Rollout weights in NVFP4 (``generation.vllm_cfg.precision: nvfp4``): the
+    trained bf16 buffer is copied into the rollout model's own buffer and every
+    linear-layer weight (not the embeddings, LM head, norms or MoE routers, the
+    reference's default NVFP4 ignore list) is replaced by its NVFP4 round trip
+    (``quant_nvfp4``: e2m1 codes, e4m3 16-element block scales, fp32 tensor scale).
+    The rollout therefore samples from the NVFP4-weight model (W4A16: the GEMMs
+    run in bf16 on the dequantised values); ``stats["nvfp4_bytes"]`` is the packed
+    size of the quantised weights.
+
+    Reference: NVFP4 rollout quantisation
+    (``nemo_rl/models/generation/vllm/quantization/nvfp4_pertoken.py``) and the
+    ModelOpt real-quant rollout."""
+    name = "nvfp4"
+
+    def __init__(self, model, gen_model):
+        super().__init__()
+        self.model, self.gen_model = model, gen_model
+
+    @staticmethod
+    def quantized(name: str) -> bool:
+        if not name.endswith("weight") and not name.endswith(("gate_up_proj", "down_proj")):
+            return False
+        return any(k in name for k in ("self_attn.", "mlp.")) and not name.endswith("mlp.gate.weight") \
+            and "norm" not in name
+
+    @torch.no_grad()
+    def _sync(self) -> int:
+        from rl_b200.models.quantization import dequant_nvfp4, quant_nvfp4
+
+        # by name: the optimizer may have re-laid the trained buffer out (padding, expert shift)
+        src = {sp.name: q for sp, q in self.model.named_flat_params()}
+        packed = 0
+        for sp, p in self.gen_model.named_flat_params():
+            w = src[sp.name]
+            if not self.quantized(sp.name):
+                p.copy_(w)
+                continue
+            t = quant_nvfp4(w.reshape(-1, w.shape[-1]))  # experts' [E, rows, cols] stacks quantise row by row
+            p.copy_(dequant_nvfp4(t, p.dtype).view(p.shape))
+            packed += t.nbytes
+        bump = getattr(self.gen_model, "bump_weight_version", None)
+        if bump is not None:
+            bump()
+        self.stats["nvfp4_bytes"] = packed
+        return self.model.flat_param.numel() * self.model.flat_param.element_size()

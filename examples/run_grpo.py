@@ -51,6 +51,9 @@ def build_envs(env_cfg: dict) -> dict:
 def main(argv=None) -> dict:
     ap = argparse.ArgumentParser()
     ap.add_argument("--config", default=os.path.join(ROOT, "examples", "configs", "grpo_tiny_cpu.yaml"))
+    ap.add_argument("--role", default="trainer", choices=["trainer", "generator"],
+                    help="with policy.generation.colocated.enabled=false: this process trains (and hosts the "
+                         "data plane) or serves generation")
     args, overrides = ap.parse_known_args(argv)
     from rl_b200.algorithms.grpo import GRPOSaveState, grpo_train
     from rl_b200.data.datasets import StatefulDataLoader, SyntheticPromptDataset
@@ -106,7 +109,10 @@ def main(argv=None) -> dict:
         state.update({k: info[k] for k in state if k in info})
     logger = Logger(cfg.get("logger", {}))
     logger.log_hyperparams(cfg)
-    if (cfg["grpo"].get("single_controller") or {}).get("enabled", False):
+    colo = (cfg["policy"].get("generation") or {}).get("colocated") or {}
+    if not colo.get("enabled", True):
+        state = _run_noncolocated(args.role, cfg, policy, dl, envs, logger, tokenizer)
+    elif (cfg["grpo"].get("single_controller") or {}).get("enabled", False):
         from rl_b200.algorithms.single_controller import single_controller_train
 
         state = single_controller_train(policy, dl, envs, cfg, logger=logger, checkpointer=ck, save_state=state)
@@ -131,6 +137,34 @@ def main(argv=None) -> dict:
     policy.shutdown()  # waits for a background checkpoint write
     if ck is not None:
         ck.wait()  # and for the publication of its step directory
+    return state
+
+
+def _run_noncolocated(role: str, cfg: dict, policy, dl, envs, logger, tokenizer):
+    """Trainer or generator of non-colocated GRPO: both processes run this entry
+    point with the same config (``policy.generation.colocated``: ``host``,
+    ``data_plane_port``, ``refit_port``, ``lead``), the trainer with ``--role trainer``."""
+    from rl_b200.algorithms.grpo import GRPOSaveState
+    from rl_b200.algorithms.noncolocated import noncolocated_grpo_train, serve_generation
+    from rl_b200.data_plane.planes import StoreDataPlane
+    from rl_b200.distributed.stateless_group import StatelessProcessGroup
+    from rl_b200.weight_sync.broadcast import PackedBroadcastSynchronizer
+
+    colo = cfg["policy"]["generation"]["colocated"]
+    host = str(colo.get("host", "127.0.0.1"))
+    trainer = role == "trainer"
+    plane = StoreDataPlane(host=host, port=int(colo.get("data_plane_port", 29650)), is_master=trainer)
+    group = StatelessProcessGroup(host, int(colo.get("refit_port", 29651)), 0 if trainer else 1, 2,
+                                  timeout_s=float(colo.get("timeout_s", 600)))
+    sync = PackedBroadcastSynchronizer(policy.model.flat_param if trainer else policy.gen_model.flat_param, group,
+                                       src=0)
+    state = GRPOSaveState.default()
+    if trainer:
+        hist = noncolocated_grpo_train(policy, dl, cfg, plane, sync, logger=logger)
+        state["current_step"] = len(hist)
+    else:
+        state["current_step"] = serve_generation(policy, cfg, plane, sync, envs, tokenizer=tokenizer)
+    group.barrier()
     return state
 
 

@@ -90,3 +90,32 @@ def test_noncolocated_trainer_and_generator(lead):
     assert len(losses) == 3 and served == 3
     assert all(torch.isfinite(torch.tensor(losses)))
     assert torch.equal(tflat, gflat)  # the generator holds the trained weights
+
+
+def _role(role, pp, gp, q):
+    from examples.run_grpo import main
+
+    cfg = os.path.join(ROOT, "examples", "configs", "grpo_tiny_noncolocated_cpu.yaml")
+    st = main(["--config", cfg, "--role", role, "logger.stdout=false",
+               f"policy.generation.colocated.data_plane_port={pp}", f"policy.generation.colocated.refit_port={gp}",
+               "grpo.max_num_steps=2", f"logger.log_dir=/tmp/rlb_noncolo_{role}_{pp}"])
+    q.put((role, int(st["current_step"])))
+
+
+def test_noncolocated_through_the_entry_point():
+    from rl_b200.distributed.launch import free_port
+
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    pp, gp = free_port(), free_port()
+    procs = [ctx.Process(target=_role, args=(r, pp, gp, q)) for r in ("trainer", "generator")]
+    for p in procs:
+        p.start()
+    try:
+        got = dict(q.get(timeout=300) for _ in range(2))
+    finally:
+        for p in procs:
+            p.join(60)
+            if p.is_alive():
+                p.terminate()
+    assert got == {"trainer": 2, "generator": 2}

@@ -30,7 +30,8 @@ import torch
 
 __all__ = ["TaskDataSpec", "PROCESSOR_REGISTRY", "register_processor", "math_hf_data_processor",
            "math_data_processor", "sft_processor", "multichoice_qa_processor", "preference_preprocessor",
-           "helpsteer3_data_processor", "kd_data_processor", "format_message_log"]
+           "helpsteer3_data_processor", "kd_data_processor", "nemo_gym_data_processor",
+           "format_message_log"]
 
 
 def _read(path: Optional[str]) -> Optional[str]:
@@ -232,12 +233,31 @@ def kd_data_processor(datum_dict: dict, task_data_spec: TaskDataSpec, tokenizer,
     """Distillation prompts: the user turn of ``messages`` (or ``problem``) as the
     prompt; no ground truth needed (the teacher supplies the targets)."""
     if "messages" in datum_dict:
-        user = next(m["content"] for m in datum_dict["messages"] if m["role"] == "user")
+        msgs = datum_dict["messages"]
+        # raw-text rows (one assistant turn, e.g. ``arrow_text``) use the text itself
+        user = next((m["content"] for m in msgs if m["role"] == "user"), msgs[0]["content"] if msgs else "")
     else:
         user = datum_dict["problem"]
     log = _single_prompt_log(tokenizer, _prompt_messages(task_data_spec, user))
     length, lm = _mask_if_long(log, max_seq_length)
     return _datum(log, length, {}, lm, idx, datum_dict.get("task_name"))
+
+
+def nemo_gym_data_processor(datum_dict: dict, task_data_spec: TaskDataSpec, tokenizer, max_seq_length, idx: int):
+    """NeMo-Gym rows: the Gym server builds the prompt, so the datum carries the
+    parsed ``extra_env_info`` payload and one empty user turn (length 0).
+
+    Reference: ``nemo_rl/data/processors.py:932`` (text rows; the video and image
+    tiling branches belong to the multimodal path)."""
+    import json
+
+    import torch
+
+    info = datum_dict["extra_env_info"]
+    if isinstance(info, (str, bytes)):
+        info = json.loads(info)
+    log = [{"role": "user", "content": "", "token_ids": torch.empty(0, dtype=torch.long)}]
+    return _datum(log, 0, info, 1.0, idx, datum_dict.get("task_name"))
 
 
 PROCESSOR_REGISTRY: dict[str, Callable[..., dict]] = {
@@ -249,6 +269,7 @@ PROCESSOR_REGISTRY: dict[str, Callable[..., dict]] = {
     "helpsteer3_data_processor": helpsteer3_data_processor,
     "kd_data_processor": kd_data_processor,
     "chat_kd_processor": kd_data_processor,
+    "nemo_gym_data_processor": nemo_gym_data_processor,
 }
 
 

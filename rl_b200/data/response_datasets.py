@@ -35,7 +35,8 @@ from rl_b200.data.processors import TaskDataSpec, get_processor
 __all__ = ["Rows", "load_rows", "RawDataset", "ResponseDataset", "OpenAIFormatDataset", "OpenMathInstruct2Dataset",
            "DAPOMath17KDataset", "DAPOMathAIME2024Dataset", "DeepScalerDataset", "GSM8KDataset", "AIMEDataset",
            "NuminaMath15Dataset", "OpenR1Math220KDataset", "SquadDataset", "Tulu3SftMixtureDataset",
-           "HelpSteer3Dataset", "DATASET_REGISTRY", "load_response_dataset"]
+           "HelpSteer3Dataset", "NemoGymDataset", "OasstDataset", "oasst_threads", "ArrowTextDataset",
+           "GeneralConversationsJsonlDataset", "DATASET_REGISTRY", "load_response_dataset"]
 
 
 class Rows:
@@ -438,6 +439,220 @@ class OpenAIFormatDataset(RawDataset):
         return out
 
 
+def _rows_of_files(pattern: str) -> list[dict]:
+    """Rows of every local file a path or glob names, in sorted path order."""
+    import glob
+
+    paths = sorted(glob.glob(pattern)) if any(c in pattern for c in "*?[") else [pattern]
+    if not paths:
+        raise FileNotFoundError(f"no data files match {pattern!r}")
+    rows: list[dict] = []
+    for p in paths:
+        rows.extend(_read_local(p))
+    return rows
+
+
+class NemoGymDataset(RawDataset):
+    """NeMo-Gym task rows: each row's ``extra_env_info`` payload (a JSON string, or
+    already a dict) is handed to the Gym environment unparsed here; the processor
+    (``nemo_gym_data_processor``) parses it.
+
+    Reference: ``nemo_rl/data/datasets/response_datasets/nemogym_dataset.py:22``
+    (task name from the last two path components, ``.jsonl`` rows kept as raw
+    strings, an ``extra_env_info`` or ``text`` column otherwise, ``repeat``)."""
+
+    def __init__(self, data_path: str, repeat: int = 1, **_):
+        self.task_name = _task_name_of_path(data_path)
+        if os.path.isfile(data_path) and data_path.lower().endswith(".jsonl"):
+            with open(data_path, encoding="utf-8") as f:  # raw lines: the payload is parsed later
+                base = [{"extra_env_info": line.rstrip("\n")} for line in f if line.strip()]
+        else:
+            rows = load_rows(data_path, None, None)
+            first = rows[0] if len(rows) else {}
+            col = "extra_env_info" if "extra_env_info" in first else "text" if "text" in first else None
+            if col is None:
+                raise ValueError(f"a NeMo-Gym dataset needs an 'extra_env_info' or 'text' column; {data_path!r} "
+                                 f"has {sorted(first)}")
+            base = [{"extra_env_info": rows.raw(i)[col]} for i in range(len(rows))]
+        task = self.task_name
+        self.dataset = Rows(base).map(lambda r: {"extra_env_info": r["extra_env_info"], "task_name": task})
+        if int(repeat) > 1:
+            self.dataset = self.dataset.repeat(int(repeat))
+        self.val_dataset = None
+
+
+OASST_SYSTEM_PROMPT = ("A chat between a curious user and an artificial intelligence assistant. The assistant gives "
+                       "helpful, detailed, and polite answers to the user's questions.\n\n")
+_OASST_ROLES = {"prompter": "user", "assistant": "assistant"}
+
+
+def oasst_threads(tree: dict) -> list[list[dict]]:
+    """Every root-to-leaf thread of one OpenAssistant message tree as a message
+    list (system prompt first), depth first with replies in file order.
+
+    The tree is ``{"prompt": node}`` or a bare node ``{"text", "role", "replies"}``;
+    ``prompter`` turns become ``user``.  Written with an explicit stack, so deep
+    trees need no recursion."""
+    root = tree.get("prompt", tree if ("text" in tree and "role" in tree) else None)
+    if root is None:
+        return [[{"role": "system", "content": OASST_SYSTEM_PROMPT}]]
+    out: list[list[dict]] = []
+    stack = [(root, [{"role": "system", "content": OASST_SYSTEM_PROMPT}])]
+    while stack:
+        node, path = stack.pop()
+        if node["role"] not in _OASST_ROLES:
+            raise ValueError(f"unknown OASST role {node['role']!r}")
+        path = path + [{"role": _OASST_ROLES[node["role"]], "content": node["text"]}]
+        replies = [r for r in node.get("replies", []) if "text" in r and "role" in r]
+        if not replies:
+            out.append(path)
+        for child in reversed(replies):  # reversed onto the stack = file order off it
+            stack.append((child, path))
+    return out
+
+
+class OasstDataset(RawDataset):
+    """OpenAssistant conversation trees flattened into one row per thread (threads
+    with a single turn after the system prompt are dropped).
+
+    Reference: ``nemo_rl/data/datasets/response_datasets/oasst.py:96`` (the
+    ``2023-04-12_oasst_all.trees.jsonl.gz`` file of ``OpenAssistant/oasst1``,
+    ``split_validation_size``, ``seed``).  ``data_path`` names a local copy of the
+    trees file (``.jsonl`` or ``.jsonl.gz``); without it the file is looked up in
+    the local Hugging Face hub cache."""
+
+    HUB_FILE = "2023-04-12_oasst_all.trees.jsonl.gz"
+
+    def __init__(self, split_validation_size: float = 0.05, seed: int = 42, data_path: Optional[str] = None, **_):
+        self.task_name = "oasst"
+        path = data_path or self._cached_file()
+        opener = __import__("gzip").open if path.endswith(".gz") else open
+        rows = []
+        with opener(path, "rt", encoding="utf-8") as f:
+            for line in f:
+                if line.strip():
+                    for thread in oasst_threads(json.loads(line)):
+                        if len(thread) > 2:
+                            rows.append({"messages": thread, "task_name": self.task_name})
+        self.dataset = Rows(rows)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def _cached_file(self) -> str:
+        try:
+            from huggingface_hub import hf_hub_download
+
+            return hf_hub_download("OpenAssistant/oasst1", self.HUB_FILE, repo_type="dataset", local_files_only=True)
+        except Exception as e:  # noqa: BLE001 - say what to do offline
+            raise RuntimeError(f"OASST trees file not in the local hub cache ({type(e).__name__}); pass data_path "
+                               f"pointing at a copy of {self.HUB_FILE}") from e
+
+
+class ArrowTextDataset(RawDataset):
+    """Raw text rows (``text_key``) as single assistant turns for distillation / SFT,
+    optionally packed: consecutive non-empty rows joined with newlines until the
+    pack reaches ``characters_per_sample`` characters.
+
+    Reference: ``nemo_rl/data/datasets/response_datasets/arrow_text_dataset.py:33``
+    (``data_files`` path / glob / hub id, ``subset``, ``split``, ``text_key``,
+    ``characters_per_sample``, task ``x_token``)."""
+
+    def __init__(self, data_files: str, subset: Optional[str] = None, split: str = "train", text_key: str = "text",
+                 characters_per_sample: Optional[int] = None, split_validation_size: float = 0.0, seed: int = 42,
+                 **_):
+        self.task_name, self.text_key = "x_token", text_key
+        if os.path.isfile(data_files) or any(c in data_files for c in "*?["):
+            raw = Rows(_rows_of_files(data_files))
+        else:
+            raw = load_rows(data_files, subset, split)
+        texts = [t for t in (raw.raw(i).get(text_key) for i in range(len(raw))) if isinstance(t, str) and t]
+        if characters_per_sample and int(characters_per_sample) > 0:
+            packs, buf, n = [], [], 0
+            for t in texts:
+                buf.append(t)
+                n += len(t)
+                if n >= int(characters_per_sample):
+                    packs.append("\n".join(buf))
+                    buf, n = [], 0
+            if buf:
+                packs.append("\n".join(buf))
+            texts = packs
+        task = self.task_name
+        self.dataset = Rows([{"text": t} for t in texts]).map(
+            lambda r: {"messages": [{"role": "assistant", "content": r["text"]}], "task_name": task})
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+
+# canonical media tags, the aliases rows may use for them, and the role names
+# ShareGPT-style rows use
+MEDIA_TAGS = ("image", "video", "audio", "video-audio")
+MEDIA_TAG_ALIASES = {"speech": "audio", "speeches": "audio", "sound": "audio", "audios": "audio",
+                     "images": "image", "videos": "video"}
+CONVERSATION_ROLES = {"user": "user", "assistant": "assistant", "human": "user", "gpt": "assistant",
+                      "agent": "assistant"}
+
+
+class GeneralConversationsJsonlDataset(RawDataset):
+    """ShareGPT-style JSONL rows ``{"conversations": [{"from", "value"}...], <media
+    key>: file or [files]}`` turned into OpenAI-style messages whose content is a
+    list of ``{"type": "text", "text": ...}`` / ``{"type": m, m: path}`` fragments,
+    the ``<image>`` / ``<video>`` / ``<audio>`` / ``<video-audio>`` tags in a turn
+    consumed in order from the row's media lists (aliases such as ``sound`` or
+    ``images`` map to the canonical tag; ``video-audio`` yields a video and an
+    audio fragment).  Media names that are not files are looked up under
+    ``media_data_dir``.
+
+    Reference: ``nemo_rl/data/datasets/response_datasets/
+    general_conversations_dataset.py:147`` (``_datum_preprocessor`` ``:231``)."""
+
+    task_name = "general-conversation-jsonl"
+
+    def __init__(self, data_path: str, media_data_dir: Optional[str] = None, split_validation_size: float = 0,
+                 seed: int = 42, **_):
+        import re
+
+        self.media_data_dir = media_data_dir
+        self._split = re.compile("(" + "|".join(re.escape(f"<{t}>") for t in MEDIA_TAGS) + ")")
+        self.dataset = load_rows(data_path, None, None).map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def _media(self, tag: str, name: Any) -> list[dict]:
+        if (self.media_data_dir is not None and isinstance(name, str) and not os.path.isfile(name)
+                and os.path.isfile(os.path.join(self.media_data_dir, name))):
+            name = os.path.join(self.media_data_dir, name)
+        return [{"type": t, t: name} for t in tag.split("-")]
+
+    def format_data(self, row: dict) -> dict:
+        media: dict[str, list] = {}
+        for key, val in row.items():
+            tag = MEDIA_TAG_ALIASES.get(key, key)
+            if tag in MEDIA_TAGS and val is not None and not (key != tag and tag in row):
+                media[tag] = list(val) if isinstance(val, (list, tuple)) else [val]
+        used = {t: 0 for t in media}
+        msgs = []
+        for turn in row.get("conversations", []):
+            role = CONVERSATION_ROLES.get(turn["from"])
+            if role is None:
+                raise ValueError(f"unknown conversation role {turn['from']!r}")
+            text = turn["value"]
+            for alias, tag in MEDIA_TAG_ALIASES.items():
+                text = text.replace(f"<{alias}>", f"<{tag}>")
+            content = []
+            for part in self._split.split(text):
+                tag = part[1:-1] if part.startswith("<") and part[1:-1] in MEDIA_TAGS else None
+                if tag is not None:
+                    if tag not in media or used[tag] >= len(media[tag]):
+                        raise ValueError(f"{part} in a turn but the row has no {tag!r} entry left for it")
+                    content += self._media(tag, media[tag][used[tag]])
+                    used[tag] += 1
+                elif part.strip():
+                    content.append({"type": "text", "text": part})
+            msgs.append({"role": role, "content": content})
+        return {"messages": msgs, "task_name": self.task_name}
+
+
 DATASET_REGISTRY: dict[str, Callable[..., RawDataset]] = {
     "OpenMathInstruct-2": OpenMathInstruct2Dataset,
     "DAPOMath17K": DAPOMath17KDataset,
@@ -455,6 +670,10 @@ DATASET_REGISTRY: dict[str, Callable[..., RawDataset]] = {
     "HelpSteer3": HelpSteer3Dataset,
     "openai_format": OpenAIFormatDataset,
     "ResponseDataset": ResponseDataset,
+    "NemoGymDataset": NemoGymDataset,
+    "open_assistant": OasstDataset,
+    "arrow_text": ArrowTextDataset,
+    "general-conversation-jsonl": GeneralConversationsJsonlDataset,
 }
 
 

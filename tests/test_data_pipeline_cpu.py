@@ -145,6 +145,82 @@ def test_named_datasets_from_local_files(tmp_path):
         load_response_dataset({"dataset_name": "NoSuchDataset"})
 
 
+def test_nemogym_oasst_arrow_text_and_conversation_datasets(tmp_path):
+    import gzip
+
+    from rl_b200.data.processors import PROCESSOR_REGISTRY, TaskDataSpec
+    from rl_b200.data.response_datasets import load_response_dataset
+    from rl_b200.data.tokenizer import get_tokenizer
+
+    # NeMo-Gym: raw JSONL lines kept as strings, task name from the path, repeat; the processor parses them
+    os.makedirs(tmp_path / "gym")
+    gym = _write_jsonl(tmp_path / "gym" / "tasks.jsonl", [{"responses_create_params": {"input": "x"},
+                                                           "agent_ref": {"name": "a1"}}, {"agent_ref": {"name": "a2"}}])
+    ds = load_response_dataset({"dataset_name": "NemoGymDataset", "data_path": gym, "repeat": 2})
+    assert ds.task_name == "gym-tasks" and len(ds.dataset) == 4
+    assert isinstance(ds.dataset[0]["extra_env_info"], str) and ds.dataset[3]["task_name"] == "gym-tasks"
+    d = PROCESSOR_REGISTRY["nemo_gym_data_processor"](ds.dataset[1], None, None, 128, 1)
+    assert d["extra_env_info"]["agent_ref"]["name"] == "a2" and d["length"] == 0
+    assert d["message_log"][0]["token_ids"].numel() == 0 and d["loss_multiplier"] == 1.0
+    # a parquet / json file with a ``text`` column stands in for extra_env_info
+    import pyarrow as pa
+    import pyarrow.parquet as pq
+
+    txt = str(tmp_path / "gym" / "rows.parquet")
+    pq.write_table(pa.table({"text": [json.dumps({"k": 1})]}), txt)
+    assert json.loads(load_response_dataset({"dataset_name": "NemoGymDataset", "data_path": txt}).dataset[0][
+        "extra_env_info"]) == {"k": 1}
+    with pytest.raises(ValueError):
+        load_response_dataset({"dataset_name": "NemoGymDataset",
+                               "data_path": _write_jsonl(tmp_path / "bad.json", [{"other": 1}, {"other": 2}])})
+
+    # OASST: every root-to-leaf thread, system prompt first, single-turn threads dropped
+    tree = {"prompt": {"role": "prompter", "text": "hi", "replies": [
+        {"role": "assistant", "text": "A1", "replies": [{"role": "prompter", "text": "more", "replies": []}]},
+        {"role": "assistant", "text": "A2", "replies": []}]}}
+    lone = {"prompt": {"role": "prompter", "text": "alone", "replies": []}}
+    gz = tmp_path / "trees.jsonl.gz"
+    with gzip.open(gz, "wt", encoding="utf-8") as f:
+        f.write(json.dumps(tree) + "\n" + json.dumps(lone) + "\n")
+    ds = load_response_dataset({"dataset_name": "open_assistant", "data_path": str(gz), "split_validation_size": 0})
+    threads = [[(m["role"], m["content"]) for m in r["messages"][1:]] for r in ds.dataset]
+    assert threads == [[("user", "hi"), ("assistant", "A1"), ("user", "more")], [("user", "hi"), ("assistant", "A2")]]
+    assert ds.dataset[0]["messages"][0]["role"] == "system" and ds.task_name == "oasst"
+
+    # arrow_text: empty / non-string rows dropped, packing by characters joined with newlines
+    for i in range(2):
+        pq.write_table(pa.table({"body": ["aaaa", "", "bbbbbb", None, "cc"][i:]}), str(tmp_path / f"s{i}.parquet"))
+    ds = load_response_dataset({"dataset_name": "arrow_text", "data_files": str(tmp_path / "s*.parquet"),
+                                "text_key": "body"})
+    assert [r["messages"][0]["content"] for r in ds.dataset] == ["aaaa", "bbbbbb", "cc", "bbbbbb", "cc"]
+    assert ds.task_name == "x_token" and ds.dataset[0]["messages"][0]["role"] == "assistant"
+    ds = load_response_dataset({"dataset_name": "arrow_text", "data_files": str(tmp_path / "s0.parquet"),
+                                "text_key": "body", "characters_per_sample": 9})
+    assert [r["messages"][0]["content"] for r in ds.dataset] == ["aaaa\nbbbbbb", "cc"]
+    tok = get_tokenizer({"name": "byte"})
+    d = PROCESSOR_REGISTRY["kd_data_processor"](ds.dataset[1], TaskDataSpec(task_name="x_token"), tok, 256, 0)
+    assert d["length"] > 0  # raw-text rows tokenise without a user turn
+
+    # general conversations: role mapping, media aliases, tags consumed in order, media dir lookup
+    os.makedirs(tmp_path / "media")
+    (tmp_path / "media" / "a.wav").write_bytes(b"RIFF")
+    conv = _write_jsonl(tmp_path / "conv.jsonl", [{
+        "sound": "a.wav", "image": ["i0.jpg", "i1.jpg"],
+        "conversations": [{"from": "human", "value": "Listen <sound> and see <image> <image>"},
+                          {"from": "gpt", "value": "ok"}]}])
+    ds = load_response_dataset({"dataset_name": "general-conversation-jsonl", "data_path": conv,
+                                "media_data_dir": str(tmp_path / "media")})
+    user, asst = ds.dataset[0]["messages"]
+    assert user["role"] == "user" and asst == {"role": "assistant", "content": [{"type": "text", "text": "ok"}]}
+    types = [c["type"] for c in user["content"]]
+    assert types == ["text", "audio", "text", "image", "image"]
+    assert user["content"][1]["audio"] == str(tmp_path / "media" / "a.wav")  # found under media_data_dir
+    assert [c.get("image") for c in user["content"] if c["type"] == "image"] == ["i0.jpg", "i1.jpg"]
+    bad = _write_jsonl(tmp_path / "conv_bad.jsonl", [{"conversations": [{"from": "robot", "value": "x"}]}])
+    with pytest.raises(ValueError):
+        load_response_dataset({"dataset_name": "general-conversation-jsonl", "data_path": bad}).dataset[0]
+
+
 def test_setup_response_data_binds_processors_and_envs(tmp_path):
     from rl_b200.data.tokenizer import ByteTokenizer
     from rl_b200.data.utils import setup_response_data

@@ -20,6 +20,20 @@ __all__ = ["sft_train", "build_sft_batch", "sft_validate"]
 
 
 def build_sft_batch(batch, roles_to_train_on=("assistant",)) -> BatchedDataDict:
+    """Message logs -> right-padded rows with the trained roles' tokens masked in.
+    Packed Megatron SFT rows (``packed_segments``) contribute one row per packed
+    conversation, its tokens and target mask taken as the preprocessor made them."""
+    if batch.get("packed_segments") is not None:
+        lm = batch.get("loss_multiplier")
+        logs, mult = [], []
+        for i, segs in enumerate(batch["packed_segments"]):
+            for sgm in segs or []:
+                logs.append([{"role": "assistant", "token_ids": sgm["token_ids"],
+                              "token_loss_mask": sgm["token_loss_mask"].bool()}])
+                mult.append(float(lm[i]) if isinstance(lm, torch.Tensor) else 1.0)
+        flat, lengths = batched_message_log_to_flat_message(logs)
+        return BatchedDataDict({"input_ids": flat["token_ids"], "input_lengths": lengths,
+                                "token_mask": flat["token_loss_mask"].float(), "sample_mask": torch.tensor(mult)})
     logs = batch["message_log"]
     add_loss_mask_to_message_log(logs, roles_to_train_on=roles_to_train_on)
     flat, lengths = batched_message_log_to_flat_message(logs)

@@ -126,6 +126,8 @@ def rl_collate_fn(batch: list[DatumSpec]) -> dict:
         "idx": torch.tensor([b.get("idx", i) for i, b in enumerate(batch)], dtype=torch.int64),
         "stop_strings": [b.get("stop_strings") for b in batch],
     })
+    if any("packed_segments" in b for b in batch):  # packed Megatron SFT rows
+        out["packed_segments"] = [b.get("packed_segments") for b in batch]
     return out
 
 

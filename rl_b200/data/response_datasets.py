@@ -36,7 +36,8 @@ __all__ = ["Rows", "load_rows", "RawDataset", "ResponseDataset", "OpenAIFormatDa
            "DAPOMath17KDataset", "DAPOMathAIME2024Dataset", "DeepScalerDataset", "GSM8KDataset", "AIMEDataset",
            "NuminaMath15Dataset", "OpenR1Math220KDataset", "SquadDataset", "Tulu3SftMixtureDataset",
            "HelpSteer3Dataset", "NemoGymDataset", "OasstDataset", "oasst_threads", "ArrowTextDataset",
-           "GeneralConversationsJsonlDataset", "DATASET_REGISTRY", "load_response_dataset"]
+           "GeneralConversationsJsonlDataset", "NemotronCascade2SFTMathDataset",
+           "MegatronSFTPackedDataset", "DATASET_REGISTRY", "load_response_dataset"]
 
 
 class Rows:
@@ -653,6 +654,80 @@ class GeneralConversationsJsonlDataset(RawDataset):
         return {"messages": msgs, "task_name": self.task_name}
 
 
+class NemotronCascade2SFTMathDataset(_HubResponseDataset):
+    """``nvidia/Nemotron-Cascade-2-SFT-Data`` (``math`` subset): chat rows already in
+    OpenAI message form ending with the assistant turn; ``max_samples`` draws a
+    seeded random subset before the validation split.
+
+    Reference: ``nemo_rl/data/datasets/response_datasets/nemotron_cascade2_sft.py``."""
+
+    HUB, SUBSET = "nvidia/Nemotron-Cascade-2-SFT-Data", "math"
+
+    def __init__(self, split: str = "train", split_validation_size: float = 0.05, seed: int = 42,
+                 max_samples: Optional[int] = None, data_path: Optional[str] = None, **_):
+        self.task_name = "Nemotron-Cascade-2-SFT-Math"
+        rows = self._load(data_path, self.SUBSET, split)
+        if max_samples is not None and int(max_samples) > 0:
+            order = list(range(len(rows)))
+            random.Random(seed).shuffle(order)
+            rows = rows.select(order[:min(int(max_samples), len(rows))])
+        self.dataset = rows.map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        msgs = row["messages"]
+        if not msgs or msgs[-1]["role"] != "assistant":
+            raise ValueError(f"expected the last message to be the assistant's, got {msgs}")
+        return {"messages": msgs, "task_name": self.task_name}
+
+
+class MegatronSFTPackedDataset(RawDataset):
+    """Megatron-LM offline-packed SFT records (``chat_key`` holds one packed message
+    list, system message first, assistant message last, string contents), turned
+    into pre-shifted rows by ``megatron_sft_packed_preprocessor`` with the
+    ``data_config["megatron_sft"]`` prompt format.
+
+    Reference: ``nemo_rl/data/datasets/response_datasets/megatron_sft_packed.py:29``."""
+
+    def __init__(self, data_path: str, chat_key: str, subset: Optional[str] = None, split: Optional[str] = None,
+                 split_validation_size: float = 0, seed: int = 42, context_parallel_size: Optional[int] = None,
+                 **_):
+        if context_parallel_size is None or int(context_parallel_size) < 1:
+            raise ValueError("packed Megatron SFT data needs the policy's context_parallel_size (>= 1)")
+        self.context_parallel_size, self.chat_key = int(context_parallel_size), chat_key
+        self.task_name = "megatron_sft_packed"
+        self.dataset = load_rows(data_path, subset, split).map(self.format_data)
+        self.val_dataset = None
+        self.split_train_validation(split_validation_size, seed)
+
+    def format_data(self, row):
+        msgs = list(row[self.chat_key])
+        if not msgs or msgs[0]["role"] != "system":
+            raise ValueError("packed Megatron SFT records must start with a system message")
+        if msgs[-1]["role"] != "assistant":
+            raise ValueError("packed Megatron SFT records must end with an assistant message")
+        if any(not isinstance(m["content"], str) for m in msgs):
+            raise ValueError("packed Megatron SFT records need string contents")
+        return {"packed_messages": msgs, "task_name": self.task_name}
+
+    def set_processor(self) -> None:
+        import functools
+
+        from rl_b200.data.megatron_sft_packed import megatron_sft_packed_preprocessor, resolve_prompt_format
+
+        cfg = dict((getattr(self, "data_config", None) or {}).get("megatron_sft") or {})
+        unknown = set(cfg) - {"prompt_format", "override_pad_token"}
+        if unknown:
+            raise ValueError(f"unknown megatron_sft settings: {sorted(unknown)}")
+        if "prompt_format" not in cfg:
+            raise ValueError("data.megatron_sft.prompt_format is required for megatron_sft_packed")
+        resolve_prompt_format(cfg["prompt_format"], cfg.get("override_pad_token"))
+        self.processor = functools.partial(megatron_sft_packed_preprocessor, prompt_format=cfg["prompt_format"],
+                                           pad_token=cfg.get("override_pad_token"),
+                                           context_parallel_size=self.context_parallel_size)
+
+
 DATASET_REGISTRY: dict[str, Callable[..., RawDataset]] = {
     "OpenMathInstruct-2": OpenMathInstruct2Dataset,
     "DAPOMath17K": DAPOMath17KDataset,
@@ -674,6 +749,8 @@ DATASET_REGISTRY: dict[str, Callable[..., RawDataset]] = {
     "open_assistant": OasstDataset,
     "arrow_text": ArrowTextDataset,
     "general-conversation-jsonl": GeneralConversationsJsonlDataset,
+    "Nemotron-Cascade-2-SFT-Math": NemotronCascade2SFTMathDataset,
+    "megatron_sft_packed": MegatronSFTPackedDataset,
 }
 
 
@@ -688,10 +765,11 @@ def _external_class(dotted: str) -> Callable[..., RawDataset]:
     return cls
 
 
-def load_response_dataset(data_config: dict) -> RawDataset:
+def load_response_dataset(data_config: dict, *, context_parallel_size: Optional[int] = None) -> RawDataset:
     """Build the dataset a ``data.train`` / ``data.validation`` entry names:
     a registry key, or a dotted import path of a ``RawDataset`` subclass; then bind
-    its task spec (prompt / system prompt files) and processor."""
+    its task spec (prompt / system prompt files) and processor.
+    ``context_parallel_size`` (the policy's) is passed to ``megatron_sft_packed``."""
     name = data_config["dataset_name"]
     if name in DATASET_REGISTRY:
         factory = DATASET_REGISTRY[name]
@@ -700,7 +778,9 @@ def load_response_dataset(data_config: dict) -> RawDataset:
     else:
         raise ValueError(f"unknown dataset_name {name!r}: use one of {sorted(DATASET_REGISTRY)}, 'ResponseDataset' "
                          f"for a local file, or a dotted path to a dataset class")
-    kwargs = {k: v for k, v in data_config.items() if k != "dataset_name"}
+    kwargs = {k: v for k, v in data_config.items() if k not in ("dataset_name", "megatron_sft")}
+    if name == "megatron_sft_packed":
+        kwargs["context_parallel_size"] = context_parallel_size
     ds = factory(**kwargs)
     ds.set_task_spec(data_config)
     ds.set_processor()

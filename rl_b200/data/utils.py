@@ -148,9 +148,10 @@ def _entries(x) -> list[dict]:
 
 
 def setup_response_data(tokenizer, data_config: dict, env_configs: Optional[dict] = None, is_vlm: bool = False,
-                        *, load_validation: bool = True):
+                        *, load_validation: bool = True, context_parallel_size: Optional[int] = None):
     """Train / validation datasets (and, with ``env_configs``, the task -> environment
-    maps) from the ``data:`` block.  Returns ``(train, val)`` without environment
+    maps) from the ``data:`` block (``context_parallel_size``: the policy's, for
+    packed Megatron SFT data).  Returns ``(train, val)`` without environment
     configs, else ``(train, val, task_to_env, val_task_to_env)``; ``val`` is None
     when no validation data is configured."""
     if is_vlm:
@@ -167,7 +168,7 @@ def setup_response_data(tokenizer, data_config: dict, env_configs: Optional[dict
     val_procs, val_pres, val_task_to_env, val_parts = {}, {}, {}, []
     for cfg in _entries(data_config.get("train")):
         update_single_dataset_config(cfg, default)
-        ds = load_response_dataset(cfg)
+        ds = load_response_dataset(cfg, context_parallel_size=context_parallel_size)
         parts.append(ds.dataset)
         procs[ds.task_name] = (ds.task_spec, ds.processor)
         if ds.preprocessor is not None:
@@ -186,7 +187,7 @@ def setup_response_data(tokenizer, data_config: dict, env_configs: Optional[dict
     if load_validation:
         for cfg in _entries(data_config.get("validation")):
             update_single_dataset_config(cfg, default)
-            ds = load_response_dataset(cfg)
+            ds = load_response_dataset(cfg, context_parallel_size=context_parallel_size)
             val_parts.append(ds.dataset)
             val_procs[ds.task_name] = (ds.task_spec, ds.processor)
             if ds.preprocessor is not None:

@@ -1,6 +1,7 @@
 """CPU unit tests of the framework layer (no GPU): configs, batch containers, packing,
 losses, advantage estimators, checkpoint formats, environments and training loops."""
 
+import json
 import math
 import os
 import random
@@ -325,6 +326,35 @@ def test_sft_loss_decreases():
     sft_train(w, dl, {"sft": {"max_num_epochs": 6}, "policy": {"train_global_batch_size": 8}},
               step_callback=lambda s, m: losses.append(m["loss"]))
     assert len(losses) == 12 and losses[-1] < losses[0]
+
+
+def test_sft_trains_on_packed_megatron_rows(tmp_path):
+    from rl_b200.algorithms.sft import build_sft_batch, sft_train
+    from rl_b200.data.datasets import StatefulDataLoader
+    from rl_b200.data.response_datasets import load_response_dataset
+    from rl_b200.data.tokenizer import get_tokenizer
+
+    tok = get_tokenizer({"name": "byte"})
+    path = tmp_path / "p.jsonl.packed"
+    with open(path, "w") as f:
+        for i in range(8):
+            rec = [{"role": "system", "content": "s"}, {"role": "user", "content": f"u{i}"},
+                   {"role": "assistant", "content": "abc"}, {"role": "system", "content": "t"},
+                   {"role": "user", "content": "v"}, {"role": "assistant", "content": f"d{i}"}]
+            f.write(json.dumps({"conv": rec}) + "\n")
+    ds = load_response_dataset({"dataset_name": "megatron_sft_packed", "data_path": str(path), "chat_key": "conv",
+                                "megatron_sft": {"prompt_format": "identity"}}, context_parallel_size=1)
+    rows = [ds.processor(ds.dataset[i], ds.task_spec, tok, 24, i) for i in range(len(ds.dataset))]
+    dl = StatefulDataLoader(rows, 4, shuffle=False)
+    data = build_sft_batch(next(iter(dl)))
+    assert data["input_ids"].shape[0] == 8  # two conversations per packed row
+    assert float(data["token_mask"].sum()) == 4 * 9  # 10 text tokens a pack: 9 targets, padding masked
+    w = _tiny_policy()
+    losses = []
+    sft_train(w, StatefulDataLoader(rows, 4, shuffle=False), {"sft": {"max_num_epochs": 5},
+                                                              "policy": {"train_global_batch_size": 8}},
+              step_callback=lambda s, m: losses.append(m["loss"]))
+    assert len(losses) == 10 and losses[-1] < losses[0]
 
 
 def test_dpo_and_rm_loops():

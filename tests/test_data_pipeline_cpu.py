@@ -221,6 +221,84 @@ def test_nemogym_oasst_arrow_text_and_conversation_datasets(tmp_path):
         load_response_dataset({"dataset_name": "general-conversation-jsonl", "data_path": bad}).dataset[0]
 
 
+def test_cascade_sft_and_megatron_packed_sft_rows(tmp_path):
+    import warnings
+
+    from rl_b200.data.megatron_sft_packed import IGNORE_INDEX, PROMPT_FORMATS
+    from rl_b200.data.response_datasets import load_response_dataset
+    from rl_b200.data.tokenizer import get_tokenizer
+
+    casc = _write_jsonl(tmp_path / "casc.jsonl", [{"messages": [{"role": "user", "content": f"q{i}"},
+                                                                {"role": "assistant", "content": f"a{i}"}]}
+                                                  for i in range(10)])
+    ds = load_response_dataset({"dataset_name": "Nemotron-Cascade-2-SFT-Math", "data_path": casc,
+                                "max_samples": 4, "split_validation_size": 0.25, "seed": 1})
+    assert len(ds.dataset) == 3 and len(ds.val_dataset) == 1 and ds.task_name == "Nemotron-Cascade-2-SFT-Math"
+
+    tok = get_tokenizer({"name": "byte"})
+    rec = [{"role": "system", "content": "S"}, {"role": "user", "content": "hi"}, {"role": "assistant", "content": "yo"},
+           {"role": "system", "content": "T"}, {"role": "user", "content": "q"}, {"role": "assistant", "content": "ok"}]
+    path = _write_jsonl(tmp_path / "p.jsonl.packed", [{"conv": rec}])
+    cfg = {"dataset_name": "megatron_sft_packed", "data_path": path, "chat_key": "conv",
+           "megatron_sft": {"prompt_format": "nemotron-h-aligned"}}
+    with pytest.raises(ValueError):  # the policy's CP size is required
+        load_response_dataset(cfg)
+    ds = load_response_dataset(cfg, context_parallel_size=1)
+    row = ds.dataset[0]
+    assert row["task_name"] == "megatron_sft_packed" and len(row["packed_messages"]) == 6
+    L = 160
+    d = ds.processor(row, ds.task_spec, tok, L, 0)
+    # expected tokens / labels from the format's rendering, turn by turn
+    fmt = PROMPT_FORMATS["nemotron-h-aligned"]
+    toks, labs, cu = [], [], [0]
+    for conv in (rec[:3], rec[3:]):
+        for m in conv:
+            ids = tok.encode(fmt.render(m["role"], m["content"]))
+            toks += ids
+            labs += ids if m["role"] == "assistant" else [IGNORE_INDEX] * len(ids)
+        cu.append(len(toks))
+    pad = tok.pad_token_id
+    cu[-1] = L
+    toks += [pad] * (L + 1 - len(toks))
+    labs += [pad] * (L + 1 - len(labs))
+    assert d["input_ids"].tolist() == toks[:-1] and d["target_ids"].tolist() == labs[1:]
+    assert d["packed_cu_seqlens"].tolist() == cu
+    exp_mask = [float(t not in (pad, IGNORE_INDEX)) for t in labs[1:]]
+    assert d["token_mask"].tolist() == exp_mask and sum(exp_mask) == len(tok.encode("yo\n")) + len(tok.encode("ok\n"))
+    pos = d["position_ids"].tolist()
+    assert pos[0] == 0 and pos[cu[1]] == 0 and pos[cu[1] - 1] == cu[1] - 1
+    # the segment form: (input, target, counted) triples are exactly the pre-shifted row's
+    trip = []
+    for k, sgm in enumerate(d["packed_segments"]):
+        a = cu[k]
+        ids, m = sgm["token_ids"].tolist(), sgm["token_loss_mask"].tolist()
+        assert len(ids) == cu[k + 1] - a + 1 and m[0] == 0.0
+        trip += [(ids[j - 1], ids[j], m[j]) for j in range(1, len(ids))]
+    direct = [(d["input_ids"][p].item(), toks[p + 1], d["token_mask"][p].item()) for p in range(L)]
+    assert trip == direct
+
+    # context parallelism: every conversation padded to a multiple of 2 * cp; the pack length must be one too
+    ds2 = load_response_dataset(cfg, context_parallel_size=2)
+    d2 = ds2.processor(row, ds2.task_spec, tok, L, 0)
+    seg = (d2["packed_cu_seqlens"][1:] - d2["packed_cu_seqlens"][:-1]).tolist()
+    assert all(x % 4 == 0 for x in seg) and d2["packed_context_parallel_size"] == 2
+    with pytest.raises(ValueError):
+        ds2.processor(row, ds2.task_spec, tok, 90, 0)
+    # overflow: the second conversation is cut, with a warning
+    with warnings.catch_warnings(record=True) as w:
+        warnings.simplefilter("always")
+        d3 = ds.processor(row, ds.task_spec, tok, cu[1] + 5, 0)
+    assert any("overflowed" in str(x.message) for x in w)
+    assert d3["packed_cu_seqlens"].tolist() == [0, cu[1], cu[1] + 5] and d3["input_ids"].numel() == cu[1] + 5
+    # the identity format trains on every token, the next conversation's first one included
+    di = load_response_dataset({**cfg, "megatron_sft": {"prompt_format": "identity"}}, context_parallel_size=1)
+    d4 = di.processor(row, di.task_spec, tok, 32, 0)
+    n_text = sum(len(m["content"]) for m in rec)
+    assert d4["token_mask"].sum().item() == n_text - 1
+    with pytest.raises(ValueError):  # unknown option in the megatron_sft block
+        load_response_dataset({**cfg, "megatron_sft": {"prompt_format": "identity", "x": 1}}, context_parallel_size=1)
+
+
 def test_setup_response_data_binds_processors_and_envs(tmp_path):
     from rl_b200.data.tokenizer import ByteTokenizer
     from rl_b200.data.utils import setup_response_data

@@ -357,6 +357,54 @@ def test_sft_trains_on_packed_megatron_rows(tmp_path):
     assert len(losses) == 10 and losses[-1] < losses[0]
 
 
+def test_preference_datasets_feed_the_dpo_loop(tmp_path):
+    from rl_b200.algorithms.dpo import dpo_train
+    from rl_b200.data.datasets import StatefulDataLoader
+    from rl_b200.data.preference_datasets import PreferenceSamples, load_preference_dataset
+    from rl_b200.data.tokenizer import get_tokenizer
+
+    def jsonl(name, rows):
+        with open(tmp_path / name, "w") as f:
+            f.writelines(json.dumps(r) + "\n" for r in rows)
+        return str(tmp_path / name)
+
+    tok = get_tokenizer({"name": "byte"})
+    b = jsonl("bin.jsonl", [{"q": f"p{i}", "good": "yes", "bad": "no!"} for i in range(8)])
+    ds = load_preference_dataset({"dataset_name": "BinaryPreferenceDataset", "data_path": b, "prompt_key": "q",
+                                  "chosen_key": "good", "rejected_key": "bad"})
+    row = ds.dataset[0]
+    assert row["context"] == [{"role": "user", "content": "p0"}] and row["completions"][0]["rank"] == 0
+    smp = PreferenceSamples(ds, tok, 64)
+    s0 = smp[0]
+    assert tok.decode(s0["chosen"]).strip().endswith("yes") and tok.decode(s0["rejected"]).strip().endswith("no!")
+    assert "p0" in tok.decode(s0["prompt"]) and "yes" not in tok.decode(s0["prompt"])
+    # HelpSteer3 preference: the sign of overall_preference picks the side; 0 warns
+    h = jsonl("hs.jsonl", [{"context": "c", "response1": "r1", "response2": "r2", "overall_preference": p}
+                           for p in (-2, 3, 0)])
+    ds = load_preference_dataset({"dataset_name": "HelpSteer3", "data_path": h})
+    side = lambda r: [c["completion"][0]["content"] for c in sorted(r["completions"], key=lambda c: c["rank"])]
+    assert side(ds.dataset[0]) == ["r1", "r2"] and side(ds.dataset[1]) == ["r2", "r1"]
+    with pytest.warns(UserWarning):
+        assert side(ds.dataset[2]) == ["r1", "r1"]
+    # Tulu3: shared context checked
+    t = jsonl("tulu.jsonl", [{"chosen": [{"role": "user", "content": "u"}, {"role": "assistant", "content": "A"}],
+                              "rejected": [{"role": "user", "content": "u"}, {"role": "assistant", "content": "B"}]},
+                             {"chosen": [{"role": "user", "content": "u"}, {"role": "assistant", "content": "A"}],
+                              "rejected": [{"role": "user", "content": "v"}, {"role": "assistant", "content": "B"}]}])
+    ds = load_preference_dataset({"dataset_name": "Tulu3Preference", "data_path": t})
+    assert side(ds.dataset[0]) == ["A", "B"] and ds.dataset[0]["context"] == [{"role": "user", "content": "u"}]
+    with pytest.raises(ValueError):
+        ds.dataset[1]
+    # generic rows already in the context / completions form, then the DPO loop on the binary set
+    g = jsonl("gen.jsonl", [ds.dataset[0]])
+    assert load_preference_dataset({"dataset_name": "PreferenceDataset", "data_path": g}).dataset[0][
+        "task_name"].endswith("-gen")  # parent directory + file name
+    out = []
+    dpo_train(_tiny_policy(), StatefulDataLoader(smp, 4, shuffle=False, collate_fn=lambda x: x),
+              {"dpo": {"max_num_epochs": 1, "reference_policy_kl_penalty": 0.1}}, step_callback=lambda s, m: out.append(m))
+    assert len(out) == 2 and all(math.isfinite(m["loss"]) for m in out)
+
+
 def test_dpo_and_rm_loops():
     from rl_b200.algorithms.dpo import dpo_train, rm_train
     from rl_b200.data.datasets import PreferenceDataset, StatefulDataLoader

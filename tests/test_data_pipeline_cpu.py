@@ -299,6 +299,58 @@ def test_cascade_sft_and_megatron_packed_sft_rows(tmp_path):
         load_response_dataset({**cfg, "megatron_sft": {"prompt_format": "identity", "x": 1}}, context_parallel_size=1)
 
 
+def test_eval_datasets_rekey_and_process(tmp_path):
+    import csv
+
+    from rl_b200.data.eval_datasets import load_eval_dataset
+    from rl_b200.data.tokenizer import get_tokenizer
+
+    def write_csv(name, header, rows):
+        with open(tmp_path / name, "w", newline="") as f:
+            w = csv.writer(f)
+            w.writerow(header)
+            w.writerows(rows)
+        return str(tmp_path / name)
+
+    tok = get_tokenizer({"name": "byte"})
+    math = write_csv("math_500_test.csv", ["Question", "Answer"], [["1+1?", "2"], ["2*3?", "6"]])
+    ds = load_eval_dataset({"dataset_name": "math500", "data_path": math})
+    assert ds.task_spec.task_name == "math_500_test" and ds.rekeyed_ds[1] == {"problem": "2*3?", "expected_answer": "6"}
+    d = ds.processor(ds.rekeyed_ds[0], ds.task_spec, tok, 256, 0)
+    assert d["extra_env_info"]["ground_truth"] == "2" and d["length"] > 0
+
+    mmlu = write_csv("mmlu_DE.csv", ["Question", "A", "B", "C", "D", "Answer", "Subject"],
+                     [["q", "a", "b", "c", "d", "C", "physics"]])
+    ds = load_eval_dataset({"dataset_name": "mmlu_DE-DE", "data_path": mmlu})
+    assert ds.task_spec.task_name == "MMLU_DE-DE" and ds.rekeyed_ds[0]["options"]["C"] == "c"
+    d = ds.processor(ds.rekeyed_ds[0], ds.task_spec, tok, 256, 0)
+    assert d["extra_env_info"] == {"ground_truth": "C", "subject": "physics"}
+    with pytest.raises(ValueError):
+        load_eval_dataset({"dataset_name": "mmlu_XX-YY", "data_path": mmlu})
+
+    gp = _write_jsonl(tmp_path / "gpqa.jsonl", [{"Question": f"q{i}", "Correct Answer": "right",
+                                                  "Incorrect Answer 1": "w1", "Incorrect Answer 2": "w2",
+                                                  "Incorrect Answer 3": "w3"} for i in range(12)])
+    a = load_eval_dataset({"dataset_name": "gpqa_diamond", "data_path": gp})
+    b = load_eval_dataset({"dataset_name": "gpqa_diamond", "data_path": gp})
+    rows = [a.rekeyed_ds[i] for i in range(12)]
+    assert rows == [b.rekeyed_ds[i] for i in range(12)]  # seeded: reproducible
+    assert all(r["options"][r["answer"]] == "right" for r in rows) and len({r["answer"] for r in rows}) > 1
+    assert a.task_spec.task_name == "GPQA_diamond"
+
+    pro = _write_jsonl(tmp_path / "pro.jsonl", [{"question": "q", "options": ["o0", "o1", "o2", "o3", "o4"],
+                                                 "answer": "E", "category": "law"}])
+    ds = load_eval_dataset({"dataset_name": "mmlu_pro", "data_path": pro})
+    assert ds.rekeyed_ds[0]["options"]["E"] == "o4" and ds.task_spec.task_name == "MMLU-Pro"
+
+    local = write_csv("my_set.csv", ["prob", "sol"], [["3+4?", "7"]])
+    ds = load_eval_dataset({"dataset_name": local, "problem_key": "prob", "solution_key": "sol", "split": None,
+                            "file_format": "csv"})
+    assert ds.task_spec.task_name == "my_set" and ds.rekeyed_ds[0]["expected_answer"] == "7"
+    with pytest.raises(NotImplementedError):
+        load_eval_dataset({"dataset_name": "mmau"})
+
+
 def test_setup_response_data_binds_processors_and_envs(tmp_path):
     from rl_b200.data.tokenizer import ByteTokenizer
     from rl_b200.data.utils import setup_response_data

@@ -30,7 +30,7 @@ from rl_b200.data.processors import TaskDataSpec, math_data_processor, multichoi
 from rl_b200.data.response_datasets import Rows, load_rows
 
 __all__ = ["MathDataset", "GPQADataset", "MMLUDataset", "MMLUProDataset", "LocalMathDataset", "MMLU_LANGUAGES",
-           "load_eval_dataset"]
+           "load_eval_dataset", "setup_eval_data"]
 
 SIMPLE_EVALS = "https://openaipublic.blob.core.windows.net/simple-evals"
 MMLU_LANGUAGES = ("AR-XY", "BN-BD", "DE-DE", "EN-US", "ES-LA", "FR-FR", "HI-IN", "ID-ID", "IT-IT", "JA-JP", "KO-KR",
@@ -165,3 +165,16 @@ def load_eval_dataset(data_config: dict) -> _EvalDataset:
     return LocalMathDataset(data_path=name, problem_key=data_config["problem_key"],
                             solution_key=data_config["solution_key"], split=data_config.get("split"),
                             file_format=data_config.get("file_format", "csv"), **common)
+
+
+def setup_eval_data(tokenizer, data_config: dict):
+    """``(processed dataset, eval dataset)`` for an ``eval`` run: the benchmark's
+    rows through its processor at ``data_config["max_input_seq_length"]``, ready
+    for a ``StatefulDataLoader`` and ``run_env_eval`` (reference:
+    ``examples/run_eval.py`` ``setup_data``)."""
+    from rl_b200.data.utils import AllTaskProcessedDataset
+
+    base = load_eval_dataset(data_config)
+    ds = AllTaskProcessedDataset(base.rekeyed_ds, tokenizer, base.task_spec, base.processor,
+                                 max_seq_length=data_config.get("max_input_seq_length"))
+    return ds, base

@@ -349,6 +349,13 @@ def test_eval_datasets_rekey_and_process(tmp_path):
     assert ds.task_spec.task_name == "my_set" and ds.rekeyed_ds[0]["expected_answer"] == "7"
     with pytest.raises(NotImplementedError):
         load_eval_dataset({"dataset_name": "mmau"})
+    # processed for the eval loop: datums with the ground truth for the math environment
+    from rl_b200.data.datasets import StatefulDataLoader
+    from rl_b200.data.eval_datasets import setup_eval_data
+
+    ds, base = setup_eval_data(tok, {"dataset_name": "math500", "data_path": math, "max_input_seq_length": 128})
+    batch = next(iter(StatefulDataLoader(ds, 2, shuffle=False)))
+    assert [e["ground_truth"] for e in batch["extra_env_info"]] == ["2", "6"] and batch["length"].min() > 0
 
 
 def test_setup_response_data_binds_processors_and_envs(tmp_path):
